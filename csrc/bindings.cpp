@@ -1,0 +1,234 @@
+// bindings.cpp -- torch-facing wrappers of the extern "C" launchers.
+//
+// Every op runs on the caller's current CUDA stream (so CUDA-graph capture
+// and stream scoping compose with torch), checks devices, dtypes, shapes and
+// alignment, and raises on a launcher error instead of returning silently.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cstdint>
+
+#include "sched/abi.h"
+
+extern "C" {
+int sched_gemm_bf16(const void *x, int ldx, const void *w, void *y, int ldy, int T, int N, int K,
+                    int epi, int splits, float *ws, uint32_t *counters, int *status,
+                    cudaStream_t stream);
+int sched_gemm_split_count(int T, int N, int K, int num_sms);
+int sched_attn_decode(const void *q, void *out, const void *k_cache, const void *v_cache,
+                      int num_pages, const int32_t *block_table, int bt_stride, const void *items,
+                      int num_items, int Hq, int Hkv, float sm_scale, float *part_o,
+                      float *part_lse, SchedSlots slots, int woven, int acquire, int grid,
+                      int pf_blocks, float dT, float dR, float H, int *status, cudaStream_t st);
+int sched_attn_merge(const float *part_o, const float *part_lse, const int32_t *merge_req,
+                     const int32_t *merge_begin, int rows, int Hq, void *out, cudaStream_t st);
+int sched_attn_decode_occupancy(int group);
+int sched_attn_decode_smem_bytes();
+int sched_attn_prefill(const void *q, void *out, const void *k_cache, const void *v_cache,
+                       const int32_t *block_table, int bt_stride, const int32_t *kv_lens,
+                       const void *tiles, int num_tiles, int Hq, int Hkv, int page_size,
+                       float sm_scale, cudaStream_t st);
+int sched_add_rmsnorm(const void *x, void *res, const void *w, void *y, int T, int H, float eps,
+                      cudaStream_t st);
+int sched_rope_kv_append(const void *qkv, const int32_t *pos, const int32_t *slot,
+                         const float *cos_sin, void *q_out, void *k_cache, void *v_cache, int T,
+                         int Hq, int Hkv, int D, int page_size, cudaStream_t st);
+int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int H,
+                    cudaStream_t st);
+int sched_argmax(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
+                 int id_offset, cudaStream_t st);
+}
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const at::Tensor &t, const char *name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_bf16(const at::Tensor &t, const char *name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+}
+void check_i32(const at::Tensor &t, const char *name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kInt, name, " must be int32");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+void check_rc(int rc, const char *op) { TORCH_CHECK(rc == 0, op, " launch failed (code ", rc, ")"); }
+
+template <typename T>
+T *ptr_or_null(const c10::optional<at::Tensor> &t) {
+  return (t.has_value() && t->defined()) ? static_cast<T *>(t->data_ptr()) : nullptr;
+}
+
+// ---------------------------------------------------------------- GEMM
+void gemm(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int64_t epi, int64_t splits,
+          const c10::optional<at::Tensor> &ws, const c10::optional<at::Tensor> &counters,
+          const c10::optional<at::Tensor> &status) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(y, "y");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && y.dim() == 2, "gemm expects 2-D tensors");
+  TORCH_CHECK(x.stride(1) == 1 && w.is_contiguous() && y.stride(1) == 1, "row-major operands");
+  const int T = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K, "K mismatch");
+  TORCH_CHECK(y.size(0) >= T, "y rows");
+  TORCH_CHECK(epi == 0 ? y.size(1) >= N : y.size(1) >= N / 2, "y columns");
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(sched_gemm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0), T,
+                           N, K, epi, splits, ptr_or_null<float>(ws),
+                           ptr_or_null<uint32_t>(counters), ptr_or_null<int>(status),
+                           cur_stream()),
+           "gemm");
+}
+
+int64_t gemm_split_count(int64_t T, int64_t N, int64_t K, int64_t sms) {
+  return sched_gemm_split_count(T, N, K, sms);
+}
+
+// ---------------------------------------------------------------- attention
+SchedSlots make_slots(const c10::optional<at::Tensor> &order, const c10::optional<at::Tensor> &ctrl,
+                      const c10::optional<at::Tensor> &timer, const c10::optional<at::Tensor> &queue,
+                      int64_t max_tasks) {
+  SchedSlots s{};
+  s.order = ptr_or_null<const int32_t>(order);
+  s.ctrl = ptr_or_null<const SchedCtrl>(ctrl);
+  s.timer = ptr_or_null<unsigned long long>(timer);
+  s.queue = ptr_or_null<uint32_t>(queue);
+  s.max_tasks = static_cast<uint32_t>(max_tasks);
+  return s;
+}
+
+void attn_decode(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache,
+                 const at::Tensor &v_cache, const at::Tensor &block_table, const at::Tensor &items,
+                 int64_t num_items, double sm_scale, const c10::optional<at::Tensor> &part_o,
+                 const c10::optional<at::Tensor> &part_lse,
+                 const c10::optional<at::Tensor> &order, const c10::optional<at::Tensor> &ctrl,
+                 const c10::optional<at::Tensor> &timer, const c10::optional<at::Tensor> &queue,
+                 int64_t max_tasks, int64_t woven, int64_t acquire, int64_t grid,
+                 int64_t pf_blocks, double dT, double dR, double H,
+                 const c10::optional<at::Tensor> &status) {
+  check_bf16(q, "q");
+  check_bf16(out, "out");
+  check_bf16(k_cache, "k_cache");
+  check_bf16(v_cache, "v_cache");
+  check_i32(block_table, "block_table");
+  check_i32(items, "items");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.is_contiguous(), "q [B, Hq, 128]");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == 16 && k_cache.size(3) == 128 &&
+                  k_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes(),
+              "cache [pages, Hkv, 16, 128]");
+  TORCH_CHECK(items.numel() >= num_items * 4, "items [n, 4]");
+  const int Hq = q.size(1), Hkv = k_cache.size(1);
+  c10::cuda::CUDAGuard g(q.device());
+  SchedSlots sl = make_slots(order, ctrl, timer, queue, max_tasks);
+  check_rc(sched_attn_decode(q.data_ptr(), out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                             k_cache.size(0), block_table.data_ptr<int32_t>(),
+                             block_table.stride(0), items.data_ptr(), num_items, Hq, Hkv,
+                             (float)sm_scale, ptr_or_null<float>(part_o),
+                             ptr_or_null<float>(part_lse), sl, woven, acquire, grid, pf_blocks,
+                             (float)dT, (float)dR, (float)H, ptr_or_null<int>(status),
+                             cur_stream()),
+           "attn_decode");
+}
+
+void attn_merge(const at::Tensor &part_o, const at::Tensor &part_lse, const at::Tensor &merge_req,
+                const at::Tensor &merge_begin, int64_t rows, at::Tensor &out) {
+  check_i32(merge_req, "merge_req");
+  check_i32(merge_begin, "merge_begin");
+  check_bf16(out, "out");
+  c10::cuda::CUDAGuard g(out.device());
+  check_rc(sched_attn_merge(part_o.data_ptr<float>(), part_lse.data_ptr<float>(),
+                            merge_req.data_ptr<int32_t>(), merge_begin.data_ptr<int32_t>(), rows,
+                            out.size(1), out.data_ptr(), cur_stream()),
+           "attn_merge");
+}
+
+void attn_prefill(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache,
+                  const at::Tensor &v_cache, const at::Tensor &block_table,
+                  const at::Tensor &kv_lens, const at::Tensor &tiles, int64_t num_tiles,
+                  double sm_scale) {
+  check_bf16(q, "q");
+  check_bf16(out, "out");
+  check_i32(block_table, "block_table");
+  check_i32(kv_lens, "kv_lens");
+  check_i32(tiles, "tiles");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.is_contiguous(), "q [T, Hq, 128]");
+  c10::cuda::CUDAGuard g(q.device());
+  check_rc(sched_attn_prefill(q.data_ptr(), out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                              block_table.data_ptr<int32_t>(), block_table.stride(0),
+                              kv_lens.data_ptr<int32_t>(), tiles.data_ptr(), num_tiles, q.size(1),
+                              k_cache.size(1), k_cache.size(2), (float)sm_scale, cur_stream()),
+           "attn_prefill");
+}
+
+int64_t attn_decode_occupancy(int64_t group) { return sched_attn_decode_occupancy(group); }
+int64_t attn_decode_smem_bytes() { return sched_attn_decode_smem_bytes(); }
+
+// ---------------------------------------------------------------- elementwise
+void add_rmsnorm(const at::Tensor &x, const c10::optional<at::Tensor> &res, const at::Tensor &w,
+                 at::Tensor &y, double eps) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  check_bf16(y, "y");
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous(), "contiguous rows");
+  const int H = x.size(-1), T = x.numel() / H;
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(sched_add_rmsnorm(x.data_ptr(), res.has_value() ? res->data_ptr() : nullptr,
+                             w.data_ptr(), y.data_ptr(), T, H, (float)eps, cur_stream()),
+           "add_rmsnorm");
+}
+
+void rope_kv_append(const at::Tensor &qkv, const at::Tensor &pos, const at::Tensor &slot,
+                    const at::Tensor &cos_sin, at::Tensor &q_out, at::Tensor &k_cache,
+                    at::Tensor &v_cache, int64_t Hq, int64_t Hkv) {
+  check_bf16(qkv, "qkv");
+  check_i32(pos, "pos");
+  check_i32(slot, "slot");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin float32");
+  const int T = qkv.size(0);
+  c10::cuda::CUDAGuard g(qkv.device());
+  check_rc(sched_rope_kv_append(qkv.data_ptr(), pos.data_ptr<int32_t>(), slot.data_ptr<int32_t>(),
+                                cos_sin.data_ptr<float>(), q_out.data_ptr(), k_cache.data_ptr(),
+                                v_cache.data_ptr(), T, Hq, Hkv, k_cache.size(3), k_cache.size(2),
+                                cur_stream()),
+           "rope_kv_append");
+}
+
+void embedding(const at::Tensor &ids, const at::Tensor &table, at::Tensor &out) {
+  check_i32(ids, "ids");
+  check_bf16(table, "table");
+  c10::cuda::CUDAGuard g(ids.device());
+  check_rc(sched_embedding(ids.data_ptr<int32_t>(), table.data_ptr(), out.data_ptr(), ids.numel(),
+                           table.size(1), cur_stream()),
+           "embedding");
+}
+
+void argmax(const at::Tensor &logits, at::Tensor &ids, const c10::optional<at::Tensor> &maxv,
+            int64_t id_offset) {
+  check_bf16(logits, "logits");
+  check_i32(ids, "ids");
+  c10::cuda::CUDAGuard g(logits.device());
+  check_rc(sched_argmax(logits.data_ptr(), logits.size(0), logits.size(1), logits.stride(0),
+                        ids.data_ptr<int32_t>(), ptr_or_null<float>(maxv), id_offset, cur_stream()),
+           "argmax");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sched_pass_b200 sm_100a kernels";
+  m.def("gemm", &gemm);
+  m.def("gemm_split_count", &gemm_split_count);
+  m.def("attn_decode", &attn_decode);
+  m.def("attn_merge", &attn_merge);
+  m.def("attn_prefill", &attn_prefill);
+  m.def("attn_decode_occupancy", &attn_decode_occupancy);
+  m.def("attn_decode_smem_bytes", &attn_decode_smem_bytes);
+  m.def("add_rmsnorm", &add_rmsnorm);
+  m.def("rope_kv_append", &rope_kv_append);
+  m.def("embedding", &embedding);
+  m.def("argmax", &argmax);
+}

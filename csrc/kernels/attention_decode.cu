@@ -1,0 +1,679 @@
+// attention_decode.cu -- paged decode attention on the sm_100a tensor cores,
+// with every scheduling lever of the manifest woven in at declared points.
+//
+// Problem: for each request b and KV head h, the G = Hq/Hkv query heads of h
+// attend (one query token each) to the request's KV tokens, stored in
+// 16-token pages addressed through a block table. The cache layout is
+// [pages, Hkv, 16, 128] (one page of one head = 4 KB contiguous), so one TMA
+// box (16 rows x 64 columns, 128-byte swizzle) fetches half a page-head.
+//
+// Tensor-core mapping ("transposed" decode): a decode query group is only G
+// rows, far below the 128-row MMA, so the KV tokens take the M dimension:
+//   S^T[128 tok x 16] = K_blk[128 tok x 128 d] . Q^T            (kind::f16)
+//   O^T[128 d  x 16] = V_blk^T[128 d x 128 tok] . P^T[128 tok x 16]
+// with the G heads padded to N = 16. S^T lands in TMEM with one token per
+// lane, so each of the 128 softmax threads owns one token of the block; the
+// PV result lands with one head-dimension row per lane, so the same thread
+// owns one output row d and keeps its G running accumulators in registers.
+//
+// Warp roles (192 threads): warps 0-3 softmax + output (TMEM quarters 0-3),
+// warp 4 TMA producer and task acquisition, warp 5 MMA issuer. KV blocks of
+// 128 tokens flow through a STAGES-deep ring; S and O are double-buffered in
+// TMEM and P in shared memory, so the S MMA of block i+1 and the PV MMA of
+// block i run while the softmax of block i+1 is computed.
+//
+// Scheduling levers (sched/weave.cuh): tasks are (work item, KV head) with a
+// work item = (request, KV range). A task is placed by pi (task =
+// order[raw] with the order_size guard), observed by the timer (cycles added
+// into timer[task]), truncated by shed (tokens at absolute position >= tau
+// are dropped: exact truncated softmax, and the dropped KV is never read),
+// and steered by the L2 policy (urgent tasks prefetch ahead and load with
+// evict_last; polite tasks load with evict_first). Acquisition is static
+// (grid = tasks), ticket (grid = workers, atomic counter that resets itself
+// when the last worker exits), or cluster launch control (grid = tasks,
+// idle CTAs steal unlaunched ones). The producer claims the next task right
+// after it has issued the last load of the current one: late binding with
+// a look-ahead of at most STAGES blocks.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+
+#include "common.cuh"
+#include "sched/ptx.cuh"
+#include "sched/weave.cuh"
+#include "tmap.h"
+
+namespace attn {
+
+constexpr int D = 128;
+constexpr int PS = 16;                 // tokens per page
+constexpr int BLK = 128;               // tokens per KV block (MMA M)
+constexpr int PAGES_PER_BLK = BLK / PS;
+constexpr int NPAD = 16;               // MMA N (query heads, padded)
+constexpr int STAGES = 3;
+constexpr int kThreads = 192;
+constexpr int kSoftmaxThreads = 128;
+constexpr int HALF = BLK * 128;        // bytes of one 64-column half of a K or V block
+constexpr int KV_BLOCK_BYTES = 2 * HALF;
+constexpr int STAGE_BYTES = 2 * KV_BLOCK_BYTES;  // K + V
+constexpr int Q_BYTES = 2 * NPAD * 128;          // two 64-column halves of 16 rows
+constexpr int P_BYTES = 2 * NPAD * 128;          // two 64-token halves of 16 rows
+constexpr int TMEM_COLS = 64;  // S: cols [0,16) and [16,32); O: [32,48) and [48,64)
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + Q_BYTES + 2 * P_BYTES + 1024;
+
+struct Item {
+  int32_t req;       // request (row of q/out and of the block table)
+  int32_t kv_begin;  // first token of the range
+  int32_t kv_end;    // one past the last token
+  int32_t part;      // -1: write the final output; >= 0: partial slot for the merge
+};
+
+struct Params {
+  const __nv_bfloat16 *q;  // [B, Hq, D]
+  __nv_bfloat16 *out;      // [B, Hq, D]
+  const int32_t *block_table;
+  int bt_stride;
+  const Item *items;
+  int num_items;
+  int num_tasks;  // num_items * Hkv
+  int Hq, Hkv;
+  float scale_log2;  // softmax scale * log2(e)
+  float *part_o;     // [parts, Hq, D] (normalised partial outputs)
+  float *part_lse;   // [parts, Hq] (log2-domain LSE)
+  SchedSlots slots;
+  sched::PolicyConsts pc;
+  int pf_blocks;  // urgent prefetch distance in KV blocks
+  int *status;
+};
+
+struct TaskInfo {
+  int32_t task;  // -1 = no more work
+  int32_t req, kvh, kv_begin, kv_end, part, nblk, prio;  // prio: 0 none, 1 urgent, 2 polite
+};
+
+struct Shared {
+  uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
+  uint64_t s_ready[2], s_free[2], p_ready[2], o_ready[2], o_free[2];
+  uint64_t q_ready, task_full[2], task_empty[2], clc_bar;
+  alignas(16) uint4 clc_result;
+  TaskInfo tasks[2];
+  float red_max[4][NPAD];
+  float red_sum[4][NPAD];
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t byte_in_row) {
+  // 128-byte swizzle: the 16-byte chunk index is XORed with (row % 8).
+  return row * 128u + ((((byte_in_row >> 4) ^ (row & 7u)) << 4) | (byte_in_row & 15u));
+}
+
+template <int G, bool WOVEN, int ACQ>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                  const Params p) {
+  static_assert(G >= 1 && G <= NPAD, "group size");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *base = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *stages = base;
+  uint8_t *q_sm = base + STAGES * STAGE_BYTES;
+  uint8_t *p_sm = q_sm + Q_BYTES;  // two buffers of P_BYTES
+  Shared &sh = *reinterpret_cast<Shared *>(p_sm + 2 * P_BYTES);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const SchedSlots &sl = p.slots;
+
+  // ------------------------------------------------------------------ setup
+  if (warp == 0) {
+    ptx::tmem_alloc(&sh.tmem_base, TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  if (threadIdx.x == 32 * 4) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&sh.k_full[s], 1);
+      ptx::mbar_init(&sh.v_full[s], 1);
+      ptx::mbar_init(&sh.kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&sh.s_ready[i], 1);
+      ptx::mbar_init(&sh.s_free[i], kSoftmaxThreads);
+      ptx::mbar_init(&sh.p_ready[i], kSoftmaxThreads);
+      ptx::mbar_init(&sh.o_ready[i], 1);
+      ptx::mbar_init(&sh.o_free[i], kSoftmaxThreads);
+      ptx::mbar_init(&sh.task_full[i], 1);
+      ptx::mbar_init(&sh.task_empty[i], 1 + kSoftmaxThreads);
+    }
+    ptx::mbar_init(&sh.q_ready, kSoftmaxThreads);
+    ptx::mbar_init(&sh.clc_bar, 1);
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tmK);
+    ptx::prefetch_tmap(&tmV);
+  }
+  // Zero the KV ring, Q and P buffers once: blocks that extend past a
+  // request's last page are never loaded, and the masked (P = 0) rows they
+  // contribute must multiply finite values.
+  {
+    uint4 z = make_uint4(0, 0, 0, 0);
+    uint4 *b4 = reinterpret_cast<uint4 *>(base);
+    const int n16 = (STAGES * STAGE_BYTES + Q_BYTES + 2 * P_BYTES) / 16;
+    for (int i = threadIdx.x; i < n16; i += kThreads) b4[i] = z;
+  }
+  ptx::fence_proxy_async_smem();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+
+  // Launch-wide acquisition decision (uniform across the grid).
+  uint32_t wq_tasks = (WOVEN && ACQ != (int)sched::Acquire::Static) ? sched::wq_num_tasks(sl) : 0u;
+  const bool dynamic = wq_tasks != 0u;
+  const uint32_t ntasks = dynamic ? min(wq_tasks, (uint32_t)p.num_tasks) : (uint32_t)p.num_tasks;
+
+  if (WOVEN) sched::pdl_wait();
+
+  if (warp == 4) {
+    // ============================================================ producer
+    if (lane == 0) {
+      uint32_t raw = blockIdx.x;
+      uint32_t clc_phase = 0;
+      int blk_counter = 0;  // global KV block counter of this CTA (ring position)
+      int j = 0;            // task counter of this CTA
+      const uint64_t pol_last = ptx::policy_evict_last();
+      const uint64_t pol_first = ptx::policy_evict_first();
+      bool stop = false;
+      while (!stop) {
+        TaskInfo ti;
+        ti.task = -1;
+        if (raw < ntasks) {
+          uint32_t task = WOVEN ? sched::remap(sl, raw, ntasks) : raw;
+          const int item = task / p.Hkv;
+          const Item it = p.items[item];
+          ti.task = (int32_t)task;
+          ti.req = it.req;
+          ti.kvh = task % p.Hkv;
+          ti.kv_begin = it.kv_begin;
+          int kv_end = it.kv_end;
+          ti.prio = 0;
+          if (WOVEN) {
+            const uint32_t tau = sched::budget(sl, task);
+            if (tau != 0xFFFFFFFFu) kv_end = min(kv_end, (int)tau);
+            const sched::PolicyFlags pf = sched::policy(sl, task, p.pc);
+            ti.prio = pf.urgent ? 1 : (pf.polite ? 2 : 0);
+          }
+          ti.kv_end = max(kv_end, it.kv_begin);
+          ti.part = it.part;
+          ti.nblk = (ti.kv_end - ti.kv_begin + BLK - 1) / BLK;
+        }
+        // publish the task to the MMA and softmax warps
+        const int slot = j & 1;
+        if (!ptx::mbar_wait(&sh.task_empty[slot], ((j >> 1) & 1) ^ 1, kWaitBudgetNs)) {
+          report_status(p.status, kStatusEpilogueTimeout);
+          ti.task = -1;
+        }
+        sh.tasks[slot] = ti;
+        ptx::mbar_arrive(&sh.task_full[slot]);
+        ++j;
+        if (ti.task < 0) break;
+
+        // stream the task's KV blocks
+        const int32_t *bt = p.block_table + (size_t)ti.req * p.bt_stride;
+        const int first_page = ti.kv_begin / PS;  // kv_begin is block-aligned
+        const int last_page = (ti.kv_end + PS - 1) / PS;
+        for (int b = 0; b < ti.nblk; ++b, ++blk_counter) {
+          const int s = blk_counter % STAGES;
+          const uint32_t ph = (blk_counter / STAGES) & 1;
+          if (!ptx::mbar_wait(&sh.kv_empty[s], ph ^ 1, kWaitBudgetNs)) {
+            report_status(p.status, kStatusMmaTimeout);
+            stop = true;
+            break;
+          }
+          uint8_t *kst = stages + s * STAGE_BYTES;
+          uint8_t *vst = kst + KV_BLOCK_BYTES;
+          const int pg0 = first_page + b * PAGES_PER_BLK;
+          const int npg = min(PAGES_PER_BLK, last_page - pg0);
+          const uint32_t bytes = (uint32_t)npg * PS * 128 * 2;  // two halves
+          ptx::mbar_arrive_expect_tx(&sh.k_full[s], bytes);
+          ptx::mbar_arrive_expect_tx(&sh.v_full[s], bytes);
+          for (int pi = 0; pi < npg; ++pi) {
+            const int page = __ldg(bt + pg0 + pi);
+            const int row = (page * p.Hkv + ti.kvh) * PS;
+            uint8_t *kd = kst + pi * PS * 128;
+            uint8_t *vd = vst + pi * PS * 128;
+            if (WOVEN && ti.prio != 0) {
+              const uint64_t pol = ti.prio == 1 ? pol_last : pol_first;
+              ptx::tma_load_2d_hint(kd, &tmK, &sh.k_full[s], 0, row, pol);
+              ptx::tma_load_2d_hint(kd + HALF, &tmK, &sh.k_full[s], 64, row, pol);
+              ptx::tma_load_2d_hint(vd, &tmV, &sh.v_full[s], 0, row, pol);
+              ptx::tma_load_2d_hint(vd + HALF, &tmV, &sh.v_full[s], 64, row, pol);
+            } else {
+              ptx::tma_load_2d(kd, &tmK, &sh.k_full[s], 0, row);
+              ptx::tma_load_2d(kd + HALF, &tmK, &sh.k_full[s], 64, row);
+              ptx::tma_load_2d(vd, &tmV, &sh.v_full[s], 0, row);
+              ptx::tma_load_2d(vd + HALF, &tmV, &sh.v_full[s], 64, row);
+            }
+          }
+          // urgent: warm L2 with the pages pf_blocks ahead (pure hint)
+          if (WOVEN && ti.prio == 1 && p.pf_blocks > 0) {
+            const int pf0 = pg0 + p.pf_blocks * PAGES_PER_BLK;
+            const int pfn = min(PAGES_PER_BLK, last_page - pf0);
+            for (int pi = 0; pi < pfn; ++pi) {
+              const int row = (__ldg(bt + pf0 + pi) * p.Hkv + ti.kvh) * PS;
+              ptx::tma_prefetch_2d(&tmK, 0, row);
+              ptx::tma_prefetch_2d(&tmK, 64, row);
+              ptx::tma_prefetch_2d(&tmV, 0, row);
+              ptx::tma_prefetch_2d(&tmV, 64, row);
+            }
+          }
+        }
+        if (stop) {
+          // tell the consumers there is nothing more
+          const int s2 = j & 1;
+          if (ptx::mbar_wait(&sh.task_empty[s2], ((j >> 1) & 1) ^ 1, kWaitBudgetNs)) {
+            TaskInfo none;
+            none.task = -1;
+            sh.tasks[s2] = none;
+            ptx::mbar_arrive(&sh.task_full[s2]);
+          }
+          break;
+        }
+        // acquire the next task (late binding: after this task's last load)
+        if (!dynamic) {
+          raw = ntasks;  // static: one task per CTA
+        } else if (ACQ == (int)sched::Acquire::Ticket) {
+          raw = sl.queue != nullptr ? gridDim.x + sched::claim_ticket(sl) : ntasks;
+        } else if (ACQ == (int)sched::Acquire::Clc) {
+          bool to = false;
+          raw = sched::claim_clc(&sh.clc_result, &sh.clc_bar, clc_phase, ntasks,
+                                 kWaitBudgetNs, &to);
+          if (to) report_status(p.status, kStatusClcTimeout);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = ptx::idesc_f16(BLK, NPAD, 1, false, false);  // K-major A, K-major B
+      constexpr uint32_t idO = ptx::idesc_f16(D, NPAD, 1, true, false);     // MN-major A (V^T)
+      int blk = 0;  // global block counter
+      int j = 0;
+      bool ok = true;
+      while (ok) {
+        const int slot = j & 1;
+        if (!ptx::mbar_wait(&sh.task_full[slot], (j >> 1) & 1, kWaitBudgetNs)) {
+          report_status(p.status, kStatusEpilogueTimeout);
+          break;
+        }
+        const TaskInfo ti = sh.tasks[slot];
+        ++j;
+        if (ti.task < 0) break;
+        // Q of this task is written by the softmax warps
+        if (!ptx::mbar_wait(&sh.q_ready, (j - 1) & 1, kWaitBudgetNs)) {
+          report_status(p.status, kStatusEpilogueTimeout);
+          break;
+        }
+        auto issue_s = [&](int g) -> bool {  // g: global block index
+          const int s = g % STAGES;
+          const int sb = g & 1;
+          if (!ptx::mbar_wait(&sh.k_full[s], (g / STAGES) & 1, kWaitBudgetNs)) return false;
+          if (!ptx::mbar_wait(&sh.s_free[sb], ((g >> 1) & 1) ^ 1, kWaitBudgetNs)) return false;
+          ptx::tc_fence_after();
+          const uint8_t *kst = stages + s * STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint8_t *a = kst + (kk / 4) * HALF + (kk % 4) * 32;
+            const uint8_t *b = q_sm + (kk / 4) * (NPAD * 128) + (kk % 4) * 32;
+            ptx::mma_f16_ss(tmem + sb * 16, ptx::smem_desc(a, 16, 1024, ptx::kLayoutSW128),
+                            ptx::smem_desc(b, 16, 1024, ptx::kLayoutSW128), idS, kk > 0);
+          }
+          ptx::mma_commit(&sh.s_ready[sb]);
+          return true;
+        };
+        auto issue_o = [&](int g) -> bool {
+          const int s = g % STAGES;
+          const int ob = g & 1;
+          if (!ptx::mbar_wait(&sh.v_full[s], (g / STAGES) & 1, kWaitBudgetNs)) return false;
+          if (!ptx::mbar_wait(&sh.p_ready[ob], (g >> 1) & 1, kWaitBudgetNs)) return false;
+          if (!ptx::mbar_wait(&sh.o_free[ob], ((g >> 1) & 1) ^ 1, kWaitBudgetNs)) return false;
+          ptx::tc_fence_after();
+          const uint8_t *vst = stages + s * STAGE_BYTES + KV_BLOCK_BYTES;
+          const uint8_t *pb = p_sm + ob * P_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BLK / 16; ++kk) {
+            // A = V^T, MN-major: 64 d per 128-byte row, other d-half at +HALF (LBO),
+            // 8-token groups at +1024 (SBO); 16 tokens per MMA = +2048 bytes.
+            const uint8_t *a = vst + kk * 2048;
+            const uint8_t *b = pb + (kk / 4) * (NPAD * 128) + (kk % 4) * 32;
+            ptx::mma_f16_ss(tmem + 32 + ob * 16, ptx::smem_desc(a, HALF, 1024, ptx::kLayoutSW128),
+                            ptx::smem_desc(b, 16, 1024, ptx::kLayoutSW128), idO, kk > 0);
+          }
+          ptx::mma_commit(&sh.o_ready[ob]);
+          ptx::mma_commit(&sh.kv_empty[s]);
+          return true;
+        };
+        const int g0 = blk;
+        if (ti.nblk > 0 && !issue_s(g0)) ok = false;
+        for (int b = 0; ok && b < ti.nblk; ++b) {
+          if (b + 1 < ti.nblk && !issue_s(g0 + b + 1)) { ok = false; break; }
+          if (!issue_o(g0 + b)) { ok = false; break; }
+        }
+        if (!ok) report_status(p.status, kStatusTmaTimeout);
+        blk += ti.nblk;
+        ptx::mbar_arrive(&sh.task_empty[slot]);
+      }
+    }
+  } else {
+    // ============================================================ softmax + output
+    const int t = threadIdx.x;  // 0..127: token row of S^T, d row of O^T
+    const int q4 = warp;        // TMEM lane quarter
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    int blk = 0;
+    int j = 0;
+    while (true) {
+      const int slot = j & 1;
+      if (!ptx::mbar_wait(&sh.task_full[slot], (j >> 1) & 1, kWaitBudgetNs)) {
+        report_status(p.status, kStatusEpilogueTimeout);
+        break;
+      }
+      const TaskInfo ti = sh.tasks[slot];
+      ++j;
+      if (ti.task < 0) break;
+      const unsigned long long t0 = sched::clock_now();
+      const bool timer_off = WOVEN ? sched::timer_off_at_entry(sl) : true;
+
+      // Q rows of this task -> swizzled K-major tile (rows >= G stay zero).
+      if (t < G * 16) {
+        const int h = t / 16, c = t % 16;
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(
+            p.q + ((size_t)ti.req * p.Hq + ti.kvh * G + h) * D) + c);
+        *reinterpret_cast<uint4 *>(q_sm + (c / 8) * (NPAD * 128) + swz(h, (c % 8) * 16)) = v;
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(&sh.q_ready);
+
+      float m_run[G], l_run[G], o_acc[G], alpha_prev[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        m_run[h] = -INFINITY;
+        l_run[h] = 0.f;
+        o_acc[h] = 0.f;
+        alpha_prev[h] = 1.f;
+      }
+      for (int b = 0; b < ti.nblk; ++b) {
+        const int g = blk + b;
+        const int sb = g & 1;
+        if (!ptx::mbar_wait(&sh.s_ready[sb], (g >> 1) & 1, kWaitBudgetNs)) {
+          report_status(p.status, kStatusMmaTimeout);
+          break;
+        }
+        ptx::tc_fence_after();
+        uint32_t sr[16];
+        ptx::tmem_ld16(tmem + lane_off + sb * 16, sr);
+        ptx::tmem_ld_wait();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&sh.s_free[sb]);
+        const int tok = ti.kv_begin + b * BLK + t;
+        const bool valid = tok < ti.kv_end;
+        float s[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) s[h] = valid ? __uint_as_float(sr[h]) * p.scale_log2 : -INFINITY;
+        // block max per head: warp, then across the 4 warps
+        float mx[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          float v = s[h];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+          mx[h] = v;
+        }
+        if (lane == 0)
+#pragma unroll
+          for (int h = 0; h < G; ++h) sh.red_max[q4][h] = mx[h];
+        named_bar(1, kSoftmaxThreads);
+        float alpha[G], pr[G], ps[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float bm = fmaxf(fmaxf(sh.red_max[0][h], sh.red_max[1][h]),
+                                 fmaxf(sh.red_max[2][h], sh.red_max[3][h]));
+          const float m_new = fmaxf(m_run[h], bm);
+          // m_new == -inf only when every token so far was masked
+          alpha[h] = (m_new == -INFINITY) ? 1.f : exp2f(m_run[h] - m_new);
+          pr[h] = (m_new == -INFINITY) ? 0.f : exp2f(s[h] - m_new);
+          m_run[h] = m_new;
+          float v = pr[h];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          ps[h] = v;
+        }
+        if (lane == 0)
+#pragma unroll
+          for (int h = 0; h < G; ++h) sh.red_sum[q4][h] = ps[h];
+        // P^T -> shared (bf16, swizzled K-major, row = head, column = token)
+        uint8_t *pb = p_sm + sb * P_BYTES + (t / 64) * (NPAD * 128);
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+          *reinterpret_cast<__nv_bfloat16 *>(pb + swz(h, (t % 64) * 2)) = __float2bfloat16(pr[h]);
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(&sh.p_ready[sb]);
+        named_bar(1, kSoftmaxThreads);
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+          l_run[h] = l_run[h] * alpha[h] +
+                     (sh.red_sum[0][h] + sh.red_sum[1][h] + sh.red_sum[2][h] + sh.red_sum[3][h]);
+        // fold in the previous block's PV result (one-block delay)
+        if (b > 0) {
+          const int gp = g - 1, ob = gp & 1;
+          if (!ptx::mbar_wait(&sh.o_ready[ob], (gp >> 1) & 1, kWaitBudgetNs)) {
+            report_status(p.status, kStatusMmaTimeout);
+            break;
+          }
+          ptx::tc_fence_after();
+          uint32_t orr[16];
+          ptx::tmem_ld16(tmem + lane_off + 32 + ob * 16, orr);
+          ptx::tmem_ld_wait();
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(&sh.o_free[ob]);
+#pragma unroll
+          for (int h = 0; h < G; ++h) o_acc[h] = o_acc[h] * alpha_prev[h] + __uint_as_float(orr[h]);
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) alpha_prev[h] = alpha[h];
+        named_bar(2, kSoftmaxThreads);  // red_* reuse guard for the next block
+      }
+      if (ti.nblk > 0) {
+        const int gp = blk + ti.nblk - 1, ob = gp & 1;
+        if (ptx::mbar_wait(&sh.o_ready[ob], (gp >> 1) & 1, kWaitBudgetNs)) {
+          ptx::tc_fence_after();
+          uint32_t orr[16];
+          ptx::tmem_ld16(tmem + lane_off + 32 + ob * 16, orr);
+          ptx::tmem_ld_wait();
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(&sh.o_free[ob]);
+#pragma unroll
+          for (int h = 0; h < G; ++h) o_acc[h] = o_acc[h] * alpha_prev[h] + __uint_as_float(orr[h]);
+        } else {
+          report_status(p.status, kStatusMmaTimeout);
+        }
+      }
+      blk += ti.nblk;
+      // output: thread t owns head-dimension row d = t
+      const int hq0 = ti.kvh * G;
+      if (ti.part < 0) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float v = l_run[h] > 0.f ? o_acc[h] / l_run[h] : 0.f;
+          p.out[((size_t)ti.req * p.Hq + hq0 + h) * D + t] = __float2bfloat16(v);
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float v = l_run[h] > 0.f ? o_acc[h] / l_run[h] : 0.f;
+          p.part_o[((size_t)ti.part * p.Hq + hq0 + h) * D + t] = v;
+          if (t == 0)
+            p.part_lse[(size_t)ti.part * p.Hq + hq0 + h] =
+                l_run[h] > 0.f ? m_run[h] + __log2f(l_run[h]) : -INFINITY;
+        }
+      }
+      if (WOVEN && t == 0) sched::timer_commit(sl, timer_off, (uint32_t)ti.task, t0);
+      ptx::mbar_arrive(&sh.task_empty[slot]);
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) ptx::tmem_dealloc(tmem, TMEM_COLS);
+  if (WOVEN) {
+    sched::pdl_launch_dependents();
+    // ticket queue: the last worker to leave resets the counters for the next launch
+    if (ACQ == (int)sched::Acquire::Ticket && dynamic && sl.queue != nullptr && threadIdx.x == 0) {
+      __threadfence();
+      const uint32_t done = atomicAdd(sl.queue + 1, 1u);
+      if (done == gridDim.x - 1) {
+        sl.queue[0] = 0u;
+        sl.queue[1] = 0u;
+        __threadfence();
+      }
+    }
+  }
+}
+
+// Merge split-KV partials: out[b, hq, :] = sum_i w_i * o_i, w_i = 2^(lse_i - lse).
+__global__ void merge_kernel(const float *part_o, const float *part_lse, const int32_t *merge_req,
+                             const int32_t *merge_begin, int Hq, __nv_bfloat16 *out) {
+  const int r = blockIdx.x;   // merge row (one split request)
+  const int hq = blockIdx.y;  // query head
+  const int d = threadIdx.x;  // 0..127
+  const int b0 = merge_begin[r], b1 = merge_begin[r + 1];
+  float mx = -INFINITY;
+  for (int i = b0; i < b1; ++i) mx = fmaxf(mx, part_lse[(size_t)i * Hq + hq]);
+  float acc = 0.f, wsum = 0.f;
+  if (mx != -INFINITY) {
+    for (int i = b0; i < b1; ++i) {
+      const float w = exp2f(part_lse[(size_t)i * Hq + hq] - mx);
+      acc += w * part_o[((size_t)i * Hq + hq) * D + d];
+      wsum += w;
+    }
+  }
+  out[((size_t)merge_req[r] * Hq + hq) * D + d] = __float2bfloat16(wsum > 0.f ? acc / wsum : 0.f);
+}
+
+template <int G, bool WOVEN, int ACQ>
+static int launch(const CUtensorMap &tk, const CUtensorMap &tv, const Params &p, int grid,
+                  cudaStream_t st) {
+  auto kern = decode_kernel<G, WOVEN, ACQ>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    attr = true;
+  }
+  if (WOVEN) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, tk, tv, p);
+  } else {
+    kern<<<grid, kThreads, SMEM, st>>>(tk, tv, p);
+  }
+  return 0;
+}
+
+template <int G>
+static int dispatch_acq(bool woven, int acq, const CUtensorMap &tk, const CUtensorMap &tv,
+                        const Params &p, int grid, cudaStream_t st) {
+  if (!woven) return launch<G, false, 0>(tk, tv, p, grid, st);
+  switch (acq) {
+    case 1: return launch<G, true, 1>(tk, tv, p, grid, st);
+    case 2: return launch<G, true, 2>(tk, tv, p, grid, st);
+    default: return launch<G, true, 0>(tk, tv, p, grid, st);
+  }
+}
+
+}  // namespace attn
+
+extern "C" int sched_attn_decode_smem_bytes() { return attn::SMEM; }
+
+// Resident CTAs per SM of the woven static kernel (the CLC prefix R = this x SMs).
+extern "C" int sched_attn_decode_occupancy(int group) {
+  int blocks = 0;
+  const void *k = nullptr;
+  switch (group) {
+    case 1: k = (const void *)attn::decode_kernel<1, true, 2>; break;
+    case 2: k = (const void *)attn::decode_kernel<2, true, 2>; break;
+    case 8: k = (const void *)attn::decode_kernel<8, true, 2>; break;
+    default: k = (const void *)attn::decode_kernel<4, true, 2>; break;
+  }
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k, attn::kThreads, attn::SMEM) !=
+      cudaSuccess)
+    return 0;
+  return blocks;
+}
+
+// q [B, Hq, 128] bf16; k_cache/v_cache [pages, Hkv, 16, 128] bf16;
+// items [num_items] (req, kv_begin, kv_end, part); grid: tasks (static/CLC)
+// or workers (ticket). Returns 0 on success.
+extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
+                                 const void *v_cache, int num_pages, const int32_t *block_table,
+                                 int bt_stride, const void *items, int num_items, int Hq, int Hkv,
+                                 float sm_scale, float *part_o, float *part_lse, SchedSlots slots,
+                                 int woven, int acquire, int grid, int pf_blocks, float dT,
+                                 float dR, float H, int *status, cudaStream_t st) {
+  if (num_items <= 0) return 0;
+  const int G = Hq / Hkv;
+  if (Hq % Hkv != 0 || (G != 1 && G != 2 && G != 4 && G != 8)) return -1;
+  attn::Params p;
+  p.q = static_cast<const __nv_bfloat16 *>(q);
+  p.out = static_cast<__nv_bfloat16 *>(out);
+  p.block_table = block_table;
+  p.bt_stride = bt_stride;
+  p.items = static_cast<const attn::Item *>(items);
+  p.num_items = num_items;
+  p.num_tasks = num_items * Hkv;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.part_o = part_o;
+  p.part_lse = part_lse;
+  p.slots = slots;
+  p.pc.dT = dT;
+  p.pc.dR = dR;
+  p.pc.H = H;
+  p.pf_blocks = pf_blocks;
+  p.status = status;
+  if (grid <= 0) grid = p.num_tasks;
+  try {
+    const uint64_t rows = (uint64_t)num_pages * Hkv * attn::PS;
+    CUtensorMap tk = tmap::make_2d(k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, attn::D,
+                                   attn::D, attn::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap tv = tmap::make_2d(v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, attn::D,
+                                   attn::D, attn::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    switch (G) {
+      case 1: attn::dispatch_acq<1>(woven, acquire, tk, tv, p, grid, st); break;
+      case 2: attn::dispatch_acq<2>(woven, acquire, tk, tv, p, grid, st); break;
+      case 8: attn::dispatch_acq<8>(woven, acquire, tk, tv, p, grid, st); break;
+      default: attn::dispatch_acq<4>(woven, acquire, tk, tv, p, grid, st); break;
+    }
+  } catch (const std::exception &) {
+    return -3;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int sched_attn_merge(const float *part_o, const float *part_lse,
+                                const int32_t *merge_req, const int32_t *merge_begin, int rows,
+                                int Hq, void *out, cudaStream_t st) {
+  if (rows <= 0) return 0;
+  attn::merge_kernel<<<dim3(rows, Hq), attn::D, 0, st>>>(
+      part_o, part_lse, merge_req, merge_begin, Hq, static_cast<__nv_bfloat16 *>(out));
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}

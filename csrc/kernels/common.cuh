@@ -1,0 +1,39 @@
+// common.cuh -- small shared pieces of the framework's CUDA kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// Status codes written (first writer wins) into a caller-provided device word
+// when a bounded wait gives up. 0 = OK. The host reads and clears the word.
+enum KernelStatus : int {
+  kStatusOk = 0,
+  kStatusTmaTimeout = 1,      // a TMA completion never arrived
+  kStatusMmaTimeout = 2,      // a tensor-core commit never arrived
+  kStatusEpilogueTimeout = 3, // the epilogue never saw its accumulator
+  kStatusPeerTimeout = 4,     // a peer GPU's flag never arrived
+  kStatusClcTimeout = 5,      // a cluster-launch-control response never arrived
+  kStatusBadArgument = 6,
+};
+
+__device__ __forceinline__ void report_status(int *status, int code) {
+  if (status != nullptr) atomicCAS(status, 0, code);
+}
+
+// Wall-time budget (ns) of every bounded wait on an mbarrier or a flag.
+constexpr uint64_t kWaitBudgetNs = 2000000000ull;
+
+__device__ __forceinline__ float bf16_to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+// Named barrier among `nthreads` threads (ids 1..15 are free for kernels).
+__device__ __forceinline__ void named_bar(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}

@@ -1,0 +1,259 @@
+// elementwise.cu -- the bandwidth-bound per-token kernels of a decoder layer.
+//
+//   * fused residual-add + RMSNorm: res += x; y = res * rsqrt(mean(res^2) + eps) * w
+//     (one read of x and res, one write of res and y: the add that closes a
+//     sub-block and the norm that opens the next one cost one pass);
+//   * RoPE + KV append: rotates q and k of the fused QKV projection output,
+//     writes q to the attention input and k, v straight into their pages of
+//     the paged cache (no intermediate k/v tensors);
+//   * token embedding gather;
+//   * greedy sampling (row argmax over the vocabulary).
+// All accesses are 16-byte vectors; one CTA per token row.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace ew {
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) s += red[i];
+  return s;
+}
+
+// H = hidden size, multiple of 8; NT threads, each owns H / NT / 8 vectors.
+template <int NT, int VPT>
+__global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const __nv_bfloat16 *__restrict__ x,
+                                                         __nv_bfloat16 *__restrict__ res,
+                                                         const __nv_bfloat16 *__restrict__ w,
+                                                         __nv_bfloat16 *__restrict__ y, int H,
+                                                         float eps) {
+  __shared__ float red[NT / 32];
+  const size_t row = blockIdx.x;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * NT) * 8;
+    if (c < H) {
+      uint4 xv = *reinterpret_cast<const uint4 *>(x + row * H + c);
+      const __nv_bfloat16 *xe = reinterpret_cast<const __nv_bfloat16 *>(&xv);
+      if (res != nullptr) {
+        uint4 rv = *reinterpret_cast<const uint4 *>(res + row * H + c);
+        const __nv_bfloat16 *re = reinterpret_cast<const __nv_bfloat16 *>(&rv);
+        uint4 ov;
+        __nv_bfloat16 *oe = reinterpret_cast<__nv_bfloat16 *>(&ov);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          // the residual stream is kept in bf16: round the sum once, like a
+          // separate add kernel would
+          oe[j] = __float2bfloat16(__bfloat162float(xe[j]) + __bfloat162float(re[j]));
+          v[i][j] = __bfloat162float(oe[j]);
+        }
+        *reinterpret_cast<uint4 *>(res + row * H + c) = ov;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(xe[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  const float inv = rsqrtf(block_sum<NT>(ss, red) / (float)H + eps);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * NT) * 8;
+    if (c < H) {
+      uint4 wv = *reinterpret_cast<const uint4 *>(w + c);
+      const __nv_bfloat16 *we = reinterpret_cast<const __nv_bfloat16 *>(&wv);
+      uint4 ov;
+      ov.x = pack_bf16x2(v[i][0] * inv * __bfloat162float(we[0]), v[i][1] * inv * __bfloat162float(we[1]));
+      ov.y = pack_bf16x2(v[i][2] * inv * __bfloat162float(we[2]), v[i][3] * inv * __bfloat162float(we[3]));
+      ov.z = pack_bf16x2(v[i][4] * inv * __bfloat162float(we[4]), v[i][5] * inv * __bfloat162float(we[5]));
+      ov.w = pack_bf16x2(v[i][6] * inv * __bfloat162float(we[6]), v[i][7] * inv * __bfloat162float(we[7]));
+      *reinterpret_cast<uint4 *>(y + row * H + c) = ov;
+    }
+  }
+}
+
+// One warp per head of one token. Rotate-half RoPE (pairs d, d + D/2) with a
+// precomputed [max_pos, D/2] table of (cos, sin). Head order in qkv:
+// Hq query heads, Hkv key heads, Hkv value heads.
+template <int D>
+__global__ void rope_kv_append_kernel(const __nv_bfloat16 *__restrict__ qkv,
+                                      const int32_t *__restrict__ pos,
+                                      const int32_t *__restrict__ slot,
+                                      const float2 *__restrict__ cos_sin,
+                                      __nv_bfloat16 *__restrict__ q_out,
+                                      __nv_bfloat16 *__restrict__ k_cache,
+                                      __nv_bfloat16 *__restrict__ v_cache, int Hq, int Hkv,
+                                      int page_size) {
+  constexpr int HALF = D / 2;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nheads = Hq + 2 * Hkv;
+  const int p = pos[t];
+  const int s = slot[t];
+  const int page = s / page_size, off = s % page_size;
+  const __nv_bfloat16 *src_row = qkv + (size_t)t * nheads * D;
+  for (int h = warp; h < nheads; h += blockDim.x / 32) {
+    const __nv_bfloat16 *src = src_row + (size_t)h * D;
+    __nv_bfloat16 *dst;
+    if (h < Hq) {
+      dst = q_out + ((size_t)t * Hq + h) * D;
+    } else if (h < Hq + Hkv) {
+      if (s < 0) continue;  // padding token: no cache write
+      dst = k_cache + (((size_t)page * Hkv + (h - Hq)) * page_size + off) * D;
+    } else {
+      if (s < 0) continue;
+      dst = v_cache + (((size_t)page * Hkv + (h - Hq - Hkv)) * page_size + off) * D;
+      // value heads are copied unrotated
+      for (int d = lane * 8; d < D; d += 32 * 8)
+        *reinterpret_cast<uint4 *>(dst + d) = *reinterpret_cast<const uint4 *>(src + d);
+      continue;
+    }
+    // each lane rotates pairs (d, d + HALF) for d = lane, lane + 32, ...
+    for (int d = lane; d < HALF; d += 32) {
+      const float2 cs = cos_sin[(size_t)p * HALF + d];
+      const float a = __bfloat162float(src[d]);
+      const float b = __bfloat162float(src[d + HALF]);
+      dst[d] = __float2bfloat16(a * cs.x - b * cs.y);
+      dst[d + HALF] = __float2bfloat16(b * cs.x + a * cs.y);
+    }
+  }
+}
+
+__global__ void embedding_kernel(const int32_t *__restrict__ ids,
+                                 const __nv_bfloat16 *__restrict__ table,
+                                 __nv_bfloat16 *__restrict__ out, int H) {
+  const int t = blockIdx.x;
+  const size_t id = (size_t)ids[t];
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
+    *reinterpret_cast<uint4 *>(out + (size_t)t * H + c) =
+        *reinterpret_cast<const uint4 *>(table + id * H + c);
+}
+
+// Row argmax; ties resolve to the lowest index. Also emits the row max so a
+// vocabulary-parallel caller can combine shards (value, index) pairs.
+__global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16 *__restrict__ logits,
+                                                      int V, int ld, int32_t *__restrict__ ids,
+                                                      float *__restrict__ maxv, int id_offset) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int t = blockIdx.x;
+  const __nv_bfloat16 *row = logits + (size_t)t * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  const int nvec = V / 8;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    uint4 u = *reinterpret_cast<const uint4 *>(row + i * 8);
+    const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = __bfloat162float(e[j]);
+      if (v > best) {
+        best = v;
+        bi = i * 8 + j;
+      }
+    }
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
+    const float v = __bfloat162float(row[i]);
+    if (v > best) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) {
+    sv[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (w == 0) {
+    best = l < (int)(blockDim.x / 32) ? sv[l] : -INFINITY;
+    bi = l < (int)(blockDim.x / 32) ? si[l] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (l == 0) {
+      ids[t] = bi + id_offset;
+      if (maxv != nullptr) maxv[t] = best;
+    }
+  }
+}
+
+}  // namespace ew
+
+extern "C" int sched_add_rmsnorm(const void *x, void *res, const void *w, void *y, int T, int H,
+                                 float eps, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (H % 8 != 0) return -1;
+  const __nv_bfloat16 *xb = static_cast<const __nv_bfloat16 *>(x);
+  __nv_bfloat16 *rb = static_cast<__nv_bfloat16 *>(res);
+  const __nv_bfloat16 *wb = static_cast<const __nv_bfloat16 *>(w);
+  __nv_bfloat16 *yb = static_cast<__nv_bfloat16 *>(y);
+  if (H <= 256 * 8 * 2)
+    ew::add_rmsnorm_kernel<256, 2><<<T, 256, 0, st>>>(xb, rb, wb, yb, H, eps);
+  else if (H <= 512 * 8 * 2)
+    ew::add_rmsnorm_kernel<512, 2><<<T, 512, 0, st>>>(xb, rb, wb, yb, H, eps);
+  else if (H <= 1024 * 8 * 2)
+    ew::add_rmsnorm_kernel<1024, 2><<<T, 1024, 0, st>>>(xb, rb, wb, yb, H, eps);
+  else
+    return -1;
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int sched_rope_kv_append(const void *qkv, const int32_t *pos, const int32_t *slot,
+                                    const float *cos_sin, void *q_out, void *k_cache,
+                                    void *v_cache, int T, int Hq, int Hkv, int D, int page_size,
+                                    cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (D != 128) return -1;
+  ew::rope_kv_append_kernel<128><<<T, 256, 0, st>>>(
+      static_cast<const __nv_bfloat16 *>(qkv), pos, slot, reinterpret_cast<const float2 *>(cos_sin),
+      static_cast<__nv_bfloat16 *>(q_out), static_cast<__nv_bfloat16 *>(k_cache),
+      static_cast<__nv_bfloat16 *>(v_cache), Hq, Hkv, page_size);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int H,
+                               cudaStream_t st) {
+  if (T <= 0) return 0;
+  ew::embedding_kernel<<<T, 256, 0, st>>>(ids, static_cast<const __nv_bfloat16 *>(table),
+                                          static_cast<__nv_bfloat16 *>(out), H);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int sched_argmax(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
+                            int id_offset, cudaStream_t st) {
+  if (T <= 0) return 0;
+  ew::argmax_kernel<<<T, 1024, 0, st>>>(static_cast<const __nv_bfloat16 *>(logits), V, ld, ids,
+                                        maxv, id_offset);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}

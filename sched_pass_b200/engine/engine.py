@@ -1,0 +1,412 @@
+"""The serving engine: scheduler -> step plan -> device buffers -> forward.
+
+Per step:
+  1. the scheduler picks the decode set and the prefill chunks;
+  2. the planner (numpy + the native host runtime) lays out token rows
+     (decode rows first), positions, KV slots, block-table rows, the decode
+     work items (each request split into S KV chunks so that even small
+     batches fill the SMs) and the prefill query tiles, all into ONE pinned
+     int32 buffer that is copied to the device with one async copy;
+  3. the scheduling levers are programmed: the controller orders the decode
+     tasks (LPT / region order when cluster launch control is armed), the
+     probe cadence switches the per-task timer on every ``timer_every`` steps,
+     shed budgets are written for low-urgency requests, and the control
+     block is published (stream-ordered, before the forward);
+  4. decode-only steps replay a CUDA graph captured for the batch bucket;
+     mixed steps run eagerly;
+  5. the sampled token ids come back with one D2H copy; the timer of a probe
+     step is folded into the controller's cost model.
+
+Timing of a step is taken on the device (CUDA events around the forward).
+"""
+from __future__ import annotations
+
+import math
+import os
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..models.config import ModelConfig
+from ..models.llama import ForwardBatch, KVCache, Llama, init_weights
+from ..runtime.controller import SchedControlPlane
+from ..runtime.sched_rt import SchedPlane
+from . import native
+from .request import Request, State
+from .scheduler import Scheduler, StepPlan
+
+DECODE_BUCKETS = (1, 2, 4, 8, 12, 16, 24, 32, 40, 48, 56, 64, 80, 96, 112, 128, 160, 192, 224, 256)
+Q_TILE = 64
+
+
+@dataclass
+class EngineConfig:
+    max_batch: int = 256
+    max_prefill_tokens: int = 4096
+    max_context: int = 4096
+    num_pages: int = 0              # 0: sized from max_batch * max_context
+    cuda_graphs: bool = True
+    levers: bool = True             # weave the levers into the decode kernel
+    acquire: str = "static"         # static | ticket | clc | auto
+    timer_every: int = 8            # probe cadence of the per-task timer (0 = never)
+    plan_every: int = 1             # re-order cadence
+    lpt_block: int = 16
+    clc_uncertainty: float = 0.75   # arm CLC above this estimator uncertainty (auto)
+    shed_fraction: float = 0.0      # fraction of lowest-urgency requests given a tau
+    shed_ratio: float = 0.5         # tau = ratio * context length
+    target_tasks: int = 0           # decode tasks to aim for (0 = 2 x SMs)
+    seed: int = 0
+
+
+@dataclass
+class StepStats:
+    n_decode: int
+    n_prefill_tokens: int
+    device_ms: float
+    graph: bool
+
+
+class Engine:
+    """Single-process engine for one tensor-parallel rank (``tp`` from
+    ``parallel.tp``; None for one GPU). Every rank of a TP group runs the same
+    scheduler on the same requests, so plans agree without communication."""
+
+    def __init__(self, cfg: ModelConfig, ecfg: EngineConfig | None = None, device="cuda", tp=None,
+                 weights=None, model_factory=None):
+        self.cfg = cfg
+        self.ecfg = ecfg or EngineConfig()
+        e = self.ecfg
+        self.device = torch.device(device)
+        self.tp = tp
+        tp_size = tp.world if tp is not None else 1
+        tp_rank = tp.rank if tp is not None else 0
+        self.max_pages_per_req = (e.max_context + 15) // 16
+        if not e.num_pages:
+            e.num_pages = e.max_batch * self.max_pages_per_req + 64
+        self.kv = KVCache(cfg, e.num_pages, self.device, tp_size=tp_size)
+        if weights is None:
+            weights = init_weights(cfg, self.device, tp_rank, tp_size, seed=e.seed,
+                                   moe_builder=getattr(model_factory, "moe_builder", None))
+        T = max(e.max_prefill_tokens + e.max_batch, 256)
+        if model_factory is not None:
+            self.model = model_factory(cfg, weights, self.kv, self.device, tp, T, e.max_context + 16)
+        else:
+            self.model = Llama(cfg, weights, self.kv, self.device, tp=tp, max_tokens=T,
+                               max_pos=e.max_context + 16)
+        self.sched = Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context)
+        self.hkv = cfg.n_kv_heads // tp_size
+        self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.target_tasks = e.target_tasks or 2 * self.sms
+        self._alloc_buffers(T)
+        # scheduling control plane (device-resident tables)
+        max_tasks = e.max_batch * 8 * self.hkv
+        self.plane = SchedPlane(max_tasks=max_tasks, device=str(self.device), mode="device")
+        self.controller = SchedControlPlane(policy="lpt")
+        self.R = self._resident_prefix()
+        self.step_no = 0
+        self.graphs: dict[int, tuple] = {}
+        self._pool = None
+        self.stats: list[StepStats] = []
+        self.clock = 0.0  # workload clock in seconds (device time + idle gaps)
+        self._probe_pending = None
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc_buffers(self, T: int) -> None:
+        e = self.ecfg
+        B = e.max_batch
+        R = B + e.max_prefill_tokens // 1  # rows of the block table: decode + prefill requests
+        R = min(R, 2 * B)
+        S_max = 8
+        self.rows_max = R
+        self.layout = {}
+        off = 0
+
+        def reserve(name, n):
+            nonlocal off
+            self.layout[name] = (off, n)
+            off += (n + 3) // 4 * 4  # keep 16-byte alignment of every field
+
+        reserve("ids", T)
+        reserve("pos", T)
+        reserve("slot", T)
+        reserve("block_table", R * self.max_pages_per_req)
+        reserve("kv_lens", R)
+        reserve("items", B * S_max * 4)
+        reserve("merge_req", B)
+        reserve("merge_begin", B + 1)
+        reserve("tiles", (e.max_prefill_tokens // Q_TILE + B) * 4)
+        reserve("sample_idx", 2 * B)
+        self.packed_len = off
+        self.host = torch.zeros(off, dtype=torch.int32, pin_memory=True)
+        self.dev = torch.zeros(off, dtype=torch.int32, device=self.device)
+        self.host_np = self.host.numpy()
+        self.out_ids = torch.zeros(2 * B, dtype=torch.int32, device=self.device)
+        self.out_host = torch.zeros(2 * B, dtype=torch.int32, pin_memory=True)
+        self.part_o = torch.zeros(B * S_max, self.cfg.n_q_heads // (self.tp.world if self.tp else 1),
+                                  self.cfg.head_dim, dtype=torch.float32, device=self.device)
+        self.part_lse = torch.zeros(B * S_max, self.part_o.shape[1], dtype=torch.float32, device=self.device)
+        self.sample_idx64 = torch.zeros(2 * B, dtype=torch.int64, device=self.device)
+
+    def _view(self, name, shape=None):
+        o, n = self.layout[name]
+        v = self.dev[o:o + n]
+        return v.view(*shape) if shape is not None else v
+
+    def _host(self, name):
+        o, n = self.layout[name]
+        return self.host_np[o:o + n]
+
+    def _resident_prefix(self) -> int:
+        try:
+            return self.plane.r_for_kernel(self.cfg.group)
+        except Exception:
+            return self.sms
+
+    def splits_for(self, n_decode: int) -> int:
+        tasks = max(1, n_decode * self.hkv)
+        return int(min(8, max(1, math.ceil(self.target_tasks / tasks))))
+
+    # ------------------------------------------------------------------ public API
+    def add_request(self, req: Request) -> None:
+        self.sched.add(req)
+
+    def has_work(self) -> bool:
+        return not self.sched.idle
+
+    # ------------------------------------------------------------------ planning
+    def _fill(self, plan: StepPlan, bucket: int | None):
+        """Write the step's inputs into the pinned staging buffer."""
+        e = self.ecfg
+        dec = plan.decode
+        nd = len(dec)
+        ndp = bucket if bucket is not None else nd   # padded decode rows (graph bucket)
+        pre = plan.prefill
+        n_pre_tok = sum(n for _, _, n in pre)
+        T = ndp + n_pre_tok
+        ids, pos, slot = self._host("ids"), self._host("pos"), self._host("slot")
+        mp = self.max_pages_per_req
+        bt = self._host("block_table").reshape(-1, mp)
+        kvl = self._host("kv_lens")
+        # decode rows
+        for i, r in enumerate(dec):
+            p = r.total_len - 1
+            ids[i] = r.next_input_token()
+            pos[i] = p
+            slot[i] = r.pages[p // 16] * 16 + p % 16
+            npg = len(r.pages)
+            bt[i, :npg] = r.pages
+            kvl[i] = r.total_len
+        if ndp > nd:  # padding rows: no cache write, empty attention items
+            ids[nd:ndp] = 0
+            pos[nd:ndp] = 0
+            slot[nd:ndp] = -1
+            kvl[nd:ndp] = 0
+        # prefill rows
+        row = ndp
+        tiles = []
+        for j, (r, start, n) in enumerate(pre):
+            br = ndp + j
+            ids[row:row + n] = r.prompt[start:start + n]
+            pp = np.arange(start, start + n, dtype=np.int32)
+            pos[row:row + n] = pp
+            pg = np.asarray(r.pages, dtype=np.int32)
+            slot[row:row + n] = pg[pp // 16] * 16 + pp % 16
+            bt[br, :pg.size] = pg
+            kvl[br] = start + n
+            for t0 in range(0, n, Q_TILE):
+                tiles.append((br, row - ndp + t0, min(Q_TILE, n - t0), start + t0))
+            row += n
+        # decode plan
+        S = self.splits_for(ndp) if ndp else 1
+        n_items = 0
+        if ndp:
+            items, mreq, mbeg = native.plan_decode(kvl[:ndp].copy(), S)
+            n_items = items.shape[0]
+            self._host("items")[:n_items * 4] = items.reshape(-1)
+            if S > 1:
+                self._host("merge_req")[:ndp] = mreq
+                self._host("merge_begin")[:ndp + 1] = mbeg
+        th = self._host("tiles")
+        for k, t in enumerate(tiles):
+            th[4 * k:4 * k + 4] = t
+        # sampled rows: every decode row (padded too), plus the last row of each finished prompt
+        sidx = self._host("sample_idx")
+        ns = ndp
+        sidx[:ndp] = np.arange(ndp, dtype=np.int32)
+        sample_map = [(r.rid, i) for i, r in enumerate(dec)]
+        row = ndp
+        for r, start, n in pre:
+            if start + n >= r.prompt_len:
+                sidx[ns] = row + n - 1
+                sample_map.append((r.rid, ns))
+                ns += 1
+            row += n
+        return dict(T=T, nd=ndp, n_items=n_items, S=S, n_tiles=len(tiles), n_sample=ns,
+                    sample_map=sample_map, n_real_decode=nd)
+
+    def _batch(self, info, slots) -> ForwardBatch:
+        mp = self.max_pages_per_req
+        nd, S = info["nd"], info["S"]
+        n_items = info["n_items"]
+        return ForwardBatch(
+            ids=self._view("ids"), pos=self._view("pos"), slot=self._view("slot"),
+            n_tokens=info["T"], n_decode=nd,
+            block_table=self._view("block_table", (-1, mp)), kv_lens=self._view("kv_lens"),
+            items=self._view("items", (-1, 4)), n_items=n_items,
+            part_o=self.part_o if S > 1 else None, part_lse=self.part_lse if S > 1 else None,
+            merge_req=self._view("merge_req"), merge_begin=self._view("merge_begin"),
+            n_merge=nd if S > 1 else 0,
+            tiles=self._view("tiles", (-1, 4)), n_tiles=info["n_tiles"],
+            sample_idx=self.sample_idx64, n_sample=info["n_sample"], out_ids=self.out_ids,
+            slots=slots, acquire=self._acq_code(),
+            grid=min(self.R, n_items * self.hkv) if self.ecfg.acquire == "ticket" else 0,
+        )
+
+    def _acq_code(self) -> int:
+        return {"static": 0, "ticket": 1, "clc": 2, "auto": 2}.get(self.ecfg.acquire, 0)
+
+    # ------------------------------------------------------------------ levers
+    def _program_levers(self, plan: StepPlan, info) -> None:
+        """Order, timer cadence, shed and work-queue arming for this step."""
+        e = self.ecfg
+        nd, n_items = info["nd"], info["n_items"]
+        if not e.levers or nd == 0:
+            return
+        n_tasks = n_items * self.hkv
+        plane = self.plane
+        replan = (self.step_no % max(1, e.plan_every)) == 0
+        if replan:
+            items = self._host("items")[:n_items * 4].reshape(-1, 4)
+            cost = native.task_costs(items, n_items, self.hkv)
+            arm_clc = False
+            if e.acquire == "clc":
+                arm_clc = True
+            elif e.acquire == "auto":
+                dec = plan.decode
+                unc = self.controller.uncertainty([r.rid for r in dec], [r.total_len for r in dec])
+                arm_clc = n_tasks > self.R and unc > e.clc_uncertainty
+            if arm_clc:
+                order = native.region_order(cost, self.R, e.lpt_block)
+            elif n_tasks > self.R:
+                order = native.grouped_lpt(cost, e.lpt_block)
+            else:
+                order = None  # one wave: ordering cannot help; identity
+            if order is not None:
+                plane.install_order(torch.from_numpy(order), n_tasks)
+            else:
+                plane.set_order_size(0)
+                plane.reset_order()
+            plane.set_num_tasks(n_tasks if (arm_clc or e.acquire == "ticket") else 0)
+        # shed: tau for the lowest-urgency fraction of decode requests
+        if e.shed_fraction > 0:
+            dec = plan.decode
+            k = int(len(dec) * e.shed_fraction)
+            low = sorted(range(len(dec)), key=lambda i: dec[i].urgency)[:k]
+            tau = np.zeros(n_tasks, dtype=np.int64)
+            items = self._host("items")[:n_items * 4].reshape(-1, 4)
+            low_set = set(low)
+            for it in range(n_items):
+                if int(items[it, 0]) in low_set:
+                    r = dec[int(items[it, 0])]
+                    tau[it * self.hkv:(it + 1) * self.hkv] = max(1, int(e.shed_ratio * r.total_len))
+            plane.set_rows(tau=np.minimum(tau, 0xFFFF), n=n_tasks)
+        probe = e.timer_every > 0 and (self.step_no % e.timer_every) == 0
+        plane.set_timer_enabled(probe)
+        if probe:
+            plane.clear_timer()
+        plane.push()
+        self._probe = probe
+
+    def _fold_probe(self, plan: StepPlan, info) -> None:
+        if not getattr(self, "_probe", False) or info["nd"] == 0:
+            return
+        cyc = self.plane.timer_t[: info["n_items"] * self.hkv].view(info["n_items"], self.hkv).sum(1)
+        cyc = cyc.cpu().numpy()
+        items = self._host("items")[: info["n_items"] * 4].reshape(-1, 4)
+        per_req = np.zeros(info["nd"], dtype=np.float64)
+        np.add.at(per_req, items[:, 0], cyc)
+        dec = plan.decode
+        self.controller.observe([r.rid for r in dec], [r.total_len for r in dec],
+                                per_req[: len(dec)].tolist())
+
+    # ------------------------------------------------------------------ graphs
+    def _bucket(self, nd: int) -> int | None:
+        for b in DECODE_BUCKETS:
+            if b >= nd and b <= self.ecfg.max_batch:
+                return b
+        return None
+
+    def _graph_for(self, bucket: int, info, slots):
+        g = self.graphs.get(bucket)
+        if g is not None:
+            return g
+        batch = self._batch(info, slots)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up outside capture (lazy inits, attributes)
+                self.model.forward(batch)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(graph, pool=self._pool):
+            self.model.forward(batch)
+        self.graphs[bucket] = (graph, info["S"], info["n_items"])
+        return self.graphs[bucket]
+
+    # ------------------------------------------------------------------ step
+    def step(self) -> tuple[StepPlan, list]:
+        plan = self.sched.schedule()
+        if plan.empty:
+            return plan, []
+        nd = len(plan.decode)
+        decode_only = not plan.prefill
+        bucket = self._bucket(nd) if (decode_only and self.ecfg.cuda_graphs) else None
+        info = self._fill(plan, bucket)
+        slots = self.plane.slots() if self.ecfg.levers else None
+        self._program_levers(plan, info)
+        # one H2D copy of every step input
+        self.dev[: self.packed_len].copy_(self.host[: self.packed_len], non_blocking=True)
+        si = self._view("sample_idx")
+        self.sample_idx64[: info["n_sample"]].copy_(si[: info["n_sample"]])
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        used_graph = False
+        if bucket is not None:
+            graph, S, n_items = self._graph_for(bucket, info, slots)
+            assert S == info["S"] and n_items == info["n_items"]
+            graph.replay()
+            used_graph = True
+        else:
+            self.model.forward(self._batch(info, slots))
+        ev1.record()
+        ns = info["n_sample"]
+        self.out_host[:ns].copy_(self.out_ids[:ns], non_blocking=True)
+        ev1.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        self.clock += ms / 1e3
+        self._fold_probe(plan, info)
+        out = self.out_host[:ns].numpy()
+        sampled = {rid: int(out[i]) for rid, i in info["sample_map"]}
+        done = self.sched.commit(plan, sampled, self.clock)
+        if done:
+            self.controller.forget([r.rid for r in done])
+        self.stats.append(StepStats(nd, plan.n_tokens - nd, ms, used_graph))
+        self.step_no += 1
+        return plan, done
+
+    # ------------------------------------------------------------------ convenience
+    def generate(self, prompts, max_new_tokens: int = 16) -> list:
+        """Greedy generation for a list of prompts (token id arrays)."""
+        reqs = [Request(rid=i, prompt=np.asarray(p, dtype=np.int32), max_new_tokens=max_new_tokens)
+                for i, p in enumerate(prompts)]
+        for r in reqs:
+            self.add_request(r)
+        while self.has_work():
+            self.step()
+        return [r.output for r in reqs]

@@ -1,0 +1,152 @@
+"""Continuous-batching scheduler with chunked prefill.
+
+Every step serves all running decode requests (one token each) and fills
+the remaining token budget with prefill chunks of waiting / partially
+prefilled requests, oldest first. Pages come from the native allocator; when
+a decode request needs a page and none is free, the most recently admitted
+request is preempted (its pages are freed and it restarts from its prompt,
+keeping the tokens it already generated as part of its new prompt).
+"""
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .native import PageAllocator
+from .request import Request, State
+
+
+@dataclass
+class StepPlan:
+    decode: list = field(default_factory=list)    # requests decoding one token
+    prefill: list = field(default_factory=list)   # (request, start, n_tokens)
+    preempted: list = field(default_factory=list)
+
+    @property
+    def n_tokens(self) -> int:
+        return len(self.decode) + sum(n for _, _, n in self.prefill)
+
+    @property
+    def empty(self) -> bool:
+        return not self.decode and not self.prefill
+
+
+class Scheduler:
+    def __init__(self, num_pages: int, page_size: int = 16, max_batch: int = 256,
+                 max_prefill_tokens: int = 4096, max_context: int = 8192):
+        self.alloc = PageAllocator(num_pages)
+        self.page_size = page_size
+        self.max_batch = max_batch
+        self.max_prefill_tokens = max_prefill_tokens
+        self.max_context = max_context
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []   # admitted (PREFILL or DECODE), admission order
+
+    def add(self, req: Request) -> None:
+        if req.prompt_len + req.max_new_tokens > self.max_context:
+            raise ValueError(f"request {req.rid}: {req.prompt_len}+{req.max_new_tokens} tokens exceed "
+                             f"max_context {self.max_context}")
+        self.waiting.append(req)
+
+    @property
+    def idle(self) -> bool:
+        return not self.waiting and not self.running
+
+    def _pages_needed(self, req: Request, upto: int) -> int:
+        return max(0, (upto + self.page_size - 1) // self.page_size - len(req.pages))
+
+    def _grow(self, req: Request, upto: int) -> bool:
+        n = self._pages_needed(req, upto)
+        if n == 0:
+            return True
+        got = self.alloc.take(n)
+        if got is None:
+            return False
+        req.pages.extend(int(p) for p in got)
+        return True
+
+    def release(self, req: Request) -> None:
+        if req.pages:
+            self.alloc.give(np.asarray(req.pages, dtype=np.int32))
+            req.pages = []
+
+    def _preempt(self, victim: Request, plan: StepPlan) -> None:
+        self.running.remove(victim)
+        self.release(victim)
+        # restart from scratch: generated tokens become part of the prompt
+        if victim.output:
+            victim.prompt = np.concatenate([victim.prompt, np.asarray(victim.output, dtype=np.int32)])
+            victim.max_new_tokens -= len(victim.output)
+            victim.output = []
+        victim.cached = 0
+        victim.state = State.WAITING
+        victim.preemptions += 1
+        self.waiting.appendleft(victim)
+        plan.preempted.append(victim)
+
+    def schedule(self) -> StepPlan:
+        plan = StepPlan()
+        # 1. decode: every request whose prompt is fully cached
+        for req in list(self.running):
+            if req.state != State.DECODE or req not in self.running:
+                continue
+            while not self._grow(req, req.total_len):
+                victim = self.running[-1]
+                if victim is req and len(self.running) == 1:
+                    raise MemoryError("KV cache too small for a single request")
+                self._preempt(victim, plan)
+                if victim is req:
+                    break
+            if req in self.running:
+                plan.decode.append(req)
+        # 2. prefill: continue partial prefills, then admit new requests
+        budget = self.max_prefill_tokens
+        for req in self.running:
+            if budget <= 0:
+                break
+            if req.state == State.PREFILL:
+                n = min(budget, req.prompt_len - req.cached)
+                if n > 0 and self._grow(req, req.cached + n):
+                    plan.prefill.append((req, req.cached, n))
+                    budget -= n
+        while budget > 0 and self.waiting and len(self.running) < self.max_batch:
+            req = self.waiting[0]
+            n = min(budget, req.prompt_len)
+            # keep room for the decode pages of everything already running
+            reserve = len(plan.decode)
+            if self._pages_needed(req, n) + reserve > self.alloc.free:
+                break
+            if not self._grow(req, n):
+                break
+            self.waiting.popleft()
+            req.state = State.PREFILL
+            self.running.append(req)
+            plan.prefill.append((req, 0, n))
+            budget -= n
+        return plan
+
+    def commit(self, plan: StepPlan, sampled: dict, now: float) -> list:
+        """Apply one step's results. ``sampled`` maps rid -> next token for
+        every request that produced one. Returns the requests that finished."""
+        done = []
+        for req, start, n in plan.prefill:
+            req.cached = start + n
+            if req.cached >= req.prompt_len:
+                req.state = State.DECODE
+        for req in plan.decode:
+            req.cached = req.total_len
+        for req in list(plan.decode) + [r for r, _, _ in plan.prefill]:
+            tok = sampled.get(req.rid)
+            if tok is None:
+                continue
+            req.output.append(int(tok))
+            req.token_times.append(now)
+            if req.finished:
+                req.state = State.DONE
+                if req in self.running:
+                    self.running.remove(req)
+                self.release(req)
+                done.append(req)
+        return done

@@ -1,0 +1,251 @@
+"""Llama-architecture decoder (Llama-3 8B / 70B shapes) on the sm_100a kernels.
+
+Weights are random (normal, std 1/sqrt(fan_in)) and created directly on the
+device, sharded for tensor parallelism: column-parallel QKV and gate/up
+(each rank owns whole heads / whole FFN columns), row-parallel o_proj and
+down_proj (their partial sums are reduced across ranks by the fused
+GEMM + all-reduce kernels of ``parallel.tp``), vocabulary-parallel LM head.
+
+One forward handles a mixed batch: the first ``n_decode`` token rows are
+decode tokens (one per running request), the rest are prefill chunks. All
+projections, norms and RoPE run once over all rows; attention splits into
+the decode kernel (rows [0, n_decode)) and the prefill kernel (the rest).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from .. import ops
+from .config import ModelConfig
+
+GATE_UP_BLOCK = 64  # gate/up interleave granularity of the SwiGLU GEMM epilogue
+
+
+def rope_table(cfg: ModelConfig, max_pos: int, device) -> torch.Tensor:
+    """[max_pos, head_dim/2, 2] float32 (cos, sin) for rotate-half RoPE."""
+    half = cfg.head_dim // 2
+    inv = cfg.rope_theta ** (-torch.arange(0, half, dtype=torch.float64) * 2.0 / cfg.head_dim)
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.stack([ang.cos(), ang.sin()], dim=-1).to(torch.float32).to(device).contiguous()
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = GATE_UP_BLOCK) -> torch.Tensor:
+    """[I, H] gate and up -> [2I, H] with blocks (gate[j:j+64], up[j:j+64])."""
+    I, H = gate.shape
+    assert I % block == 0
+    g = gate.reshape(I // block, block, H)
+    u = up.reshape(I // block, block, H)
+    return torch.stack([g, u], dim=1).reshape(2 * I, H).contiguous()
+
+
+def deinterleave_gate_up(w: torch.Tensor, block: int = GATE_UP_BLOCK):
+    I2, H = w.shape
+    v = w.reshape(I2 // (2 * block), 2, block, H)
+    return v[:, 0].reshape(-1, H), v[:, 1].reshape(-1, H)
+
+
+@dataclass
+class LayerWeights:
+    ln_in: torch.Tensor
+    qkv: torch.Tensor      # [(hq + 2 hkv) * D, H]   (this rank's heads)
+    o: torch.Tensor        # [H, hq * D]
+    ln_post: torch.Tensor
+    gate_up: torch.Tensor  # [2 * I_local, H] interleaved (dense layers)
+    down: torch.Tensor     # [H, I_local]
+    moe: object = None     # parallel.ep.MoEWeights for expert layers
+
+
+@dataclass
+class ModelWeights:
+    embed: torch.Tensor     # [V, H] (replicated)
+    layers: list
+    ln_final: torch.Tensor
+    lm_head: torch.Tensor   # [V_local, H]
+    vocab_offset: int = 0
+
+
+def _normal(shape, std, device, gen):
+    t = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    t.normal_(0.0, std, generator=gen)
+    return t
+
+
+def init_weights(cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int = 1, seed: int = 0,
+                 moe_builder=None) -> ModelWeights:
+    """Random weights of this rank's shard (no full tensor is materialised)."""
+    assert cfg.n_q_heads % tp_size == 0 and cfg.n_kv_heads % tp_size == 0
+    assert cfg.ffn % (tp_size * GATE_UP_BLOCK) == 0 and cfg.vocab % tp_size == 0 or True
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed * 1000003 + tp_rank)
+    H, D = cfg.hidden, cfg.head_dim
+    hq, hkv = cfg.n_q_heads // tp_size, cfg.n_kv_heads // tp_size
+    I = cfg.ffn // tp_size
+    ones = lambda: torch.ones(H, dtype=torch.bfloat16, device=device)
+    layers = []
+    for li in range(cfg.n_layers):
+        lw = LayerWeights(
+            ln_in=ones(),
+            qkv=_normal(((hq + 2 * hkv) * D, H), 1.0 / math.sqrt(H), device, gen),
+            o=_normal((H, hq * D), 1.0 / math.sqrt(cfg.n_q_heads * D), device, gen),
+            ln_post=ones(),
+            gate_up=None if cfg.n_experts else _normal((2 * I, H), 1.0 / math.sqrt(H), device, gen),
+            down=None if cfg.n_experts else _normal((H, I), 1.0 / math.sqrt(cfg.ffn), device, gen),
+        )
+        if cfg.n_experts:
+            lw.moe = moe_builder(li, gen)
+        layers.append(lw)
+    v_local = (cfg.vocab + tp_size - 1) // tp_size
+    v_local = (v_local + 127) // 128 * 128  # GEMM row tiles
+    # the embedding is replicated: same seed on every rank
+    egen = torch.Generator(device=device)
+    egen.manual_seed(seed * 1000003 + 7777)
+    embed = _normal((cfg.vocab, H), 1.0, device, egen)
+    lm = _normal((v_local, H), 1.0 / math.sqrt(H), device, gen)
+    return ModelWeights(embed=embed, layers=layers, ln_final=ones(), lm_head=lm,
+                        vocab_offset=tp_rank * v_local)
+
+
+@dataclass
+class ForwardBatch:
+    """Device inputs of one forward (static buffers when graph-captured)."""
+
+    ids: torch.Tensor          # [T] int32
+    pos: torch.Tensor          # [T] int32 absolute positions
+    slot: torch.Tensor         # [T] int32 KV slot = page * 16 + offset (-1: no write)
+    n_tokens: int
+    n_decode: int
+    block_table: torch.Tensor  # [R, max_pages] int32, rows = batch requests
+    kv_lens: torch.Tensor      # [R] int32 (tokens in the cache after this step)
+    # decode attention plan
+    items: torch.Tensor | None = None       # [n_items, 4] int32
+    n_items: int = 0
+    part_o: torch.Tensor | None = None
+    part_lse: torch.Tensor | None = None
+    merge_req: torch.Tensor | None = None
+    merge_begin: torch.Tensor | None = None
+    n_merge: int = 0
+    # prefill attention plan
+    tiles: torch.Tensor | None = None       # [n_tiles, 4] int32
+    n_tiles: int = 0
+    # rows whose logits are sampled
+    sample_idx: torch.Tensor | None = None  # [S] int64
+    n_sample: int = 0
+    out_ids: torch.Tensor | None = None     # [S] int32
+    # scheduling tables for the woven decode kernel
+    slots: dict | None = None
+    acquire: int = 0
+    grid: int = 0
+
+
+class KVCache:
+    """Paged KV pool: per layer [pages, Hkv_local, 16, D] for K and for V.
+
+    Zero-initialised: pages beyond a request's last token are read by the
+    block-granular decode kernel with probability weight zero, and must hold
+    finite values."""
+
+    def __init__(self, cfg: ModelConfig, num_pages: int, device, tp_size: int = 1, page_size: int = 16):
+        self.page_size = page_size
+        self.num_pages = num_pages
+        hkv = cfg.n_kv_heads // tp_size
+        self.k = torch.zeros(cfg.n_layers, num_pages, hkv, page_size, cfg.head_dim,
+                             dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros_like(self.k)
+
+    def bytes(self) -> int:
+        return 2 * self.k.numel() * self.k.element_size()
+
+
+class Llama:
+    """Forward pass of one tensor-parallel rank."""
+
+    def __init__(self, cfg: ModelConfig, weights: ModelWeights, kv: KVCache, device,
+                 tp=None, max_tokens: int = 8192, max_pos: int = 8192):
+        self.cfg = cfg
+        self.w = weights
+        self.kv = kv
+        self.device = torch.device(device)
+        self.tp = tp
+        self.tp_size = tp.world if tp is not None else 1
+        self.hq = cfg.n_q_heads // self.tp_size
+        self.hkv = cfg.n_kv_heads // self.tp_size
+        self.cos_sin = rope_table(cfg, max_pos, self.device)
+        self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
+        self.max_tokens = max_tokens
+        self._alloc(max_tokens)
+
+    def _alloc(self, T: int) -> None:
+        cfg, dev = self.cfg, self.device
+        bf = torch.bfloat16
+        self.h = torch.empty(T, cfg.hidden, dtype=bf, device=dev)       # residual stream
+        self.normed = torch.empty(T, cfg.hidden, dtype=bf, device=dev)
+        self.delta = torch.empty(T, cfg.hidden, dtype=bf, device=dev)
+        self.qkv = torch.empty(T, (self.hq + 2 * self.hkv) * cfg.head_dim, dtype=bf, device=dev)
+        self.q = torch.empty(T, self.hq, cfg.head_dim, dtype=bf, device=dev)
+        self.attn = torch.empty(T, self.hq, cfg.head_dim, dtype=bf, device=dev)
+        ffn_local = cfg.ffn // self.tp_size
+        self.act = torch.empty(T, ffn_local, dtype=bf, device=dev)
+
+    # row-parallel projection: partial sums reduced across TP ranks
+    def _row_linear(self, x, w, out):
+        if self.tp is None:
+            return ops.linear(x, w, out)
+        return self.tp.linear_allreduce(x, w, out)
+
+    def _attention(self, li: int, b: ForwardBatch) -> None:
+        kc, vc = self.kv.k[li], self.kv.v[li]
+        nd = b.n_decode
+        if nd > 0:
+            q = self.q[:nd]
+            out = self.attn[:nd]
+            ops.attention_decode(q, out, kc, vc, b.block_table, b.items, b.n_items, self.sm_scale,
+                                 part_o=b.part_o, part_lse=b.part_lse, slots=b.slots,
+                                 woven=b.slots is not None, acquire=b.acquire, grid=b.grid)
+            if b.n_merge > 0:
+                ops.attention_merge(b.part_o, b.part_lse, b.merge_req, b.merge_begin, b.n_merge, out)
+        if b.n_tiles > 0:
+            T = b.n_tokens
+            ops.attention_prefill(self.q[nd:T], self.attn[nd:T], kc, vc, b.block_table, b.kv_lens,
+                                  b.tiles, b.n_tiles, self.sm_scale)
+
+    def _mlp(self, li: int, x: torch.Tensor, T: int) -> torch.Tensor:
+        lw = self.w.layers[li]
+        act = ops.linear(x, lw.gate_up, self.act[:T], swiglu=True)
+        return self._row_linear(act, lw.down, self.delta[:T])
+
+    def forward(self, b: ForwardBatch) -> torch.Tensor:
+        cfg = self.cfg
+        T = b.n_tokens
+        h, normed, delta = self.h[:T], self.normed[:T], self.delta[:T]
+        ops.embedding(b.ids[:T], self.w.embed, h)
+        for li, lw in enumerate(self.w.layers):
+            if li == 0:
+                ops.add_rmsnorm(h, None, lw.ln_in, cfg.rms_eps, normed)
+            else:
+                ops.add_rmsnorm(delta, h, lw.ln_in, cfg.rms_eps, normed)
+            ops.linear(normed, lw.qkv, self.qkv[:T])
+            ops.rope_kv_append(self.qkv[:T], b.pos[:T], b.slot[:T], self.cos_sin, self.q[:T],
+                               self.kv.k[li], self.kv.v[li], self.hq, self.hkv)
+            self._attention(li, b)
+            self._row_linear(self.attn[:T].view(T, -1), lw.o, delta)
+            ops.add_rmsnorm(delta, h, lw.ln_post, cfg.rms_eps, normed)
+            d = self._mlp(li, normed, T)
+            if d is not delta:
+                delta.copy_(d)
+        ops.add_rmsnorm(delta, h, self.w.ln_final, cfg.rms_eps, normed)
+        return self.sample(b)
+
+    def sample(self, b: ForwardBatch) -> torch.Tensor:
+        """Greedy next token of the rows in ``b.sample_idx``."""
+        S = b.n_sample
+        if S == 0:
+            return b.out_ids[:0]
+        rows = self.normed.index_select(0, b.sample_idx[:S]) if b.sample_idx is not None else self.normed[:S]
+        if self.tp is None:
+            logits = ops.linear(rows, self.w.lm_head)
+            return ops.argmax(logits[:, :self.cfg.vocab], b.out_ids[:S])
+        return self.tp.sharded_argmax(rows, self.w.lm_head, self.w.vocab_offset, self.cfg.vocab,
+                                      b.out_ids[:S])

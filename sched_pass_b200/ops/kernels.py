@@ -1,0 +1,159 @@
+"""Thin wrappers: allocate outputs, own the per-device scratch, call the
+native launchers on the current stream. No computation happens in Python."""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from .._ext import ext
+
+_lock = threading.Lock()
+_status: dict[int, torch.Tensor] = {}
+_ws: dict[tuple[int, int], "Workspace"] = {}
+
+
+def status_buffer(device=None) -> torch.Tensor:
+    """The int32 word kernels write a KernelStatus code into when a bounded
+    wait gives up (0 = OK)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    with _lock:
+        t = _status.get(idx)
+        if t is None:
+            t = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+            _status[idx] = t
+    return t
+
+
+STATUS_NAMES = {0: "ok", 1: "tma-timeout", 2: "mma-timeout", 3: "epilogue-timeout",
+                4: "peer-timeout", 5: "clc-timeout", 6: "bad-argument"}
+
+
+def check_status(device=None, clear: bool = True) -> int:
+    """Read (and clear) the status word; raises on a non-zero code."""
+    s = status_buffer(device)
+    code = int(s.item())
+    if clear and code:
+        s.zero_()
+    if code:
+        raise RuntimeError(f"kernel reported status {code} ({STATUS_NAMES.get(code, '?')})")
+    return code
+
+
+class Workspace:
+    """Split-K scratch of the GEMM: one fp32 partial-tile slice per split and
+    per-tile arrival counters. The counters stay zero between calls (the last
+    split of a tile resets its counter), so they are zeroed once here. One
+    workspace per stream: calls that share it must be stream-ordered."""
+
+    def __init__(self, device, floats: int = 1 << 23, counters: int = 1 << 16):
+        self.device = torch.device(device)
+        self.ws = torch.zeros(floats, dtype=torch.float32, device=self.device)
+        self.counters = torch.zeros(counters, dtype=torch.int32, device=self.device)
+
+    def fits(self, T: int, N: int, splits: int) -> bool:
+        tn = 16 if T <= 16 else 32 if T <= 32 else 64 if T <= 64 else 128 if T <= 128 else 256
+        t_pad = (T + tn - 1) // tn * tn
+        return (splits * t_pad * N <= self.ws.numel()
+                and (N // 128) * (t_pad // tn) <= self.counters.numel())
+
+
+def workspace(device=None, stream_key: int = 0) -> Workspace:
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    with _lock:
+        w = _ws.get((idx, stream_key))
+        if w is None:
+            w = Workspace(f"cuda:{idx}")
+            _ws[(idx, stream_key)] = w
+    return w
+
+
+_sm_count: dict[int, int] = {}
+
+
+def _sms(dev: torch.device) -> int:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    n = _sm_count.get(idx)
+    if n is None:
+        n = torch.cuda.get_device_properties(idx).multi_processor_count
+        _sm_count[idx] = n
+    return n
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *,
+           swiglu: bool = False, splits: int | None = None, ws: Workspace | None = None) -> torch.Tensor:
+    """y = x @ w.T on the tcgen05 GEMM. ``swiglu``: w holds interleaved
+    gate/up rows (64 gate rows, then their 64 up rows, per 128-row tile) and
+    y = silu(gate) * up with N/2 columns."""
+    T, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(T, N // 2 if swiglu else N, dtype=torch.bfloat16, device=x.device)
+    E = ext()
+    if splits is None:
+        splits = E.gemm_split_count(T, N, K, _sms(x.device))
+    if splits > 1:
+        ws = ws or workspace(x.device)
+        if not ws.fits(T, N, splits):
+            splits = 1
+    E.gemm(x, w, out, 1 if swiglu else 0, int(splits),
+           ws.ws if (splits > 1 and ws is not None) else None,
+           ws.counters if (splits > 1 and ws is not None) else None,
+           status_buffer(x.device))
+    return out
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor, eps: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """residual += x (in place, when given); returns rmsnorm(residual or x) * weight."""
+    if out is None:
+        out = torch.empty_like(x)
+    ext().add_rmsnorm(x, residual, weight, out, float(eps))
+    return out
+
+
+def rope_kv_append(qkv: torch.Tensor, pos: torch.Tensor, slot: torch.Tensor, cos_sin: torch.Tensor,
+                   q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                   n_q_heads: int, n_kv_heads: int) -> torch.Tensor:
+    ext().rope_kv_append(qkv, pos, slot, cos_sin, q_out, k_cache, v_cache, n_q_heads, n_kv_heads)
+    return q_out
+
+
+def attention_decode(q, out, k_cache, v_cache, block_table, items, num_items, sm_scale, *,
+                     part_o=None, part_lse=None, slots=None, woven=True, acquire=0, grid=0,
+                     pf_blocks=2, dT=1.0, dR=1.0, H=0.25):
+    s = slots or {}
+    ext().attn_decode(q, out, k_cache, v_cache, block_table, items, int(num_items), float(sm_scale),
+                      part_o, part_lse, s.get("order"), s.get("ctrl"), s.get("timer"),
+                      s.get("queue"), int(s.get("max_tasks", 0)), int(bool(woven)), int(acquire),
+                      int(grid), int(pf_blocks), float(dT), float(dR), float(H),
+                      status_buffer(q.device))
+    return out
+
+
+def attention_merge(part_o, part_lse, merge_req, merge_begin, rows, out):
+    ext().attn_merge(part_o, part_lse, merge_req, merge_begin, int(rows), out)
+    return out
+
+
+def attention_prefill(q, out, k_cache, v_cache, block_table, kv_lens, tiles, num_tiles, sm_scale):
+    ext().attn_prefill(q, out, k_cache, v_cache, block_table, kv_lens, tiles, int(num_tiles),
+                       float(sm_scale))
+    return out
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    ext().embedding(ids, table, out)
+    return out
+
+
+def argmax(logits: torch.Tensor, out: torch.Tensor | None = None, maxv: torch.Tensor | None = None,
+           id_offset: int = 0) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    ext().argmax(logits, out, maxv, int(id_offset))
+    return out

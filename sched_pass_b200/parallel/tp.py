@@ -1,0 +1,85 @@
+"""Tensor parallelism over NVLink: process group, row-parallel reductions,
+vocabulary-parallel sampling.
+
+``TensorParallel.linear_allreduce`` is the row-parallel projection
+(o_proj, down_proj): every rank multiplies its K-shard and the partial sums
+are added across ranks. Two implementations share the interface:
+
+* ``fused`` (default on >= 2 GPUs): one sm_100a kernel per projection that
+  runs the tcgen05 GEMM and pushes each finished fp32 tile to every peer's
+  symmetric buffer over NVLink (peer stores), then reduces the peers' tiles
+  locally after a per-tile flag handshake (``comm/fused_collective.cu``);
+* ``nccl``: the GEMM kernel followed by ``all_reduce`` on NCCL -- the
+  baseline the fused path is measured against.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+
+class TensorParallel:
+    def __init__(self, group=None, mode: str | None = None, device=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device) if device is not None else torch.device(
+            "cuda", torch.cuda.current_device())
+        self.mode = mode or os.environ.get("SCHED_TP_MODE", "fused")
+        self._fused = None
+        if self.mode == "fused" and self.world > 1:
+            from .fused import FusedAllReduce
+            self._fused = FusedAllReduce(self.group, self.device)
+
+    def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return ops.linear(x, w, out)
+        if self._fused is not None:
+            return self._fused.linear_allreduce(x, w, out)
+        ops.linear(x, w, out)
+        dist.all_reduce(out, group=self.group)
+        return out
+
+    def sharded_argmax(self, rows: torch.Tensor, lm_head: torch.Tensor, vocab_offset: int, vocab: int,
+                       out: torch.Tensor) -> torch.Tensor:
+        """Greedy token over a vocabulary split across ranks: local logits and
+        local (max, argmax), exchange the pairs, keep the best (lowest global
+        id on ties)."""
+        S = rows.shape[0]
+        logits = ops.linear(rows, lm_head)
+        v_local = min(lm_head.shape[0], max(0, vocab - vocab_offset))
+        ids = torch.empty(S, dtype=torch.int32, device=rows.device)
+        mx = torch.empty(S, dtype=torch.float32, device=rows.device)
+        ops.argmax(logits[:, :v_local], ids, mx, vocab_offset)
+        pair = torch.stack([mx, ids.float()], dim=0)  # exact for ids < 2^24
+        allp = torch.empty(self.world, 2, S, dtype=torch.float32, device=rows.device)
+        dist.all_gather_into_tensor(allp, pair, group=self.group)
+        vals, gids = allp[:, 0], allp[:, 1]
+        best = vals.max(dim=0).values
+        cand = torch.where(vals == best[None], gids, torch.full_like(gids, float(2 ** 30)))
+        out.copy_(cand.min(dim=0).values.to(torch.int32))
+        return out
+
+    def barrier(self) -> None:
+        dist.barrier(group=self.group)
+
+
+def init_distributed(backend: str = "nccl", timeout_s: float = 120.0):
+    """Initialise torch.distributed from torchrun's environment (127.0.0.1
+    rendezvous). Returns (rank, world, local_rank)."""
+    import datetime
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend=backend, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=timeout_s),
+                                device_id=torch.device("cuda", local) if backend == "nccl" else None)
+    return rank, world, local

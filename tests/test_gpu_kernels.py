@@ -1,0 +1,297 @@
+"""Numerics of the sm_100a kernels against plain fp32 PyTorch statements."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from sched_pass_b200 import ops
+from sched_pass_b200.models import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _clean_status():
+    yield
+    ops.check_status()
+
+
+# ------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("T", [1, 5, 16, 33, 64, 100, 128, 200, 257])
+@pytest.mark.parametrize("NK", [(128, 64), (384, 256), (1024, 512)])
+@pytest.mark.parametrize("split", [1, 3])
+def test_gemm_matches_fp32(T, NK, split):
+    N, K = NK
+    g = torch.Generator(device=DEV).manual_seed(T * 31 + N)
+    x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    y = ops.linear(x, w, splits=split)
+    torch.cuda.synchronize()
+    assert rel_err(y, ref.linear(x, w)) < 1e-2
+
+
+@pytest.mark.parametrize("T", [3, 64, 300])
+@pytest.mark.parametrize("split", [1, 4])
+def test_gemm_swiglu(T, split):
+    I, K = 256, 512
+    g = torch.Generator(device=DEV).manual_seed(7)
+    x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(2 * I, K, device=DEV, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    y = ops.linear(x, w, swiglu=True, splits=split)
+    torch.cuda.synchronize()
+    assert y.shape == (T, I)
+    assert rel_err(y, ref.swiglu_linear(x, w)) < 1e-2
+
+
+def test_gemm_split_workspace_stays_clean():
+    # different problems through one workspace: none may see another's partial
+    # sums, the arrival counters return to zero, and split-K is deterministic
+    x = torch.randn(8, 1024, device=DEV).to(torch.bfloat16)
+    w1 = torch.randn(512, 1024, device=DEV).to(torch.bfloat16)
+    w2 = torch.randn(512, 1024, device=DEV).to(torch.bfloat16)
+    ys = []
+    for w in (w1, w2, w1):
+        y = ops.linear(x, w, splits=4)
+        assert rel_err(y, ref.linear(x, w)) < 1e-2
+        ys.append(y)
+    assert torch.equal(ys[0], ys[2])
+    ws = ops.workspace()
+    torch.cuda.synchronize()
+    assert ws.counters.abs().max().item() == 0
+
+
+def test_gemm_large_prefill_shape():
+    T, N, K = 1536, 1024, 4096
+    x = torch.randn(T, K, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV) / 64).to(torch.bfloat16)
+    assert rel_err(ops.linear(x, w), ref.linear(x, w)) < 1e-2
+
+
+# ------------------------------------------------------------------ elementwise
+def test_add_rmsnorm():
+    T, H = 7, 4096
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    r = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    w = torch.randn(H, device=DEV).to(torch.bfloat16)
+    r0 = r.clone()
+    y = ops.add_rmsnorm(x, r, w, 1e-5)
+    s = (x.float() + r0.float()).to(torch.bfloat16)
+    assert torch.equal(r, s)
+    assert rel_err(y, ref.rmsnorm(s, w, 1e-5)) < 1e-2
+    y2 = ops.add_rmsnorm(x, None, w, 1e-5)
+    assert rel_err(y2, ref.rmsnorm(x, w, 1e-5)) < 1e-2
+
+
+def test_rope_kv_append():
+    from sched_pass_b200.models.config import LLAMA_TINY
+    from sched_pass_b200.models.llama import rope_table
+    cfg = LLAMA_TINY
+    T, Hq, Hkv, D = 5, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim
+    cs = rope_table(cfg, 1024, DEV)
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV).to(torch.bfloat16)
+    pos = torch.tensor([0, 3, 17, 100, 999], dtype=torch.int32, device=DEV)
+    slot = torch.tensor([5 * 16 + 0, 2 * 16 + 3, 7 * 16 + 1, -1, 0], dtype=torch.int32, device=DEV)
+    kc = torch.zeros(8, Hkv, 16, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=DEV)
+    ops.rope_kv_append(qkv, pos, slot, cs, q, kc, vc, Hq, Hkv)
+    v = qkv.view(T, Hq + 2 * Hkv, D)
+    q_ref = ref.rope(v[:, :Hq], pos, cs)
+    k_ref = ref.rope(v[:, Hq:Hq + Hkv], pos, cs)
+    assert rel_err(q, q_ref) < 1e-2
+    for t in range(T):
+        s = int(slot[t])
+        if s < 0:
+            continue
+        assert rel_err(kc[s // 16, :, s % 16], k_ref[t]) < 1e-2
+        assert torch.equal(vc[s // 16, :, s % 16], v[t, Hq + Hkv:])
+
+
+def test_embedding_and_argmax():
+    table = torch.randn(1000, 512, device=DEV).to(torch.bfloat16)
+    ids = torch.tensor([3, 999, 0, 17], dtype=torch.int32, device=DEV)
+    assert torch.equal(ops.embedding(ids, table), table[ids.long()])
+    logits = torch.randn(6, 128256, device=DEV).to(torch.bfloat16)
+    logits[2, 77777] = 100.0
+    got = ops.argmax(logits)
+    assert torch.equal(got.long(), logits.float().argmax(-1))
+    assert got[2].item() == 77777
+
+
+# ------------------------------------------------------------------ decode attention
+def make_paged(B, Hkv, lens, seed=0, pages_extra=7):
+    D = 128
+    total_pages = sum((int(n) + 15) // 16 for n in lens) + pages_extra
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(total_pages, generator=g)
+    kc = torch.randn(total_pages, Hkv, 16, D, generator=g).to(torch.bfloat16).to(DEV)
+    vc = torch.randn(total_pages, Hkv, 16, D, generator=g).to(torch.bfloat16).to(DEV)
+    maxp = max((int(n) + 15) // 16 for n in lens)
+    bt = torch.zeros(B, maxp, dtype=torch.int32)
+    k = 0
+    for b, n in enumerate(lens):
+        npg = (int(n) + 15) // 16
+        bt[b, :npg] = perm[k:k + npg]
+        k += npg
+    return kc, vc, bt.to(DEV)
+
+
+def run_decode(q, kc, vc, bt, lens, S=1, slots=None, woven=False, acquire=0, grid=0):
+    from sched_pass_b200.engine import native
+    B, Hq, D = q.shape
+    items, mreq, mbeg = native.plan_decode(np.asarray(lens, dtype=np.int32), S)
+    it = torch.from_numpy(items).to(DEV)
+    out = torch.zeros_like(q)
+    po = pl = None
+    if S > 1:
+        po = torch.zeros(B * S, Hq, D, dtype=torch.float32, device=DEV)
+        pl = torch.zeros(B * S, Hq, dtype=torch.float32, device=DEV)
+    ops.attention_decode(q, out, kc, vc, bt, it, items.shape[0], 1 / math.sqrt(D), part_o=po,
+                         part_lse=pl, slots=slots, woven=woven, acquire=acquire, grid=grid)
+    if S > 1:
+        ops.attention_merge(po, pl, torch.from_numpy(mreq).to(DEV), torch.from_numpy(mbeg).to(DEV), B, out)
+    torch.cuda.synchronize()
+    return out, items
+
+
+LENS = [1, 15, 16, 17, 127, 128, 129, 300, 1000, 2049]
+
+
+@pytest.mark.parametrize("G", [1, 4, 8])
+def test_decode_attention_stock(G):
+    Hkv = 2
+    B = len(LENS)
+    kc, vc, bt = make_paged(B, Hkv, LENS, seed=G)
+    q = torch.randn(B, Hkv * G, 128, device=DEV).to(torch.bfloat16)
+    out, _ = run_decode(q, kc, vc, bt, LENS)
+    r = ref.decode_attention_paged(q, kc, vc, bt, LENS, 1 / math.sqrt(128))
+    assert rel_err(out, r) < 2e-2
+
+
+@pytest.mark.parametrize("S", [2, 3, 8])
+def test_decode_attention_split_kv(S):
+    Hkv, G = 2, 4
+    B = len(LENS)
+    kc, vc, bt = make_paged(B, Hkv, LENS, seed=S)
+    q = torch.randn(B, Hkv * G, 128, device=DEV).to(torch.bfloat16)
+    out, _ = run_decode(q, kc, vc, bt, LENS, S=S)
+    r = ref.decode_attention_paged(q, kc, vc, bt, LENS, 1 / math.sqrt(128))
+    assert rel_err(out, r) < 2e-2
+
+
+def _plane(n_tasks):
+    from sched_pass_b200.runtime.sched_rt import SchedPlane
+    return SchedPlane(max_tasks=max(n_tasks, 64), device=DEV, mode="device")
+
+
+def test_decode_levers_null_tables_are_bit_exact():
+    Hkv, G = 2, 4
+    B = len(LENS)
+    kc, vc, bt = make_paged(B, Hkv, LENS, seed=11)
+    q = torch.randn(B, Hkv * G, 128, device=DEV).to(torch.bfloat16)
+    stock, _ = run_decode(q, kc, vc, bt, LENS, woven=False)
+    woven_null, _ = run_decode(q, kc, vc, bt, LENS, woven=True, slots=None)
+    assert torch.equal(stock, woven_null)
+    p = _plane(B * Hkv)
+    neutral, _ = run_decode(q, kc, vc, bt, LENS, woven=True, slots=p.slots())
+    assert torch.equal(stock, neutral)
+
+
+def test_decode_pi_reversed_and_lpt_bit_exact_with_timer():
+    Hkv, G = 2, 4
+    B = len(LENS)
+    n = B * Hkv
+    kc, vc, bt = make_paged(B, Hkv, LENS, seed=12)
+    q = torch.randn(B, Hkv * G, 128, device=DEV).to(torch.bfloat16)
+    stock, items = run_decode(q, kc, vc, bt, LENS)
+    p = _plane(n)
+    p.install_order(torch.arange(n - 1, -1, -1, dtype=torch.int32), n)
+    p.set_timer_enabled(True)
+    p.push()
+    p.clear_timer()
+    rev, _ = run_decode(q, kc, vc, bt, LENS, woven=True, slots=p.slots())
+    assert torch.equal(stock, rev)
+    cyc = p.read_timer()[:n]
+    assert (cyc > 0).all(), "every task's timer row must be filled"
+    # timer switched off -> rows stay zero; order_size mismatch -> identity (still exact)
+    p.set_timer_enabled(False)
+    p.set_order_size(n + 1)
+    p.push()
+    p.clear_timer()
+    again, _ = run_decode(q, kc, vc, bt, LENS, woven=True, slots=p.slots())
+    assert torch.equal(stock, again)
+    assert int(p.read_timer()[:n].abs().sum()) == 0
+
+
+def test_decode_shed_is_exact_truncated_softmax():
+    Hkv, G = 2, 4
+    B = len(LENS)
+    n = B * Hkv
+    kc, vc, bt = make_paged(B, Hkv, LENS, seed=13)
+    q = torch.randn(B, Hkv * G, 128, device=DEV).to(torch.bfloat16)
+    taus = [max(1, L // 2) for L in LENS]
+    p = _plane(n)
+    p.set_rows(tau=np.repeat(np.asarray(taus), Hkv), n=n)
+    p.push()
+    out, _ = run_decode(q, kc, vc, bt, LENS, woven=True, slots=p.slots())
+    r = ref.decode_attention_paged(q, kc, vc, bt, LENS, 1 / math.sqrt(128), taus=taus)
+    assert rel_err(out, r) < 2e-2
+
+
+@pytest.mark.parametrize("acquire", [1, 2])
+def test_decode_work_queue_bit_exact(acquire):
+    Hkv, G = 8, 4
+    lens = list(np.random.default_rng(5).integers(16, 4000, size=64))
+    B = len(lens)
+    n = B * Hkv
+    kc, vc, bt = make_paged(B, Hkv, lens, seed=14)
+    q = torch.randn(B, Hkv * G, 128, device=DEV).to(torch.bfloat16)
+    stock, _ = run_decode(q, kc, vc, bt, lens)
+    p = _plane(n)
+    cost = torch.tensor([float(lens[t // Hkv]) for t in range(n)])
+    p.install_order(p.region_order(cost, 148), n)
+    p.set_num_tasks(n)
+    p.set_timer_enabled(True)
+    p.push()
+    p.clear_timer()
+    grid = 148 if acquire == 1 else 0
+    for _ in range(3):  # repeated launches: the ticket queue resets itself
+        out, _ = run_decode(q, kc, vc, bt, lens, woven=True, slots=p.slots(), acquire=acquire, grid=grid)
+        assert torch.equal(stock, out)
+    assert (p.read_timer()[:n] > 0).all()
+    assert int(p.queue_t.abs().sum()) == 0
+
+
+# ------------------------------------------------------------------ prefill attention
+@pytest.mark.parametrize("qlens,prefix", [([1, 64, 65, 200], [0, 0, 0, 0]), ([37, 128], [100, 16])])
+def test_prefill_attention(qlens, prefix):
+    Hkv, G = 2, 4
+    Hq, D = Hkv * G, 128
+    total = [q + p for q, p in zip(qlens, prefix)]
+    kc, vc, bt = make_paged(len(qlens), Hkv, total, seed=21)
+    Tq = sum(qlens)
+    q = torch.randn(Tq, Hq, D, device=DEV).to(torch.bfloat16)
+    tiles, row = [], 0
+    for b, (ql, pf) in enumerate(zip(qlens, prefix)):
+        for t0 in range(0, ql, 64):
+            tiles.append((b, row + t0, min(64, ql - t0), pf + t0))
+        row += ql
+    tt = torch.tensor(tiles, dtype=torch.int32, device=DEV)
+    kvl = torch.tensor(total, dtype=torch.int32, device=DEV)
+    out = torch.zeros_like(q)
+    ops.attention_prefill(q, out, kc, vc, bt, kvl, tt, len(tiles), 1 / math.sqrt(D))
+    torch.cuda.synchronize()
+    row = 0
+    for b, (ql, pf) in enumerate(zip(qlens, prefix)):
+        k = ref.gather_kv(kc, bt[b], total[b])
+        v = ref.gather_kv(vc, bt[b], total[b])
+        r = ref.attention(q[row:row + ql], k, v, 1 / math.sqrt(D), causal_offset=pf)
+        assert rel_err(out[row:row + ql], r) < 2e-2
+        row += ql
