@@ -9,18 +9,16 @@
 
 #include <cstdint>
 
+#include "gemm_api.h"
 #include "sched/abi.h"
 
 extern "C" {
-int sched_gemm_bf16(const void *x, int ldx, const void *w, void *y, int ldy, int T, int N, int K,
-                    int epi, int splits, float *ws, uint32_t *counters, int *status,
-                    cudaStream_t stream);
-int sched_gemm_split_count(int T, int N, int K, int num_sms);
 int sched_attn_decode(const void *q, void *out, const void *k_cache, const void *v_cache,
                       int num_pages, const int32_t *block_table, int bt_stride, const void *items,
                       int num_items, int Hq, int Hkv, float sm_scale, float *part_o,
-                      float *part_lse, SchedSlots slots, int woven, int acquire, int grid,
-                      int pf_blocks, float dT, float dR, float H, int *status, cudaStream_t st);
+                      float *part_lse, uint32_t *merge_cnt, int splits, SchedSlots slots,
+                      int woven, int acquire, int grid, int pf_blocks, float dT, float dR,
+                      float H, int *status, cudaStream_t st);
 int sched_attn_merge(const float *part_o, const float *part_lse, const int32_t *merge_req,
                      const int32_t *merge_begin, int rows, int Hq, void *out, cudaStream_t st);
 int sched_attn_decode_occupancy(int group);
@@ -64,28 +62,87 @@ T *ptr_or_null(const c10::optional<at::Tensor> &t) {
 }
 
 // ---------------------------------------------------------------- GEMM
-void gemm(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int64_t epi, int64_t splits,
-          const c10::optional<at::Tensor> &ws, const c10::optional<at::Tensor> &counters,
-          const c10::optional<at::Tensor> &status) {
-  check_bf16(x, "x");
-  check_bf16(w, "w");
-  check_bf16(y, "y");
-  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && y.dim() == 2, "gemm expects 2-D tensors");
-  TORCH_CHECK(x.stride(1) == 1 && w.is_contiguous() && y.stride(1) == 1, "row-major operands");
-  const int T = x.size(0), K = x.size(1), N = w.size(0);
-  TORCH_CHECK(w.size(1) == K, "K mismatch");
-  TORCH_CHECK(y.size(0) >= T, "y rows");
-  TORCH_CHECK(epi == 0 ? y.size(1) >= N : y.size(1) >= N / 2, "y columns");
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(sched_gemm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0), T,
-                           N, K, epi, splits, ptr_or_null<float>(ws),
-                           ptr_or_null<uint32_t>(counters), ptr_or_null<int>(status),
-                           cur_stream()),
-           "gemm");
+int num_sms(const at::Tensor &t) {
+  static int n[64] = {0};
+  const int d = t.get_device();
+  if (d >= 0 && d < 64) {
+    if (n[d] == 0) n[d] = at::cuda::getDeviceProperties(d)->multiProcessorCount;
+    return n[d];
+  }
+  return 148;
 }
 
-int64_t gemm_split_count(int64_t T, int64_t N, int64_t K, int64_t sms) {
-  return sched_gemm_split_count(T, N, K, sms);
+GemmArgs base_args(const at::Tensor &x, const at::Tensor &w, int64_t grid,
+                   const c10::optional<at::Tensor> &ws, const c10::optional<at::Tensor> &counters,
+                   const c10::optional<at::Tensor> &status) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "gemm expects 2-D operands");
+  TORCH_CHECK(x.stride(1) == 1 && w.is_contiguous(), "row-major operands");
+  TORCH_CHECK(w.size(1) == x.size(1), "K mismatch");
+  GemmArgs a{};
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.w = w.data_ptr();
+  a.T = x.size(0);
+  a.K = x.size(1);
+  a.N = w.size(0);
+  a.grid = grid;
+  a.num_sms = num_sms(x);
+  a.ws = ptr_or_null<float>(ws);
+  a.ws_floats = (ws.has_value() && ws->defined()) ? ws->numel() : 0;
+  a.counters = ptr_or_null<uint32_t>(counters);
+  a.counter_count = (counters.has_value() && counters->defined()) ? counters->numel() : 0;
+  a.status = ptr_or_null<int>(status);
+  return a;
+}
+
+void gemm(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int64_t epi, int64_t grid,
+          const c10::optional<at::Tensor> &ws, const c10::optional<at::Tensor> &counters,
+          const c10::optional<at::Tensor> &status) {
+  GemmArgs a = base_args(x, w, grid, ws, counters, status);
+  check_bf16(y, "y");
+  TORCH_CHECK(y.dim() == 2 && y.stride(1) == 1 && y.size(0) >= a.T, "y [T, ldy]");
+  TORCH_CHECK(epi == kEpiStore ? y.size(1) >= a.N : y.size(1) >= a.N / 2, "y columns");
+  TORCH_CHECK(epi == kEpiStore || epi == kEpiSwiGLU, "use gemm_qkv_rope for the QKV epilogue");
+  a.y = y.data_ptr();
+  a.ldy = y.stride(0);
+  a.epi = epi;
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(sched_gemm_run(&a, cur_stream()), "gemm");
+}
+
+void gemm_qkv_rope(const at::Tensor &x, const at::Tensor &w, const at::Tensor &pos,
+                   const at::Tensor &slot, const at::Tensor &cos_sin, at::Tensor &q_out,
+                   at::Tensor &k_cache, at::Tensor &v_cache, int64_t Hq, int64_t Hkv,
+                   int64_t grid, const c10::optional<at::Tensor> &ws,
+                   const c10::optional<at::Tensor> &counters,
+                   const c10::optional<at::Tensor> &status) {
+  GemmArgs a = base_args(x, w, grid, ws, counters, status);
+  check_i32(pos, "pos");
+  check_i32(slot, "slot");
+  check_bf16(q_out, "q_out");
+  check_bf16(k_cache, "k_cache");
+  check_bf16(v_cache, "v_cache");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin float32");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(3) == 128 && k_cache.is_contiguous(), "cache layout");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.numel() >= a.T * Hq * 128, "q_out [T, Hq, 128]");
+  a.epi = kEpiRopeKV;
+  a.pos = pos.data_ptr<int32_t>();
+  a.slot = slot.data_ptr<int32_t>();
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.q_out = reinterpret_cast<__nv_bfloat16 *>(q_out.data_ptr());
+  a.k_cache = reinterpret_cast<__nv_bfloat16 *>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<__nv_bfloat16 *>(v_cache.data_ptr());
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.page_size = k_cache.size(2);
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(sched_gemm_run(&a, cur_stream()), "gemm_qkv_rope");
+}
+
+int64_t gemm_ws_floats(int64_t T, int64_t N, int64_t K, int64_t grid) {
+  return sched_gemm_ws_floats(T, N, K, grid);
 }
 
 // ---------------------------------------------------------------- attention
@@ -105,6 +162,7 @@ void attn_decode(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache
                  const at::Tensor &v_cache, const at::Tensor &block_table, const at::Tensor &items,
                  int64_t num_items, double sm_scale, const c10::optional<at::Tensor> &part_o,
                  const c10::optional<at::Tensor> &part_lse,
+                 const c10::optional<at::Tensor> &merge_cnt, int64_t splits,
                  const c10::optional<at::Tensor> &order, const c10::optional<at::Tensor> &ctrl,
                  const c10::optional<at::Tensor> &timer, const c10::optional<at::Tensor> &queue,
                  int64_t max_tasks, int64_t woven, int64_t acquire, int64_t grid,
@@ -128,7 +186,8 @@ void attn_decode(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache
                              k_cache.size(0), block_table.data_ptr<int32_t>(),
                              block_table.stride(0), items.data_ptr(), num_items, Hq, Hkv,
                              (float)sm_scale, ptr_or_null<float>(part_o),
-                             ptr_or_null<float>(part_lse), sl, woven, acquire, grid, pf_blocks,
+                             ptr_or_null<float>(part_lse), ptr_or_null<uint32_t>(merge_cnt),
+                             splits, sl, woven, acquire, grid, pf_blocks,
                              (float)dT, (float)dR, (float)H, ptr_or_null<int>(status),
                              cur_stream()),
            "attn_decode");
@@ -221,7 +280,8 @@ void argmax(const at::Tensor &logits, at::Tensor &ids, const c10::optional<at::T
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sched_pass_b200 sm_100a kernels";
   m.def("gemm", &gemm);
-  m.def("gemm_split_count", &gemm_split_count);
+  m.def("gemm_qkv_rope", &gemm_qkv_rope);
+  m.def("gemm_ws_floats", &gemm_ws_floats);
   m.def("attn_decode", &attn_decode);
   m.def("attn_merge", &attn_merge);
   m.def("attn_prefill", &attn_prefill);

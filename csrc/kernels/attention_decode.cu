@@ -83,6 +83,9 @@ struct Params {
   float scale_log2;  // softmax scale * log2(e)
   float *part_o;     // [parts, Hq, D] (normalised partial outputs)
   float *part_lse;   // [parts, Hq] (log2-domain LSE)
+  uint32_t *merge_cnt;  // [requests * Hkv] arrival counters (zero between calls), or null
+  int splits;           // chunks per request when merging in-kernel (part = req * splits + s)
+  int total_rows;       // rows of the cache tensor maps: pages * Hkv * 16 (an out-of-range row)
   SchedSlots slots;
   sched::PolicyConsts pc;
   int pf_blocks;  // urgent prefetch distance in KV blocks
@@ -103,6 +106,7 @@ struct Shared {
   float red_max[4][NPAD];
   float red_sum[4][NPAD];
   uint32_t tmem_base;
+  int merge_last;
 };
 
 __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t byte_in_row) {
@@ -153,13 +157,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tmK);
     ptx::prefetch_tmap(&tmV);
   }
-  // Zero the KV ring, Q and P buffers once: blocks that extend past a
-  // request's last page are never loaded, and the masked (P = 0) rows they
-  // contribute must multiply finite values.
+  // Q and P rows >= G are MMA padding and must be zero; they are never
+  // written afterwards. (KV rows past a request's last page come from
+  // out-of-range TMA boxes, which the hardware fills with zeros.)
+  if (WOVEN) sched::pdl_launch_dependents();
   {
     uint4 z = make_uint4(0, 0, 0, 0);
-    uint4 *b4 = reinterpret_cast<uint4 *>(base);
-    const int n16 = (STAGES * STAGE_BYTES + Q_BYTES + 2 * P_BYTES) / 16;
+    uint4 *b4 = reinterpret_cast<uint4 *>(q_sm);
+    const int n16 = (Q_BYTES + 2 * P_BYTES) / 16;
     for (int i = threadIdx.x; i < n16; i += kThreads) b4[i] = z;
   }
   ptx::fence_proxy_async_smem();
@@ -235,12 +240,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t *vst = kst + KV_BLOCK_BYTES;
           const int pg0 = first_page + b * PAGES_PER_BLK;
           const int npg = min(PAGES_PER_BLK, last_page - pg0);
-          const uint32_t bytes = (uint32_t)npg * PS * 128 * 2;  // two halves
-          ptx::mbar_arrive_expect_tx(&sh.k_full[s], bytes);
-          ptx::mbar_arrive_expect_tx(&sh.v_full[s], bytes);
-          for (int pi = 0; pi < npg; ++pi) {
-            const int page = __ldg(bt + pg0 + pi);
-            const int row = (page * p.Hkv + ti.kvh) * PS;
+          ptx::mbar_arrive_expect_tx(&sh.k_full[s], KV_BLOCK_BYTES);
+          ptx::mbar_arrive_expect_tx(&sh.v_full[s], KV_BLOCK_BYTES);
+          for (int pi = 0; pi < PAGES_PER_BLK; ++pi) {
+            // pages past the request's end: an out-of-range box reads zeros
+            const int row = pi < npg ? (__ldg(bt + pg0 + pi) * p.Hkv + ti.kvh) * PS : p.total_rows;
             uint8_t *kd = kst + pi * PS * 128;
             uint8_t *vd = vst + pi * PS * 128;
             if (WOVEN && ti.prio != 0) {
@@ -282,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // acquire the next task (late binding: after this task's last load)
         if (!dynamic) {
-          raw = ntasks;  // static: one task per CTA
+          raw += gridDim.x;  // static: grid-stride (one task per CTA when grid == tasks)
         } else if (ACQ == (int)sched::Acquire::Ticket) {
           raw = sl.queue != nullptr ? gridDim.x + sched::claim_ticket(sl) : ntasks;
         } else if (ACQ == (int)sched::Acquire::Clc) {
@@ -516,6 +520,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             p.part_lse[(size_t)ti.part * p.Hq + hq0 + h] =
                 l_run[h] > 0.f ? m_run[h] + __log2f(l_run[h]) : -INFINITY;
         }
+        if (p.merge_cnt != nullptr) {
+          // the last chunk of (request, KV head) to finish merges all chunks
+          __threadfence();
+          named_bar(1, kSoftmaxThreads);
+          if (t == 0) {
+            const uint32_t prev = atomicAdd(&p.merge_cnt[ti.req * p.Hkv + ti.kvh], 1u);
+            sh.merge_last = prev == (uint32_t)(p.splits - 1);
+          }
+          named_bar(1, kSoftmaxThreads);
+          if (sh.merge_last) {
+            __threadfence();
+            const int part0 = ti.req * p.splits;
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+              float mx = -INFINITY;
+              for (int s2 = 0; s2 < p.splits; ++s2)
+                mx = fmaxf(mx, __ldcg(&p.part_lse[(size_t)(part0 + s2) * p.Hq + hq0 + h]));
+              float acc = 0.f, wsum = 0.f;
+              if (mx != -INFINITY) {
+                for (int s2 = 0; s2 < p.splits; ++s2) {  // fixed order: deterministic
+                  const float w = exp2f(__ldcg(&p.part_lse[(size_t)(part0 + s2) * p.Hq + hq0 + h]) - mx);
+                  acc += w * __ldcg(&p.part_o[((size_t)(part0 + s2) * p.Hq + hq0 + h) * D + t]);
+                  wsum += w;
+                }
+              }
+              p.out[((size_t)ti.req * p.Hq + hq0 + h) * D + t] =
+                  __float2bfloat16(wsum > 0.f ? acc / wsum : 0.f);
+            }
+            if (t == 0) p.merge_cnt[ti.req * p.Hkv + ti.kvh] = 0u;
+          }
+          named_bar(1, kSoftmaxThreads);  // merge_last is rewritten by the next task
+        }
       }
       if (WOVEN && t == 0) sched::timer_commit(sl, timer_off, (uint32_t)ti.task, t0);
       ptx::mbar_arrive(&sh.task_empty[slot]);
@@ -526,7 +562,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0) ptx::tmem_dealloc(tmem, TMEM_COLS);
   if (WOVEN) {
-    sched::pdl_launch_dependents();
     // ticket queue: the last worker to leave resets the counters for the next launch
     if (ACQ == (int)sched::Acquire::Ticket && dynamic && sl.queue != nullptr && threadIdx.x == 0) {
       __threadfence();
@@ -621,13 +656,16 @@ extern "C" int sched_attn_decode_occupancy(int group) {
 
 // q [B, Hq, 128] bf16; k_cache/v_cache [pages, Hkv, 16, 128] bf16;
 // items [num_items] (req, kv_begin, kv_end, part); grid: tasks (static/CLC)
-// or workers (ticket). Returns 0 on success.
+// or workers (ticket); a static launch with fewer CTAs than tasks strides.
+// With merge_cnt, split requests (part >= 0, part = req * splits + s) are
+// merged in-kernel by the last chunk to finish. Returns 0 on success.
 extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
                                  const void *v_cache, int num_pages, const int32_t *block_table,
                                  int bt_stride, const void *items, int num_items, int Hq, int Hkv,
-                                 float sm_scale, float *part_o, float *part_lse, SchedSlots slots,
-                                 int woven, int acquire, int grid, int pf_blocks, float dT,
-                                 float dR, float H, int *status, cudaStream_t st) {
+                                 float sm_scale, float *part_o, float *part_lse,
+                                 uint32_t *merge_cnt, int splits, SchedSlots slots, int woven,
+                                 int acquire, int grid, int pf_blocks, float dT, float dR, float H,
+                                 int *status, cudaStream_t st) {
   if (num_items <= 0) return 0;
   const int G = Hq / Hkv;
   if (Hq % Hkv != 0 || (G != 1 && G != 2 && G != 4 && G != 8)) return -1;
@@ -644,6 +682,9 @@ extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.part_o = part_o;
   p.part_lse = part_lse;
+  p.merge_cnt = merge_cnt;
+  p.splits = splits > 0 ? splits : 1;
+  p.total_rows = num_pages * Hkv * attn::PS;
   p.slots = slots;
   p.pc.dT = dT;
   p.pc.dR = dR;

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 // Status codes written (first writer wins) into a caller-provided device word
 // when a bounded wait gives up. 0 = OK. The host reads and clears the word.
 enum KernelStatus : int {
@@ -36,4 +38,23 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x));
 // Named barrier among `nthreads` threads (ids 1..15 are free for kernels).
 __device__ __forceinline__ void named_bar(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous kernel in the stream drains; it must call griddepcontrol.wait
+// (ptx::pdl_wait) before touching memory that kernel writes or reads.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }

@@ -15,6 +15,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "sched/ptx.cuh"
 
 namespace ew {
 
@@ -40,6 +41,8 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const __nv_bfloat16 *__
                                                          float eps) {
   __shared__ float red[NT / 32];
   const size_t row = blockIdx.x;
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   float v[VPT][8];
   float ss = 0.f;
 #pragma unroll
@@ -137,6 +140,8 @@ __global__ void embedding_kernel(const int32_t *__restrict__ ids,
                                  const __nv_bfloat16 *__restrict__ table,
                                  __nv_bfloat16 *__restrict__ out, int H) {
   const int t = blockIdx.x;
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const size_t id = (size_t)ids[t];
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
     *reinterpret_cast<uint4 *>(out + (size_t)t * H + c) =
@@ -151,6 +156,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16 *__res
   __shared__ float sv[32];
   __shared__ int si[32];
   const int t = blockIdx.x;
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
   const __nv_bfloat16 *row = logits + (size_t)t * ld;
   float best = -INFINITY;
   int bi = 0x7fffffff;
@@ -219,11 +226,11 @@ extern "C" int sched_add_rmsnorm(const void *x, void *res, const void *w, void *
   const __nv_bfloat16 *wb = static_cast<const __nv_bfloat16 *>(w);
   __nv_bfloat16 *yb = static_cast<__nv_bfloat16 *>(y);
   if (H <= 256 * 8 * 2)
-    ew::add_rmsnorm_kernel<256, 2><<<T, 256, 0, st>>>(xb, rb, wb, yb, H, eps);
+    launch_pdl(ew::add_rmsnorm_kernel<256, 2>, T, 256, 0, st, xb, rb, wb, yb, H, eps);
   else if (H <= 512 * 8 * 2)
-    ew::add_rmsnorm_kernel<512, 2><<<T, 512, 0, st>>>(xb, rb, wb, yb, H, eps);
+    launch_pdl(ew::add_rmsnorm_kernel<512, 2>, T, 512, 0, st, xb, rb, wb, yb, H, eps);
   else if (H <= 1024 * 8 * 2)
-    ew::add_rmsnorm_kernel<1024, 2><<<T, 1024, 0, st>>>(xb, rb, wb, yb, H, eps);
+    launch_pdl(ew::add_rmsnorm_kernel<1024, 2>, T, 1024, 0, st, xb, rb, wb, yb, H, eps);
   else
     return -1;
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
@@ -245,15 +252,15 @@ extern "C" int sched_rope_kv_append(const void *qkv, const int32_t *pos, const i
 extern "C" int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int H,
                                cudaStream_t st) {
   if (T <= 0) return 0;
-  ew::embedding_kernel<<<T, 256, 0, st>>>(ids, static_cast<const __nv_bfloat16 *>(table),
-                                          static_cast<__nv_bfloat16 *>(out), H);
+  launch_pdl(ew::embedding_kernel, T, 256, 0, st, ids, static_cast<const __nv_bfloat16 *>(table),
+             static_cast<__nv_bfloat16 *>(out), H);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
 extern "C" int sched_argmax(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
                             int id_offset, cudaStream_t st) {
   if (T <= 0) return 0;
-  ew::argmax_kernel<<<T, 1024, 0, st>>>(static_cast<const __nv_bfloat16 *>(logits), V, ld, ids,
-                                        maxv, id_offset);
+  launch_pdl(ew::argmax_kernel, T, 1024, 0, st, static_cast<const __nv_bfloat16 *>(logits), V, ld,
+             ids, maxv, id_offset);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

@@ -5,31 +5,42 @@
 // Decode-first design ("swap-AB"): the MMA's M dimension runs over 128 rows
 // of the weight (output features) and its N dimension over a tile of TN
 // tokens (16..256). A decode step has few tokens and many weight rows, so the
-// weight stream -- the HBM-bound part -- always fills the 128-row MMA, and
-// the token count only sets the (cheap) N width. Prefill uses TN = 256.
+// weight stream -- the HBM-bound part -- always fills the 128-row MMA, and the
+// token count only sets the (cheap) N width. Prefill uses TN = 256.
+//
+// Persistent stream-K schedule: the k-block iterations of all tiles
+// (tiles x K/64) are split into `grid` contiguous, equal ranges, one per CTA
+// (at most one CTA per SM), so every SM streams the same number of weight
+// bytes no matter how the tile count divides the SM count. A CTA's range
+// covers one or more tile *segments*. A tile covered by one segment is
+// finished in place; otherwise each segment stores its fp32 partial into a
+// workspace slice of its CTA (two per CTA: only a CTA's first and last
+// segments can be partial) and bumps the tile's arrival counter, and the last
+// segment to arrive sums the slices in segment order (fixed order: results
+// are bit-reproducible), applies the epilogue and resets the counter to zero.
 //
 // One CTA = 6 warps:
-//   warp 0  TMA producer: one elected thread streams W and X K-blocks (64
-//           elements = one 128-byte swizzle atom) into an STAGES-deep ring;
-//   warp 1  MMA issuer: one thread issues 4 x tcgen05.mma (K = 16 each) per
-//           stage into a TMEM accumulator [128 lanes x TN columns], and
-//           tcgen05.commit frees the stage when those MMAs retire;
-//   warps 2-5 epilogue: tcgen05.ld the accumulator, stage 16-token slabs in
-//           shared memory, and write coalesced rows.
+//   warp 0  TMA producer: streams W and X K-blocks (64 elements = one
+//           128-byte swizzle atom) through an STAGES-deep ring, continuously
+//           across segment boundaries;
+//   warp 1  MMA issuer: 4 x tcgen05.mma (K = 16) per stage into one of two
+//           TMEM accumulators [128 lanes x TN columns] (segments alternate);
+//           tcgen05.commit frees each stage as its MMAs retire;
+//   warps 2-5 epilogue: tcgen05.ld the finished accumulator while the MMA
+//           warp already fills the other one, stage 16-token slabs in shared
+//           memory, write coalesced rows.
 //
-// Split-K (decode): when the (row-tile x token-tile) grid cannot fill the
-// 148 SMs, K is split S ways. Every split stores its fp32 partial tile into
-// its own slice of a workspace [S][T_pad][N]; the last split to finish a tile
-// (per-tile arrival counter) sums the S slices in split order -- a fixed
-// order, so results are bit-reproducible run to run -- applies the epilogue,
-// writes bf16 and resets the tile's counter to zero (counters stay zero
-// between calls; the partial slices need no clearing because every split
-// rewrites its slice). Calls sharing one workspace must not run concurrently.
+// Programmatic dependent launch: the producer issues the weight loads of the
+// first stages before griddepcontrol.wait (weights do not depend on the
+// previous kernel), then the activation loads; the epilogue waits before its
+// first global write. Every CTA triggers its dependents at entry.
 //
-// Epilogues: plain store, or SwiGLU over an interleaved gate/up weight whose
-// 128-row tile holds 64 gate rows followed by the 64 matching up rows
-// (out[t, j] = silu(gate) * up), which fuses the MLP activation into the
-// gate_up projection.
+// Epilogues: plain store; SwiGLU over an interleaved gate/up weight whose
+// 128-row tile holds 64 gate rows followed by the matching 64 up rows
+// (out[t, j] = silu(gate) * up); and RoPE + KV append for the fused QKV
+// projection, where a 128-row tile is exactly one head: query heads are
+// rotated into the attention input, key heads rotated and value heads copied
+// straight into their page slots of the paged KV cache.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -39,6 +50,7 @@
 #include <stdexcept>
 
 #include "common.cuh"
+#include "gemm_api.h"
 #include "sched/ptx.cuh"
 #include "tmap.h"
 
@@ -51,32 +63,140 @@ constexpr int kEpiThreads = 128;
 constexpr int kSlab = 16;  // tokens per epilogue slab
 constexpr int kSlabPitch = BM + 4;
 
-enum Epi : int { kEpiStore = 0, kEpiSwiGLU = 1 };
-
 template <int TN>
 struct Cfg {
   static constexpr int W_BYTES = BM * BK * 2;
   static constexpr int X_BYTES = TN * BK * 2;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-  static constexpr int STAGES = TN >= 256 ? 4 : (TN >= 128 ? 3 : (TN >= 64 ? 4 : 5));
-  static constexpr int TMEM_COLS = TN < 32 ? 32 : TN;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 12 ? 12 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int ACC_COLS = TN < 32 ? 32 : TN;  // one accumulator
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;       // two accumulators
   static constexpr int SLAB_BYTES = kSlab * kSlabPitch * 4;
-  static constexpr int SMEM = 1024 /*align*/ + STAGES * STAGE_BYTES + SLAB_BYTES + 256;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SLAB_BYTES + 512;
 };
 
 struct Params {
-  __nv_bfloat16 *y;
-  int T, N, K, ldy;
-  int n_tiles, t_tiles, splits, kb_per_split;
-  float *ws;           // [splits, T_pad, N] fp32 partial tiles (split > 1 only)
-  uint32_t *counters;  // [n_tiles * t_tiles], zero between calls
-  int *status;
+  GemmArgs a;
+  int n_tiles, t_tiles, kb, tiles;
+  long long units;  // tiles * kb
+  int grid;
 };
+
+// One segment: the k-block range [kb0, kb1) of `tile` handled by one CTA.
+struct Seg {
+  int tile, kb0, kb1;
+  int seg, nsegs;  // position among the tile's segments
+};
+
+__device__ __forceinline__ long long cta_begin(const Params &p, int c) {
+  return (long long)c * p.units / p.grid;
+}
+__device__ __forceinline__ int cta_of_unit(const Params &p, long long u) {
+  return (int)(((u + 1) * p.grid - 1) / p.units);
+}
+
+// The k-th segment of CTA c; false when c has fewer segments. Every role
+// derives the same sequence from the CTA index, so no hand-off is needed.
+__device__ __forceinline__ bool segment(const Params &p, int c, int k, Seg &s) {
+  const long long b = cta_begin(p, c), e = cta_begin(p, c + 1);
+  if (b >= e) return false;
+  const int tile = (int)(b / p.kb) + k;
+  const long long tb = (long long)tile * p.kb, te = tb + p.kb;
+  if (tb >= e) return false;
+  const long long lo = max(b, tb), hi = min(e, te);
+  s.tile = tile;
+  s.kb0 = (int)(lo - tb);
+  s.kb1 = (int)(hi - tb);
+  const int c0 = cta_of_unit(p, tb), c1 = cta_of_unit(p, te - 1);
+  s.seg = c - c0;
+  s.nsegs = c1 - c0 + 1;
+  return true;
+}
+
+// Epilogue writer: token row v[0..127] (fp32, shared memory) of tile
+// (n_tile, token t); thread k of 8 writes its share.
+template <int EPI>
+__device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, const float *v,
+                                          int k) {
+  if (EPI == kEpiStore) {
+    const int c = k * 16;
+    uint4 o0, o1;
+    o0.x = pack_bf16x2(v[c + 0], v[c + 1]);
+    o0.y = pack_bf16x2(v[c + 2], v[c + 3]);
+    o0.z = pack_bf16x2(v[c + 4], v[c + 5]);
+    o0.w = pack_bf16x2(v[c + 6], v[c + 7]);
+    o1.x = pack_bf16x2(v[c + 8], v[c + 9]);
+    o1.y = pack_bf16x2(v[c + 10], v[c + 11]);
+    o1.z = pack_bf16x2(v[c + 12], v[c + 13]);
+    o1.w = pack_bf16x2(v[c + 14], v[c + 15]);
+    uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(a.y) +
+                                           (size_t)t * a.ldy + n_tile * BM + c);
+    dst[0] = o0;
+    dst[1] = o1;
+  } else if (EPI == kEpiSwiGLU) {
+    const int c = k * 8;  // 8 gate rows; their up rows sit 64 rows further
+    float g[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) g[j] = silu(v[c + j]) * v[c + 64 + j];
+    uint4 o;
+    o.x = pack_bf16x2(g[0], g[1]);
+    o.y = pack_bf16x2(g[2], g[3]);
+    o.z = pack_bf16x2(g[4], g[5]);
+    o.w = pack_bf16x2(g[6], g[7]);
+    *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(a.y) + (size_t)t * a.ldy +
+                               n_tile * (BM / 2) + c) = o;
+  } else {  // kEpiRopeKV: the tile is one head
+    const int h = n_tile;
+    const int c = k * 8;  // rotate pairs (c + j, c + j + 64)
+    __nv_bfloat16 *dst;
+    bool rotate = true;
+    if (h < a.Hq) {
+      dst = a.q_out + ((size_t)t * a.Hq + h) * BM;
+    } else {
+      const int s = a.slot[t];
+      if (s < 0) return;  // padding row: no cache write
+      const int page = s / a.page_size, off = s % a.page_size;
+      const bool is_k = h < a.Hq + a.Hkv;
+      const int kvh = is_k ? h - a.Hq : h - a.Hq - a.Hkv;
+      __nv_bfloat16 *cache = is_k ? a.k_cache : a.v_cache;
+      dst = cache + (((size_t)page * a.Hkv + kvh) * a.page_size + off) * BM;
+      rotate = is_k;
+    }
+    float lo[8], hi[8];
+    if (rotate) {
+      const float2 *cs = reinterpret_cast<const float2 *>(a.cos_sin) + (size_t)a.pos[t] * (BM / 2) + c;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 r = cs[j];
+        const float x = v[c + j], y = v[c + 64 + j];
+        lo[j] = x * r.x - y * r.y;
+        hi[j] = y * r.x + x * r.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        lo[j] = v[c + j];
+        hi[j] = v[c + 64 + j];
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(lo[0], lo[1]);
+    o.y = pack_bf16x2(lo[2], lo[3]);
+    o.z = pack_bf16x2(lo[4], lo[5]);
+    o.w = pack_bf16x2(lo[6], lo[7]);
+    *reinterpret_cast<uint4 *>(dst + c) = o;
+    o.x = pack_bf16x2(hi[0], hi[1]);
+    o.y = pack_bf16x2(hi[2], hi[3]);
+    o.z = pack_bf16x2(hi[4], hi[5]);
+    o.w = pack_bf16x2(hi[6], hi[7]);
+    *reinterpret_cast<uint4 *>(dst + 64 + c) = o;
+  }
+}
 
 template <int TN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_swapab_kernel(const __grid_constant__ CUtensorMap tmW,
-                       const __grid_constant__ CUtensorMap tmX, Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                const Params p) {
   using C = Cfg<TN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>(
@@ -86,25 +206,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::STAGES * C::STAGE_BYTES + C::SLAB_BYTES);
   uint64_t *full = bars;
   uint64_t *empty = bars + C::STAGES;
-  uint64_t *accum = bars + 2 * C::STAGES;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * C::STAGES + 1);
-  __shared__ int last_flag;
+  uint64_t *acc_full = bars + 2 * C::STAGES;       // [2]
+  uint64_t *acc_empty = bars + 2 * C::STAGES + 2;  // [2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * C::STAGES + 4);
+  volatile int *last_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  const int c = blockIdx.x;
+  const GemmArgs &a = p.a;
 
-  // unit -> (split, n_tile, t_tile); token tiles innermost so neighbouring
-  // CTAs reuse the same weight tile from L2 during prefill.
-  int unit = blockIdx.x;
-  const int t_tile = unit % p.t_tiles;
-  unit /= p.t_tiles;
-  const int n_tile = unit % p.n_tiles;
-  const int split = unit / p.n_tiles;
-  const int kb_total = p.K / BK;
-  const int kb_begin = split * p.kb_per_split;
-  const int kb_end = min(kb_total, kb_begin + p.kb_per_split);
-  const int nkb = kb_end - kb_begin;
-
+  ptx::pdl_launch_dependents();
   if (warp == 0) {
     ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
     ptx::tmem_relinquish();
@@ -114,7 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
-    ptx::mbar_init(accum, 1);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&acc_full[i], 1);
+      ptx::mbar_init(&acc_empty[i], kEpiThreads);
+    }
     ptx::fence_mbar_init();
   }
   if (threadIdx.x == 64) {
@@ -127,168 +242,162 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ============================================================ producer
     if (ptx::elect_one()) {
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
-        if (!ptx::mbar_wait(&empty[s], ph ^ 1, kWaitBudgetNs)) {
-          report_status(p.status, kStatusMmaTimeout);
-          break;
+      // Weights of the first stages do not depend on the previous kernel:
+      // fetch them before waiting for it.
+      int pre = 0;
+      {
+        Seg s;
+        for (int k = 0; pre < C::STAGES && segment(p, c, k, s); ++k) {
+          const int nt = s.tile / p.t_tiles;
+          for (int kb = s.kb0; kb < s.kb1 && pre < C::STAGES; ++kb, ++pre) {
+            ptx::mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
+            ptx::tma_load_2d(stage_mem + pre * C::STAGE_BYTES, &tmW, &full[pre], kb * BK, nt * BM);
+          }
         }
-        uint8_t *st = stage_mem + s * C::STAGE_BYTES;
-        ptx::mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-        const int kc = (kb_begin + i) * BK;
-        ptx::tma_load_2d(st, &tmW, &full[s], kc, n_tile * BM);
-        ptx::tma_load_2d(st + C::W_BYTES, &tmX, &full[s], kc, t_tile * TN);
+      }
+      ptx::pdl_wait();
+      Seg s;
+      int i = 0;
+      bool ok = true;
+      for (int k = 0; ok && segment(p, c, k, s); ++k) {
+        const int nt = s.tile / p.t_tiles, tt = s.tile % p.t_tiles;
+        for (int kb = s.kb0; kb < s.kb1; ++kb, ++i) {
+          const int st = i % C::STAGES;
+          uint8_t *sm = stage_mem + st * C::STAGE_BYTES;
+          if (i >= pre) {
+            if (!ptx::mbar_wait(&empty[st], ((i / C::STAGES) & 1) ^ 1, kWaitBudgetNs)) {
+              report_status(a.status, kStatusMmaTimeout);
+              ok = false;
+              break;
+            }
+            ptx::mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+            ptx::tma_load_2d(sm, &tmW, &full[st], kb * BK, nt * BM);
+          }
+          ptx::tma_load_2d(sm + C::W_BYTES, &tmX, &full[st], kb * BK, tt * TN);
+        }
       }
     }
   } else if (warp == 1) {
+    // ============================================================ MMA
     if (ptx::elect_one()) {
       constexpr uint32_t idesc = ptx::idesc_f16(BM, TN, /*bf16*/ 1, false, false);
+      Seg s;
+      int i = 0;
       bool ok = true;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
-        if (!ptx::mbar_wait(&full[s], ph, kWaitBudgetNs)) {
-          report_status(p.status, kStatusTmaTimeout);
-          ok = false;
+      for (int k = 0; ok && segment(p, c, k, s); ++k) {
+        const int ab = k & 1;
+        if (!ptx::mbar_wait(&acc_empty[ab], ((k >> 1) & 1) ^ 1, kWaitBudgetNs)) {
+          report_status(a.status, kStatusEpilogueTimeout);
           break;
         }
         ptx::tc_fence_after();
-        uint8_t *st = stage_mem + s * C::STAGE_BYTES;
+        const uint32_t acc = tmem + ab * C::ACC_COLS;
+        for (int kb = s.kb0; kb < s.kb1; ++kb, ++i) {
+          const int st = i % C::STAGES;
+          if (!ptx::mbar_wait(&full[st], (i / C::STAGES) & 1, kWaitBudgetNs)) {
+            report_status(a.status, kStatusTmaTimeout);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          uint8_t *sm = stage_mem + st * C::STAGE_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          uint64_t a = ptx::smem_desc(st + kk * 32, 16, 1024, ptx::kLayoutSW128);
-          uint64_t b = ptx::smem_desc(st + C::W_BYTES + kk * 32, 16, 1024, ptx::kLayoutSW128);
-          ptx::mma_f16_ss(tmem, a, b, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t da = ptx::smem_desc(sm + kk * 32, 16, 1024, ptx::kLayoutSW128);
+            const uint64_t db = ptx::smem_desc(sm + C::W_BYTES + kk * 32, 16, 1024, ptx::kLayoutSW128);
+            ptx::mma_f16_ss(acc, da, db, idesc, (kb > s.kb0 || kk > 0) ? 1u : 0u);
+          }
+          ptx::mma_commit(&empty[st]);
         }
-        ptx::mma_commit(&empty[s]);
+        ptx::mma_commit(&acc_full[ab]);  // fires when the segment's MMAs retire
       }
-      (void)ok;
-      ptx::mma_commit(accum);  // fires once all issued MMAs retire (immediately if none)
     }
   } else {
-    // ---------------------------------------------------------------- epilogue
-    const int et = threadIdx.x - 64;  // 0..127
-    const int q = warp & 3;           // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;    // accumulator row = weight row within the tile
-    const bool waited = ptx::mbar_wait(accum, 0, kWaitBudgetNs);
-    if (!waited) report_status(p.status, kStatusEpilogueTimeout);
-    ptx::tc_fence_after();
-    const int t0 = t_tile * TN;
-    const int n0 = n_tile * BM;
-    const bool direct = (p.splits == 1);
-    for (int c = 0; c < TN / kSlab; ++c) {
-      if (t0 + c * kSlab >= p.T) break;
-      uint32_t r[16];
-      ptx::tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c * kSlab, r);
-      ptx::tmem_ld_wait();
-      if (nkb == 0 || !waited) {
+    // ============================================================ epilogue
+    const int et = threadIdx.x - 64;       // 0..127
+    const int q = warp & 3;                // TMEM lane quarter of this warp
+    const int row = q * 32 + lane;         // accumulator row = weight row in the tile
+    const int tj = et / 8, part = et % 8;  // slab token / writer share
+    ptx::pdl_wait();
+    Seg s;
+    for (int k = 0; segment(p, c, k, s); ++k) {
+      const int ab = k & 1;
+      const bool waited = ptx::mbar_wait(&acc_full[ab], (k >> 1) & 1, kWaitBudgetNs);
+      if (!waited) report_status(a.status, kStatusEpilogueTimeout);
+      ptx::tc_fence_after();
+      const int nt = s.tile / p.t_tiles, tt = s.tile % p.t_tiles;
+      const int t0 = tt * TN;
+      const bool direct = s.nsegs == 1;
+      // two partial slots per CTA: slot 1 for the segment that opens its tile
+      // (the CTA's last segment), slot 0 for a continuation (its first)
+      float *wsl = direct ? nullptr : a.ws + ((size_t)c * 2 + (s.seg == 0 ? 1 : 0)) * ((size_t)TN * BM);
+      for (int ch = 0; ch < TN / kSlab; ++ch) {
+        if (t0 + ch * kSlab >= a.T) break;
+        uint32_t r[16];
+        ptx::tmem_ld16(tmem + ab * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + ch * kSlab, r);
+        ptx::tmem_ld_wait();
+        if (!waited) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) r[j] = 0u;
-      }
-#pragma unroll
-      for (int j = 0; j < 16; ++j) slab[j * kSlabPitch + row] = __uint_as_float(r[j]);
-      named_bar(1, kEpiThreads);
-      // 16 tokens x 128 rows: each thread handles 16 consecutive values of one token.
-      const int tj = et / 8;          // token within slab
-      const int col = (et % 8) * 16;  // first row (feature) of this thread's run
-      const int t = t0 + c * kSlab + tj;
-      if (t < p.T) {
-        const float *src = slab + tj * kSlabPitch + col;
+          for (int j = 0; j < 16; ++j) r[j] = 0u;
+        }
         if (direct) {
-          if (EPI == kEpiStore) {
-            uint4 o0, o1;
-            o0.x = pack_bf16x2(src[0], src[1]);
-            o0.y = pack_bf16x2(src[2], src[3]);
-            o0.z = pack_bf16x2(src[4], src[5]);
-            o0.w = pack_bf16x2(src[6], src[7]);
-            o1.x = pack_bf16x2(src[8], src[9]);
-            o1.y = pack_bf16x2(src[10], src[11]);
-            o1.z = pack_bf16x2(src[12], src[13]);
-            o1.w = pack_bf16x2(src[14], src[15]);
-            uint4 *dst = reinterpret_cast<uint4 *>(p.y + (size_t)t * p.ldy + n0 + col);
-            dst[0] = o0;
-            dst[1] = o1;
-          } else if (col < 64) {
-            // SwiGLU: rows [0,64) are gate, [64,128) the matching up rows.
-            const float *up = src + 64;
-            float v[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = silu(src[j]) * up[j];
-            uint4 o0, o1;
-            o0.x = pack_bf16x2(v[0], v[1]);
-            o0.y = pack_bf16x2(v[2], v[3]);
-            o0.z = pack_bf16x2(v[4], v[5]);
-            o0.w = pack_bf16x2(v[6], v[7]);
-            o1.x = pack_bf16x2(v[8], v[9]);
-            o1.y = pack_bf16x2(v[10], v[11]);
-            o1.z = pack_bf16x2(v[12], v[13]);
-            o1.w = pack_bf16x2(v[14], v[15]);
-            uint4 *dst = reinterpret_cast<uint4 *>(p.y + (size_t)t * p.ldy + n_tile * 64 + col);
-            dst[0] = o0;
-            dst[1] = o1;
-          }
+          for (int j = 0; j < 16; ++j) slab[j * kSlabPitch + row] = __uint_as_float(r[j]);
+          named_bar(1, kEpiThreads);
+          const int t = t0 + ch * kSlab + tj;
+          if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part);
+          named_bar(1, kEpiThreads);
         } else {
-          const size_t t_pad = (size_t)p.t_tiles * TN;
-          float4 *dst = reinterpret_cast<float4 *>(p.ws + ((size_t)split * t_pad + t) * p.N + n0 + col);
+          // partial slice [TN tokens][128 rows]: a warp stores 32 consecutive rows
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            __stcg(dst + j, make_float4(src[4 * j], src[4 * j + 1], src[4 * j + 2], src[4 * j + 3]));
+          for (int j = 0; j < 16; ++j)
+            __stcg(wsl + (size_t)(ch * kSlab + j) * BM + row, __uint_as_float(r[j]));
         }
       }
-      named_bar(1, kEpiThreads);
-    }
-    if (!direct) {
-      // Arrival: the last split of this tile finishes it.
-      if (et == 0) {
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&acc_empty[ab]);  // the MMA warp may refill this accumulator
+      if (!direct) {
         __threadfence();
-        uint32_t prev = atomicAdd(&p.counters[n_tile * p.t_tiles + t_tile], 1u);
-        last_flag = (prev == (uint32_t)(p.splits - 1)) ? 1 : 0;
-      }
-      named_bar(1, kEpiThreads);
-      if (last_flag) {
-        __threadfence();
-        const int tmax = min(TN, p.T - t0);
-        const size_t slice = (size_t)p.t_tiles * TN * p.N;
-        // 128 threads sweep the [tmax x 128] tile, 8 features per thread-step;
-        // SwiGLU threads own 8 gate rows and read the matching 8 up rows.
-        for (int idx = et; idx < tmax * (BM / 8); idx += kEpiThreads) {
-          const int tj = idx / (BM / 8);
-          const int col = (idx % (BM / 8)) * 8;
-          if (EPI == kEpiSwiGLU && col >= 64) continue;
-          const int t = t0 + tj;
-          const float *src = p.ws + (size_t)t * p.N + n0 + col;
-          float a[8], u[8];
+        named_bar(1, kEpiThreads);
+        if (et == 0) {
+          const uint32_t prev = atomicAdd(&a.counters[s.tile], 1u);
+          *last_flag = (prev == (uint32_t)(s.nsegs - 1)) ? 1 : 0;
+        }
+        named_bar(1, kEpiThreads);
+        if (*last_flag) {
+          __threadfence();
+          const int c0 = c - s.seg;  // CTA of the tile's first segment
+          const int tmax = min(TN, a.T - t0);
+          for (int ch = 0; ch * kSlab < tmax; ++ch) {
+            const int tl = ch * kSlab + tj;
+            float acc[16];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) a[j] = u[j] = 0.f;
-          for (int sp = 0; sp < p.splits; ++sp) {
-            const float4 *s4 = reinterpret_cast<const float4 *>(src + sp * slice);
-            const float4 x0 = __ldcg(s4), x1 = __ldcg(s4 + 1);
-            a[0] += x0.x; a[1] += x0.y; a[2] += x0.z; a[3] += x0.w;
-            a[4] += x1.x; a[5] += x1.y; a[6] += x1.z; a[7] += x1.w;
-            if (EPI == kEpiSwiGLU) {
-              const float4 y0 = __ldcg(s4 + 16), y1 = __ldcg(s4 + 17);  // +64 floats: up rows
-              u[0] += y0.x; u[1] += y0.y; u[2] += y0.z; u[3] += y0.w;
-              u[4] += y1.x; u[5] += y1.y; u[6] += y1.z; u[7] += y1.w;
+            for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+            if (tl < tmax) {
+              for (int sg = 0; sg < s.nsegs; ++sg) {  // fixed order: deterministic sums
+                const float *slice = a.ws + ((size_t)(c0 + sg) * 2 + (sg == 0 ? 1 : 0)) * ((size_t)TN * BM);
+                const float4 *src = reinterpret_cast<const float4 *>(slice + (size_t)tl * BM + part * 16);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float4 x = __ldcg(src + j);
+                  acc[4 * j] += x.x;
+                  acc[4 * j + 1] += x.y;
+                  acc[4 * j + 2] += x.z;
+                  acc[4 * j + 3] += x.w;
+                }
+              }
             }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) slab[tj * kSlabPitch + part * 16 + j] = acc[j];
+            named_bar(1, kEpiThreads);
+            if (tl < tmax) write_row<EPI>(a, nt, t0 + tl, slab + tj * kSlabPitch, part);
+            named_bar(1, kEpiThreads);
           }
-          uint4 o;
-          if (EPI == kEpiStore) {
-            o.x = pack_bf16x2(a[0], a[1]);
-            o.y = pack_bf16x2(a[2], a[3]);
-            o.z = pack_bf16x2(a[4], a[5]);
-            o.w = pack_bf16x2(a[6], a[7]);
-            *reinterpret_cast<uint4 *>(p.y + (size_t)t * p.ldy + n0 + col) = o;
-          } else {
-            o.x = pack_bf16x2(silu(a[0]) * u[0], silu(a[1]) * u[1]);
-            o.y = pack_bf16x2(silu(a[2]) * u[2], silu(a[3]) * u[3]);
-            o.z = pack_bf16x2(silu(a[4]) * u[4], silu(a[5]) * u[5]);
-            o.w = pack_bf16x2(silu(a[6]) * u[6], silu(a[7]) * u[7]);
-            *reinterpret_cast<uint4 *>(p.y + (size_t)t * p.ldy + n_tile * 64 + col) = o;
-          }
+          if (et == 0) a.counters[s.tile] = 0u;
         }
-        if (et == 0) p.counters[n_tile * p.t_tiles + t_tile] = 0u;
+        named_bar(1, kEpiThreads);  // last_flag is rewritten by the next segment
       }
     }
   }
@@ -299,33 +408,40 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int TN, int EPI>
-static void launch_tn(const CUtensorMap &tw, const CUtensorMap &tx, const Params &p, int grid,
+static void launch_tn(const CUtensorMap &tw, const CUtensorMap &tx, const Params &p,
                       cudaStream_t stream) {
   using C = Cfg<TN>;
-  auto kern = gemm_swapab_kernel<TN, EPI>;
+  auto kern = gemm_kernel<TN, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     attr_set = true;
   }
-  kern<<<grid, kThreads, C::SMEM, stream>>>(tw, tx, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
 }
 
 template <int EPI>
 static void dispatch(int tn, const CUtensorMap &tw, const CUtensorMap &tx, const Params &p,
-                     int grid, cudaStream_t stream) {
+                     cudaStream_t stream) {
   switch (tn) {
-    case 16: launch_tn<16, EPI>(tw, tx, p, grid, stream); break;
-    case 32: launch_tn<32, EPI>(tw, tx, p, grid, stream); break;
-    case 64: launch_tn<64, EPI>(tw, tx, p, grid, stream); break;
-    case 128: launch_tn<128, EPI>(tw, tx, p, grid, stream); break;
-    default: launch_tn<256, EPI>(tw, tx, p, grid, stream); break;
+    case 16: launch_tn<16, EPI>(tw, tx, p, stream); break;
+    case 32: launch_tn<32, EPI>(tw, tx, p, stream); break;
+    case 64: launch_tn<64, EPI>(tw, tx, p, stream); break;
+    case 128: launch_tn<128, EPI>(tw, tx, p, stream); break;
+    default: launch_tn<256, EPI>(tw, tx, p, stream); break;
   }
 }
 
-}  // namespace gemm
-
-// Token-tile width for T tokens.
 static int pick_tn(int T) {
   if (T <= 16) return 16;
   if (T <= 32) return 32;
@@ -334,56 +450,69 @@ static int pick_tn(int T) {
   return 256;
 }
 
-extern "C" int sched_gemm_split_count(int T, int N, int K, int num_sms) {
-  const int tn = pick_tn(T);
-  const int units = (N / gemm::BM) * ((T + tn - 1) / tn);
-  const int kb = K / gemm::BK;
-  const int target = 2 * num_sms;
-  if (units >= num_sms) return 1;
-  int s = (target + units - 1) / units;
-  s = std::min(s, std::max(1, kb / 4));
-  return std::max(1, s);
+// Schedule of one call: grid, segments bound, whether tiles get split.
+static void plan(const GemmArgs &a, Params &p, int &tn) {
+  tn = pick_tn(a.T);
+  p.n_tiles = a.N / BM;
+  p.t_tiles = (a.T + tn - 1) / tn;
+  p.kb = a.K / BK;
+  p.tiles = p.n_tiles * p.t_tiles;
+  p.units = (long long)p.tiles * p.kb;
+  int grid = a.grid > 0 ? a.grid : (a.num_sms > 0 ? a.num_sms : 148);
+  // at least 4 k-blocks per CTA keeps the pipeline worth its set-up
+  grid = (int)std::min<long long>(grid, std::max<long long>(1, p.units / 4));
+  p.grid = std::max(1, grid);
 }
 
-// Host launcher. Returns 0 on success, a negative value on a bad argument.
-//   x  [T, K] bf16 row-major (pitch ldx), w [N, K] bf16 row-major,
-//   y  [T, ldy] bf16; epi 0: ldy >= N, epi 1 (SwiGLU): writes N/2 columns.
-//   ws/counters: split-K workspace ([splits x T_pad x N] fp32, and
-//   n_tiles*t_tiles u32 counters that must be zero) -- required when splits > 1.
-extern "C" int sched_gemm_bf16(const void *x, int ldx, const void *w, void *y, int ldy, int T,
-                               int N, int K, int epi, int splits, float *ws, uint32_t *counters,
-                               int *status, cudaStream_t stream) {
-  if (T <= 0) return 0;
-  if (N % gemm::BM != 0 || K % gemm::BK != 0) return -1;
-  if (splits > 1 && (ws == nullptr || counters == nullptr)) return -2;
-  const int tn = pick_tn(T);
+static bool splits_tiles(const Params &p) {
+  return p.units % p.grid != 0 || (p.units / p.grid) % p.kb != 0;
+}
+
+}  // namespace gemm
+
+// Workspace floats a call of this shape needs (0 when no tile is split).
+extern "C" long long sched_gemm_ws_floats(int T, int N, int K, int grid) {
+  GemmArgs a{};
+  a.T = T;
+  a.N = N;
+  a.K = K;
+  a.grid = grid;
   gemm::Params p;
-  p.y = static_cast<__nv_bfloat16 *>(y);
-  p.T = T;
-  p.N = N;
-  p.K = K;
-  p.ldy = ldy;
-  p.n_tiles = N / gemm::BM;
-  p.t_tiles = (T + tn - 1) / tn;
-  const int kb = K / gemm::BK;
-  splits = std::max(1, std::min(splits, kb));
-  p.kb_per_split = (kb + splits - 1) / splits;
-  p.splits = (kb + p.kb_per_split - 1) / p.kb_per_split;
-  p.ws = ws;
-  p.counters = counters;
-  p.status = status;
+  int tn;
+  gemm::plan(a, p, tn);
+  if (!gemm::splits_tiles(p)) return 0;
+  return (long long)p.grid * 2 * tn * gemm::BM;
+}
+
+extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
+  const GemmArgs &a = *args;
+  if (a.T <= 0) return 0;
+  if (a.N % gemm::BM != 0 || a.K % gemm::BK != 0) return -1;
+  gemm::Params p;
+  int tn;
+  p.a = a;
+  gemm::plan(a, p, tn);
+  if (gemm::splits_tiles(p)) {
+    if (a.ws == nullptr || a.counters == nullptr) return -2;
+    const long long need = (long long)p.grid * 2 * tn * gemm::BM;
+    if (need > a.ws_floats || p.tiles > a.counter_count) return -5;
+  }
+  if (a.epi == kEpiRopeKV && (a.N / gemm::BM != a.Hq + 2 * a.Hkv || a.cos_sin == nullptr ||
+                              a.pos == nullptr || a.slot == nullptr))
+    return -6;
   try {
-    CUtensorMap tw = tmap::make_2d(w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, gemm::BM,
+    CUtensorMap tw = tmap::make_2d(a.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.K,
+                                   gemm::BM, gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap tx = tmap::make_2d(a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.K, a.ldx, tn,
                                    gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
-    CUtensorMap tx = tmap::make_2d(x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, K, ldx, tn, gemm::BK,
-                                   CU_TENSOR_MAP_SWIZZLE_128B);
-    const int grid = p.n_tiles * p.t_tiles * p.splits;
-    if (epi == gemm::kEpiSwiGLU)
-      gemm::dispatch<gemm::kEpiSwiGLU>(tn, tw, tx, p, grid, stream);
+    if (a.epi == kEpiSwiGLU)
+      gemm::dispatch<kEpiSwiGLU>(tn, tw, tx, p, stream);
+    else if (a.epi == kEpiRopeKV)
+      gemm::dispatch<kEpiRopeKV>(tn, tw, tx, p, stream);
     else
-      gemm::dispatch<gemm::kEpiStore>(tn, tw, tx, p, grid, stream);
+      gemm::dispatch<kEpiStore>(tn, tw, tx, p, stream);
   } catch (const std::exception &) {
     return -3;
   }
-  return (int)cudaPeekAtLastError() == 0 ? 0 : -4;
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

@@ -149,6 +149,7 @@ class Engine:
                                   self.cfg.head_dim, dtype=torch.float32, device=self.device)
         self.part_lse = torch.zeros(B * S_max, self.part_o.shape[1], dtype=torch.float32, device=self.device)
         self.sample_idx64 = torch.zeros(2 * B, dtype=torch.int64, device=self.device)
+        self.merge_cnt = torch.zeros(B * self.cfg.n_kv_heads, dtype=torch.int32, device=self.device)
 
     def _view(self, name, shape=None):
         o, n = self.layout[name]
@@ -258,12 +259,19 @@ class Engine:
             items=self._view("items", (-1, 4)), n_items=n_items,
             part_o=self.part_o if S > 1 else None, part_lse=self.part_lse if S > 1 else None,
             merge_req=self._view("merge_req"), merge_begin=self._view("merge_begin"),
-            n_merge=nd if S > 1 else 0,
+            n_merge=nd if S > 1 else 0, merge_cnt=self.merge_cnt if S > 1 else None, splits=S,
             tiles=self._view("tiles", (-1, 4)), n_tiles=info["n_tiles"],
             sample_idx=self.sample_idx64, n_sample=info["n_sample"], out_ids=self.out_ids,
-            slots=slots, acquire=self._acq_code(),
-            grid=min(self.R, n_items * self.hkv) if self.ecfg.acquire == "ticket" else 0,
+            slots=slots, acquire=self._acq_code(), grid=self._grid(n_items * self.hkv),
         )
+
+    def _grid(self, n_tasks: int) -> int:
+        """CTAs of the decode launch: persistent (R) for static stride and
+        ticket acquisition, one per task for cluster launch control (idle CTAs
+        steal the unlaunched ones)."""
+        if self.ecfg.acquire in ("static", "ticket") or not self.ecfg.levers:
+            return max(1, min(self.R, n_tasks))
+        return n_tasks
 
     def _acq_code(self) -> int:
         return {"static": 0, "ticket": 1, "clc": 2, "auto": 2}.get(self.ecfg.acquire, 0)
@@ -299,7 +307,9 @@ class Engine:
             else:
                 plane.set_order_size(0)
                 plane.reset_order()
-            plane.set_num_tasks(n_tasks if (arm_clc or e.acquire == "ticket") else 0)
+            # claims stay on for the acquisition modes: the decode kernel is
+            # persistent either way, arming only changes the order policy
+            plane.set_num_tasks(n_tasks if e.acquire in ("ticket", "clc", "auto") else 0)
         # shed: tau for the lowest-urgency fraction of decode requests
         if e.shed_fraction > 0:
             dec = plan.decode

@@ -127,6 +127,8 @@ class ForwardBatch:
     merge_req: torch.Tensor | None = None
     merge_begin: torch.Tensor | None = None
     n_merge: int = 0
+    merge_cnt: torch.Tensor | None = None   # in-kernel merge counters (zero between calls)
+    splits: int = 1
     # prefill attention plan
     tiles: torch.Tensor | None = None       # [n_tiles, 4] int32
     n_tiles: int = 0
@@ -202,9 +204,10 @@ class Llama:
             q = self.q[:nd]
             out = self.attn[:nd]
             ops.attention_decode(q, out, kc, vc, b.block_table, b.items, b.n_items, self.sm_scale,
-                                 part_o=b.part_o, part_lse=b.part_lse, slots=b.slots,
-                                 woven=b.slots is not None, acquire=b.acquire, grid=b.grid)
-            if b.n_merge > 0:
+                                 part_o=b.part_o, part_lse=b.part_lse, merge_cnt=b.merge_cnt,
+                                 splits=b.splits, slots=b.slots, woven=b.slots is not None,
+                                 acquire=b.acquire, grid=b.grid)
+            if b.n_merge > 0 and b.merge_cnt is None:
                 ops.attention_merge(b.part_o, b.part_lse, b.merge_req, b.merge_begin, b.n_merge, out)
         if b.n_tiles > 0:
             T = b.n_tokens
@@ -226,9 +229,8 @@ class Llama:
                 ops.add_rmsnorm(h, None, lw.ln_in, cfg.rms_eps, normed)
             else:
                 ops.add_rmsnorm(delta, h, lw.ln_in, cfg.rms_eps, normed)
-            ops.linear(normed, lw.qkv, self.qkv[:T])
-            ops.rope_kv_append(self.qkv[:T], b.pos[:T], b.slot[:T], self.cos_sin, self.q[:T],
-                               self.kv.k[li], self.kv.v[li], self.hq, self.hkv)
+            ops.linear_qkv_rope(normed, lw.qkv, b.pos[:T], b.slot[:T], self.cos_sin, self.q[:T],
+                                self.kv.k[li], self.kv.v[li], self.hq, self.hkv)
             self._attention(li, b)
             self._row_linear(self.attn[:T].view(T, -1), lw.o, delta)
             ops.add_rmsnorm(delta, h, lw.ln_post, cfg.rms_eps, normed)

@@ -42,21 +42,20 @@ def check_status(device=None, clear: bool = True) -> int:
 
 
 class Workspace:
-    """Split-K scratch of the GEMM: one fp32 partial-tile slice per split and
-    per-tile arrival counters. The counters stay zero between calls (the last
-    split of a tile resets its counter), so they are zeroed once here. One
-    workspace per stream: calls that share it must be stream-ordered."""
+    """Stream-K scratch of the GEMM: fp32 partial-tile slices and per-tile
+    arrival counters. The counters stay zero between calls (the last segment
+    of a tile resets its counter), so they are zeroed once here; the slices
+    need no clearing (every segment rewrites its own). One workspace per
+    stream: calls that share it must be stream-ordered."""
 
-    def __init__(self, device, floats: int = 1 << 23, counters: int = 1 << 16):
+    def __init__(self, device, floats: int = 1 << 24, counters: int = 1 << 16):
         self.device = torch.device(device)
         self.ws = torch.zeros(floats, dtype=torch.float32, device=self.device)
         self.counters = torch.zeros(counters, dtype=torch.int32, device=self.device)
 
-    def fits(self, T: int, N: int, splits: int) -> bool:
-        tn = 16 if T <= 16 else 32 if T <= 32 else 64 if T <= 64 else 128 if T <= 128 else 256
-        t_pad = (T + tn - 1) // tn * tn
-        return (splits * t_pad * N <= self.ws.numel()
-                and (N // 128) * (t_pad // tn) <= self.counters.numel())
+    def ensure(self, floats: int) -> None:
+        if floats > self.ws.numel():
+            self.ws = torch.zeros(int(floats * 1.25), dtype=torch.float32, device=self.device)
 
 
 def workspace(device=None, stream_key: int = 0) -> Workspace:
@@ -70,39 +69,42 @@ def workspace(device=None, stream_key: int = 0) -> Workspace:
     return w
 
 
-_sm_count: dict[int, int] = {}
+_ws_need: dict[tuple, int] = {}
 
 
-def _sms(dev: torch.device) -> int:
-    idx = dev.index if dev.index is not None else torch.cuda.current_device()
-    n = _sm_count.get(idx)
-    if n is None:
-        n = torch.cuda.get_device_properties(idx).multi_processor_count
-        _sm_count[idx] = n
-    return n
+def _ws_for(x, N, K, grid, ws):
+    ws = ws or workspace(x.device)
+    key = (x.shape[0], N, K, grid)
+    need = _ws_need.get(key)
+    if need is None:
+        need = int(ext().gemm_ws_floats(x.shape[0], N, K, grid))
+        _ws_need[key] = need
+    ws.ensure(need)
+    return ws
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *,
-           swiglu: bool = False, splits: int | None = None, ws: Workspace | None = None) -> torch.Tensor:
+           swiglu: bool = False, grid: int = 0, ws: Workspace | None = None) -> torch.Tensor:
     """y = x @ w.T on the tcgen05 GEMM. ``swiglu``: w holds interleaved
     gate/up rows (64 gate rows, then their 64 up rows, per 128-row tile) and
-    y = silu(gate) * up with N/2 columns."""
+    y = silu(gate) * up with N/2 columns. ``grid``: CTAs (0 = one per SM)."""
     T, K = x.shape
     N = w.shape[0]
     if out is None:
         out = torch.empty(T, N // 2 if swiglu else N, dtype=torch.bfloat16, device=x.device)
-    E = ext()
-    if splits is None:
-        splits = E.gemm_split_count(T, N, K, _sms(x.device))
-    if splits > 1:
-        ws = ws or workspace(x.device)
-        if not ws.fits(T, N, splits):
-            splits = 1
-    E.gemm(x, w, out, 1 if swiglu else 0, int(splits),
-           ws.ws if (splits > 1 and ws is not None) else None,
-           ws.counters if (splits > 1 and ws is not None) else None,
-           status_buffer(x.device))
+    ws = _ws_for(x, N, K, grid, ws)
+    ext().gemm(x, w, out, 1 if swiglu else 0, int(grid), ws.ws, ws.counters, status_buffer(x.device))
     return out
+
+
+def linear_qkv_rope(x, w, pos, slot, cos_sin, q_out, k_cache, v_cache, n_q_heads, n_kv_heads, *,
+                    grid: int = 0, ws: Workspace | None = None):
+    """Fused QKV projection + RoPE + KV append: q heads rotated into q_out,
+    k heads rotated and v heads copied into their paged-cache slots."""
+    ws = _ws_for(x, w.shape[0], x.shape[1], grid, ws)
+    ext().gemm_qkv_rope(x, w, pos, slot, cos_sin, q_out, k_cache, v_cache, int(n_q_heads),
+                        int(n_kv_heads), int(grid), ws.ws, ws.counters, status_buffer(x.device))
+    return q_out
 
 
 def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Tensor, eps: float,
@@ -122,11 +124,14 @@ def rope_kv_append(qkv: torch.Tensor, pos: torch.Tensor, slot: torch.Tensor, cos
 
 
 def attention_decode(q, out, k_cache, v_cache, block_table, items, num_items, sm_scale, *,
-                     part_o=None, part_lse=None, slots=None, woven=True, acquire=0, grid=0,
-                     pf_blocks=2, dT=1.0, dR=1.0, H=0.25):
+                     part_o=None, part_lse=None, merge_cnt=None, splits=1, slots=None, woven=True,
+                     acquire=0, grid=0, pf_blocks=2, dT=1.0, dR=1.0, H=0.25):
+    """Paged decode attention. Items (req, kv_begin, kv_end, part) x KV heads
+    are the tasks. With ``merge_cnt`` (int32 [requests * Hkv], zero), split
+    requests (part = req * splits + s) are merged inside the kernel."""
     s = slots or {}
     ext().attn_decode(q, out, k_cache, v_cache, block_table, items, int(num_items), float(sm_scale),
-                      part_o, part_lse, s.get("order"), s.get("ctrl"), s.get("timer"),
+                      part_o, part_lse, merge_cnt, int(splits), s.get("order"), s.get("ctrl"), s.get("timer"),
                       s.get("queue"), int(s.get("max_tasks", 0)), int(bool(woven)), int(acquire),
                       int(grid), int(pf_blocks), float(dT), float(dR), float(H),
                       status_buffer(q.device))

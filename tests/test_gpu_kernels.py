@@ -25,26 +25,26 @@ def _clean_status():
 
 # ------------------------------------------------------------------ GEMM
 @pytest.mark.parametrize("T", [1, 5, 16, 33, 64, 100, 128, 200, 257])
-@pytest.mark.parametrize("NK", [(128, 64), (384, 256), (1024, 512)])
-@pytest.mark.parametrize("split", [1, 3])
-def test_gemm_matches_fp32(T, NK, split):
+@pytest.mark.parametrize("NK", [(128, 64), (384, 256), (1024, 512), (6144, 4096)])
+@pytest.mark.parametrize("grid", [0, 7, 148])
+def test_gemm_matches_fp32(T, NK, grid):
     N, K = NK
     g = torch.Generator(device=DEV).manual_seed(T * 31 + N)
     x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
     w = (torch.randn(N, K, device=DEV, generator=g) / math.sqrt(K)).to(torch.bfloat16)
-    y = ops.linear(x, w, splits=split)
+    y = ops.linear(x, w, grid=grid)
     torch.cuda.synchronize()
     assert rel_err(y, ref.linear(x, w)) < 1e-2
 
 
 @pytest.mark.parametrize("T", [3, 64, 300])
-@pytest.mark.parametrize("split", [1, 4])
-def test_gemm_swiglu(T, split):
+@pytest.mark.parametrize("grid", [0, 5])
+def test_gemm_swiglu(T, grid):
     I, K = 256, 512
     g = torch.Generator(device=DEV).manual_seed(7)
     x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
     w = (torch.randn(2 * I, K, device=DEV, generator=g) / math.sqrt(K)).to(torch.bfloat16)
-    y = ops.linear(x, w, swiglu=True, splits=split)
+    y = ops.linear(x, w, swiglu=True, grid=grid)
     torch.cuda.synchronize()
     assert y.shape == (T, I)
     assert rel_err(y, ref.swiglu_linear(x, w)) < 1e-2
@@ -58,7 +58,7 @@ def test_gemm_split_workspace_stays_clean():
     w2 = torch.randn(512, 1024, device=DEV).to(torch.bfloat16)
     ys = []
     for w in (w1, w2, w1):
-        y = ops.linear(x, w, splits=4)
+        y = ops.linear(x, w, grid=6)
         assert rel_err(y, ref.linear(x, w)) < 1e-2
         ys.append(y)
     assert torch.equal(ys[0], ys[2])
@@ -72,6 +72,39 @@ def test_gemm_large_prefill_shape():
     x = torch.randn(T, K, device=DEV).to(torch.bfloat16)
     w = (torch.randn(N, K, device=DEV) / 64).to(torch.bfloat16)
     assert rel_err(ops.linear(x, w), ref.linear(x, w)) < 1e-2
+
+
+@pytest.mark.parametrize("T", [1, 9, 40, 130])
+@pytest.mark.parametrize("grid", [0, 11])
+def test_gemm_qkv_rope_kv_append(T, grid):
+    from sched_pass_b200.models.config import LLAMA_TINY
+    from sched_pass_b200.models.llama import rope_table
+    cfg = LLAMA_TINY
+    Hq, Hkv, D, H = cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden
+    cs = rope_table(cfg, 4096, DEV)
+    g = torch.Generator(device=DEV).manual_seed(T)
+    x = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn((Hq + 2 * Hkv) * D, H, device=DEV, generator=g) / math.sqrt(H)).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), device=DEV, dtype=torch.int32)
+    pages = 64
+    slot = torch.randperm(pages * 16, device=DEV)[:T].to(torch.int32)
+    slot[0] = -1  # a padding row writes no cache entry
+    kc = torch.zeros(pages, Hkv, 16, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=DEV)
+    ops.linear_qkv_rope(x, w, pos, slot, cs, q, kc, vc, Hq, Hkv, grid=grid)
+    torch.cuda.synchronize()
+    qkv = ref.linear(x, w).to(torch.bfloat16).view(T, Hq + 2 * Hkv, D)
+    assert rel_err(q, ref.rope(qkv[:, :Hq], pos, cs)) < 1e-2
+    k_ref = ref.rope(qkv[:, Hq:Hq + Hkv], pos, cs)
+    for t in range(T):
+        s = int(slot[t])
+        if s < 0:
+            continue
+        assert rel_err(kc[s // 16, :, s % 16], k_ref[t]) < 1e-2
+        assert rel_err(vc[s // 16, :, s % 16], qkv[t, Hq + Hkv:]) < 1e-2
+    if T > 1:
+        assert kc[slot[1:].long() // 16].abs().sum() > 0
 
 
 # ------------------------------------------------------------------ elementwise
@@ -184,6 +217,37 @@ def test_decode_attention_split_kv(S):
     out, _ = run_decode(q, kc, vc, bt, LENS, S=S)
     r = ref.decode_attention_paged(q, kc, vc, bt, LENS, 1 / math.sqrt(128))
     assert rel_err(out, r) < 2e-2
+
+
+@pytest.mark.parametrize("S", [2, 5])
+@pytest.mark.parametrize("acquire", [0, 2])
+def test_decode_in_kernel_merge(S, acquire):
+    from sched_pass_b200.engine import native
+    Hkv, G = 2, 4
+    B = len(LENS)
+    kc, vc, bt = make_paged(B, Hkv, LENS, seed=30 + S)
+    q = torch.randn(B, Hkv * G, 128, device=DEV).to(torch.bfloat16)
+    items, _, _ = native.plan_decode(np.asarray(LENS, dtype=np.int32), S)
+    it = torch.from_numpy(items).to(DEV)
+    po = torch.zeros(B * S, Hkv * G, 128, dtype=torch.float32, device=DEV)
+    pl = torch.zeros(B * S, Hkv * G, dtype=torch.float32, device=DEV)
+    cnt = torch.zeros(B * Hkv, dtype=torch.int32, device=DEV)
+    p = _plane(items.shape[0] * Hkv)
+    if acquire == 2:
+        p.set_num_tasks(items.shape[0] * Hkv)
+        p.push()
+    r = ref.decode_attention_paged(q, kc, vc, bt, LENS, 1 / math.sqrt(128))
+    outs = []
+    for grid in (0, 37):
+        out = torch.zeros_like(q)
+        ops.attention_decode(q, out, kc, vc, bt, it, items.shape[0], 1 / math.sqrt(128), part_o=po,
+                             part_lse=pl, merge_cnt=cnt, splits=S, slots=p.slots(), woven=True,
+                             acquire=acquire, grid=grid if acquire == 0 else 0)
+        torch.cuda.synchronize()
+        assert rel_err(out, r) < 2e-2
+        assert int(cnt.abs().sum()) == 0
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
 
 
 def _plane(n_tasks):
