@@ -141,6 +141,33 @@ void gemm_qkv_rope(const at::Tensor &x, const at::Tensor &w, const at::Tensor &p
   check_rc(sched_gemm_run(&a, cur_stream()), "gemm_qkv_rope");
 }
 
+// Row-parallel projection with the all-reduce fused into the GEMM epilogue.
+// recv/flags: this process's addresses of every rank's slab and flag array.
+void gemm_allreduce(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int64_t rank,
+                    int64_t world, const std::vector<int64_t> &recv,
+                    const std::vector<int64_t> &flags, int64_t grid,
+                    const c10::optional<at::Tensor> &ws,
+                    const c10::optional<at::Tensor> &counters,
+                    const c10::optional<at::Tensor> &status) {
+  GemmArgs a = base_args(x, w, grid, ws, counters, status);
+  check_bf16(y, "y");
+  TORCH_CHECK(y.dim() == 2 && y.stride(1) == 1 && y.size(1) >= a.N, "y [T, >= N]");
+  TORCH_CHECK(world >= 1 && world <= kMaxWorld && (int64_t)recv.size() == world &&
+                  (int64_t)flags.size() == world,
+              "one slab and one flag array per rank");
+  a.y = y.data_ptr();
+  a.ldy = y.stride(0);
+  a.epi = kEpiAllReduce;
+  a.rank = rank;
+  a.world = world;
+  for (int j = 0; j < world; ++j) {
+    a.recv[j] = reinterpret_cast<__nv_bfloat16 *>(recv[j]);
+    a.flags[j] = reinterpret_cast<uint32_t *>(flags[j]);
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(sched_gemm_run(&a, cur_stream()), "gemm_allreduce");
+}
+
 int64_t gemm_ws_floats(int64_t T, int64_t N, int64_t K, int64_t grid) {
   return sched_gemm_ws_floats(T, N, K, grid);
 }
@@ -277,7 +304,11 @@ void argmax(const at::Tensor &logits, at::Tensor &ids, const c10::optional<at::T
 
 }  // namespace
 
+void register_symm(py::module &m);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  register_symm(m);
+  m.def("gemm_allreduce", &gemm_allreduce);
   m.doc() = "sched_pass_b200 sm_100a kernels";
   m.def("gemm", &gemm);
   m.def("gemm_qkv_rope", &gemm_qkv_rope);

@@ -40,7 +40,11 @@
 // (out[t, j] = silu(gate) * up); and RoPE + KV append for the fused QKV
 // projection, where a 128-row tile is exactly one head: query heads are
 // rotated into the attention input, key heads rotated and value heads copied
-// straight into their page slots of the paged KV cache.
+// straight into their page slots of the paged KV cache; and the fused
+// all-reduce of a row-parallel projection (see publish_tile /
+// reduce_owned_chunks): each finished tile is pushed over NVLink as the MMA
+// warp is already working on the next one, so the transfer overlaps the math
+// tile by tile.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -145,6 +149,23 @@ __device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, 
     o.w = pack_bf16x2(g[6], g[7]);
     *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(a.y) + (size_t)t * a.ldy +
                                n_tile * (BM / 2) + c) = o;
+  } else if (EPI == kEpiAllReduce) {
+    const int c = k * 16;
+    uint4 o0, o1;
+    o0.x = pack_bf16x2(v[c + 0], v[c + 1]);
+    o0.y = pack_bf16x2(v[c + 2], v[c + 3]);
+    o0.z = pack_bf16x2(v[c + 4], v[c + 5]);
+    o0.w = pack_bf16x2(v[c + 6], v[c + 7]);
+    o1.x = pack_bf16x2(v[c + 8], v[c + 9]);
+    o1.y = pack_bf16x2(v[c + 10], v[c + 11]);
+    o1.z = pack_bf16x2(v[c + 12], v[c + 13]);
+    o1.w = pack_bf16x2(v[c + 14], v[c + 15]);
+    const size_t off = ((size_t)a.rank * a.T + t) * a.N + (size_t)n_tile * BM + c;
+    for (int j = 0; j < a.world; ++j) {  // NVLink stores into every rank's slab
+      uint4 *dst = reinterpret_cast<uint4 *>(a.recv[j] + off);
+      dst[0] = o0;
+      dst[1] = o1;
+    }
   } else {  // kEpiRopeKV: the tile is one head
     const int h = n_tile;
     const int c = k * 8;  // rotate pairs (c + j, c + j + 64)
@@ -190,6 +211,94 @@ __device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, 
     o.z = pack_bf16x2(hi[4], hi[5]);
     o.w = pack_bf16x2(hi[6], hi[7]);
     *reinterpret_cast<uint4 *>(dst + 64 + c) = o;
+  }
+}
+
+// All-reduce, part 1: after this rank's partial of `tile` has been stored
+// into every rank's slab, raise the flag of each 16-token chunk of the tile
+// on every rank (release at system scope: the data is visible to the reader
+// that acquires the flag). Flag (src, tile, chunk) lives in the reader's array.
+template <int TN>
+__device__ __forceinline__ void publish_tile(const Params &p, int tile, int et) {
+  const GemmArgs &a = p.a;
+  constexpr int CH = TN / kSlab;
+  __threadfence_system();
+  named_bar(1, kEpiThreads);
+  const int tt = tile % p.t_tiles;
+  const int chunks = (min(TN, a.T - tt * TN) + kSlab - 1) / kSlab;
+  for (int i = et; i < a.world * chunks; i += kEpiThreads) {
+    const int j = i / chunks, ch = i % chunks;
+    ptx::st_release_sys(a.flags[j] + ((size_t)a.rank * p.tiles + tile) * CH + ch, 1u);
+  }
+}
+
+// All-reduce, part 2: the reduction units are (tile, 16-token chunk); CTA c
+// owns units c, c + grid, ... on every rank (the same assignment everywhere,
+// independent of timing). For each owned unit it waits for the chunk flags
+// of all ranks, sums their partials in rank order (the same order on every
+// rank: bit-identical results), writes the bf16 output and clears its flags.
+// Pushes never wait, so no wait can form a cycle.
+template <int TN>
+__device__ void reduce_owned_chunks(const Params &p, int c, int et) {
+  const GemmArgs &a = p.a;
+  constexpr int CH = TN / kSlab;
+  const __nv_bfloat16 *mine = a.recv[a.rank];
+  uint32_t *my_flags = a.flags[a.rank];
+  const int units = p.tiles * CH;
+  for (int u = c; u < units; u += p.grid) {
+    const int tile = u / CH, ch = u % CH;
+    const int nt = tile / p.t_tiles, tt = tile % p.t_tiles;
+    const int t0 = tt * TN + ch * kSlab;
+    if (t0 >= a.T) continue;  // uniform across the CTA
+    const int tmax = min(kSlab, a.T - t0);
+    if (et < a.world) {
+      const uint32_t *f = my_flags + ((size_t)et * p.tiles + tile) * CH + ch;
+      bool ok = ptx::ld_acquire_sys(f) == 1u;
+      if (!ok) {
+        const uint64_t start = ptx::globaltimer_ns();
+        while (!ok) {
+          for (int i = 0; i < 64 && !ok; ++i) ok = ptx::ld_acquire_sys(f) == 1u;
+          if (!ok && ptx::globaltimer_ns() - start > kWaitBudgetNs) break;
+        }
+        if (!ok) report_status(a.status, kStatusPeerTimeout);
+      }
+    }
+    named_bar(1, kEpiThreads);
+    // 16 tokens x 128 columns: thread et handles token et / 8, 16 columns
+    const int tl = et / 8, col = (et % 8) * 16;
+    if (tl < tmax) {
+      const int t = t0 + tl;
+      float acc[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+      for (int src = 0; src < a.world; ++src) {
+        const uint4 *q = reinterpret_cast<const uint4 *>(
+            mine + ((size_t)src * a.T + t) * a.N + (size_t)nt * BM + col);
+        const uint4 u0 = __ldcv(q), u1 = __ldcv(q + 1);
+        const __nv_bfloat16 *e0 = reinterpret_cast<const __nv_bfloat16 *>(&u0);
+        const __nv_bfloat16 *e1 = reinterpret_cast<const __nv_bfloat16 *>(&u1);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          acc[j] += __bfloat162float(e0[j]);
+          acc[8 + j] += __bfloat162float(e1[j]);
+        }
+      }
+      uint4 o0, o1;
+      o0.x = pack_bf16x2(acc[0], acc[1]);
+      o0.y = pack_bf16x2(acc[2], acc[3]);
+      o0.z = pack_bf16x2(acc[4], acc[5]);
+      o0.w = pack_bf16x2(acc[6], acc[7]);
+      o1.x = pack_bf16x2(acc[8], acc[9]);
+      o1.y = pack_bf16x2(acc[10], acc[11]);
+      o1.z = pack_bf16x2(acc[12], acc[13]);
+      o1.w = pack_bf16x2(acc[14], acc[15]);
+      uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(a.y) + (size_t)t * a.ldy +
+                                             (size_t)nt * BM + col);
+      dst[0] = o0;
+      dst[1] = o1;
+    }
+    named_bar(1, kEpiThreads);
+    if (et < a.world) my_flags[((size_t)et * p.tiles + tile) * CH + ch] = 0u;
   }
 }
 
@@ -358,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(&acc_empty[ab]);  // the MMA warp may refill this accumulator
+      if (EPI == kEpiAllReduce && direct) publish_tile<TN>(p, s.tile, et);
       if (!direct) {
         __threadfence();
         named_bar(1, kEpiThreads);
@@ -396,10 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar(1, kEpiThreads);
           }
           if (et == 0) a.counters[s.tile] = 0u;
+          if (EPI == kEpiAllReduce) publish_tile<TN>(p, s.tile, et);
         }
         named_bar(1, kEpiThreads);  // last_flag is rewritten by the next segment
       }
     }
+    if (EPI == kEpiAllReduce) reduce_owned_chunks<TN>(p, c, et);
   }
 
   ptx::tc_fence_before();
@@ -500,6 +612,11 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   if (a.epi == kEpiRopeKV && (a.N / gemm::BM != a.Hq + 2 * a.Hkv || a.cos_sin == nullptr ||
                               a.pos == nullptr || a.slot == nullptr))
     return -6;
+  if (a.epi == kEpiAllReduce) {
+    if (a.world < 1 || a.world > kMaxWorld || a.rank < 0 || a.rank >= a.world) return -7;
+    for (int j = 0; j < a.world; ++j)
+      if (a.recv[j] == nullptr || a.flags[j] == nullptr) return -7;
+  }
   try {
     CUtensorMap tw = tmap::make_2d(a.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.K,
                                    gemm::BM, gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -507,6 +624,8 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
                                    gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
     if (a.epi == kEpiSwiGLU)
       gemm::dispatch<kEpiSwiGLU>(tn, tw, tx, p, stream);
+    else if (a.epi == kEpiAllReduce)
+      gemm::dispatch<kEpiAllReduce>(tn, tw, tx, p, stream);
     else if (a.epi == kEpiRopeKV)
       gemm::dispatch<kEpiRopeKV>(tn, tw, tx, p, stream);
     else

@@ -1,0 +1,78 @@
+"""Row-parallel projection + all-reduce: fused sm_100a kernel vs GEMM + NCCL.
+
+Run under torchrun (one rank per GPU). For each decode/prefill shape of the
+Llama-3-8B o_proj / down_proj at this TP degree: device time of the fused
+kernel and of the baseline (our GEMM followed by NCCL all_reduce), max over
+ranks, and the fused kernel's fraction of its roofline, where the roofline
+time is the slowest of: weight bytes / measured HBM bandwidth, FLOPs /
+measured bf16 peak, and bytes this rank must push over NVLink / 770 GB/s.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..parallel.tp import TensorParallel, init_distributed
+from .common import measured_peaks
+
+NVLINK_GBPS = 770.0  # measured peer copy per direction on this pool
+
+
+def dev_time(fn, iters=30, warmup=5):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    e.synchronize()
+    t = torch.tensor([s.elapsed_time(e) / iters], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens", default="1,16,64,256,2048")
+    args = ap.parse_args()
+    rank, world, local = init_distributed("nccl")
+    dev = torch.device("cuda", local)
+    peaks = measured_peaks()
+    fused = TensorParallel(mode="fused", device=dev)
+    base = TensorParallel(mode="nccl", device=dev)
+    for name, (N, Kfull) in {"o_proj": (4096, 4096), "down_proj": (4096, 14336)}.items():
+        K = Kfull // world
+        w = (torch.randn(N, K, device=dev) / math.sqrt(Kfull)).to(torch.bfloat16)
+        for T in (int(t) for t in args.tokens.split(",")):
+            x = torch.randn(T, K, device=dev).to(torch.bfloat16)
+            y = torch.empty(T, N, dtype=torch.bfloat16, device=dev)
+            t_f = dev_time(lambda: fused.linear_allreduce(x, w, y))
+            t_b = dev_time(lambda: base.linear_allreduce(x, w, y))
+            wbytes = N * K * 2
+            t_hbm = wbytes / (peaks["hbm_gbs"] * 1e9)
+            t_flop = 2 * T * N * K / (peaks["bf16_tflops"] * 1e12)
+            t_nvl = (world - 1) * T * N * 2 / (NVLINK_GBPS * 1e9)
+            roof = max(t_hbm, t_flop, t_nvl)
+            rec = {"op": name, "tp": world, "T": T, "N": N, "K_local": K,
+                   "fused_us": round(t_f * 1e3, 2), "gemm_plus_nccl_us": round(t_b * 1e3, 2),
+                   "speedup": round(t_b / t_f, 3), "roofline_us": round(roof * 1e6, 2),
+                   "bound": ["hbm", "tensor", "nvlink"][[t_hbm, t_flop, t_nvl].index(roof)],
+                   "frac_of_roofline": round(roof * 1e3 / t_f, 3)}
+            if rank == 0:
+                print(json.dumps(rec), flush=True)
+    ops.check_status()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

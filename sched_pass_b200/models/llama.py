@@ -108,6 +108,56 @@ def init_weights(cfg: ModelConfig, device, tp_rank: int = 0, tp_size: int = 1, s
                         vocab_offset=tp_rank * v_local)
 
 
+def full_weights(cfg: ModelConfig, seed: int = 0) -> ModelWeights:
+    """Unsharded random weights on the CPU (fp32 generator, bf16 storage), for
+    comparing tensor-parallel shards against a single-GPU model."""
+    g = torch.Generator().manual_seed(seed)
+    H, D = cfg.hidden, cfg.head_dim
+    rnd = lambda shape, std: (torch.randn(shape, generator=g) * std).to(torch.bfloat16)
+    layers = []
+    for _ in range(cfg.n_layers):
+        layers.append(LayerWeights(
+            ln_in=torch.ones(H, dtype=torch.bfloat16),
+            qkv=rnd((cfg.qkv_dim, H), 1.0 / math.sqrt(H)),
+            o=rnd((H, cfg.n_q_heads * D), 1.0 / math.sqrt(cfg.n_q_heads * D)),
+            ln_post=torch.ones(H, dtype=torch.bfloat16),
+            gate_up=rnd((2 * cfg.ffn, H), 1.0 / math.sqrt(H)),
+            down=rnd((H, cfg.ffn), 1.0 / math.sqrt(cfg.ffn))))
+    v = (cfg.vocab + 127) // 128 * 128
+    return ModelWeights(embed=rnd((cfg.vocab, H), 1.0), layers=layers,
+                        ln_final=torch.ones(H, dtype=torch.bfloat16), lm_head=rnd((v, H), 1.0 / math.sqrt(H)))
+
+
+def shard_weights(cfg: ModelConfig, full: ModelWeights, rank: int, world: int, device) -> ModelWeights:
+    """This rank's tensor-parallel shard of ``full``: whole q/kv heads and
+    whole 64-row gate/up blocks per rank, the matching K-slices of o/down,
+    and a contiguous vocabulary slice of the LM head."""
+    D = cfg.head_dim
+    hq, hkv = cfg.n_q_heads // world, cfg.n_kv_heads // world
+    I = cfg.ffn // world
+    to = lambda t: t.to(device).contiguous()
+    layers = []
+    for lw in full.layers:
+        q = lw.qkv[: cfg.n_q_heads * D].view(cfg.n_q_heads, D, -1)
+        k = lw.qkv[cfg.n_q_heads * D:(cfg.n_q_heads + cfg.n_kv_heads) * D].view(cfg.n_kv_heads, D, -1)
+        v = lw.qkv[(cfg.n_q_heads + cfg.n_kv_heads) * D:].view(cfg.n_kv_heads, D, -1)
+        qkv = torch.cat([q[rank * hq:(rank + 1) * hq].reshape(-1, cfg.hidden),
+                         k[rank * hkv:(rank + 1) * hkv].reshape(-1, cfg.hidden),
+                         v[rank * hkv:(rank + 1) * hkv].reshape(-1, cfg.hidden)])
+        gate, up = deinterleave_gate_up(lw.gate_up)
+        gu = interleave_gate_up(gate[rank * I:(rank + 1) * I], up[rank * I:(rank + 1) * I])
+        layers.append(LayerWeights(
+            ln_in=to(lw.ln_in), qkv=to(qkv), o=to(lw.o[:, rank * hq * D:(rank + 1) * hq * D]),
+            ln_post=to(lw.ln_post), gate_up=to(gu), down=to(lw.down[:, rank * I:(rank + 1) * I])))
+    v_local = (cfg.vocab + world - 1) // world
+    v_local = (v_local + 127) // 128 * 128
+    lm = torch.zeros(v_local, cfg.hidden, dtype=torch.bfloat16)
+    rows = full.lm_head[rank * v_local:min((rank + 1) * v_local, full.lm_head.shape[0])]
+    lm[: rows.shape[0]] = rows
+    return ModelWeights(embed=to(full.embed), layers=layers, ln_final=to(full.ln_final), lm_head=to(lm),
+                        vocab_offset=rank * v_local)
+
+
 @dataclass
 class ForwardBatch:
     """Device inputs of one forward (static buffers when graph-captured)."""

@@ -1,0 +1,41 @@
+"""Multi-GPU checks (2+ GPUs), run as torchrun child processes."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _ngpus():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def run_torchrun(worker, n, timeout=600, env=None):
+    cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", f"--nproc-per-node={n}", "--master-addr=127.0.0.1", "--master-port=29531",
+           os.path.join(ROOT, "tests", "workers", worker)]
+    e = dict(os.environ)
+    e.update(env or {})
+    r = subprocess.run(cmd, capture_output=True, text=True, env=e, cwd=ROOT)
+    return r
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+def test_fused_allreduce_and_tp_engine():
+    n = 2 if _ngpus() < 4 else min(_ngpus(), 8)
+    r = run_torchrun("tp_worker.py", n)
+    line = [l for l in r.stdout.splitlines() if l.startswith("TPJSON ")]
+    assert r.returncode == 0 and line, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.loads(line[0][len("TPJSON "):])
+    for c in res["checks"]:
+        assert c["rel_err"] < 1e-2, c
+        assert c["identical_on_ranks"], c
+    # bf16 partial sums across ranks round differently from one GPU's GEMM,
+    # so greedy paths may diverge late; the first tokens must agree
+    assert all(res["first_token_match"]), res
+    assert res["token_match_rate"] >= 0.8, res
