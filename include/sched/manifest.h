@@ -59,7 +59,7 @@ inline constexpr Lever kLevers[] = {
      "linear value -> 0) on the loop's canonical induction variable; tau == 0 is bit-exact"},
     {"policy", Effect::Hint, 80, "ctrl", "SCHED_NO_POLICY", true, 3, "-nop",
      "urgent (hint 1, or hint 0 with q*dT - lambda_bw*dR - H > 0): L2 evict_last prefetch "
-     "ahead of the stream; polite (hint 2): discard the consumed L2 lines"},
+     "ahead of the stream; polite (hint 2): demote consumed lines to normal L2 priority"},
     {"timer", Effect::Observe, 0, "timer,ctrl", "SCHED_NO_TIMER", true, 4, "-ti",
      "clock64 bracket, thread 0 adds the task's cycles to timer[task]; ctrl.flags bit0 is read "
      "once at entry and switches this launch's write off"},

@@ -113,10 +113,12 @@ __device__ __forceinline__ void timer_commit(const SchedSlots &s, bool off, uint
 __device__ __forceinline__ void l2_prefetch_evict_last(const void *p) {
   asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
 }
-__device__ __forceinline__ void l2_discard_line(const void *p) {
-  // discard needs a 128-byte aligned line address
+// Polite tier: demote a consumed 128-byte line to normal eviction priority.
+// (discard.global.L2 is not used: it drops the line without write-back, so
+// data still dirty in L2 would be lost.)
+__device__ __forceinline__ void l2_demote_line(const void *p) {
   const void *a = reinterpret_cast<const void *>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(127));
-  asm volatile("discard.global.L2 [%0], 128;" ::"l"(a) : "memory");
+  asm volatile("applypriority.global.L2::evict_normal [%0], 128;" ::"l"(a) : "memory");
 }
 
 // PDL overlap points.

@@ -79,7 +79,8 @@ def build_extension(verbose: bool = False):
     )
 
 
-WEAVE_SOURCES = ["weave/ir.cpp", "weave/weave_pass.cpp", "weave/workqueue_pass.cpp", "weave/main.cpp"]
+WEAVE_SOURCES = ["weave/ir.cpp", "weave/passes.cpp", "weave/weave_pass.cpp", "weave/workqueue_pass.cpp",
+                 "weave/main.cpp"]
 
 
 def weave_binary() -> str:

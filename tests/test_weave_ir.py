@@ -1,0 +1,174 @@
+"""The IR weaver on hand-written NVPTX fixtures (GPU-free): structure of the
+woven code (FileCheck-style ordered patterns), knob gating, verification by
+LLVM's own parser/verifier, and the manifest mirror."""
+import os
+import re
+
+import pytest
+
+from sched_pass_b200.compiler.weave import manifest_csv, weave
+from sched_pass_b200.runtime.manifest import MANIFEST
+
+HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "ir")
+
+
+def fixture(name):
+    with open(os.path.join(HERE, name)) as f:
+        return f.read()
+
+
+def check_order(text, patterns):
+    """Each regex must match, in order, after the previous match."""
+    pos = 0
+    for p in patterns:
+        m = re.compile(p, re.M).search(text, pos)
+        assert m, f"pattern not found after offset {pos}: {p}"
+        pos = m.end()
+
+
+def verify(text):
+    import llvmlite.binding as llvm
+    llvm.initialize_all_targets()
+    llvm.initialize_all_asmprinters()
+    m = llvm.parse_assembly(text)
+    m.verify()
+
+
+def test_weave_paged_linear_structure():
+    out, notes = weave(fixture("paged_linear.ll"))
+    verify(out)
+    check_order(out, [
+        r"define ptx_kernel void @paged_linear\(.*\"sched-instrumented\"",
+        # timer: clock at entry, off-flag latched at entry, gated on ctrl armed
+        r"%sched\.t0 = call i64 @llvm\.nvvm\.read\.ptx\.sreg\.clock64\(\)",
+        r"%sched\.flags = load i32",
+        r"%sched\.timer\.off = icmp ne i32",
+        r"%sched\.timer\.gate = select i1 %sched\.ctrl\.armed",
+        # pi: armed + bounds guard, table load, order_size validity, clamp, select
+        r"%sched\.pid = call i32 @llvm\.nvvm\.read\.ptx\.sreg\.ctaid\.x\(\)",
+        r"%sched\.order\.use = and i1 %sched\.task_order\.armed, %sched\.pid\.inb",
+        r"%sched\.task\.mapped = load i32",
+        r"%sched\.order\.size = load i32",
+        r"%sched\.order\.valid = or i1",
+        r"%sched\.order\.szok = and i1",
+        r"%sched\.task\.ingrid = icmp ult i32 %sched\.task\.mapped, %sched\.ntiles",
+        r"%sched\.task\.ok = and i1 %sched\.task\.ingrid, %sched\.order\.szok",
+        r"%sched\.task = select i1 %sched\.task\.ok, i32 %sched\.task\.mapped, i32 %sched\.pid",
+        # the original ctaid use now reads the remapped task
+        r"%row = mul i32 %sched\.task, %nb",
+        # shed on the canonical IV %i, value mask after the stream load
+        r"%v = load float",
+        r"%sched\.keep(\.\d+)? = icmp ult i32 %i, %sched\.budget",
+        r"select i1 %sched\.keep(\.\d+)?, float %v, float 0\.000000e\+00",
+        # timer at the return: cycles, gate, guarded monotonic atomic add
+        r"%sched\.cycles = sub i64 %sched\.t1, %sched\.t0",
+        r"%sched\.timer\.on = xor i1 %sched\.timer\.gate, true",
+        r"br i1 %sched\.timer\.ok, label %sched\.timer\.do, label %sched\.timer\.ret",
+        r"atomicrmw add ptr %sched\.timer\.row, i64 %sched\.cycles monotonic",
+    ])
+    assert any("remapped 1 ctaid" in n for n in notes)
+    assert any("polite tier only" in n for n in notes)  # index-based stream
+
+
+def test_weave_softmax_masks_score_not_values():
+    out, notes = weave(fixture("softmax_decode.ll"))
+    verify(out)
+    check_order(out, [
+        r"%s = fmul float %s\.next, %scale",
+        r"%sched\.keep = icmp ult i32 %t, %sched\.budget",
+        r"%sched\.shed\.score = select i1 %sched\.keep, float %s, float 0xFFF0000000000000",
+        r"%m\.next = call float @llvm\.maxnum\.f32\(float %m, float %sched\.shed\.score\)",
+        r"%ds = fsub float %sched\.shed\.score, %m\.next",
+    ])
+    assert out.count("%sched.shed.score = ") == 1
+    assert "%sched.shed.val" not in out  # V loads untouched in a softmax kernel
+    # the accumulator the kernel reads back and rewrites is never a stream site:
+    # no L2 hint may follow its load, and no discard is ever emitted
+    check_order(out, [r"%av = load float, ptr %a\.gep"])
+    after = out.split("%av = load float, ptr %a.gep", 1)[1].split("\n", 2)[1]
+    assert "applypriority" not in after and "discard" not in out
+    assert any("softmax score mask" in n for n in notes)
+
+
+@pytest.mark.parametrize("knob,absent", [
+    ("SCHED_NO_INDIRECT", "%sched.task.mapped"),
+    ("SCHED_NO_TIMER", "%sched.t0"),
+    ("SCHED_NO_SHED", "%sched.keep"),
+    ("SCHED_NO_POLICY", "applypriority.global.L2"),
+])
+def test_disable_knobs(knob, absent):
+    out, _ = weave(fixture("paged_linear.ll"), {knob: "1"})
+    verify(out)
+    assert absent not in out
+    full, _ = weave(fixture("paged_linear.ll"))
+    assert absent in full
+
+
+def test_pdl_points():
+    out, _ = weave(fixture("paged_linear.ll"), {"SCHED_PDL": "1"})
+    verify(out)
+    check_order(out, [r"griddepcontrol\.wait", r"griddepcontrol\.launch_dependents;.*\n\s*ret void"])
+
+
+@pytest.mark.parametrize("clc", [False, True])
+def test_workqueue_driver(clc):
+    env = {"SCHED_WORKQUEUE": "1"}
+    if clc:
+        env["SCHED_CLC"] = "1"
+    text = fixture("paged_linear.ll")
+    if not clc:
+        text = text.replace("@__sched_timer = ", "@__sched_queue = addrspace(1) externally_initialized global ptr null, align 8\n@__sched_timer = ")
+    out, notes = weave(text, env)
+    verify(out)
+    check_order(out, [
+        r"define ptx_kernel void @paged_linear\(.*\"sched-wq-driver\"",
+        r"%sched\.grid1d = and i1",
+        r"br i1 %sched\.wq\.armed, label %sched\.dyn, label %sched\.stock",
+        r"sched\.stock:",
+        r"call void @paged_linear\.sched_body\(",
+        r"sched\.dyn:",
+        r"%sched\.ntasks = load i32",
+        r"sched\.loop:",
+        r"%sched\.raw = phi i32 \[ %sched\.first, %sched\.bound \], \[ %sched\.raw\.next, %sched\.claimed \]",
+        r"call void @paged_linear\.sched_body\(",
+        r"call void @llvm\.nvvm\.barrier0\(\)",
+        r"sched\.claim:",
+        (r"clusterlaunchcontrol\.try_cancel" if clc else r"atomicrmw add ptr %sched\.queue\.slot, i32 1"),
+        r"sched\.claimed:",
+        r"define internal void @paged_linear\.sched_body\(.*i32 %sched\.task\.arg\).*\"sched-task-body\"",
+        r"%row = mul i32 %sched\.task\.arg, %nb",
+        r"atomicrmw add ptr %sched\.timer\.row",
+    ])
+    if clc:
+        assert "setp.lt.u32 %pl, %cnt" in out  # the claim's wait is bounded
+
+
+def test_baked_addresses_use_a_non_constant_slot():
+    text = fixture("paged_linear.ll")
+    for g in ("@__sched_task_order", "@__sched_ctrl", "@__sched_timer"):
+        text = "\n".join(l for l in text.splitlines() if not l.startswith(g + " ="))
+    base = 0x5C00_0000_0000
+    env = {"SCHED_BAKE_TASK_ORDER": base, "SCHED_BAKE_CTRL": base + 0x40000, "SCHED_BAKE_TIMER": base + 0x80000}
+    out, _ = weave(text, env)
+    verify(out)
+    assert f"@__sched_ctrl.bakedslot = internal addrspace(1) global i64 {base + 0x40000}" in out
+    assert "inttoptr i64 %sched.ctrl.baked" in out
+
+
+def test_no_slots_no_weave():
+    text = fixture("paged_linear.ll")
+    for g in ("@__sched_task_order", "@__sched_ctrl", "@__sched_timer"):
+        text = "\n".join(l for l in text.splitlines() if not l.startswith(g + " ="))
+    out, _ = weave(text)
+    verify(out)
+    assert "%sched.task.mapped" not in out and "%sched.t0" not in out
+
+
+def test_manifest_mirror_matches_cpp():
+    rows = manifest_csv()
+    assert [r["name"] for r in rows] == [m[0] for m in MANIFEST]
+    for r, m in zip(rows, MANIFEST):
+        name, effect, min_sm, knob, disables, tag = m
+        assert r["effect"] == effect and int(r["minSm"]) == min_sm and r["knob"] == knob
+        assert int(r["disableKnob"]) == int(disables) and r["tag"] == tag
+    assert [int(r["order"]) for r in rows] == list(range(len(rows)))
