@@ -36,7 +36,15 @@ int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int
                     cudaStream_t st);
 int sched_argmax(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
                  int id_offset, cudaStream_t st);
+int sched_moe_router(const void *x, const void *wr, int T, int H, int E, int K, int32_t *ids,
+                     float *wts, cudaStream_t st);
+int sched_moe_quantize(const void *in, int R, int I, void *out, float *scale,
+                       const uint32_t *rows_valid, int rows_per_expert, cudaStream_t st);
+int sched_moe_combine_norm(const void *c, int K, void *h, const void *w, void *y, int T, int H,
+                           float eps, uint32_t *cnt, uint32_t *dropped_step, uint32_t *arrivals,
+                           int *status, cudaStream_t st);
 }
+#include "moe_api.h"
 
 namespace {
 
@@ -302,6 +310,105 @@ void argmax(const at::Tensor &logits, at::Tensor &ids, const c10::optional<at::T
            "argmax");
 }
 
+// ---------------------------------------------------------------- MoE
+void moe_router(const at::Tensor &x, const at::Tensor &wr, at::Tensor &ids, at::Tensor &wts, int64_t k) {
+  check_bf16(x, "x");
+  check_bf16(wr, "wr");
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(sched_moe_router(x.data_ptr(), wr.data_ptr(), x.size(0), x.size(1), wr.size(0), k,
+                            ids.data_ptr<int32_t>(), wts.data_ptr<float>(), cur_stream()),
+           "moe_router");
+}
+
+// p: dict-like flat vector of int64 arguments (see sched_pass_b200/parallel/ep.py)
+void moe_dispatch(const at::Tensor &x, const at::Tensor &ids, const at::Tensor &wts, int64_t T,
+                  int64_t K, int64_t E, int64_t E_local, int64_t rank, int64_t world, int64_t capacity,
+                  int64_t rows, const std::vector<int64_t> &slab, const std::vector<int64_t> &slab_scale,
+                  const std::vector<int64_t> &slab_meta, const std::vector<int64_t> &counter,
+                  const std::vector<int64_t> &done, int64_t local_done, int64_t combine_local,
+                  int64_t dropped_step, int64_t dropped_total, const c10::optional<at::Tensor> &status) {
+  moe::DispatchArgs a{};
+  a.x = reinterpret_cast<const __nv_bfloat16 *>(x.data_ptr());
+  a.ids = ids.data_ptr<int32_t>();
+  a.wts = wts.data_ptr<float>();
+  a.T = T;
+  a.H = x.size(1);
+  a.K = K;
+  a.E = E;
+  a.E_local = E_local;
+  a.rank = rank;
+  a.world = world;
+  a.capacity = capacity;
+  a.rows_per_expert = rows;
+  for (int r = 0; r < world; ++r) {
+    a.slab[r] = reinterpret_cast<uint8_t *>(slab[r]);
+    a.slab_scale[r] = reinterpret_cast<float *>(slab_scale[r]);
+    a.slab_meta[r] = reinterpret_cast<int32_t *>(slab_meta[r]);
+    a.counter[r] = reinterpret_cast<uint32_t *>(counter[r]);
+    a.done[r] = reinterpret_cast<uint32_t *>(done[r]);
+  }
+  a.local_done = reinterpret_cast<uint32_t *>(local_done);
+  a.combine_local = reinterpret_cast<__nv_bfloat16 *>(combine_local);
+  a.dropped_step = reinterpret_cast<uint32_t *>(dropped_step);
+  a.dropped_total = reinterpret_cast<uint32_t *>(dropped_total);
+  a.status = ptr_or_null<int>(status);
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(sched_moe_dispatch(&a, cur_stream()), "moe_dispatch");
+}
+
+void moe_expert_gemm(int64_t epi, const at::Tensor &w, int64_t x_ptr, int64_t E_local, int64_t N, int64_t K,
+                     int64_t rows, const at::Tensor &w_scale, int64_t x_scale, int64_t act, int64_t counter,
+                     int64_t done, int64_t rows_valid, int64_t tiles_done, int64_t world, int64_t capacity,
+                     int64_t meta, const std::vector<int64_t> &combine, const std::vector<int64_t> &combine_cnt,
+                     int64_t k_top, const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(w.is_cuda() && w.element_size() == 1, "w: fp8 e4m3 [E_local * N, K]");
+  moe::ExpertArgs a{};
+  a.E_local = E_local;
+  a.N = N;
+  a.K = K;
+  a.rows_per_expert = rows;
+  a.w_scale = w_scale.data_ptr<float>();
+  a.x_scale = reinterpret_cast<const float *>(x_scale);
+  a.act = reinterpret_cast<__nv_bfloat16 *>(act);
+  a.counter = reinterpret_cast<uint32_t *>(counter);
+  a.done = reinterpret_cast<uint32_t *>(done);
+  a.rows_valid = reinterpret_cast<uint32_t *>(rows_valid);
+  a.tiles_done = reinterpret_cast<uint32_t *>(tiles_done);
+  a.world = world;
+  a.capacity = capacity;
+  a.meta = reinterpret_cast<const int32_t *>(meta);
+  for (size_t r = 0; r < combine.size() && r < moe::kMaxWorld; ++r) {
+    a.combine[r] = reinterpret_cast<__nv_bfloat16 *>(combine[r]);
+    a.combine_cnt[r] = reinterpret_cast<uint32_t *>(combine_cnt[r]);
+  }
+  a.k_top = k_top;
+  a.status = ptr_or_null<int>(status);
+  c10::cuda::CUDAGuard g(w.device());
+  check_rc(sched_moe_expert_gemm(epi, w.data_ptr(), reinterpret_cast<const void *>(x_ptr), &a, cur_stream()),
+           "moe_expert_gemm");
+}
+
+void moe_quantize(int64_t in, int64_t R, int64_t I, int64_t out, int64_t scale, int64_t rows_valid,
+                  int64_t rows) {
+  check_rc(sched_moe_quantize(reinterpret_cast<const void *>(in), R, I, reinterpret_cast<void *>(out),
+                              reinterpret_cast<float *>(scale), reinterpret_cast<const uint32_t *>(rows_valid),
+                              rows, cur_stream()),
+           "moe_quantize");
+}
+
+void moe_combine_norm(int64_t c, int64_t K, at::Tensor &h, const at::Tensor &w, at::Tensor &y, int64_t T,
+                      double eps, int64_t cnt, int64_t dropped_step, int64_t arrivals,
+                      const c10::optional<at::Tensor> &status) {
+  check_bf16(h, "h");
+  check_bf16(y, "y");
+  c10::cuda::CUDAGuard g(h.device());
+  check_rc(sched_moe_combine_norm(reinterpret_cast<const void *>(c), K, h.data_ptr(), w.data_ptr(), y.data_ptr(), T,
+                                  h.size(1), (float)eps, reinterpret_cast<uint32_t *>(cnt),
+                                  reinterpret_cast<uint32_t *>(dropped_step), reinterpret_cast<uint32_t *>(arrivals),
+                                  ptr_or_null<int>(status), cur_stream()),
+           "moe_combine_norm");
+}
+
 }  // namespace
 
 void register_symm(py::module &m);
@@ -322,4 +429,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_kv_append", &rope_kv_append);
   m.def("embedding", &embedding);
   m.def("argmax", &argmax);
+  m.def("moe_router", &moe_router);
+  m.def("moe_dispatch", &moe_dispatch);
+  m.def("moe_expert_gemm", &moe_expert_gemm);
+  m.def("moe_quantize", &moe_quantize);
+  m.def("moe_combine_norm", &moe_combine_norm);
 }

@@ -109,3 +109,25 @@ def llama_forward_tokens(cfg, weights, token_ids, cos_sin):
         h = (h + d.to(torch.bfloat16).float()).to(torch.bfloat16).float()
     x = rmsnorm(h, weights.ln_final, cfg.rms_eps).to(torch.bfloat16)
     return linear(x[-1:], weights.lm_head)[0, : cfg.vocab]
+
+
+def moe(x, router, w13_experts, w2_experts, top_k, block=64, quantize_x=None, quantize_act=None):
+    """Top-k softmax-routed SwiGLU experts. w13_experts[e]: [2I, H] with
+    gate/up interleaved per ``block`` rows; w2_experts[e]: [H, I]; all fp32.
+    ``quantize_x(x) -> x'`` / ``quantize_act(a) -> a'`` optionally apply the
+    kernels' quantisation of the token rows and of the SwiGLU output."""
+    xf = x.float()
+    logits = xf @ router.float().t()
+    val, idx = logits.topk(top_k, dim=-1)
+    wts = torch.softmax(val, dim=-1)
+    xq = quantize_x(xf) if quantize_x is not None else xf
+    out = torch.zeros_like(xf)
+    for t in range(xf.shape[0]):
+        for j in range(top_k):
+            e = int(idx[t, j])
+            y = swiglu_linear(xq[t:t + 1], w13_experts[e], block)
+            y = y.to(torch.bfloat16).float()
+            if quantize_act is not None:
+                y = quantize_act(y)
+            out[t] += wts[t, j] * (y @ w2_experts[e].float().t())[0]
+    return out, idx, wts

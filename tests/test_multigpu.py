@@ -39,3 +39,15 @@ def test_fused_allreduce_and_tp_engine():
     # so greedy paths may diverge late; the first tokens must agree
     assert all(res["first_token_match"]), res
     assert res["token_match_rate"] >= 0.8, res
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_layer():
+    n = 2 if _ngpus() < 4 else min(_ngpus(), 8)
+    r = run_torchrun("ep_worker.py", n)
+    line = [l for l in r.stdout.splitlines() if l.startswith("EPJSON ")]
+    assert r.returncode == 0 and line, r.stdout[-3000:] + r.stderr[-3000:]
+    for res in json.loads(line[0][len("EPJSON "):]):
+        assert res["dropped"] == 0, res
+        for c in res["checks"]:
+            assert c["rel_err"] < 3e-2, c
