@@ -51,6 +51,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 #include <stdexcept>
 
 #include "common.cuh"
@@ -634,4 +635,62 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
     return -3;
   }
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+// ---------------------------------------------------------------------------
+// Fixed-scratch entry point (declared with its contract in gemm_api.h).
+namespace gemm {
+
+static __device__ __align__(256) float g_fixed_ws[kFixedScratchWsFloats];
+static __device__ __align__(256) uint32_t g_fixed_counters[kFixedScratchCounters];
+
+constexpr int kFixedMaxDevices = 64;
+struct FixedScratch {
+  float *ws = nullptr;
+  uint32_t *counters = nullptr;
+};
+static std::mutex g_fixed_mu;
+static FixedScratch g_fixed[kFixedMaxDevices];
+
+// Device addresses of the arrays on the current device, looked up once.
+static bool fixed_scratch(FixedScratch &out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kFixedMaxDevices) return false;
+  std::lock_guard<std::mutex> lock(g_fixed_mu);
+  FixedScratch &s = g_fixed[dev];
+  if (s.ws == nullptr) {
+    void *ws = nullptr, *cnt = nullptr;
+    if (cudaGetSymbolAddress(&ws, g_fixed_ws) != cudaSuccess ||
+        cudaGetSymbolAddress(&cnt, g_fixed_counters) != cudaSuccess) {
+      cudaGetLastError();  // leave no sticky-looking error for the caller's next check
+      return false;
+    }
+    s.ws = static_cast<float *>(ws);
+    s.counters = static_cast<uint32_t *>(cnt);
+  }
+  out = s;
+  return true;
+}
+
+}  // namespace gemm
+
+extern "C" int sched_gemm_run_fixed_scratch(const GemmArgs *args, cudaStream_t stream) {
+  if (args == nullptr || args->epi == kEpiAllReduce) return kFixedScratchBadEpilogue;
+  GemmArgs a = *args;
+  if (a.T <= 0) return 0;
+  if (a.N % gemm::BM != 0 || a.K % gemm::BK != 0) return -1;
+  gemm::Params p;
+  int tn;
+  gemm::plan(a, p, tn);
+  if (gemm::splits_tiles(p)) {
+    const long long need = (long long)p.grid * 2 * tn * gemm::BM;
+    if (need > kFixedScratchWsFloats || p.tiles > kFixedScratchCounters) return kFixedScratchTooLarge;
+  }
+  gemm::FixedScratch s;
+  if (!gemm::fixed_scratch(s)) return kFixedScratchLookupFailed;
+  a.ws = s.ws;
+  a.ws_floats = kFixedScratchWsFloats;
+  a.counters = s.counters;
+  a.counter_count = kFixedScratchCounters;
+  return sched_gemm_run(&a, stream);
 }

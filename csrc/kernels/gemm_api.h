@@ -47,3 +47,47 @@ struct GemmArgs {
 
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream);
 extern "C" long long sched_gemm_ws_floats(int T, int N, int K, int grid);
+
+// ---------------------------------------------------------------------------
+// Fixed-scratch entry point: sched_gemm_run without caller-provided scratch.
+//
+// No counterpart in the reference: it is for callers that may not allocate
+// device memory at all (an embedding host whose allocator is off limits, a
+// memory-capped sandbox, code that runs after the pool is sized). Instead of
+// `ws` / `counters` it uses file-scope device arrays compiled into the
+// module, so the call allocates nothing: no cudaMalloc or cudaFree and no
+// caching allocator behind it.
+//
+//   * `ws`, `ws_floats`, `counters` and `counter_count` in *args are ignored;
+//     every other field means what it means for sched_gemm_run.
+//   * Scratch capacity is fixed: kFixedScratchWsFloats floats of stream-K
+//     partial slices (16 MiB) and kFixedScratchCounters tile counters. A call
+//     whose schedule needs more (sched_gemm_ws_floats(T, N, K, grid) above the
+//     first, or more split tiles than the second) is refused with
+//     kFixedScratchTooLarge before anything is launched; a smaller `grid`
+//     needs less.
+//   * The per-tile counters must be zero when a call starts. They start zero
+//     (static storage) and each call that completes with a zero status word
+//     leaves them zero again: the last CTA on a split tile resets its
+//     counter. A call that reports a non-zero status may leave them dirty,
+//     after which results of this entry point on that device are unreliable.
+//     The partial slices need no initial value.
+//   * The scratch is one per device and shared by all calls on it: calls
+//     that can overlap in time (different streams, or host threads on
+//     unsynchronised streams) race on it and corrupt each other. Calls in
+//     one stream are ordered and safe.
+//   * The first call on each device looks up the arrays' device addresses
+//     (cudaGetSymbolAddress, with that device current) and caches them;
+//     make that first call before any stream capture begins. The stream must
+//     belong to the current device.
+//   * kEpiAllReduce is refused (kFixedScratchBadEpilogue): its peer receive
+//     buffers come from a symmetric allocation.
+// Returns 0, a sched_gemm_run code, or one of the codes below.
+constexpr long long kFixedScratchWsFloats = 1ll << 22;
+constexpr int kFixedScratchCounters = 1 << 14;
+enum FixedScratchError : int {
+  kFixedScratchTooLarge = -8,      // the call needs more scratch than the fixed capacity
+  kFixedScratchLookupFailed = -9,  // no current device, or cudaGetSymbolAddress failed
+  kFixedScratchBadEpilogue = -10,  // kEpiAllReduce or a null args pointer
+};
+extern "C" int sched_gemm_run_fixed_scratch(const GemmArgs *args, cudaStream_t stream);

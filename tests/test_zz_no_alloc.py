@@ -1,0 +1,97 @@
+"""The fixed-scratch GEMM entry point, called through its exported C symbol.
+
+``sched_gemm_run_fixed_scratch`` runs the stream-K tcgen05 GEMM with scratch
+that lives in the module's own device arrays, so the call allocates nothing.
+It is checked against the regular entry point (``ops.linear``, which hands the
+kernel a caller-owned workspace) on shapes whose tiles are split across CTAs,
+i.e. shapes that really use the scratch, twice in a row each: the second call
+only agrees if the first left the tile counters at zero. This file is named to
+be collected last so that it also runs after every other GPU test.
+"""
+import ctypes
+import math
+
+import pytest
+import torch
+
+from sched_pass_b200 import _build, ops
+from sched_pass_b200._ext import ext
+
+pytestmark = pytest.mark.gpu
+
+EPI_STORE, EPI_SWIGLU, EPI_ALLREDUCE = 0, 1, 3
+TOO_LARGE, BAD_EPILOGUE = -8, -10
+WS_CAP = 1 << 22
+
+
+class GemmArgs(ctypes.Structure):
+    """Mirror of the C struct GemmArgs (natural x86-64 layout)."""
+    _fields_ = [
+        ("x", ctypes.c_void_p), ("ldx", ctypes.c_int),
+        ("w", ctypes.c_void_p), ("y", ctypes.c_void_p), ("ldy", ctypes.c_int),
+        ("T", ctypes.c_int), ("N", ctypes.c_int), ("K", ctypes.c_int),
+        ("epi", ctypes.c_int), ("grid", ctypes.c_int), ("num_sms", ctypes.c_int),
+        ("ws", ctypes.c_void_p), ("ws_floats", ctypes.c_longlong),
+        ("counters", ctypes.c_void_p), ("counter_count", ctypes.c_int),
+        ("status", ctypes.c_void_p),
+        ("pos", ctypes.c_void_p), ("slot", ctypes.c_void_p), ("cos_sin", ctypes.c_void_p),
+        ("q_out", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+        ("Hq", ctypes.c_int), ("Hkv", ctypes.c_int), ("page_size", ctypes.c_int),
+        ("rank", ctypes.c_int), ("world", ctypes.c_int),
+        ("recv", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8),
+    ]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    ext()  # builds / loads the extension; ctypes then shares the loaded image
+    so = ctypes.CDLL(_build.ext_path())
+    so.sched_gemm_run_fixed_scratch.argtypes = [ctypes.POINTER(GemmArgs), ctypes.c_void_p]
+    so.sched_gemm_run_fixed_scratch.restype = ctypes.c_int
+    so.sched_gemm_ws_floats.argtypes = [ctypes.c_int] * 4
+    so.sched_gemm_ws_floats.restype = ctypes.c_longlong
+    return so
+
+
+def call(lib, x, w, y, epi, grid):
+    st = ops.status_buffer(x.device)
+    a = GemmArgs(x=x.data_ptr(), ldx=x.stride(0), w=w.data_ptr(), y=y.data_ptr(), ldy=y.stride(0),
+                 T=x.shape[0], N=w.shape[0], K=x.shape[1], epi=epi, grid=grid,
+                 num_sms=torch.cuda.get_device_properties(x.device).multi_processor_count,
+                 status=st.data_ptr())
+    return lib.sched_gemm_run_fixed_scratch(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("T,N,K,epi,grid", [
+    (1, 4096, 4096, EPI_STORE, 0),
+    (16, 6144, 4096, EPI_STORE, 148),
+    (40, 4096, 1024, EPI_STORE, 97),
+    (16, 4096, 2048, EPI_SWIGLU, 0),
+    (64, 2048, 4096, EPI_SWIGLU, 148),
+])
+def test_fixed_scratch_matches_regular_entry_point(lib, T, N, K, epi, grid):
+    assert lib.sched_gemm_ws_floats(T, N, K, grid) > 0, "shape must split tiles (use the scratch)"
+    g = torch.Generator(device="cuda").manual_seed(T * 7 + N)
+    x = torch.randn(T, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    cols = N // 2 if epi == EPI_SWIGLU else N
+    want = ops.linear(x, w, swiglu=epi == EPI_SWIGLU, grid=grid)
+    for _ in range(2):
+        y = torch.full((T, cols), float("nan"), dtype=torch.bfloat16, device="cuda")
+        assert call(lib, x, w, y, epi, grid) == 0
+        torch.cuda.synchronize()
+        ops.check_status()
+        err = ((y.float() - want.float()).norm() / want.float().norm()).item()
+        assert err < 1e-2, err
+
+
+def test_fixed_scratch_refuses_what_it_cannot_hold(lib):
+    T, N, K = 256, 8192, 4096
+    assert lib.sched_gemm_ws_floats(T, N, K, 148) > WS_CAP
+    x = torch.zeros(T, K, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(N, K, dtype=torch.bfloat16, device="cuda")
+    y = torch.zeros(T, N, dtype=torch.bfloat16, device="cuda")
+    assert call(lib, x, w, y, EPI_STORE, 148) == TOO_LARGE
+    assert call(lib, x, w, y, EPI_ALLREDUCE, 148) == BAD_EPILOGUE
+    torch.cuda.synchronize()
+    ops.check_status()
