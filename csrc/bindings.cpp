@@ -80,6 +80,10 @@ int num_sms(const at::Tensor &t) {
   return 148;
 }
 
+// Diagnostic: when set, every GEMM launch records per-CTA timestamps here.
+unsigned long long *g_gemm_trace = nullptr;
+void set_gemm_trace(int64_t ptr) { g_gemm_trace = reinterpret_cast<unsigned long long *>(ptr); }
+
 GemmArgs base_args(const at::Tensor &x, const at::Tensor &w, int64_t grid,
                    const c10::optional<at::Tensor> &ws, const c10::optional<at::Tensor> &counters,
                    const c10::optional<at::Tensor> &status) {
@@ -97,6 +101,7 @@ GemmArgs base_args(const at::Tensor &x, const at::Tensor &w, int64_t grid,
   a.N = w.size(0);
   a.grid = grid;
   a.num_sms = num_sms(x);
+  a.trace = g_gemm_trace;
   a.ws = ptr_or_null<float>(ws);
   a.ws_floats = (ws.has_value() && ws->defined()) ? ws->numel() : 0;
   a.counters = ptr_or_null<uint32_t>(counters);
@@ -360,7 +365,8 @@ void moe_expert_gemm(int64_t epi, const at::Tensor &w, int64_t x_ptr, int64_t E_
                      int64_t rows, const at::Tensor &w_scale, int64_t x_scale, int64_t act, int64_t counter,
                      int64_t done, int64_t rows_valid, int64_t tiles_done, int64_t world, int64_t capacity,
                      int64_t meta, const std::vector<int64_t> &combine, const std::vector<int64_t> &combine_cnt,
-                     int64_t k_top, const c10::optional<at::Tensor> &status) {
+                     int64_t k_top, int64_t ws, int64_t tile_counters, int64_t grid, int64_t trace,
+                     const c10::optional<at::Tensor> &status) {
   TORCH_CHECK(w.is_cuda() && w.element_size() == 1, "w: fp8 e4m3 [E_local * N, K]");
   moe::ExpertArgs a{};
   a.E_local = E_local;
@@ -382,6 +388,10 @@ void moe_expert_gemm(int64_t epi, const at::Tensor &w, int64_t x_ptr, int64_t E_
     a.combine_cnt[r] = reinterpret_cast<uint32_t *>(combine_cnt[r]);
   }
   a.k_top = k_top;
+  a.ws = reinterpret_cast<float *>(ws);
+  a.tile_counters = reinterpret_cast<uint32_t *>(tile_counters);
+  a.grid = grid;
+  a.trace = reinterpret_cast<unsigned long long *>(trace);
   a.status = ptr_or_null<int>(status);
   c10::cuda::CUDAGuard g(w.device());
   check_rc(sched_moe_expert_gemm(epi, w.data_ptr(), reinterpret_cast<const void *>(x_ptr), &a, cur_stream()),
@@ -429,6 +439,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_kv_append", &rope_kv_append);
   m.def("embedding", &embedding);
   m.def("argmax", &argmax);
+  m.def("set_gemm_trace", &set_gemm_trace);
   m.def("moe_router", &moe_router);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_expert_gemm", &moe_expert_gemm);

@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   ptx::fence_proxy_async_smem();
   ptx::tc_fence_before();
+  __syncwarp();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
@@ -558,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  __syncwarp();  // reconverge single-lane roles before the CTA barrier
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 0) ptx::tmem_dealloc(tmem, TMEM_COLS);
@@ -614,7 +616,7 @@ static int launch(const CUtensorMap &tk, const CUtensorMap &tv, const Params &p,
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
     cudaLaunchKernelEx(&cfg, kern, tk, tv, p);
   } else {
     kern<<<grid, kThreads, SMEM, st>>>(tk, tv, p);

@@ -1,6 +1,8 @@
 // common.cuh -- small shared pieces of the framework's CUDA kernels.
 #pragma once
 
+#include <cstdlib>
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -43,9 +45,23 @@ __device__ __forceinline__ void named_bar(uint32_t id, uint32_t nthreads) {
 // Launch with programmatic stream serialization: the kernel may start while
 // the previous kernel in the stream drains; it must call griddepcontrol.wait
 // (ptx::pdl_wait) before touching memory that kernel writes or reads.
+// Programmatic dependent launch for every kernel launch of this library;
+// SCHED_PDL=0 in the environment turns it off (plain stream-ordered launches).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("SCHED_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t st, Args &&...args) {
+  if (!pdl_enabled()) {
+    kernel<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
+    return cudaGetLastError();
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;

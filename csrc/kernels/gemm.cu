@@ -78,6 +78,7 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * ACC_COLS;       // two accumulators
   static constexpr int SLAB_BYTES = kSlab * kSlabPitch * 4;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SLAB_BYTES + 512;
+  static constexpr int smem(int stages) { return 1024 + stages * STAGE_BYTES + SLAB_BYTES + 512; }
 };
 
 struct Params {
@@ -85,6 +86,7 @@ struct Params {
   int n_tiles, t_tiles, kb, tiles;
   long long units;  // tiles * kb
   int grid;
+  int stages;  // ring depth of this launch (<= Cfg<TN>::STAGES)
 };
 
 // One segment: the k-block range [kb0, kb1) of `tile` handled by one CTA.
@@ -312,13 +314,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *base = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *stage_mem = base;
-  float *slab = reinterpret_cast<float *>(base + C::STAGES * C::STAGE_BYTES);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::STAGES * C::STAGE_BYTES + C::SLAB_BYTES);
+  const int S = p.stages;
+  float *slab = reinterpret_cast<float *>(base + S * C::STAGE_BYTES);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + S * C::STAGE_BYTES + C::SLAB_BYTES);
   uint64_t *full = bars;
-  uint64_t *empty = bars + C::STAGES;
-  uint64_t *acc_full = bars + 2 * C::STAGES;       // [2]
-  uint64_t *acc_empty = bars + 2 * C::STAGES + 2;  // [2]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * C::STAGES + 4);
+  uint64_t *empty = bars + S;
+  uint64_t *acc_full = bars + 2 * S;       // [2]
+  uint64_t *acc_empty = bars + 2 * S + 2;  // [2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
   volatile int *last_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -327,12 +330,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const GemmArgs &a = p.a;
 
   ptx::pdl_launch_dependents();
+  if (a.trace && threadIdx.x == 0) a.trace[c * 4] = ptx::globaltimer_ns();
   if (warp == 0) {
     ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
     ptx::tmem_relinquish();
   }
   if (threadIdx.x == 32) {
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
@@ -347,6 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tmX);
   }
   ptx::tc_fence_before();
+  __syncwarp();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
@@ -359,9 +364,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pre = 0;
       {
         Seg s;
-        for (int k = 0; pre < C::STAGES && segment(p, c, k, s); ++k) {
+        for (int k = 0; pre < S && segment(p, c, k, s); ++k) {
           const int nt = s.tile / p.t_tiles;
-          for (int kb = s.kb0; kb < s.kb1 && pre < C::STAGES; ++kb, ++pre) {
+          for (int kb = s.kb0; kb < s.kb1 && pre < S; ++kb, ++pre) {
             ptx::mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
             ptx::tma_load_2d(stage_mem + pre * C::STAGE_BYTES, &tmW, &full[pre], kb * BK, nt * BM);
           }
@@ -374,10 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; ok && segment(p, c, k, s); ++k) {
         const int nt = s.tile / p.t_tiles, tt = s.tile % p.t_tiles;
         for (int kb = s.kb0; kb < s.kb1; ++kb, ++i) {
-          const int st = i % C::STAGES;
+          const int st = i % S;
           uint8_t *sm = stage_mem + st * C::STAGE_BYTES;
           if (i >= pre) {
-            if (!ptx::mbar_wait(&empty[st], ((i / C::STAGES) & 1) ^ 1, kWaitBudgetNs)) {
+            if (!ptx::mbar_wait(&empty[st], ((i / S) & 1) ^ 1, kWaitBudgetNs)) {
               report_status(a.status, kStatusMmaTimeout);
               ok = false;
               break;
@@ -405,8 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         const uint32_t acc = tmem + ab * C::ACC_COLS;
         for (int kb = s.kb0; kb < s.kb1; ++kb, ++i) {
-          const int st = i % C::STAGES;
-          if (!ptx::mbar_wait(&full[st], (i / C::STAGES) & 1, kWaitBudgetNs)) {
+          const int st = i % S;
+          if (!ptx::mbar_wait(&full[st], (i / S) & 1, kWaitBudgetNs)) {
             report_status(a.status, kStatusTmaTimeout);
             ok = false;
             break;
@@ -478,6 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         named_bar(1, kEpiThreads);
         if (*last_flag) {
+          if (a.trace && et == 0) a.trace[c * 4 + 1] += 1ull << 32;
           __threadfence();
           const int c0 = c - s.seg;  // CTA of the tile's first segment
           const int tmax = min(TN, a.T - t0);
@@ -487,16 +493,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) acc[j] = 0.f;
             if (tl < tmax) {
-              for (int sg = 0; sg < s.nsegs; ++sg) {  // fixed order: deterministic sums
-                const float *slice = a.ws + ((size_t)(c0 + sg) * 2 + (sg == 0 ? 1 : 0)) * ((size_t)TN * BM);
-                const float4 *src = reinterpret_cast<const float4 *>(slice + (size_t)tl * BM + part * 16);
+              // fixed segment order (deterministic sums); the loads of four
+              // segments are issued together so their latencies overlap
+              for (int sg0 = 0; sg0 < s.nsegs; sg0 += 4) {
+                float4 v[4][4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const float4 x = __ldcg(src + j);
-                  acc[4 * j] += x.x;
-                  acc[4 * j + 1] += x.y;
-                  acc[4 * j + 2] += x.z;
-                  acc[4 * j + 3] += x.w;
+                for (int u = 0; u < 4; ++u) {
+                  const int sg = sg0 + u;
+                  if (sg < s.nsegs) {
+                    const float *slice = a.ws + ((size_t)(c0 + sg) * 2 + (sg == 0 ? 1 : 0)) * ((size_t)TN * BM);
+                    const float4 *src = reinterpret_cast<const float4 *>(slice + (size_t)tl * BM + part * 16);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) v[u][j] = __ldcg(src + j);
+                  }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  if (sg0 + u < s.nsegs) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                      acc[4 * j] += v[u][j].x;
+                      acc[4 * j + 1] += v[u][j].y;
+                      acc[4 * j + 2] += v[u][j].z;
+                      acc[4 * j + 3] += v[u][j].w;
+                    }
+                  }
                 }
               }
             }
@@ -512,12 +533,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar(1, kEpiThreads);  // last_flag is rewritten by the next segment
       }
     }
+    if (a.trace && et == 0) {
+      const unsigned long long te = ptx::globaltimer_ns();
+      a.trace[c * 4 + 1] += te & 0xffffffffull;  // epilogue done (low 32 bits)
+      *reinterpret_cast<volatile unsigned long long *>(slab) = te;
+    }
     if (EPI == kEpiAllReduce) reduce_owned_chunks<TN>(p, c, et);
   }
 
+  // the producer and MMA warps ran their role on one elected lane: reconverge
+  // each warp before the CTA-wide barrier (bar.sync is warp-aligned)
+  __syncwarp();
   ptx::tc_fence_before();
   __syncthreads();
+  if (a.trace && threadIdx.x == 0) {
+    const unsigned long long te = *reinterpret_cast<volatile unsigned long long *>(slab);
+    const unsigned long long tp = ptx::globaltimer_ns();
+    a.trace[c * 4 + 2] = tp;
+    if (te > tp) a.trace[c * 4 + 0] = 0;  // marks a barrier that did not order the epilogue
+  }
   if (warp == 0) ptx::tmem_dealloc(tmem, C::TMEM_COLS);
+  if (a.trace && threadIdx.x == 0) a.trace[c * 4 + 3] = ptx::globaltimer_ns();
 }
 
 template <int TN, int EPI>
@@ -533,25 +569,41 @@ static void launch_tn(const CUtensorMap &tw, const CUtensorMap &tx, const Params
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.dynamicSmemBytes = C::smem(p.stages);
   cfg.stream = stream;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
 }
 
+// Ring depth: the deepest that fits, unless SCHED_GEMM_SMEM_KB caps the
+// shared memory of a CTA (a smaller CTA lets the next kernel's CTA become
+// resident beside it and start its weight prefetch during this one's tail).
+template <int TN>
+static int stages_for() {
+  using C = Cfg<TN>;
+  static const int cap_kb = [] {
+    const char *v = std::getenv("SCHED_GEMM_SMEM_KB");
+    return v ? std::atoi(v) : 0;
+  }();
+  if (cap_kb <= 0) return C::STAGES;
+  int s = C::STAGES;
+  while (s > 2 && C::smem(s) > cap_kb * 1024) --s;
+  return s;
+}
+
 template <int EPI>
-static void dispatch(int tn, const CUtensorMap &tw, const CUtensorMap &tx, const Params &p,
+static void dispatch(int tn, const CUtensorMap &tw, const CUtensorMap &tx, Params p,
                      cudaStream_t stream) {
   switch (tn) {
-    case 16: launch_tn<16, EPI>(tw, tx, p, stream); break;
-    case 32: launch_tn<32, EPI>(tw, tx, p, stream); break;
-    case 64: launch_tn<64, EPI>(tw, tx, p, stream); break;
-    case 128: launch_tn<128, EPI>(tw, tx, p, stream); break;
-    default: launch_tn<256, EPI>(tw, tx, p, stream); break;
+    case 16: p.stages = stages_for<16>(); launch_tn<16, EPI>(tw, tx, p, stream); break;
+    case 32: p.stages = stages_for<32>(); launch_tn<32, EPI>(tw, tx, p, stream); break;
+    case 64: p.stages = stages_for<64>(); launch_tn<64, EPI>(tw, tx, p, stream); break;
+    case 128: p.stages = stages_for<128>(); launch_tn<128, EPI>(tw, tx, p, stream); break;
+    default: p.stages = stages_for<256>(); launch_tn<256, EPI>(tw, tx, p, stream); break;
   }
 }
 
@@ -605,6 +657,7 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   int tn;
   p.a = a;
   gemm::plan(a, p, tn);
+
   if (gemm::splits_tiles(p)) {
     if (a.ws == nullptr || a.counters == nullptr) return -2;
     const long long need = (long long)p.grid * 2 * tn * gemm::BM;

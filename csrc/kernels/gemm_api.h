@@ -43,6 +43,9 @@ struct GemmArgs {
   int rank, world;
   __nv_bfloat16 *recv[kMaxWorld];
   uint32_t *flags[kMaxWorld];
+  // optional per-CTA %globaltimer trace [grid][4]: entry, producer past the
+  // dependency wait, last TMA issued, CTA done (nullptr: off)
+  unsigned long long *trace;
 };
 
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream);

@@ -45,39 +45,41 @@ constexpr int kMaxTopK = 8;
 constexpr int QB = 128;  // quantisation block (columns)
 
 // ---------------------------------------------------------------- routing
-// One warp per token: logits over E experts (bf16 router weight [E, H]),
-// top-k by value, weights = softmax over the selected logits (Mixtral).
+// One CTA per token, one warp per expert: logits over E experts (bf16 router
+// weight [E, H]), top-k by value, weights = softmax over the selected logits
+// (Mixtral). Every warp's loads are independent, so the dot products overlap.
 __global__ void router_topk_kernel(const __nv_bfloat16 *__restrict__ x, const __nv_bfloat16 *__restrict__ wr,
                                    int T, int H, int E, int K, int32_t *__restrict__ ids,
                                    float *__restrict__ wts) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
-  if (warp >= T) return;
+  __shared__ float logit[32];
+  const int t = blockIdx.x, e = threadIdx.x / 32, lane = threadIdx.x % 32;
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
-  float logit[32];
-  const __nv_bfloat16 *row = x + (size_t)warp * H;
-  for (int e = 0; e < E; ++e) {
-    float s = 0.f;
-    for (int c = lane * 8; c < H; c += 256) {
-      const uint4 a = *reinterpret_cast<const uint4 *>(row + c);
-      const uint4 b = *reinterpret_cast<const uint4 *>(wr + (size_t)e * H + c);
-      const __nv_bfloat16 *ae = reinterpret_cast<const __nv_bfloat16 *>(&a);
-      const __nv_bfloat16 *be = reinterpret_cast<const __nv_bfloat16 *>(&b);
+  const __nv_bfloat16 *row = x + (size_t)t * H;
+  const __nv_bfloat16 *w = wr + (size_t)e * H;
+  float s = 0.f;
+#pragma unroll 4
+  for (int c = lane * 8; c < H; c += 256) {
+    const uint4 a = *reinterpret_cast<const uint4 *>(row + c);
+    const uint4 b = __ldg(reinterpret_cast<const uint4 *>(w + c));
+    const __nv_bfloat16 *ae = reinterpret_cast<const __nv_bfloat16 *>(&a);
+    const __nv_bfloat16 *be = reinterpret_cast<const __nv_bfloat16 *>(&b);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s += __bfloat162float(ae[j]) * __bfloat162float(be[j]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    logit[e] = s;
+    for (int j = 0; j < 8; ++j) s += __bfloat162float(ae[j]) * __bfloat162float(be[j]);
   }
-  if (lane == 0) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) logit[e] = s;
+  __syncwarp();
+  __syncthreads();
+  if (threadIdx.x == 0) {
     int sel[kMaxTopK];
     float val[kMaxTopK];
     unsigned used = 0;
     for (int k = 0; k < K; ++k) {
       int best = -1;
-      for (int e = 0; e < E; ++e)
-        if (!(used >> e & 1u) && (best < 0 || logit[e] > logit[best])) best = e;
+      for (int j = 0; j < E; ++j)
+        if (!(used >> j & 1u) && (best < 0 || logit[j] > logit[best])) best = j;
       used |= 1u << best;
       sel[k] = best;
       val[k] = logit[best];
@@ -85,44 +87,36 @@ __global__ void router_topk_kernel(const __nv_bfloat16 *__restrict__ x, const __
     float m = val[0], den = 0.f;
     for (int k = 0; k < K; ++k) den += __expf(val[k] - m);
     for (int k = 0; k < K; ++k) {
-      ids[warp * K + k] = sel[k];
-      wts[warp * K + k] = __expf(val[k] - m) / den;
+      ids[t * K + k] = sel[k];
+      wts[t * K + k] = __expf(val[k] - m) / den;
     }
   }
 }
 
 // ---------------------------------------------------------------- dispatch
-// One CTA (128 threads) per (token, k).
+// One CTA (128 threads) per token: its K slots are claimed in parallel, the
+// row is quantised once (one fp32 scale per 128 columns) and stored to every
+// destination slab.
 __global__ void __launch_bounds__(128) dispatch_kernel(const DispatchArgs a) {
-  const int t = blockIdx.x / a.K, k = blockIdx.x % a.K;
-  __shared__ int slot_s;
+  const int t = blockIdx.x;
+  __shared__ int slot_s[kMaxTopK];
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
-  if (t >= a.T) goto announce;  // a rank with no tokens still announces completion
-  {
-  const int e = a.ids[t * a.K + k];
-  const int owner = e / a.E_local, le = e % a.E_local;
-  if (threadIdx.x == 0) {
-    const uint32_t s = atomicAdd_system(a.counter[owner] + le, 1u);
-    slot_s = (int)s < a.capacity ? (int)s : -1;
-    if (slot_s < 0) {
-      atomicAdd(a.dropped_step, 1u);
-      if (a.dropped_total) atomicAdd(a.dropped_total, 1u);
+  if (t < a.T) {
+    if (threadIdx.x < a.K) {
+      const int k = threadIdx.x;
+      const int e = a.ids[t * a.K + k];
+      const int owner = e / a.E_local, le = e % a.E_local;
+      const uint32_t s = atomicAdd_system(a.counter[owner] + le, 1u);
+      slot_s[k] = (int)s < a.capacity ? (int)s : -1;
+      if (slot_s[k] < 0) {
+        atomicAdd(a.dropped_step, 1u);
+        if (a.dropped_total) atomicAdd(a.dropped_total, 1u);
+      }
     }
-  }
-  __syncthreads();
-  const int slot = slot_s;
-  if (slot < 0) {
-    // dropped by the capacity cap: its combine row contributes zero
-    __nv_bfloat16 *c = a.combine_local + ((size_t)t * a.K + k) * a.H;
-    for (int col = threadIdx.x * 8; col < a.H; col += 128 * 8)
-      *reinterpret_cast<uint4 *>(c + col) = make_uint4(0, 0, 0, 0);
-  } else {
-    const size_t row = (size_t)le * a.rows_per_expert + slot;
+    __syncwarp();
+    __syncthreads();
     const __nv_bfloat16 *src = a.x + (size_t)t * a.H;
-    uint8_t *dst = a.slab[owner] + row * a.H;
-    float *dscale = a.slab_scale[owner] + row * (a.H / QB);
-    // each warp quantises 128-column blocks: amax -> scale -> e4m3
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     for (int blk = warp; blk < a.H / QB; blk += 4) {
       const uint2 u = *reinterpret_cast<const uint2 *>(src + blk * QB + lane * 4);
@@ -143,42 +137,122 @@ __global__ void __launch_bounds__(128) dispatch_kernel(const DispatchArgs a) {
         const __nv_fp8_e4m3 q(f[j] * inv);
         packed |= (uint32_t)(*reinterpret_cast<const uint8_t *>(&q)) << (8 * j);
       }
-      *reinterpret_cast<uint32_t *>(dst + blk * QB + lane * 4) = packed;
-      if (lane == 0) dscale[blk] = scale;
+      for (int k = 0; k < a.K; ++k) {
+        const int slot = slot_s[k];
+        if (slot < 0) continue;
+        const int e = a.ids[t * a.K + k];
+        const int owner = e / a.E_local, le = e % a.E_local;
+        const size_t row = (size_t)le * a.rows_per_expert + slot;
+        *reinterpret_cast<uint32_t *>(a.slab[owner] + row * a.H + blk * QB + lane * 4) = packed;
+        if (lane == 0) a.slab_scale[owner][(size_t)blk * a.E_local * a.rows_per_expert + row] = scale;
+      }
     }
-    if (threadIdx.x == 0) {
-      int4 meta = make_int4(a.rank, t, k, __float_as_int(a.wts[t * a.K + k]));
-      *reinterpret_cast<int4 *>(a.slab_meta[owner] + row * 4) = meta;
+    if (threadIdx.x < a.K) {
+      const int k = threadIdx.x;
+      const int e = a.ids[t * a.K + k];
+      const int owner = e / a.E_local, le = e % a.E_local;
+      if (slot_s[k] >= 0) {
+        const size_t row = (size_t)le * a.rows_per_expert + slot_s[k];
+        *reinterpret_cast<int4 *>(a.slab_meta[owner] + row * 4) =
+            make_int4(a.rank, t, k, __float_as_int(a.wts[t * a.K + k]));
+      }
+    }
+    // dropped assignments contribute zero rows to the local combine buffer
+    for (int k = 0; k < a.K; ++k) {
+      if (slot_s[k] >= 0) continue;
+      __nv_bfloat16 *c = a.combine_local + ((size_t)t * a.K + k) * a.H;
+      for (int col = threadIdx.x * 8; col < a.H; col += 128 * 8)
+        *reinterpret_cast<uint4 *>(c + col) = make_uint4(0, 0, 0, 0);
     }
   }
-  }
-announce:
   // the last dispatch CTA of this rank announces completion to every owner
-  __threadfence_system();
+  // (a rank with no tokens launches one CTA that only announces)
+  ptx::fence_acq_rel_sys();
+  __syncwarp();
   __syncthreads();
   if (threadIdx.x == 0) {
     const uint32_t fin = atomicAdd(a.local_done, 1u);
     if (fin == gridDim.x - 1) {
       *a.local_done = 0u;
-      __threadfence_system();
+      ptx::fence_acq_rel_sys();
       for (int r = 0; r < a.world; ++r) atomicAdd_system(a.done[r], 1u);
     }
   }
 }
 
 // ---------------------------------------------------------------- fp8 expert GEMM
+// Persistent stream-K over the ACTIVE tiles only. How many rows each expert
+// received is known on the device alone, so every CTA derives the same
+// schedule from the row counts: tiles (expert, n-tile, token-tile) with
+// token tiles fastest (CTAs running together share each weight tile through
+// L2), units = tiles x K-blocks split evenly over the grid. A tile cut
+// between CTAs is reduced by its last-arriving CTA from per-CTA fp32 slices
+// in a fixed order (deterministic), exactly like the dense GEMM.
 constexpr int BM = 128;
 constexpr int BK = 128;  // fp8 elements per stage = 128 bytes
 constexpr int TN = 64;   // rows (tokens) per tile
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, each on half of the tokens
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;
+constexpr int HALF = TN / 2;
+constexpr int NP = 8;  // TMEM partial buffers (per-K-block MMA results)
 constexpr int W_BYTES = BM * BK;
 constexpr int X_BYTES = TN * BK;
 constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
 constexpr int STAGES = 8;
-constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 512;
+constexpr int UP_PITCH = TN + 1;                // [64 up rows][TN tokens] fp32, conflict-free
+constexpr int UP_BYTES = (BM / 2) * UP_PITCH * 4;
+constexpr int kMaxExperts = 32;
+constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + UP_BYTES + 1024;
+
+struct Sched {
+  int tprefix[kMaxExperts + 1];  // active-tile prefix over experts
+  int ttc[kMaxExperts];          // token tiles of each expert
+  int rows[kMaxExperts];
+  long long units;
+  int kb;
+};
+
+struct Seg {
+  int tile, kb0, kb1, seg, nsegs;
+};
+
+// Units go to the first G = min(grid, units) CTAs, so every one of them gets
+// at least one unit and a tile's segments are exactly CTAs c0..c1.
+__device__ __forceinline__ long long eff_grid(const Sched &s) {
+  return s.units < (long long)gridDim.x ? s.units : (long long)gridDim.x;
+}
+__device__ __forceinline__ long long unit_begin(const Sched &s, int c) {
+  const long long G = eff_grid(s);
+  return c >= G ? s.units : (long long)c * s.units / G;
+}
+__device__ __forceinline__ int cta_of_unit(const Sched &s, long long u) {
+  return (int)(((u + 1) * eff_grid(s) - 1) / s.units);
+}
+__device__ __forceinline__ bool segment(const Sched &s, int c, int k, Seg &g) {
+  const long long b = unit_begin(s, c), e = unit_begin(s, c + 1);
+  if (b >= e) return false;
+  const int tile = (int)(b / s.kb) + k;
+  const long long tb = (long long)tile * s.kb, te = tb + s.kb;
+  if (tb >= e) return false;
+  g.tile = tile;
+  g.kb0 = (int)(max(b, tb) - tb);
+  g.kb1 = (int)(min(e, te) - tb);
+  const int c0 = cta_of_unit(s, tb), c1 = cta_of_unit(s, te - 1);
+  g.seg = c - c0;
+  g.nsegs = c1 - c0 + 1;
+  return true;
+}
+__device__ __forceinline__ void tile_coords(const Sched &s, int E_local, int tile, int &ex, int &nt, int &tt) {
+  ex = 0;
+  while (ex + 1 < E_local && tile >= s.tprefix[ex + 1]) ++ex;
+  const int j = tile - s.tprefix[ex];
+  nt = j / s.ttc[ex];
+  tt = j % s.ttc[ex];
+}
 
 // gate/up: the last CTA publishes the row counts for the down GEMM and
-// clears the receive counters (every CTA has read its rows by now).
+// clears the receive counters (every CTA read them at its start).
 __device__ __forceinline__ void finish_gate_up(const ExpertArgs &a) {
   __threadfence();
   const uint32_t fin = atomicAdd(a.tiles_done, 1u);
@@ -199,47 +273,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const ExpertArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *bars = reinterpret_cast<uint64_t *>(base + STAGES * STAGE_BYTES);
-  uint64_t *full = bars, *empty = bars + STAGES, *p_full = bars + 2 * STAGES, *p_empty = bars + 2 * STAGES + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
-  int *valid_s = reinterpret_cast<int *>(tmem_slot + 1);
+  float *up_sm = reinterpret_cast<float *>(base + STAGES * STAGE_BYTES);  // [64][UP_PITCH]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(up_sm + (BM / 2) * UP_PITCH);
+  uint64_t *full = bars, *empty = bars + STAGES;
+  uint64_t *p_full = bars + 2 * STAGES, *p_empty = bars + 2 * STAGES + NP;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 2 * NP);
+  volatile int *last_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  __shared__ Sched sch;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // n-tiles fastest, token tiles next: the (usually few) valid token tiles
-  // occupy the first CTAs; the rest exit right after the row-count check
-  int tile = blockIdx.x;
-  const int nt = tile % a.n_tiles;
-  tile /= a.n_tiles;
-  const int tt = tile % a.t_tiles;
-  const int ex = tile / a.t_tiles;
-  const int kb_total = a.K / BK;
+  const int c = blockIdx.x;
+  const size_t x_rows = (size_t)a.E_local * a.rows_per_expert;  // x_scale is [K / 128][x_rows]
 
   ptx::pdl_launch_dependents();
-  // rows of this expert: gate/up waits for every source's dispatch first
-  if (threadIdx.x == 0) {
-    ptx::pdl_wait();
-    int rows;
-    if (EPI == kExpSwiGLU) {
-      bool ok = ptx::ld_acquire_sys(a.done) >= (uint32_t)a.world;
-      if (!ok) {
-        const uint64_t t0 = ptx::globaltimer_ns();
-        while (!ok && ptx::globaltimer_ns() - t0 < kWaitBudgetNs) ok = ptx::ld_acquire_sys(a.done) >= (uint32_t)a.world;
-        if (!ok) report_status(a.status, kStatusPeerTimeout);
-      }
-      rows = min((int)ptx::ld_acquire_sys(a.counter + ex), a.capacity);
-    } else {
-      rows = (int)__ldcg(a.rows_valid + ex);
-    }
-    *valid_s = rows;
-  }
-  __syncthreads();
-  const int valid = *valid_s;
-  const bool active = tt * TN < valid;
-  if (!active) {
-    if (EPI == kExpSwiGLU && threadIdx.x == 0) finish_gate_up(a);
-    return;
-  }
   if (warp == 0) {
-    ptx::tmem_alloc(tmem_slot, 2 * TN);
+    ptx::tmem_alloc(tmem_slot, NP * TN);
     ptx::tmem_relinquish();
   }
   if (threadIdx.x == 32) {
@@ -247,9 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NP; ++i) {
       ptx::mbar_init(&p_full[i], 1);
-      ptx::mbar_init(&p_empty[i], 128);
+      ptx::mbar_init(&p_empty[i], kEpiThreads);
     }
     ptx::fence_mbar_init();
   }
@@ -257,130 +304,213 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tmap(&tmW);
     ptx::prefetch_tmap(&tmX);
   }
+  // the schedule: rows per expert (gate/up waits for every source first)
+  if (threadIdx.x == 0) {
+    if (a.trace) a.trace[c * 4] = ptx::globaltimer_ns();
+    ptx::pdl_wait();
+    if (EPI == kExpSwiGLU) {
+      bool ok = ptx::ld_acquire_sys(a.done) >= (uint32_t)a.world;
+      if (!ok) {
+        const uint64_t t0 = ptx::globaltimer_ns();
+        while (!ok && ptx::globaltimer_ns() - t0 < kWaitBudgetNs) ok = ptx::ld_acquire_sys(a.done) >= (uint32_t)a.world;
+        if (!ok) report_status(a.status, kStatusPeerTimeout);
+      }
+    }
+    int acc = 0;
+    for (int e = 0; e < a.E_local; ++e) {
+      const uint32_t n = EPI == kExpSwiGLU ? ptx::ld_acquire_sys(a.counter + e) : __ldcg(a.rows_valid + e);
+      const int rows = min(min((int)n, a.capacity), a.rows_per_expert);
+      sch.rows[e] = rows;
+      sch.ttc[e] = (rows + TN - 1) / TN;
+      sch.tprefix[e] = acc;
+      acc += sch.ttc[e] * a.n_tiles;
+    }
+    sch.tprefix[a.E_local] = acc;
+    sch.kb = a.K / BK;
+    sch.units = (long long)acc * sch.kb;
+  }
   ptx::tc_fence_before();
+  __syncwarp();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (a.trace && threadIdx.x == 0) a.trace[c * 4 + 1] = ptx::globaltimer_ns();
 
-  if (active && warp == 0) {
+  if (sch.units > 0 && warp == 0) {
+    // ============================================================ producer
     if (ptx::elect_one()) {
-      // the slab rows arrived through peers' generic stores; TMA reads them
+      // slab rows arrived through peers' generic stores; TMA reads them
       ptx::fence_proxy_async_global();
-      for (int kb = 0; kb < kb_total; ++kb) {
-        const int s = kb % STAGES;
-        if (!ptx::mbar_wait(&empty[s], ((kb / STAGES) & 1) ^ 1)) {
-          report_status(a.status, kStatusMmaTimeout);
-          break;
+      Seg g;
+      int i = 0;
+      bool ok = true;
+      for (int k = 0; ok && segment(sch, c, k, g); ++k) {
+        int ex, nt, tt;
+        tile_coords(sch, a.E_local, g.tile, ex, nt, tt);
+        for (int kb = g.kb0; kb < g.kb1; ++kb, ++i) {
+          const int st = i % STAGES;
+          if (!ptx::mbar_wait(&empty[st], ((i / STAGES) & 1) ^ 1)) {
+            report_status(a.status, kStatusMmaTimeout);
+            ok = false;
+            break;
+          }
+          uint8_t *sm = base + st * STAGE_BYTES;
+          ptx::mbar_arrive_expect_tx(&full[st], STAGE_BYTES);
+          ptx::tma_load_2d(sm, &tmW, &full[st], kb * BK, ex * a.N + nt * BM);
+          ptx::tma_load_2d(sm + W_BYTES, &tmX, &full[st], kb * BK, ex * a.rows_per_expert + tt * TN);
         }
-        uint8_t *st = base + s * STAGE_BYTES;
-        ptx::mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-        ptx::tma_load_2d(st, &tmW, &full[s], kb * BK, ex * a.N + nt * BM);
-        ptx::tma_load_2d(st + W_BYTES, &tmX, &full[s], kb * BK, ex * a.rows_per_expert + tt * TN);
       }
+      if (a.trace) a.trace[c * 4 + 2] = ptx::globaltimer_ns();
     }
-  } else if (active && warp == 1) {
+  } else if (sch.units > 0 && warp == 1) {
+    // ============================================================ MMA
     if (ptx::elect_one()) {
       constexpr uint32_t idesc = ptx::idesc_e4m3(BM, TN);
-      for (int kb = 0; kb < kb_total; ++kb) {
-        const int s = kb % STAGES, pb = kb & 1;
-        if (!ptx::mbar_wait(&full[s], (kb / STAGES) & 1) ||
-            !ptx::mbar_wait(&p_empty[pb], ((kb >> 1) & 1) ^ 1)) {
-          report_status(a.status, kStatusTmaTimeout);
-          break;
+      Seg g;
+      int i = 0;
+      bool ok = true;
+      for (int k = 0; ok && segment(sch, c, k, g); ++k) {
+        for (int kb = g.kb0; kb < g.kb1; ++kb, ++i) {
+          const int st = i % STAGES, pb = i % NP;
+          if (!ptx::mbar_wait(&full[st], (i / STAGES) & 1) ||
+              !ptx::mbar_wait(&p_empty[pb], ((i / NP) & 1) ^ 1)) {
+            report_status(a.status, kStatusTmaTimeout);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          uint8_t *sm = base + st * STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            const uint64_t da = ptx::smem_desc(sm + kk * 32, 16, 1024, ptx::kLayoutSW128);
+            const uint64_t db = ptx::smem_desc(sm + W_BYTES + kk * 32, 16, 1024, ptx::kLayoutSW128);
+            ptx::mma_f8_ss(tmem + pb * TN, da, db, idesc, kk > 0 ? 1u : 0u);
+          }
+          ptx::mma_commit(&empty[st]);
+          ptx::mma_commit(&p_full[pb]);
+        }
+      }
+    }
+  } else if (sch.units > 0 && warp >= 2) {
+    // ============================================================ promotion + epilogue
+    // acc[t] += partial[row][t] * s_w[kb] * s_x[kb][t]; warp pair (q, half)
+    // covers TMEM lanes 32q.. and token columns half*32..
+    const int q = warp & 3, hf = (warp - 2) / 4, row = q * 32 + lane, et = threadIdx.x - 64;
+    Seg g;
+    int i = 0;
+    bool ok = true;
+    for (int k = 0; segment(sch, c, k, g); ++k) {
+      int ex, nt, tt;
+      tile_coords(sch, a.E_local, g.tile, ex, nt, tt);
+      const int r0 = ex * a.rows_per_expert + tt * TN;
+      const float *sw = a.w_scale + ((size_t)ex * a.n_tiles + nt) * sch.kb;
+      float acc[HALF];
+#pragma unroll
+      for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
+      for (int kb = g.kb0; kb < g.kb1; ++kb, ++i) {
+        const int pb = i % NP;
+        // this K-block's activation scales of our 32 tokens (warp-uniform: broadcast loads)
+        const float4 *xs4 = reinterpret_cast<const float4 *>(a.x_scale + (size_t)kb * x_rows + r0 + hf * HALF);
+        float s[HALF];
+        const float swk = __ldg(sw + kb);
+#pragma unroll
+        for (int j = 0; j < HALF / 4; ++j) {
+          const float4 v = __ldg(xs4 + j);
+          s[4 * j] = v.x * swk;
+          s[4 * j + 1] = v.y * swk;
+          s[4 * j + 2] = v.z * swk;
+          s[4 * j + 3] = v.w * swk;
+        }
+        if (ok && !ptx::mbar_wait(&p_full[pb], (i / NP) & 1)) {
+          report_status(a.status, kStatusEpilogueTimeout);
+          ok = false;
         }
         ptx::tc_fence_after();
-        uint8_t *st = base + s * STAGE_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BK / 32; ++kk) {
-          const uint64_t da = ptx::smem_desc(st + kk * 32, 16, 1024, ptx::kLayoutSW128);
-          const uint64_t db = ptx::smem_desc(st + W_BYTES + kk * 32, 16, 1024, ptx::kLayoutSW128);
-          ptx::mma_f8_ss(tmem + pb * TN, da, db, idesc, kk > 0 ? 1u : 0u);
-        }
-        ptx::mma_commit(&empty[s]);
-        ptx::mma_commit(&p_full[pb]);
-      }
-    }
-  } else if (active && warp >= 2) {
-    // promotion: acc[t] += partial[row][t] * s_w[kb] * s_x[t][kb]
-    const int q = warp & 3, row = q * 32 + lane;
-    float acc[TN];
-#pragma unroll
-    for (int j = 0; j < TN; ++j) acc[j] = 0.f;
-    const float *sw = a.w_scale + ((size_t)ex * a.n_tiles + nt) * kb_total;
-    const int r0 = ex * a.rows_per_expert + tt * TN;
-    bool ok = true;
-    for (int kb = 0; kb < kb_total && ok; ++kb) {
-      const int pb = kb & 1;
-      if (!ptx::mbar_wait(&p_full[pb], (kb >> 1) & 1)) {
-        report_status(a.status, kStatusEpilogueTimeout);
-        ok = false;
-        break;
-      }
-      ptx::tc_fence_after();
-      const float swk = __ldg(sw + kb);
-#pragma unroll
-      for (int c = 0; c < TN / 16; ++c) {
-        uint32_t r[16];
-        ptx::tmem_ld16(tmem + pb * TN + ((uint32_t)(q * 32) << 16) + c * 16, r);
+        uint32_t r0v[16], r1v[16];
+        const uint32_t taddr = tmem + pb * TN + hf * HALF + ((uint32_t)(q * 32) << 16);
+        ptx::tmem_ld16(taddr, r0v);
+        ptx::tmem_ld16(taddr + 16, r1v);
         ptx::tmem_ld_wait();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&p_empty[pb]);
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          acc[c * 16 + j] += __uint_as_float(r[j]) * swk * __ldg(a.x_scale + (size_t)(r0 + c * 16 + j) * a.ex_ld + kb);
+        for (int j = 0; j < 16; ++j) {
+          acc[j] = fmaf(__uint_as_float(r0v[j]), s[j], acc[j]);
+          acc[16 + j] = fmaf(__uint_as_float(r1v[j]), s[16 + j], acc[16 + j]);
+        }
       }
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(&p_empty[pb]);
-    }
-    // stage the tile through shared memory (reusing the ring) for row-wise writes
-    __syncwarp();
-    float *tile_sm = reinterpret_cast<float *>(base);  // [TN][BM + 4]
-    named_bar(1, 128);  // the ring is idle: every MMA has been consumed
+      if (!ok) {
 #pragma unroll
-    for (int j = 0; j < TN; ++j) tile_sm[j * (BM + 4) + row] = acc[j];
-    named_bar(1, 128);
-    const int et = threadIdx.x - 64;
-    if (EPI == kExpSwiGLU) {
-      // 64 gate rows + their 64 up rows -> 64 act columns per token
-      for (int idx = et; idx < TN * 8; idx += 128) {
-        const int tj = idx / 8, c = (idx % 8) * 8;
-        if (tt * TN + tj >= valid) continue;
-        const float *v = tile_sm + tj * (BM + 4);
-        uint4 o;
-        o.x = pack_bf16x2(silu(v[c]) * v[c + 64], silu(v[c + 1]) * v[c + 65]);
-        o.y = pack_bf16x2(silu(v[c + 2]) * v[c + 66], silu(v[c + 3]) * v[c + 67]);
-        o.z = pack_bf16x2(silu(v[c + 4]) * v[c + 68], silu(v[c + 5]) * v[c + 69]);
-        o.w = pack_bf16x2(silu(v[c + 6]) * v[c + 70], silu(v[c + 7]) * v[c + 71]);
-        *reinterpret_cast<uint4 *>(a.act + (size_t)(r0 + tj) * (a.N / 2) + nt * 64 + c) = o;
+        for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
       }
-    } else {
-      // combine: row (weighted) back to its source over NVLink
-      for (int idx = et; idx < TN * 16; idx += 128) {
-        const int tj = idx / 16, c = (idx % 16) * 8;
-        if (tt * TN + tj >= valid) continue;
-        const int4 m = *reinterpret_cast<const int4 *>(a.meta + (size_t)(r0 + tj) * 4);
-        const float w = __int_as_float(m.w);
-        const float *v = tile_sm + tj * (BM + 4);
-        uint4 o;
-        o.x = pack_bf16x2(v[c] * w, v[c + 1] * w);
-        o.y = pack_bf16x2(v[c + 2] * w, v[c + 3] * w);
-        o.z = pack_bf16x2(v[c + 4] * w, v[c + 5] * w);
-        o.w = pack_bf16x2(v[c + 6] * w, v[c + 7] * w);
-        __nv_bfloat16 *dst = a.combine[m.x] + ((size_t)m.y * a.k_top + m.z) * a.N + nt * BM + c;
-        *reinterpret_cast<uint4 *>(dst) = o;
+      if (g.nsegs > 1) {
+        // two partial slots per CTA: 1 for the segment that opens its tile,
+        // 0 for a continuation
+        float *wsl = a.ws + ((size_t)c * 2 + (g.seg == 0 ? 1 : 0)) * ((size_t)TN * BM);
+#pragma unroll
+        for (int j = 0; j < HALF; ++j) __stcg(wsl + (hf * HALF + j) * BM + row, acc[j]);
+        __threadfence();
+        named_bar(1, kEpiThreads);
+        if (et == 0) *last_flag = atomicAdd(&a.tile_counters[g.tile], 1u) == (uint32_t)(g.nsegs - 1) ? 1 : 0;
+        named_bar(1, kEpiThreads);
+        const bool last = *last_flag;
+        if (!last) continue;  // uniform across the epilogue threads
+        __threadfence();
+        const int c0 = c - g.seg;
+#pragma unroll
+        for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
+        for (int sg = 0; sg < g.nsegs; ++sg) {  // fixed order: deterministic sums
+          const float *sl = a.ws + ((size_t)(c0 + sg) * 2 + (sg == 0 ? 1 : 0)) * ((size_t)TN * BM);
+#pragma unroll
+          for (int j = 0; j < HALF; ++j) acc[j] += __ldcg(sl + (hf * HALF + j) * BM + row);
+        }
+        if (et == 0) a.tile_counters[g.tile] = 0u;
       }
-      __threadfence_system();
-      named_bar(1, 128);
-      // one count per (row, n-tile) pushed: the source expects N/128 per row
-      for (int tj = et; tj < TN; tj += 128) {
-        if (tt * TN + tj >= valid) continue;
-        const int src = a.meta[(size_t)(r0 + tj) * 4];
-        atomicAdd_system(a.combine_cnt[src], 1u);
+      // outputs straight from the accumulators: thread (row, half) holds
+      // output feature `row` of its 32 tokens
+      const int valid = sch.rows[ex] - tt * TN;
+      if (EPI == kExpSwiGLU) {
+        // gate rows 0..63 pair with up rows 64..127 (held by quarters 2, 3)
+        if (q >= 2) {
+#pragma unroll
+          for (int j = 0; j < HALF; ++j) up_sm[(row - 64) * UP_PITCH + hf * HALF + j] = acc[j];
+        }
+        named_bar(1, kEpiThreads);
+        if (q < 2) {
+          __nv_bfloat16 *dst = a.act + (size_t)r0 * (a.N / 2) + nt * 64 + row;
+#pragma unroll
+          for (int j = 0; j < HALF; ++j) {
+            const int tok = hf * HALF + j;
+            if (tok < valid) dst[(size_t)tok * (a.N / 2)] = __float2bfloat16(silu(acc[j]) * up_sm[row * UP_PITCH + tok]);
+          }
+        }
+      } else {
+        // combine: each weighted row goes back to its source over NVLink
+#pragma unroll
+        for (int j = 0; j < HALF; ++j) {
+          const int tok = hf * HALF + j;
+          if (tok >= valid) continue;
+          const int4 m = *reinterpret_cast<const int4 *>(a.meta + (size_t)(r0 + tok) * 4);
+          a.combine[m.x][((size_t)m.y * a.k_top + m.z) * a.N + nt * BM + row] =
+              __float2bfloat16(acc[j] * __int_as_float(m.w));
+        }
+        __threadfence_system();
+        named_bar(1, kEpiThreads);
+        // one count per (row, n-tile): the source expects N / 128 per row
+        if (et < TN && et < valid) {
+          const int src = a.meta[(size_t)(r0 + et) * 4];
+          atomicAdd_system(a.combine_cnt[src], 1u);
+        }
       }
+      named_bar(1, kEpiThreads);  // up_sm is rewritten by the next tile
     }
   }
 
+  __syncwarp();  // reconverge the elected-lane roles before the CTA barrier
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 0) ptx::tmem_dealloc(tmem, 2 * TN);
+  if (a.trace && threadIdx.x == 0) a.trace[c * 4 + 3] = ptx::globaltimer_ns();
+  if (warp == 0) ptx::tmem_dealloc(tmem, NP * TN);
   if (EPI == kExpSwiGLU && threadIdx.x == 0) finish_gate_up(a);
 }
 
@@ -407,6 +537,7 @@ __global__ void __launch_bounds__(512) combine_norm_kernel(const __nv_bfloat16 *
       if (!ok) report_status(status, kStatusPeerTimeout);
     }
   }
+  __syncwarp();
   __syncthreads();
   float v[8];
   float ss = 0.f;
@@ -436,6 +567,7 @@ __global__ void __launch_bounds__(512) combine_norm_kernel(const __nv_bfloat16 *
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+  __syncwarp();
   __syncthreads();
   float tot = 0.f;
   for (int i = 0; i < (int)blockDim.x / 32; ++i) tot += red[i];
@@ -451,6 +583,7 @@ __global__ void __launch_bounds__(512) combine_norm_kernel(const __nv_bfloat16 *
     *reinterpret_cast<uint4 *>(y + (size_t)t * H + col) = ov;
   }
   // the last token's CTA clears the counter for the next layer
+  __syncwarp();
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -462,34 +595,71 @@ __global__ void __launch_bounds__(512) combine_norm_kernel(const __nv_bfloat16 *
   }
 }
 
-// activation quantisation for the down GEMM: bf16 [R, I] -> e4m3 + scale per 128
-__global__ void quantize_kernel(const __nv_bfloat16 *__restrict__ in, int I, uint8_t *__restrict__ out,
-                                float *__restrict__ scale, const uint32_t *rows_valid, int rows_per_expert) {
-  const int r = blockIdx.x, blk = blockIdx.y;  // one warp per (row, 128-block)
-  const int lane = threadIdx.x;
+// activation quantisation for the down GEMM: bf16 [R, I] -> e4m3 + scale per
+// 128 columns, for the valid rows of each expert only (rows_valid is known on
+// the device alone, so the grid is fixed and strides over the valid units).
+__global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__restrict__ in, int I,
+                                                       uint8_t *__restrict__ out, float *__restrict__ scale,
+                                                       const uint32_t *rows_valid, int rows_per_expert,
+                                                       int E_local) {
+  __shared__ int prefix[33];
+  const size_t R = (size_t)E_local * rows_per_expert;
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
-  const int ex = r / rows_per_expert;
-  if (r % rows_per_expert >= (int)__ldcg(rows_valid + ex)) return;
-  const uint2 u = *reinterpret_cast<const uint2 *>(in + (size_t)r * I + blk * QB + lane * 4);
-  const __nv_bfloat16 *v = reinterpret_cast<const __nv_bfloat16 *>(&u);
-  float f[4], m = 0.f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    f[j] = __bfloat162float(v[j]);
-    m = fmaxf(m, fabsf(f[j]));
+  const int nb = I / QB;
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < E_local; ++e) {
+      prefix[e] = acc;
+      acc += min((int)__ldcg(rows_valid + e), rows_per_expert) * nb;
+    }
+    prefix[E_local] = acc;
   }
+  __syncwarp();
+  __syncthreads();
+  const int total = prefix[E_local];
+  const int lane = threadIdx.x % 32;
+  const int warps = gridDim.x * (blockDim.x / 32);
+  constexpr int U = 4;  // 128-column blocks per warp step: loads first, then math
+  for (int u0 = (blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * U; u0 < total; u0 += warps * U) {
+    uint2 raw[U];
+    size_t off[U];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  const float s = m > 0.f ? m / 448.f : 1.f, inv = 1.f / s;
-  uint32_t packed = 0;
+    for (int i = 0; i < U; ++i) {
+      const int u = u0 + i;
+      off[i] = ~size_t(0);
+      if (u < total) {
+        int ex = 0;
+        while (u >= prefix[ex + 1]) ++ex;
+        const int local = u - prefix[ex];
+        const int r = ex * rows_per_expert + local / nb, blk = local % nb;
+        off[i] = (size_t)r * I + blk * QB;
+        raw[i] = *reinterpret_cast<const uint2 *>(in + off[i] + lane * 4);
+      }
+    }
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const __nv_fp8_e4m3 q(f[j] * inv);
-    packed |= (uint32_t)(*reinterpret_cast<const uint8_t *>(&q)) << (8 * j);
+    for (int i = 0; i < U; ++i) {
+      if (off[i] == ~size_t(0)) continue;
+      const __nv_bfloat16 *v = reinterpret_cast<const __nv_bfloat16 *>(&raw[i]);
+      float f[4], m = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        f[j] = __bfloat162float(v[j]);
+        m = fmaxf(m, fabsf(f[j]));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float sc = m > 0.f ? m / 448.f : 1.f, inv = 1.f / sc;
+      uint32_t packed = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_fp8_e4m3 q(f[j] * inv);
+        packed |= (uint32_t)(*reinterpret_cast<const uint8_t *>(&q)) << (8 * j);
+      }
+      *reinterpret_cast<uint32_t *>(out + off[i] + lane * 4) = packed;
+      if (lane == 0) scale[(off[i] % I) / QB * R + off[i] / I] = sc;
+    }
   }
-  *reinterpret_cast<uint32_t *>(out + (size_t)r * I + blk * QB + lane * 4) = packed;
-  if (lane == 0) scale[(size_t)r * (I / QB) + blk] = s;
 }
 
 }  // namespace moe
@@ -498,7 +668,7 @@ extern "C" int sched_moe_router(const void *x, const void *wr, int T, int H, int
                                 float *wts, cudaStream_t st) {
   if (T <= 0) return 0;
   if (E > 32 || K > moe::kMaxTopK || H % 256 != 0) return -1;
-  launch_pdl(moe::router_topk_kernel, (T + 3) / 4, 128, 0, st, static_cast<const __nv_bfloat16 *>(x),
+  launch_pdl(moe::router_topk_kernel, T, 32 * E, 0, st, static_cast<const __nv_bfloat16 *>(x),
              static_cast<const __nv_bfloat16 *>(wr), T, H, E, K, ids, wts);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
@@ -506,7 +676,8 @@ extern "C" int sched_moe_router(const void *x, const void *wr, int T, int H, int
 extern "C" int sched_moe_dispatch(const moe::DispatchArgs *a, cudaStream_t st) {
   if (a->H % moe::QB != 0 || a->world > moe::kMaxWorld || a->T < 0) return -1;
   // T == 0 still launches one CTA: every rank must announce completion
-  launch_pdl(moe::dispatch_kernel, a->T > 0 ? a->T * a->K : 1, 128, 0, st, *a);
+  if (a->K > moe::kMaxTopK) return -1;
+  launch_pdl(moe::dispatch_kernel, a->T > 0 ? a->T : 1, 128, 0, st, *a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -515,15 +686,21 @@ extern "C" int sched_moe_expert_gemm(int epi, const void *w, const void *x, cons
                                      cudaStream_t st) {
   moe::ExpertArgs a = *args;
   if (a.N % moe::BM != 0 || a.K % moe::BK != 0 || a.rows_per_expert % moe::TN != 0) return -1;
+  if (a.E_local < 1 || a.E_local > moe::kMaxExperts || a.ws == nullptr || a.tile_counters == nullptr) return -1;
   a.n_tiles = a.N / moe::BM;
   a.t_tiles = a.rows_per_expert / moe::TN;
   a.ex_ld = a.K / moe::QB;
+  int grid = a.grid;
+  if (grid <= 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&grid, cudaDevAttrMultiProcessorCount, dev);
+  }
   try {
     CUtensorMap tw = tmap::make_2d(w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.E_local * a.N, a.K, a.K,
                                    moe::BM, moe::BK, CU_TENSOR_MAP_SWIZZLE_128B);
     CUtensorMap tx = tmap::make_2d(x, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)a.E_local * a.rows_per_expert,
                                    a.K, a.K, moe::TN, moe::BK, CU_TENSOR_MAP_SWIZZLE_128B);
-    const int grid = a.E_local * a.n_tiles * a.t_tiles;
     if (epi == moe::kExpSwiGLU) {
       static bool s0 = false;
       if (!s0) {
@@ -549,8 +726,13 @@ extern "C" int sched_moe_quantize(const void *in, int R, int I, void *out, float
                                   const uint32_t *rows_valid, int rows_per_expert, cudaStream_t st) {
   if (R <= 0) return 0;
   if (I % moe::QB != 0) return -1;
-  launch_pdl(moe::quantize_kernel, dim3(R, I / moe::QB), 32, 0, st, static_cast<const __nv_bfloat16 *>(in), I,
-             static_cast<uint8_t *>(out), scale, rows_valid, rows_per_expert);
+  const int E_local = R / rows_per_expert;
+  if (E_local > 32 || R % rows_per_expert != 0) return -1;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  launch_pdl(moe::quantize_kernel, 2 * sms, 256, 0, st, static_cast<const __nv_bfloat16 *>(in), I,
+             static_cast<uint8_t *>(out), scale, rows_valid, rows_per_expert, E_local);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

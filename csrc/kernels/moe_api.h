@@ -31,7 +31,7 @@ struct DispatchArgs {
 struct ExpertArgs {
   int E_local, N, K, rows_per_expert, n_tiles, t_tiles;
   const float *w_scale;  // [E_local, N / 128, K / 128]
-  const float *x_scale;  // [E_local * rows, K / 128]
+  const float *x_scale;  // [K / 128, E_local * rows]: one row of token scales per K-block
   int ex_ld;             // x_scale row pitch (K / 128)
   // gate/up: wait for sources, then SwiGLU into act [E_local * rows, N / 2] bf16
   __nv_bfloat16 *act;
@@ -46,6 +46,14 @@ struct ExpertArgs {
   uint32_t *combine_cnt[kMaxWorld];   // every rank's received-row counter
   int k_top;
   int *status;
+  // stream-K: partial slices [grid][2][TN * 128] fp32 and per-tile arrival
+  // counters [E_local * n_tiles * t_tiles] (zero between calls)
+  float *ws;
+  uint32_t *tile_counters;
+  int grid;  // persistent CTAs (0: one per SM)
+  // optional per-CTA %globaltimer trace [grid][4]: entry, schedule known,
+  // last TMA issued, epilogue done (nullptr: off)
+  unsigned long long *trace;
 };
 
 }  // namespace moe

@@ -174,6 +174,19 @@ class Engine:
     def add_request(self, req: Request) -> None:
         self.sched.add(req)
 
+    def add_prefilled(self, req: Request, first_token: int) -> None:
+        """Admit ``req`` as if its prompt had been prefilled: its pages are
+        allocated and left with whatever the cache holds there (see
+        ``fill_kv_random``), and decoding starts from ``first_token``."""
+        self.sched.admit_cached(req, first_token, self.clock)
+
+    def fill_kv_random(self, seed: int = 0) -> None:
+        """Fill every KV page with N(0, 1) values (synthetic contexts)."""
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        for t in list(self.kv.k) + list(self.kv.v):
+            t.normal_(generator=g)
+
     def has_work(self) -> bool:
         return not self.sched.idle
 

@@ -50,6 +50,23 @@ class Scheduler:
                              f"max_context {self.max_context}")
         self.waiting.append(req)
 
+    def admit_cached(self, req: Request, first_token: int, now: float) -> None:
+        """Admit a request whose prompt K/V are already in its pages (written
+        by the caller) and whose first output token is known: it joins the
+        decode set directly. Used to start decode benchmarks from a warm
+        cache without running their prefill."""
+        if len(self.running) >= self.max_batch:
+            raise RuntimeError("decode batch is full")
+        if req.prompt_len + req.max_new_tokens > self.max_context:
+            raise ValueError(f"request {req.rid} exceeds max_context {self.max_context}")
+        if not self._grow(req, req.prompt_len):
+            raise MemoryError("no free KV pages for the cached prompt")
+        req.cached = req.prompt_len
+        req.state = State.DECODE
+        req.output.append(int(first_token))
+        req.token_times.append(now)
+        self.running.append(req)
+
     @property
     def idle(self) -> bool:
         return not self.waiting and not self.running

@@ -41,7 +41,11 @@ def mixtral_factory(ep: ExpertParallel, rank: int, world: int):
     """Engine model factory: builds expert weights for this rank and the model."""
 
     def moe_builder(layer, gen):
-        return build_moe_weights(ep.cfg, rank, world, gen, ep.device, layer)
+        # experts differ across ranks: seed from the shared stream plus the rank
+        g = torch.Generator(device=ep.device)
+        g.manual_seed(int(torch.randint(0, 2**31 - 1, (1,), generator=gen, device=gen.device).item())
+                      * 131 + rank)
+        return build_moe_weights(ep.cfg, rank, world, g, ep.device, layer)
 
     def make(cfg, weights, kv, device, tp, T, max_pos):
         return Mixtral(cfg, weights, kv, device, ep, max_tokens=T, max_pos=max_pos)

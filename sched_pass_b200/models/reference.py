@@ -131,3 +131,34 @@ def moe(x, router, w13_experts, w2_experts, top_k, block=64, quantize_x=None, qu
                 y = quantize_act(y)
             out[t] += wts[t, j] * (y @ w2_experts[e].float().t())[0]
     return out, idx, wts
+
+
+def mixtral_forward_tokens(cfg, weights, token_ids, cos_sin, experts_of, quantize=None):
+    """``llama_forward_tokens`` with the FFN replaced by top-k MoE.
+    ``experts_of(layer_weights) -> (w13 list, w2 list)`` gives fp32 expert
+    weights; ``quantize`` is applied to expert inputs and SwiGLU outputs."""
+    dev = weights.embed.device
+    ids = torch.as_tensor(token_ids, dtype=torch.long, device=dev)
+    T = ids.numel()
+    pos = torch.arange(T, device=dev)
+    h = weights.embed[ids].float()
+    D = cfg.head_dim
+    for lw in weights.layers:
+        x = rmsnorm(h, lw.ln_in, cfg.rms_eps).to(torch.bfloat16)
+        qkv = linear(x, lw.qkv)
+        hq = lw.o.shape[1] // D
+        hkv = (lw.qkv.shape[0] // D - hq) // 2
+        q = qkv[:, : hq * D].reshape(T, hq, D)
+        k = qkv[:, hq * D:(hq + hkv) * D].reshape(T, hkv, D)
+        v = qkv[:, (hq + hkv) * D:].reshape(T, hkv, D)
+        q = rope(q.to(torch.bfloat16), pos, cos_sin).to(torch.bfloat16)
+        k = rope(k.to(torch.bfloat16), pos, cos_sin).to(torch.bfloat16)
+        a = attention(q, k, v.to(torch.bfloat16), 1.0 / math.sqrt(D), causal_offset=0)
+        o = linear(a.reshape(T, -1).to(torch.bfloat16), lw.o)
+        h = (h + o.to(torch.bfloat16).float()).to(torch.bfloat16).float()
+        x = rmsnorm(h, lw.ln_post, cfg.rms_eps).to(torch.bfloat16)
+        w13, w2 = experts_of(lw)
+        d, _, _ = moe(x, lw.moe.router, w13, w2, cfg.top_k, quantize_x=quantize, quantize_act=quantize)
+        h = (h + d).to(torch.bfloat16).float()
+    x = rmsnorm(h, weights.ln_final, cfg.rms_eps).to(torch.bfloat16)
+    return linear(x[-1:], weights.lm_head)[0, : cfg.vocab]

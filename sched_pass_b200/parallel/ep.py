@@ -140,7 +140,7 @@ class ExpertParallel:
         # symmetric (peer-visible) region, one allocation carved into parts
         parts = {
             "slab": R * H,                      # fp8
-            "slab_scale": R * (H // QB) * 4,
+            "slab_scale": R * (H // QB) * 4,     # [H / 128, R]: per K-block rows of token scales
             "slab_meta": R * 4 * 4,
             "counter": max(self.E_local, 4) * 4,
             "done": 16,
@@ -163,7 +163,7 @@ class ExpertParallel:
         dev = self.device
         self.act = torch.zeros(R, I, dtype=torch.bfloat16, device=dev)
         self.act_q = torch.zeros(R, I, dtype=torch.uint8, device=dev)
-        self.act_scale = torch.zeros(R, I // QB, dtype=torch.float32, device=dev)
+        self.act_scale = torch.zeros(I // QB, R, dtype=torch.float32, device=dev)  # [I / 128, R]
         self.words = torch.zeros(64, dtype=torch.int32, device=dev)  # counters below
         base = self.words.data_ptr()
         self.rows_valid = base            # [E_local] (<= 16)
@@ -172,8 +172,24 @@ class ExpertParallel:
         self.dropped_step = base + 72
         self.dropped_total_ptr = base + 76
         self.arrivals = base + 80
+        # stream-K scratch of the expert GEMMs: two fp32 [TN, 128] slices per
+        # CTA and one arrival counter per tile (zero between calls)
+        self.grid = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.ws = torch.empty(self.grid * 2 * TN * 128, dtype=torch.float32, device=dev)
+        max_n_tiles = max(2 * I, H) // 128
+        self.tile_counters = torch.zeros(self.E_local * max_n_tiles * (self.rows // TN), dtype=torch.int32,
+                                         device=dev)
         self.ids = torch.zeros(max_tokens, K, dtype=torch.int32, device=dev)
         self.wts = torch.zeros(max_tokens, K, dtype=torch.float32, device=dev)
+
+    def enable_trace(self, on: bool = True) -> None:
+        """Record per-CTA %globaltimer stamps of the two expert GEMMs
+        (``self.trace[gemm, cta] = entry, schedule, last TMA, done``)."""
+        self.trace = torch.zeros(2, self.grid, 4, dtype=torch.int64, device=self.device) if on else None
+
+    def _trace_ptr(self, i: int) -> int:
+        t = getattr(self, "trace", None)
+        return t[i].data_ptr() if t is not None else 0
 
     def dropped_total(self) -> int:
         return int(self.words[19].item())
@@ -197,13 +213,15 @@ class ExpertParallel:
         E.moe_expert_gemm(0, w.w13, self.mine("slab"), self.E_local, 2 * self.I, self.H, self.rows, w.s13,
                           self.mine("slab_scale"), self.act.data_ptr(), self.mine("counter"), self.mine("done"),
                           self.rows_valid, self.tiles_done, self.world, self.capacity, self.mine("slab_meta"),
-                          [], [], self.K, st)
+                          [], [], self.K, self.ws.data_ptr(), self.tile_counters.data_ptr(), self.grid,
+                          self._trace_ptr(0), st)
         E.moe_quantize(self.act.data_ptr(), self.act.shape[0], self.I, self.act_q.data_ptr(),
                        self.act_scale.data_ptr(), self.rows_valid, self.rows)
         E.moe_expert_gemm(1, w.w2, self.act_q.data_ptr(), self.E_local, self.H, self.I, self.rows, w.s2,
                           self.act_scale.data_ptr(), 0, self.mine("counter"), self.mine("done"), self.rows_valid,
                           self.tiles_done, self.world, self.capacity, self.mine("slab_meta"),
-                          self.peer("combine"), self.peer("combine_cnt"), self.K, st)
+                          self.peer("combine"), self.peer("combine_cnt"), self.K, self.ws.data_ptr(),
+                          self.tile_counters.data_ptr(), self.grid, self._trace_ptr(1), st)
         if T:
             E.moe_combine_norm(self.mine("combine"), self.K, h, ln_next, y, T, eps, self.mine("combine_cnt"),
                                self.dropped_step, self.arrivals, st)

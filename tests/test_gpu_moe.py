@@ -72,3 +72,34 @@ def test_moe_capacity_drops_overflow():
     torch.cuda.synchronize()
     ops.check_status()
     assert ep.dropped_total() == expect and expect > 0
+
+
+def test_mixtral_engine_generates_like_reference():
+    import numpy as np
+
+    from sched_pass_b200.engine.engine import Engine, EngineConfig
+    from sched_pass_b200.models.llama import rope_table
+    from sched_pass_b200.models.mixtral import mixtral_factory
+
+    cfg = MIXTRAL_TINY
+    ecfg = EngineConfig(max_batch=8, max_prefill_tokens=128, max_context=256)
+    T = max(ecfg.max_prefill_tokens + ecfg.max_batch, 256)
+    ep = ExpertParallel(cfg, "cuda", max_tokens=T)
+    eng = Engine(cfg, ecfg, "cuda", model_factory=mixtral_factory(ep, 0, 1))
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, cfg.vocab, size=int(n)).astype(np.int32) for n in (5, 40, 17)]
+    out = eng.generate(prompts, max_new_tokens=4)
+    ops.check_status()
+    assert all(len(o) == 4 for o in out)
+    cos_sin = rope_table(cfg, 512, "cuda")
+
+    def experts_of(lw):
+        return experts(cfg, lw.moe)
+
+    for p, o in zip(prompts, out):
+        logits = ref.mixtral_forward_tokens(cfg, eng.model.w, p, cos_sin, experts_of, quantize=quant_rows)
+        top2 = logits.topk(2).values
+        if (top2[0] - top2[1]).item() > 0.05:  # skip near-ties
+            assert int(logits.argmax()) == o[0]
+    assert ep.dropped_total() == 0
+    ep.close()
