@@ -440,6 +440,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &embedding);
   m.def("argmax", &argmax);
   m.def("set_gemm_trace", &set_gemm_trace);
+  m.def("gemm_plan", [](int64_t T, int64_t N, int64_t K, int64_t epi, int64_t sms) {
+    int cs = 0, grid = 0;
+    sched_gemm_plan(T, N, K, epi, sms, &cs, &grid);
+    return std::make_tuple(cs, grid);
+  });
   m.def("moe_router", &moe_router);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_expert_gemm", &moe_expert_gemm);

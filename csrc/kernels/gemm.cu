@@ -79,6 +79,12 @@ struct Cfg {
   static constexpr int SLAB_BYTES = kSlab * kSlabPitch * 4;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SLAB_BYTES + 512;
   static constexpr int smem(int stages) { return 1024 + stages * STAGE_BYTES + SLAB_BYTES + 512; }
+  // cluster split-K: each CTA's fp32 partial tile [TN][128] lives in shared
+  // memory for its peers to read over DSMEM
+  static constexpr int RED_BYTES = TN * BM * 4;
+  static constexpr int CSTAGES_RAW = (200 * 1024 - RED_BYTES) / STAGE_BYTES;
+  static constexpr int CSTAGES = CSTAGES_RAW > 12 ? 12 : CSTAGES_RAW;
+  static constexpr int CSMEM = 1024 + CSTAGES * STAGE_BYTES + SLAB_BYTES + RED_BYTES + 512;
 };
 
 struct Params {
@@ -87,6 +93,7 @@ struct Params {
   long long units;  // tiles * kb
   int grid;
   int stages;  // ring depth of this launch (<= Cfg<TN>::STAGES)
+  int cs;      // cluster split-K: CTAs per cluster (0: stream-K kernel)
 };
 
 // One segment: the k-block range [kb0, kb1) of `tile` handled by one CTA.
@@ -556,6 +563,243 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (a.trace && threadIdx.x == 0) a.trace[c * 4 + 3] = ptx::globaltimer_ns();
 }
 
+// ============================================================================
+// Cluster split-K variant (decode shapes). The grid is G/CS clusters of CS
+// CTAs; cluster k owns tiles k, k + G/CS, ... and its CTA r accumulates the
+// K-blocks [r*kb/CS, (r+1)*kb/CS) of each in TMEM. The partial tiles are
+// reduced through distributed shared memory inside the cluster: every CTA
+// copies its accumulator to its own shared memory, signals its peers'
+// mbarriers, and then sums one CS-th of the tile's tokens from all CS copies
+// (in rank order: deterministic) and runs the epilogue on them. No partial
+// ever leaves the GPC, so there is no global workspace, no counter and no
+// serial fix-up at the end (which is what limits stream-K at these sizes).
+template <int TN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_cluster_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                        const Params p) {
+  using C = Cfg<TN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *base = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  uint8_t *stage_mem = base;
+  float *slab = reinterpret_cast<float *>(base + S * C::STAGE_BYTES);
+  float *red = reinterpret_cast<float *>(base + S * C::STAGE_BYTES + C::SLAB_BYTES);  // [TN][BM]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + S * C::STAGE_BYTES + C::SLAB_BYTES + C::RED_BYTES);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + S;
+  uint64_t *acc_full = bars + 2 * S;       // [2]
+  uint64_t *acc_empty = bars + 2 * S + 2;  // [2]
+  uint64_t *red_ready = bars + 2 * S + 4;  // CS arrivals: every peer's partial is in place
+  uint64_t *red_free = bars + 2 * S + 5;   // CS arrivals: every peer has read ours
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 6);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const GemmArgs &a = p.a;
+  const int CS = p.cs;
+  const int rank = (int)ptx::cluster_ctarank();
+  const int cid = blockIdx.x / CS;
+  const int nclusters = gridDim.x / CS;
+  const int kb0 = rank * p.kb / CS, kb1 = (rank + 1) * p.kb / CS;
+
+  ptx::pdl_launch_dependents();
+  if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4] = ptx::globaltimer_ns();
+  if (warp == 0) {
+    ptx::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&acc_full[i], 1);
+      ptx::mbar_init(&acc_empty[i], kEpiThreads);
+    }
+    ptx::mbar_init(red_ready, CS);
+    ptx::mbar_init(red_free, CS);
+    ptx::fence_mbar_init();
+  }
+  if (threadIdx.x == 64) {
+    ptx::prefetch_tmap(&tmW);
+    ptx::prefetch_tmap(&tmX);
+  }
+  __syncwarp();
+  ptx::tc_fence_before();
+  ptx::cluster_sync_all();  // peers' barriers are initialised before any remote arrive
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ============================================================ producer
+    if (ptx::elect_one()) {
+      int pre = 0;  // weights of the first stages do not depend on the previous kernel
+      for (int tile = cid; tile < p.tiles && pre < S; tile += nclusters) {
+        const int nt = tile / p.t_tiles;
+        for (int kb = kb0; kb < kb1 && pre < S; ++kb, ++pre) {
+          ptx::mbar_arrive_expect_tx(&full[pre], C::STAGE_BYTES);
+          ptx::tma_load_2d(stage_mem + pre * C::STAGE_BYTES, &tmW, &full[pre], kb * BK, nt * BM);
+        }
+      }
+      ptx::pdl_wait();
+      int i = 0;
+      bool ok = true;
+      for (int tile = cid; ok && tile < p.tiles; tile += nclusters) {
+        const int nt = tile / p.t_tiles, tt = tile % p.t_tiles;
+        for (int kb = kb0; kb < kb1; ++kb, ++i) {
+          const int st = i % S;
+          uint8_t *sm = stage_mem + st * C::STAGE_BYTES;
+          if (i >= pre) {
+            if (!ptx::mbar_wait(&empty[st], ((i / S) & 1) ^ 1, kWaitBudgetNs)) {
+              report_status(a.status, kStatusMmaTimeout);
+              ok = false;
+              break;
+            }
+            ptx::mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+            ptx::tma_load_2d(sm, &tmW, &full[st], kb * BK, nt * BM);
+          }
+          ptx::tma_load_2d(sm + C::W_BYTES, &tmX, &full[st], kb * BK, tt * TN);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ============================================================ MMA
+    if (ptx::elect_one()) {
+      constexpr uint32_t idesc = ptx::idesc_f16(BM, TN, /*bf16*/ 1, false, false);
+      int i = 0, j = 0;
+      bool ok = true;
+      for (int tile = cid; ok && tile < p.tiles; tile += nclusters, ++j) {
+        const int ab = j & 1;
+        if (!ptx::mbar_wait(&acc_empty[ab], ((j >> 1) & 1) ^ 1, kWaitBudgetNs)) {
+          report_status(a.status, kStatusEpilogueTimeout);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t acc = tmem + ab * C::ACC_COLS;
+        for (int kb = kb0; kb < kb1; ++kb, ++i) {
+          const int st = i % S;
+          if (!ptx::mbar_wait(&full[st], (i / S) & 1, kWaitBudgetNs)) {
+            report_status(a.status, kStatusTmaTimeout);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          uint8_t *sm = stage_mem + st * C::STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t da = ptx::smem_desc(sm + kk * 32, 16, 1024, ptx::kLayoutSW128);
+            const uint64_t db = ptx::smem_desc(sm + C::W_BYTES + kk * 32, 16, 1024, ptx::kLayoutSW128);
+            ptx::mma_f16_ss(acc, da, db, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          ptx::mma_commit(&empty[st]);
+        }
+        ptx::mma_commit(&acc_full[ab]);
+      }
+    }
+  } else {
+    // ============================================================ epilogue
+    const int et = threadIdx.x - 64;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int tj = et / 8, part = et % 8;
+    ptx::pdl_wait();
+    const uint32_t red_addr = ptx::smem_u32(red);
+    const uint32_t ready_addr = ptx::smem_u32(red_ready), free_addr = ptx::smem_u32(red_free);
+    int j = 0;
+    for (int tile = cid; tile < p.tiles; tile += nclusters, ++j) {
+      const int ab = j & 1;
+      const bool waited = ptx::mbar_wait(&acc_full[ab], (j >> 1) & 1, kWaitBudgetNs);
+      if (!waited) report_status(a.status, kStatusEpilogueTimeout);
+      ptx::tc_fence_after();
+      const int nt = tile / p.t_tiles, tt = tile % p.t_tiles;
+      const int t0 = tt * TN;
+      const int tvalid = min(TN, a.T - t0);
+      if (CS == 1) {
+        // whole K in this CTA: straight to the epilogue
+        for (int ch = 0; ch * kSlab < tvalid; ++ch) {
+          uint32_t r[16];
+          ptx::tmem_ld16(tmem + ab * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + ch * kSlab, r);
+          ptx::tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) slab[jj * kSlabPitch + row] = waited ? __uint_as_float(r[jj]) : 0.f;
+          named_bar(1, kEpiThreads);
+          const int t = t0 + ch * kSlab + tj;
+          if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part);
+          named_bar(1, kEpiThreads);
+        }
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&acc_empty[ab]);
+        continue;
+      }
+      // our partial may overwrite `red` once every peer has read the previous one
+      if (j > 0 && !ptx::mbar_wait_cluster(red_free, (j - 1) & 1, kWaitBudgetNs))
+        report_status(a.status, kStatusPeerTimeout);
+      for (int ch = 0; ch * kSlab < tvalid; ++ch) {
+        uint32_t r[16];
+        ptx::tmem_ld16(tmem + ab * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + ch * kSlab, r);
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) red[(ch * kSlab + jj) * BM + row] = waited ? __uint_as_float(r[jj]) : 0.f;
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&acc_empty[ab]);  // the MMA warp may start tile j + 2
+      named_bar(1, kEpiThreads);
+      if (et == 0)
+        for (int s2 = 0; s2 < CS; ++s2) ptx::mbar_arrive_cluster(ptx::mapa_shared(ready_addr, s2));
+      if (!ptx::mbar_wait_cluster(red_ready, j & 1, kWaitBudgetNs)) report_status(a.status, kStatusPeerTimeout);
+      // sum our share of the tile's tokens over the CS partials, rank order
+      const int lo = rank * tvalid / CS, hi = (rank + 1) * tvalid / CS;
+      for (int b = lo; b < hi; b += kSlab) {
+        const int tl = b + tj;
+        float acc[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
+        if (tl < hi) {
+          const uint32_t off = red_addr + (uint32_t)((tl * BM + part * 16) * 4);
+          for (int s0 = 0; s0 < CS; s0 += 4) {
+            float4 v[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (s0 + u < CS) {
+                const uint32_t src = ptx::mapa_shared(off, s0 + u);
+#pragma unroll
+                for (int x = 0; x < 4; ++x) v[u][x] = ptx::ld_dsmem_v4(src + 16 * x);
+              }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (s0 + u < CS) {
+#pragma unroll
+                for (int x = 0; x < 4; ++x) {
+                  acc[4 * x] += v[u][x].x;
+                  acc[4 * x + 1] += v[u][x].y;
+                  acc[4 * x + 2] += v[u][x].z;
+                  acc[4 * x + 3] += v[u][x].w;
+                }
+              }
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) slab[tj * kSlabPitch + part * 16 + jj] = acc[jj];
+        named_bar(1, kEpiThreads);
+        if (tl < hi) write_row<EPI>(a, nt, t0 + tl, slab + tj * kSlabPitch, part);
+        named_bar(1, kEpiThreads);
+      }
+      // every peer's partial has been read: release them
+      named_bar(1, kEpiThreads);
+      if (et == 0)
+        for (int s2 = 0; s2 < CS; ++s2) ptx::mbar_arrive_cluster(ptx::mapa_shared(free_addr, s2));
+    }
+  }
+
+  __syncwarp();
+  ptx::tc_fence_before();
+  ptx::cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
+  if (warp == 0) ptx::tmem_dealloc(tmem, C::TMEM_COLS);
+  if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4 + 3] = ptx::globaltimer_ns();
+}
+
 template <int TN, int EPI>
 static void launch_tn(const CUtensorMap &tw, const CUtensorMap &tx, const Params &p,
                       cudaStream_t stream) {
@@ -579,6 +823,103 @@ static void launch_tn(const CUtensorMap &tw, const CUtensorMap &tx, const Params
   cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
 }
 
+template <int TN, int EPI>
+static void launch_cluster_tn(const CUtensorMap &tw, const CUtensorMap &tx, const Params &p,
+                              cudaStream_t stream) {
+  using C = Cfg<TN>;
+  auto kern = gemm_cluster_kernel<TN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::CSMEM);
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::CSMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = p.cs;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
+}
+
+// Clusters of `cs` CTAs of this instantiation that fit on the GPU at once.
+template <int TN, int EPI>
+static int cluster_capacity(int cs) {
+  using C = Cfg<TN>;
+  static int cache[9] = {-1, -1, -1, -1, -1, -1, -1, -1, -1};
+  if (cs < 1 || cs > 8) return 0;
+  if (cache[cs] >= 0) return cache[cs];
+  auto kern = gemm_cluster_kernel<TN, EPI>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::CSMEM);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cs * 64);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::CSMEM;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cs;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[cs] = n;
+  return n;
+}
+
+// Cluster split-K plan of a call: cluster size and grid, or cs = 0 when the
+// stream-K kernel is the better schedule. Cost model in K-blocks per CTA:
+// cluster plan = rounds of tiles x K-blocks per rank (+2 for the DSMEM
+// reduction), against the stream-K ideal units / SMs. Stream-K pays a serial
+// global-memory fix-up per split tile on top of its ideal, which dominates
+// when tiles are cut into two or more segments (tiles <= SMs / 2): there the
+// cluster plan is taken within SCHED_GEMM_CLUSTER_SLACK (default 1.32) of
+// the ideal; with more tiles only a near-perfect (<= 1.05) cluster plan is.
+// (Measured on B200, Llama-3-8B decode shapes: o_proj and down_proj go to
+// clusters, qkv and gate_up stay on stream-K.)
+template <int TN, int EPI>
+static void plan_cluster(Params &p, int num_sms) {
+  p.cs = 0;
+  static const double slack = [] {
+    const char *v = std::getenv("SCHED_GEMM_CLUSTER_SLACK");
+    return v ? std::atof(v) : 1.32;
+  }();
+  if (slack <= 0.0) return;
+  const double ideal = (double)p.units / num_sms;
+  double best = 1e30;
+  int best_cs = 0, best_grid = 0;
+  for (int cs = 1; cs <= 8; ++cs) {
+    if (p.kb < cs) break;
+    const int ncl = std::min(cluster_capacity<TN, EPI>(cs), num_sms / cs);
+    if (ncl <= 0) continue;
+    const int rounds = (p.tiles + ncl - 1) / ncl;
+    const int used = std::min(ncl, p.tiles);
+    const double cost = (double)rounds * ((p.kb + cs - 1) / cs) + (cs > 1 ? 2.0 : 0.0);
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_cs = cs;
+      best_grid = used * cs;
+    }
+  }
+  const double limit = (2 * p.tiles <= num_sms) ? slack : std::min(slack, 1.05);
+  if (best_cs > 0 && best <= limit * ideal) {
+    p.cs = best_cs;
+    p.grid = best_grid;
+  }
+}
+
 // Ring depth: the deepest that fits, unless SCHED_GEMM_SMEM_KB caps the
 // shared memory of a CTA (a smaller CTA lets the next kernel's CTA become
 // resident beside it and start its weight prefetch during this one's tail).
@@ -595,15 +936,39 @@ static int stages_for() {
   return s;
 }
 
+template <int TN, int EPI>
+static void launch_any(const CUtensorMap &tw, const CUtensorMap &tx, Params p, cudaStream_t stream) {
+  if (p.cs > 0) {
+    p.stages = Cfg<TN>::CSTAGES;
+    launch_cluster_tn<TN, EPI>(tw, tx, p, stream);
+  } else {
+    p.stages = stages_for<TN>();
+    launch_tn<TN, EPI>(tw, tx, p, stream);
+  }
+}
+
 template <int EPI>
 static void dispatch(int tn, const CUtensorMap &tw, const CUtensorMap &tx, Params p,
                      cudaStream_t stream) {
   switch (tn) {
-    case 16: p.stages = stages_for<16>(); launch_tn<16, EPI>(tw, tx, p, stream); break;
-    case 32: p.stages = stages_for<32>(); launch_tn<32, EPI>(tw, tx, p, stream); break;
-    case 64: p.stages = stages_for<64>(); launch_tn<64, EPI>(tw, tx, p, stream); break;
-    case 128: p.stages = stages_for<128>(); launch_tn<128, EPI>(tw, tx, p, stream); break;
-    default: p.stages = stages_for<256>(); launch_tn<256, EPI>(tw, tx, p, stream); break;
+    case 16: launch_any<16, EPI>(tw, tx, p, stream); break;
+    case 32: launch_any<32, EPI>(tw, tx, p, stream); break;
+    case 64: launch_any<64, EPI>(tw, tx, p, stream); break;
+    case 128: launch_any<128, EPI>(tw, tx, p, stream); break;
+    default: launch_any<256, EPI>(tw, tx, p, stream); break;
+  }
+}
+
+// The cluster plan for the instantiation a call will use (TN <= 128 and a
+// row-wise epilogue; the NVLink all-reduce epilogue stays on stream-K).
+template <int EPI>
+static void plan_cluster_for(int tn, Params &p, int num_sms) {
+  switch (tn) {
+    case 16: plan_cluster<16, EPI>(p, num_sms); break;
+    case 32: plan_cluster<32, EPI>(p, num_sms); break;
+    case 64: plan_cluster<64, EPI>(p, num_sms); break;
+    case 128: plan_cluster<128, EPI>(p, num_sms); break;
+    default: p.cs = 0; break;
   }
 }
 
@@ -649,6 +1014,34 @@ extern "C" long long sched_gemm_ws_floats(int T, int N, int K, int grid) {
   return (long long)p.grid * 2 * tn * gemm::BM;
 }
 
+// The schedule sched_gemm_run would use for a default-grid call of this
+// shape: writes the cluster size (0 = stream-K) and the grid.
+extern "C" void sched_gemm_plan(int T, int N, int K, int epi, int num_sms, int *cs, int *grid) {
+  GemmArgs a{};
+  a.T = T;
+  a.N = N;
+  a.K = K;
+  a.epi = epi;
+  a.num_sms = num_sms;
+  gemm::Params p;
+  int tn;
+  gemm::plan(a, p, tn);
+  p.cs = 0;
+  if (epi != kEpiAllReduce) {
+    p.grid = num_sms;
+    p.units = (long long)p.tiles * p.kb;
+    if (epi == kEpiSwiGLU)
+      gemm::plan_cluster_for<kEpiSwiGLU>(tn, p, num_sms);
+    else if (epi == kEpiRopeKV)
+      gemm::plan_cluster_for<kEpiRopeKV>(tn, p, num_sms);
+    else
+      gemm::plan_cluster_for<kEpiStore>(tn, p, num_sms);
+    if (p.cs == 0) gemm::plan(a, p, tn);
+  }
+  *cs = p.cs;
+  *grid = p.grid;
+}
+
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   const GemmArgs &a = *args;
   if (a.T <= 0) return 0;
@@ -657,8 +1050,22 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   int tn;
   p.a = a;
   gemm::plan(a, p, tn);
+  p.cs = 0;
+  if (a.grid <= 0 && a.epi != kEpiAllReduce) {
+    // the default schedule: cluster split-K where it fits the shape
+    const int sms = a.num_sms > 0 ? a.num_sms : 148;
+    p.grid = std::max(1, sms);
+    p.units = (long long)p.tiles * p.kb;
+    if (a.epi == kEpiSwiGLU)
+      gemm::plan_cluster_for<kEpiSwiGLU>(tn, p, sms);
+    else if (a.epi == kEpiRopeKV)
+      gemm::plan_cluster_for<kEpiRopeKV>(tn, p, sms);
+    else
+      gemm::plan_cluster_for<kEpiStore>(tn, p, sms);
+    if (p.cs == 0) gemm::plan(a, p, tn);  // back to the stream-K grid
+  }
 
-  if (gemm::splits_tiles(p)) {
+  if (p.cs == 0 && gemm::splits_tiles(p)) {
     if (a.ws == nullptr || a.counters == nullptr) return -2;
     const long long need = (long long)p.grid * 2 * tn * gemm::BM;
     if (need > a.ws_floats || p.tiles > a.counter_count) return -5;

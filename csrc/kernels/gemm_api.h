@@ -49,6 +49,8 @@ struct GemmArgs {
 };
 
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream);
+// Schedule of a default-grid call: cluster size (0 = stream-K) and grid.
+extern "C" void sched_gemm_plan(int T, int N, int K, int epi, int num_sms, int *cs, int *grid);
 extern "C" long long sched_gemm_ws_floats(int T, int N, int K, int grid);
 
 // ---------------------------------------------------------------------------
