@@ -14,7 +14,7 @@ class State(enum.Enum):
     DONE = 3
 
 
-@dataclass
+@dataclass(eq=False)  # identity semantics: requests are compared and hashed by object
 class Request:
     rid: int
     prompt: np.ndarray            # int32 token ids

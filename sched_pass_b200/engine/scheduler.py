@@ -106,8 +106,10 @@ class Scheduler:
     def schedule(self) -> StepPlan:
         plan = StepPlan()
         # 1. decode: every request whose prompt is fully cached
+        # (a preempted request leaves `running` and becomes WAITING, so the
+        # state alone says whether it is still admitted)
         for req in list(self.running):
-            if req.state != State.DECODE or req not in self.running:
+            if req.state != State.DECODE:
                 continue
             while not self._grow(req, req.total_len):
                 victim = self.running[-1]
@@ -116,7 +118,7 @@ class Scheduler:
                 self._preempt(victim, plan)
                 if victim is req:
                     break
-            if req in self.running:
+            if req.state == State.DECODE:
                 plan.decode.append(req)
         # 2. prefill: continue partial prefills, then admit new requests
         budget = self.max_prefill_tokens
