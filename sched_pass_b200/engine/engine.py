@@ -35,6 +35,7 @@ from ..models.llama import ForwardBatch, KVCache, Llama, init_weights
 from ..runtime.controller import SchedControlPlane
 from ..runtime.sched_rt import SchedPlane
 from . import native
+from .plugin import HookRunner, SchedPlugin, SchedPluginConfig
 from .request import Request, State
 from .scheduler import Scheduler, StepPlan
 
@@ -59,6 +60,7 @@ class EngineConfig:
     shed_ratio: float = 0.5         # tau = ratio * context length
     target_tasks: int = 0           # decode tasks to aim for (0 = 2 x SMs)
     seed: int = 0
+    verbose: bool = False           # print the scheduling plugin's effective config
 
 
 @dataclass
@@ -111,7 +113,14 @@ class Engine:
         self._pool = None
         self.stats: list[StepStats] = []
         self.clock = 0.0  # workload clock in seconds (device time + idle gaps)
-        self._probe_pending = None
+        # per-step hooks; the scheduling plugin programs the levers
+        self.hooks = HookRunner()
+        self.plugin = None
+        if e.levers:
+            pcfg = SchedPluginConfig.from_engine_config(e).with_env()
+            self.plugin = SchedPlugin(pcfg).register(self) if e.verbose else SchedPlugin(pcfg)
+            if not e.verbose:
+                self.hooks.register(self.plugin)
 
     # ------------------------------------------------------------------ buffers
     def _alloc_buffers(self, T: int) -> None:
@@ -290,70 +299,10 @@ class Engine:
         return {"static": 0, "ticket": 1, "clc": 2, "auto": 2}.get(self.ecfg.acquire, 0)
 
     # ------------------------------------------------------------------ levers
-    def _program_levers(self, plan: StepPlan, info) -> None:
-        """Order, timer cadence, shed and work-queue arming for this step."""
-        e = self.ecfg
-        nd, n_items = info["nd"], info["n_items"]
-        if not e.levers or nd == 0:
-            return
-        n_tasks = n_items * self.hkv
-        plane = self.plane
-        replan = (self.step_no % max(1, e.plan_every)) == 0
-        if replan:
-            items = self._host("items")[:n_items * 4].reshape(-1, 4)
-            cost = native.task_costs(items, n_items, self.hkv)
-            arm_clc = False
-            if e.acquire == "clc":
-                arm_clc = True
-            elif e.acquire == "auto":
-                dec = plan.decode
-                unc = self.controller.uncertainty([r.rid for r in dec], [r.total_len for r in dec])
-                arm_clc = n_tasks > self.R and unc > e.clc_uncertainty
-            if arm_clc:
-                order = native.region_order(cost, self.R, e.lpt_block)
-            elif n_tasks > self.R:
-                order = native.grouped_lpt(cost, e.lpt_block)
-            else:
-                order = None  # one wave: ordering cannot help; identity
-            if order is not None:
-                plane.install_order(torch.from_numpy(order), n_tasks)
-            else:
-                plane.set_order_size(0)
-                plane.reset_order()
-            # claims stay on for the acquisition modes: the decode kernel is
-            # persistent either way, arming only changes the order policy
-            plane.set_num_tasks(n_tasks if e.acquire in ("ticket", "clc", "auto") else 0)
-        # shed: tau for the lowest-urgency fraction of decode requests
-        if e.shed_fraction > 0:
-            dec = plan.decode
-            k = int(len(dec) * e.shed_fraction)
-            low = sorted(range(len(dec)), key=lambda i: dec[i].urgency)[:k]
-            tau = np.zeros(n_tasks, dtype=np.int64)
-            items = self._host("items")[:n_items * 4].reshape(-1, 4)
-            low_set = set(low)
-            for it in range(n_items):
-                if int(items[it, 0]) in low_set:
-                    r = dec[int(items[it, 0])]
-                    tau[it * self.hkv:(it + 1) * self.hkv] = max(1, int(e.shed_ratio * r.total_len))
-            plane.set_rows(tau=np.minimum(tau, 0xFFFF), n=n_tasks)
-        probe = e.timer_every > 0 and (self.step_no % e.timer_every) == 0
-        plane.set_timer_enabled(probe)
-        if probe:
-            plane.clear_timer()
-        plane.push()
-        self._probe = probe
-
-    def _fold_probe(self, plan: StepPlan, info) -> None:
-        if not getattr(self, "_probe", False) or info["nd"] == 0:
-            return
-        cyc = self.plane.timer_t[: info["n_items"] * self.hkv].view(info["n_items"], self.hkv).sum(1)
-        cyc = cyc.cpu().numpy()
-        items = self._host("items")[: info["n_items"] * 4].reshape(-1, 4)
-        per_req = np.zeros(info["nd"], dtype=np.float64)
-        np.add.at(per_req, items[:, 0], cyc)
-        dec = plan.decode
-        self.controller.observe([r.rid for r in dec], [r.total_len for r in dec],
-                                per_req[: len(dec)].tolist())
+    def register_hook(self, hook) -> None:
+        """Add a per-step hook (``on_batch_begin(engine, plan, info)`` /
+        ``on_batch_end(engine, plan, info, ms)``); see engine/plugin.py."""
+        self.hooks.register(hook)
 
     # ------------------------------------------------------------------ graphs
     def _bucket(self, nd: int) -> int | None:
@@ -391,7 +340,7 @@ class Engine:
         bucket = self._bucket(nd) if (decode_only and self.ecfg.cuda_graphs) else None
         info = self._fill(plan, bucket)
         slots = self.plane.slots() if self.ecfg.levers else None
-        self._program_levers(plan, info)
+        self.hooks.begin(self, plan, info)
         # one H2D copy of every step input
         self.dev[: self.packed_len].copy_(self.host[: self.packed_len], non_blocking=True)
         si = self._view("sample_idx")
@@ -413,7 +362,7 @@ class Engine:
         ev1.synchronize()
         ms = ev0.elapsed_time(ev1)
         self.clock += ms / 1e3
-        self._fold_probe(plan, info)
+        self.hooks.end(self, plan, info, ms)
         out = self.out_host[:ns].numpy()
         sampled = {rid: int(out[i]) for rid, i in info["sample_map"]}
         done = self.sched.commit(plan, sampled, self.clock)

@@ -1,0 +1,199 @@
+"""HTTP front end of the serving engine.
+
+``EngineServer`` owns an engine and runs it on a dedicated thread (the only
+thread that touches the GPU): HTTP handlers enqueue requests and wait for
+their completion; the engine thread admits queued requests between steps,
+steps while there is work, and completes finished requests. Endpoints:
+
+* ``POST /generate`` -- ``{"input_ids": [...], "sampling_params":
+  {"max_new_tokens": N}}`` (the ``/generate`` shape SGLang-style clients
+  and ``engine/loadgen.py`` send); returns ``{"output_ids": [...],
+  "meta_info": {"prompt_tokens", "completion_tokens", "e2e_latency",
+  "ttft", "tpot"}}``. Decoding is greedy and runs ``max_new_tokens`` tokens.
+* ``GET /health`` -- liveness plus queue depths.
+* ``GET /stats`` -- steps, decode tokens, the scheduling plugin's counters.
+
+    python -m sched_pass_b200.engine.server --model llama-3-8b --port 30000
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import queue
+import threading
+import time
+
+import numpy as np
+
+
+class EngineServer:
+    def __init__(self, engine, idle_wait_s: float = 0.002):
+        self.engine = engine
+        self.idle_wait_s = idle_wait_s
+        self._inbox: queue.Queue = queue.Queue()
+        self._pending: dict = {}
+        self._next_rid = 0
+        self._lock = threading.Lock()
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+        self.steps = 0
+        self.decode_tokens = 0
+        self.error: BaseException | None = None
+
+    # ---------------------------------------------------------------- client side
+    def submit(self, input_ids, max_new_tokens: int, urgency: float = 0.0) -> cf.Future:
+        """Queue one request; the future resolves to the response dict."""
+        from .request import Request
+        ids = np.asarray(input_ids, dtype=np.int32)
+        if ids.ndim != 1 or ids.size == 0:
+            raise ValueError("input_ids must be a non-empty list of token ids")
+        if max_new_tokens < 1:
+            raise ValueError("max_new_tokens must be >= 1")
+        fut: cf.Future = cf.Future()
+        with self._lock:
+            rid = self._next_rid
+            self._next_rid += 1
+        req = Request(rid=rid, prompt=ids, max_new_tokens=int(max_new_tokens), urgency=float(urgency))
+        req._t_submit = time.perf_counter()  # host clock of the HTTP side
+        self._inbox.put((req, fut))
+        return fut
+
+    # ---------------------------------------------------------------- engine thread
+    def _admit(self) -> None:
+        while True:
+            try:
+                req, fut = self._inbox.get_nowait()
+            except queue.Empty:
+                return
+            req.arrival = self.engine.clock
+            try:
+                self.engine.add_request(req)
+            except Exception as e:  # noqa: BLE001 - a bad request fails alone
+                fut.set_exception(e)
+                continue
+            self._pending[req.rid] = (req, fut)
+
+    def _complete(self, done) -> None:
+        now = time.perf_counter()
+        for r in done:
+            item = self._pending.pop(r.rid, None)
+            if item is None:
+                continue
+            _, fut = item
+            tpot = r.tpot()
+            fut.set_result({
+                "output_ids": [int(t) for t in r.output],
+                "meta_info": {"prompt_tokens": r.prompt_len, "completion_tokens": len(r.output),
+                              "e2e_latency": now - r._t_submit, "ttft": r.ttft(), "tpot": tpot,
+                              "preemptions": r.preemptions},
+            })
+
+    def _loop(self) -> None:
+        try:
+            dev = getattr(self.engine, "device", None)
+            if dev is not None and getattr(dev, "type", "") == "cuda":
+                import torch
+                torch.cuda.set_device(dev)
+            while not self._stop.is_set():
+                self._admit()
+                if self.engine.has_work():
+                    plan, done = self.engine.step()
+                    self.steps += 1
+                    self.decode_tokens += len(plan.decode)
+                    self._complete(done)
+                else:
+                    try:
+                        item = self._inbox.get(timeout=self.idle_wait_s)
+                        self._inbox.put(item)
+                    except queue.Empty:
+                        pass
+        except BaseException as e:  # noqa: BLE001 - report to every waiter
+            self.error = e
+            for _, fut in list(self._pending.values()):
+                if not fut.done():
+                    fut.set_exception(e)
+            self._pending.clear()
+
+    def start(self) -> "EngineServer":
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._loop, name="sched-engine", daemon=True)
+            self._thread.start()
+        return self
+
+    def stop(self, timeout: float = 10.0) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout)
+            self._thread = None
+
+    # ---------------------------------------------------------------- HTTP
+    def app(self):
+        import asyncio
+
+        from fastapi import FastAPI, HTTPException
+        from fastapi.responses import JSONResponse
+
+        app = FastAPI(title="sched_pass_b200")
+
+        @app.post("/generate")
+        async def generate(body: dict):
+            ids = body.get("input_ids")
+            sp = body.get("sampling_params") or {}
+            if ids is None:
+                raise HTTPException(400, "input_ids is required (token ids; no tokenizer in this server)")
+            try:
+                fut = self.submit(ids, int(sp.get("max_new_tokens", 16)), float(body.get("urgency", 0.0)))
+            except ValueError as e:
+                raise HTTPException(400, str(e)) from e
+            try:
+                return JSONResponse(await asyncio.wrap_future(fut))
+            except Exception as e:  # noqa: BLE001
+                raise HTTPException(500, repr(e)) from e
+
+        @app.get("/health")
+        async def health():
+            return {"ok": self.error is None, "queued": self._inbox.qsize(), "running": len(self._pending)}
+
+        @app.get("/stats")
+        async def stats():
+            out = {"steps": self.steps, "decode_tokens": self.decode_tokens, "queued": self._inbox.qsize(),
+                   "running": len(self._pending)}
+            plugin = getattr(self.engine, "plugin", None)
+            if plugin is not None:
+                s = plugin.stats
+                out["sched"] = {"planned": s.planned, "probes": s.probes, "clc_armed": s.clc_armed,
+                                "orders": s.orders, "hook_errors": self.engine.hooks.errors}
+            return out
+
+        return app
+
+    def serve(self, host: str = "127.0.0.1", port: int = 30000, log_level: str = "warning") -> None:
+        import uvicorn
+        self.start()
+        try:
+            uvicorn.run(self.app(), host=host, port=port, log_level=log_level)
+        finally:
+            self.stop()
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="llama-3-8b")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=30000)
+    ap.add_argument("--max-batch", type=int, default=128)
+    ap.add_argument("--max-context", type=int, default=4096)
+    ap.add_argument("--acquire", default="auto")
+    a = ap.parse_args(argv)
+    import torch
+
+    from ..models.config import get_config
+    from .engine import Engine, EngineConfig
+    eng = Engine(get_config(a.model), EngineConfig(max_batch=a.max_batch, max_context=a.max_context,
+                                                   acquire=a.acquire, verbose=True), torch.device("cuda"))
+    EngineServer(eng).serve(a.host, a.port)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

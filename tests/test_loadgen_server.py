@@ -1,0 +1,110 @@
+"""Load generator and HTTP server on the CPU, with a fake model behind the
+real scheduler (continuous batching, chunked prefill, page accounting)."""
+import json
+import socket
+import threading
+import time
+
+import numpy as np
+
+from sched_pass_b200.engine import loadgen
+from sched_pass_b200.engine.scheduler import Scheduler
+from sched_pass_b200.engine.server import EngineServer
+
+
+class FakeEngine:
+    """Engine interface over the real Scheduler; the 'model' emits
+    (previous token + 1) mod vocab and every step takes 1 ms of clock."""
+
+    def __init__(self, vocab=1000, num_pages=4096, max_batch=16, max_prefill=256, max_context=4096):
+        self.sched = Scheduler(num_pages, 16, max_batch, max_prefill, max_context)
+        self.clock = 0.0
+        self.vocab = vocab
+        self.device = None
+        self.step_no = 0
+
+    def add_request(self, r):
+        self.sched.add(r)
+
+    def has_work(self):
+        return not self.sched.idle
+
+    def step(self):
+        plan = self.sched.schedule()
+        sampled = {}
+        for r in plan.decode:
+            sampled[r.rid] = (r.next_input_token() + 1) % self.vocab
+        for r, start, n in plan.prefill:
+            if start + n >= r.prompt_len:
+                sampled[r.rid] = (int(r.prompt[-1]) + 1) % self.vocab
+        self.clock += 0.001
+        done = self.sched.commit(plan, sampled, self.clock)
+        self.step_no += 1
+        return plan, done
+
+
+def test_inprocess_run_completes_everything():
+    work = loadgen.dispersed(40, mu=4.0, sigma=0.8, lo=8, hi=300, out=5, vocab=1000, seed=1, rate=200.0)
+    eng = FakeEngine()
+    res, wall = loadgen.run_inprocess(eng, work)
+    assert all(r.ok for r in res) and all(r.n_out == 5 for r in res)
+    s = loadgen.summarize(res, wall)
+    assert s["n_ok"] == 40 and s["tpot_p50"] is not None and s["tpot_p50"] >= 0.001 - 1e-9
+
+
+def test_trace_roundtrip_with_truncated_tail(tmp_path):
+    p = tmp_path / "t.jsonl"
+    recs = [{"chat_id": i, "timestamp": 0.5 * i, "input_length": 20 + 7 * i, "output_length": 3,
+             "hash_ids": [100 + j for j in range(i + 2)]} for i in range(6)]
+    text = "\n".join(json.dumps(r) for r in recs) + "\n" + '{"chat_id": 99, "timest'
+    p.write_text(text)
+    got = loadgen.load_trace(str(p))
+    assert len(got) == 6
+    work = loadgen.from_trace(got, vocab=1000, speed=2.0)
+    assert [len(w.prompt) for w in work] == [20 + 7 * i for i in range(6)]
+    assert work[3].arrival == 0.75
+    # shared hash prefix -> shared token prefix
+    assert np.array_equal(work[2].prompt[:32], work[4].prompt[:32])
+    assert loadgen.selftest(str(p)) == 0
+
+
+def test_server_futures_and_http_replay():
+    srv = EngineServer(FakeEngine()).start()
+    try:
+        futs = [srv.submit([1, 2, 3], 4), srv.submit(list(range(50)), 2)]
+        outs = [f.result(timeout=10) for f in futs]
+        assert outs[0]["output_ids"] == [4, 5, 6, 7]
+        assert outs[1]["output_ids"] == [50, 51]
+        assert outs[0]["meta_info"]["completion_tokens"] == 4
+        try:
+            srv.submit([], 3)
+        except ValueError:
+            pass
+        else:
+            raise AssertionError("empty prompt accepted")
+
+        import uvicorn
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        server = uvicorn.Server(uvicorn.Config(srv.app(), host="127.0.0.1", port=port, log_level="error"))
+        th = threading.Thread(target=server.run, daemon=True)
+        th.start()
+        for _ in range(200):
+            if server.started:
+                break
+            time.sleep(0.02)
+        assert server.started
+        work = loadgen.dispersed(24, mu=3.5, sigma=0.5, lo=4, hi=64, out=3, vocab=1000, seed=2)
+        res, wall = loadgen.replay_http(f"http://127.0.0.1:{port}", work, concurrency=8, realtime=False)
+        assert all(r.ok and r.n_out == 3 for r in res)
+        import requests
+        st = requests.get(f"http://127.0.0.1:{port}/stats", timeout=5).json()
+        assert st["steps"] > 0 and st["decode_tokens"] > 0
+        assert requests.get(f"http://127.0.0.1:{port}/health", timeout=5).json()["ok"]
+        r = requests.post(f"http://127.0.0.1:{port}/generate", json={"sampling_params": {}}, timeout=5)
+        assert r.status_code == 400
+        server.should_exit = True
+        th.join(10)
+    finally:
+        srv.stop()
