@@ -352,9 +352,23 @@ class SchedPlane:
     def set_order_size(self, n: int) -> None:
         struct.pack_into("<I", self._ctrl_host, CTRL_ORDER_SIZE_OFF, int(n))
 
-    def install_order(self, tasks, n: int) -> None:
+    def install_order(self, tasks, n: int, validate: bool = True) -> None:
         """Concurrent-safe install: the table first, the validity stamp
-        (order_size) with the next push."""
+        (order_size) with the next push. A batch larger than the table raises
+        (never truncated), and a host-side order that is not a permutation of
+        [0, n) raises before anything is written (a duplicate entry would run
+        one task twice and drop another). Device tensors are not inspected:
+        that would synchronise the stream."""
+        n = int(n)
+        if n > self.N:
+            raise RuntimeError(f"batch of {n} tasks exceeds the control tables' capacity "
+                               f"(SCHED_MAX_TASKS={self.N}); raise max_tasks")
+        if validate and not (isinstance(tasks, torch.Tensor) and tasks.is_cuda):
+            import numpy as np
+            t = np.asarray(torch.as_tensor(tasks).cpu(), dtype=np.int64)[:n]
+            if t.size != n or (n and (t.min() < 0 or t.max() >= n or
+                                      np.bincount(t, minlength=n).max() != 1)):
+                raise ValueError(f"order is not a permutation of [0, {n}): refusing to install it")
         self.set_order(tasks)
         self.set_order_size(n)
 
