@@ -45,6 +45,9 @@ int sched_moe_combine_norm(const void *c, int K, void *h, const void *w, void *y
                            int *status, cudaStream_t st);
 }
 #include "moe_api.h"
+extern "C" int sched_kv_page_copy(const void *src_k, const void *src_v, long long src_pages, void *dst_k,
+                                  void *dst_v, long long dst_pages, const int32_t *pairs, int n_pairs,
+                                  int layers, int heads, cudaStream_t st);
 
 namespace {
 
@@ -419,6 +422,20 @@ void moe_combine_norm(int64_t c, int64_t K, at::Tensor &h, const at::Tensor &w, 
            "moe_combine_norm");
 }
 
+// Page moves between KV pools (device <-> pinned host); pairs [n, 2] int32 on the device.
+void kv_page_copy(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &dst_k, at::Tensor &dst_v,
+                  const at::Tensor &pairs, int64_t n_pairs) {
+  TORCH_CHECK(src_k.dim() == 5 && dst_k.dim() == 5, "pools are [layers, pages, heads, 16, 128]");
+  TORCH_CHECK(src_k.size(0) == dst_k.size(0) && src_k.size(2) == dst_k.size(2), "pool shapes differ");
+  TORCH_CHECK(src_k.is_contiguous() && src_v.is_contiguous() && dst_k.is_contiguous() && dst_v.is_contiguous(),
+              "contiguous pools");
+  TORCH_CHECK(pairs.is_cuda() && pairs.scalar_type() == at::kInt && pairs.is_contiguous(), "pairs int32 on device");
+  check_rc(sched_kv_page_copy(src_k.data_ptr(), src_v.data_ptr(), src_k.size(1), dst_k.data_ptr(), dst_v.data_ptr(),
+                              dst_k.size(1), pairs.data_ptr<int32_t>(), n_pairs, src_k.size(0), src_k.size(2),
+                              cur_stream()),
+           "kv_page_copy");
+}
+
 }  // namespace
 
 void register_symm(py::module &m);
@@ -446,6 +463,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return std::make_tuple(cs, grid);
   });
   m.def("moe_router", &moe_router);
+  m.def("kv_page_copy", &kv_page_copy);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_expert_gemm", &moe_expert_gemm);
   m.def("moe_quantize", &moe_quantize);

@@ -40,8 +40,8 @@ KERNEL_SOURCES = [
     "kernels/attention_prefill.cu",
     "kernels/elementwise.cu",
     "kernels/moe.cu",
+    "kernels/kv_tier.cu",
     "kernels/microbench.cu",
-    "comm/fused_collective.cu",
 ]
 HOST_SOURCES = ["bindings.cpp", "comm/symm.cpp"]
 

@@ -61,6 +61,8 @@ class EngineConfig:
     target_tasks: int = 0           # decode tasks to aim for (0 = 2 x SMs)
     seed: int = 0
     verbose: bool = False           # print the scheduling plugin's effective config
+    host_kv_pages: int = 0          # tiered KV: pinned host pages the device pool spills to (0 = off)
+    kv_staging_pages: int = 0       # device pages a step may stage host-resident KV into
 
 
 @dataclass
@@ -88,7 +90,12 @@ class Engine:
         self.max_pages_per_req = (e.max_context + 15) // 16
         if not e.num_pages:
             e.num_pages = e.max_batch * self.max_pages_per_req + 64
-        self.kv = KVCache(cfg, e.num_pages, self.device, tp_size=tp_size)
+        n_stage = e.kv_staging_pages if e.host_kv_pages else 0
+        self.kv = KVCache(cfg, e.num_pages + n_stage, self.device, tp_size=tp_size)
+        self.tier = None
+        if e.host_kv_pages:
+            from .tiered_kv import TieredKV
+            self.tier = TieredKV(self.kv, e.num_pages, n_stage, e.host_kv_pages, self.device)
         if weights is None:
             weights = init_weights(cfg, self.device, tp_rank, tp_size, seed=e.seed,
                                    moe_builder=getattr(model_factory, "moe_builder", None))
@@ -98,7 +105,7 @@ class Engine:
         else:
             self.model = Llama(cfg, weights, self.kv, self.device, tp=tp, max_tokens=T,
                                max_pos=e.max_context + 16)
-        self.sched = Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context)
+        self.sched = Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context, tier=self.tier)
         self.hkv = cfg.n_kv_heads // tp_size
         self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.target_tasks = e.target_tasks or 2 * self.sms
@@ -214,13 +221,16 @@ class Engine:
         bt = self._host("block_table").reshape(-1, mp)
         kvl = self._host("kv_lens")
         # decode rows
+        if self.tier is not None:
+            self.tier.stage(dec)  # host-resident pages this step reads -> staging pages
         for i, r in enumerate(dec):
             p = r.total_len - 1
             ids[i] = r.next_input_token()
             pos[i] = p
-            slot[i] = r.pages[p // 16] * 16 + p % 16
-            npg = len(r.pages)
-            bt[i, :npg] = r.pages
+            slot[i] = r.pages[p // 16] * 16 + p % 16  # the last page is always on the device
+            pages = self.tier.pages_for(r) if self.tier is not None else r.pages
+            npg = len(pages)
+            bt[i, :npg] = pages
             kvl[i] = r.total_len
         if ndp > nd:  # padding rows: no cache write, empty attention items
             ids[nd:ndp] = 0

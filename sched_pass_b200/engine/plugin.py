@@ -230,7 +230,7 @@ class SchedPlugin:
             # arming only selects whether its claims run
             plane.set_num_tasks(n_tasks if engine.ecfg.acquire in ("ticket", "clc", "auto") else 0)
             self._hints(engine, plan, items, n_items)
-        if c.enforce and c.shed_fraction > 0:
+        if c.enforce and (c.shed_fraction > 0 or any(r.tau for r in plan.decode)):
             self._shed(engine, plan, items, n_items)
         plane.set_timer_enabled(probe)
         if probe:
@@ -249,18 +249,24 @@ class SchedPlugin:
 
     # ------------------------------------------------------------- pieces
     def _shed(self, engine, plan, items, n_items) -> None:
+        """tau rows: a request's own budget (``Request.tau``) when it has one,
+        else ``shed_ratio`` x context for the lowest-urgency ``shed_fraction``.
+        The budget is written back to the request so the tiered KV store
+        knows which pages the kernel will not read."""
         c = self.cfg
         dec = plan.decode
         k = int(len(dec) * c.shed_fraction)
-        if k == 0:
+        low = set(sorted((i for i in range(len(dec)) if not dec[i].tau), key=lambda i: dec[i].urgency)[:k])
+        for i in low:
+            dec[i].tau = max(1, int(c.shed_ratio * dec[i].total_len))
+        if not any(r.tau for r in dec):
             return
-        low = set(sorted(range(len(dec)), key=lambda i: dec[i].urgency)[:k])
         hkv = engine.hkv
         tau = np.zeros(n_items * hkv, dtype=np.int64)
         for it in range(n_items):
-            ri = int(items[it, 0])
-            if ri in low:
-                tau[it * hkv:(it + 1) * hkv] = max(1, int(c.shed_ratio * dec[ri].total_len))
+            r = dec[int(items[it, 0])]
+            if r.tau:
+                tau[it * hkv:(it + 1) * hkv] = min(int(r.tau), r.total_len)
         engine.plane.set_rows(tau=np.minimum(tau, 0xFFFF), n=n_items * hkv)
 
     def _hints(self, engine, plan, items, n_items) -> None:

@@ -35,8 +35,9 @@ class StepPlan:
 
 class Scheduler:
     def __init__(self, num_pages: int, page_size: int = 16, max_batch: int = 256,
-                 max_prefill_tokens: int = 4096, max_context: int = 8192):
+                 max_prefill_tokens: int = 4096, max_context: int = 8192, tier=None):
         self.alloc = PageAllocator(num_pages)
+        self.tier = tier  # optional TieredKV: spill to host before preempting
         self.page_size = page_size
         self.max_batch = max_batch
         self.max_prefill_tokens = max_prefill_tokens
@@ -79,6 +80,11 @@ class Scheduler:
         if n == 0:
             return True
         got = self.alloc.take(n)
+        if got is None and self.tier is not None:
+            freed = self.tier.spill(n - self.alloc.free, self.running, protect=req)
+            if freed:
+                self.alloc.give(np.asarray(freed, dtype=np.int32))
+            got = self.alloc.take(n)
         if got is None:
             return False
         req.pages.extend(int(p) for p in got)
@@ -86,7 +92,14 @@ class Scheduler:
 
     def release(self, req: Request) -> None:
         if req.pages:
-            self.alloc.give(np.asarray(req.pages, dtype=np.int32))
+            pages = np.asarray(req.pages, dtype=np.int64)
+            if self.tier is not None:
+                from .tiered_kv import HOST_BASE
+                host = pages[pages >= HOST_BASE]
+                if host.size:
+                    self.tier.free_host(host.tolist())
+                pages = pages[pages < HOST_BASE]
+            self.alloc.give(pages.astype(np.int32))
             req.pages = []
 
     def _preempt(self, victim: Request, plan: StepPlan) -> None:

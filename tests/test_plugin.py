@@ -42,7 +42,7 @@ class FakePlane:
 
 class Req:
     def __init__(self, rid, n, urgency):
-        self.rid, self.total_len, self.urgency = rid, n, urgency
+        self.rid, self.total_len, self.urgency, self.tau = rid, n, urgency, 0
 
 
 class Plan:
