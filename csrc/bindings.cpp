@@ -45,6 +45,12 @@ int sched_moe_combine_norm(const void *c, int K, void *h, const void *w, void *y
                            int *status, cudaStream_t st);
 }
 #include "moe_api.h"
+extern "C" int sched_probe_stream(const void *src, size_t bytes, int policy, unsigned *sink, int grid,
+                                  cudaStream_t st);
+extern "C" int sched_probe_tasks(const uint32_t *cost, int n_tasks, int mode, int grid, int memory,
+                                 const void *data, size_t data_bytes, unsigned *hits, unsigned *per_cta,
+                                 unsigned *ticket, unsigned *sink, int *status, cudaStream_t st);
+extern "C" int sched_probe_tasks_occupancy();
 extern "C" int sched_kv_page_copy(const void *src_k, const void *src_v, long long src_pages, void *dst_k,
                                   void *dst_v, long long dst_pages, const int32_t *pairs, int n_pairs,
                                   int layers, int heads, cudaStream_t st);
@@ -422,6 +428,28 @@ void moe_combine_norm(int64_t c, int64_t K, at::Tensor &h, const at::Tensor &w, 
            "moe_combine_norm");
 }
 
+void probe_stream(const at::Tensor &src, int64_t policy, at::Tensor &sink, int64_t grid) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "src on the device");
+  c10::cuda::CUDAGuard g(src.device());
+  check_rc(sched_probe_stream(src.data_ptr(), src.numel() * src.element_size(), policy,
+                              reinterpret_cast<unsigned *>(sink.data_ptr()), grid, cur_stream()),
+           "probe_stream");
+}
+
+void probe_tasks(const at::Tensor &cost, int64_t mode, int64_t grid, int64_t memory, const at::Tensor &data,
+                 at::Tensor &hits, at::Tensor &per_cta, at::Tensor &ticket, at::Tensor &sink,
+                 const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(cost.is_cuda() && cost.scalar_type() == at::kInt, "cost int32 on the device");
+  c10::cuda::CUDAGuard g(cost.device());
+  check_rc(sched_probe_tasks(reinterpret_cast<const uint32_t *>(cost.data_ptr()), cost.numel(), mode, grid, memory,
+                             data.data_ptr(), data.numel() * data.element_size(),
+                             reinterpret_cast<unsigned *>(hits.data_ptr()),
+                             reinterpret_cast<unsigned *>(per_cta.data_ptr()),
+                             reinterpret_cast<unsigned *>(ticket.data_ptr()),
+                             reinterpret_cast<unsigned *>(sink.data_ptr()), ptr_or_null<int>(status), cur_stream()),
+           "probe_tasks");
+}
+
 // Page moves between KV pools (device <-> pinned host); pairs [n, 2] int32 on the device.
 void kv_page_copy(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &dst_k, at::Tensor &dst_v,
                   const at::Tensor &pairs, int64_t n_pairs) {
@@ -464,6 +492,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("moe_router", &moe_router);
   m.def("kv_page_copy", &kv_page_copy);
+  m.def("probe_stream", &probe_stream);
+  m.def("probe_tasks", &probe_tasks);
+  m.def("probe_tasks_occupancy", &sched_probe_tasks_occupancy);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_expert_gemm", &moe_expert_gemm);
   m.def("moe_quantize", &moe_quantize);
