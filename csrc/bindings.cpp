@@ -18,7 +18,8 @@ int sched_attn_decode(const void *q, void *out, const void *k_cache, const void 
                       int num_items, int Hq, int Hkv, float sm_scale, float *part_o,
                       float *part_lse, uint32_t *merge_cnt, int splits, SchedSlots slots,
                       int woven, int acquire, int grid, int pf_blocks, float dT, float dR,
-                      float H, int *status, cudaStream_t st);
+                      float H, const void *stage_k, const void *stage_v, int stage_pages,
+                      int stage_split, int *status, cudaStream_t st);
 int sched_attn_merge(const float *part_o, const float *part_lse, const int32_t *merge_req,
                      const int32_t *merge_begin, int rows, int Hq, void *out, cudaStream_t st);
 int sched_attn_decode_occupancy(int group);
@@ -53,7 +54,7 @@ extern "C" int sched_probe_tasks(const uint32_t *cost, int n_tasks, int mode, in
 extern "C" int sched_probe_tasks_occupancy();
 extern "C" int sched_kv_page_copy(const void *src_k, const void *src_v, long long src_pages, void *dst_k,
                                   void *dst_v, long long dst_pages, const int32_t *pairs, int n_pairs,
-                                  int layers, int heads, cudaStream_t st);
+                                  const int *n_dev, int layers, int heads, cudaStream_t st);
 
 namespace {
 
@@ -216,10 +217,17 @@ void attn_decode(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache
                  const c10::optional<at::Tensor> &timer, const c10::optional<at::Tensor> &queue,
                  int64_t max_tasks, int64_t woven, int64_t acquire, int64_t grid,
                  int64_t pf_blocks, double dT, double dR, double H,
-                 const c10::optional<at::Tensor> &status) {
+                 const c10::optional<at::Tensor> &stage_k, const c10::optional<at::Tensor> &stage_v,
+                 int64_t stage_split, const c10::optional<at::Tensor> &status) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   check_bf16(k_cache, "k_cache");
+  const bool staged = stage_k.has_value() && stage_k->defined();
+  if (staged) {
+    TORCH_CHECK(stage_v.has_value() && stage_v->defined() && stage_k->is_contiguous() && stage_v->is_contiguous() &&
+                    stage_k->dim() == 4 && stage_k->size(1) == k_cache.size(1),
+                "staging pool [pages, Hkv, 16, 128]");
+  }
   check_bf16(v_cache, "v_cache");
   check_i32(block_table, "block_table");
   check_i32(items, "items");
@@ -237,8 +245,9 @@ void attn_decode(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache
                              (float)sm_scale, ptr_or_null<float>(part_o),
                              ptr_or_null<float>(part_lse), ptr_or_null<uint32_t>(merge_cnt),
                              splits, sl, woven, acquire, grid, pf_blocks,
-                             (float)dT, (float)dR, (float)H, ptr_or_null<int>(status),
-                             cur_stream()),
+                             (float)dT, (float)dR, (float)H, staged ? stage_k->data_ptr() : nullptr,
+                             staged ? stage_v->data_ptr() : nullptr, staged ? (int)stage_k->size(0) : 0,
+                             (int)stage_split, ptr_or_null<int>(status), cur_stream()),
            "attn_decode");
 }
 
@@ -451,16 +460,17 @@ void probe_tasks(const at::Tensor &cost, int64_t mode, int64_t grid, int64_t mem
 }
 
 // Page moves between KV pools (device <-> pinned host); pairs [n, 2] int32 on the device.
+// With n_dev (int32 [1] on the device) n_pairs is a capacity and the count is read there.
 void kv_page_copy(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &dst_k, at::Tensor &dst_v,
-                  const at::Tensor &pairs, int64_t n_pairs) {
+                  const at::Tensor &pairs, int64_t n_pairs, const c10::optional<at::Tensor> &n_dev) {
   TORCH_CHECK(src_k.dim() == 5 && dst_k.dim() == 5, "pools are [layers, pages, heads, 16, 128]");
   TORCH_CHECK(src_k.size(0) == dst_k.size(0) && src_k.size(2) == dst_k.size(2), "pool shapes differ");
   TORCH_CHECK(src_k.is_contiguous() && src_v.is_contiguous() && dst_k.is_contiguous() && dst_v.is_contiguous(),
               "contiguous pools");
   TORCH_CHECK(pairs.is_cuda() && pairs.scalar_type() == at::kInt && pairs.is_contiguous(), "pairs int32 on device");
   check_rc(sched_kv_page_copy(src_k.data_ptr(), src_v.data_ptr(), src_k.size(1), dst_k.data_ptr(), dst_v.data_ptr(),
-                              dst_k.size(1), pairs.data_ptr<int32_t>(), n_pairs, src_k.size(0), src_k.size(2),
-                              cur_stream()),
+                              dst_k.size(1), pairs.data_ptr<int32_t>(), n_pairs, ptr_or_null<int>(n_dev),
+                              src_k.size(0), src_k.size(2), cur_stream()),
            "kv_page_copy");
 }
 

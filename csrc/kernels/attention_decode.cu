@@ -86,6 +86,7 @@ struct Params {
   uint32_t *merge_cnt;  // [requests * Hkv] arrival counters (zero between calls), or null
   int splits;           // chunks per request when merging in-kernel (part = req * splits + s)
   int total_rows;       // rows of the cache tensor maps: pages * Hkv * 16 (an out-of-range row)
+  int stage_split;      // block-table ids >= this name pages of the staging pool (tmK2/tmV2)
   SchedSlots slots;
   sched::PolicyConsts pc;
   int pf_blocks;  // urgent prefetch distance in KV blocks
@@ -117,6 +118,7 @@ __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t byte_in_row) {
 template <int G, bool WOVEN, int ACQ>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                  const __grid_constant__ CUtensorMap tmK2, const __grid_constant__ CUtensorMap tmV2,
                   const Params p) {
   static_assert(G >= 1 && G <= NPAD, "group size");
   extern __shared__ uint8_t smem_raw[];
@@ -244,21 +246,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::mbar_arrive_expect_tx(&sh.k_full[s], KV_BLOCK_BYTES);
           ptx::mbar_arrive_expect_tx(&sh.v_full[s], KV_BLOCK_BYTES);
           for (int pi = 0; pi < PAGES_PER_BLK; ++pi) {
-            // pages past the request's end: an out-of-range box reads zeros
-            const int row = pi < npg ? (__ldg(bt + pg0 + pi) * p.Hkv + ti.kvh) * PS : p.total_rows;
+            // pages past the request's end: an out-of-range box reads zeros;
+            // ids from stage_split on live in the staging pool (tiered KV)
+            const int page = pi < npg ? __ldg(bt + pg0 + pi) : -1;
+            const bool staged = page >= p.stage_split;
+            const int row = page < 0 ? p.total_rows
+                                     : ((staged ? page - p.stage_split : page) * p.Hkv + ti.kvh) * PS;
+            const CUtensorMap *mk = staged ? &tmK2 : &tmK;
+            const CUtensorMap *mv = staged ? &tmV2 : &tmV;
             uint8_t *kd = kst + pi * PS * 128;
             uint8_t *vd = vst + pi * PS * 128;
             if (WOVEN && ti.prio != 0) {
               const uint64_t pol = ti.prio == 1 ? pol_last : pol_first;
-              ptx::tma_load_2d_hint(kd, &tmK, &sh.k_full[s], 0, row, pol);
-              ptx::tma_load_2d_hint(kd + HALF, &tmK, &sh.k_full[s], 64, row, pol);
-              ptx::tma_load_2d_hint(vd, &tmV, &sh.v_full[s], 0, row, pol);
-              ptx::tma_load_2d_hint(vd + HALF, &tmV, &sh.v_full[s], 64, row, pol);
+              ptx::tma_load_2d_hint(kd, mk, &sh.k_full[s], 0, row, pol);
+              ptx::tma_load_2d_hint(kd + HALF, mk, &sh.k_full[s], 64, row, pol);
+              ptx::tma_load_2d_hint(vd, mv, &sh.v_full[s], 0, row, pol);
+              ptx::tma_load_2d_hint(vd + HALF, mv, &sh.v_full[s], 64, row, pol);
             } else {
-              ptx::tma_load_2d(kd, &tmK, &sh.k_full[s], 0, row);
-              ptx::tma_load_2d(kd + HALF, &tmK, &sh.k_full[s], 64, row);
-              ptx::tma_load_2d(vd, &tmV, &sh.v_full[s], 0, row);
-              ptx::tma_load_2d(vd + HALF, &tmV, &sh.v_full[s], 64, row);
+              ptx::tma_load_2d(kd, mk, &sh.k_full[s], 0, row);
+              ptx::tma_load_2d(kd + HALF, mk, &sh.k_full[s], 64, row);
+              ptx::tma_load_2d(vd, mv, &sh.v_full[s], 0, row);
+              ptx::tma_load_2d(vd + HALF, mv, &sh.v_full[s], 64, row);
             }
           }
           // urgent: warm L2 with the pages pf_blocks ahead (pure hint)
@@ -266,11 +274,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int pf0 = pg0 + p.pf_blocks * PAGES_PER_BLK;
             const int pfn = min(PAGES_PER_BLK, last_page - pf0);
             for (int pi = 0; pi < pfn; ++pi) {
-              const int row = (__ldg(bt + pf0 + pi) * p.Hkv + ti.kvh) * PS;
-              ptx::tma_prefetch_2d(&tmK, 0, row);
-              ptx::tma_prefetch_2d(&tmK, 64, row);
-              ptx::tma_prefetch_2d(&tmV, 0, row);
-              ptx::tma_prefetch_2d(&tmV, 64, row);
+              const int page = __ldg(bt + pf0 + pi);
+              const bool staged = page >= p.stage_split;
+              const int row = ((staged ? page - p.stage_split : page) * p.Hkv + ti.kvh) * PS;
+              const CUtensorMap *mk = staged ? &tmK2 : &tmK;
+              const CUtensorMap *mv = staged ? &tmV2 : &tmV;
+              ptx::tma_prefetch_2d(mk, 0, row);
+              ptx::tma_prefetch_2d(mk, 64, row);
+              ptx::tma_prefetch_2d(mv, 0, row);
+              ptx::tma_prefetch_2d(mv, 64, row);
             }
           }
         }
@@ -598,8 +610,8 @@ __global__ void merge_kernel(const float *part_o, const float *part_lse, const i
 }
 
 template <int G, bool WOVEN, int ACQ>
-static int launch(const CUtensorMap &tk, const CUtensorMap &tv, const Params &p, int grid,
-                  cudaStream_t st) {
+static int launch(const CUtensorMap &tk, const CUtensorMap &tv, const CUtensorMap &tk2,
+                  const CUtensorMap &tv2, const Params &p, int grid, cudaStream_t st) {
   auto kern = decode_kernel<G, WOVEN, ACQ>;
   static bool attr = false;
   if (!attr) {
@@ -617,21 +629,22 @@ static int launch(const CUtensorMap &tk, const CUtensorMap &tv, const Params &p,
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaLaunchKernelEx(&cfg, kern, tk, tv, p);
+    cudaLaunchKernelEx(&cfg, kern, tk, tv, tk2, tv2, p);
   } else {
-    kern<<<grid, kThreads, SMEM, st>>>(tk, tv, p);
+    kern<<<grid, kThreads, SMEM, st>>>(tk, tv, tk2, tv2, p);
   }
   return 0;
 }
 
 template <int G>
 static int dispatch_acq(bool woven, int acq, const CUtensorMap &tk, const CUtensorMap &tv,
-                        const Params &p, int grid, cudaStream_t st) {
-  if (!woven) return launch<G, false, 0>(tk, tv, p, grid, st);
+                        const CUtensorMap &tk2, const CUtensorMap &tv2, const Params &p, int grid,
+                        cudaStream_t st) {
+  if (!woven) return launch<G, false, 0>(tk, tv, tk2, tv2, p, grid, st);
   switch (acq) {
-    case 1: return launch<G, true, 1>(tk, tv, p, grid, st);
-    case 2: return launch<G, true, 2>(tk, tv, p, grid, st);
-    default: return launch<G, true, 0>(tk, tv, p, grid, st);
+    case 1: return launch<G, true, 1>(tk, tv, tk2, tv2, p, grid, st);
+    case 2: return launch<G, true, 2>(tk, tv, tk2, tv2, p, grid, st);
+    default: return launch<G, true, 0>(tk, tv, tk2, tv2, p, grid, st);
   }
 }
 
@@ -667,8 +680,10 @@ extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
                                  float sm_scale, float *part_o, float *part_lse,
                                  uint32_t *merge_cnt, int splits, SchedSlots slots, int woven,
                                  int acquire, int grid, int pf_blocks, float dT, float dR, float H,
-                                 int *status, cudaStream_t st) {
+                                 const void *stage_k, const void *stage_v, int stage_pages,
+                                 int stage_split, int *status, cudaStream_t st) {
   if (num_items <= 0) return 0;
+  if (stage_k != nullptr && (stage_v == nullptr || stage_pages <= 0 || stage_split <= 0)) return -1;
   const int G = Hq / Hkv;
   if (Hq % Hkv != 0 || (G != 1 && G != 2 && G != 4 && G != 8)) return -1;
   attn::Params p;
@@ -687,6 +702,7 @@ extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
   p.merge_cnt = merge_cnt;
   p.splits = splits > 0 ? splits : 1;
   p.total_rows = num_pages * Hkv * attn::PS;
+  p.stage_split = stage_k != nullptr ? stage_split : 0x7fffffff;
   p.slots = slots;
   p.pc.dT = dT;
   p.pc.dR = dR;
@@ -700,11 +716,19 @@ extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
                                    attn::D, attn::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     CUtensorMap tv = tmap::make_2d(v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, attn::D,
                                    attn::D, attn::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap tk2 = tk, tv2 = tv;
+    if (stage_k != nullptr) {
+      const uint64_t srows = (uint64_t)stage_pages * Hkv * attn::PS;
+      tk2 = tmap::make_2d(stage_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, srows, attn::D, attn::D, attn::PS, 64,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+      tv2 = tmap::make_2d(stage_v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, srows, attn::D, attn::D, attn::PS, 64,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    }
     switch (G) {
-      case 1: attn::dispatch_acq<1>(woven, acquire, tk, tv, p, grid, st); break;
-      case 2: attn::dispatch_acq<2>(woven, acquire, tk, tv, p, grid, st); break;
-      case 8: attn::dispatch_acq<8>(woven, acquire, tk, tv, p, grid, st); break;
-      default: attn::dispatch_acq<4>(woven, acquire, tk, tv, p, grid, st); break;
+      case 1: attn::dispatch_acq<1>(woven, acquire, tk, tv, tk2, tv2, p, grid, st); break;
+      case 2: attn::dispatch_acq<2>(woven, acquire, tk, tv, tk2, tv2, p, grid, st); break;
+      case 8: attn::dispatch_acq<8>(woven, acquire, tk, tv, tk2, tv2, p, grid, st); break;
+      default: attn::dispatch_acq<4>(woven, acquire, tk, tv, tk2, tv2, p, grid, st); break;
     }
   } catch (const std::exception &) {
     return -3;

@@ -62,7 +62,7 @@ class EngineConfig:
     seed: int = 0
     verbose: bool = False           # print the scheduling plugin's effective config
     host_kv_pages: int = 0          # tiered KV: pinned host pages the device pool spills to (0 = off)
-    kv_staging_pages: int = 0       # device pages a step may stage host-resident KV into
+    kv_staging_pages: int = 0       # staging slots (one layer of a host page each; 0 = host_kv_pages)
 
 
 @dataclass
@@ -90,12 +90,12 @@ class Engine:
         self.max_pages_per_req = (e.max_context + 15) // 16
         if not e.num_pages:
             e.num_pages = e.max_batch * self.max_pages_per_req + 64
-        n_stage = e.kv_staging_pages if e.host_kv_pages else 0
-        self.kv = KVCache(cfg, e.num_pages + n_stage, self.device, tp_size=tp_size)
+        self.kv = KVCache(cfg, e.num_pages, self.device, tp_size=tp_size)
         self.tier = None
         if e.host_kv_pages:
             from .tiered_kv import TieredKV
-            self.tier = TieredKV(self.kv, e.num_pages, n_stage, e.host_kv_pages, self.device)
+            self.tier = TieredKV(self.kv, e.num_pages, e.kv_staging_pages or e.host_kv_pages,
+                                 e.host_kv_pages, self.device)
         if weights is None:
             weights = init_weights(cfg, self.device, tp_rank, tp_size, seed=e.seed,
                                    moe_builder=getattr(model_factory, "moe_builder", None))
@@ -295,6 +295,7 @@ class Engine:
             tiles=self._view("tiles", (-1, 4)), n_tiles=info["n_tiles"],
             sample_idx=self.sample_idx64, n_sample=info["n_sample"], out_ids=self.out_ids,
             slots=slots, acquire=self._acq_code(), grid=self._grid(n_items * self.hkv),
+            tier=self.tier if (self.tier is not None and nd > 0) else None,
         )
 
     def _grid(self, n_tasks: int) -> int:

@@ -1,13 +1,11 @@
-"""Tiered KV store: the device page pool spills to pinned host memory.
+"""Tiered KV store: the device page pool spills to pinned host memory, and
+the spilled pages a step reads stream back one layer at a time.
 
-Pages live in one of three places:
+Pages live in one of two pools:
 
 * device pages ``[0, n_device)`` -- handed out by the scheduler's allocator;
 * host pages, named ``HOST_BASE + h`` in a request's page list -- a pinned
-  host pool with the device pool's layout ([layers, pages, heads, 16, 128]);
-* staging pages ``[n_device, n_device + n_staging)`` of the device pool --
-  never owned by a request: each step copies the host pages that step reads
-  into them, and the step's block table points there.
+  host pool with the device pool's layout ([layers, pages, heads, 16, 128]).
 
 Spilling happens when the allocator runs dry (the scheduler calls ``spill``
 before it would preempt anyone). Victims are chosen by the scheduling
@@ -19,15 +17,22 @@ plane's own signals, in this order:
    oldest first.
 
 A request's last page (where the next token's K/V is appended) and requests
-still in prefill are never spilled. Each step, ``stage`` gathers the host
-pages inside every decode request's read horizon into staging pages, in the
-order the decode kernel will claim their tasks (most urgent request first,
-the order pi and the policy rows favour), and launches one copy kernel over
-PCIe on the engine's stream, so the step's kernels run after it.
+still in prefill are never spilled.
 
-The copies are ``csrc/kernels/kv_tier.cu`` (zero-copy loads/stores of the
-mapped pinned pool). The reference names KV tiering as its unbuilt "MOVE"
-lever (ROADMAP.md:462-482 of jc-su/sched-pass); this is the mechanism.
+Each step, ``stage`` gives every host page inside a decode request's read
+horizon a staging slot ``s`` and writes ``split + s`` into the step's block
+table (``split`` = the device pool's page count; the decode kernel reads
+ids >= split from a second, staging pool). Slots are assigned in the order
+the decode kernel claims its tasks (most urgent request first). The staging
+pool holds ONE layer: two buffers alternate between even and odd layers, so
+layer l's pages are copied over PCIe (``csrc/kernels/kv_tier.cu``, zero-copy
+loads of the mapped pinned pool, on a side stream) while layer l-1 computes,
+and the copy for layer l+2 waits until layer l's attention has read the
+buffer. Staging costs 2 x slots x one layer's page of device memory, so the
+read set of a step may exceed HBM (the 70B / 131k-context configuration).
+
+The reference names KV tiering as its unbuilt "MOVE" lever
+(ROADMAP.md:462-482 of jc-su/sched-pass); this is the mechanism.
 """
 from __future__ import annotations
 
@@ -49,23 +54,33 @@ class TieredKV:
     def __init__(self, kv, n_device: int, n_staging: int, n_host: int, device):
         self.kv = kv
         self.n_device = int(n_device)
-        self.n_staging = int(n_staging)
+        self.n_staging = max(1, int(n_staging))
         self.n_host = int(n_host)
         self.device = torch.device(device)
-        if kv.num_pages < self.n_device + self.n_staging:
-            raise ValueError("the device KV pool must hold the allocator's pages plus the staging pages")
+        if kv.num_pages < self.n_device:
+            raise ValueError("the device KV pool is smaller than the allocator's page count")
+        self.split = kv.num_pages  # block-table ids >= split name staging slots
         L, _, H, P, D = kv.k.shape
-        shape = (L, self.n_host, H, P, D)
-        pin = self.device.type == "cuda"
-        self.host_k = torch.zeros(shape, dtype=kv.k.dtype, pin_memory=pin)
-        self.host_v = torch.zeros(shape, dtype=kv.v.dtype, pin_memory=pin)
+        self.layers = L
+        on_cuda = self.device.type == "cuda"
+        self.host_k = torch.zeros((L, self.n_host, H, P, D), dtype=kv.k.dtype, pin_memory=on_cuda)
+        self.host_v = torch.zeros((L, self.n_host, H, P, D), dtype=kv.v.dtype, pin_memory=on_cuda)
+        # two one-layer staging buffers (even / odd layers)
+        self.stage_k = torch.zeros((2, self.n_staging, H, P, D), dtype=kv.k.dtype, device=self.device)
+        self.stage_v = torch.zeros_like(self.stage_k)
         self._free_host = list(range(self.n_host - 1, -1, -1))
         self.spilled_pages = 0
         self.staged_pages = 0
         self.last_stage = 0
-        self._pairs_dev = torch.zeros(max(1, self.n_staging) * 2, dtype=torch.int32, device=self.device)
-        self._pairs_host = torch.zeros(max(1, self.n_staging) * 2, dtype=torch.int32, pin_memory=pin)
+        cap = 2 * self.n_staging
+        self.pairs_dev = torch.zeros(cap, dtype=torch.int32, device=self.device)  # (host page, slot)
+        self.count_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._pairs_pin = torch.zeros(cap + 1, dtype=torch.int32, pin_memory=on_cuda)
+        self._spill_dev = torch.zeros(2, dtype=torch.int32, device=self.device)
         self._translation: dict = {}
+        self._stream = torch.cuda.Stream(self.device) if on_cuda else None
+        self._ev_fetch = [torch.cuda.Event() for _ in range(2)] if on_cuda else None
+        self._ev_read = [torch.cuda.Event() for _ in range(2)] if on_cuda else None
 
     # ------------------------------------------------------------ host pool
     @property
@@ -126,18 +141,26 @@ class TieredKV:
             pairs.append((d, h))
             r.pages[i] = HOST_BASE + h
             freed.append(d)
-        self._copy(self.kv.k, self.kv.v, self.host_k, self.host_v, pairs)
+        self._copy_all_layers(self.kv.k, self.kv.v, self.host_k, self.host_v, pairs)
         self.spilled_pages += len(pairs)
         return freed
 
+    def _copy_all_layers(self, src_k, src_v, dst_k, dst_v, pairs) -> None:
+        n = len(pairs)
+        arr = torch.from_numpy(np.asarray(pairs, dtype=np.int32).reshape(-1))
+        if n * 2 > self._spill_dev.numel():
+            self._spill_dev = torch.zeros(n * 2, dtype=torch.int32, device=self.device)
+        self._spill_dev[: n * 2].copy_(arr)  # pageable source: a synchronous copy
+        ext().kv_page_copy(src_k, src_v, dst_k, dst_v, self._spill_dev, n, None)
+
     # ------------------------------------------------------------ staging
     def stage(self, decode_requests) -> None:
-        """Copy the host pages each decode request reads this step into
-        staging pages; ``pages_for`` then gives the translated page list."""
+        """Give each host page a decode request reads this step a staging
+        slot (most urgent request first) and publish the pairs for the
+        per-layer copies; ``pages_for`` gives the translated page list."""
         self._translation.clear()
         pairs = []
-        nxt = self.n_device
-        for r in sorted(decode_requests, key=lambda r: -r.urgency):  # most urgent first
+        for r in sorted(decode_requests, key=lambda r: -r.urgency):
             if not any(is_host(p) for p in r.pages):
                 continue
             hz = self.horizon_pages(r)
@@ -148,34 +171,64 @@ class TieredKV:
                 if i >= hz:
                     tr[i] = 0  # never read this step: any valid device page
                     continue
-                if nxt >= self.n_device + self.n_staging:
+                if len(pairs) >= self.n_staging:
                     raise RuntimeError(
                         f"this step reads more host-resident KV pages than the {self.n_staging} staging "
-                        "pages hold; raise kv_staging_pages (or spill less)")
-                pairs.append((int(p) - HOST_BASE, nxt))
-                tr[i] = nxt
-                nxt += 1
+                        "slots hold; raise kv_staging_pages (or spill less)")
+                tr[i] = self.split + len(pairs)
+                pairs.append((int(p) - HOST_BASE, len(pairs)))
             self._translation[id(r)] = tr
-        self.last_stage = len(pairs)
-        if pairs:
-            self._copy(self.host_k, self.host_v, self.kv.k, self.kv.v, pairs)
-            self.staged_pages += len(pairs)
+        n = len(pairs)
+        self.last_stage = n
+        self.staged_pages += n
+        buf = self._pairs_pin.numpy()
+        buf[0] = n
+        if n:
+            buf[1:1 + 2 * n] = np.asarray(pairs, dtype=np.int32).reshape(-1)
+        self.count_dev.copy_(self._pairs_pin[:1], non_blocking=True)
+        if n:
+            self.pairs_dev[: 2 * n].copy_(self._pairs_pin[1:1 + 2 * n], non_blocking=True)
+        # the pinned buffer is rewritten next step: let these copies finish
+        # (the engine synchronises once per step anyway)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
 
     def pages_for(self, req):
         return self._translation.get(id(req), req.pages)
 
-    # ------------------------------------------------------------ copies
-    def _copy(self, src_k, src_v, dst_k, dst_v, pairs) -> None:
-        n = len(pairs)
-        if n == 0:
+    # ------------------------------------------------------------ per-layer streaming
+    def _fetch(self, layer: int) -> None:
+        b = layer & 1
+        ext().kv_page_copy(self.host_k[layer:layer + 1], self.host_v[layer:layer + 1],
+                           self.stage_k[b:b + 1], self.stage_v[b:b + 1], self.pairs_dev, self.n_staging,
+                           self.count_dev)
+
+    def begin_forward(self) -> None:
+        """Fork the copy stream and start the copies of layers 0 and 1."""
+        main = torch.cuda.current_stream(self.device)
+        self._stream.wait_stream(main)
+        with torch.cuda.stream(self._stream):
+            for layer in range(min(2, self.layers)):
+                self._fetch(layer)
+                self._ev_fetch[layer & 1].record(self._stream)
+
+    def before_attention(self, layer: int):
+        """Wait for this layer's pages; returns the decode kernel's staging pool."""
+        b = layer & 1
+        torch.cuda.current_stream(self.device).wait_event(self._ev_fetch[b])
+        return (self.stage_k[b], self.stage_v[b], self.split)
+
+    def after_attention(self, layer: int) -> None:
+        """Layer ``layer`` has read its buffer: refill it for ``layer + 2``."""
+        b = layer & 1
+        nxt = layer + 2
+        if nxt >= self.layers:
             return
-        arr = np.asarray(pairs, dtype=np.int32).reshape(-1)
-        if n * 2 > self._pairs_host.numel():
-            self._pairs_host = torch.zeros(n * 2, dtype=torch.int32, pin_memory=self._pairs_host.is_pinned())
-            self._pairs_dev = torch.zeros(n * 2, dtype=torch.int32, device=self.device)
-        self._pairs_host[: n * 2].numpy()[:] = arr
-        self._pairs_dev[: n * 2].copy_(self._pairs_host[: n * 2], non_blocking=True)
-        ext().kv_page_copy(src_k, src_v, dst_k, dst_v, self._pairs_dev, n)
-        # the pinned staging of the pairs is rewritten by the next call: keep
-        # the host from getting ahead of the copy that reads it
-        torch.cuda.current_stream(self.device).synchronize()
+        self._ev_read[b].record(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self._stream):
+            self._stream.wait_event(self._ev_read[b])
+            self._fetch(nxt)
+            self._ev_fetch[b].record(self._stream)
+
+    def end_forward(self) -> None:
+        torch.cuda.current_stream(self.device).wait_stream(self._stream)

@@ -190,6 +190,8 @@ class ForwardBatch:
     slots: dict | None = None
     acquire: int = 0
     grid: int = 0
+    # tiered KV: per-layer staging of host-resident pages (engine/tiered_kv.py)
+    tier: object = None
 
 
 class KVCache:
@@ -253,10 +255,13 @@ class Llama:
         if nd > 0:
             q = self.q[:nd]
             out = self.attn[:nd]
+            stage = b.tier.before_attention(li) if b.tier is not None else None
             ops.attention_decode(q, out, kc, vc, b.block_table, b.items, b.n_items, self.sm_scale,
                                  part_o=b.part_o, part_lse=b.part_lse, merge_cnt=b.merge_cnt,
                                  splits=b.splits, slots=b.slots, woven=b.slots is not None,
-                                 acquire=b.acquire, grid=b.grid)
+                                 acquire=b.acquire, grid=b.grid, stage=stage)
+            if b.tier is not None:
+                b.tier.after_attention(li)
             if b.n_merge > 0 and b.merge_cnt is None:
                 ops.attention_merge(b.part_o, b.part_lse, b.merge_req, b.merge_begin, b.n_merge, out)
         if b.n_tiles > 0:
@@ -274,6 +279,8 @@ class Llama:
         T = b.n_tokens
         h, normed, delta = self.h[:T], self.normed[:T], self.delta[:T]
         ops.embedding(b.ids[:T], self.w.embed, h)
+        if b.tier is not None:
+            b.tier.begin_forward()
         for li, lw in enumerate(self.w.layers):
             if li == 0:
                 ops.add_rmsnorm(h, None, lw.ln_in, cfg.rms_eps, normed)
@@ -287,6 +294,8 @@ class Llama:
             d = self._mlp(li, normed, T)
             if d is not delta:
                 delta.copy_(d)
+        if b.tier is not None:
+            b.tier.end_forward()
         ops.add_rmsnorm(delta, h, self.w.ln_final, cfg.rms_eps, normed)
         return self.sample(b)
 

@@ -26,6 +26,8 @@ class Mixtral(Llama):
         layers = self.w.layers
         ops.embedding(b.ids[:T], self.w.embed, h)
         ops.add_rmsnorm(h, None, layers[0].ln_in, cfg.rms_eps, normed)
+        if b.tier is not None:
+            b.tier.begin_forward()
         for li, lw in enumerate(layers):
             ops.linear_qkv_rope(normed, lw.qkv, b.pos[:T], b.slot[:T], self.cos_sin, self.q[:T],
                                 self.kv.k[li], self.kv.v[li], self.hq, self.hkv)
@@ -34,6 +36,8 @@ class Mixtral(Llama):
             ops.add_rmsnorm(delta, h, lw.ln_post, cfg.rms_eps, normed)
             nxt = layers[li + 1].ln_in if li + 1 < len(layers) else self.w.ln_final
             self.ep.layer(lw.moe, normed, h, nxt, normed, cfg.rms_eps)
+        if b.tier is not None:
+            b.tier.end_forward()
         return self.sample(b)
 
 

@@ -19,13 +19,13 @@ def test_page_copy_roundtrip_through_pinned_host():
     hk = torch.zeros(L, 6, H, 16, 128, dtype=torch.bfloat16, pin_memory=True)
     hv = torch.zeros_like(hk, pin_memory=True)
     pairs = torch.tensor([[7, 0], [2, 5], [9, 3]], dtype=torch.int32, device="cuda")
-    ext().kv_page_copy(k, v, hk, hv, pairs, 3)
+    ext().kv_page_copy(k, v, hk, hv, pairs, 3, None)
     torch.cuda.synchronize()
     for s, d in ((7, 0), (2, 5), (9, 3)):
         assert torch.equal(hk[:, d], k[:, s].cpu()) and torch.equal(hv[:, d], v[:, s].cpu())
     k2, v2 = torch.zeros_like(k), torch.zeros_like(v)
     back = torch.tensor([[0, 1], [5, 4], [3, 8]], dtype=torch.int32, device="cuda")
-    ext().kv_page_copy(hk, hv, k2, v2, back, 3)
+    ext().kv_page_copy(hk, hv, k2, v2, back, 3, None)
     torch.cuda.synchronize()
     assert torch.equal(k2[:, 1], k[:, 7]) and torch.equal(v2[:, 8], v[:, 9])
 

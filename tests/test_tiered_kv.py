@@ -1,7 +1,8 @@
 """Tiered KV bookkeeping on the CPU: spill order (never-read pages first,
-then least urgent), the appended page stays on the device, staging
-translation, host pages returned on release. The page copies run as torch
-copies here (the CUDA kernel is covered by the GPU tests)."""
+then least urgent), the appended page stays on the device, staging slots
+and the published copy pairs, host pages returned on release. The page
+copies run as torch copies here (the CUDA kernel and the per-layer
+streaming are covered by the GPU tests)."""
 import numpy as np
 import pytest
 import torch
@@ -20,11 +21,11 @@ def cpu_copy(src_k, src_v, dst_k, dst_v, pairs):
 
 
 def make(n_device=40, n_staging=16, n_host=64):
-    kv = KVCache(LLAMA_TINY, n_device + n_staging, "cpu")
+    kv = KVCache(LLAMA_TINY, n_device, "cpu")
     kv.k.copy_(torch.arange(kv.k.numel(), dtype=torch.float32).reshape(kv.k.shape).to(torch.bfloat16))
     kv.v.copy_(-kv.k)
     tier = TieredKV(kv, n_device, n_staging, n_host, "cpu")
-    tier._copy = cpu_copy
+    tier._copy_all_layers = cpu_copy
     sched = Scheduler(n_device, 16, 8, 256, 4096, tier=tier)
     return kv, tier, sched
 
@@ -69,10 +70,14 @@ def test_stage_translates_read_pages_and_release_returns_host_pages():
     assert host_idx
     tier.stage([a, b])
     tr = tier.pages_for(b)
+    pairs = tier._pairs_pin.numpy()
+    n = int(pairs[0])
+    assert n == len(host_idx) and tier.last_stage == n
+    got = {int(pairs[2 + 2 * j]): int(pairs[1 + 2 * j]) for j in range(n)}  # slot -> host page
     for i in host_idx:
-        s = tr[i]
-        assert 40 <= s < 56
-        assert torch.equal(kv.k[:, s], tier.host_k[:, b.pages[i] - HOST_BASE])
+        slot = tr[i] - tier.split
+        assert tier.split == 40 and 0 <= slot < 16
+        assert got[slot] == b.pages[i] - HOST_BASE
     assert tier.pages_for(a) == a.pages
     free0 = tier.host_free
     b.state = State.DONE
