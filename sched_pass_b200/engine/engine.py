@@ -372,6 +372,11 @@ class Engine:
         self.out_host[:ns].copy_(self.out_ids[:ns], non_blocking=True)
         ev1.synchronize()
         ms = ev0.elapsed_time(ev1)
+        if self.tp is not None and self.tp.world > 1:
+            # every tensor-parallel rank must make the same scheduling
+            # decisions (admissions follow the workload clock): advance all
+            # clocks by the slowest rank's step time
+            ms = self.tp.max_over_ranks(ms)
         self.clock += ms / 1e3
         self.hooks.end(self, plan, info, ms)
         out = self.out_host[:ns].numpy()

@@ -35,6 +35,17 @@ class TensorParallel:
             from .fused import FusedAllReduce
             self._fused = FusedAllReduce(self.group, self.device)
 
+    def max_over_ranks(self, value: float) -> float:
+        """The maximum of a host scalar over the group (one small collective)."""
+        if self.world == 1:
+            return float(value)
+        t = getattr(self, "_scalar", None)
+        if t is None:
+            t = self._scalar = torch.zeros(1, dtype=torch.float64, device=self.device)
+        t.fill_(float(value))
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        return float(t.item())
+
     def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return ops.linear(x, w, out)

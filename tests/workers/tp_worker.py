@@ -39,19 +39,22 @@ def main():
     ops.check_status()
     # engine: TP generation == single-GPU generation
     from sched_pass_b200.engine.engine import Engine, EngineConfig
-    from sched_pass_b200.models.config import LLAMA_TINY
+    from sched_pass_b200.models.config import LLAMA_TINY, ModelConfig
     from sched_pass_b200.models.llama import full_weights, shard_weights
-    full = full_weights(LLAMA_TINY, seed=5)
+    # heads must split evenly over the ranks (LLAMA_TINY has 2 KV heads)
+    cfg = LLAMA_TINY if LLAMA_TINY.n_kv_heads % world == 0 else ModelConfig(
+        "llama-tiny-kv8", 2, 512, 8, 8, 128, 1024, 1024)
+    full = full_weights(cfg, seed=5)
     rng = np.random.default_rng(0)
-    prompts = [rng.integers(0, LLAMA_TINY.vocab, size=int(n)).astype(np.int32) for n in (9, 70, 33)]
+    prompts = [rng.integers(0, cfg.vocab, size=int(n)).astype(np.int32) for n in (9, 70, 33)]
     ecfg = dict(max_batch=8, max_prefill_tokens=256, max_context=512)
-    eng = Engine(LLAMA_TINY, EngineConfig(**ecfg), dev, tp=tp,
-                 weights=shard_weights(LLAMA_TINY, full, rank, world, dev))
+    eng = Engine(cfg, EngineConfig(**ecfg), dev, tp=tp,
+                 weights=shard_weights(cfg, full, rank, world, dev))
     tp_out = eng.generate(prompts, max_new_tokens=5)
     del eng
     if rank == 0:
-        single = Engine(LLAMA_TINY, EngineConfig(**ecfg), dev,
-                        weights=shard_weights(LLAMA_TINY, full, 0, 1, dev))
+        single = Engine(cfg, EngineConfig(**ecfg), dev,
+                        weights=shard_weights(cfg, full, 0, 1, dev))
         ref_out = single.generate(prompts, max_new_tokens=5)
         out["first_token_match"] = [a[0] == b[0] for a, b in zip(tp_out, ref_out)]
         pairs = [(x, y) for a, b in zip(tp_out, ref_out) for x, y in zip(a, b)]
