@@ -54,6 +54,9 @@ constexpr int BLK = 128;               // tokens per KV block (MMA M)
 constexpr int PAGES_PER_BLK = BLK / PS;
 constexpr int NPAD = 16;               // MMA N (query heads, padded)
 constexpr int STAGES = 3;
+// The MMA warp issues S = K.Q^T of block b+1 before O = V^T.P^T of block b,
+// so two KV stages are in use at once: the ring needs at least two.
+static_assert(STAGES >= 2, "the S/O issue order needs two KV stages in flight");
 constexpr int kThreads = 192;
 constexpr int kSoftmaxThreads = 128;
 constexpr int HALF = BLK * 128;        // bytes of one 64-column half of a K or V block

@@ -58,7 +58,7 @@ class EngineConfig:
     clc_uncertainty: float = 0.75   # arm CLC above this estimator uncertainty (auto)
     shed_fraction: float = 0.0      # fraction of lowest-urgency requests given a tau
     shed_ratio: float = 0.5         # tau = ratio * context length
-    target_tasks: int = 0           # decode tasks to aim for (0 = 2 x SMs)
+    target_tasks: int = 0           # decode tasks to aim for (0 = one per SM)
     seed: int = 0
     verbose: bool = False           # print the scheduling plugin's effective config
     host_kv_pages: int = 0          # tiered KV: pinned host pages the device pool spills to (0 = off)
@@ -108,7 +108,7 @@ class Engine:
         self.sched = Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context, tier=self.tier)
         self.hkv = cfg.n_kv_heads // tp_size
         self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        self.target_tasks = e.target_tasks or 2 * self.sms
+        self.target_tasks = e.target_tasks or self.sms
         self._alloc_buffers(T)
         # scheduling control plane (device-resident tables)
         max_tasks = e.max_batch * 8 * self.hkv
@@ -183,8 +183,13 @@ class Engine:
             return self.sms
 
     def splits_for(self, n_decode: int) -> int:
+        """KV splits per request: only when the (request, KV head) tasks leave
+        SMs idle. A split task pays its own set-up and the merge of its
+        partials, so on B200 one task per (request, head) beats splitting as
+        soon as the tasks roughly fill the GPU (measured: 16 requests x 8
+        heads x 1536 tokens take 40 us unsplit, 55 us in 3 splits)."""
         tasks = max(1, n_decode * self.hkv)
-        return int(min(8, max(1, math.ceil(self.target_tasks / tasks))))
+        return int(min(8, max(1, self.target_tasks // tasks)))
 
     # ------------------------------------------------------------------ public API
     def add_request(self, req: Request) -> None:
