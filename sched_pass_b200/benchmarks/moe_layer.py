@@ -10,6 +10,11 @@ the bytes the layer must read: the weights of every expert that received a
 token plus the activations.
 
     python -m sched_pass_b200.benchmarks.moe_layer --tokens 128
+
+``--hot FRAC`` sends a fraction of the tokens to expert 0 (a shared component
+along its router row: the reference's hot-expert imbalance experiment), and
+``--capacity-factor CF`` caps every expert at CF x tokens x top_k / experts
+rows (the E2 capacity lever; the overflow is dropped and counted).
 """
 from __future__ import annotations
 
@@ -25,6 +30,8 @@ def main(argv=None):
     ap.add_argument("--tokens", type=int, default=128)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--hot", type=float, default=0.0, help="fraction of tokens routed to expert 0")
+    ap.add_argument("--capacity-factor", type=float, default=0.0, help="0: no cap")
     args = ap.parse_args(argv)
 
     from sched_pass_b200 import ops
@@ -35,10 +42,18 @@ def main(argv=None):
     cfg = get_config(args.model)
     dev = torch.device("cuda", 0)
     T = args.tokens
-    ep = ExpertParallel(cfg, dev, max_tokens=max(T, 1))
+    cap = None
+    if args.capacity_factor > 0:
+        cap = max(1, int(args.capacity_factor * T * cfg.top_k / cfg.n_experts))
+    ep = ExpertParallel(cfg, dev, max_tokens=max(T, 1), capacity=cap)
     g = torch.Generator(device=dev).manual_seed(0)
     w = build_moe_weights(cfg, 0, 1, g, dev)
-    x = torch.randn(T, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
+    x = torch.randn(T, cfg.hidden, device=dev, generator=g)
+    n_hot = int(args.hot * T)
+    if n_hot:
+        r0 = w.router[0].float()
+        x[:n_hot] += 8.0 * r0 / r0.norm()  # +8 on expert 0's logit (others ~ N(0, 1))
+    x = x.to(torch.bfloat16)
     h = torch.randn(T, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
     y = torch.empty_like(x)
     ln = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=dev)
@@ -64,6 +79,8 @@ def main(argv=None):
     peaks = measured_peaks()
     hbm = peaks.get("hbm_gbs", 6650.0)
     out = {"kernel": "moe_layer", "model": cfg.name, "tokens": T, "experts_active": active,
+           "hot": args.hot, "capacity": cap, "dropped": ep.dropped_total(),
+           "rows_per_expert": [int(v) for v in ep.words[: ep.E_local].tolist()],
            "us_median": round(us, 2), "us_min": round(times[0], 2),
            "bytes": wbytes + abytes, "achieved_gbs": round((wbytes + abytes) / us / 1e3, 1),
            "frac_of_measured_hbm": round((wbytes + abytes) / us / 1e3 / hbm, 3)}
