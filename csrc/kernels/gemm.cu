@@ -242,6 +242,41 @@ __device__ __forceinline__ void publish_tile(const Params &p, int tile, int et) 
   }
 }
 
+// How many flag releases chunk `ch` of token tile `tt` receives from one rank:
+// 1 under stream-K (one CTA writes the whole tile); under cluster split-K each
+// cluster rank releases the chunks its share of tokens [r*tv/cs, (r+1)*tv/cs)
+// touches, so the count is the number of shares that intersect the chunk.
+template <int TN>
+__device__ __forceinline__ uint32_t chunk_contributors(const Params &p, int tt, int ch) {
+  if (p.cs <= 1) return 1u;
+  const int tv = min(TN, p.a.T - tt * TN);
+  const int c0 = ch * kSlab, c1 = min(c0 + kSlab, tv);
+  uint32_t n = 0;
+  for (int r = 0; r < p.cs; ++r) {
+    const int lo = r * tv / p.cs, hi = (r + 1) * tv / p.cs;
+    n += (lo < hi && lo < c1 && hi > c0) ? 1u : 0u;
+  }
+  return n;
+}
+
+// Cluster split-K, all-reduce epilogue: after this CTA pushed its token rows
+// [lo, hi) of a tile to every rank, release each chunk those rows touch
+// (one count per chunk and rank; readers wait for chunk_contributors).
+template <int TN>
+__device__ __forceinline__ void publish_rows(const Params &p, int tile, int lo, int hi, int et) {
+  const GemmArgs &a = p.a;
+  constexpr int CH = TN / kSlab;
+  __threadfence_system();
+  named_bar(1, kEpiThreads);
+  if (lo >= hi) return;
+  const int c_first = lo / kSlab, c_last = (hi - 1) / kSlab;
+  const int chunks = c_last - c_first + 1;
+  for (int i = et; i < a.world * chunks; i += kEpiThreads) {
+    const int j = i / chunks, ch = c_first + i % chunks;
+    ptx::red_add_release_sys(a.flags[j] + ((size_t)a.rank * p.tiles + tile) * CH + ch, 1u);
+  }
+}
+
 // All-reduce, part 2: the reduction units are (tile, 16-token chunk); CTA c
 // owns units c, c + grid, ... on every rank (the same assignment everywhere,
 // independent of timing). For each owned unit it waits for the chunk flags
@@ -263,11 +298,12 @@ __device__ void reduce_owned_chunks(const Params &p, int c, int et) {
     const int tmax = min(kSlab, a.T - t0);
     if (et < a.world) {
       const uint32_t *f = my_flags + ((size_t)et * p.tiles + tile) * CH + ch;
-      bool ok = ptx::ld_acquire_sys(f) == 1u;
+      const uint32_t need = chunk_contributors<TN>(p, tt, ch);
+      bool ok = ptx::ld_acquire_sys(f) >= need;
       if (!ok) {
         const uint64_t start = ptx::globaltimer_ns();
         while (!ok) {
-          for (int i = 0; i < 64 && !ok; ++i) ok = ptx::ld_acquire_sys(f) == 1u;
+          for (int i = 0; i < 64 && !ok; ++i) ok = ptx::ld_acquire_sys(f) >= need;
           if (!ok && ptx::globaltimer_ns() - start > kWaitBudgetNs) break;
         }
         if (!ok) report_status(a.status, kStatusPeerTimeout);
@@ -731,6 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_before();
         ptx::mbar_arrive(&acc_empty[ab]);
+        if (EPI == kEpiAllReduce) publish_rows<TN>(p, tile, 0, tvalid, et);
         continue;
       }
       // our partial may overwrite `red` once every peer has read the previous one
@@ -790,7 +827,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar(1, kEpiThreads);
       if (et == 0)
         for (int s2 = 0; s2 < CS; ++s2) ptx::mbar_arrive_cluster(ptx::mapa_shared(free_addr, s2));
+      if (EPI == kEpiAllReduce) publish_rows<TN>(p, tile, lo, hi, et);
     }
+    if (EPI == kEpiAllReduce) reduce_owned_chunks<TN>(p, blockIdx.x, et);
   }
 
   __syncwarp();
@@ -959,8 +998,9 @@ static void dispatch(int tn, const CUtensorMap &tw, const CUtensorMap &tx, Param
   }
 }
 
-// The cluster plan for the instantiation a call will use (TN <= 128 and a
-// row-wise epilogue; the NVLink all-reduce epilogue stays on stream-K).
+// The cluster plan for the instantiation a call will use (TN <= 128; with
+// the NVLink all-reduce epilogue each cluster rank pushes its share of the
+// tile's tokens and releases the chunks it touched, see publish_rows).
 template <int EPI>
 static void plan_cluster_for(int tn, Params &p, int num_sms) {
   switch (tn) {
@@ -1027,13 +1067,15 @@ extern "C" void sched_gemm_plan(int T, int N, int K, int epi, int num_sms, int *
   int tn;
   gemm::plan(a, p, tn);
   p.cs = 0;
-  if (epi != kEpiAllReduce) {
+  {
     p.grid = num_sms;
     p.units = (long long)p.tiles * p.kb;
     if (epi == kEpiSwiGLU)
       gemm::plan_cluster_for<kEpiSwiGLU>(tn, p, num_sms);
     else if (epi == kEpiRopeKV)
       gemm::plan_cluster_for<kEpiRopeKV>(tn, p, num_sms);
+    else if (epi == kEpiAllReduce)
+      gemm::plan_cluster_for<kEpiAllReduce>(tn, p, num_sms);
     else
       gemm::plan_cluster_for<kEpiStore>(tn, p, num_sms);
     if (p.cs == 0) gemm::plan(a, p, tn);
@@ -1051,7 +1093,7 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   p.a = a;
   gemm::plan(a, p, tn);
   p.cs = 0;
-  if (a.grid <= 0 && a.epi != kEpiAllReduce) {
+  if (a.grid <= 0) {
     // the default schedule: cluster split-K where it fits the shape
     const int sms = a.num_sms > 0 ? a.num_sms : 148;
     p.grid = std::max(1, sms);
@@ -1060,6 +1102,8 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
       gemm::plan_cluster_for<kEpiSwiGLU>(tn, p, sms);
     else if (a.epi == kEpiRopeKV)
       gemm::plan_cluster_for<kEpiRopeKV>(tn, p, sms);
+    else if (a.epi == kEpiAllReduce)
+      gemm::plan_cluster_for<kEpiAllReduce>(tn, p, sms);
     else
       gemm::plan_cluster_for<kEpiStore>(tn, p, sms);
     if (p.cs == 0) gemm::plan(a, p, tn);  // back to the stream-K grid
