@@ -52,9 +52,18 @@ extern "C" int sched_probe_tasks(const uint32_t *cost, int n_tasks, int mode, in
                                  const void *data, size_t data_bytes, unsigned *hits, unsigned *per_cta,
                                  unsigned *ticket, unsigned *sink, int *status, cudaStream_t st);
 extern "C" int sched_probe_tasks_occupancy();
+extern "C" int sched_probe_mix(const void *R, size_t r_bytes, const void *S, size_t s_bytes, int mode, float frac,
+                               unsigned *sink, int grid, cudaStream_t st);
+extern "C" int sched_probe_pdl_pairs(float *buf, float *out, int n, const float *table, int work, int prologue,
+                                     int pdl, int pairs, cudaStream_t st);
+extern "C" int sched_probe_pdl_produce(float *buf, int n, int work, cudaStream_t st);
 extern "C" int sched_kv_page_copy(const void *src_k, const void *src_v, long long src_pages, void *dst_k,
                                   void *dst_v, long long dst_pages, const int32_t *pairs, int n_pairs,
                                   const int *n_dev, int layers, int heads, cudaStream_t st);
+extern "C" int sched_kv_page_copy_fp8(const void *src_k, const void *src_v, long long src_pages, void *dst_k,
+                                      void *dst_v, long long dst_pages, float *scale_k, float *scale_v, int to_fp8,
+                                      const int32_t *pairs, int n_pairs, const int *n_dev, int layers, int heads,
+                                      cudaStream_t st);
 
 namespace {
 
@@ -459,6 +468,35 @@ void probe_tasks(const at::Tensor &cost, int64_t mode, int64_t grid, int64_t mem
            "probe_tasks");
 }
 
+void probe_mix(const at::Tensor &R, const at::Tensor &S, int64_t mode, double frac, at::Tensor &sink,
+               int64_t grid) {
+  TORCH_CHECK(R.is_cuda() && S.is_cuda() && R.is_contiguous() && S.is_contiguous(), "R, S on the device");
+  TORCH_CHECK(mode >= 0 && mode <= 2, "mode is 0 (plain), 1 or 2 (pinned fractions)");
+  TORCH_CHECK(frac > 0.0 && frac <= 1.0, "the pinned fraction must be in (0, 1]");
+  TORCH_CHECK(grid > 0 && sink.numel() >= grid, "sink holds one word per CTA");
+  c10::cuda::CUDAGuard g(R.device());
+  check_rc(sched_probe_mix(R.data_ptr(), R.numel() * R.element_size(), S.data_ptr(), S.numel() * S.element_size(),
+                           mode, (float)frac, reinterpret_cast<unsigned *>(sink.data_ptr()), grid, cur_stream()),
+           "probe_mix");
+}
+
+void probe_pdl_pairs(at::Tensor &buf, at::Tensor &out, const at::Tensor &table, int64_t work, int64_t prologue,
+                     bool pdl, int64_t pairs) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && out.sizes() == buf.sizes() &&
+                  out.scalar_type() == at::kFloat && table.numel() >= 256 && table.scalar_type() == at::kFloat,
+              "float32 buf/out of one shape and a float32 table of >= 256 entries");
+  c10::cuda::CUDAGuard g(buf.device());
+  check_rc(sched_probe_pdl_pairs(buf.data_ptr<float>(), out.data_ptr<float>(), buf.numel(), table.data_ptr<float>(),
+                                 work, prologue, pdl ? 1 : 0, pairs, cur_stream()),
+           "probe_pdl_pairs");
+}
+
+void probe_pdl_produce(at::Tensor &buf, int64_t work) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && buf.is_contiguous(), "float32 buf");
+  c10::cuda::CUDAGuard g(buf.device());
+  check_rc(sched_probe_pdl_produce(buf.data_ptr<float>(), buf.numel(), work, cur_stream()), "probe_pdl_produce");
+}
+
 // Page moves between KV pools (device <-> pinned host); pairs [n, 2] int32 on the device.
 // With n_dev (int32 [1] on the device) n_pairs is a capacity and the count is read there.
 void kv_page_copy(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &dst_k, at::Tensor &dst_v,
@@ -472,6 +510,32 @@ void kv_page_copy(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &
                               dst_k.size(1), pairs.data_ptr<int32_t>(), n_pairs, ptr_or_null<int>(n_dev),
                               src_k.size(0), src_k.size(2), cur_stream()),
            "kv_page_copy");
+}
+
+// Page moves between a bf16 pool and an fp8 (uint8 storage) pool; the scales
+// [layers, fp8 pool pages, heads] fp32 belong to the fp8 pool.
+void kv_page_copy_fp8(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &dst_k, at::Tensor &dst_v,
+                      at::Tensor &scale_k, at::Tensor &scale_v, bool to_fp8, const at::Tensor &pairs,
+                      int64_t n_pairs, const c10::optional<at::Tensor> &n_dev) {
+  TORCH_CHECK(src_k.dim() == 5 && dst_k.dim() == 5, "pools are [layers, pages, heads, 16, 128]");
+  TORCH_CHECK(src_k.size(0) == dst_k.size(0) && src_k.size(2) == dst_k.size(2), "pool shapes differ");
+  TORCH_CHECK(src_k.size(3) == 16 && src_k.size(4) == 128 && dst_k.size(3) == 16 && dst_k.size(4) == 128,
+              "pages of 16 tokens x head dim 128");
+  TORCH_CHECK(src_k.is_contiguous() && src_v.is_contiguous() && dst_k.is_contiguous() && dst_v.is_contiguous() &&
+                  scale_k.is_contiguous() && scale_v.is_contiguous(),
+              "contiguous pools");
+  const at::Tensor &q = to_fp8 ? dst_k : src_k;
+  const at::Tensor &b = to_fp8 ? src_k : dst_k;
+  TORCH_CHECK(q.element_size() == 1 && b.scalar_type() == at::kBFloat16, "an fp8 (1-byte) pool and a bf16 pool");
+  TORCH_CHECK(scale_k.scalar_type() == at::kFloat && scale_k.numel() == q.size(0) * q.size(1) * q.size(2) &&
+                  scale_v.numel() == scale_k.numel(),
+              "scales [layers, fp8 pages, heads] float32");
+  TORCH_CHECK(pairs.is_cuda() && pairs.scalar_type() == at::kInt && pairs.is_contiguous(), "pairs int32 on device");
+  check_rc(sched_kv_page_copy_fp8(src_k.data_ptr(), src_v.data_ptr(), src_k.size(1), dst_k.data_ptr(),
+                                  dst_v.data_ptr(), dst_k.size(1), scale_k.data_ptr<float>(),
+                                  scale_v.data_ptr<float>(), to_fp8 ? 1 : 0, pairs.data_ptr<int32_t>(), n_pairs,
+                                  ptr_or_null<int>(n_dev), src_k.size(0), src_k.size(2), cur_stream()),
+           "kv_page_copy_fp8");
 }
 
 }  // namespace
@@ -505,6 +569,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("probe_stream", &probe_stream);
   m.def("probe_tasks", &probe_tasks);
   m.def("probe_tasks_occupancy", &sched_probe_tasks_occupancy);
+  m.def("probe_mix", &probe_mix);
+  m.def("kv_page_copy_fp8", &kv_page_copy_fp8);
+  m.def("probe_pdl_pairs", &probe_pdl_pairs);
+  m.def("probe_pdl_produce", &probe_pdl_produce);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_expert_gemm", &moe_expert_gemm);
   m.def("moe_quantize", &moe_quantize);

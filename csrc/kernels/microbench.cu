@@ -14,6 +14,21 @@
 //    coverage; per-CTA task counts and the makespan show the balance (the
 //    reference's experiments/clc/clc_probe.cu, clc_membound_probe.cu,
 //    clc_noise_probe.cu family, re-measured on B200).
+// 3. mix_probe: a reused set R read over and over, interleaved 1:1 with a
+//    stream S read once (S >> L2). Mode 0 is plain loads (L2's default
+//    replacement); mode 1 pins a fraction f of R's lines (evict_last, the
+//    rest evict_unchanged) and streams S evict_first; mode 2 is mode 1 with
+//    the unpinned part of R evict_first too. Sweeping |R| asks whether cache
+//    management pays when a reused set is flooded by a stream (the
+//    reference's test/cache_reuse.cu:1-45); sweeping f on an R larger than
+//    L2 asks whether residency is a continuous per-request budget (its
+//    test/cache_budget.cu:1-32).
+// 4. pdl_producer / pdl_consumer: two dependent kernels on one stream. The
+//    producer releases its dependents at entry; the consumer runs an
+//    independent prologue, then griddepcontrol.wait, then reads what the
+//    producer wrote. With programmatic stream serialization the prologue and
+//    the consumer's launch overlap the producer; results must not change
+//    (the reference's test/pdl_overlap.cu:1-70 gates).
 // Every wait here is bounded; nothing spins on another CTA.
 #include <cuda_runtime.h>
 
@@ -152,6 +167,65 @@ __global__ void __launch_bounds__(128) task_probe(const TaskArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- mix
+__device__ __forceinline__ uint4 ld_plain(const uint4 *a) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(a));
+  return v;
+}
+
+__global__ void __launch_bounds__(512) mix_probe(const uint4 *__restrict__ R, size_t rn,
+                                                 const uint4 *__restrict__ S, size_t sn, int mode, float frac,
+                                                 unsigned *__restrict__ sink) {
+  uint64_t pin = 0, str = 0;
+  if (mode == 1)
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, %1;" : "=l"(pin) : "f"(frac));
+  else if (mode == 2)
+    asm volatile("createpolicy.fractional.L2::evict_last.L2::evict_first.b64 %0, %1;" : "=l"(pin) : "f"(frac));
+  if (mode != 0) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(str));
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t j = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  size_t r = j % rn;
+  unsigned acc = 0;
+  for (; j < sn; j += stride) {
+    uint4 a, b;
+    if (mode == 0) {
+      a = ld_plain(R + r);
+      b = ld_plain(S + j);
+    } else {
+      a = ld_hint(R + r, pin);
+      b = ld_hint(S + j, str);
+    }
+    acc ^= a.x ^ a.w ^ b.y ^ b.z;
+    r += stride;
+    while (r >= rn) r -= rn;
+  }
+  if (acc == 0x9E3779B9u) sink[blockIdx.x] = acc;
+}
+
+// ---------------------------------------------------------------- PDL pair
+__global__ void __launch_bounds__(256) pdl_producer(float *__restrict__ buf, int n, int work) {
+  ptx::pdl_launch_dependents();  // the consumer may launch now; it waits before reading
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float v = (float)(i & 1023) * 1e-3f;
+  for (int k = 0; k < work; ++k) v = fmaf(v, 0.999f, 1e-3f);
+  buf[i] = v;
+}
+
+__global__ void __launch_bounds__(256) pdl_consumer(const float *__restrict__ buf, float *__restrict__ out, int n,
+                                                    const float *__restrict__ table, int prologue) {
+  // independent prologue: work that does not touch the producer's output
+  // (a consumer's control-table reads, its weights)
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  float t = 0.f;
+  for (int k = 0; k < prologue; ++k) t = fmaf(t, 0.5f, table[(i + k) & 255]);
+  ptx::pdl_wait();
+  if (i < n) out[i] = buf[i] * 2.0f + t;
+}
+
 }  // namespace probe
 
 extern "C" int sched_probe_stream(const void *src, size_t bytes, int policy, unsigned *sink, int grid,
@@ -188,4 +262,46 @@ extern "C" int sched_probe_tasks_occupancy() {
   int n = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, probe::task_probe, 128, 0);
   return n;
+}
+
+extern "C" int sched_probe_mix(const void *R, size_t r_bytes, const void *S, size_t s_bytes, int mode, float frac,
+                               unsigned *sink, int grid, cudaStream_t st) {
+  if (r_bytes < 16 || s_bytes < 16 || grid <= 0 || mode < 0 || mode > 2 || !(frac > 0.f && frac <= 1.f)) return -1;
+  probe::mix_probe<<<grid, 512, 0, st>>>(static_cast<const uint4 *>(R), r_bytes / 16, static_cast<const uint4 *>(S),
+                                         s_bytes / 16, mode, frac, sink);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+// `pairs` producer -> consumer launches back to back on `st`; with pdl the
+// consumer is launched with programmatic stream serialization.
+extern "C" int sched_probe_pdl_pairs(float *buf, float *out, int n, const float *table, int work, int prologue,
+                                     int pdl, int pairs, cudaStream_t st) {
+  if (n <= 0 || pairs <= 0) return -1;
+  const dim3 grid((n + 255) / 256), block(256);
+  for (int it = 0; it < pairs; ++it) {
+    probe::pdl_producer<<<grid, block, 0, st>>>(buf, n, work);
+    if (pdl) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = grid;
+      cfg.blockDim = block;
+      cfg.stream = st;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      at[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, probe::pdl_consumer, (const float *)buf, out, n, table, prologue) != cudaSuccess)
+        return -4;
+    } else {
+      probe::pdl_consumer<<<grid, block, 0, st>>>(buf, out, n, table, prologue);
+    }
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+// One producer launch (for fixtures whose consumer is another module's kernel).
+extern "C" int sched_probe_pdl_produce(float *buf, int n, int work, cudaStream_t st) {
+  if (n <= 0) return -1;
+  probe::pdl_producer<<<(n + 255) / 256, 256, 0, st>>>(buf, n, work);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

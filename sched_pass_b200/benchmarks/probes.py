@@ -8,8 +8,15 @@
   CTAs), a ticket queue (R CTAs) and cluster launch control (one CTA per
   task), on uniform, bimodal (straggler) and memory-bound task mixes; every
   run checks that each task executed exactly once.
+* ``reuse``: a reused set R (16 MiB .. 256 MiB) read 1:1 with a 2 GiB stream
+  S, plain loads vs R pinned (evict_last) and S streamed (evict_first): does
+  cache management pay once a stream floods a reused set?
+* ``budget``: R = 192 MiB (> L2), the pinned fraction f of R swept from
+  0.125 to 1: is L2 residency a continuous per-request budget?
+* ``pdl``: producer -> consumer pairs with and without programmatic stream
+  serialization, consumer prologue 0 / 256 FMAs; us per pair.
 
-    python -m sched_pass_b200.benchmarks.probes [--only stream|tasks]
+    python -m sched_pass_b200.benchmarks.probes [--only stream|tasks|reuse|budget|pdl]
 """
 from __future__ import annotations
 
@@ -110,14 +117,83 @@ def tasks():
     return out
 
 
+MIX_MODES = ["lru", "pin_R_stream_S", "pin_R_rest_first"]
+
+
+def _mix(R, S, mode, frac, sink, grid):
+    return _time(lambda: ext().probe_mix(R, S, mode, frac, sink, grid))
+
+
+def reuse(s_gib: float = 2.0):
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    S = torch.randint(0, 1 << 30, (int(s_gib * (1 << 28)),), dtype=torch.int32, device="cuda")
+    sink = torch.zeros(1 << 16, dtype=torch.int32, device="cuda")
+    s_bytes = S.numel() * 4
+    out = []
+    for r_mib in (16, 32, 64, 96, 128, 192, 256):
+        R = torch.randint(0, 1 << 30, (r_mib << 18,), dtype=torch.int32, device="cuda")
+        for mode in (0, 1):
+            ms = _mix(R, S, mode, 1.0, sink, sms * 4)
+            # every iteration reads one R vector and one S vector: 2 x |S| bytes requested;
+            # if R stays in L2 only |S| comes from DRAM
+            rec = {"probe": "reuse", "R_MiB": r_mib, "S_GiB": s_gib, "mode": MIX_MODES[mode], "ms": round(ms, 3),
+                   "requested_GBps": round(2 * s_bytes / ms / 1e6, 1),
+                   "dram_GBps_if_R_hits": round(s_bytes / ms / 1e6, 1)}
+            print(json.dumps(rec), flush=True)
+            out.append(rec)
+        del R
+    return out
+
+
+def budget(r_mib: int = 192, s_gib: float = 2.0):
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    S = torch.randint(0, 1 << 30, (int(s_gib * (1 << 28)),), dtype=torch.int32, device="cuda")
+    R = torch.randint(0, 1 << 30, (r_mib << 18,), dtype=torch.int32, device="cuda")
+    sink = torch.zeros(1 << 16, dtype=torch.int32, device="cuda")
+    out = []
+    base = _mix(R, S, 0, 1.0, sink, sms * 4)
+    print(json.dumps({"probe": "budget", "R_MiB": r_mib, "mode": "lru", "ms": round(base, 3)}), flush=True)
+    for mode in (1, 2):
+        for f in (0.125, 0.25, 0.375, 0.5, 0.625, 0.75, 1.0):
+            ms = _mix(R, S, mode, f, sink, sms * 4)
+            rec = {"probe": "budget", "R_MiB": r_mib, "mode": MIX_MODES[mode], "pin_fraction": f,
+                   "pinned_MiB": round(f * r_mib, 1), "ms": round(ms, 3), "vs_lru": round(ms / base, 3)}
+            print(json.dumps(rec), flush=True)
+            out.append(rec)
+    return out
+
+
+def pdl(n: int = 148 * 256 * 4, pairs: int = 200):
+    buf = torch.zeros(n, device="cuda")
+    out_ = torch.zeros(n, device="cuda")
+    table = torch.rand(256, device="cuda")
+    res = []
+    for work in (64, 1024):
+        for prologue in (0, 256):
+            row = {"probe": "pdl", "threads": n, "producer_fmas": work, "consumer_prologue_fmas": prologue}
+            for on in (False, True):
+                ms = _time(lambda: ext().probe_pdl_pairs(buf, out_, table, work, prologue, on, pairs))
+                row["us_per_pair_" + ("pdl" if on else "plain")] = round(ms * 1e3 / pairs, 2)
+            row["saved_us_per_pair"] = round(row["us_per_pair_plain"] - row["us_per_pair_pdl"], 2)
+            print(json.dumps(row), flush=True)
+            res.append(row)
+    return res
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", choices=["stream", "tasks"])
+    ap.add_argument("--only", choices=["stream", "tasks", "reuse", "budget", "pdl"])
     a = ap.parse_args(argv)
     if a.only in (None, "stream"):
         stream()
     if a.only in (None, "tasks"):
         tasks()
+    if a.only in (None, "reuse"):
+        reuse()
+    if a.only in (None, "budget"):
+        budget()
+    if a.only in (None, "pdl"):
+        pdl()
 
 
 if __name__ == "__main__":

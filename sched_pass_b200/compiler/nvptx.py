@@ -42,6 +42,25 @@ class CudaError(RuntimeError):
     pass
 
 
+# cuda.h launch-config structs, for cuLaunchKernelEx (programmatic dependent launch)
+_ATTR_PROGRAMMATIC_STREAM_SERIALIZATION = 6
+
+
+class _AttrValue(ctypes.Union):
+    _fields_ = [("pad", ctypes.c_char * 64), ("i", ctypes.c_int)]
+
+
+class _Attr(ctypes.Structure):
+    _fields_ = [("id", ctypes.c_int), ("pad", ctypes.c_char * 4), ("value", _AttrValue)]
+
+
+class _LaunchConfig(ctypes.Structure):
+    _fields_ = [("gridDimX", ctypes.c_uint), ("gridDimY", ctypes.c_uint), ("gridDimZ", ctypes.c_uint),
+                ("blockDimX", ctypes.c_uint), ("blockDimY", ctypes.c_uint), ("blockDimZ", ctypes.c_uint),
+                ("sharedMemBytes", ctypes.c_uint), ("hStream", ctypes.c_void_p),
+                ("attrs", ctypes.POINTER(_Attr)), ("numAttrs", ctypes.c_uint)]
+
+
 class CudaModule:
     def __init__(self, ptx: bytes):
         torch.cuda.init()
@@ -78,9 +97,11 @@ class CudaModule:
         torch.cuda.synchronize()
         self._check("cuMemcpyHtoD", self.cu.cuMemcpyHtoD_v2(d, ctypes.byref(v), ctypes.c_size_t(8)))
 
-    def launch(self, name: str, grid, block, args, shared: int = 0) -> None:
+    def launch(self, name: str, grid, block, args, shared: int = 0, pdl: bool = False) -> None:
         """args: torch tensors (passed as device pointers), ints (i32),
-        floats (f32) or ctypes values."""
+        floats (f32) or ctypes values. ``pdl`` launches with programmatic
+        stream serialization (the kernel may start while the previous grid on
+        the stream drains; a woven PDL point waits for it)."""
         holders = []
         for a in args:
             if isinstance(a, torch.Tensor):
@@ -95,6 +116,15 @@ class CudaModule:
         g = (tuple(grid) + (1, 1, 1))[:3]
         b = (tuple(block) + (1, 1, 1))[:3]
         stream = torch.cuda.current_stream().cuda_stream
+        if pdl:
+            attr = _Attr()
+            attr.id = _ATTR_PROGRAMMATIC_STREAM_SERIALIZATION
+            attr.value.i = 1
+            cfg = _LaunchConfig(g[0], g[1], g[2], b[0], b[1], b[2], shared, ctypes.c_void_p(stream),
+                                ctypes.pointer(attr), 1)
+            self._check("cuLaunchKernelEx", self.cu.cuLaunchKernelEx(ctypes.byref(cfg), self.function(name),
+                                                                     params, None))
+            return
         self._check("cuLaunchKernel", self.cu.cuLaunchKernel(
             self.function(name), ctypes.c_uint(g[0]), ctypes.c_uint(g[1]), ctypes.c_uint(g[2]),
             ctypes.c_uint(b[0]), ctypes.c_uint(b[1]), ctypes.c_uint(b[2]), ctypes.c_uint(shared),

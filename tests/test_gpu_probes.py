@@ -45,3 +45,34 @@ def test_stream_probe_policies():
         b.synchronize()
         gbs = src.numel() * 4 / a.elapsed_time(b) / 1e6
         assert gbs > 1000, (pol, gbs)
+
+
+def test_pdl_pairs_bit_exact():
+    """Programmatic dependent launch changes timing, never results: the
+    consumer reads the producer's output after griddepcontrol.wait."""
+    n = 1 << 20
+    buf = torch.zeros(n, device="cuda")
+    table = torch.rand(256, device="cuda")
+    outs = []
+    for pdl in (False, True):
+        for prologue in (0, 64):
+            out = torch.zeros(n, device="cuda")
+            buf.zero_()
+            ext().probe_pdl_pairs(buf, out, table, 512, prologue, pdl, 3)
+            torch.cuda.synchronize()
+            outs.append(out)
+            if prologue == 0:
+                assert torch.equal(out, buf * 2) and buf.abs().sum().item() > 0
+    assert torch.equal(outs[0], outs[2]) and torch.equal(outs[1], outs[3])
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_mix_probe_runs(mode):
+    R = torch.zeros(8 << 20, dtype=torch.int32, device="cuda")   # 32 MiB reused
+    S = torch.zeros(64 << 20, dtype=torch.int32, device="cuda")  # 256 MiB streamed
+    sink = torch.zeros(1 << 12, dtype=torch.int32, device="cuda")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    ext().probe_mix(R, S, mode, 0.5 if mode else 1.0, sink, sms * 4)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError):
+        ext().probe_mix(R, S, 1, 0.0, sink, sms * 4)  # fraction outside (0, 1]

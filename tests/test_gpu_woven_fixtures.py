@@ -213,3 +213,35 @@ def test_paged_linear_fixture():
     shed = run(woven)
     ref_half = (kv.view(-1, 64)[bt.view(nreq, nb)[:, :nb // 2].long()] * w[None, :nb // 2, None]).sum(1).flatten()
     assert (shed - ref_half).abs().max().item() < 1e-3
+
+
+def test_paged_linear_pdl_after_producer():
+    """PDL lever: the woven consumer, launched with programmatic stream
+    serialization right behind a kernel that writes its KV (and releases its
+    dependents at entry), reads only finished data -- the same bits as a
+    plain launch -- and its woven timer still fills."""
+    from sched_pass_b200._ext import ext
+    woven = _compile("paged_linear.ll", {"SCHED_PDL": "1"})
+    nreq, nb = 32, 24
+    kv = torch.empty(nreq * nb * 64, device="cuda")
+    bt = torch.randperm(nreq * nb, device="cuda").to(torch.int32)
+    w = torch.randn(nb, device="cuda")
+    t = Tables()
+    t.u32(abi.CTRL_ORDER_SIZE_OFF, nreq)
+    t.push()
+    t.arm(woven)
+
+    def run(pdl):
+        out = torch.zeros(nreq * 64, device="cuda")
+        kv.zero_()
+        t.timer.zero_()
+        ext().probe_pdl_produce(kv, 2048)  # a long producer: the consumer would see zeros if it ran early
+        woven.launch("paged_linear", (nreq,), (64,), [kv, bt, w, out, nb], pdl=pdl)
+        torch.cuda.synchronize()
+        return out
+    plain = run(False)
+    got = run(True)
+    assert torch.equal(got, plain)
+    ref = (kv.view(-1, 64)[bt.view(nreq, nb).long()] * w[None, :, None]).sum(1).flatten()
+    assert (got - ref).abs().max().item() < 1e-3 and kv.abs().sum().item() > 0
+    assert (t.timer[:nreq] > 0).all()
