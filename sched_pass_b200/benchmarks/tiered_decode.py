@@ -46,6 +46,8 @@ def parse(argv=None):
     ap.add_argument("--shed-ratio", type=float, default=0.5)
     ap.add_argument("--device-kv-gb", type=float, default=0.0, help="cap of the device KV pool (0: what fits)")
     ap.add_argument("--acquire", default="auto")
+    ap.add_argument("--host-kv-dtype", default="bf16", choices=["bf16", "fp8"],
+                    help="host pool storage; fp8 halves the bytes staged over PCIe")
     ap.add_argument("--seed", type=int, default=0)
     return ap.parse_args(argv)
 
@@ -87,7 +89,8 @@ def main(argv=None):
     max_ctx = int(ctx.max()) + args.output + 16
     ecfg = EngineConfig(max_batch=args.requests, max_prefill_tokens=256,
                         max_context=(max_ctx + 127) // 128 * 128, num_pages=alloc_pages,
-                        host_kv_pages=host_pages, kv_staging_pages=staging, acquire=args.acquire,
+                        host_kv_pages=host_pages, kv_staging_pages=staging, host_kv_dtype=args.host_kv_dtype,
+                        acquire=args.acquire,
                         shed_fraction=args.shed_fraction, shed_ratio=args.shed_ratio, seed=args.seed)
     eng = Engine(cfg, ecfg, dev, tp=tp)
     g = torch.Generator(device=dev)
@@ -140,11 +143,12 @@ def main(argv=None):
         "config": {"model": cfg.name + "-arch", "requests": args.requests,
                    "context": [args.ctx_min, args.ctx_max], "output_tokens": args.output,
                    "parallelism": f"tp{world}", "shed": f"{args.shed_fraction} least urgent, tau={args.shed_ratio}x",
-                   "acquire": args.acquire},
+                   "acquire": args.acquire, "host_kv_dtype": args.host_kv_dtype},
         "kv": {"pages_needed": need_pages, "device_pages": alloc_pages, "staging_pages": staging,
                "host_pages": host_pages, "spilled_pages": eng.tier.spilled_pages,
                "staged_pages_per_step": round(staged, 1),
-               "staged_gb_per_step": round(staged * page_bytes / 1e9, 3)},
+               "staged_gb_per_step": round(staged * page_bytes / (2 if args.host_kv_dtype == "fp8" else 1) / 1e9,
+                                           3)},
         "e2e": {"value": round(tokens / host_s, 3), "unit": "decode tokens/s",
                 "h2d_bytes_per_step": eng.packed_len * 4, "d2h_bytes_per_step": 4 * args.requests},
         "clocks": clocks,

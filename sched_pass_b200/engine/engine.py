@@ -63,6 +63,7 @@ class EngineConfig:
     verbose: bool = False           # print the scheduling plugin's effective config
     host_kv_pages: int = 0          # tiered KV: pinned host pages the device pool spills to (0 = off)
     kv_staging_pages: int = 0       # staging slots (one layer of a host page each; 0 = host_kv_pages)
+    host_kv_dtype: str = "bf16"     # host pool storage: "bf16" or "fp8" (e4m3 + per-head page scales)
 
 
 @dataclass
@@ -95,7 +96,7 @@ class Engine:
         if e.host_kv_pages:
             from .tiered_kv import TieredKV
             self.tier = TieredKV(self.kv, e.num_pages, e.kv_staging_pages or e.host_kv_pages,
-                                 e.host_kv_pages, self.device)
+                                 e.host_kv_pages, self.device, host_dtype=e.host_kv_dtype)
         if weights is None:
             weights = init_weights(cfg, self.device, tp_rank, tp_size, seed=e.seed,
                                    moe_builder=getattr(model_factory, "moe_builder", None))

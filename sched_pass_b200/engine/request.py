@@ -29,6 +29,7 @@ class Request:
     urgency: float = 0.0          # control-plane q (0..1)
     tau: int = 0                  # shed budget in tokens (0 = none)
     preemptions: int = 0
+    spilled_pages: int = 0        # pages moved to the host KV tier (tiered KV)
 
     @property
     def prompt_len(self) -> int:

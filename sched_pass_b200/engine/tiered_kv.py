@@ -31,6 +31,11 @@ and the copy for layer l+2 waits until layer l's attention has read the
 buffer. Staging costs 2 x slots x one layer's page of device memory, so the
 read set of a step may exceed HBM (the 70B / 131k-context configuration).
 
+With ``host_dtype="fp8"`` the host pool stores e4m3 pages with one fp32
+scale per (layer, page, head, K|V): a spill quantizes, the staging copy
+dequantizes back to bf16, so half the bytes cross PCIe per step (the
+decode kernel still reads bf16). Cold pages then carry fp8 precision.
+
 The reference names KV tiering as its unbuilt "MOVE" lever
 (ROADMAP.md:462-482 of jc-su/sched-pass); this is the mechanism.
 """
@@ -51,7 +56,10 @@ def is_host(page: int) -> bool:
 
 
 class TieredKV:
-    def __init__(self, kv, n_device: int, n_staging: int, n_host: int, device):
+    def __init__(self, kv, n_device: int, n_staging: int, n_host: int, device, host_dtype: str = "bf16"):
+        if host_dtype not in ("bf16", "fp8"):
+            raise ValueError(f"host_dtype must be 'bf16' or 'fp8', not {host_dtype!r}")
+        self.host_dtype = host_dtype
         self.kv = kv
         self.n_device = int(n_device)
         self.n_staging = max(1, int(n_staging))
@@ -63,8 +71,12 @@ class TieredKV:
         L, _, H, P, D = kv.k.shape
         self.layers = L
         on_cuda = self.device.type == "cuda"
-        self.host_k = torch.zeros((L, self.n_host, H, P, D), dtype=kv.k.dtype, pin_memory=on_cuda)
-        self.host_v = torch.zeros((L, self.n_host, H, P, D), dtype=kv.v.dtype, pin_memory=on_cuda)
+        hdt = torch.uint8 if host_dtype == "fp8" else kv.k.dtype  # fp8 e4m3 bytes
+        self.host_k = torch.zeros((L, self.n_host, H, P, D), dtype=hdt, pin_memory=on_cuda)
+        self.host_v = torch.zeros((L, self.n_host, H, P, D), dtype=hdt, pin_memory=on_cuda)
+        if host_dtype == "fp8":
+            self.host_scale_k = torch.ones((L, self.n_host, H), dtype=torch.float32, pin_memory=on_cuda)
+            self.host_scale_v = torch.ones((L, self.n_host, H), dtype=torch.float32, pin_memory=on_cuda)
         # two one-layer staging buffers (even / odd layers)
         self.stage_k = torch.zeros((2, self.n_staging, H, P, D), dtype=kv.k.dtype, device=self.device)
         self.stage_v = torch.zeros_like(self.stage_k)
@@ -140,6 +152,7 @@ class TieredKV:
             d = int(r.pages[i])
             pairs.append((d, h))
             r.pages[i] = HOST_BASE + h
+            r.spilled_pages += 1
             freed.append(d)
         self._copy_all_layers(self.kv.k, self.kv.v, self.host_k, self.host_v, pairs)
         self.spilled_pages += len(pairs)
@@ -151,7 +164,11 @@ class TieredKV:
         if n * 2 > self._spill_dev.numel():
             self._spill_dev = torch.zeros(n * 2, dtype=torch.int32, device=self.device)
         self._spill_dev[: n * 2].copy_(arr)  # pageable source: a synchronous copy
-        ext().kv_page_copy(src_k, src_v, dst_k, dst_v, self._spill_dev, n, None)
+        if self.host_dtype == "fp8":
+            ext().kv_page_copy_fp8(src_k, src_v, dst_k, dst_v, self.host_scale_k, self.host_scale_v, True,
+                                   self._spill_dev, n, None)
+        else:
+            ext().kv_page_copy(src_k, src_v, dst_k, dst_v, self._spill_dev, n, None)
 
     # ------------------------------------------------------------ staging
     def stage(self, decode_requests) -> None:
@@ -199,6 +216,12 @@ class TieredKV:
     # ------------------------------------------------------------ per-layer streaming
     def _fetch(self, layer: int) -> None:
         b = layer & 1
+        if self.host_dtype == "fp8":
+            ext().kv_page_copy_fp8(self.host_k[layer:layer + 1], self.host_v[layer:layer + 1],
+                                   self.stage_k[b:b + 1], self.stage_v[b:b + 1],
+                                   self.host_scale_k[layer:layer + 1], self.host_scale_v[layer:layer + 1], False,
+                                   self.pairs_dev, self.n_staging, self.count_dev)
+            return
         ext().kv_page_copy(self.host_k[layer:layer + 1], self.host_v[layer:layer + 1],
                            self.stage_k[b:b + 1], self.stage_v[b:b + 1], self.pairs_dev, self.n_staging,
                            self.count_dev)
