@@ -57,7 +57,16 @@ bool symm_can_access(int64_t device, int64_t peer) {
   return ok != 0;
 }
 
+// A non-owning uint8 tensor over this rank's own buffer (for inspection:
+// the slab a fused collective left behind). The buffer must outlive it.
+at::Tensor symm_view(int64_t ptr, int64_t bytes, int64_t device) {
+  TORCH_CHECK(ptr != 0 && bytes > 0, "symm: null or empty view");
+  return torch::from_blob(reinterpret_cast<void *>(ptr), {bytes},
+                          at::TensorOptions().dtype(at::kByte).device(at::kCUDA, (int)device));
+}
+
 void register_symm(py::module &m) {
+  m.def("symm_view", &symm_view);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);

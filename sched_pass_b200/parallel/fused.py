@@ -48,6 +48,14 @@ class FusedAllReduce:
                              ws.counters, ops.status_buffer(x.device))
         return out
 
+    def last_slab(self, T: int, N: int) -> torch.Tensor:
+        """bf16 [world, T, N]: the partials every rank pushed into this rank's
+        slab in the most recent call (the inputs of its reduction)."""
+        slab, _ = self.sets[self.k ^ 1]
+        raw = ext().symm_view(slab.local, slab.nbytes, self.device.index)
+        # the kernel packs the slab for the call's shape: [(src * T + t) * N + n]
+        return raw.view(torch.bfloat16)[: self.world * T * N].view(self.world, T, N)
+
     def close(self):
         for a, b in self.sets:
             a.close()

@@ -32,10 +32,16 @@ def main():
             tp.linear_allreduce(x, w, y)
         torch.cuda.synchronize()
         err = ((y.float().cpu() - ref).norm() / ref.norm()).item()
+        # the kernel's output is the rank-order reduction of the partials it received (CPU oracle)
+        from sched_pass_b200.parallel import protocol
+        slab = tp._fused.last_slab(T, N).cpu().view(torch.int16).numpy().view(np.uint16)
+        oracle = protocol.reduce_rank_order(slab)
+        oracle_ok = bool(np.array_equal(y.cpu().view(torch.int16).numpy().view(np.uint16), oracle))
         ys = [torch.empty_like(y) for _ in range(world)]
         dist.all_gather(ys, y)
         same = all(torch.equal(ys[0], z) for z in ys)
-        out["checks"].append({"T": T, "N": N, "K": K, "rel_err": err, "identical_on_ranks": same})
+        out["checks"].append({"T": T, "N": N, "K": K, "rel_err": err, "identical_on_ranks": same,
+                              "matches_protocol_oracle": oracle_ok})
     ops.check_status()
     # engine: TP generation == single-GPU generation
     from sched_pass_b200.engine.engine import Engine, EngineConfig
