@@ -32,8 +32,8 @@ int sched_add_rmsnorm(const void *x, void *res, const void *w, void *y, int T, i
                       cudaStream_t st);
 int sched_rope_kv_append(const void *qkv, const int32_t *pos, const int32_t *slot,
                          const float *cos_sin, void *q_out, void *k_cache, void *v_cache, int T,
-                         int Hq, int Hkv, int D, int page_size, cudaStream_t st);
-int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int H,
+                         int Hq, int Hkv, int D, int page_size, int num_pages, int *status, cudaStream_t st);
+int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int H, int vocab, int *status,
                     cudaStream_t st);
 int sched_argmax(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
                  int id_offset, cudaStream_t st);
@@ -59,11 +59,11 @@ extern "C" int sched_probe_pdl_pairs(float *buf, float *out, int n, const float 
 extern "C" int sched_probe_pdl_produce(float *buf, int n, int work, cudaStream_t st);
 extern "C" int sched_kv_page_copy(const void *src_k, const void *src_v, long long src_pages, void *dst_k,
                                   void *dst_v, long long dst_pages, const int32_t *pairs, int n_pairs,
-                                  const int *n_dev, int layers, int heads, cudaStream_t st);
+                                  const int *n_dev, int layers, int heads, int *status, cudaStream_t st);
 extern "C" int sched_kv_page_copy_fp8(const void *src_k, const void *src_v, long long src_pages, void *dst_k,
                                       void *dst_v, long long dst_pages, float *scale_k, float *scale_v, int to_fp8,
                                       const int32_t *pairs, int n_pairs, const int *n_dev, int layers, int heads,
-                                      cudaStream_t st);
+                                      int *status, cudaStream_t st);
 
 namespace {
 
@@ -169,6 +169,7 @@ void gemm_qkv_rope(const at::Tensor &x, const at::Tensor &w, const at::Tensor &p
   a.Hq = Hq;
   a.Hkv = Hkv;
   a.page_size = k_cache.size(2);
+  a.kv_pages = k_cache.size(0);
   c10::cuda::CUDAGuard g(x.device());
   check_rc(sched_gemm_run(&a, cur_stream()), "gemm_qkv_rope");
 }
@@ -309,7 +310,7 @@ void add_rmsnorm(const at::Tensor &x, const c10::optional<at::Tensor> &res, cons
 
 void rope_kv_append(const at::Tensor &qkv, const at::Tensor &pos, const at::Tensor &slot,
                     const at::Tensor &cos_sin, at::Tensor &q_out, at::Tensor &k_cache,
-                    at::Tensor &v_cache, int64_t Hq, int64_t Hkv) {
+                    at::Tensor &v_cache, int64_t Hq, int64_t Hkv, const c10::optional<at::Tensor> &status) {
   check_bf16(qkv, "qkv");
   check_i32(pos, "pos");
   check_i32(slot, "slot");
@@ -319,16 +320,17 @@ void rope_kv_append(const at::Tensor &qkv, const at::Tensor &pos, const at::Tens
   check_rc(sched_rope_kv_append(qkv.data_ptr(), pos.data_ptr<int32_t>(), slot.data_ptr<int32_t>(),
                                 cos_sin.data_ptr<float>(), q_out.data_ptr(), k_cache.data_ptr(),
                                 v_cache.data_ptr(), T, Hq, Hkv, k_cache.size(3), k_cache.size(2),
-                                cur_stream()),
+                                k_cache.size(0), ptr_or_null<int>(status), cur_stream()),
            "rope_kv_append");
 }
 
-void embedding(const at::Tensor &ids, const at::Tensor &table, at::Tensor &out) {
+void embedding(const at::Tensor &ids, const at::Tensor &table, at::Tensor &out,
+               const c10::optional<at::Tensor> &status) {
   check_i32(ids, "ids");
   check_bf16(table, "table");
   c10::cuda::CUDAGuard g(ids.device());
   check_rc(sched_embedding(ids.data_ptr<int32_t>(), table.data_ptr(), out.data_ptr(), ids.numel(),
-                           table.size(1), cur_stream()),
+                           table.size(1), table.size(0), ptr_or_null<int>(status), cur_stream()),
            "embedding");
 }
 
@@ -500,7 +502,8 @@ void probe_pdl_produce(at::Tensor &buf, int64_t work) {
 // Page moves between KV pools (device <-> pinned host); pairs [n, 2] int32 on the device.
 // With n_dev (int32 [1] on the device) n_pairs is a capacity and the count is read there.
 void kv_page_copy(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &dst_k, at::Tensor &dst_v,
-                  const at::Tensor &pairs, int64_t n_pairs, const c10::optional<at::Tensor> &n_dev) {
+                  const at::Tensor &pairs, int64_t n_pairs, const c10::optional<at::Tensor> &n_dev,
+                  const c10::optional<at::Tensor> &status) {
   TORCH_CHECK(src_k.dim() == 5 && dst_k.dim() == 5, "pools are [layers, pages, heads, 16, 128]");
   TORCH_CHECK(src_k.size(0) == dst_k.size(0) && src_k.size(2) == dst_k.size(2), "pool shapes differ");
   TORCH_CHECK(src_k.is_contiguous() && src_v.is_contiguous() && dst_k.is_contiguous() && dst_v.is_contiguous(),
@@ -508,7 +511,7 @@ void kv_page_copy(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &
   TORCH_CHECK(pairs.is_cuda() && pairs.scalar_type() == at::kInt && pairs.is_contiguous(), "pairs int32 on device");
   check_rc(sched_kv_page_copy(src_k.data_ptr(), src_v.data_ptr(), src_k.size(1), dst_k.data_ptr(), dst_v.data_ptr(),
                               dst_k.size(1), pairs.data_ptr<int32_t>(), n_pairs, ptr_or_null<int>(n_dev),
-                              src_k.size(0), src_k.size(2), cur_stream()),
+                              src_k.size(0), src_k.size(2), ptr_or_null<int>(status), cur_stream()),
            "kv_page_copy");
 }
 
@@ -516,7 +519,8 @@ void kv_page_copy(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &
 // [layers, fp8 pool pages, heads] fp32 belong to the fp8 pool.
 void kv_page_copy_fp8(const at::Tensor &src_k, const at::Tensor &src_v, at::Tensor &dst_k, at::Tensor &dst_v,
                       at::Tensor &scale_k, at::Tensor &scale_v, bool to_fp8, const at::Tensor &pairs,
-                      int64_t n_pairs, const c10::optional<at::Tensor> &n_dev) {
+                      int64_t n_pairs, const c10::optional<at::Tensor> &n_dev,
+                      const c10::optional<at::Tensor> &status) {
   TORCH_CHECK(src_k.dim() == 5 && dst_k.dim() == 5, "pools are [layers, pages, heads, 16, 128]");
   TORCH_CHECK(src_k.size(0) == dst_k.size(0) && src_k.size(2) == dst_k.size(2), "pool shapes differ");
   TORCH_CHECK(src_k.size(3) == 16 && src_k.size(4) == 128 && dst_k.size(3) == 16 && dst_k.size(4) == 128,
@@ -534,7 +538,8 @@ void kv_page_copy_fp8(const at::Tensor &src_k, const at::Tensor &src_v, at::Tens
   check_rc(sched_kv_page_copy_fp8(src_k.data_ptr(), src_v.data_ptr(), src_k.size(1), dst_k.data_ptr(),
                                   dst_v.data_ptr(), dst_k.size(1), scale_k.data_ptr<float>(),
                                   scale_v.data_ptr<float>(), to_fp8 ? 1 : 0, pairs.data_ptr<int32_t>(), n_pairs,
-                                  ptr_or_null<int>(n_dev), src_k.size(0), src_k.size(2), cur_stream()),
+                                  ptr_or_null<int>(n_dev), src_k.size(0), src_k.size(2), ptr_or_null<int>(status),
+                                  cur_stream()),
            "kv_page_copy_fp8");
 }
 

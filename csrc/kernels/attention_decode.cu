@@ -90,6 +90,8 @@ struct Params {
   int splits;           // chunks per request when merging in-kernel (part = req * splits + s)
   int total_rows;       // rows of the cache tensor maps: pages * Hkv * 16 (an out-of-range row)
   int stage_split;      // block-table ids >= this name pages of the staging pool (tmK2/tmV2)
+  int num_pages;        // pages of the device pool: ids in [num_pages, stage_split) are bad
+  int stage_pages;      // pages of the staging pool: ids >= stage_split + stage_pages are bad
   SchedSlots slots;
   sched::PolicyConsts pc;
   int pf_blocks;  // urgent prefetch distance in KV blocks
@@ -112,6 +114,14 @@ struct Shared {
   uint32_t tmem_base;
   int merge_last;
 };
+
+// A block-table id names a device page [0, num_pages) or a staging page
+// [stage_split, stage_split + stage_pages).
+__device__ __forceinline__ bool page_ok(const Params &p, int page) {
+  if (page < 0) return false;
+  if (page >= p.stage_split) return page - p.stage_split < p.stage_pages;
+  return page < p.num_pages;
+}
 
 __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t byte_in_row) {
   // 128-byte swizzle: the 16-byte chunk index is XORed with (row % 8).
@@ -251,7 +261,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int pi = 0; pi < PAGES_PER_BLK; ++pi) {
             // pages past the request's end: an out-of-range box reads zeros;
             // ids from stage_split on live in the staging pool (tiered KV)
-            const int page = pi < npg ? __ldg(bt + pg0 + pi) : -1;
+            int page = pi < npg ? __ldg(bt + pg0 + pi) : -1;
+            if (pi < npg && !page_ok(p, page)) {  // reported; read as an out-of-range (zero) box
+              report_bad_index(p.status, kSiteDecodePage, page);
+              page = -1;
+            }
             const bool staged = page >= p.stage_split;
             const int row = page < 0 ? p.total_rows
                                      : ((staged ? page - p.stage_split : page) * p.Hkv + ti.kvh) * PS;
@@ -278,6 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int pfn = min(PAGES_PER_BLK, last_page - pf0);
             for (int pi = 0; pi < pfn; ++pi) {
               const int page = __ldg(bt + pf0 + pi);
+              if (!page_ok(p, page)) continue;
               const bool staged = page >= p.stage_split;
               const int row = ((staged ? page - p.stage_split : page) * p.Hkv + ti.kvh) * PS;
               const CUtensorMap *mk = staged ? &tmK2 : &tmK;
@@ -706,6 +721,8 @@ extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
   p.splits = splits > 0 ? splits : 1;
   p.total_rows = num_pages * Hkv * attn::PS;
   p.stage_split = stage_k != nullptr ? stage_split : 0x7fffffff;
+  p.num_pages = num_pages;
+  p.stage_pages = stage_k != nullptr ? stage_pages : 0;
   p.slots = slots;
   p.pc.dT = dT;
   p.pc.dR = dR;

@@ -19,10 +19,31 @@ enum KernelStatus : int {
   kStatusPeerTimeout = 4,     // a peer GPU's flag never arrived
   kStatusClcTimeout = 5,      // a cluster-launch-control response never arrived
   kStatusBadArgument = 6,
+  kStatusBadIndex = 7,        // a caller-provided index was out of range; that access was skipped
 };
 
+// Where a bad index came from (status word 1).
+enum IndexSite : int {
+  kSiteCopySrcPage = 1,   // kv page copy: source page of a pair
+  kSiteCopyDstPage = 2,   // kv page copy: destination page of a pair
+  kSiteKvSlot = 3,        // KV append: cache slot of a token
+  kSiteTokenId = 4,       // embedding: token id
+  kSiteDecodePage = 5,    // decode attention: block-table page id
+};
+
+// A status buffer holds 4 int32 words: [0] the code, and for
+// kStatusBadIndex [1] the site and [2..3] the offending index (int64) of the
+// first fault. Only the thread whose CAS set the code writes words 1-3.
 __device__ __forceinline__ void report_status(int *status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
+}
+
+__device__ __forceinline__ void report_bad_index(int *status, int site, long long index) {
+  if (status == nullptr) return;
+  if (atomicCAS(status, 0, kStatusBadIndex) == 0) {
+    status[1] = site;
+    *reinterpret_cast<long long *>(status + 2) = index;
+  }
 }
 
 // Wall-time budget (ns) of every bounded wait on an mbarrier or a flag.

@@ -100,13 +100,18 @@ __global__ void rope_kv_append_kernel(const __nv_bfloat16 *__restrict__ qkv,
                                       __nv_bfloat16 *__restrict__ q_out,
                                       __nv_bfloat16 *__restrict__ k_cache,
                                       __nv_bfloat16 *__restrict__ v_cache, int Hq, int Hkv,
-                                      int page_size) {
+                                      int page_size, int num_pages, int *status) {
   constexpr int HALF = D / 2;
   const int t = blockIdx.x;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nheads = Hq + 2 * Hkv;
   const int p = pos[t];
-  const int s = slot[t];
+  int s = slot[t];
+  // a slot outside the cache is reported and its cache writes skipped
+  if (s >= 0 && (long long)s >= (long long)num_pages * page_size) {
+    if (threadIdx.x == 0) report_bad_index(status, kSiteKvSlot, s);
+    s = -1;
+  }
   const int page = s / page_size, off = s % page_size;
   const __nv_bfloat16 *src_row = qkv + (size_t)t * nheads * D;
   for (int h = warp; h < nheads; h += blockDim.x / 32) {
@@ -138,14 +143,20 @@ __global__ void rope_kv_append_kernel(const __nv_bfloat16 *__restrict__ qkv,
 
 __global__ void embedding_kernel(const int32_t *__restrict__ ids,
                                  const __nv_bfloat16 *__restrict__ table,
-                                 __nv_bfloat16 *__restrict__ out, int H) {
+                                 __nv_bfloat16 *__restrict__ out, int H, int vocab, int *status) {
   const int t = blockIdx.x;
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
-  const size_t id = (size_t)ids[t];
+  const int id = ids[t];
+  if (id < 0 || id >= vocab) {  // reported; the row is zeroed instead of read out of bounds
+    if (threadIdx.x == 0) report_bad_index(status, kSiteTokenId, id);
+    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
+      *reinterpret_cast<uint4 *>(out + (size_t)t * H + c) = make_uint4(0, 0, 0, 0);
+    return;
+  }
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
     *reinterpret_cast<uint4 *>(out + (size_t)t * H + c) =
-        *reinterpret_cast<const uint4 *>(table + id * H + c);
+        *reinterpret_cast<const uint4 *>(table + (size_t)id * H + c);
 }
 
 // Row argmax; ties resolve to the lowest index. Also emits the row max so a
@@ -239,21 +250,21 @@ extern "C" int sched_add_rmsnorm(const void *x, void *res, const void *w, void *
 extern "C" int sched_rope_kv_append(const void *qkv, const int32_t *pos, const int32_t *slot,
                                     const float *cos_sin, void *q_out, void *k_cache,
                                     void *v_cache, int T, int Hq, int Hkv, int D, int page_size,
-                                    cudaStream_t st) {
+                                    int num_pages, int *status, cudaStream_t st) {
   if (T <= 0) return 0;
   if (D != 128) return -1;
   ew::rope_kv_append_kernel<128><<<T, 256, 0, st>>>(
       static_cast<const __nv_bfloat16 *>(qkv), pos, slot, reinterpret_cast<const float2 *>(cos_sin),
       static_cast<__nv_bfloat16 *>(q_out), static_cast<__nv_bfloat16 *>(k_cache),
-      static_cast<__nv_bfloat16 *>(v_cache), Hq, Hkv, page_size);
+      static_cast<__nv_bfloat16 *>(v_cache), Hq, Hkv, page_size, num_pages, status);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
-extern "C" int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int H,
-                               cudaStream_t st) {
+extern "C" int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int H, int vocab,
+                               int *status, cudaStream_t st) {
   if (T <= 0) return 0;
   launch_pdl(ew::embedding_kernel, T, 256, 0, st, ids, static_cast<const __nv_bfloat16 *>(table),
-             static_cast<__nv_bfloat16 *>(out), H);
+             static_cast<__nv_bfloat16 *>(out), H, vocab, status);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

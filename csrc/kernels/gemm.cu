@@ -186,6 +186,10 @@ __device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, 
     } else {
       const int s = a.slot[t];
       if (s < 0) return;  // padding row: no cache write
+      if (a.kv_pages > 0 && (long long)s >= (long long)a.kv_pages * a.page_size) {
+        report_bad_index(a.status, kSiteKvSlot, s);
+        return;
+      }
       const int page = s / a.page_size, off = s % a.page_size;
       const bool is_k = h < a.Hq + a.Hkv;
       const int kvh = is_k ? h - a.Hq : h - a.Hq - a.Hkv;

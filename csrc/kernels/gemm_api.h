@@ -29,7 +29,7 @@ struct GemmArgs {
   long long ws_floats;
   uint32_t *counters;  // per-tile arrival counters, zero between calls
   int counter_count;
-  int *status;
+  int *status;    // 4 int32 words (code, site, int64 index of a bad index) or null
   // kEpiRopeKV only
   const int32_t *pos;    // [T] absolute positions
   const int32_t *slot;   // [T] page * page_size + offset, -1 = no cache write
@@ -46,6 +46,9 @@ struct GemmArgs {
   // optional per-CTA %globaltimer trace [grid][4]: entry, producer past the
   // dependency wait, last TMA issued, CTA done (nullptr: off)
   unsigned long long *trace;
+  // kEpiRopeKV: pages of the KV cache; a token slot beyond them is reported
+  // (kStatusBadIndex, site kSiteKvSlot) and not written. 0: unchecked.
+  int kv_pages;
 };
 
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream);

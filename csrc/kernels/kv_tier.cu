@@ -34,7 +34,23 @@ struct CopyArgs {
   int layers;
   long long src_layer_pages, dst_layer_pages;  // pages per layer in each pool
   int page_vec;       // 16-byte vectors per page of one layer
+  int *status;        // a pair outside either pool is skipped and reported (kStatusBadIndex)
 };
+
+// A pair whose pages lie outside their pools is skipped; thread `lead`
+// reports it. Uniform across the threads that share the pair.
+__device__ __forceinline__ bool pair_ok(const int2 pr, long long src_pages, long long dst_pages, int *status,
+                                        bool lead) {
+  if (pr.x < 0 || pr.x >= src_pages) {
+    if (lead) report_bad_index(status, kSiteCopySrcPage, pr.x);
+    return false;
+  }
+  if (pr.y < 0 || pr.y >= dst_pages) {
+    if (lead) report_bad_index(status, kSiteCopyDstPage, pr.y);
+    return false;
+  }
+  return true;
+}
 
 __global__ void __launch_bounds__(256) page_copy_kernel(const CopyArgs a) {
   // units (pair, layer, k|v), pair slowest, grid-stride: a fixed grid serves
@@ -46,6 +62,7 @@ __global__ void __launch_bounds__(256) page_copy_kernel(const CopyArgs a) {
     const int pi = (int)(u / per_pair), rem = (int)(u % per_pair);
     const int layer = rem >> 1, kv = rem & 1;
     const int2 pr = a.pairs[pi];
+    if (!pair_ok(pr, a.src_layer_pages, a.dst_layer_pages, a.status, threadIdx.x == 0)) continue;
     const uint4 *src = (kv ? a.src_v : a.src_k) + ((size_t)layer * a.src_layer_pages + pr.x) * a.page_vec;
     uint4 *dst = (kv ? a.dst_v : a.dst_k) + ((size_t)layer * a.dst_layer_pages + pr.y) * a.page_vec;
     // issue several loads before the stores: PCIe latency is microseconds
@@ -76,6 +93,7 @@ struct QuantArgs {
   int layers, heads;
   long long src_layer_pages, dst_layer_pages;
   int to_fp8;                // 1: bf16 -> fp8 (spill), 0: fp8 -> bf16 (fetch)
+  int *status;
 };
 
 constexpr int kHeadElems = 16 * 128;  // one page of one head
@@ -128,6 +146,7 @@ __global__ void __launch_bounds__(256) quant_copy_kernel(const QuantArgs a) {
     rem /= a.heads;
     const int kv = rem & 1, layer = rem >> 1;
     const int2 pr = a.pairs[pi];
+    if (!pair_ok(pr, a.src_layer_pages, a.dst_layer_pages, a.status, lane == 0)) continue;
     const size_t src_head = ((size_t)layer * a.src_layer_pages + pr.x) * a.heads + head;
     const size_t dst_head = ((size_t)layer * a.dst_layer_pages + pr.y) * a.heads + head;
     if (a.to_fp8) {
@@ -179,11 +198,12 @@ __global__ void __launch_bounds__(256) quant_copy_kernel(const QuantArgs a) {
 // Copy page data (all layers, K and V) for every (src, dst) pair from pool A
 // to pool B. Pools are [layers][pages_A|B][heads][16][128] bf16; either may be
 // pinned host memory. With `n_dev`, `n_pairs` is the capacity and the count
-// actually copied is read from *n_dev on the device. Returns 0, -1 on bad
-// arguments, -4 on a launch error.
+// actually copied is read from *n_dev on the device. A pair naming a page
+// outside its pool is skipped and reported in `status` (kStatusBadIndex).
+// Returns 0, -1 on bad arguments, -4 on a launch error.
 extern "C" int sched_kv_page_copy(const void *src_k, const void *src_v, long long src_pages, void *dst_k,
                                   void *dst_v, long long dst_pages, const int32_t *pairs, int n_pairs,
-                                  const int *n_dev, int layers, int heads, cudaStream_t st) {
+                                  const int *n_dev, int layers, int heads, int *status, cudaStream_t st) {
   if (n_pairs <= 0) return 0;
   if (layers <= 0 || heads <= 0 || src_pages <= 0 || dst_pages <= 0) return -1;
   kvtier::CopyArgs a{};
@@ -198,6 +218,7 @@ extern "C" int sched_kv_page_copy(const void *src_k, const void *src_v, long lon
   a.src_layer_pages = src_pages;
   a.dst_layer_pages = dst_pages;
   a.page_vec = heads * 16 * 128 * 2 / 16;
+  a.status = status;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -214,7 +235,7 @@ extern "C" int sched_kv_page_copy(const void *src_k, const void *src_v, long lon
 extern "C" int sched_kv_page_copy_fp8(const void *src_k, const void *src_v, long long src_pages, void *dst_k,
                                       void *dst_v, long long dst_pages, float *scale_k, float *scale_v, int to_fp8,
                                       const int32_t *pairs, int n_pairs, const int *n_dev, int layers, int heads,
-                                      cudaStream_t st) {
+                                      int *status, cudaStream_t st) {
   if (n_pairs <= 0) return 0;
   if (layers <= 0 || heads <= 0 || src_pages <= 0 || dst_pages <= 0 || !scale_k || !scale_v) return -1;
   kvtier::QuantArgs a{};
@@ -232,6 +253,7 @@ extern "C" int sched_kv_page_copy_fp8(const void *src_k, const void *src_v, long
   a.src_layer_pages = src_pages;
   a.dst_layer_pages = dst_pages;
   a.to_fp8 = to_fp8 ? 1 : 0;
+  a.status = status;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -46,6 +46,7 @@ import math
 import numpy as np
 import torch
 
+from .. import ops
 from .._ext import ext
 
 HOST_BASE = 1 << 30
@@ -166,9 +167,9 @@ class TieredKV:
         self._spill_dev[: n * 2].copy_(arr)  # pageable source: a synchronous copy
         if self.host_dtype == "fp8":
             ext().kv_page_copy_fp8(src_k, src_v, dst_k, dst_v, self.host_scale_k, self.host_scale_v, True,
-                                   self._spill_dev, n, None)
+                                   self._spill_dev, n, None, ops.status_buffer(self.device))
         else:
-            ext().kv_page_copy(src_k, src_v, dst_k, dst_v, self._spill_dev, n, None)
+            ext().kv_page_copy(src_k, src_v, dst_k, dst_v, self._spill_dev, n, None, ops.status_buffer(self.device))
 
     # ------------------------------------------------------------ staging
     def stage(self, decode_requests) -> None:
@@ -220,11 +221,11 @@ class TieredKV:
             ext().kv_page_copy_fp8(self.host_k[layer:layer + 1], self.host_v[layer:layer + 1],
                                    self.stage_k[b:b + 1], self.stage_v[b:b + 1],
                                    self.host_scale_k[layer:layer + 1], self.host_scale_v[layer:layer + 1], False,
-                                   self.pairs_dev, self.n_staging, self.count_dev)
+                                   self.pairs_dev, self.n_staging, self.count_dev, ops.status_buffer(self.device))
             return
         ext().kv_page_copy(self.host_k[layer:layer + 1], self.host_v[layer:layer + 1],
                            self.stage_k[b:b + 1], self.stage_v[b:b + 1], self.pairs_dev, self.n_staging,
-                           self.count_dev)
+                           self.count_dev, ops.status_buffer(self.device))
 
     def begin_forward(self) -> None:
         """Fork the copy stream and start the copies of layers 0 and 1."""

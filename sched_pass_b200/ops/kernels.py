@@ -14,30 +14,46 @@ _ws: dict[tuple[int, int], "Workspace"] = {}
 
 
 def status_buffer(device=None) -> torch.Tensor:
-    """The int32 word kernels write a KernelStatus code into when a bounded
-    wait gives up (0 = OK)."""
+    """The kernels' status words (int32 x 4): [0] a KernelStatus code, set by
+    the first bounded wait that gives up or the first out-of-range index
+    (0 = OK); for a bad index [1] names the site and [2..3] hold the index."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     with _lock:
         t = _status.get(idx)
         if t is None:
-            t = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+            t = torch.zeros(4, dtype=torch.int32, device=f"cuda:{idx}")
             _status[idx] = t
     return t
 
 
 STATUS_NAMES = {0: "ok", 1: "tma-timeout", 2: "mma-timeout", 3: "epilogue-timeout",
-                4: "peer-timeout", 5: "clc-timeout", 6: "bad-argument"}
+                4: "peer-timeout", 5: "clc-timeout", 6: "bad-argument", 7: "bad-index"}
+INDEX_SITES = {1: "kv page copy: source page", 2: "kv page copy: destination page", 3: "KV append: cache slot",
+               4: "embedding: token id", 5: "decode attention: block-table page"}
+
+
+class KernelStatusError(RuntimeError):
+    def __init__(self, code: int, site: int = 0, index: int = 0):
+        self.code, self.site, self.index = code, site, index
+        msg = f"kernel reported status {code} ({STATUS_NAMES.get(code, '?')})"
+        if code == 7:
+            msg += f": {INDEX_SITES.get(site, site)} {index} out of range (access skipped)"
+        super().__init__(msg)
 
 
 def check_status(device=None, clear: bool = True) -> int:
-    """Read (and clear) the status word; raises on a non-zero code."""
+    """Read (and clear) the status words; raises KernelStatusError on a
+    non-zero code."""
     s = status_buffer(device)
-    code = int(s.item())
+    w = s.cpu()
+    code = int(w[0])
     if clear and code:
         s.zero_()
     if code:
-        raise RuntimeError(f"kernel reported status {code} ({STATUS_NAMES.get(code, '?')})")
+        site = int(w[1])
+        index = int(w[2:4].view(torch.int64)[0]) if code == 7 else 0
+        raise KernelStatusError(code, site, index)
     return code
 
 
@@ -119,7 +135,8 @@ def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor | None, weight: torch.Te
 def rope_kv_append(qkv: torch.Tensor, pos: torch.Tensor, slot: torch.Tensor, cos_sin: torch.Tensor,
                    q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                    n_q_heads: int, n_kv_heads: int) -> torch.Tensor:
-    ext().rope_kv_append(qkv, pos, slot, cos_sin, q_out, k_cache, v_cache, n_q_heads, n_kv_heads)
+    ext().rope_kv_append(qkv, pos, slot, cos_sin, q_out, k_cache, v_cache, n_q_heads, n_kv_heads,
+                         status_buffer(qkv.device))
     return q_out
 
 
@@ -155,7 +172,7 @@ def attention_prefill(q, out, k_cache, v_cache, block_table, kv_lens, tiles, num
 def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
-    ext().embedding(ids, table, out)
+    ext().embedding(ids, table, out, status_buffer(ids.device))
     return out
 
 

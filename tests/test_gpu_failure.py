@@ -27,7 +27,7 @@ def test_combine_wait_for_missing_rows_times_out_with_status():
     ext().moe_combine_norm(c.data_ptr(), K, h, w, y, T, 1e-5, base, base + 4, base + 8, st)
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
-    code = int(st.item())
+    code = int(st[0].item())
     assert STATUS_NAMES.get(code) == "peer-timeout", code
     assert dt < 30
     st.zero_()
@@ -51,7 +51,7 @@ def test_expert_gemm_wait_for_absent_sources_times_out():
                           ep.rows_valid, ep.tiles_done, 1, ep.capacity, ep.mine("slab_meta"), [], [], ep.K,
                           ep.ws.data_ptr(), ep.tile_counters.data_ptr(), ep.grid, 0, st)
     torch.cuda.synchronize()
-    assert STATUS_NAMES.get(int(st.item())) == "peer-timeout"
+    assert STATUS_NAMES.get(int(st[0].item())) == "peer-timeout"
     st.zero_()
     ep.close()
     ops.check_status()

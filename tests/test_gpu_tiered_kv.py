@@ -19,13 +19,13 @@ def test_page_copy_roundtrip_through_pinned_host():
     hk = torch.zeros(L, 6, H, 16, 128, dtype=torch.bfloat16, pin_memory=True)
     hv = torch.zeros_like(hk, pin_memory=True)
     pairs = torch.tensor([[7, 0], [2, 5], [9, 3]], dtype=torch.int32, device="cuda")
-    ext().kv_page_copy(k, v, hk, hv, pairs, 3, None)
+    ext().kv_page_copy(k, v, hk, hv, pairs, 3, None, None)
     torch.cuda.synchronize()
     for s, d in ((7, 0), (2, 5), (9, 3)):
         assert torch.equal(hk[:, d], k[:, s].cpu()) and torch.equal(hv[:, d], v[:, s].cpu())
     k2, v2 = torch.zeros_like(k), torch.zeros_like(v)
     back = torch.tensor([[0, 1], [5, 4], [3, 8]], dtype=torch.int32, device="cuda")
-    ext().kv_page_copy(hk, hv, k2, v2, back, 3, None)
+    ext().kv_page_copy(hk, hv, k2, v2, back, 3, None, None)
     torch.cuda.synchronize()
     assert torch.equal(k2[:, 1], k[:, 7]) and torch.equal(v2[:, 8], v[:, 9])
 
@@ -79,7 +79,7 @@ def test_fp8_page_copy_matches_fp32_reference():
     sk = torch.zeros(L, 5, H, dtype=torch.float32, pin_memory=True)
     sv = torch.zeros_like(sk, pin_memory=True)
     pairs = torch.tensor([[7, 0], [4, 3], [1, 4]], dtype=torch.int32, device="cuda")
-    ext().kv_page_copy_fp8(k, v, hk, hv, sk, sv, True, pairs, 3, None)
+    ext().kv_page_copy_fp8(k, v, hk, hv, sk, sv, True, pairs, 3, None, None)
     torch.cuda.synchronize()
     for s, d in ((7, 0), (4, 3), (1, 4)):
         for x, hq, hs in ((k, hk, sk), (v, hv, sv)):
@@ -90,7 +90,7 @@ def test_fp8_page_copy_matches_fp32_reference():
     # fetch back through the dequantizing copy into a bf16 pool
     k2, v2 = torch.zeros_like(k), torch.zeros_like(v)
     back = torch.tensor([[0, 2], [3, 5], [4, 8]], dtype=torch.int32, device="cuda")
-    ext().kv_page_copy_fp8(hk, hv, k2, v2, sk, sv, False, back, 3, None)
+    ext().kv_page_copy_fp8(hk, hv, k2, v2, sk, sv, False, back, 3, None, None)
     torch.cuda.synchronize()
     for s, d in ((7, 2), (4, 5), (1, 8)):
         for x, y in ((k, k2), (v, v2)):

@@ -39,7 +39,7 @@ class GemmArgs(ctypes.Structure):
         ("Hq", ctypes.c_int), ("Hkv", ctypes.c_int), ("page_size", ctypes.c_int),
         ("rank", ctypes.c_int), ("world", ctypes.c_int),
         ("recv", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8),
-        ("trace", ctypes.c_void_p),
+        ("trace", ctypes.c_void_p), ("kv_pages", ctypes.c_int),
     ]
 
 
