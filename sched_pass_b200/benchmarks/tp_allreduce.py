@@ -2,8 +2,9 @@
 
 Run under torchrun (one rank per GPU). For each decode/prefill shape of the
 Llama-3-8B o_proj / down_proj at this TP degree: device time of the fused
-kernel and of the baseline (our GEMM followed by NCCL all_reduce), max over
-ranks, and the fused kernel's fraction of its roofline, where the roofline
+kernel and of the baseline (our GEMM followed by NCCL all_reduce) from
+CUDA-graph replays (as the engine runs them; eager back-to-back times are
+reported beside them), max over ranks, and the fused kernel's fraction of its roofline, where the roofline
 time is the slowest of: weight bytes / measured HBM bandwidth, FLOPs /
 measured bf16 peak, and bytes this rank must push over NVLink / 770 GB/s.
 """
@@ -25,6 +26,8 @@ NVLINK_GBPS = 770.0  # measured peer copy per direction on this pool
 
 
 def dev_time(fn, iters=30, warmup=5):
+    """ms per call of back-to-back eager launches (includes the host's
+    launch cost when that exceeds the kernel), max over ranks."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -40,6 +43,37 @@ def dev_time(fn, iters=30, warmup=5):
     return float(t)
 
 
+def graph_time(fn, iters=30, replays=5):
+    """ms per call with `iters` calls (an even number: the fused path's two
+    buffer sets alternate in capture order) captured in one CUDA graph and
+    replayed -- the device time the engine sees, as its decode steps replay
+    graphs. Max over ranks; ranks synchronise between replays."""
+    assert iters % 2 == 0
+    fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ts = []
+    for _ in range(replays + 1):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        g.replay()
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e) / iters)
+        dist.barrier()
+    del g  # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
+    t = torch.tensor([sorted(ts[1:])[len(ts[1:]) // 2]], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", default="1,16,64,256,2048")
@@ -48,6 +82,7 @@ def main():
     dev = torch.device("cuda", local)
     peaks = measured_peaks()
     fused = TensorParallel(mode="fused", device=dev)
+    fused.fused_max_bytes = 0  # time the fused kernel at every size
     base = TensorParallel(mode="nccl", device=dev)
     for name, (N, Kfull) in {"o_proj": (4096, 4096), "down_proj": (4096, 14336)}.items():
         K = Kfull // world
@@ -55,8 +90,10 @@ def main():
         for T in (int(t) for t in args.tokens.split(",")):
             x = torch.randn(T, K, device=dev).to(torch.bfloat16)
             y = torch.empty(T, N, dtype=torch.bfloat16, device=dev)
-            t_f = dev_time(lambda: fused.linear_allreduce(x, w, y))
-            t_b = dev_time(lambda: base.linear_allreduce(x, w, y))
+            t_fe = dev_time(lambda: fused.linear_allreduce(x, w, y))
+            t_be = dev_time(lambda: base.linear_allreduce(x, w, y))
+            t_f = graph_time(lambda: fused.linear_allreduce(x, w, y))
+            t_b = graph_time(lambda: base.linear_allreduce(x, w, y))
             wbytes = N * K * 2
             t_hbm = wbytes / (peaks["hbm_gbs"] * 1e9)
             t_flop = 2 * T * N * K / (peaks["bf16_tflops"] * 1e12)
@@ -64,7 +101,9 @@ def main():
             roof = max(t_hbm, t_flop, t_nvl)
             rec = {"op": name, "tp": world, "T": T, "N": N, "K_local": K,
                    "fused_us": round(t_f * 1e3, 2), "gemm_plus_nccl_us": round(t_b * 1e3, 2),
+                   "eager_fused_us": round(t_fe * 1e3, 2), "eager_gemm_plus_nccl_us": round(t_be * 1e3, 2),
                    "speedup": round(t_b / t_f, 3), "roofline_us": round(roof * 1e6, 2),
+                   "oneshot_push_bytes": (world - 1) * T * N * 2,
                    "bound": ["hbm", "tensor", "nvlink"][[t_hbm, t_flop, t_nvl].index(roof)],
                    "frac_of_roofline": round(roof * 1e3 / t_f, 3)}
             if rank == 0:

@@ -8,6 +8,12 @@ between consecutive calls so a fast rank can run one call ahead without
 overwriting data a slower rank is still reading (the next use of a set is
 causally after the slow rank finished with it: the fast rank needs the slow
 rank's pushes of the intervening call first).
+
+Under CUDA graphs the sets alternate in capture order, so a replay reuses
+the sequence it was captured with. Two calls in a row on the same set are
+only safe after a cross-rank synchronisation: the engine's step ends with
+one (every rank waits for its step, then all-reduces the step time), and a
+graph that is replayed back to back must capture an even number of calls.
 """
 from __future__ import annotations
 

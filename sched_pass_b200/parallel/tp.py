@@ -6,11 +6,19 @@ vocabulary-parallel sampling.
 are added across ranks. Two implementations share the interface:
 
 * ``fused`` (default on >= 2 GPUs): one sm_100a kernel per projection that
-  runs the tcgen05 GEMM and pushes each finished fp32 tile to every peer's
-  symmetric buffer over NVLink (peer stores), then reduces the peers' tiles
-  locally after a per-tile flag handshake (``comm/fused_collective.cu``);
+  runs the tcgen05 GEMM and pushes each finished bf16 partial tile to every
+  peer's symmetric buffer over NVLink (peer stores), then reduces the
+  peers' tiles locally after a per-chunk flag handshake (``kEpiAllReduce``
+  in ``csrc/kernels/gemm.cu``; ``parallel/fused.py``);
 * ``nccl``: the GEMM kernel followed by ``all_reduce`` on NCCL -- the
   baseline the fused path is measured against.
+
+The fused kernel is a one-shot all-reduce: each rank pushes its whole
+partial to every peer, (W - 1) x T x N x 2 bytes, where a ring or NVLS
+all-reduce moves about 2 (W - 1) / W of one partial. It wins while its
+lower fixed latency dominates (decode-sized T) and loses once the bytes do,
+so ``fused_max_bytes`` (``SCHED_TP_FUSED_MAX_BYTES``) routes projections
+whose one-shot push exceeds it to GEMM + NCCL.
 """
 from __future__ import annotations
 
@@ -21,6 +29,9 @@ import torch.distributed as dist
 
 from .. import ops
 
+# one-shot push bytes per rank up to which the fused kernel is used (0 = always)
+DEFAULT_FUSED_MAX_BYTES = 0
+
 
 class TensorParallel:
     def __init__(self, group=None, mode: str | None = None, device=None):
@@ -30,10 +41,21 @@ class TensorParallel:
         self.device = torch.device(device) if device is not None else torch.device(
             "cuda", torch.cuda.current_device())
         self.mode = mode or os.environ.get("SCHED_TP_MODE", "fused")
+        # one-shot push bytes above which the NCCL path is used (0: always fused)
+        self.fused_max_bytes = int(os.environ.get("SCHED_TP_FUSED_MAX_BYTES", str(DEFAULT_FUSED_MAX_BYTES)))
+        self.fused_calls = 0
+        self.nccl_calls = 0
         self._fused = None
         if self.mode == "fused" and self.world > 1:
             from .fused import FusedAllReduce
             self._fused = FusedAllReduce(self.group, self.device)
+
+    def use_fused(self, T: int, N: int) -> bool:
+        """Whether a [T, N] row-parallel output goes through the one-shot
+        fused kernel (the same answer on every rank: it depends on shapes only)."""
+        if self.fused_max_bytes <= 0:
+            return True
+        return (self.world - 1) * T * N * 2 <= self.fused_max_bytes
 
     def max_over_ranks(self, value: float) -> float:
         """The maximum of a host scalar over the group (one small collective)."""
@@ -49,8 +71,10 @@ class TensorParallel:
     def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return ops.linear(x, w, out)
-        if self._fused is not None:
+        if self._fused is not None and self.use_fused(x.shape[0], w.shape[0]):
+            self.fused_calls += 1
             return self._fused.linear_allreduce(x, w, out)
+        self.nccl_calls += 1
         ops.linear(x, w, out)
         dist.all_reduce(out, group=self.group)
         return out
