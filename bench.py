@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--requests", type=int, default=2000)
     ap.add_argument("--max-batch", type=int, default=128)
     ap.add_argument("--acquire", default="auto", choices=["static", "ticket", "clc", "auto"])
-    ap.add_argument("--tp-mode", default=None, choices=[None, "fused", "nccl"])
+    ap.add_argument("--tp-mode", default=None, choices=[None, "fused", "nccl", "sp"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
     return ap.parse_args()

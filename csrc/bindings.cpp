@@ -11,6 +11,7 @@
 
 #include "gemm_api.h"
 #include "sched/abi.h"
+#include "sp_api.h"
 
 extern "C" {
 int sched_attn_decode(const void *q, void *out, const void *k_cache, const void *v_cache,
@@ -129,10 +130,12 @@ GemmArgs base_args(const at::Tensor &x, const at::Tensor &w, int64_t grid,
   return a;
 }
 
+// x_ready: address of the gathered rows' ready flags (0: x is local and ready)
 void gemm(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int64_t epi, int64_t grid,
           const c10::optional<at::Tensor> &ws, const c10::optional<at::Tensor> &counters,
-          const c10::optional<at::Tensor> &status) {
+          const c10::optional<at::Tensor> &status, int64_t x_ready) {
   GemmArgs a = base_args(x, w, grid, ws, counters, status);
+  a.x_ready = reinterpret_cast<const uint32_t *>(x_ready);
   check_bf16(y, "y");
   TORCH_CHECK(y.dim() == 2 && y.stride(1) == 1 && y.size(0) >= a.T, "y [T, ldy]");
   TORCH_CHECK(epi == kEpiStore ? y.size(1) >= a.N : y.size(1) >= a.N / 2, "y columns");
@@ -149,8 +152,9 @@ void gemm_qkv_rope(const at::Tensor &x, const at::Tensor &w, const at::Tensor &p
                    at::Tensor &k_cache, at::Tensor &v_cache, int64_t Hq, int64_t Hkv,
                    int64_t grid, const c10::optional<at::Tensor> &ws,
                    const c10::optional<at::Tensor> &counters,
-                   const c10::optional<at::Tensor> &status) {
+                   const c10::optional<at::Tensor> &status, int64_t x_ready) {
   GemmArgs a = base_args(x, w, grid, ws, counters, status);
+  a.x_ready = reinterpret_cast<const uint32_t *>(x_ready);
   check_i32(pos, "pos");
   check_i32(slot, "slot");
   check_bf16(q_out, "q_out");
@@ -199,6 +203,76 @@ void gemm_allreduce(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int
   }
   c10::cuda::CUDAGuard g(x.device());
   check_rc(sched_gemm_run(&a, cur_stream()), "gemm_allreduce");
+}
+
+// Row-parallel projection, sequence-parallel output: each finished row goes
+// to the slab of the rank that owns the token (kEpiReduceScatter); the owner
+// reduces it in sp_reduce_norm. recv/flags: every rank's slab and row flags.
+void gemm_reduce_scatter(const at::Tensor &x, const at::Tensor &w, int64_t rank, int64_t world,
+                         const std::vector<int64_t> &recv, const std::vector<int64_t> &flags,
+                         int64_t grid, const c10::optional<at::Tensor> &ws,
+                         const c10::optional<at::Tensor> &counters,
+                         const c10::optional<at::Tensor> &status) {
+  GemmArgs a = base_args(x, w, grid, ws, counters, status);
+  TORCH_CHECK(world >= 1 && world <= kMaxWorld && (int64_t)recv.size() == world &&
+                  (int64_t)flags.size() == world,
+              "one slab and one flag array per rank");
+  a.epi = kEpiReduceScatter;
+  a.rank = rank;
+  a.world = world;
+  for (int j = 0; j < world; ++j) {
+    a.recv[j] = reinterpret_cast<__nv_bfloat16 *>(recv[j]);
+    a.flags[j] = reinterpret_cast<uint32_t *>(flags[j]);
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  check_rc(sched_gemm_run(&a, cur_stream()), "gemm_reduce_scatter");
+}
+
+// Sequence-parallel reduce + residual + RMSNorm + all-gather push (sp_api.h).
+void sp_reduce_norm(int64_t slab, int64_t row_flags, at::Tensor &res, const at::Tensor &w,
+                    const c10::optional<at::Tensor> &delta, const std::vector<int64_t> &gather,
+                    const std::vector<int64_t> &ready, int64_t clear, int64_t clear_n, int64_t T,
+                    int64_t rank, int64_t world, double eps, const c10::optional<at::Tensor> &status) {
+  check_bf16(res, "res");
+  check_bf16(w, "w");
+  TORCH_CHECK(res.dim() == 2 && res.is_contiguous() && res.size(0) >= T, "res [>= T, H] contiguous");
+  const int64_t H = res.size(1);
+  TORCH_CHECK(w.numel() == H && w.is_contiguous(), "w [H]");
+  TORCH_CHECK(world >= 1 && world <= kMaxWorld && (int64_t)gather.size() == world &&
+                  (int64_t)ready.size() == world && rank >= 0 && rank < world,
+              "one gather buffer and one ready array per rank");
+  SpNormArgs a{};
+  a.slab = reinterpret_cast<const __nv_bfloat16 *>(slab);
+  a.row_flags = reinterpret_cast<uint32_t *>(row_flags);
+  a.res = reinterpret_cast<__nv_bfloat16 *>(res.data_ptr());
+  a.w = reinterpret_cast<const __nv_bfloat16 *>(w.data_ptr());
+  if (delta.has_value() && delta->defined()) {
+    check_bf16(*delta, "delta");
+    TORCH_CHECK(delta->is_contiguous() && delta->size(0) >= T && delta->size(1) == H, "delta [>= T, H]");
+    a.delta = reinterpret_cast<__nv_bfloat16 *>(delta->data_ptr());
+  }
+  for (int j = 0; j < world; ++j) {
+    a.gather[j] = reinterpret_cast<__nv_bfloat16 *>(gather[j]);
+    a.ready[j] = reinterpret_cast<uint32_t *>(ready[j]);
+  }
+  a.clear = reinterpret_cast<uint32_t *>(clear);
+  a.clear_n = clear_n;
+  a.T = T;
+  a.H = H;
+  a.rank = rank;
+  a.world = world;
+  a.eps = (float)eps;
+  a.status = ptr_or_null<int>(status);
+  c10::cuda::CUDAGuard g(res.device());
+  check_rc(sched_sp_reduce_norm(&a, cur_stream()), "sp_reduce_norm");
+}
+
+void sp_wait_rows(int64_t ready, int64_t T, const at::Tensor &status) {
+  check_cuda(status, "status");
+  c10::cuda::CUDAGuard g(status.device());
+  check_rc(sched_sp_wait_rows(reinterpret_cast<const uint32_t *>(ready), T,
+                              static_cast<int *>(status.data_ptr()), cur_stream()),
+           "sp_wait_rows");
 }
 
 int64_t gemm_ws_floats(int64_t T, int64_t N, int64_t K, int64_t grid) {
@@ -550,6 +624,9 @@ void register_symm(py::module &m);
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_symm(m);
   m.def("gemm_allreduce", &gemm_allreduce);
+  m.def("gemm_reduce_scatter", &gemm_reduce_scatter);
+  m.def("sp_reduce_norm", &sp_reduce_norm);
+  m.def("sp_wait_rows", &sp_wait_rows);
   m.doc() = "sched_pass_b200 sm_100a kernels";
   m.def("gemm", &gemm);
   m.def("gemm_qkv_rope", &gemm_qkv_rope);

@@ -7,7 +7,11 @@
 //     writes q to the attention input and k, v straight into their pages of
 //     the paged cache (no intermediate k/v tensors);
 //   * token embedding gather;
-//   * greedy sampling (row argmax over the vocabulary).
+//   * greedy sampling (row argmax over the vocabulary);
+//   * the sequence-parallel norm of the tensor-parallel layer: reduction of
+//     the world's row partials (pushed by the reduce-scatter GEMM), residual
+//     add + RMSNorm with the same arithmetic as the fused add + RMSNorm, and
+//     the all-gather push of the normed row to every rank.
 // All accesses are 16-byte vectors; one CTA per token row.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -16,6 +20,7 @@
 
 #include "common.cuh"
 #include "sched/ptx.cuh"
+#include "sp_api.h"
 
 namespace ew {
 
@@ -226,6 +231,108 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16 *__res
   }
 }
 
+// Sequence-parallel norm: one CTA per owned row t. The arithmetic after the
+// reduction is add_rmsnorm_kernel's, with the same NT / VPT, so the normed
+// rows are bit-identical to those of the all-reduce path.
+template <int NT, int VPT>
+__global__ void __launch_bounds__(NT) sp_reduce_norm_kernel(const SpNormArgs a) {
+  __shared__ float red[NT / 32];
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  for (int i = blockIdx.x * NT + threadIdx.x; i < a.clear_n; i += gridDim.x * NT) a.clear[i] = 0u;
+  const int t = sp_row_begin(a.rank, a.T, a.world) + (int)blockIdx.x;
+  if (t >= sp_row_begin(a.rank + 1, a.T, a.world)) return;  // a rank without rows clears only
+  const int H = a.H;
+  const int nflags = a.world * (H / 128);
+  // every source rank's every 128-column tile of the row has landed
+  for (int i = threadIdx.x; i < nflags; i += NT) {
+    const uint32_t *f = a.row_flags + (size_t)i * a.T + t;
+    if (ptx::ld_acquire_sys(f) == 0u) {
+      const uint64_t start = ptx::globaltimer_ns();
+      bool ok = false;
+      while (!ok) {
+        for (int k = 0; k < 64 && !ok; ++k) ok = ptx::ld_acquire_sys(f) != 0u;
+        if (!ok && ptx::globaltimer_ns() - start > kWaitBudgetNs) break;
+      }
+      if (!ok) report_status(a.status, kStatusPeerTimeout);
+    }
+  }
+  __syncthreads();
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * NT) * 8;
+    if (c < H) {
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int src = 0; src < a.world; ++src) {  // rank order: the same sum on every rank
+        const uint4 u = __ldcv(reinterpret_cast<const uint4 *>(a.slab + ((size_t)src * a.T + t) * H + c));
+        const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += __bfloat162float(e[j]);
+      }
+      uint4 dv;
+      dv.x = pack_bf16x2(acc[0], acc[1]);
+      dv.y = pack_bf16x2(acc[2], acc[3]);
+      dv.z = pack_bf16x2(acc[4], acc[5]);
+      dv.w = pack_bf16x2(acc[6], acc[7]);
+      if (a.delta != nullptr) *reinterpret_cast<uint4 *>(a.delta + (size_t)t * H + c) = dv;
+      const __nv_bfloat16 *xe = reinterpret_cast<const __nv_bfloat16 *>(&dv);
+      const uint4 rv = *reinterpret_cast<const uint4 *>(a.res + (size_t)t * H + c);
+      const __nv_bfloat16 *re = reinterpret_cast<const __nv_bfloat16 *>(&rv);
+      uint4 ov;
+      __nv_bfloat16 *oe = reinterpret_cast<__nv_bfloat16 *>(&ov);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        oe[j] = __float2bfloat16(__bfloat162float(xe[j]) + __bfloat162float(re[j]));
+        v[i][j] = __bfloat162float(oe[j]);
+      }
+      *reinterpret_cast<uint4 *>(a.res + (size_t)t * H + c) = ov;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  const float inv = rsqrtf(block_sum<NT>(ss, red) / (float)H + a.eps);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = (threadIdx.x + i * NT) * 8;
+    if (c < H) {
+      uint4 wv = *reinterpret_cast<const uint4 *>(a.w + c);
+      const __nv_bfloat16 *we = reinterpret_cast<const __nv_bfloat16 *>(&wv);
+      uint4 ov;
+      ov.x = pack_bf16x2(v[i][0] * inv * __bfloat162float(we[0]), v[i][1] * inv * __bfloat162float(we[1]));
+      ov.y = pack_bf16x2(v[i][2] * inv * __bfloat162float(we[2]), v[i][3] * inv * __bfloat162float(we[3]));
+      ov.z = pack_bf16x2(v[i][4] * inv * __bfloat162float(we[4]), v[i][5] * inv * __bfloat162float(we[5]));
+      ov.w = pack_bf16x2(v[i][6] * inv * __bfloat162float(we[6]), v[i][7] * inv * __bfloat162float(we[7]));
+      for (int j = 0; j < a.world; ++j)  // all-gather: NVLink stores into every rank's copy
+        *reinterpret_cast<uint4 *>(a.gather[j] + (size_t)t * H + c) = ov;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if ((int)threadIdx.x < a.world) ptx::st_release_sys(a.ready[threadIdx.x] + t, 1u);
+  // the row's partials are consumed: its flags are zero for the slab set's next use
+  for (int i = threadIdx.x; i < nflags; i += NT) a.row_flags[(size_t)i * a.T + t] = 0u;
+}
+
+__global__ void __launch_bounds__(256) sp_wait_rows_kernel(const uint32_t *ready, int T, int *status) {
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    if (ptx::ld_acquire_sys(ready + t) != 0u) continue;
+    const uint64_t start = ptx::globaltimer_ns();
+    bool ok = false;
+    while (!ok) {
+      for (int k = 0; k < 64 && !ok; ++k) ok = ptx::ld_acquire_sys(ready + t) != 0u;
+      if (!ok && ptx::globaltimer_ns() - start > kWaitBudgetNs) break;
+    }
+    if (!ok) report_status(status, kStatusPeerTimeout);
+  }
+  __syncthreads();
+}
+
 }  // namespace ew
 
 extern "C" int sched_add_rmsnorm(const void *x, void *res, const void *w, void *y, int T, int H,
@@ -273,5 +380,35 @@ extern "C" int sched_argmax(const void *logits, int T, int V, int ld, int32_t *i
   if (T <= 0) return 0;
   launch_pdl(ew::argmax_kernel, T, 1024, 0, st, static_cast<const __nv_bfloat16 *>(logits), V, ld,
              ids, maxv, id_offset);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int sched_sp_reduce_norm(const SpNormArgs *args, cudaStream_t st) {
+  if (args == nullptr) return -1;
+  const SpNormArgs &a = *args;
+  if (a.T <= 0) return 0;
+  if (a.H % 128 != 0 || a.world < 1 || a.world > kMaxWorld || a.rank < 0 || a.rank >= a.world) return -1;
+  if (a.slab == nullptr || a.row_flags == nullptr || a.res == nullptr || a.w == nullptr) return -1;
+  for (int j = 0; j < a.world; ++j)
+    if (a.gather[j] == nullptr || a.ready[j] == nullptr) return -1;
+  if (a.clear_n > 0 && a.clear == nullptr) return -1;
+  const int rows = sp_row_begin(a.rank + 1, a.T, a.world) - sp_row_begin(a.rank, a.T, a.world);
+  const int grid = rows > 0 ? rows : 1;
+  // the thread shapes of sched_add_rmsnorm (same reduction order)
+  if (a.H <= 256 * 8 * 2)
+    launch_pdl(ew::sp_reduce_norm_kernel<256, 2>, grid, 256, 0, st, a);
+  else if (a.H <= 512 * 8 * 2)
+    launch_pdl(ew::sp_reduce_norm_kernel<512, 2>, grid, 512, 0, st, a);
+  else if (a.H <= 1024 * 8 * 2)
+    launch_pdl(ew::sp_reduce_norm_kernel<1024, 2>, grid, 1024, 0, st, a);
+  else
+    return -1;
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int sched_sp_wait_rows(const uint32_t *ready, int T, int *status, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (ready == nullptr) return -1;
+  launch_pdl(ew::sp_wait_rows_kernel, 1, 256, 0, st, ready, T, status);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

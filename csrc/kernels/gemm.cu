@@ -159,7 +159,7 @@ __device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, 
     o.w = pack_bf16x2(g[6], g[7]);
     *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(a.y) + (size_t)t * a.ldy +
                                n_tile * (BM / 2) + c) = o;
-  } else if (EPI == kEpiAllReduce) {
+  } else if (EPI == kEpiAllReduce || EPI == kEpiReduceScatter) {
     const int c = k * 16;
     uint4 o0, o1;
     o0.x = pack_bf16x2(v[c + 0], v[c + 1]);
@@ -171,8 +171,14 @@ __device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, 
     o1.z = pack_bf16x2(v[c + 12], v[c + 13]);
     o1.w = pack_bf16x2(v[c + 14], v[c + 15]);
     const size_t off = ((size_t)a.rank * a.T + t) * a.N + (size_t)n_tile * BM + c;
-    for (int j = 0; j < a.world; ++j) {  // NVLink stores into every rank's slab
-      uint4 *dst = reinterpret_cast<uint4 *>(a.recv[j] + off);
+    if (EPI == kEpiAllReduce) {
+      for (int j = 0; j < a.world; ++j) {  // NVLink stores into every rank's slab
+        uint4 *dst = reinterpret_cast<uint4 *>(a.recv[j] + off);
+        dst[0] = o0;
+        dst[1] = o1;
+      }
+    } else {  // only the owner of the token reduces it
+      uint4 *dst = reinterpret_cast<uint4 *>(a.recv[sp_row_owner(t, a.T, a.world)] + off);
       dst[0] = o0;
       dst[1] = o1;
     }
@@ -279,6 +285,68 @@ __device__ __forceinline__ void publish_rows(const Params &p, int tile, int lo, 
     const int j = i / chunks, ch = c_first + i % chunks;
     ptx::red_add_release_sys(a.flags[j] + ((size_t)a.rank * p.tiles + tile) * CH + ch, 1u);
   }
+}
+
+// Reduce-scatter: after this CTA stored the token rows [lo, hi) of `tile`
+// (tile-local row indices) into their owners' slabs, raise each row's flag
+// (source = this rank, n-tile, token) in the owner's row-flag array. Every
+// row is written by exactly one CTA (stream-K: the tile's finishing segment;
+// cluster split-K: the cluster rank whose share holds it), so the owner waits
+// for the value 1.
+template <int TN>
+__device__ __forceinline__ void publish_rows_rs(const Params &p, int tile, int lo, int hi, int et) {
+  const GemmArgs &a = p.a;
+  __threadfence_system();
+  named_bar(1, kEpiThreads);
+  const int nt = tile / p.t_tiles, t0 = (tile % p.t_tiles) * TN;
+  for (int r = lo + et; r < hi; r += kEpiThreads) {
+    const int t = t0 + r;
+    uint32_t *f = a.flags[sp_row_owner(t, a.T, a.world)] + ((size_t)a.rank * p.n_tiles + nt) * a.T + t;
+    ptx::st_release_sys(f, 1u);
+  }
+}
+
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t *p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+// Gathered activations: the producer lane waits until the rows [r0, r1) of X
+// have been raised in x_ready (r0 is a multiple of 16). Flags are polled
+// eight 16-byte vectors at a time (the loads of a batch are in flight
+// together); once all are set, a system-scope fence turns the observation
+// into an acquire of the owners' releases, and a proxy fence orders it
+// before this thread's TMA (async-proxy) reads of the rows. On timeout the
+// status word is set and the loads go ahead (no hang).
+__device__ __noinline__ void wait_rows_ready(const uint32_t *ready, int r0, int r1, int *status) {
+  const uint64_t start = ptx::globaltimer_ns();
+  for (;;) {
+    bool all = true;
+    for (int t = r0; t < r1; t += 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (t + 4 * u < r1) v[u] = ld_volatile_v4(ready + t + 4 * u);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int b = t + 4 * u;
+        if (b < r1)
+          all = all && v[u].x != 0u && (b + 1 >= r1 || v[u].y != 0u) && (b + 2 >= r1 || v[u].z != 0u) &&
+                (b + 3 >= r1 || v[u].w != 0u);
+      }
+    }
+    if (all) break;
+    if (ptx::globaltimer_ns() - start > kWaitBudgetNs) {
+      report_status(status, kStatusPeerTimeout);
+      return;
+    }
+  }
+  ptx::fence_acq_rel_sys();
+  ptx::fence_proxy_async_global();
 }
 
 // All-reduce, part 2: the reduction units are (tile, 16-token chunk); CTA c
@@ -425,6 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int k = 0; ok && segment(p, c, k, s); ++k) {
         const int nt = s.tile / p.t_tiles, tt = s.tile % p.t_tiles;
+        if (a.x_ready) wait_rows_ready(a.x_ready, tt * TN, min(a.T, tt * TN + TN), a.status);
         for (int kb = s.kb0; kb < s.kb1; ++kb, ++i) {
           const int st = i % S;
           uint8_t *sm = stage_mem + st * C::STAGE_BYTES;
@@ -521,6 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_before();
       ptx::mbar_arrive(&acc_empty[ab]);  // the MMA warp may refill this accumulator
       if (EPI == kEpiAllReduce && direct) publish_tile<TN>(p, s.tile, et);
+      if (EPI == kEpiReduceScatter && direct) publish_rows_rs<TN>(p, s.tile, 0, min(TN, a.T - t0), et);
       if (!direct) {
         __threadfence();
         named_bar(1, kEpiThreads);
@@ -576,6 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (et == 0) a.counters[s.tile] = 0u;
           if (EPI == kEpiAllReduce) publish_tile<TN>(p, s.tile, et);
+          if (EPI == kEpiReduceScatter) publish_rows_rs<TN>(p, s.tile, 0, tmax, et);
         }
         named_bar(1, kEpiThreads);  // last_flag is rewritten by the next segment
       }
@@ -688,6 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = cid; ok && tile < p.tiles; tile += nclusters) {
         const int nt = tile / p.t_tiles, tt = tile % p.t_tiles;
+        if (a.x_ready) wait_rows_ready(a.x_ready, tt * TN, min(a.T, tt * TN + TN), a.status);
         for (int kb = kb0; kb < kb1; ++kb, ++i) {
           const int st = i % S;
           uint8_t *sm = stage_mem + st * C::STAGE_BYTES;
@@ -772,6 +844,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_before();
         ptx::mbar_arrive(&acc_empty[ab]);
         if (EPI == kEpiAllReduce) publish_rows<TN>(p, tile, 0, tvalid, et);
+        if (EPI == kEpiReduceScatter) publish_rows_rs<TN>(p, tile, 0, tvalid, et);
         continue;
       }
       // our partial may overwrite `red` once every peer has read the previous one
@@ -832,6 +905,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (et == 0)
         for (int s2 = 0; s2 < CS; ++s2) ptx::mbar_arrive_cluster(ptx::mapa_shared(free_addr, s2));
       if (EPI == kEpiAllReduce) publish_rows<TN>(p, tile, lo, hi, et);
+      if (EPI == kEpiReduceScatter) publish_rows_rs<TN>(p, tile, lo, hi, et);
     }
     if (EPI == kEpiAllReduce) reduce_owned_chunks<TN>(p, blockIdx.x, et);
   }
@@ -1080,6 +1154,8 @@ extern "C" void sched_gemm_plan(int T, int N, int K, int epi, int num_sms, int *
       gemm::plan_cluster_for<kEpiRopeKV>(tn, p, num_sms);
     else if (epi == kEpiAllReduce)
       gemm::plan_cluster_for<kEpiAllReduce>(tn, p, num_sms);
+    else if (epi == kEpiReduceScatter)
+      gemm::plan_cluster_for<kEpiReduceScatter>(tn, p, num_sms);
     else
       gemm::plan_cluster_for<kEpiStore>(tn, p, num_sms);
     if (p.cs == 0) gemm::plan(a, p, tn);
@@ -1108,6 +1184,8 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
       gemm::plan_cluster_for<kEpiRopeKV>(tn, p, sms);
     else if (a.epi == kEpiAllReduce)
       gemm::plan_cluster_for<kEpiAllReduce>(tn, p, sms);
+    else if (a.epi == kEpiReduceScatter)
+      gemm::plan_cluster_for<kEpiReduceScatter>(tn, p, sms);
     else
       gemm::plan_cluster_for<kEpiStore>(tn, p, sms);
     if (p.cs == 0) gemm::plan(a, p, tn);  // back to the stream-K grid
@@ -1121,7 +1199,8 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   if (a.epi == kEpiRopeKV && (a.N / gemm::BM != a.Hq + 2 * a.Hkv || a.cos_sin == nullptr ||
                               a.pos == nullptr || a.slot == nullptr))
     return -6;
-  if (a.epi == kEpiAllReduce) {
+  if (a.x_ready != nullptr && (reinterpret_cast<uintptr_t>(a.x_ready) & 15) != 0) return -7;
+  if (a.epi == kEpiAllReduce || a.epi == kEpiReduceScatter) {
     if (a.world < 1 || a.world > kMaxWorld || a.rank < 0 || a.rank >= a.world) return -7;
     for (int j = 0; j < a.world; ++j)
       if (a.recv[j] == nullptr || a.flags[j] == nullptr) return -7;
@@ -1135,6 +1214,8 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
       gemm::dispatch<kEpiSwiGLU>(tn, tw, tx, p, stream);
     else if (a.epi == kEpiAllReduce)
       gemm::dispatch<kEpiAllReduce>(tn, tw, tx, p, stream);
+    else if (a.epi == kEpiReduceScatter)
+      gemm::dispatch<kEpiReduceScatter>(tn, tw, tx, p, stream);
     else if (a.epi == kEpiRopeKV)
       gemm::dispatch<kEpiRopeKV>(tn, tw, tx, p, stream);
     else
@@ -1183,7 +1264,8 @@ static bool fixed_scratch(FixedScratch &out) {
 }  // namespace gemm
 
 extern "C" int sched_gemm_run_fixed_scratch(const GemmArgs *args, cudaStream_t stream) {
-  if (args == nullptr || args->epi == kEpiAllReduce) return kFixedScratchBadEpilogue;
+  if (args == nullptr || args->epi == kEpiAllReduce || args->epi == kEpiReduceScatter)
+    return kFixedScratchBadEpilogue;
   GemmArgs a = *args;
   if (a.T <= 0) return 0;
   if (a.N % gemm::BM != 0 || a.K % gemm::BK != 0) return -1;

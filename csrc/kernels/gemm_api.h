@@ -11,7 +11,25 @@ enum GemmEpilogue : int {
   kEpiRopeKV = 2,  // fused QKV: rotate q/k heads, write q to q_out, k/v into the paged cache
   kEpiAllReduce = 3,  // row-parallel: push bf16 partial tiles to every rank over NVLink,
                       // then each rank sums the world's partials of the tiles it owns
+  kEpiReduceScatter = 4,  // row-parallel, sequence-parallel output: push each finished bf16
+                          // row only to the rank that owns the token and raise its row flag;
+                          // the owner reduces (sched_sp_reduce_norm), no reduction here
 };
+
+// Token ownership of the sequence-parallel path: rank r owns the contiguous
+// rows [r*T/world, (r+1)*T/world) (some ranks own none when T < world).
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline int sp_row_owner(int t, int T, int world) {
+  return (int)(((long long)(t + 1) * world - 1) / T);
+}
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline int sp_row_begin(int r, int T, int world) {
+  return (int)((long long)r * T / world);
+}
 
 constexpr int kMaxWorld = 8;
 
@@ -39,7 +57,10 @@ struct GemmArgs {
   int Hq, Hkv, page_size;
   // kEpiAllReduce only: this rank's view of every rank's receive slab
   // [world][T][N] (bf16 partials) and flag array [world][tiles][TN/16] (u32,
-  // zero between calls: the owner of a chunk resets its flags after use)
+  // zero between calls: the owner of a chunk resets its flags after use).
+  // kEpiReduceScatter: the same slabs; the flag arrays are row flags
+  // [world (source)][N/128][T] (u32, zero between calls: the owner of a row
+  // resets them when it has reduced the row).
   int rank, world;
   __nv_bfloat16 *recv[kMaxWorld];
   uint32_t *flags[kMaxWorld];
@@ -49,6 +70,12 @@ struct GemmArgs {
   // kEpiRopeKV: pages of the KV cache; a token slot beyond them is reported
   // (kStatusBadIndex, site kSiteKvSlot) and not written. 0: unchecked.
   int kv_pages;
+  // Gathered input (any epilogue; nullptr: none). Row t of x is read only
+  // after x_ready[t] != 0: the owner of the row raises it with a
+  // system-scope release once the row has landed in this rank's copy of x
+  // (sched_sp_reduce_norm's all-gather push). Must be 16-byte aligned and
+  // readable up to T rounded up to a multiple of 4.
+  const uint32_t *x_ready;
 };
 
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream);
@@ -88,14 +115,15 @@ extern "C" long long sched_gemm_ws_floats(int T, int N, int K, int grid);
 //     (cudaGetSymbolAddress, with that device current) and caches them;
 //     make that first call before any stream capture begins. The stream must
 //     belong to the current device.
-//   * kEpiAllReduce is refused (kFixedScratchBadEpilogue): its peer receive
-//     buffers come from a symmetric allocation.
+//   * kEpiAllReduce and kEpiReduceScatter are refused
+//     (kFixedScratchBadEpilogue): their peer receive buffers come from a
+//     symmetric allocation.
 // Returns 0, a sched_gemm_run code, or one of the codes below.
 constexpr long long kFixedScratchWsFloats = 1ll << 22;
 constexpr int kFixedScratchCounters = 1 << 14;
 enum FixedScratchError : int {
   kFixedScratchTooLarge = -8,      // the call needs more scratch than the fixed capacity
   kFixedScratchLookupFailed = -9,  // no current device, or cudaGetSymbolAddress failed
-  kFixedScratchBadEpilogue = -10,  // kEpiAllReduce or a null args pointer
+  kFixedScratchBadEpilogue = -10,  // kEpiAllReduce, kEpiReduceScatter or a null args pointer
 };
 extern "C" int sched_gemm_run_fixed_scratch(const GemmArgs *args, cudaStream_t stream);

@@ -7,6 +7,12 @@ CUDA-graph replays (as the engine runs them; eager back-to-back times are
 reported beside them), max over ranks, and the fused kernel's fraction of its roofline, where the roofline
 time is the slowest of: weight bytes / measured HBM bandwidth, FLOPs /
 measured bf16 peak, and bytes this rank must push over NVLink / 770 GB/s.
+
+``--sp`` adds the sequence-parallel sub-layer ("projection + residual add +
+RMSNorm, ready for the next GEMM") in its three forms: fused all-reduce +
+add_rmsnorm, GEMM + NCCL all-reduce + add_rmsnorm, and GEMM -> reduce-scatter
++ the owner's reduce/norm/all-gather kernel (parallel/sp.py), whose roofline
+counts 2 (W-1)/W x T x N x 2 NVLink bytes.
 """
 from __future__ import annotations
 
@@ -74,9 +80,53 @@ def graph_time(fn, iters=30, replays=5):
     return float(t)
 
 
+def sp_sublayer(args, shapes, world, rank, dev, peaks, fused, base):
+    """Row-parallel projection + residual add + RMSNorm, three ways (graph
+    replays, max over ranks)."""
+    sptp = TensorParallel(mode="sp", device=dev)
+    tokens = [int(t) for t in args.tokens.split(",")]
+    sp = sptp.sequence_parallel(4096, max(tokens))
+    lnw = torch.ones(4096, dtype=torch.bfloat16, device=dev)
+    for name, (N, Kfull) in shapes.items():
+        K = Kfull // world
+        w = (torch.randn(N, K, device=dev) / math.sqrt(Kfull)).to(torch.bfloat16)
+        for T in tokens:
+            x = torch.randn(T, K, device=dev).to(torch.bfloat16)
+            y = torch.empty(T, N, dtype=torch.bfloat16, device=dev)
+            res = torch.randn(T, N, device=dev).to(torch.bfloat16)
+            normed = torch.empty_like(y)
+
+            def ar_path(tp):
+                tp.linear_allreduce(x, w, y)
+                ops.add_rmsnorm(y, res, lnw, 1e-5, normed)
+
+            def sp_path():
+                sp.linear_rs(x, w)
+                sp.reduce_norm(res, lnw, 1e-5, T)
+
+            t_f = graph_time(lambda: ar_path(fused))
+            t_b = graph_time(lambda: ar_path(base))
+            t_s = graph_time(sp_path)
+            t_hbm = N * K * 2 / (peaks["hbm_gbs"] * 1e9)
+            t_flop = 2 * T * N * K / (peaks["bf16_tflops"] * 1e12)
+            t_nvl = 2 * (world - 1) / world * T * N * 2 / (NVLINK_GBPS * 1e9)
+            roof = max(t_hbm, t_flop, t_nvl)
+            rec = {"sublayer": name + "+norm", "tp": world, "T": T, "N": N, "K_local": K,
+                   "sp_us": round(t_s * 1e3, 2), "fused_ar_us": round(t_f * 1e3, 2),
+                   "gemm_nccl_us": round(t_b * 1e3, 2), "sp_vs_fused": round(t_f / t_s, 3),
+                   "sp_vs_nccl": round(t_b / t_s, 3), "sp_roofline_us": round(roof * 1e6, 2),
+                   "sp_bound": ["hbm", "tensor", "nvlink"][[t_hbm, t_flop, t_nvl].index(roof)],
+                   "sp_frac_of_roofline": round(roof * 1e3 / t_s, 3)}
+            if rank == 0:
+                print(json.dumps(rec), flush=True)
+    ops.check_status()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", default="1,16,64,256,2048")
+    ap.add_argument("--sp", action="store_true", help="also time the sequence-parallel sub-layer")
+    ap.add_argument("--sp-only", action="store_true")
     args = ap.parse_args()
     rank, world, local = init_distributed("nccl")
     dev = torch.device("cuda", local)
@@ -84,7 +134,10 @@ def main():
     fused = TensorParallel(mode="fused", device=dev)
     fused.fused_max_bytes = 0  # time the fused kernel at every size
     base = TensorParallel(mode="nccl", device=dev)
-    for name, (N, Kfull) in {"o_proj": (4096, 4096), "down_proj": (4096, 14336)}.items():
+    shapes = {"o_proj": (4096, 4096), "down_proj": (4096, 14336)}
+    if args.sp or args.sp_only:
+        sp_sublayer(args, shapes, world, rank, dev, peaks, fused, base)
+    for name, (N, Kfull) in ({} if args.sp_only else shapes).items():
         K = Kfull // world
         w = (torch.randn(N, K, device=dev) / math.sqrt(Kfull)).to(torch.bfloat16)
         for T in (int(t) for t in args.tokens.split(",")):

@@ -229,6 +229,9 @@ class Llama:
         self.cos_sin = rope_table(cfg, max_pos, self.device)
         self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
         self.max_tokens = max_tokens
+        # sequence-parallel layer plumbing (tensor-parallel mode "sp"), else None
+        self.sp = tp.sequence_parallel(cfg.hidden, max_tokens) if tp is not None else None
+        self._sp_out = None
         self._alloc(max_tokens)
 
     def _alloc(self, T: int) -> None:
@@ -274,7 +277,41 @@ class Llama:
         act = ops.linear(x, lw.gate_up, self.act[:T], swiglu=True)
         return self._row_linear(act, lw.down, self.delta[:T])
 
+    def _forward_sp(self, b: ForwardBatch) -> torch.Tensor:
+        """Sequence-parallel forward (``parallel/sp.py``): o_proj and down_proj
+        reduce-scatter their partial rows to the rank that owns the token,
+        which adds the residual and normalises them, then all-gathers the
+        normed rows into every rank's copy of the next GEMM's input; that
+        GEMM waits per token tile on the rows' ready flags. The residual
+        stream ``h`` is only current on the rows this rank owns."""
+        cfg, sp = self.cfg, self.sp
+        T = b.n_tokens
+        h = self.h[:T]
+        ops.embedding(b.ids[:T], self.w.embed, h)
+        if b.tier is not None:
+            b.tier.begin_forward()
+        layers = self.w.layers
+        x, ready = self.normed[:T], 0
+        ops.add_rmsnorm(h, None, layers[0].ln_in, cfg.rms_eps, x)  # every rank, every row
+        for li, lw in enumerate(layers):
+            ops.linear_qkv_rope(x, lw.qkv, b.pos[:T], b.slot[:T], self.cos_sin, self.q[:T],
+                                self.kv.k[li], self.kv.v[li], self.hq, self.hkv, x_ready=ready)
+            self._attention(li, b)
+            sp.linear_rs(self.attn[:T].view(T, -1), lw.o)
+            x, ready = sp.reduce_norm(h, lw.ln_post, cfg.rms_eps, T)
+            act = ops.linear(x, lw.gate_up, self.act[:T], swiglu=True, x_ready=ready)
+            sp.linear_rs(act, lw.down)
+            nxt = layers[li + 1].ln_in if li + 1 < len(layers) else self.w.ln_final
+            x, ready = sp.reduce_norm(h, nxt, cfg.rms_eps, T)
+        if b.tier is not None:
+            b.tier.end_forward()
+        sp.wait_rows(ready, T)  # sampling reads the gathered final rows with library ops
+        self._sp_out = x
+        return self.sample(b)
+
     def forward(self, b: ForwardBatch) -> torch.Tensor:
+        if self.sp is not None:
+            return self._forward_sp(b)
         cfg = self.cfg
         T = b.n_tokens
         h, normed, delta = self.h[:T], self.normed[:T], self.delta[:T]
@@ -304,7 +341,8 @@ class Llama:
         S = b.n_sample
         if S == 0:
             return b.out_ids[:0]
-        rows = self.normed.index_select(0, b.sample_idx[:S]) if b.sample_idx is not None else self.normed[:S]
+        final = self._sp_out if self.sp is not None else self.normed
+        rows = final.index_select(0, b.sample_idx[:S]) if b.sample_idx is not None else final[:S]
         if self.tp is None:
             logits = ops.linear(rows, self.w.lm_head)
             return ops.argmax(logits[:, :self.cfg.vocab], b.out_ids[:S])

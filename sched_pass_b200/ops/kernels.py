@@ -100,26 +100,33 @@ def _ws_for(x, N, K, grid, ws):
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *,
-           swiglu: bool = False, grid: int = 0, ws: Workspace | None = None) -> torch.Tensor:
+           swiglu: bool = False, grid: int = 0, ws: Workspace | None = None,
+           x_ready: int = 0) -> torch.Tensor:
     """y = x @ w.T on the tcgen05 GEMM. ``swiglu``: w holds interleaved
     gate/up rows (64 gate rows, then their 64 up rows, per 128-row tile) and
-    y = silu(gate) * up with N/2 columns. ``grid``: CTAs (0 = one per SM)."""
+    y = silu(gate) * up with N/2 columns. ``grid``: CTAs (0 = one per SM).
+    ``x_ready``: device address of per-row ready flags of a gathered x (the
+    sequence-parallel all-gather); each token tile is loaded once its rows
+    are raised. 0: x is ready."""
     T, K = x.shape
     N = w.shape[0]
     if out is None:
         out = torch.empty(T, N // 2 if swiglu else N, dtype=torch.bfloat16, device=x.device)
     ws = _ws_for(x, N, K, grid, ws)
-    ext().gemm(x, w, out, 1 if swiglu else 0, int(grid), ws.ws, ws.counters, status_buffer(x.device))
+    ext().gemm(x, w, out, 1 if swiglu else 0, int(grid), ws.ws, ws.counters, status_buffer(x.device),
+               int(x_ready))
     return out
 
 
 def linear_qkv_rope(x, w, pos, slot, cos_sin, q_out, k_cache, v_cache, n_q_heads, n_kv_heads, *,
-                    grid: int = 0, ws: Workspace | None = None):
+                    grid: int = 0, ws: Workspace | None = None, x_ready: int = 0):
     """Fused QKV projection + RoPE + KV append: q heads rotated into q_out,
-    k heads rotated and v heads copied into their paged-cache slots."""
+    k heads rotated and v heads copied into their paged-cache slots.
+    ``x_ready`` as in ``linear``."""
     ws = _ws_for(x, w.shape[0], x.shape[1], grid, ws)
     ext().gemm_qkv_rope(x, w, pos, slot, cos_sin, q_out, k_cache, v_cache, int(n_q_heads),
-                        int(n_kv_heads), int(grid), ws.ws, ws.counters, status_buffer(x.device))
+                        int(n_kv_heads), int(grid), ws.ws, ws.counters, status_buffer(x.device),
+                        int(x_ready))
     return q_out
 
 

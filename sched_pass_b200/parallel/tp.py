@@ -11,7 +11,12 @@ are added across ranks. Two implementations share the interface:
   peers' tiles locally after a per-chunk flag handshake (``kEpiAllReduce``
   in ``csrc/kernels/gemm.cu``; ``parallel/fused.py``);
 * ``nccl``: the GEMM kernel followed by ``all_reduce`` on NCCL -- the
-  baseline the fused path is measured against.
+  baseline the fused path is measured against;
+* ``sp`` (sequence parallel): the model runs its row-parallel projections as
+  GEMM -> reduce-scatter, the residual add + RMSNorm on the rows each rank
+  owns, and an all-gather fused into that norm that the next GEMM consumes
+  tile by tile (``parallel/sp.py``); ``linear_allreduce`` itself then falls
+  back to GEMM + NCCL for callers outside the decoder layer.
 
 The fused kernel is a one-shot all-reduce: each rank pushes its whole
 partial to every peer, (W - 1) x T x N x 2 bytes, where a ring or NVLS
@@ -46,9 +51,24 @@ class TensorParallel:
         self.fused_calls = 0
         self.nccl_calls = 0
         self._fused = None
+        self._sp = None
+        if self.mode not in ("fused", "nccl", "sp"):
+            raise ValueError(f"unknown tensor-parallel mode {self.mode!r}")
         if self.mode == "fused" and self.world > 1:
             from .fused import FusedAllReduce
             self._fused = FusedAllReduce(self.group, self.device)
+
+    def sequence_parallel(self, hidden: int, max_tokens: int):
+        """The sequence-parallel buffers of this group (``mode == "sp"``),
+        created on first use for the model's hidden size; None otherwise."""
+        if self.mode != "sp" or self.world == 1:
+            return None
+        if self._sp is None:
+            from .sp import SequenceParallel
+            self._sp = SequenceParallel(self.group, self.device, hidden, max_tokens)
+        elif self._sp.hidden != hidden or self._sp.max_tokens < max_tokens:
+            raise ValueError("one sequence-parallel buffer set per group: hidden size / tokens differ")
+        return self._sp
 
     def use_fused(self, T: int, N: int) -> bool:
         """Whether a [T, N] row-parallel output goes through the one-shot

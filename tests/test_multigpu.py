@@ -52,3 +52,20 @@ def test_expert_parallel_layer():
         assert res["dropped"] == 0, res
         for c in res["checks"]:
             assert c["rel_err"] < 3e-2, c
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+def test_sequence_parallel_matches_fused_allreduce():
+    """GEMM -> reduce-scatter, owner's reduce + residual + RMSNorm +
+    all-gather, and the ready-gated GEMM reproduce the fused all-reduce path
+    bit for bit (same partials, same rank-order sum, same norm arithmetic),
+    and the TP engine generates the same tokens in both modes."""
+    n = 2 if _ngpus() < 4 else min(_ngpus(), 8)
+    r = run_torchrun("sp_worker.py", n)
+    line = [l for l in r.stdout.splitlines() if l.startswith("SPJSON ")]
+    assert r.returncode == 0 and line, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.loads(line[0][len("SPJSON "):])
+    for c in res["checks"]:
+        assert c["delta_bits"] and c["residual_bits"] and c["normed_bits"], c
+        assert c["gated_gemm_bits"] and c["identical_on_ranks"], c
+    assert res["engine_identical"], res

@@ -40,6 +40,7 @@ class GemmArgs(ctypes.Structure):
         ("rank", ctypes.c_int), ("world", ctypes.c_int),
         ("recv", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8),
         ("trace", ctypes.c_void_p), ("kv_pages", ctypes.c_int),
+        ("x_ready", ctypes.c_void_p),
     ]
 
 
