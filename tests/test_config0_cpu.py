@@ -136,3 +136,23 @@ def test_tau_is_exact_truncated_softmax(kernels):
     full = reference(lens, bt, kc, vc, q)
     cut = [b for b in range(B) if 0 < taus[b] < lens[b]]
     assert cut and all(np.abs(full[b] - ref[b]).max() > 1e-3 for b in cut)
+
+
+def test_shed_quality_sweep_is_monotone(kernels):
+    """Quality of the shed lever as its budget grows (the reference's tau
+    sweep, test/py/eval_quality.py:31-76): tau = f * len for growing f,
+    executed by the woven kernel; the cosine similarity of the output to
+    full attention rises with f and reaches 1 at f = 1 (tau = len keeps
+    every token: the kernel's output equals the untruncated one)."""
+    _, woven = kernels
+    lens, bt, kc, vc, q, _, maxp = build(3)
+    full = reference(lens, bt, kc, vc, q).reshape(-1)
+    cos = []
+    for f in (0.1, 0.25, 0.5, 0.75, 0.9, 1.0):
+        t = Tables()
+        for b in range(B):
+            t.set_row(b, tau=max(1, int(f * lens[b])))
+        out = run(woven, lens, bt, kc, vc, q, maxp, t).reshape(-1).astype(np.float64)
+        cos.append(float(out @ full / np.linalg.norm(out) / np.linalg.norm(full)))
+    assert all(b > a for a, b in zip(cos, cos[1:])), cos
+    assert cos[-1] > 1 - 1e-6 and cos[0] < 0.9, cos
