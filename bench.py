@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--output", type=int, default=128)
     ap.add_argument("--requests", type=int, default=2000)
     ap.add_argument("--max-batch", type=int, default=128)
+    ap.add_argument("--step-tokens", type=int, default=0,
+                    help="cap on decode + prefill tokens per engine step (0: prefill chunks up to 2048)")
     ap.add_argument("--acquire", default="auto", choices=["static", "ticket", "clc", "auto"])
     ap.add_argument("--tp-mode", default=None, choices=[None, "fused", "nccl", "sp"])
     ap.add_argument("--seed", type=int, default=0)
@@ -94,7 +96,7 @@ def main():
     tp = TensorParallel(mode=args.tp_mode, device=dev) if world > 1 else None
     cfg = get_config(args.model)
     max_ctx = args.prompt + args.output + 16
-    ecfg = EngineConfig(max_batch=args.max_batch, max_prefill_tokens=2048,
+    ecfg = EngineConfig(max_batch=args.max_batch, max_prefill_tokens=2048, max_step_tokens=args.step_tokens,
                         max_context=(max_ctx + 127) // 128 * 128, cuda_graphs=not args.no_graphs,
                         levers=True, acquire=args.acquire, seed=args.seed)
     eng = Engine(cfg, ecfg, dev, tp=tp)
@@ -195,6 +197,7 @@ def main():
             "requests": args.requests, "parallelism": f"tp{world}",
             "tp_collective": (tp.mode if tp is not None else "none"),
             "levers": "pi+timer(1/8)+policy armed; acquire=" + args.acquire,
+            "step_tokens": args.step_tokens or None,
             "l2": "inputs larger than L2 (weights stream every step)",
             "workload_clock_s": round(eng.clock - clock0, 3),
         },

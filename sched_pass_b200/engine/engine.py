@@ -47,6 +47,7 @@ Q_TILE = 64
 class EngineConfig:
     max_batch: int = 256
     max_prefill_tokens: int = 4096
+    max_step_tokens: int = 0        # cap on decode + prefill tokens per step (0 = none; see Scheduler)
     max_context: int = 4096
     num_pages: int = 0              # 0: sized from max_batch * max_context
     cuda_graphs: bool = True
@@ -106,7 +107,8 @@ class Engine:
         else:
             self.model = Llama(cfg, weights, self.kv, self.device, tp=tp, max_tokens=T,
                                max_pos=e.max_context + 16)
-        self.sched = Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context, tier=self.tier)
+        self.sched = Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context, tier=self.tier,
+                               max_step_tokens=e.max_step_tokens)
         self.hkv = cfg.n_kv_heads // tp_size
         self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.target_tasks = e.target_tasks or self.sms

@@ -2,7 +2,12 @@
 
 Every step serves all running decode requests (one token each) and fills
 the remaining token budget with prefill chunks of waiting / partially
-prefilled requests, oldest first. Pages come from the native allocator; when
+prefilled requests, oldest first. The prefill budget of a step is
+``max_prefill_tokens``, further capped (when ``max_step_tokens`` > 0) so that
+decode + prefill tokens stay within ``max_step_tokens``: a step whose token
+count keeps every GEMM weight-bandwidth-bound costs about what a decode-only
+step costs, so prefill chunks of that size ride along with the decode batch
+instead of stalling it for a whole-prompt step (stall-free batching). Pages come from the native allocator; when
 a decode request needs a page and none is free, the most recently admitted
 request is preempted (its pages are freed and it restarts from its prompt,
 keeping the tokens it already generated as part of its new prompt).
@@ -35,12 +40,14 @@ class StepPlan:
 
 class Scheduler:
     def __init__(self, num_pages: int, page_size: int = 16, max_batch: int = 256,
-                 max_prefill_tokens: int = 4096, max_context: int = 8192, tier=None):
+                 max_prefill_tokens: int = 4096, max_context: int = 8192, tier=None,
+                 max_step_tokens: int = 0):
         self.alloc = PageAllocator(num_pages)
         self.tier = tier  # optional TieredKV: spill to host before preempting
         self.page_size = page_size
         self.max_batch = max_batch
         self.max_prefill_tokens = max_prefill_tokens
+        self.max_step_tokens = max_step_tokens  # 0: no cap on decode + prefill tokens
         self.max_context = max_context
         self.waiting: deque[Request] = deque()
         self.running: list[Request] = []   # admitted (PREFILL or DECODE), admission order
@@ -134,7 +141,7 @@ class Scheduler:
             if req.state == State.DECODE:
                 plan.decode.append(req)
         # 2. prefill: continue partial prefills, then admit new requests
-        budget = self.max_prefill_tokens
+        budget = self.prefill_budget(len(plan.decode))
         for req in self.running:
             if budget <= 0:
                 break
@@ -158,6 +165,13 @@ class Scheduler:
             plan.prefill.append((req, 0, n))
             budget -= n
         return plan
+
+    def prefill_budget(self, n_decode: int) -> int:
+        """Prefill tokens a step with ``n_decode`` decode tokens may add: at
+        least one page's worth, so prefill always progresses."""
+        if self.max_step_tokens <= 0:
+            return self.max_prefill_tokens
+        return min(self.max_prefill_tokens, max(self.max_step_tokens - n_decode, self.page_size))
 
     def commit(self, plan: StepPlan, sampled: dict, now: float) -> list:
         """Apply one step's results. ``sampled`` maps rid -> next token for
