@@ -51,7 +51,7 @@ def test_prefill_progresses_when_decode_fills_the_cap():
     s = Scheduler(num_pages=20000, page_size=16, max_batch=64, max_prefill_tokens=2048, max_context=4096,
                   max_step_tokens=24)
     # 30 requests decode at once (> the cap of 24): each step still admits a page of prefill
-    reqs = make(30, prompt=40, out=50)
+    reqs = make(30, prompt=40, out=200)
     shapes, done = drive(s, reqs, arrivals_per_step=30)
     assert len(done) == 30
     assert all(d + p <= max(24, d + 16) for d, p in shapes)
