@@ -172,3 +172,68 @@ def test_manifest_mirror_matches_cpp():
         assert r["effect"] == effect and int(r["minSm"]) == min_sm and r["knob"] == knob
         assert int(r["disableKnob"]) == int(disables) and r["tag"] == tag
     assert [int(r["order"]) for r in rows] == list(range(len(rows)))
+
+
+def test_weave_arith_stream_prefetches_ahead():
+    """Arithmetic stream (the reference's arith_decode fixture): the KV
+    address is affine in the canonical IV, so the urgent tier prefetches a
+    fixed distance ahead (8 iterations x 64 floats = 2048 bytes for the KV
+    stream, 8 x 4 bytes for the weights), under the urgency predicate."""
+    out, notes = weave(fixture("arith_decode.ll"))
+    verify(out)
+    check_order(out, [
+        r"define ptx_kernel void @arith_decode\(",
+        r"%sched\.task = select i1 %sched\.task\.ok",
+        r"%sched\.pf\.ahead = add i64 %sched\.pf\.int, 2048",
+        r"prefetch\.global\.L2::evict_last \[\$0\]; \}\", \"l,r,~\{memory\}\"\(i64 %sched\.pf\.ahead, i32 %sched\.urgent\.i32\)",
+        r"%v = load float",
+    ])
+    assert "%sched.pf.ahead.1 = add i64 %sched.pf.int.1, 32" in out
+    assert not any("polite tier only" in n for n in notes)
+
+
+def test_arith_fixture_runs_bit_exact_on_the_host():
+    """The woven arith fixture executed on the CPU (hint-only asm dropped):
+    urgent policy + reversed pi leave the result bit-exact; tau truncates the
+    contraction exactly."""
+    import ctypes
+    import struct
+
+    import numpy as np
+
+    from sched_pass_b200.compiler.cpu_exec import HostKernel
+    from sched_pass_b200.runtime import abi
+
+    src = fixture("arith_decode.ll")
+    woven, _ = weave(src)
+    stock, wk = HostKernel(src), HostKernel(woven)
+    R, NT, D = 6, 40, 64
+    rng = np.random.default_rng(4)
+    kv = rng.standard_normal((R * NT, D)).astype(np.float32)
+    w = rng.standard_normal(NT).astype(np.float32)
+    p = ctypes.c_void_p
+
+    def run(k, tables=None):
+        out = np.zeros((R, D), np.float32)
+        if tables is not None:
+            order, ctrl = tables
+            k.set_global_ptr("__sched_task_order", order.ctypes.data)
+            k.set_global_ptr("__sched_ctrl", ctrl.ctypes.data)
+        k.run("arith_decode", (R,), (D,), [kv.ctypes.data, w.ctypes.data, out.ctypes.data, NT],
+              [p, p, p, ctypes.c_int32])
+        return out
+
+    base = run(stock)
+    assert np.allclose(base, (kv.reshape(R, NT, D) * w[None, :, None]).sum(1), atol=1e-4)
+    order = np.arange(R - 1, -1, -1, dtype=np.int32)
+    ctrl = np.zeros(abi.ctrl_bytes(64), np.uint8)
+    struct.pack_into("<I", ctrl, abi.CTRL_ORDER_SIZE_OFF, R)
+    for r in range(R):
+        struct.pack_into("<fHB", ctrl, abi.CTRL_ROWS_OFF + abi.ROW_SIZE * r, 1.0, 0, 1)  # urgent
+    assert np.array_equal(run(wk, (order, ctrl)), base)
+    tau = 13
+    for r in range(R):
+        struct.pack_into("<fHB", ctrl, abi.CTRL_ROWS_OFF + abi.ROW_SIZE * r, 0.0, tau, 0)
+    cut = run(wk, (order, ctrl))
+    want = (kv.reshape(R, NT, D)[:, :tau] * w[None, :tau, None]).sum(1)
+    assert np.allclose(cut, want, atol=1e-4) and not np.allclose(cut, base, atol=1e-3)
