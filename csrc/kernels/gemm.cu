@@ -321,8 +321,11 @@ __device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t *p) {
 // together); once all are set, a system-scope fence turns the observation
 // into an acquire of the owners' releases, and a proxy fence orders it
 // before this thread's TMA (async-proxy) reads of the rows. On timeout the
-// status word is set and the loads go ahead (no hang).
+// status word is set and the loads go ahead (no hang). The budget is half of
+// the MMA warp's wait on the stage, so a missing row ends as a peer timeout
+// and the stage still lands before the MMA warp gives up on it.
 __device__ __noinline__ void wait_rows_ready(const uint32_t *ready, int r0, int r1, int *status) {
+  constexpr uint64_t kReadyBudgetNs = kWaitBudgetNs / 2;
   const uint64_t start = ptx::globaltimer_ns();
   for (;;) {
     bool all = true;
@@ -340,7 +343,7 @@ __device__ __noinline__ void wait_rows_ready(const uint32_t *ready, int r0, int 
       }
     }
     if (all) break;
-    if (ptx::globaltimer_ns() - start > kWaitBudgetNs) {
+    if (ptx::globaltimer_ns() - start > kReadyBudgetNs) {
       report_status(status, kStatusPeerTimeout);
       return;
     }
