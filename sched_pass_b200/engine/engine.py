@@ -41,6 +41,7 @@ from .scheduler import Scheduler, StepPlan
 
 DECODE_BUCKETS = (1, 2, 4, 8, 12, 16, 24, 32, 40, 48, 56, 64, 80, 96, 112, 128, 160, 192, 224, 256)
 Q_TILE = 64
+MIXED_SEGMENTS = 4  # prefill requests per step of a fixed-shape (graph) mixed step
 
 
 @dataclass
@@ -48,6 +49,8 @@ class EngineConfig:
     max_batch: int = 256
     max_prefill_tokens: int = 4096
     max_step_tokens: int = 0        # cap on decode + prefill tokens per step (0 = none; see Scheduler)
+    mixed_graphs: bool = True       # with max_step_tokens: pad mixed steps to a fixed shape per decode
+                                    # bucket and replay them from CUDA graphs
     max_context: int = 4096
     num_pages: int = 0              # 0: sized from max_batch * max_context
     cuda_graphs: bool = True
@@ -107,8 +110,11 @@ class Engine:
         else:
             self.model = Llama(cfg, weights, self.kv, self.device, tp=tp, max_tokens=T,
                                max_pos=e.max_context + 16)
+        capped = e.max_step_tokens > 0
         self.sched = Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context, tier=self.tier,
-                               max_step_tokens=e.max_step_tokens)
+                               max_step_tokens=e.max_step_tokens,
+                               round_decode=(lambda nd: self._bucket(nd) or nd) if capped else None,
+                               max_prefill_segments=MIXED_SEGMENTS if capped else 0)
         self.hkv = cfg.n_kv_heads // tp_size
         self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.target_tasks = e.target_tasks or self.sms
@@ -215,8 +221,29 @@ class Engine:
         return not self.sched.idle
 
     # ------------------------------------------------------------------ planning
-    def _fill(self, plan: StepPlan, bucket: int | None):
-        """Write the step's inputs into the pinned staging buffer."""
+    def _mixed_pad(self, b: int) -> int:
+        """Prefill rows of a fixed-shape mixed step with decode bucket ``b``:
+        the scheduler's largest prefill budget for that bucket."""
+        e = self.ecfg
+        return min(e.max_prefill_tokens, max(e.max_step_tokens - b, 16))
+
+    def _mixed_bucket(self, plan: StepPlan):
+        """Decode bucket of a mixed step that fits the fixed shape, else None."""
+        e = self.ecfg
+        if e.max_step_tokens <= 0 or not e.mixed_graphs or self.tier is not None:
+            return None
+        nd = len(plan.decode)
+        b = self._bucket(nd) if nd else 0
+        if b is None or len(plan.prefill) > MIXED_SEGMENTS:
+            return None
+        if sum(n for _, _, n in plan.prefill) > self._mixed_pad(b):
+            return None
+        return b
+
+    def _fill(self, plan: StepPlan, bucket: int | None, pad: int | None = None):
+        """Write the step's inputs into the pinned staging buffer. ``pad``:
+        a fixed-shape mixed step (prefill rows padded to ``pad`` tokens,
+        prefill tiles and sampled rows to their bounds)."""
         e = self.ecfg
         dec = plan.decode
         nd = len(dec)
@@ -260,6 +287,14 @@ class Engine:
             for t0 in range(0, n, Q_TILE):
                 tiles.append((br, row - ndp + t0, min(Q_TILE, n - t0), start + t0))
             row += n
+        if pad is not None:
+            # padding rows: no cache write, in no attention tile, never sampled
+            ids[row:ndp + pad] = 0
+            pos[row:ndp + pad] = 0
+            slot[row:ndp + pad] = -1
+            T = ndp + pad
+            n_tiles_max = -(-pad // Q_TILE) + MIXED_SEGMENTS - 1
+            tiles += [(ndp, 0, 0, 0)] * (n_tiles_max - len(tiles))  # empty tiles (nq = 0)
         # decode plan
         S = self.splits_for(ndp) if ndp else 1
         n_items = 0
@@ -285,8 +320,11 @@ class Engine:
                 sample_map.append((r.rid, ns))
                 ns += 1
             row += n
+        if pad is not None:
+            sidx[ns:ndp + MIXED_SEGMENTS] = 0  # dummy rows, results ignored
+            ns = ndp + MIXED_SEGMENTS
         return dict(T=T, nd=ndp, n_items=n_items, S=S, n_tiles=len(tiles), n_sample=ns,
-                    sample_map=sample_map, n_real_decode=nd)
+                    sample_map=sample_map, n_real_decode=nd, pad=pad)
 
     def _batch(self, info, slots) -> ForwardBatch:
         mp = self.max_pages_per_req
@@ -330,7 +368,7 @@ class Engine:
                 return b
         return None
 
-    def _graph_for(self, bucket: int, info, slots):
+    def _graph_for(self, bucket, info, slots):
         g = self.graphs.get(bucket)
         if g is not None:
             return g
@@ -357,7 +395,13 @@ class Engine:
         nd = len(plan.decode)
         decode_only = not plan.prefill
         bucket = self._bucket(nd) if (decode_only and self.ecfg.cuda_graphs) else None
-        info = self._fill(plan, bucket)
+        mixed = None if decode_only else self._mixed_bucket(plan)
+        if mixed is not None:
+            info = self._fill(plan, mixed, pad=self._mixed_pad(mixed))
+            key = ("mixed", mixed) if self.ecfg.cuda_graphs else None
+        else:
+            info = self._fill(plan, bucket)
+            key = bucket
         slots = self.plane.slots() if self.ecfg.levers else None
         self.hooks.begin(self, plan, info)
         # one H2D copy of every step input
@@ -368,8 +412,8 @@ class Engine:
         ev1 = torch.cuda.Event(enable_timing=True)
         ev0.record()
         used_graph = False
-        if bucket is not None:
-            graph, S, n_items = self._graph_for(bucket, info, slots)
+        if key is not None:
+            graph, S, n_items = self._graph_for(key, info, slots)
             assert S == info["S"] and n_items == info["n_items"]
             graph.replay()
             used_graph = True

@@ -41,13 +41,16 @@ class StepPlan:
 class Scheduler:
     def __init__(self, num_pages: int, page_size: int = 16, max_batch: int = 256,
                  max_prefill_tokens: int = 4096, max_context: int = 8192, tier=None,
-                 max_step_tokens: int = 0):
+                 max_step_tokens: int = 0, round_decode=None, max_prefill_segments: int = 0):
         self.alloc = PageAllocator(num_pages)
         self.tier = tier  # optional TieredKV: spill to host before preempting
         self.page_size = page_size
         self.max_batch = max_batch
         self.max_prefill_tokens = max_prefill_tokens
         self.max_step_tokens = max_step_tokens  # 0: no cap on decode + prefill tokens
+        # the engine pads decode rows to a graph bucket: the cap counts padded rows
+        self.round_decode = round_decode
+        self.max_prefill_segments = max_prefill_segments  # requests prefilled per step (0: any)
         self.max_context = max_context
         self.waiting: deque[Request] = deque()
         self.running: list[Request] = []   # admitted (PREFILL or DECODE), admission order
@@ -142,15 +145,16 @@ class Scheduler:
                 plan.decode.append(req)
         # 2. prefill: continue partial prefills, then admit new requests
         budget = self.prefill_budget(len(plan.decode))
+        seg_cap = self.max_prefill_segments or (1 << 30)
         for req in self.running:
-            if budget <= 0:
+            if budget <= 0 or len(plan.prefill) >= seg_cap:
                 break
             if req.state == State.PREFILL:
                 n = min(budget, req.prompt_len - req.cached)
                 if n > 0 and self._grow(req, req.cached + n):
                     plan.prefill.append((req, req.cached, n))
                     budget -= n
-        while budget > 0 and self.waiting and len(self.running) < self.max_batch:
+        while budget > 0 and self.waiting and len(self.running) < self.max_batch and len(plan.prefill) < seg_cap:
             req = self.waiting[0]
             n = min(budget, req.prompt_len)
             # keep room for the decode pages of everything already running
@@ -171,6 +175,8 @@ class Scheduler:
         least one page's worth, so prefill always progresses."""
         if self.max_step_tokens <= 0:
             return self.max_prefill_tokens
+        if self.round_decode is not None and n_decode > 0:
+            n_decode = self.round_decode(n_decode)
         return min(self.max_prefill_tokens, max(self.max_step_tokens - n_decode, self.page_size))
 
     def commit(self, plan: StepPlan, sampled: dict, now: float) -> list:

@@ -64,3 +64,27 @@ def test_chunked_prefill_and_preemption():
     outs = eng.generate(ps, max_new_tokens=3)
     assert all(len(o) == 3 for o in outs)
     assert eng.sched.alloc.free == eng.sched.alloc.num_pages
+
+
+def test_capped_mixed_steps_replay_graphs_with_the_eager_tokens():
+    """With a per-step token cap, mixed decode + prefill steps are padded to a
+    fixed shape per decode bucket and replayed from CUDA graphs; the padded
+    eager run of the same steps produces the same tokens, every step stays
+    within the cap (counting padded decode rows), and graphs serve the mixed
+    steps."""
+    ps = prompts(10, lo=40, hi=400, seed=7)
+    runs = {}
+    for graphs in (False, True):
+        eng, _ = make_engine(cuda_graphs=graphs, max_step_tokens=96)
+        runs[graphs] = eng.generate(ps, max_new_tokens=8)
+        ops.check_status()
+        mixed = [s for s in eng.stats if s.n_prefill_tokens > 0 and s.n_decode > 0]
+        assert mixed, "no mixed steps"
+        assert all(s.n_prefill_tokens <= 96 for s in eng.stats)
+        if graphs:
+            assert sum(s.graph for s in mixed) >= len(mixed) // 2, [(s.n_decode, s.graph) for s in mixed]
+        assert eng.sched.alloc.free == eng.sched.alloc.num_pages
+        eng.graphs.clear()
+        del eng
+        torch.cuda.empty_cache()
+    assert runs[True] == runs[False]
