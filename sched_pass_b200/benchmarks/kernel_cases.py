@@ -1,0 +1,138 @@
+"""Small standalone cases of single kernels, for device timing and for
+``ncu`` captures of one launch (inputs above L2 where the kernel streams,
+a few hundred MB on the device at most).
+
+  --case sp_norm   sequence-parallel reduce + residual + RMSNorm + all-gather
+                   (``sp_reduce_norm_kernel``) for W ranks emulated on one
+                   GPU: every rank's reduce-scatter GEMM runs first, then the
+                   owners' norms, so no launch waits on a later one
+  --case prefill   causal paged prefill attention of one 1536-token prompt
+                   (Llama-3-8B heads: 32 query / 8 KV, head_dim 128)
+  --case sample    embedding gather (T tokens) and greedy argmax over the
+                   128256-entry vocabulary
+
+Prints one JSON line per case with the median device time (CUDA events,
+after warm-up) and the algorithmic bytes / FLOPs per launch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from .. import ops
+from .._ext import ext
+from .common import measured_peaks
+
+
+def events_ms(fn, reps):
+    fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e))
+    return sorted(ts)[len(ts) // 2]
+
+
+def case_sp_norm(args, peaks):
+    W, T, H, K = args.world, args.tokens, 4096, 2048
+    M = (T + 3) // 4 * 4
+    dev = "cuda"
+    z = lambda *s, dt=torch.bfloat16: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
+    slab = [z(W, M, H) for _ in range(W)]
+    rflags = [z(W * (H // 128) * M, dt=torch.int32) for _ in range(W)]
+    gather = [[z(M, H) for _ in range(W)] for _ in range(2)]
+    ready = [[z(M, dt=torch.int32) for _ in range(W)] for _ in range(2)]
+    xs = [torch.randn(T, K, device=dev).to(torch.bfloat16) for _ in range(W)]
+    ws = [(torch.randn(H, K, device=dev) / math.sqrt(K * W)).to(torch.bfloat16) for _ in range(W)]
+    res = [torch.randn(T, H, device=dev).to(torch.bfloat16) for _ in range(W)]
+    lnw = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    st = ops.status_buffer()
+    ptrs = lambda lst: [t.data_ptr() for t in lst]  # noqa: E731
+    k = [0]
+
+    def push():
+        for r in range(W):
+            w_ = ops.kernels._ws_for(xs[r], H, K, 0, None)
+            ext().gemm_reduce_scatter(xs[r], ws[r], r, W, ptrs(slab), ptrs(rflags), 0, w_.ws, w_.counters, st)
+
+    def norms():
+        g = k[0]
+        for r in range(W):
+            ext().sp_reduce_norm(slab[r].data_ptr(), rflags[r].data_ptr(), res[r], lnw, None, ptrs(gather[g]),
+                                 ptrs(ready[g]), ready[g ^ 1][r].data_ptr(), M, T, r, W, 1e-5, st)
+        k[0] ^= 1
+
+    ts = []
+    for _ in range(args.reps):
+        push()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        norms()
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e) / W)
+    ops.check_status()
+    ms = sorted(ts)[len(ts) // 2]
+    rows = T / W
+    byts = rows * H * 2 * (W + 2 + W)  # partials in, residual in/out, W gathered copies out
+    print(json.dumps({"case": "sp_norm", "world": W, "T": T, "H": H, "us_per_rank": round(ms * 1e3, 2),
+                      "bytes_per_rank": int(byts), "GBps": round(byts / (ms * 1e-3) / 1e9, 1),
+                      "frac_hbm_of_measured": round(byts / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)}))
+
+
+def case_prefill(args, peaks):
+    T, Hq, Hkv, D, PS = 1536, 32, 8, 128, 16
+    pages = T // PS
+    dev = "cuda"
+    q = torch.randn(T, Hq, D, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    kc = torch.randn(pages, Hkv, PS, D, device=dev).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    bt = torch.randperm(pages, device=dev).to(torch.int32).view(1, pages)
+    kvl = torch.tensor([T], dtype=torch.int32, device=dev)
+    tiles = torch.tensor([[0, t0, 64, t0] for t0 in range(0, T, 64)], dtype=torch.int32, device=dev)
+    fn = lambda: ops.attention_prefill(q, out, kc, vc, bt, kvl, tiles, tiles.shape[0], 1 / math.sqrt(D))  # noqa: E731
+    ms = events_ms(fn, args.reps)
+    flops = 4 * (T * (T + 1) / 2) * Hq * D  # causal QK^T and PV
+    print(json.dumps({"case": "prefill", "T": T, "us": round(ms * 1e3, 2), "TFLOPs": round(flops / (ms * 1e-3) / 1e12, 1),
+                      "frac_bf16_of_measured": round(flops / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 3)}))
+
+
+def case_sample(args, peaks):
+    V, H = 128256, 4096
+    dev = "cuda"
+    table = torch.randn(V, H, device=dev).to(torch.bfloat16)
+    ids = torch.randint(0, V, (args.tokens,), device=dev, dtype=torch.int32)
+    out = torch.empty(args.tokens, H, dtype=torch.bfloat16, device=dev)
+    ms_e = events_ms(lambda: ops.embedding(ids, table, out), args.reps)
+    logits = torch.randn(128, V, device=dev).to(torch.bfloat16)
+    ms_a = events_ms(lambda: ops.argmax(logits), args.reps)
+    ops.check_status()
+    print(json.dumps({"case": "sample", "embedding_T": args.tokens, "embedding_us": round(ms_e * 1e3, 2),
+                      "embedding_GBps": round(2 * args.tokens * H * 2 / (ms_e * 1e-3) / 1e9, 1),
+                      "argmax_rows": 128, "argmax_us": round(ms_a * 1e3, 2),
+                      "argmax_GBps": round(128 * V * 2 / (ms_a * 1e-3) / 1e9, 1)}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="sp_norm", choices=["sp_norm", "prefill", "sample"])
+    ap.add_argument("--world", type=int, default=2)
+    ap.add_argument("--tokens", type=int, default=256)
+    ap.add_argument("--reps", type=int, default=5)
+    args = ap.parse_args()
+    peaks = measured_peaks()
+    {"sp_norm": case_sp_norm, "prefill": case_prefill, "sample": case_sample}[args.case](args, peaks)
+
+
+if __name__ == "__main__":
+    main()
