@@ -12,6 +12,8 @@ steps while there is work, and completes finished requests. Endpoints:
   "ttft", "tpot"}}``. Decoding is greedy and runs ``max_new_tokens`` tokens.
 * ``GET /health`` -- liveness plus queue depths.
 * ``GET /stats`` -- steps, decode tokens, the scheduling plugin's counters.
+* ``GET /metrics`` -- the same and step-time / TPOT / TTFT / latency
+  histograms in the Prometheus text format (``engine/metrics.py``).
 
     python -m sched_pass_b200.engine.server --model llama-3-8b --port 30000
 """
@@ -39,6 +41,11 @@ class EngineServer:
         self.steps = 0
         self.decode_tokens = 0
         self.error: BaseException | None = None
+        try:
+            from .metrics import ServerMetrics
+            self.metrics = ServerMetrics(self)
+        except ImportError:  # prometheus_client absent: /metrics answers 404
+            self.metrics = None
 
     # ---------------------------------------------------------------- client side
     def submit(self, input_ids, max_new_tokens: int, urgency: float = 0.0) -> cf.Future:
@@ -81,6 +88,8 @@ class EngineServer:
                 continue
             _, fut = item
             tpot = r.tpot()
+            if self.metrics is not None:
+                self.metrics.on_done(tpot, r.ttft(), now - r._t_submit)
             fut.set_result({
                 "output_ids": [int(t) for t in r.output],
                 "meta_info": {"prompt_tokens": r.prompt_len, "completion_tokens": len(r.output),
@@ -100,6 +109,8 @@ class EngineServer:
                     plan, done = self.engine.step()
                     self.steps += 1
                     self.decode_tokens += len(plan.decode)
+                    if self.metrics is not None:
+                        self.metrics.on_step(self.engine, plan)
                     self._complete(done)
                 else:
                     try:
@@ -131,7 +142,7 @@ class EngineServer:
         import asyncio
 
         from fastapi import FastAPI, HTTPException
-        from fastapi.responses import JSONResponse
+        from fastapi.responses import JSONResponse, Response
 
         app = FastAPI(title="sched_pass_b200")
 
@@ -164,6 +175,12 @@ class EngineServer:
                 out["sched"] = {"planned": s.planned, "probes": s.probes, "clc_armed": s.clc_armed,
                                 "orders": s.orders, "hook_errors": self.engine.hooks.errors}
             return out
+
+        @app.get("/metrics")
+        async def metrics():
+            if self.metrics is None:
+                raise HTTPException(404, "prometheus_client is not installed")
+            return Response(self.metrics.text(), media_type="text/plain; version=0.0.4; charset=utf-8")
 
         return app
 

@@ -102,6 +102,17 @@ def test_server_futures_and_http_replay():
         st = requests.get(f"http://127.0.0.1:{port}/stats", timeout=5).json()
         assert st["steps"] > 0 and st["decode_tokens"] > 0
         assert requests.get(f"http://127.0.0.1:{port}/health", timeout=5).json()["ok"]
+        m = requests.get(f"http://127.0.0.1:{port}/metrics", timeout=5)
+        assert m.status_code == 200
+        vals = {}
+        for line in m.text.splitlines():
+            if line and not line.startswith("#"):
+                k, v = line.rsplit(" ", 1)
+                vals[k] = float(v)
+        assert vals["sched_engine_steps_total"] == st["steps"] > 0
+        assert vals["sched_requests_finished_total"] == 26  # 2 submitted directly + 24 replayed
+        assert vals["sched_request_tpot_ms_count"] == 26 and vals["sched_requests_queued"] == 0
+        assert vals["sched_engine_prefill_tokens_total"] > 0
         r = requests.post(f"http://127.0.0.1:{port}/generate", json={"sampling_params": {}}, timeout=5)
         assert r.status_code == 400
         server.should_exit = True
