@@ -111,3 +111,50 @@ def test_second_arena_in_one_process_is_refused():
         print("OK")
     """)
     assert "OK" in out
+
+
+PHASE = """
+    import json, os, sys
+    import numpy as np, torch
+    sys.path.insert(0, os.path.join(%(root)r, "tests"))
+    from test_config0_cpu import B, build, reference, run
+    from sched_pass_b200.compiler.cpu_exec import HostKernel
+    from sched_pass_b200.compiler.weave import weave_cached, weaver_path
+    from sched_pass_b200.runtime.sched_rt import SchedPlane, compute_bake_env
+    p = SchedPlane(max_tasks=64, device="cpu", mode="arena")
+    assert p.arena.canonical
+    env = compute_bake_env(p.arena.base, 64, weaver_path(), {"SCHED_CACHE_ROOT": %(cache)r})
+    src = open(os.path.join(%(root)r, "tests", "ir", "softmax_decode.ll")).read()
+    src = "\\n".join(l for l in src.splitlines() if not l.startswith("@__sched_"))  # baked ABI: no named slots
+    woven, notes, hit = weave_cached(src, env, "softmax_decode")
+    k = HostKernel(woven)
+    lens, bt, kc, vc, q, taus, maxp = build(5)
+    p.install_order(torch.arange(B - 1, -1, -1), B)
+    p.set_num_tasks(B)
+    p.set_rows(tau=taus.astype(np.int64), n=B)
+    p.push()
+    out = run(k, lens, bt, kc, vc, q, maxp)  # tables reached through the baked arena addresses
+    err = float(np.abs(out - reference(lens, bt, kc, vc, q, taus)).max())
+    timer = p.read_timer()[:B]
+    print("PHASE " + json.dumps({"hit": hit, "base": p.arena.base, "err": err,
+                                 "timer_rows": int((timer > 0).sum()), "cache": env["SCHED_KERNEL_CACHE"]}))
+"""
+
+
+def test_two_processes_share_the_arena_va_and_the_woven_kernel(tmp_path):
+    """The reference's fixed-VA check (test/py/test_fixed_va.py): two
+    processes in turn map the arena at the canonical VA, derive the same
+    cache key, and the second reuses the first one's woven module, whose
+    baked table addresses then reach the second process's arena (reversed
+    pi + per-request tau: exact truncated attention, timer rows filled)."""
+    import json
+    res = []
+    for _ in range(2):
+        out = run_child(PHASE % {"root": ROOT, "cache": str(tmp_path)})
+        line = [l for l in out.splitlines() if l.startswith("PHASE ")]
+        assert line, out
+        res.append(json.loads(line[0][len("PHASE "):]))
+    assert [r["hit"] for r in res] == [False, True], res
+    assert res[0]["base"] == res[1]["base"] and res[0]["cache"] == res[1]["cache"]
+    for r in res:
+        assert r["err"] < 1e-4 and r["timer_rows"] == 8, r
