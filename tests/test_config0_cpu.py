@@ -156,3 +156,54 @@ def test_shed_quality_sweep_is_monotone(kernels):
         cos.append(float(out @ full / np.linalg.norm(out) / np.linalg.norm(full)))
     assert all(b > a for a, b in zip(cos, cos[1:])), cos
     assert cos[-1] > 1 - 1e-6 and cos[0] < 0.9, cos
+
+
+def test_indirect_channels_word_zero_means_off():
+    """Indirect channels (SCHED_TIMER_INDIRECT / SCHED_ORDER_INDIRECT, the
+    reference's device channels, test/py/test_timer_indirect.py): the slot
+    word holds the address of the timer rows / order table, so a controller
+    retargets or switches them by rewriting one word; word 0 = timer off /
+    identity order. Results stay bit-exact against stock throughout."""
+    src = open(os.path.join(HERE, "softmax_decode.ll")).read()
+    stock = HostKernel(src)
+    woven, _ = weave(src, {"SCHED_TIMER_INDIRECT": "1", "SCHED_ORDER_INDIRECT": "1"})
+    k = HostKernel(woven)
+    lens, bt, kc, vc, q, _, maxp = build(6)
+    base = run(stock, lens, bt, kc, vc, q, maxp)
+    t = Tables()
+    t.order[:B] = np.arange(B - 1, -1, -1)
+    t.set_u32(abi.CTRL_ORDER_SIZE_OFF, B)
+    words = np.zeros(2, np.uint64)  # [0] timer channel, [1] order channel
+    k.set_global_ptr("__sched_ctrl", t.ctrl.ctypes.data)
+    k.set_global_ptr("__sched_timer", words.ctypes.data)
+    k.set_global_ptr("__sched_task_order", words.ctypes.data + 8)
+
+    def launch():
+        out = np.zeros((B, G, D), np.float32)
+        acc = np.zeros((B, G, D), np.float32)
+        p = ctypes.c_void_p
+        k.run("softmax_decode", (B,), (G,),
+              [q.ctypes.data, kc.ctypes.data, vc.ctypes.data, bt.ctypes.data, lens.ctypes.data, out.ctypes.data,
+               acc.ctypes.data, maxp, G, np.log2(np.e) / np.sqrt(D)],
+              [p, p, p, p, p, p, p, ctypes.c_int32, ctypes.c_int32, ctypes.c_float])
+        return out
+
+    # both channels off (word 0): stock behaviour, no timer rows
+    assert np.array_equal(launch(), base) and (t.timer == 0).all()
+    # timer channel on: every task's row fills; order still identity
+    words[0] = t.timer.ctypes.data
+    assert np.array_equal(launch(), base) and (t.timer[:B] > 0).all()
+    # retarget the timer to a second table by rewriting the word
+    other = np.zeros(64, np.uint64)
+    words[0] = other.ctypes.data
+    before = t.timer.copy()
+    # order channel on: reversed pi, still bit-exact
+    words[1] = t.order.ctypes.data
+    assert np.array_equal(launch(), base)
+    assert np.array_equal(t.timer, before) and (other[:B] > 0).all()
+    # the order channel is live: an all-zero table sends every CTA to task 0
+    t.order[:B] = 0
+    out = launch()
+    assert np.array_equal(out[0], base[0]) and not out[1:].any()
+    words[1] = 0  # word 0: identity again
+    assert np.array_equal(launch(), base)
