@@ -21,8 +21,10 @@ The inputs of every step exceed L2 (16 GB of weights stream each step), so no
 flush is needed between steps.
 
 ``--impl reference`` runs the reference project (jc-su/sched-pass) through
-its own public API when it is installed under baseline/_ref; see DESIGN.md
-for why that arm reports itself unavailable on this pool.
+its own public API when it is installed under baseline/_ref. The reference
+has no package metadata and its serving path needs clang+LLVM (its pass
+plugin) and SGLang, none of which this image has, so that arm prints an
+``unavailable`` line with the reason.
 """
 from __future__ import annotations
 
@@ -38,7 +40,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this metric/config
+BASELINE_VALUE = None  # the reference publishes no number for this metric/config
 METRIC = "decode tokens/sec/box and p99 TPOT at 1/2/4/8 B200 vs reference NCCL build"
 
 
