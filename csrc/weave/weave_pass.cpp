@@ -336,6 +336,67 @@ struct Site {
   int loop;
 };
 
+// A cp.async in a loop: its global source address is a stream the urgent
+// tier can warm in L2 ahead of the copy (the reference's async stream sites,
+// lib/SchedWeave.cpp:264-300 / :928-942). The data lands in shared memory,
+// so it is neither value-masked nor demoted.
+struct AsyncSite {
+  std::string text;  // the call's line (its position is found again by text)
+  std::string src, src_type;
+  int loop;
+};
+
+// Split "a, b(c, d), e" at top-level commas.
+std::vector<std::string> split_top(const std::string &s) {
+  std::vector<std::string> out;
+  int depth = 0;
+  std::string cur;
+  for (char ch : s) {
+    if (ch == '(' || ch == '{' || ch == '[' || ch == '<') ++depth;
+    if (ch == ')' || ch == '}' || ch == ']' || ch == '>') --depth;
+    if (ch == ',' && depth == 0) {
+      out.push_back(trim(cur));
+      cur.clear();
+    } else {
+      cur += ch;
+    }
+  }
+  if (!trim(cur).empty()) out.push_back(trim(cur));
+  return out;
+}
+
+// `call void asm sideeffect "<asm>", "<constraints>"(<args>)` holding a
+// cp.async: the argument bound to a 64-bit ("l") constraint with pointer type
+// is the global source. False when the line is not such a call.
+bool parse_cp_async(const std::string &text, std::string &src, std::string &src_type) {
+  const size_t a = text.find("asm ");
+  if (a == std::string::npos || text.find("cp.async") == std::string::npos) return false;
+  const size_t q0 = text.find('"', a);
+  const size_t q1 = q0 == std::string::npos ? q0 : text.find('"', q0 + 1);
+  const size_t c0 = q1 == std::string::npos ? q1 : text.find('"', q1 + 1);
+  const size_t c1 = c0 == std::string::npos ? c0 : text.find('"', c0 + 1);
+  if (c1 == std::string::npos) return false;
+  const std::string asm_text = text.substr(q0 + 1, q1 - q0 - 1);
+  if (asm_text.find("cp.async") == std::string::npos || asm_text.find("bulk") != std::string::npos) return false;
+  std::vector<std::string> cons;
+  for (const std::string &k : split_top(text.substr(c0 + 1, c1 - c0 - 1)))
+    if (!starts_with(k, "~{") && !starts_with(k, "=")) cons.push_back(k);
+  const size_t p0 = text.find('(', c1), p1 = text.rfind(')');
+  if (p0 == std::string::npos || p1 == std::string::npos || p1 <= p0) return false;
+  std::vector<std::string> args = split_top(text.substr(p0 + 1, p1 - p0 - 1));
+  for (size_t i = 0; i < args.size() && i < cons.size(); ++i) {
+    const size_t sp = args[i].rfind(' ');
+    if (sp == std::string::npos) continue;
+    const std::string ty = trim(args[i].substr(0, sp)), v = trim(args[i].substr(sp + 1));
+    if (cons[i] == "l" && starts_with(ty, "ptr") && !v.empty() && v[0] == '%') {
+      src = v;
+      src_type = ty;
+      return true;
+    }
+  }
+  return false;
+}
+
 void insert_after(Block &b, int idx, const std::vector<Inst> &code) {
   b.insts.insert(b.insts.begin() + idx + 1, code.begin(), code.end());
 }
@@ -367,6 +428,7 @@ class Weaver {
     // ---- phase 0: detection while the function is untouched
     std::vector<Loop> loops = find_loops(f, defs);
     std::vector<Site> sites;
+    async_sites.clear();
     if (c.policy || c.shed) {
       const std::set<std::string> written = written_roots(f, defs);
       for (size_t li = 0; li < loops.size(); ++li) {
@@ -388,6 +450,20 @@ class Weaver {
             if (sites.size() >= 4) break;
           }
       }
+      if (c.policy)
+        for (size_t li = 0; li < loops.size(); ++li) {
+          const Loop &L = loops[li];
+          if (L.iv.empty()) continue;
+          for (int b = L.header; b <= L.latch; ++b)
+            for (const Inst &in : f.blocks[b].insts) {
+              AsyncSite as;
+              if (in.opcode != "call" || !parse_cp_async(in.text, as.src, as.src_type)) continue;
+              if (address_kind(f, defs, L, as.src) == Mu::None) continue;
+              as.text = in.text;
+              as.loop = (int)li;
+              if (async_sites.size() < 4) async_sites.push_back(as);
+            }
+        }
       for (const Loop &L : loops)
         if (L.iv.empty()) n.add(f.name + ": loop at block " + std::to_string(L.header) +
                                 " has no canonical induction variable: shed/prefetch declined there");
@@ -441,7 +517,7 @@ class Weaver {
     }
     // policy flags / shed budget from the task's row
     std::string urgent, polite, budget;
-    bool need_row = !sites.empty() && ctrl.available;
+    bool need_row = (!sites.empty() || !async_sites.empty()) && ctrl.available;
     std::string row;
     if (need_row) {
       std::string inb = f.unique("%sched.row.inb"), use = f.unique("%sched.row.use"), idx = f.unique("%sched.row.idx");
@@ -538,6 +614,7 @@ class Weaver {
   Function &f;
   const Config &c;
   Notes &n;
+  std::vector<AsyncSite> async_sites;
 
   int sm() const {
     if (starts_with(m.target_cpu, "sm_")) return std::atoi(m.target_cpu.c_str() + 3);
@@ -732,6 +809,40 @@ class Weaver {
       insert_before(f.blocks[b], i, before);
       n.add(f.name + ": L2 policy woven at a stream load");
     }
+    for (const AsyncSite &as : async_sites) emit_async_warm(as, loops[as.loop], ui);
+  }
+
+  // cp.async source warming: prefetch the source `dist` iterations ahead,
+  // predicated on the urgent tier, when the source is affine in the IV.
+  void emit_async_warm(const AsyncSite &as, const Loop &L, const std::string &ui) {
+    for (Block &b : f.blocks)
+      for (size_t i = 0; i < b.insts.size(); ++i) {
+        if (b.insts[i].text != as.text) continue;
+        Defs defs(f);
+        const Inst *gep = defs.get(f, as.src);
+        long long step = 0;
+        int elem = 0;
+        if (gep && gep->opcode == "getelementptr" && gep->operands.size() == 2) {
+          std::string ty = trim(gep->text.substr(gep->text.find("getelementptr") + 13));
+          while (starts_with(ty, "inbounds ") || starts_with(ty, "nuw ") || starts_with(ty, "nusw "))
+            ty = trim(ty.substr(ty.find(' ')));
+          elem = type_bytes(trim(ty.substr(0, ty.find(','))));
+          if (elem <= 0 || !iv_step(f, defs, L.iv, gep->operands[1], step)) step = 0;
+        }
+        if (step == 0) {
+          n.add(f.name + ": cp.async source warming declined (no affine step)");
+          return;
+        }
+        std::string pint = f.unique("%sched.apf.int"), ahead = f.unique("%sched.apf.ahead");
+        insert_before(b, (int)i,
+                      {I("  " + pint + " = ptrtoint " + as.src_type + " " + as.src + " to i64"),
+                       I("  " + ahead + " = add i64 " + pint + ", " + std::to_string(step * elem * (long long)c.prefetch_dist)),
+                       I("  call void asm sideeffect \"{ .reg .pred p; setp.ne.u32 p, $1, 0; @p prefetch.global.L2::evict_last [$0]; }\", \"l,r,~{memory}\"(i64 " +
+                         ahead + ", i32 " + ui + ")")});
+        n.add(f.name + ": cp.async source warming woven (urgent prefetch ahead)");
+        return;
+      }
+    n.add(f.name + ": cp.async site moved; warming skipped");
   }
 
   void emit_timer(const Slot &timer, const std::string &t0, const std::string &gate, const std::string &task) {

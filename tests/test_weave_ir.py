@@ -237,3 +237,28 @@ def test_arith_fixture_runs_bit_exact_on_the_host():
     cut = run(wk, (order, ctrl))
     want = (kv.reshape(R, NT, D)[:, :tau] * w[None, :tau, None]).sum(1)
     assert np.allclose(cut, want, atol=1e-4) and not np.allclose(cut, base, atol=1e-3)
+
+
+def test_cp_async_source_warming():
+    """A cp.async whose global source is affine in the canonical IV is an
+    async stream site (the reference's cp.async detection): the urgent tier
+    warms the source 8 iterations ahead (64 floats = 256 bytes per iteration
+    -> 2048), predicated on the urgency flag and placed before the copy; the
+    copy itself, its wait and the shared-memory load are untouched; the
+    policy knob removes it."""
+    src = fixture("async_copy.ll")
+    out, notes = weave(src)
+    verify(out)
+    check_order(out, [
+        r"%sched\.urgent = or i1",
+        r"%sched\.apf\.int = ptrtoint ptr addrspace\(1\) %g to i64",
+        r"%sched\.apf\.ahead = add i64 %sched\.apf\.int, 2048",
+        r"prefetch\.global\.L2::evict_last \[\$0\]; \}\", \"l,r,~\{memory\}\"\(i64 %sched\.apf\.ahead, i32 %sched\.urgent\.i32\)",
+        r"call void asm sideeffect \"cp\.async\.ca\.shared\.global \[\$0\], \[\$1\], 4;\"",
+        r"cp\.async\.wait_all",
+        r"%v = load float, ptr addrspace\(3\) %sh",
+    ])
+    assert any("cp.async source warming woven" in n for n in notes)
+    assert "%sched.keep" not in out  # shared-memory data: no value mask
+    off, _ = weave(src, {"SCHED_NO_POLICY": "1"})
+    assert "%sched.apf" not in off
