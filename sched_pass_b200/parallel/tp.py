@@ -51,7 +51,7 @@ class TensorParallel:
         self.fused_calls = 0
         self.nccl_calls = 0
         self._fused = None
-        self._sp = None
+        self._sp: dict = {}  # hidden size -> SequenceParallel
         if self.mode not in ("fused", "nccl", "sp"):
             raise ValueError(f"unknown tensor-parallel mode {self.mode!r}")
         if self.mode == "fused" and self.world > 1:
@@ -59,16 +59,17 @@ class TensorParallel:
             self._fused = FusedAllReduce(self.group, self.device)
 
     def sequence_parallel(self, hidden: int, max_tokens: int):
-        """The sequence-parallel buffers of this group (``mode == "sp"``),
-        created on first use for the model's hidden size; None otherwise."""
+        """The sequence-parallel buffers of this group (``mode == "sp"``) for
+        a hidden size, created on first use (collectively: every rank makes
+        the same calls in the same order) and replaced by a larger set when a
+        caller needs more tokens; None in the other modes."""
         if self.mode != "sp" or self.world == 1:
             return None
-        if self._sp is None:
+        sp = self._sp.get(hidden)
+        if sp is None or sp.max_tokens < max_tokens:
             from .sp import SequenceParallel
-            self._sp = SequenceParallel(self.group, self.device, hidden, max_tokens)
-        elif self._sp.hidden != hidden or self._sp.max_tokens < max_tokens:
-            raise ValueError("one sequence-parallel buffer set per group: hidden size / tokens differ")
-        return self._sp
+            sp = self._sp[hidden] = SequenceParallel(self.group, self.device, hidden, max_tokens)
+        return sp
 
     def use_fused(self, T: int, N: int) -> bool:
         """Whether a [T, N] row-parallel output goes through the one-shot
