@@ -44,11 +44,27 @@ Q_TILE = 64
 MIXED_SEGMENTS = 4  # prefill requests per step of a fixed-shape (graph) mixed step
 
 
+def order_prefill_tiles(tiles: list, mode: str = "lpt") -> list:
+    """pi for prefill attention: the order of the query tiles in the launch
+    (tile i runs as CTA column i, so the order is the order the hardware
+    starts them). "lpt": longest first by causal work, rows x keys
+    (nq x (q_pos0 + nq)), ties in plan order -- the reference's prefill pi
+    (ROADMAP.md:450-451: -15.2 % at 48 requests on FlashInfer). "identity":
+    plan order. Each tile writes only its own rows, so every order gives
+    the same bits. Tiles are (bt row, first q row, rows, first position)."""
+    if mode == "identity" or len(tiles) < 2:
+        return list(tiles)
+    if mode != "lpt":
+        raise ValueError(f"unknown prefill tile order {mode!r}")
+    return sorted(tiles, key=lambda t: -(t[2] * (t[3] + t[2])))
+
+
 @dataclass
 class EngineConfig:
     max_batch: int = 256
     max_prefill_tokens: int = 4096
     max_step_tokens: int = 0        # cap on decode + prefill tokens per step (0 = none; see Scheduler)
+    prefill_order: str = "lpt"      # order of prefill attention tiles: "lpt" (longest first) | "identity"
     mixed_graphs: bool = True       # with max_step_tokens: pad mixed steps to a fixed shape per decode
                                     # bucket and replay them from CUDA graphs
     max_context: int = 4096
@@ -287,6 +303,7 @@ class Engine:
             for t0 in range(0, n, Q_TILE):
                 tiles.append((br, row - ndp + t0, min(Q_TILE, n - t0), start + t0))
             row += n
+        tiles = order_prefill_tiles(tiles, e.prefill_order)
         if pad is not None:
             # padding rows: no cache write, in no attention tile, never sampled
             ids[row:ndp + pad] = 0

@@ -88,3 +88,18 @@ def test_capped_mixed_steps_replay_graphs_with_the_eager_tokens():
         del eng
         torch.cuda.empty_cache()
     assert runs[True] == runs[False]
+
+
+def test_prefill_tile_order_does_not_change_tokens():
+    """Longest-first prefill tiles (the default) and plan order give the
+    same tokens: each tile writes only its own rows."""
+    ps = prompts(5, lo=100, hi=400, seed=9)
+    outs = []
+    for order in ("identity", "lpt"):
+        eng, _ = make_engine(cuda_graphs=True, prefill_order=order)
+        outs.append(eng.generate(ps, max_new_tokens=4))
+        ops.check_status()
+        eng.graphs.clear()
+        del eng
+        torch.cuda.empty_cache()
+    assert outs[0] == outs[1]
