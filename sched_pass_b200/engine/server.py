@@ -16,6 +16,9 @@ steps while there is work, and completes finished requests. Endpoints:
   histograms in the Prometheus text format (``engine/metrics.py``).
 
     python -m sched_pass_b200.engine.server --model llama-3-8b --port 30000
+    # tensor parallel: rank 0 serves HTTP, the other ranks follow
+    python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \
+        -m sched_pass_b200.engine.server --model llama-3-8b --port 30000
 """
 from __future__ import annotations
 
@@ -193,6 +196,100 @@ class EngineServer:
             self.stop()
 
 
+class TPEngineServer(EngineServer):
+    """HTTP front end of a tensor-parallel engine: rank 0 of the group runs
+    this server, every other rank runs ``follow`` with its own engine shard.
+
+    Each iteration rank 0 admits the requests submitted since the last one
+    (requests its engine refuses fail alone and are not sent), broadcasts
+    them with a stop flag to the group, and every rank adds the same
+    requests and then steps: the ranks' schedulers see identical admissions,
+    so every rank issues the same collectives in the same order (the engine
+    already advances every rank's workload clock by the slowest rank's step
+    time). Only the engine thread of rank 0 talks to the group."""
+
+    def __init__(self, engine, group=None, idle_wait_s: float = 0.002):
+        super().__init__(engine, idle_wait_s)
+        self.group = group
+
+    def _admit_batch(self) -> list:
+        sent = []
+        while True:
+            try:
+                req, fut = self._inbox.get_nowait()
+            except queue.Empty:
+                break
+            req.arrival = self.engine.clock
+            try:
+                self.engine.add_request(req)
+            except Exception as e:  # noqa: BLE001 - a bad request fails alone, on rank 0 only
+                fut.set_exception(e)
+                continue
+            self._pending[req.rid] = (req, fut)
+            sent.append((req.rid, [int(t) for t in req.prompt], req.max_new_tokens, req.urgency))
+        return sent
+
+    def _loop(self) -> None:
+        import torch.distributed as dist
+        try:
+            dev = getattr(self.engine, "device", None)
+            if dev is not None and getattr(dev, "type", "") == "cuda":
+                import torch
+                torch.cuda.set_device(dev)
+            while True:
+                if not self.engine.has_work() and self._inbox.empty() and not self._stop.is_set():
+                    try:  # idle: wait briefly for a request before the next round
+                        item = self._inbox.get(timeout=self.idle_wait_s)
+                        self._inbox.put(item)
+                    except queue.Empty:
+                        pass
+                stop = self._stop.is_set()
+                msg = [{"stop": stop, "reqs": [] if stop else self._admit_batch()}]
+                dist.broadcast_object_list(msg, src=dist.get_global_rank(self.group, 0) if self.group else 0,
+                                           group=self.group)
+                if stop:
+                    break
+                if self.engine.has_work():
+                    plan, done = self.engine.step()
+                    self.steps += 1
+                    self.decode_tokens += len(plan.decode)
+                    if self.metrics is not None:
+                        self.metrics.on_step(self.engine, plan)
+                    self._complete(done)
+        except BaseException as e:  # noqa: BLE001 - report to every waiter
+            self.error = e
+            for _, fut in list(self._pending.values()):
+                if not fut.done():
+                    fut.set_exception(e)
+            self._pending.clear()
+
+
+def follow(engine, group=None) -> int:
+    """The loop of a non-zero rank of a tensor-parallel server: receive each
+    round's admitted requests from rank 0, add them, step. Returns the number
+    of steps taken when rank 0 broadcasts stop."""
+    import torch.distributed as dist
+
+    from .request import Request
+    dev = getattr(engine, "device", None)
+    if dev is not None and getattr(dev, "type", "") == "cuda":
+        import torch
+        torch.cuda.set_device(dev)
+    src = dist.get_global_rank(group, 0) if group else 0
+    steps = 0
+    while True:
+        msg = [None]
+        dist.broadcast_object_list(msg, src=src, group=group)
+        for rid, ids, max_new, urgency in msg[0]["reqs"]:
+            engine.add_request(Request(rid=rid, prompt=np.asarray(ids, dtype=np.int32), max_new_tokens=max_new,
+                                       urgency=urgency, arrival=engine.clock))
+        if msg[0]["stop"]:
+            return steps
+        if engine.has_work():
+            engine.step()
+            steps += 1
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="llama-3-8b")
@@ -201,14 +298,25 @@ def main(argv=None) -> int:
     ap.add_argument("--max-batch", type=int, default=128)
     ap.add_argument("--max-context", type=int, default=4096)
     ap.add_argument("--acquire", default="auto")
+    ap.add_argument("--tp-mode", default=None, choices=[None, "fused", "sp", "nccl"])
     a = ap.parse_args(argv)
     import torch
 
     from ..models.config import get_config
+    from ..parallel.tp import TensorParallel, init_distributed
     from .engine import Engine, EngineConfig
+    rank, world, local = init_distributed("nccl")  # torchrun's env; world 1 without it
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    tp = TensorParallel(mode=a.tp_mode, device=dev) if world > 1 else None
     eng = Engine(get_config(a.model), EngineConfig(max_batch=a.max_batch, max_context=a.max_context,
-                                                   acquire=a.acquire, verbose=True), torch.device("cuda"))
-    EngineServer(eng).serve(a.host, a.port)
+                                                   acquire=a.acquire, verbose=rank == 0), dev, tp=tp)
+    if world == 1:
+        EngineServer(eng).serve(a.host, a.port)
+    elif rank == 0:
+        TPEngineServer(eng).serve(a.host, a.port)
+    else:
+        follow(eng)
     return 0
 
 

@@ -119,3 +119,33 @@ def test_server_futures_and_http_replay():
         th.join(10)
     finally:
         srv.stop()
+
+
+def test_tensor_parallel_server_keeps_ranks_in_lockstep():
+    """Rank 0 serves and broadcasts each round's admissions; followers add
+    the same requests and step: every rank takes the same number of steps
+    and finishes the same requests with the same tokens; a request rank 0
+    refuses is never sent."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    worker = os.path.join(root, "tests", "workers", "tp_server_worker.py")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [subprocess.Popen([sys.executable, worker], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
+                              env={**os.environ, "RANK": str(r), "WORLD_SIZE": "3", "MASTER_ADDR": "127.0.0.1",
+                                   "MASTER_PORT": str(port), "CUDA_VISIBLE_DEVICES": ""}) for r in range(3)]
+    outs = []
+    for p in procs:
+        so, se = p.communicate(timeout=120)
+        assert p.returncode == 0, se[-2000:]
+        outs.append(json.loads([l for l in so.splitlines() if l.startswith("SRVJSON ")][0][len("SRVJSON "):]))
+    r0 = outs[0]
+    assert r0["error"] is None and r0["bad_rejected"]
+    assert len(r0["outputs"]) == 12
+    for o in outs[1:]:
+        assert o["steps"] == r0["steps"] > 0
+        assert o["finished"] == r0["finished"]
+    assert [r0["outputs"][str(i)] for i in range(12)] == [r0["finished"][str(i)] for i in range(12)]

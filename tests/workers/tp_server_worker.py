@@ -1,0 +1,70 @@
+"""One gloo rank of the tensor-parallel server test: rank 0 runs
+TPEngineServer and submits requests, the other ranks follow; every rank has
+a fake engine behind the real scheduler. Prints one ``SRVJSON {...}`` line."""
+import datetime
+import json
+import os
+import sys
+
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+from sched_pass_b200.engine.scheduler import Scheduler  # noqa: E402
+from sched_pass_b200.engine.server import TPEngineServer, follow  # noqa: E402
+
+
+class FakeEngine:
+    """Scheduler + a model that emits (previous token + 1) mod vocab; each
+    step advances the clock by 1 ms. Records every finished request."""
+
+    def __init__(self):
+        self.sched = Scheduler(4096, 16, 8, 64, 4096)
+        self.clock = 0.0
+        self.device = None
+        self.finished = {}
+        self.steps = 0
+
+    def add_request(self, r):
+        self.sched.add(r)
+
+    def has_work(self):
+        return not self.sched.idle
+
+    def step(self):
+        plan = self.sched.schedule()
+        sampled = {r.rid: (r.next_input_token() + 1) % 1000 for r in plan.decode}
+        for r, start, n in plan.prefill:
+            if start + n >= r.prompt_len:
+                sampled[r.rid] = (int(r.prompt[-1]) + 1) % 1000
+        self.clock += 0.001
+        done = self.sched.commit(plan, sampled, self.clock)
+        for r in done:
+            self.finished[r.rid] = list(r.output)
+        self.steps += 1
+        return plan, done
+
+
+def main():
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    rank = dist.get_rank()
+    eng = FakeEngine()
+    out = {"rank": rank}
+    if rank == 0:
+        srv = TPEngineServer(eng).start()
+        futs = [srv.submit(list(range(5 + 7 * i)), 3 + i % 4) for i in range(12)]
+        bad = srv.submit(list(range(5000)), 3)  # beyond max_context: fails on rank 0 only, never sent
+        res = [f.result(timeout=60) for f in futs]
+        out["bad_rejected"] = bad.exception(timeout=60) is not None
+        srv.stop()
+        out["outputs"] = {str(i): r["output_ids"] for i, r in enumerate(res)}
+        out["error"] = repr(srv.error) if srv.error else None
+    else:
+        follow(eng)
+    out["steps"] = eng.steps
+    out["finished"] = {str(k): v for k, v in sorted(eng.finished.items())}
+    print("SRVJSON " + json.dumps(out), flush=True)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
