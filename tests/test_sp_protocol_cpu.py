@@ -71,7 +71,7 @@ def test_row_ownership_partitions_the_tokens():
             assert seen == list(range(T)), (world, T)
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 5])
 def test_emulated_sequence_parallel_is_exact(world):
     outs = launch("exact", world)
     for r in range(world):
