@@ -208,9 +208,12 @@ class TPEngineServer(EngineServer):
     already advances every rank's workload clock by the slowest rank's step
     time). Only the engine thread of rank 0 talks to the group."""
 
-    def __init__(self, engine, group=None, idle_wait_s: float = 0.002):
+    def __init__(self, engine, group=None, idle_wait_s: float = 0.002, heartbeat=None):
         super().__init__(engine, idle_wait_s)
         self.group = group
+        # parallel.health.Heartbeat: a silent or departed rank ends the loop
+        # (RankFailure, pending requests failed) before the next broadcast
+        self.heartbeat = heartbeat
 
     def _admit_batch(self) -> list:
         sent = []
@@ -243,6 +246,8 @@ class TPEngineServer(EngineServer):
                         self._inbox.put(item)
                     except queue.Empty:
                         pass
+                if self.heartbeat is not None:
+                    self.heartbeat.check()
                 stop = self._stop.is_set()
                 msg = [{"stop": stop, "reqs": [] if stop else self._admit_batch()}]
                 dist.broadcast_object_list(msg, src=dist.get_global_rank(self.group, 0) if self.group else 0,
@@ -264,10 +269,13 @@ class TPEngineServer(EngineServer):
             self._pending.clear()
 
 
-def follow(engine, group=None) -> int:
+def follow(engine, group=None, heartbeat=None, max_rounds: int | None = None) -> int:
     """The loop of a non-zero rank of a tensor-parallel server: receive each
     round's admitted requests from rank 0, add them, step. Returns the number
-    of steps taken when rank 0 broadcasts stop."""
+    of steps taken when rank 0 broadcasts stop (or after ``max_rounds``
+    rounds). With a ``heartbeat`` a silent peer raises RankFailure before the
+    next round; a peer lost during a round ends it with the process group's
+    timeout."""
     import torch.distributed as dist
 
     from .request import Request
@@ -277,7 +285,11 @@ def follow(engine, group=None) -> int:
         torch.cuda.set_device(dev)
     src = dist.get_global_rank(group, 0) if group else 0
     steps = 0
-    while True:
+    rounds = 0
+    while max_rounds is None or rounds < max_rounds:
+        rounds += 1
+        if heartbeat is not None:
+            heartbeat.check()
         msg = [None]
         dist.broadcast_object_list(msg, src=src, group=group)
         for rid, ids, max_new, urgency in msg[0]["reqs"]:
@@ -288,6 +300,7 @@ def follow(engine, group=None) -> int:
         if engine.has_work():
             engine.step()
             steps += 1
+    return steps
 
 
 def main(argv=None) -> int:

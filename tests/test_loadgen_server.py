@@ -149,3 +149,34 @@ def test_tensor_parallel_server_keeps_ranks_in_lockstep():
         assert o["steps"] == r0["steps"] > 0
         assert o["finished"] == r0["finished"]
     assert [r0["outputs"][str(i)] for i in range(12)] == [r0["finished"][str(i)] for i in range(12)]
+
+
+def test_tensor_parallel_server_fails_requests_when_a_rank_leaves():
+    """A follower leaves between rounds: rank 0's server fails its pending
+    requests (rank failure or the group's timeout) within seconds instead of
+    waiting for ever, and the surviving follower ends too."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    worker = os.path.join(root, "tests", "workers", "tp_server_worker.py")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [subprocess.Popen([sys.executable, worker, "leave"], stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                              text=True, env={**os.environ, "RANK": str(r), "WORLD_SIZE": "3",
+                                              "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port),
+                                              "CUDA_VISIBLE_DEVICES": ""}) for r in range(3)]
+    outs = {}
+    for r, p in enumerate(procs):
+        so, se = p.communicate(timeout=120)
+        lines = [l for l in so.splitlines() if l.startswith("SRVJSON ")]
+        assert lines, (r, se[-2000:])
+        outs[r] = json.loads(lines[0][len("SRVJSON "):])
+    assert outs[2]["left"]
+    assert all(e is not None for e in outs[0]["failed"]), outs[0]
+    assert outs[0]["elapsed"] < 30, outs[0]
+    # the survivor ends with the heartbeat's RankFailure or the group's own error
+    # (timeout or a closed connection, depending on which is seen first)
+    f = outs[1]["follower"]
+    assert f == "RankFailure" or f.endswith("Error"), outs[1]

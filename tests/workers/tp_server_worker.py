@@ -44,11 +44,49 @@ class FakeEngine:
         return plan, done
 
 
+def leave_scenario(rank, eng, out):
+    """The last rank follows a few rounds, then leaves between rounds: rank
+    0's server must fail its pending requests instead of hanging."""
+    import time
+
+    from sched_pass_b200.parallel.health import Heartbeat
+    world = dist.get_world_size()
+    hb = Heartbeat(rank, world, interval=0.05, timeout=1.0).start()
+    dist.barrier()
+    if rank == 0:
+        srv = TPEngineServer(eng, heartbeat=hb, idle_wait_s=0.01).start()
+        futs = [srv.submit(list(range(20)), 4000) for _ in range(4)]  # never finish before the failure
+        t0 = time.monotonic()
+        errs = []
+        for f in futs:
+            try:
+                f.result(timeout=60)
+                errs.append(None)
+            except Exception as e:  # noqa: BLE001
+                errs.append(type(e).__name__)
+        out.update(failed=errs, elapsed=time.monotonic() - t0, error=repr(srv.error))
+        srv._stop.set()
+    elif rank == world - 1:
+        follow(eng, heartbeat=hb, max_rounds=20)
+        hb.leave()
+        out["left"] = True
+    else:
+        try:
+            follow(eng, heartbeat=hb)
+            out["follower"] = "stopped"
+        except Exception as e:  # noqa: BLE001
+            out["follower"] = type(e).__name__
+    print("SRVJSON " + json.dumps(out), flush=True)
+    os._exit(0)  # skip the group teardown: a peer is gone
+
+
 def main():
-    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60 if len(sys.argv) < 2 else 5))
     rank = dist.get_rank()
     eng = FakeEngine()
     out = {"rank": rank}
+    if len(sys.argv) > 1 and sys.argv[1] == "leave":
+        return leave_scenario(rank, eng, out)
     if rank == 0:
         srv = TPEngineServer(eng).start()
         futs = [srv.submit(list(range(5 + 7 * i)), 3 + i % 4) for i in range(12)]
