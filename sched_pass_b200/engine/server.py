@@ -326,10 +326,14 @@ def main(argv=None) -> int:
                                                    acquire=a.acquire, verbose=rank == 0), dev, tp=tp)
     if world == 1:
         EngineServer(eng).serve(a.host, a.port)
-    elif rank == 0:
-        TPEngineServer(eng).serve(a.host, a.port)
+        return 0
+    from ..parallel.health import Heartbeat
+    hb = Heartbeat(rank, world).start()
+    if rank == 0:
+        TPEngineServer(eng, heartbeat=hb).serve(a.host, a.port)
     else:
-        follow(eng)
+        follow(eng, heartbeat=hb)
+    hb.stop()
     return 0
 
 
