@@ -180,3 +180,27 @@ def test_tensor_parallel_server_fails_requests_when_a_rank_leaves():
     # (timeout or a closed connection, depending on which is seen first)
     f = outs[1]["follower"]
     assert f == "RankFailure" or f.endswith("Error"), outs[1]
+
+
+def test_serving_ab_interleaves_arms_and_restores_env():
+    """The A/B driver builds one engine per (round, arm) with the arm's
+    engine options and SCHED_* variables, interleaves the arms round by
+    round, restores the environment, and keeps each arm's best round."""
+    import os
+
+    from sched_pass_b200.benchmarks.serving_ab import run_ab
+    seen = []
+
+    def make(kw):
+        seen.append((kw.get("levers"), os.environ.get("SCHED_ENFORCE")))
+        return FakeEngine()
+
+    before = os.environ.get("SCHED_ENFORCE")
+    work = loadgen.dispersed(12, mu=3.0, sigma=0.5, lo=4, hi=40, out=3, vocab=1000, seed=3, rate=100.0)
+    lines = []
+    best = run_ab(make, work, ["stock", "observe", "enforce"], 2, emit=lines.append)
+    assert seen == [(False, before), (True, "0"), (True, "1")] * 2
+    assert os.environ.get("SCHED_ENFORCE") == before
+    assert set(best) == {"stock", "observe", "enforce"} and all(b["n_ok"] == 12 for b in best.values())
+    assert [json.loads(l).get("arm") for l in lines[:-1]] == ["stock", "observe", "enforce"] * 2
+    assert "summary" in json.loads(lines[-1])
