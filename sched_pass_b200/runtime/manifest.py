@@ -1,8 +1,12 @@
 """Python mirror of the lever registry (include/sched/manifest.h).
 
-Row order is the weave order. ``tests/test_manifest.py`` checks this mirror
+Row order is the weave order. ``tests/test_weave_ir.py`` checks this mirror
 against the C++ table, dumped by ``sched-weave --manifest=csv``.
 Fields: name, effect, min_sm, knob, knob_disables, tag.
+
+``python -m sched_pass_b200.runtime.manifest`` prints the table as markdown
+(the reference generates the same document from its C++ manifest,
+scripts/gen_manifest_doc.sh).
 """
 from __future__ import annotations
 
@@ -33,3 +37,17 @@ def levers_enabled(env) -> dict:
         present = bool(env.get(knob))
         out[name] = (not present) if disables else present
     return out
+
+
+def manifest_markdown() -> str:
+    """The lever table as markdown, one row per lever in weave order."""
+    lines = ["| order | lever | effect | min SM | knob | knob disables | cache tag |",
+             "|---|---|---|---|---|---|---|"]
+    for i, (name, effect, min_sm, knob, disables, tag) in enumerate(MANIFEST):
+        lines.append(f"| {i} | {name} | {effect} | {min_sm or '-'} | `{knob}` | {'yes' if disables else 'no (enables)'} "
+                     f"| {('`' + tag + '`') if tag else '-'} |")
+    return "\n".join(lines)
+
+
+if __name__ == "__main__":
+    print(manifest_markdown())

@@ -262,3 +262,10 @@ def test_cp_async_source_warming():
     assert "%sched.keep" not in out  # shared-memory data: no value mask
     off, _ = weave(src, {"SCHED_NO_POLICY": "1"})
     assert "%sched.apf" not in off
+
+
+def test_manifest_markdown_lists_every_lever_in_order():
+    from sched_pass_b200.runtime.manifest import manifest_markdown
+    rows = manifest_markdown().splitlines()[2:]
+    assert [r.split("|")[2].strip() for r in rows] == [m[0] for m in MANIFEST]
+    assert "`SCHED_NO_SHED`" in rows[2] and "`-nos`" in rows[2]
