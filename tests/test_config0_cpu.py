@@ -207,3 +207,31 @@ def test_indirect_channels_word_zero_means_off():
     assert np.array_equal(out[0], base[0]) and not out[1:].any()
     words[1] = 0  # word 0: identity again
     assert np.array_equal(launch(), base)
+
+
+def test_churn_steps_stay_bit_exact():
+    """48 consecutive "steps" with a changing request mix (new lengths and
+    pages every step), the order table rewritten each step (reversed,
+    rotated, stale-sized) and the timer toggled: every step's woven output
+    equals the stock kernel's (the reference's 48-step churn check,
+    test/py/test_gqa_repro_steps.py)."""
+    stock, woven = kernels_pair()
+    t = Tables()
+    for step in range(48):
+        lens, bt, kc, vc, q, _, maxp = build(100 + step)
+        base = run(stock, lens, bt, kc, vc, q, maxp)
+        kind = step % 3
+        t.order[:B] = np.arange(B - 1, -1, -1) if kind == 0 else np.roll(np.arange(B), step)
+        t.set_u32(abi.CTRL_ORDER_SIZE_OFF, B if kind != 2 else B + 1)  # kind 2: stale size -> identity
+        t.set_u32(abi.CTRL_FLAGS_OFF, abi.FLAG_TIMER_OFF if step % 2 else 0)
+        assert np.array_equal(run(woven, lens, bt, kc, vc, q, maxp, t), base), step
+
+
+_PAIR = []
+
+
+def kernels_pair():
+    if not _PAIR:
+        src = open(os.path.join(HERE, "softmax_decode.ll")).read()
+        _PAIR.extend([HostKernel(src), HostKernel(weave(src)[0])])
+    return _PAIR
