@@ -15,7 +15,9 @@ Reported:
   value       decode tokens / s of the timed steps (device time)
   e2e.value   the same through the public step API measured with the host
               clock, which includes each step's pinned H2D input copy and the
-              D2H read of the sampled tokens
+              D2H read of the sampled tokens (the engine is synchronous per
+              step, so it tracks value; forward_only_tok_s and host_gap_share
+              split the step into forward passes and the host work between)
   p99/p50 TPOT over requests that finished inside the timed window
 The inputs of every step exceed L2 (16 GB of weights stream each step), so no
 flush is needed between steps.
@@ -208,6 +210,14 @@ def main():
         "finished_in_window": len(finished),
         "step_ms_p50": round(float(np.median(step_ms)), 3) if step_ms else None,
         "step_ms_p99": round(pct(sorted(step_ms), 99), 3) if step_ms else None,
+        # the engine is synchronous per step (it reads the sampled tokens back),
+        # so the device timeline spans the host's planning and copies too and
+        # e2e matches value; these two fields split that time: forward passes
+        # alone (sum of per-step device times) vs everything between them
+        "forward_only_tok_s": (round(decode_tokens / (sum(step_ms) / 1e3), 2)
+                               if step_ms and sum(step_ms) > 0 else None),
+        "host_gap_share": (round(max(0.0, 1.0 - (sum(step_ms) / 1e3) / dev_s), 4)
+                           if step_ms and dev_s > 0 else None),
         "e2e": {"value": round(e2e, 2), "unit": "decode tokens/s", "h2d_bytes_per_step": bytes_in,
                 "d2h_bytes_per_step": 4 * 2 * args.max_batch},
         "gpu_launches": None,
