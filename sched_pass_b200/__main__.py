@@ -1,0 +1,84 @@
+"""Command line of the framework:
+
+    python -m sched_pass_b200 build                      compile the native parts (sm_100a)
+    python -m sched_pass_b200 weave IN.ll [-o OUT.ll] [--env K=V ...]
+                                                          weave the levers into LLVM IR
+    python -m sched_pass_b200 manifest [--csv]           the lever table
+    python -m sched_pass_b200 serve [server options]     HTTP server (engine/server.py)
+    python -m sched_pass_b200 loadgen [loadgen options]  load generator (engine/loadgen.py)
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+
+
+def _weave(argv) -> int:
+    from .compiler.weave import weave
+    ap = argparse.ArgumentParser(prog="sched_pass_b200 weave")
+    ap.add_argument("src")
+    ap.add_argument("-o", "--out", default="-")
+    ap.add_argument("--env", action="append", default=[], help="SCHED_* knob as KEY=VALUE (repeatable)")
+    ap.add_argument("--passes", default="sched-workqueue,sched-weave")
+    a = ap.parse_args(argv)
+    env = {}
+    for kv in a.env:
+        k, _, v = kv.partition("=")
+        if not k.startswith("SCHED_"):
+            ap.error(f"--env expects SCHED_* knobs, not {k!r}")
+        env[k] = v
+    with open(a.src) as f:
+        text = f.read()
+    out, notes = weave(text, env, a.passes)
+    for n in notes:
+        print("[sched] " + n, file=sys.stderr)
+    if a.out == "-":
+        sys.stdout.write(out)
+    else:
+        with open(a.out, "w") as f:
+            f.write(out)
+    return 0
+
+
+def _manifest(argv) -> int:
+    ap = argparse.ArgumentParser(prog="sched_pass_b200 manifest")
+    ap.add_argument("--csv", action="store_true", help="the C++ table as sched-weave dumps it")
+    a = ap.parse_args(argv)
+    if a.csv:
+        from .compiler.weave import manifest_csv
+        rows = manifest_csv()
+        print(",".join(rows[0].keys()))
+        for r in rows:
+            print(",".join(r.values()))
+    else:
+        from .runtime.manifest import manifest_markdown
+        print(manifest_markdown())
+    return 0
+
+
+def main(argv=None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if not argv or argv[0] in ("-h", "--help"):
+        print(__doc__)
+        return 0
+    cmd, rest = argv[0], argv[1:]
+    if cmd == "build":
+        from . import _build
+        _build.build_all(verbose="-v" in rest)
+        return 0
+    if cmd == "weave":
+        return _weave(rest)
+    if cmd == "manifest":
+        return _manifest(rest)
+    if cmd == "serve":
+        from .engine.server import main as serve_main
+        return serve_main(rest)
+    if cmd == "loadgen":
+        from .engine.loadgen import main as loadgen_main
+        return loadgen_main(rest)
+    print(f"unknown command {cmd!r}\n" + __doc__, file=sys.stderr)
+    return 2
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

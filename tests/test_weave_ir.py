@@ -269,3 +269,19 @@ def test_manifest_markdown_lists_every_lever_in_order():
     rows = manifest_markdown().splitlines()[2:]
     assert [r.split("|")[2].strip() for r in rows] == [m[0] for m in MANIFEST]
     assert "`SCHED_NO_SHED`" in rows[2] and "`-nos`" in rows[2]
+
+
+def test_command_line_weave_and_manifest(tmp_path):
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(HERE))
+    out = tmp_path / "w.ll"
+    r = subprocess.run([sys.executable, "-m", "sched_pass_b200", "weave", os.path.join(HERE, "paged_linear.ll"),
+                        "-o", str(out), "--env", "SCHED_PDL=1"], capture_output=True, text=True, cwd=root)
+    assert r.returncode == 0, r.stderr
+    text = out.read_text()
+    verify(text)
+    assert "griddepcontrol.wait" in text and "remapped 1 ctaid" in r.stderr
+    m = subprocess.run([sys.executable, "-m", "sched_pass_b200", "manifest", "--csv"], capture_output=True,
+                       text=True, cwd=root)
+    assert m.returncode == 0 and m.stdout.splitlines()[0] == "name,effect,minSm,knob,disableKnob,order,tag"
