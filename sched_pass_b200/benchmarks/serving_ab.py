@@ -4,7 +4,7 @@ with the levers off ("stock"), learning costs without installing anything
 "enforce-noclc" (acquisition pinned to static + pi). The reference runs the
 same three arms against SGLang (scripts/bench_ab.sh:56-58) and warns that
 end-to-end serving numbers swing 10-25 % between identical runs
-(ROADMAP.md:854-857), so the arms are interleaved over ``--repeats`` rounds
+(jc-su/sched-pass ROADMAP.md:854-857), so the arms are interleaved over ``--repeats`` rounds
 on one set of weights and the summary keeps the best round per arm.
 
     python -m sched_pass_b200.benchmarks.serving_ab --mix dispersed --requests 400 --repeats 3

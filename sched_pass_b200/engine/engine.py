@@ -49,7 +49,7 @@ def order_prefill_tiles(tiles: list, mode: str = "lpt") -> list:
     (tile i runs as CTA column i, so the order is the order the hardware
     starts them). "lpt": longest first by causal work, rows x keys
     (nq x (q_pos0 + nq)), ties in plan order -- the reference's prefill pi
-    (ROADMAP.md:450-451: -15.2 % at 48 requests on FlashInfer). "identity":
+    (jc-su/sched-pass ROADMAP.md:450-451: -15.2 % at 48 requests). "identity":
     plan order. Each tile writes only its own rows, so every order gives
     the same bits. Tiles are (bt row, first q row, rows, first position)."""
     if mode == "identity" or len(tiles) < 2:
