@@ -220,6 +220,15 @@ class Engine:
     def add_request(self, req: Request) -> None:
         self.sched.add(req)
 
+    def abort(self, req: Request) -> bool:
+        """Cancel a request between steps (pages freed, controller state
+        dropped). Every tensor-parallel rank must abort the same requests
+        before the same step."""
+        ok = self.sched.abort(req)
+        if ok:
+            self.controller.forget([req.rid])
+        return ok
+
     def add_prefilled(self, req: Request, first_token: int) -> None:
         """Admit ``req`` as if its prompt had been prefilled: its pages are
         allocated and left with whatever the cache holds there (see

@@ -112,6 +112,20 @@ class Scheduler:
             self.alloc.give(pages.astype(np.int32))
             req.pages = []
 
+    def abort(self, req: Request) -> bool:
+        """Drop a request between steps, wherever it is (waiting, prefilling
+        or decoding): its pages go back to the pools and it is marked DONE.
+        False when the scheduler does not hold it (finished already)."""
+        if req in self.running:
+            self.running.remove(req)
+        elif req in self.waiting:
+            self.waiting.remove(req)
+        else:
+            return False
+        self.release(req)
+        req.state = State.DONE
+        return True
+
     def _preempt(self, victim: Request, plan: StepPlan) -> None:
         self.running.remove(victim)
         self.release(victim)

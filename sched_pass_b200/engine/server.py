@@ -10,6 +10,9 @@ steps while there is work, and completes finished requests. Endpoints:
   and ``engine/loadgen.py`` send); returns ``{"output_ids": [...],
   "meta_info": {"prompt_tokens", "completion_tokens", "e2e_latency",
   "ttft", "tpot"}}``. Decoding is greedy and runs ``max_new_tokens`` tokens.
+  An optional ``"rid"`` (any string) names the request for ``/abort``.
+* ``POST /abort`` -- ``{"rid": ...}``: cancel a queued or running request
+  between steps (its pages are freed; its ``/generate`` call answers 499).
 * ``GET /health`` -- liveness plus queue depths.
 * ``GET /stats`` -- steps, decode tokens, the scheduling plugin's counters.
 * ``GET /metrics`` -- the same and step-time / TPOT / TTFT / latency
@@ -38,6 +41,9 @@ class EngineServer:
         self._inbox: queue.Queue = queue.Queue()
         self._pending: dict = {}
         self._next_rid = 0
+        self._aborts: queue.Queue = queue.Queue()
+        self._dropped: set = set()
+        self._named: dict = {}  # client rid -> internal rid
         self._lock = threading.Lock()
         self._stop = threading.Event()
         self._thread: threading.Thread | None = None
@@ -51,8 +57,9 @@ class EngineServer:
             self.metrics = None
 
     # ---------------------------------------------------------------- client side
-    def submit(self, input_ids, max_new_tokens: int, urgency: float = 0.0) -> cf.Future:
-        """Queue one request; the future resolves to the response dict."""
+    def submit(self, input_ids, max_new_tokens: int, urgency: float = 0.0, name: str | None = None) -> cf.Future:
+        """Queue one request; the future resolves to the response dict.
+        ``name``: a client id that ``cancel`` accepts."""
         from .request import Request
         ids = np.asarray(input_ids, dtype=np.int32)
         if ids.ndim != 1 or ids.size == 0:
@@ -63,18 +70,55 @@ class EngineServer:
         with self._lock:
             rid = self._next_rid
             self._next_rid += 1
+            if name is not None:
+                self._named[str(name)] = rid
         req = Request(rid=rid, prompt=ids, max_new_tokens=int(max_new_tokens), urgency=float(urgency))
         req._t_submit = time.perf_counter()  # host clock of the HTTP side
+        req._name = None if name is None else str(name)
         self._inbox.put((req, fut))
         return fut
 
+    def cancel(self, name) -> None:
+        """Ask the engine thread to abort the request submitted as ``name``
+        (a client id) or with internal id ``name`` (an int)."""
+        with self._lock:
+            rid = self._named.pop(str(name), None) if not isinstance(name, int) else name
+        if rid is None:
+            raise KeyError(f"no request named {name!r}")
+        self._aborts.put(rid)
+
     # ---------------------------------------------------------------- engine thread
+    def _drain_aborts(self) -> list:
+        rids = []
+        while True:
+            try:
+                rids.append(self._aborts.get_nowait())
+            except queue.Empty:
+                return rids
+
+    def _apply_aborts(self, rids) -> None:
+        """Abort on the engine (between steps) and fail the callers."""
+        for rid in rids:
+            item = self._pending.pop(rid, None)
+            if item is None:
+                # still in the inbox: it will be dropped when admitted
+                self._dropped.add(rid)
+                continue
+            req, fut = item
+            self.engine.abort(req)
+            if not fut.done():
+                fut.set_exception(cf.CancelledError(f"request {rid} aborted"))
+
     def _admit(self) -> None:
         while True:
             try:
                 req, fut = self._inbox.get_nowait()
             except queue.Empty:
                 return
+            if req.rid in self._dropped:
+                self._dropped.discard(req.rid)
+                fut.set_exception(cf.CancelledError(f"request {req.rid} aborted"))
+                continue
             req.arrival = self.engine.clock
             try:
                 self.engine.add_request(req)
@@ -90,6 +134,9 @@ class EngineServer:
             if item is None:
                 continue
             _, fut = item
+            if getattr(r, "_name", None) is not None:
+                with self._lock:
+                    self._named.pop(r._name, None)
             tpot = r.tpot()
             if self.metrics is not None:
                 self.metrics.on_done(tpot, r.ttft(), now - r._t_submit)
@@ -107,6 +154,7 @@ class EngineServer:
                 import torch
                 torch.cuda.set_device(dev)
             while not self._stop.is_set():
+                self._apply_aborts(self._drain_aborts())
                 self._admit()
                 if self.engine.has_work():
                     plan, done = self.engine.step()
@@ -156,13 +204,24 @@ class EngineServer:
             if ids is None:
                 raise HTTPException(400, "input_ids is required (token ids; no tokenizer in this server)")
             try:
-                fut = self.submit(ids, int(sp.get("max_new_tokens", 16)), float(body.get("urgency", 0.0)))
+                fut = self.submit(ids, int(sp.get("max_new_tokens", 16)), float(body.get("urgency", 0.0)),
+                                  name=body.get("rid"))
             except ValueError as e:
                 raise HTTPException(400, str(e)) from e
             try:
                 return JSONResponse(await asyncio.wrap_future(fut))
+            except (cf.CancelledError, asyncio.CancelledError) as e:
+                raise HTTPException(499, f"aborted: {e}") from e
             except Exception as e:  # noqa: BLE001
                 raise HTTPException(500, repr(e)) from e
+
+        @app.post("/abort")
+        async def abort(body: dict):
+            try:
+                self.cancel(body.get("rid"))
+            except KeyError as e:
+                raise HTTPException(404, str(e)) from e
+            return {"ok": True}
 
         @app.get("/health")
         async def health():
@@ -222,6 +281,10 @@ class TPEngineServer(EngineServer):
                 req, fut = self._inbox.get_nowait()
             except queue.Empty:
                 break
+            if req.rid in self._dropped:
+                self._dropped.discard(req.rid)
+                fut.set_exception(cf.CancelledError(f"request {req.rid} aborted"))
+                continue
             req.arrival = self.engine.clock
             try:
                 self.engine.add_request(req)
@@ -249,7 +312,11 @@ class TPEngineServer(EngineServer):
                 if self.heartbeat is not None:
                     self.heartbeat.check()
                 stop = self._stop.is_set()
-                msg = [{"stop": stop, "reqs": [] if stop else self._admit_batch()}]
+                aborts = [] if stop else [r for r in self._drain_aborts()]
+                # only requests every rank holds are aborted on the group
+                held = [r for r in aborts if r in self._pending]
+                self._apply_aborts(aborts)
+                msg = [{"stop": stop, "reqs": [] if stop else self._admit_batch(), "aborts": held}]
                 dist.broadcast_object_list(msg, src=dist.get_global_rank(self.group, 0) if self.group else 0,
                                            group=self.group)
                 if stop:
@@ -286,19 +353,28 @@ def follow(engine, group=None, heartbeat=None, max_rounds: int | None = None) ->
     src = dist.get_global_rank(group, 0) if group else 0
     steps = 0
     rounds = 0
+    held = {}  # rid -> Request this rank admitted (finished ones are dropped as they finish)
     while max_rounds is None or rounds < max_rounds:
         rounds += 1
         if heartbeat is not None:
             heartbeat.check()
         msg = [None]
         dist.broadcast_object_list(msg, src=src, group=group)
+        for rid in msg[0].get("aborts", []):
+            req = held.pop(rid, None)
+            if req is not None:
+                engine.abort(req)
         for rid, ids, max_new, urgency in msg[0]["reqs"]:
-            engine.add_request(Request(rid=rid, prompt=np.asarray(ids, dtype=np.int32), max_new_tokens=max_new,
-                                       urgency=urgency, arrival=engine.clock))
+            req = Request(rid=rid, prompt=np.asarray(ids, dtype=np.int32), max_new_tokens=max_new,
+                          urgency=urgency, arrival=engine.clock)
+            held[rid] = req
+            engine.add_request(req)
         if msg[0]["stop"]:
             return steps
         if engine.has_work():
-            engine.step()
+            _, done = engine.step()
+            for r in done:
+                held.pop(r.rid, None)
             steps += 1
     return steps
 

@@ -26,6 +26,9 @@ class FakeEngine:
     def add_request(self, r):
         self.sched.add(r)
 
+    def abort(self, r):
+        return self.sched.abort(r)
+
     def has_work(self):
         return not self.sched.idle
 
@@ -143,8 +146,9 @@ def test_tensor_parallel_server_keeps_ranks_in_lockstep():
         assert p.returncode == 0, se[-2000:]
         outs.append(json.loads([l for l in so.splitlines() if l.startswith("SRVJSON ")][0][len("SRVJSON "):]))
     r0 = outs[0]
-    assert r0["error"] is None and r0["bad_rejected"]
+    assert r0["error"] is None and r0["bad_rejected"] and r0["long_cancelled"]
     assert len(r0["outputs"]) == 12
+    assert all(o["idle"] for o in outs)  # the cancelled request left no pages behind on any rank
     for o in outs[1:]:
         assert o["steps"] == r0["steps"] > 0
         assert o["finished"] == r0["finished"]
@@ -204,3 +208,42 @@ def test_serving_ab_interleaves_arms_and_restores_env():
     assert set(best) == {"stock", "observe", "enforce"} and all(b["n_ok"] == 12 for b in best.values())
     assert [json.loads(l).get("arm") for l in lines[:-1]] == ["stock", "observe", "enforce"] * 2
     assert "summary" in json.loads(lines[-1])
+
+
+def test_cancel_running_and_queued_requests():
+    """A running request and one cancelled right after submission both end
+    with CancelledError; their pages return to the pool and the server keeps
+    serving; an unknown name is refused."""
+    import concurrent.futures as cf
+
+    import pytest
+    class SlowFake(FakeEngine):
+        def step(self):
+            time.sleep(0.001)  # a long request stays running for seconds
+            return super().step()
+
+    srv = EngineServer(SlowFake()).start()
+    try:
+        f = srv.submit([1, 2, 3], 4000, name="long")
+        for _ in range(500):
+            if srv._pending:
+                break
+            time.sleep(0.01)
+        srv.cancel("long")
+        with pytest.raises(cf.CancelledError):
+            f.result(timeout=10)
+        g = srv.submit([4, 5], 4000, name="q")
+        srv.cancel("q")
+        with pytest.raises(cf.CancelledError):
+            g.result(timeout=10)
+        assert srv.submit([7], 2).result(timeout=10)["output_ids"] == [8, 9]
+        for _ in range(500):
+            if srv.engine.sched.idle:
+                break
+            time.sleep(0.01)
+        sched = srv.engine.sched
+        assert sched.idle and sched.alloc.free == sched.alloc.num_pages
+        with pytest.raises(KeyError):
+            srv.cancel("nope")
+    finally:
+        srv.stop()

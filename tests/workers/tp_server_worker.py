@@ -27,6 +27,9 @@ class FakeEngine:
     def add_request(self, r):
         self.sched.add(r)
 
+    def abort(self, r):
+        return self.sched.abort(r)
+
     def has_work(self):
         return not self.sched.idle
 
@@ -91,14 +94,23 @@ def main():
         srv = TPEngineServer(eng).start()
         futs = [srv.submit(list(range(5 + 7 * i)), 3 + i % 4) for i in range(12)]
         bad = srv.submit(list(range(5000)), 3)  # beyond max_context: fails on rank 0 only, never sent
+        long = srv.submit(list(range(9)), 3500, name="long")  # cancelled while running
         res = [f.result(timeout=60) for f in futs]
         out["bad_rejected"] = bad.exception(timeout=60) is not None
+        srv.cancel("long")
+        import concurrent.futures as cf
+        try:
+            long.result(timeout=60)
+            out["long_cancelled"] = False
+        except cf.CancelledError:
+            out["long_cancelled"] = True
         srv.stop()
         out["outputs"] = {str(i): r["output_ids"] for i, r in enumerate(res)}
         out["error"] = repr(srv.error) if srv.error else None
     else:
         follow(eng)
     out["steps"] = eng.steps
+    out["idle"] = eng.sched.idle and eng.sched.alloc.free == eng.sched.alloc.num_pages
     out["finished"] = {str(k): v for k, v in sorted(eng.finished.items())}
     print("SRVJSON " + json.dumps(out), flush=True)
     dist.destroy_process_group()
