@@ -10,7 +10,10 @@ steps while there is work, and completes finished requests. Endpoints:
   and ``engine/loadgen.py`` send); returns ``{"output_ids": [...],
   "meta_info": {"prompt_tokens", "completion_tokens", "e2e_latency",
   "ttft", "tpot"}}``. Decoding is greedy and runs ``max_new_tokens`` tokens.
-  An optional ``"rid"`` (any string) names the request for ``/abort``.
+  An optional ``"rid"`` (any string) names the request for ``/abort``;
+  ``"stream": true`` answers with server-sent events instead, one
+  ``data: {"index": i, "token": t}`` per generated token as the engine
+  produces it and a final ``data: {"done": true, "meta_info": {...}}``.
 * ``POST /abort`` -- ``{"rid": ...}``: cancel a queued or running request
   between steps (its pages are freed; its ``/generate`` call answers 499).
 * ``GET /health`` -- liveness plus queue depths.
@@ -27,6 +30,7 @@ from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
+import json
 import queue
 import threading
 import time
@@ -57,9 +61,12 @@ class EngineServer:
             self.metrics = None
 
     # ---------------------------------------------------------------- client side
-    def submit(self, input_ids, max_new_tokens: int, urgency: float = 0.0, name: str | None = None) -> cf.Future:
+    def submit(self, input_ids, max_new_tokens: int, urgency: float = 0.0, name: str | None = None,
+               stream: bool = False) -> cf.Future:
         """Queue one request; the future resolves to the response dict.
-        ``name``: a client id that ``cancel`` accepts."""
+        ``name``: a client id that ``cancel`` accepts. ``stream``: the
+        request's tokens are also put, as they are produced, on
+        ``future.tokens`` (a queue.Queue; None marks the end)."""
         from .request import Request
         ids = np.asarray(input_ids, dtype=np.int32)
         if ids.ndim != 1 or ids.size == 0:
@@ -75,6 +82,9 @@ class EngineServer:
         req = Request(rid=rid, prompt=ids, max_new_tokens=int(max_new_tokens), urgency=float(urgency))
         req._t_submit = time.perf_counter()  # host clock of the HTTP side
         req._name = None if name is None else str(name)
+        req._stream = queue.Queue() if stream else None
+        req._sent = 0
+        fut.tokens = req._stream
         self._inbox.put((req, fut))
         return fut
 
@@ -106,6 +116,8 @@ class EngineServer:
                 continue
             req, fut = item
             self.engine.abort(req)
+            if getattr(req, "_stream", None) is not None:
+                req._stream.put(None)
             if not fut.done():
                 fut.set_exception(cf.CancelledError(f"request {rid} aborted"))
 
@@ -127,9 +139,26 @@ class EngineServer:
                 continue
             self._pending[req.rid] = (req, fut)
 
+    def _push_tokens(self, plan) -> None:
+        """Stream the tokens a step produced (requests submitted with stream)."""
+        for r in list(plan.decode) + [r for r, _, _ in plan.prefill]:
+            q = getattr(r, "_stream", None)
+            if q is None:
+                continue
+            if len(r.output) < r._sent:  # preempted: its streamed tokens moved into the prompt
+                r._sent = 0
+            base = getattr(r, "_streamed_total", 0)
+            for t in r.output[r._sent:]:
+                q.put((base, int(t)))
+                base += 1
+            r._streamed_total = base
+            r._sent = len(r.output)
+
     def _complete(self, done) -> None:
         now = time.perf_counter()
         for r in done:
+            if getattr(r, "_stream", None) is not None:
+                r._stream.put(None)
             item = self._pending.pop(r.rid, None)
             if item is None:
                 continue
@@ -162,6 +191,7 @@ class EngineServer:
                     self.decode_tokens += len(plan.decode)
                     if self.metrics is not None:
                         self.metrics.on_step(self.engine, plan)
+                    self._push_tokens(plan)
                     self._complete(done)
                 else:
                     try:
@@ -193,7 +223,7 @@ class EngineServer:
         import asyncio
 
         from fastapi import FastAPI, HTTPException
-        from fastapi.responses import JSONResponse, Response
+        from fastapi.responses import JSONResponse, Response, StreamingResponse
 
         app = FastAPI(title="sched_pass_b200")
 
@@ -203,11 +233,25 @@ class EngineServer:
             sp = body.get("sampling_params") or {}
             if ids is None:
                 raise HTTPException(400, "input_ids is required (token ids; no tokenizer in this server)")
+            stream = bool(body.get("stream", False))
             try:
                 fut = self.submit(ids, int(sp.get("max_new_tokens", 16)), float(body.get("urgency", 0.0)),
-                                  name=body.get("rid"))
+                                  name=body.get("rid"), stream=stream)
             except ValueError as e:
                 raise HTTPException(400, str(e)) from e
+            if stream:
+                async def events():
+                    while True:
+                        item = await asyncio.to_thread(fut.tokens.get)
+                        if item is None:
+                            break
+                        yield f"data: {json.dumps({'index': item[0], 'token': item[1]})}\n\n"
+                    try:
+                        res = await asyncio.wrap_future(fut)
+                        yield f"data: {json.dumps({'done': True, 'meta_info': res['meta_info']})}\n\n"
+                    except Exception as e:  # noqa: BLE001 - aborted or failed mid-stream
+                        yield f"data: {json.dumps({'done': True, 'error': repr(e)})}\n\n"
+                return StreamingResponse(events(), media_type="text/event-stream")
             try:
                 return JSONResponse(await asyncio.wrap_future(fut))
             except (cf.CancelledError, asyncio.CancelledError) as e:
@@ -327,6 +371,7 @@ class TPEngineServer(EngineServer):
                     self.decode_tokens += len(plan.decode)
                     if self.metrics is not None:
                         self.metrics.on_step(self.engine, plan)
+                    self._push_tokens(plan)
                     self._complete(done)
         except BaseException as e:  # noqa: BLE001 - report to every waiter
             self.error = e

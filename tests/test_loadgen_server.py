@@ -247,3 +247,42 @@ def test_cancel_running_and_queued_requests():
             srv.cancel("nope")
     finally:
         srv.stop()
+
+
+def test_streaming_tokens_in_process_and_over_http():
+    """Tokens stream as the engine produces them: the in-process queue and
+    the server-sent events carry exactly the final output, in order."""
+    srv = EngineServer(FakeEngine()).start()
+    try:
+        f = srv.submit(list(range(30)), 6, stream=True)
+        got = []
+        while True:
+            item = f.tokens.get(timeout=10)
+            if item is None:
+                break
+            got.append(item)
+        out = f.result(timeout=10)["output_ids"]
+        assert [t for _, t in got] == out and [i for i, _ in got] == list(range(6))
+
+        import uvicorn
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        server = uvicorn.Server(uvicorn.Config(srv.app(), host="127.0.0.1", port=port, log_level="error"))
+        th = threading.Thread(target=server.run, daemon=True)
+        th.start()
+        for _ in range(200):
+            if server.started:
+                break
+            time.sleep(0.02)
+        import requests
+        r = requests.post(f"http://127.0.0.1:{port}/generate", json={"input_ids": [3, 4, 5], "stream": True,
+                                                                     "sampling_params": {"max_new_tokens": 4}},
+                          stream=True, timeout=10)
+        events = [json.loads(l[len("data: "):]) for l in r.iter_lines(decode_unicode=True) if l.startswith("data: ")]
+        assert [e["token"] for e in events[:-1]] == [6, 7, 8, 9]
+        assert events[-1]["done"] and events[-1]["meta_info"]["completion_tokens"] == 4
+        server.should_exit = True
+        th.join(10)
+    finally:
+        srv.stop()
