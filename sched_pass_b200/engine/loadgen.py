@@ -169,9 +169,11 @@ def run_inprocess(engine, work: list, max_steps: int | None = None) -> tuple[lis
     return res, engine.clock - clock0
 
 
-async def _post(session, url, w: WorkItem, sem, results, idx):
+async def _post(session, url, w: WorkItem, sem, results, idx, stream: bool = False):
     payload = {"input_ids": [int(t) for t in w.prompt],
                "sampling_params": {"max_new_tokens": w.max_new_tokens, "temperature": 0.0, "ignore_eos": True}}
+    if stream:
+        return await _post_stream(session, url, w, sem, results, idx, payload)
     async with sem:
         t0 = time.perf_counter()
         try:
@@ -186,7 +188,37 @@ async def _post(session, url, w: WorkItem, sem, results, idx):
                           n_in=len(w.prompt), n_out=len(body.get("output_ids", [])) if ok else 0)
 
 
-async def replay_http_async(base_url: str, work: list, concurrency: int = 32, realtime: bool = True) -> list:
+async def _post_stream(session, url, w: WorkItem, sem, results, idx, payload):
+    """Streaming request: TTFT and TPOT measured on the client's clock from
+    the arrival times of the server-sent token events (what a user sees),
+    instead of the server's own accounting."""
+    payload = dict(payload, stream=True)
+    times, n, ok = [], 0, False
+    async with sem:
+        t0 = time.perf_counter()
+        try:
+            async with session.post(url, json=payload) as r:
+                async for raw in r.content:
+                    line = raw.decode().strip()
+                    if not line.startswith("data: "):
+                        continue
+                    ev = json.loads(line[len("data: "):])
+                    if ev.get("done"):
+                        ok = r.status == 200 and "error" not in ev
+                        break
+                    times.append(time.perf_counter())
+                    n += 1
+        except Exception:  # noqa: BLE001 - a failed request is a result
+            ok = False
+        dt = time.perf_counter() - t0
+    ttft = times[0] - t0 if times else None
+    tpot = (times[-1] - times[0]) / (len(times) - 1) if len(times) > 1 else None
+    results[idx] = Result(ok=ok, latency=dt, ttft=ttft, tpot=tpot, n_in=len(w.prompt), n_out=n,
+                          extra={"client_clock": True})
+
+
+async def replay_http_async(base_url: str, work: list, concurrency: int = 32, realtime: bool = True,
+                            stream: bool = False) -> list:
     import asyncio
 
     import aiohttp
@@ -203,15 +235,18 @@ async def replay_http_async(base_url: str, work: list, concurrency: int = 32, re
                 due = work[i].arrival - (time.perf_counter() - t_start)
                 if due > 0:
                     await asyncio.sleep(due)
-            tasks.append(asyncio.create_task(_post(s, url, work[i], sem, results, i)))
+            tasks.append(asyncio.create_task(_post(s, url, work[i], sem, results, i, stream)))
         await asyncio.gather(*tasks)
     return results
 
 
-def replay_http(base_url: str, work: list, concurrency: int = 32, realtime: bool = True) -> tuple[list, float]:
+def replay_http(base_url: str, work: list, concurrency: int = 32, realtime: bool = True,
+                stream: bool = False) -> tuple[list, float]:
+    """Replay ``work`` against ``/generate``. ``stream``: request server-sent
+    token events and measure TTFT / TPOT on the client's clock."""
     import asyncio
     t0 = time.perf_counter()
-    res = asyncio.run(replay_http_async(base_url, work, concurrency, realtime))
+    res = asyncio.run(replay_http_async(base_url, work, concurrency, realtime, stream))
     return res, time.perf_counter() - t0
 
 
@@ -301,6 +336,7 @@ def main(argv=None) -> int:
     ap.add_argument("--speed", type=float, default=1.0, help="trace time compression (0: all at once)")
     ap.add_argument("--base-url", help="a /generate endpoint; without it the engine runs in-process")
     ap.add_argument("--concurrency", type=int, default=32)
+    ap.add_argument("--stream", action="store_true", help="stream tokens; TTFT/TPOT on the client's clock")
     ap.add_argument("--mix", default="trace", choices=["trace", "dispersed", "poisson"])
     ap.add_argument("--n", type=int, default=256)
     ap.add_argument("--rate", type=float, default=8.0)
@@ -324,7 +360,7 @@ def main(argv=None) -> int:
     else:
         work = poisson(a.n, a.rate, a.prompt, a.output, vocab)
     if a.base_url:
-        res, wall = replay_http(a.base_url, work, a.concurrency)
+        res, wall = replay_http(a.base_url, work, a.concurrency, stream=a.stream)
     else:
         import torch
 

@@ -101,6 +101,9 @@ def test_server_futures_and_http_replay():
         work = loadgen.dispersed(24, mu=3.5, sigma=0.5, lo=4, hi=64, out=3, vocab=1000, seed=2)
         res, wall = loadgen.replay_http(f"http://127.0.0.1:{port}", work, concurrency=8, realtime=False)
         assert all(r.ok and r.n_out == 3 for r in res)
+        sres, _ = loadgen.replay_http(f"http://127.0.0.1:{port}", work[:6], concurrency=4, realtime=False,
+                                      stream=True)
+        assert all(r.ok and r.n_out == 3 and r.ttft is not None and r.tpot is not None for r in sres)
         import requests
         st = requests.get(f"http://127.0.0.1:{port}/stats", timeout=5).json()
         assert st["steps"] > 0 and st["decode_tokens"] > 0
@@ -113,8 +116,8 @@ def test_server_futures_and_http_replay():
                 k, v = line.rsplit(" ", 1)
                 vals[k] = float(v)
         assert vals["sched_engine_steps_total"] == st["steps"] > 0
-        assert vals["sched_requests_finished_total"] == 26  # 2 submitted directly + 24 replayed
-        assert vals["sched_request_tpot_ms_count"] == 26 and vals["sched_requests_queued"] == 0
+        assert vals["sched_requests_finished_total"] == 32  # 2 submitted directly + 24 + 6 replayed
+        assert vals["sched_request_tpot_ms_count"] == 32 and vals["sched_requests_queued"] == 0
         assert vals["sched_engine_prefill_tokens_total"] > 0
         r = requests.post(f"http://127.0.0.1:{port}/generate", json={"sampling_params": {}}, timeout=5)
         assert r.status_code == 400
