@@ -57,6 +57,16 @@ class ServerMetrics:
                 return float(getattr(p.stats, name, 0))
             return read
 
+        def cache_value(name):
+            def read():
+                c = getattr(getattr(eng, "sched", None), "cache", None)
+                return float(getattr(c, name, 0)) if c is not None else 0.0
+            return read
+
+        Gauge("sched_prefix_cache_hit_tokens", "Prompt tokens served from cached KV pages",
+              registry=r).set_function(cache_value("hits"))
+        Gauge("sched_prefix_cache_lookup_tokens", "Prompt tokens looked up in the prefix cache",
+              registry=r).set_function(cache_value("lookups"))
         for name, doc in (("planned", "Steps whose task order was re-planned"),
                           ("probes", "Steps with the per-task timer armed"),
                           ("clc_armed", "Steps with cluster launch control armed"),

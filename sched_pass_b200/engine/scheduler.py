@@ -20,6 +20,7 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from .native import PageAllocator
+from .prefix_cache import PrefixCache
 from .request import Request, State
 
 
@@ -41,8 +42,11 @@ class StepPlan:
 class Scheduler:
     def __init__(self, num_pages: int, page_size: int = 16, max_batch: int = 256,
                  max_prefill_tokens: int = 4096, max_context: int = 8192, tier=None,
-                 max_step_tokens: int = 0, round_decode=None, max_prefill_segments: int = 0):
+                 max_step_tokens: int = 0, round_decode=None, max_prefill_segments: int = 0,
+                 prefix_cache: bool = False):
         self.alloc = PageAllocator(num_pages)
+        # automatic prefix caching: shared prompt prefixes reuse KV pages (engine/prefix_cache.py)
+        self.cache = PrefixCache(page_size) if prefix_cache else None
         self.tier = tier  # optional TieredKV: spill to host before preempting
         self.page_size = page_size
         self.max_batch = max_batch
@@ -82,6 +86,20 @@ class Scheduler:
     def idle(self) -> bool:
         return not self.waiting and not self.running
 
+    @property
+    def free_pages(self) -> int:
+        """Pages a request can get: free ones plus cached ones nobody holds."""
+        return self.alloc.free + (self.cache.evictable if self.cache is not None else 0)
+
+    def _take(self, n: int):
+        got = self.alloc.take(n)
+        if got is None and self.cache is not None and self.cache.evictable:
+            evicted = self.cache.evict(n - self.alloc.free)
+            if evicted:
+                self.alloc.give(np.asarray(evicted, dtype=np.int32))
+            got = self.alloc.take(n)
+        return got
+
     def _pages_needed(self, req: Request, upto: int) -> int:
         return max(0, (upto + self.page_size - 1) // self.page_size - len(req.pages))
 
@@ -89,7 +107,7 @@ class Scheduler:
         n = self._pages_needed(req, upto)
         if n == 0:
             return True
-        got = self.alloc.take(n)
+        got = self._take(n)
         if got is None and self.tier is not None:
             freed = self.tier.spill(n - self.alloc.free, self.running, protect=req)
             if freed:
@@ -101,6 +119,15 @@ class Scheduler:
         return True
 
     def release(self, req: Request) -> None:
+        if req.pages and self.cache is not None:
+            # cached pages drop this request's reference; private ones go back below
+            private = []
+            for p in req.pages:
+                if self.cache.holds(p):
+                    self.cache.release(p)
+                else:
+                    private.append(p)
+            req.pages = private
         if req.pages:
             pages = np.asarray(req.pages, dtype=np.int64)
             if self.tier is not None:
@@ -170,17 +197,29 @@ class Scheduler:
                     budget -= n
         while budget > 0 and self.waiting and len(self.running) < self.max_batch and len(plan.prefill) < seg_cap:
             req = self.waiting[0]
-            n = min(budget, req.prompt_len)
+            hit_pages, keys = self.cache.peek(req.prompt) if self.cache is not None else ([], [])
+            if hit_pages:
+                self.cache.acquire(hit_pages)  # before growing: growing may evict idle cached pages
+            req.pages = list(hit_pages)
+            hit = len(hit_pages) * self.page_size
+            n = min(budget, req.prompt_len - hit)
             # keep room for the decode pages of everything already running
             reserve = len(plan.decode)
-            if self._pages_needed(req, n) + reserve > self.alloc.free:
+            if self._pages_needed(req, hit + n) + reserve > self.free_pages or not self._grow(req, hit + n):
+                if hit_pages:
+                    for p in hit_pages:
+                        self.cache.release(p)
+                req.pages = []
                 break
-            if not self._grow(req, n):
-                break
+            if self.cache is not None:
+                self.cache.lookups += req.prompt_len
+                self.cache.hits += hit
+            req._keys, req._registered = keys, len(hit_pages)
+            req.cached = hit
             self.waiting.popleft()
             req.state = State.PREFILL
             self.running.append(req)
-            plan.prefill.append((req, 0, n))
+            plan.prefill.append((req, hit, n))
             budget -= n
         return plan
 
@@ -199,6 +238,13 @@ class Scheduler:
         done = []
         for req, start, n in plan.prefill:
             req.cached = start + n
+            if self.cache is not None:
+                # prompt blocks whose K/V this step wrote become shareable
+                keys = getattr(req, "_keys", [])
+                full = min(req.cached // self.page_size, len(keys))
+                for b in range(getattr(req, "_registered", 0), full):
+                    self.cache.register(keys[b], req.pages[b])
+                req._registered = max(getattr(req, "_registered", 0), full)
             if req.cached >= req.prompt_len:
                 req.state = State.DECODE
         for req in plan.decode:

@@ -433,6 +433,7 @@ def main(argv=None) -> int:
     ap.add_argument("--max-context", type=int, default=4096)
     ap.add_argument("--acquire", default="auto")
     ap.add_argument("--tp-mode", default=None, choices=[None, "fused", "sp", "nccl"])
+    ap.add_argument("--prefix-cache", action="store_true", help="share KV pages of common prompt prefixes")
     a = ap.parse_args(argv)
     import torch
 
@@ -444,7 +445,8 @@ def main(argv=None) -> int:
     torch.cuda.set_device(dev)
     tp = TensorParallel(mode=a.tp_mode, device=dev) if world > 1 else None
     eng = Engine(get_config(a.model), EngineConfig(max_batch=a.max_batch, max_context=a.max_context,
-                                                   acquire=a.acquire, verbose=rank == 0), dev, tp=tp)
+                                                   acquire=a.acquire, verbose=rank == 0,
+                                                   prefix_cache=a.prefix_cache), dev, tp=tp)
     if world == 1:
         EngineServer(eng).serve(a.host, a.port)
         return 0
