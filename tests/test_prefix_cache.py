@@ -105,3 +105,39 @@ def test_cache_refcounts():
     assert c.evictable == 0
     c.release(5)
     assert c.evictable == 1 and c.evict(3) == [5] and not c.holds(5)
+
+
+def test_trace_replay_prefix_reuse_becomes_cache_hits():
+    """Trace records that share hash ids share token blocks (loadgen), so the
+    scheduler serves the shared blocks of later requests from cached pages."""
+    from sched_pass_b200.engine import loadgen
+
+    class Fake:
+        def __init__(self):
+            self.sched = Scheduler(2048, 16, 8, 256, 4096, prefix_cache=True)
+            self.clock = 0.0
+
+        def add_request(self, r):
+            self.sched.add(r)
+
+        def has_work(self):
+            return not self.sched.idle
+
+        def step(self):
+            plan = self.sched.schedule()
+            sampled = {r.rid: 1 for r in plan.decode}
+            for r, start, n in plan.prefill:
+                if start + n >= r.prompt_len:
+                    sampled[r.rid] = 1
+            self.clock += 0.01
+            return plan, self.sched.commit(plan, sampled, self.clock)
+
+    # four conversations turns: each record extends the previous one's blocks
+    recs = [{"chat_id": i, "timestamp": float(i), "input_length": 16 * (4 + 3 * i) + 5, "output_length": 2,
+             "hash_ids": list(range(4 + 3 * i + 1))} for i in range(4)]
+    work = loadgen.from_trace(recs, vocab=1000)
+    eng = Fake()
+    res, _ = loadgen.run_inprocess(eng, work)
+    assert all(r.ok for r in res)
+    # request i reuses the full blocks of request i-1's prompt: 4, 7, 10 blocks
+    assert eng.sched.cache.hits == 16 * (4 + 7 + 10)
