@@ -434,6 +434,7 @@ def main(argv=None) -> int:
     ap.add_argument("--acquire", default="auto")
     ap.add_argument("--tp-mode", default=None, choices=[None, "fused", "sp", "nccl"])
     ap.add_argument("--prefix-cache", action="store_true", help="share KV pages of common prompt prefixes")
+    ap.add_argument("--config", help="YAML/JSON file with engine: and sched: sections (replaces the flags above)")
     a = ap.parse_args(argv)
     import torch
 
@@ -444,9 +445,15 @@ def main(argv=None) -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     tp = TensorParallel(mode=a.tp_mode, device=dev) if world > 1 else None
-    eng = Engine(get_config(a.model), EngineConfig(max_batch=a.max_batch, max_context=a.max_context,
-                                                   acquire=a.acquire, verbose=rank == 0,
-                                                   prefix_cache=a.prefix_cache), dev, tp=tp)
+    if a.config:
+        from .config_file import apply_sched_env, load_config
+        ecfg, scfg = load_config(a.config)
+        apply_sched_env(scfg)  # the plugin reads its knobs from SCHED_*
+        ecfg.verbose = ecfg.verbose and rank == 0
+    else:
+        ecfg = EngineConfig(max_batch=a.max_batch, max_context=a.max_context, acquire=a.acquire,
+                            verbose=rank == 0, prefix_cache=a.prefix_cache)
+    eng = Engine(get_config(a.model), ecfg, dev, tp=tp)
     if world == 1:
         EngineServer(eng).serve(a.host, a.port)
         return 0
