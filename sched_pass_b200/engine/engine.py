@@ -66,6 +66,7 @@ class EngineConfig:
     max_step_tokens: int = 0        # cap on decode + prefill tokens per step (0 = none; see Scheduler)
     prefill_order: str = "lpt"      # order of prefill attention tiles: "lpt" (longest first) | "identity"
     prefix_cache: bool = False      # share the KV pages of common prompt prefixes (not with tiered KV)
+    admission: str = "fcfs"         # waiting-queue order: fcfs | urgency | lpm (longest cached prefix)
     mixed_graphs: bool = True       # with max_step_tokens: pad mixed steps to a fixed shape per decode
                                     # bucket and replay them from CUDA graphs
     max_context: int = 4096
@@ -132,7 +133,8 @@ class Engine:
                                max_step_tokens=e.max_step_tokens,
                                round_decode=(lambda nd: self._bucket(nd) or nd) if capped else None,
                                max_prefill_segments=MIXED_SEGMENTS if capped else 0,
-                               prefix_cache=e.prefix_cache and self.tier is None)
+                               prefix_cache=e.prefix_cache and self.tier is None,
+                               admission=e.admission if (e.admission != "lpm" or e.prefix_cache) else "fcfs")
         self.hkv = cfg.n_kv_heads // tp_size
         self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.target_tasks = e.target_tasks or self.sms

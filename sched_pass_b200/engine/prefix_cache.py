@@ -55,13 +55,15 @@ class PrefixCache:
     def holds(self, page: int) -> bool:
         return page in self.key_of
 
-    def peek(self, tokens: np.ndarray) -> tuple[list, list]:
+    def peek(self, tokens: np.ndarray, keys: list | None = None) -> tuple[list, list]:
         """Longest cached prefix of ``tokens`` that leaves at least one token
         to compute (the last prompt token's logits give the first output):
         (its pages, the keys of every full block of ``tokens``). Nothing is
-        referenced yet (``acquire``)."""
+        referenced yet (``acquire``). ``keys``: the block keys of ``tokens``
+        if already known (they depend on the tokens only)."""
         n_full = (len(tokens) - 1) // self.page_size
-        keys = block_keys(tokens, self.page_size, len(tokens) // self.page_size)
+        if keys is None:
+            keys = block_keys(tokens, self.page_size, len(tokens) // self.page_size)
         pages = []
         for k in keys[:n_full]:
             p = self.page_of.get(k)

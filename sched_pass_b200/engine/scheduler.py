@@ -43,10 +43,16 @@ class Scheduler:
     def __init__(self, num_pages: int, page_size: int = 16, max_batch: int = 256,
                  max_prefill_tokens: int = 4096, max_context: int = 8192, tier=None,
                  max_step_tokens: int = 0, round_decode=None, max_prefill_segments: int = 0,
-                 prefix_cache: bool = False):
+                 prefix_cache: bool = False, admission: str = "fcfs"):
         self.alloc = PageAllocator(num_pages)
         # automatic prefix caching: shared prompt prefixes reuse KV pages (engine/prefix_cache.py)
         self.cache = PrefixCache(page_size) if prefix_cache else None
+        # order of admission from the waiting queue: "fcfs" (arrival), "urgency"
+        # (the plane's q, highest first) or "lpm" (longest cached prefix first,
+        # with the prefix cache); preempted requests always go first
+        if admission not in ("fcfs", "urgency", "lpm"):
+            raise ValueError(f"admission must be fcfs|urgency|lpm, not {admission!r}")
+        self.admission = admission
         self.tier = tier  # optional TieredKV: spill to host before preempting
         self.page_size = page_size
         self.max_batch = max_batch
@@ -195,9 +201,11 @@ class Scheduler:
                 if n > 0 and self._grow(req, req.cached + n):
                     plan.prefill.append((req, req.cached, n))
                     budget -= n
+        if self.admission != "fcfs" and len(self.waiting) > 1:
+            self._order_waiting()
         while budget > 0 and self.waiting and len(self.running) < self.max_batch and len(plan.prefill) < seg_cap:
             req = self.waiting[0]
-            hit_pages, keys = self.cache.peek(req.prompt) if self.cache is not None else ([], [])
+            hit_pages, keys = self.cache.peek(req.prompt, self._keys(req)) if self.cache is not None else ([], [])
             if hit_pages:
                 self.cache.acquire(hit_pages)  # before growing: growing may evict idle cached pages
             req.pages = list(hit_pages)
@@ -222,6 +230,28 @@ class Scheduler:
             plan.prefill.append((req, hit, n))
             budget -= n
         return plan
+
+    LPM_WINDOW = 64  # waiting requests whose cached prefix is measured per step
+
+    def _keys(self, req: Request) -> list:
+        """Block keys of a request's prompt, computed once per prompt (a
+        preempted request's prompt grows by its output, which renews them)."""
+        memo = getattr(req, "_key_memo", None)
+        if memo is None or memo[0] != req.prompt_len:
+            from .prefix_cache import block_keys
+            memo = (req.prompt_len, block_keys(req.prompt, self.page_size, req.prompt_len // self.page_size))
+            req._key_memo = memo
+        return memo[1]
+
+    def _order_waiting(self) -> None:
+        """Reorder the head of the waiting queue by the admission policy
+        (stable, so ties keep arrival order; deterministic across ranks)."""
+        head = [self.waiting.popleft() for _ in range(min(len(self.waiting), self.LPM_WINDOW))]
+        if self.admission == "urgency":
+            head.sort(key=lambda r: (r.preemptions == 0, -r.urgency))
+        elif self.cache is not None:  # lpm
+            head.sort(key=lambda r: (r.preemptions == 0, -len(self.cache.peek(r.prompt, self._keys(r))[0])))
+        self.waiting.extendleft(reversed(head))
 
     def prefill_budget(self, n_decode: int) -> int:
         """Prefill tokens a step with ``n_decode`` decode tokens may add: at

@@ -141,3 +141,30 @@ def test_trace_replay_prefix_reuse_becomes_cache_hits():
     assert all(r.ok for r in res)
     # request i reuses the full blocks of request i-1's prompt: 4, 7, 10 blocks
     assert eng.sched.cache.hits == 16 * (4 + 7 + 10)
+
+
+def test_admission_policies():
+    """urgency: the most urgent waiting request is admitted first; lpm: the
+    one with the longest cached prefix; fcfs keeps arrival order."""
+    rng = np.random.default_rng(1)
+    shared = rng.integers(0, 1000, size=96).astype(np.int32)
+
+    def run(policy):
+        s = Scheduler(num_pages=256, page_size=16, max_batch=2, max_prefill_tokens=128, max_context=4096,
+                      prefix_cache=True, admission=policy)
+        warm = Request(rid=0, prompt=np.concatenate([shared, [1]]).astype(np.int32), max_new_tokens=1)
+        s.add(warm)
+        for t in range(5):  # run the warm-up request to completion: its prefix is cached
+            step(s, float(t))
+        a = Request(rid=1, prompt=rng.integers(0, 1000, size=40).astype(np.int32), max_new_tokens=5, urgency=0.9)
+        b = Request(rid=2, prompt=np.concatenate([shared, [2, 3]]).astype(np.int32), max_new_tokens=5,
+                    urgency=0.1)
+        c = Request(rid=3, prompt=rng.integers(0, 1000, size=40).astype(np.int32), max_new_tokens=5, urgency=0.5)
+        for r in (c, b, a):
+            s.add(r)
+        plan, _ = step(s, 10.0)
+        return [r.rid for r, _, _ in plan.prefill]
+
+    assert run("fcfs")[0] == 3
+    assert run("urgency")[0] == 1
+    assert run("lpm")[0] == 2
