@@ -338,6 +338,7 @@ def main(argv=None) -> int:
     ap.add_argument("--concurrency", type=int, default=32)
     ap.add_argument("--stream", action="store_true", help="stream tokens; TTFT/TPOT on the client's clock")
     ap.add_argument("--prefix-cache", action="store_true", help="in-process engine: share prompt-prefix KV pages")
+    ap.add_argument("--admission", default="fcfs", choices=["fcfs", "urgency", "lpm"])
     ap.add_argument("--mix", default="trace", choices=["trace", "dispersed", "poisson"])
     ap.add_argument("--n", type=int, default=256)
     ap.add_argument("--rate", type=float, default=8.0)
@@ -368,7 +369,8 @@ def main(argv=None) -> int:
         from .engine import Engine, EngineConfig
         longest = max(len(w.prompt) + w.max_new_tokens for w in work)
         eng = Engine(cfg, EngineConfig(max_batch=128, max_context=(longest + 127) // 128 * 128,
-                                       prefix_cache=a.prefix_cache), torch.device("cuda"))
+                                       prefix_cache=a.prefix_cache, admission=a.admission),
+                     torch.device("cuda"))
         res, wall = run_inprocess(eng, work)
         if eng.sched.cache is not None:
             c = eng.sched.cache

@@ -434,6 +434,7 @@ def main(argv=None) -> int:
     ap.add_argument("--acquire", default="auto")
     ap.add_argument("--tp-mode", default=None, choices=[None, "fused", "sp", "nccl"])
     ap.add_argument("--prefix-cache", action="store_true", help="share KV pages of common prompt prefixes")
+    ap.add_argument("--admission", default="fcfs", choices=["fcfs", "urgency", "lpm"])
     ap.add_argument("--config", help="YAML/JSON file with engine: and sched: sections (replaces the flags above)")
     a = ap.parse_args(argv)
     import torch
@@ -452,7 +453,7 @@ def main(argv=None) -> int:
         ecfg.verbose = ecfg.verbose and rank == 0
     else:
         ecfg = EngineConfig(max_batch=a.max_batch, max_context=a.max_context, acquire=a.acquire,
-                            verbose=rank == 0, prefix_cache=a.prefix_cache)
+                            verbose=rank == 0, prefix_cache=a.prefix_cache, admission=a.admission)
     eng = Engine(get_config(a.model), ecfg, dev, tp=tp)
     if world == 1:
         EngineServer(eng).serve(a.host, a.port)
