@@ -235,3 +235,50 @@ def kernels_pair():
         src = open(os.path.join(HERE, "softmax_decode.ll")).read()
         _PAIR.extend([HostKernel(src), HostKernel(weave(src)[0])])
     return _PAIR
+
+
+def test_ticket_work_queue_driver_runs_every_task():
+    """The woven ticket work queue (sched-workqueue) executed on the host:
+    W < B persistent workers claim tasks from the queue word (primed to W, the
+    reference's host protocol) through the task order; every task runs
+    (each timer row fills), results equal the stock launch of one
+    CTA per task, and num_tasks = 0 takes the stock path. One thread per CTA
+    (G = 1): the host runs a CTA's threads one after another, so a
+    shared-memory broadcast between them cannot be emulated."""
+    src = open(os.path.join(HERE, "softmax_decode.ll")).read()
+    src = src.replace("@__sched_timer = ",
+                      "@__sched_queue = addrspace(1) externally_initialized global ptr null, align 8\n"
+                      "@__sched_timer = ")
+    stock = HostKernel(src)
+    woven, _ = weave(src, {"SCHED_WORKQUEUE": "1"})
+    k = HostKernel(woven)
+    lens, bt, kc, vc, q, _, maxp = build(9)
+    q1 = np.ascontiguousarray(q[:, :1])
+    p = ctypes.c_void_p
+    types = [p, p, p, p, p, p, p, ctypes.c_int32, ctypes.c_int32, ctypes.c_float]
+
+    def launch(kern, grid):
+        out = np.zeros((B, 1, D), np.float32)
+        acc = np.zeros((B, 1, D), np.float32)
+        kern.run("softmax_decode", (grid,), (1,),
+                 [q1.ctypes.data, kc.ctypes.data, vc.ctypes.data, bt.ctypes.data, lens.ctypes.data, out.ctypes.data,
+                  acc.ctypes.data, maxp, 1, np.log2(np.e) / np.sqrt(D)], types)
+        return out
+
+    base = launch(stock, B)
+    t = Tables()
+    t.order[:B] = np.arange(B - 1, -1, -1)
+    t.set_u32(abi.CTRL_ORDER_SIZE_OFF, B)
+    queue = np.zeros(4, np.uint32)
+    k.set_global_ptr("__sched_task_order", t.order.ctypes.data)
+    k.set_global_ptr("__sched_ctrl", t.ctrl.ctypes.data)
+    k.set_global_ptr("__sched_timer", t.timer.ctypes.data)
+    k.set_global_ptr("__sched_queue", queue.ctypes.data)
+    W = 3
+    t.set_u32(abi.CTRL_NUM_TASKS_OFF, B)
+    queue[0] = W
+    assert np.array_equal(launch(k, W), base)
+    assert (t.timer[:B] > 0).all() and (t.timer[B:] == 0).all() and queue[0] >= B
+    # num_tasks = 0: the stock path (one task per CTA), still exact
+    t.set_u32(abi.CTRL_NUM_TASKS_OFF, 0)
+    assert np.array_equal(launch(k, B), base)
