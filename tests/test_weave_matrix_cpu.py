@@ -1,7 +1,9 @@
 """Null slots stay bit-exact, for every fixture and every lever-knob
 combination: each woven variant verifies under LLVM and, executed on the
 host with no control tables installed, computes exactly what the stock
-kernel computes (the contract that a disarmed weave is inert)."""
+kernel computes (the contract that a disarmed weave is inert); armed with
+neutral tables it is still exact, and the timer fills its rows exactly when
+it is compiled in."""
 import ctypes
 import itertools
 import os
@@ -11,6 +13,7 @@ import pytest
 
 from sched_pass_b200.compiler.cpu_exec import HostKernel
 from sched_pass_b200.compiler.weave import weave
+from sched_pass_b200.runtime import abi
 
 HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "ir")
 KNOBS = ["SCHED_NO_INDIRECT", "SCHED_NO_SHED", "SCHED_NO_POLICY", "SCHED_NO_TIMER", "SCHED_PDL"]
@@ -78,4 +81,14 @@ def test_every_knob_combination_is_inert_when_disarmed(fixture):
         for combo in itertools.combinations(KNOBS, r):
             out, _ = weave(src, {k: "1" for k in combo})
             llvm.parse_assembly(out).verify()
-            assert np.array_equal(run(HostKernel(out)), base), (fixture, combo)
+            k = HostKernel(out)
+            assert np.array_equal(run(k), base), (fixture, combo)
+            # armed with neutral tables: identity order, tau 0, q 0, hint auto, timer on
+            order = np.arange(4096, dtype=np.int32)
+            ctrl = np.zeros(abi.ctrl_bytes(4096), np.uint8)
+            timer = np.zeros(4096, np.uint64)
+            k.set_global_ptr("__sched_task_order", order.ctypes.data)
+            k.set_global_ptr("__sched_ctrl", ctrl.ctypes.data)
+            k.set_global_ptr("__sched_timer", timer.ctypes.data)
+            assert np.array_equal(run(k), base), (fixture, combo, "neutral tables")
+            assert ("SCHED_NO_TIMER" in combo) == (not timer.any()), (fixture, combo)
