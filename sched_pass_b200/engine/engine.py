@@ -96,6 +96,24 @@ class StepStats:
     graph: bool
 
 
+def summarize_steps(stats: list) -> dict:
+    """Aggregate of engine steps: counts by kind, device time (total, mean,
+    p50/p99 of decode-only steps), the share of steps replayed from CUDA
+    graphs, and decode / prefill tokens."""
+    if not stats:
+        return {"steps": 0}
+    dec = sorted(s.device_ms for s in stats if s.n_prefill_tokens == 0)
+    pct = lambda v, q: float(v[min(len(v) - 1, max(0, int(math.ceil(q * len(v))) - 1))]) if v else None  # noqa: E731
+    total = sum(s.device_ms for s in stats)
+    return {"steps": len(stats), "decode_only_steps": len(dec),
+            "mixed_or_prefill_steps": len(stats) - len(dec),
+            "graph_share": round(sum(1 for s in stats if s.graph) / len(stats), 4),
+            "device_ms_total": round(total, 3), "device_ms_mean": round(total / len(stats), 4),
+            "decode_step_ms_p50": pct(dec, 0.5), "decode_step_ms_p99": pct(dec, 0.99),
+            "decode_tokens": sum(s.n_decode for s in stats),
+            "prefill_tokens": sum(s.n_prefill_tokens for s in stats)}
+
+
 class Engine:
     """Single-process engine for one tensor-parallel rank (``tp`` from
     ``parallel.tp``; None for one GPU). Every rank of a TP group runs the same

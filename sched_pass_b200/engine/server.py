@@ -275,6 +275,14 @@ class EngineServer:
         async def stats():
             out = {"steps": self.steps, "decode_tokens": self.decode_tokens, "queued": self._inbox.qsize(),
                    "running": len(self._pending)}
+            stats = getattr(self.engine, "stats", None)
+            if stats:
+                from .engine import summarize_steps
+                out["engine"] = summarize_steps(list(stats[-4096:]))
+            cache = getattr(getattr(self.engine, "sched", None), "cache", None)
+            if cache is not None:
+                out["prefix_cache"] = {"hit_tokens": cache.hits, "lookup_tokens": cache.lookups,
+                                       "cached_pages": len(cache.key_of), "evictable_pages": cache.evictable}
             plugin = getattr(self.engine, "plugin", None)
             if plugin is not None:
                 s = plugin.stats

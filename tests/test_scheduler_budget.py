@@ -63,3 +63,12 @@ def test_no_cap_keeps_whole_prompt_chunks():
     shapes, done = drive(s, make(5))
     assert len(done) == 5
     assert 1536 in [p for _, p in shapes]  # a whole prompt in one step
+
+
+def test_summarize_steps():
+    from sched_pass_b200.engine.engine import StepStats, summarize_steps
+    st = [StepStats(4, 0, 4.0, True), StepStats(4, 0, 5.0, True), StepStats(4, 1536, 30.0, False)]
+    s = summarize_steps(st)
+    assert s["steps"] == 3 and s["decode_only_steps"] == 2 and s["mixed_or_prefill_steps"] == 1
+    assert s["graph_share"] == round(2 / 3, 4) and s["decode_step_ms_p50"] == 4.0
+    assert s["decode_tokens"] == 12 and s["prefill_tokens"] == 1536 and summarize_steps([]) == {"steps": 0}
