@@ -285,3 +285,11 @@ def test_command_line_weave_and_manifest(tmp_path):
     m = subprocess.run([sys.executable, "-m", "sched_pass_b200", "manifest", "--csv"], capture_output=True,
                        text=True, cwd=root)
     assert m.returncode == 0 and m.stdout.splitlines()[0] == "name,effect,minSm,knob,disableKnob,order,tag"
+
+
+def test_doctor_reports_the_environment():
+    from sched_pass_b200.__main__ import doctor
+    rep = doctor()
+    for k in ("python", "torch", "gpus", "peer_access", "nccl", "nvcc", "native", "measured_peaks"):
+        assert k in rep
+    assert set(rep["native"]) == {"extension", "weaver", "host_runtime"}
