@@ -98,6 +98,17 @@ class EngineServer:
         self._aborts.put(rid)
 
     # ---------------------------------------------------------------- engine thread
+    @staticmethod
+    def _end_stream(req) -> None:
+        if getattr(req, "_stream", None) is not None:
+            req._stream.put(None)
+
+    def _fail(self, req, fut, exc) -> None:
+        """Fail one request: its stream ends and its future raises."""
+        self._end_stream(req)
+        if not fut.done():
+            fut.set_exception(exc)
+
     def _drain_aborts(self) -> list:
         rids = []
         while True:
@@ -116,10 +127,7 @@ class EngineServer:
                 continue
             req, fut = item
             self.engine.abort(req)
-            if getattr(req, "_stream", None) is not None:
-                req._stream.put(None)
-            if not fut.done():
-                fut.set_exception(cf.CancelledError(f"request {rid} aborted"))
+            self._fail(req, fut, cf.CancelledError(f"request {rid} aborted"))
 
     def _admit(self) -> None:
         while True:
@@ -129,13 +137,13 @@ class EngineServer:
                 return
             if req.rid in self._dropped:
                 self._dropped.discard(req.rid)
-                fut.set_exception(cf.CancelledError(f"request {req.rid} aborted"))
+                self._fail(req, fut, cf.CancelledError(f"request {req.rid} aborted"))
                 continue
             req.arrival = self.engine.clock
             try:
                 self.engine.add_request(req)
             except Exception as e:  # noqa: BLE001 - a bad request fails alone
-                fut.set_exception(e)
+                self._fail(req, fut, e)
                 continue
             self._pending[req.rid] = (req, fut)
 
@@ -201,9 +209,8 @@ class EngineServer:
                         pass
         except BaseException as e:  # noqa: BLE001 - report to every waiter
             self.error = e
-            for _, fut in list(self._pending.values()):
-                if not fut.done():
-                    fut.set_exception(e)
+            for req, fut in list(self._pending.values()):
+                self._fail(req, fut, e)
             self._pending.clear()
 
     def start(self) -> "EngineServer":
@@ -335,13 +342,13 @@ class TPEngineServer(EngineServer):
                 break
             if req.rid in self._dropped:
                 self._dropped.discard(req.rid)
-                fut.set_exception(cf.CancelledError(f"request {req.rid} aborted"))
+                self._fail(req, fut, cf.CancelledError(f"request {req.rid} aborted"))
                 continue
             req.arrival = self.engine.clock
             try:
                 self.engine.add_request(req)
             except Exception as e:  # noqa: BLE001 - a bad request fails alone, on rank 0 only
-                fut.set_exception(e)
+                self._fail(req, fut, e)
                 continue
             self._pending[req.rid] = (req, fut)
             sent.append((req.rid, [int(t) for t in req.prompt], req.max_new_tokens, req.urgency))
@@ -383,9 +390,8 @@ class TPEngineServer(EngineServer):
                     self._complete(done)
         except BaseException as e:  # noqa: BLE001 - report to every waiter
             self.error = e
-            for _, fut in list(self._pending.values()):
-                if not fut.done():
-                    fut.set_exception(e)
+            for req, fut in list(self._pending.values()):
+                self._fail(req, fut, e)
             self._pending.clear()
 
 

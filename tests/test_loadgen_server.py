@@ -266,6 +266,9 @@ def test_streaming_tokens_in_process_and_over_http():
             got.append(item)
         out = f.result(timeout=10)["output_ids"]
         assert [t for _, t in got] == out and [i for i, _ in got] == list(range(6))
+        # a streamed request the engine refuses ends its stream too (no client waits for ever)
+        bad = srv.submit(list(range(5000)), 2, stream=True)
+        assert bad.tokens.get(timeout=10) is None and bad.exception(timeout=10) is not None
 
         import uvicorn
         with socket.socket() as s:
