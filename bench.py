@@ -5,28 +5,39 @@ Workload (the named config): synthetic requests with Poisson arrivals at
 8 req/s, 1536 random prompt tokens, 128 output tokens, continuous batching,
 all scheduling levers armed every step. Random-initialised bf16 weights.
 
-The engine is driven on a workload clock: every engine step advances it by
-the step's measured duration, and arrivals up to the clock are admitted
-(when nothing is running the clock jumps to the next arrival). W warm-up
-steps run first, then K steps are timed between two barriers +
-synchronisations with CUDA events on the engine's stream (max over ranks).
+Steady-state window. The engine's own scheduler is first driven through the
+workload without the model on a nominal step clock
+(``benchmarks/steady_state.py``) to pick the most representative window of
+W + K steps after ``--horizon`` seconds of workload, and is then replayed to
+the window's start (the requests in flight hold synthetic KV). The W warm-up
+and K timed steps run the model; their admissions follow the same nominal
+clock, so every GPU count serves exactly the same requests, batch sizes and
+prefill chunks (a fixed load: strong scaling). Arrivals inside the window are
+prefilled inside the timed region. Decode-step CUDA graphs for the window's
+batch sizes and one prefill-sized eager step run before timing.
+
+The K steps are timed between two barriers + synchronisations with CUDA
+events on the engine's stream (max over ranks); an event at every step start
+gives each step's duration (max over ranks), from which every request's
+inter-token intervals inside the window are formed.
 
 Reported:
-  value       decode tokens / s of the timed steps (device time)
-  e2e.value   the same through the public step API measured with the host
-              clock, which includes each step's pinned H2D input copy and the
-              D2H read of the sampled tokens (the engine is synchronous per
-              step, so it tracks value; forward_only_tok_s and host_gap_share
-              split the step into forward passes and the host work between)
-  p99/p50 TPOT over requests that finished inside the timed window
-The inputs of every step exceed L2 (16 GB of weights stream each step), so no
-flush is needed between steps.
+  value        decode tokens / s of the timed steps (device time)
+  p50/p99 TPOT per-request mean inter-token interval inside the window
+               (every request that produced two tokens in it), and the p50 /
+               p99 of all inter-token intervals
+  e2e.value    the same tokens over the host clock of the same loop, which
+               includes each step's pinned H2D input copy and the D2H read of
+               the sampled tokens through ``Engine.step`` (the public API)
+  gpu_launches kernel launches of this framework's extension in the timed
+               steps (counted at the launchers; a replayed graph adds the
+               launches it captured)
+Weights (16 GB at TP=1) stream from HBM every step, more than L2 holds, so
+no flush is needed between steps.
 
-``--impl reference`` runs the reference project (jc-su/sched-pass) through
-its own public API when it is installed under baseline/_ref. The reference
-has no package metadata and its serving path needs clang+LLVM (its pass
-plugin) and SGLang, none of which this image has, so that arm prints an
-``unavailable`` line with the reason.
+``--impl reference`` would run the reference project (jc-su/sched-pass)
+through its own public API; it cannot be installed or run here (see
+``reference_arm``), so that arm prints an ``unavailable`` line.
 """
 from __future__ import annotations
 
@@ -46,11 +57,11 @@ BASELINE_VALUE = None  # the reference publishes no number for this metric/confi
 METRIC = "decode tokens/sec/box and p99 TPOT at 1/2/4/8 B200 vs reference NCCL build"
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1500)
-    ap.add_argument("--warmup", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="llama-3-8b")
     ap.add_argument("--rate", type=float, default=8.0)
@@ -58,35 +69,84 @@ def parse():
     ap.add_argument("--output", type=int, default=128)
     ap.add_argument("--requests", type=int, default=2000)
     ap.add_argument("--max-batch", type=int, default=128)
+    ap.add_argument("--horizon", type=float, default=30.0,
+                    help="workload seconds before the earliest window start (start-up transient)")
+    ap.add_argument("--search", type=float, default=60.0,
+                    help="workload seconds after the horizon in which the window is chosen")
+    ap.add_argument("--nominal-step-ms", type=float, default=None,
+                    help="nominal decode step of the admission clock (default: the 1-GPU figure)")
+    ap.add_argument("--nominal-prefill-us", type=float, default=None,
+                    help="nominal time per prefill token of the admission clock")
     ap.add_argument("--step-tokens", type=int, default=0,
                     help="cap on decode + prefill tokens per engine step (0: prefill chunks up to 2048)")
     ap.add_argument("--acquire", default="auto", choices=["static", "ticket", "clc", "auto"])
     ap.add_argument("--tp-mode", default=None, choices=[None, "fused", "nccl", "sp"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 def reference_arm(args):
-    why = None
+    """The reference's serving path is SGLang + FlashInfer with its LLVM pass
+    plugin woven in by clang (jc-su/sched-pass SGLANG.md, scripts/bench_ab.sh).
+    pip cannot install it (no setup.py or pyproject.toml), and this image has
+    neither SGLang nor clang/LLVM development files, so nothing of its stock
+    code path can run: print the unavailable line."""
     ref = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(ref) or not os.listdir(ref):
-        why = ("reference not installable offline: jc-su/sched-pass has no Python package metadata "
-               "and needs clang+LLVM (pass plugin) and SGLang, none of which exist in this image")
-    else:
+    missing = [m for m in ("sglang",) if not _importable(m)]
+    why = ("reference not installable offline: jc-su/sched-pass has no setup.py/pyproject.toml "
+           "(pip: 'not installable'), and its serving path needs clang+LLVM for the pass plugin and "
+           f"SGLang ({', '.join(missing) or 'present'} missing in this image)")
+    if os.path.isdir(ref) and os.listdir(ref):
         why = "reference install present but its serving path needs clang+LLVM and SGLang (absent)"
     print(json.dumps({"impl": "reference", "unavailable": why}))
     return 0
 
 
-def main():
-    args = parse()
+def _importable(name: str) -> bool:
+    import importlib.util
+    return importlib.util.find_spec(name) is not None
+
+
+def pct(v, p):
+    """Nearest-rank percentile of an ascending list (None if empty)."""
+    if not v:
+        return None
+    return float(v[min(len(v) - 1, max(0, int(math.ceil(p / 100.0 * len(v))) - 1))])
+
+
+def window_tpot(produced: list, step_s: list) -> dict:
+    """Inter-token statistics of a window. ``produced[i]`` lists the request
+    ids that produced a token at timed step i (index -1: the step before the
+    window); ``step_s[i]`` is step i's duration. An interval counts when both
+    of its tokens came from steps >= -1, so it lies wholly in the window."""
+    start = np.concatenate([[0.0], np.cumsum(step_s)])  # time at which step i ends = start[i + 1]
+    last = {rid: -1 for rid in produced[0]}
+    itl, per_req = [], {}
+    for i, rids in enumerate(produced[1:]):
+        t = start[i + 1]
+        for rid in rids:
+            j = last.get(rid)
+            if j is not None:
+                dt = t - (start[j + 1] if j >= 0 else 0.0)
+                itl.append(dt)
+                per_req.setdefault(rid, []).append(dt)
+            last[rid] = i
+    tpot = sorted(float(np.mean(v)) for v in per_req.values())
+    itl.sort()
+    return {"tpot": tpot, "itl": itl, "requests": len(per_req)}
+
+
+def main(argv=None):
+    args = parse(argv)
     if args.impl == "reference":
         return reference_arm(args)
 
     import torch
     import torch.distributed as dist
 
+    from sched_pass_b200 import _ext
+    from sched_pass_b200.benchmarks import steady_state as ss
     from sched_pass_b200.engine.engine import Engine, EngineConfig
     from sched_pass_b200.engine.request import Request
     from sched_pass_b200.models.config import get_config
@@ -102,85 +162,107 @@ def main():
     max_ctx = args.prompt + args.output + 16
     ecfg = EngineConfig(max_batch=args.max_batch, max_prefill_tokens=2048, max_step_tokens=args.step_tokens,
                         max_context=(max_ctx + 127) // 128 * 128, cuda_graphs=not args.no_graphs,
-                        levers=True, acquire=args.acquire, seed=args.seed)
+                        levers=True, acquire=args.acquire, seed=args.seed, clock_sync=False)
     eng = Engine(cfg, ecfg, dev, tp=tp)
 
-    # workload: same on every rank (same seed)
+    # workload: the same on every rank (same seed)
     rng = np.random.default_rng(args.seed)
-    gaps = rng.exponential(1.0 / args.rate, size=args.requests)
-    arrivals = np.cumsum(gaps)
+    arrivals = np.cumsum(rng.exponential(1.0 / args.rate, size=args.requests))
     prompts = rng.integers(0, cfg.vocab, size=(args.requests, args.prompt), dtype=np.int64).astype(np.int32)
     reqs = [Request(rid=i, prompt=prompts[i], max_new_tokens=args.output, arrival=float(arrivals[i]),
                     urgency=float(rng.random())) for i in range(args.requests)]
-    nxt = 0
+    step_s = (args.nominal_step_ms or ss.NOMINAL_DECODE_STEP_S * 1e3) / 1e3
+    tok_s = (args.nominal_prefill_us or ss.NOMINAL_PREFILL_TOKEN_S * 1e6) / 1e6
+    cost = lambda nd, npf: ss.nominal_cost(nd, npf, step_s, tok_s)  # noqa: E731
 
-    def admit():
-        nonlocal nxt
-        while nxt < len(reqs) and reqs[nxt].arrival <= eng.clock:
-            eng.add_request(reqs[nxt])
-            nxt += 1
-        if not eng.has_work() and nxt < len(reqs):
-            eng.clock = max(eng.clock, reqs[nxt].arrival)
-            admit()
+    # 1. the window: simulate the scheduler, pick the most representative start
+    trace = ss.simulate(eng.new_scheduler, reqs, cfg.vocab, args.horizon + args.search, cost)
+    s0, window = ss.pick_window(trace, args.steps, args.warmup, args.horizon)
+
+    # 2. kernels warm before any timing: one prefill-sized eager step (two
+    # dummy prompts filling the 2048-token budget), aborted afterwards, and
+    # the decode graphs of every batch size the warm-up and timed steps see
+    dummies = [Request(rid=-1 - i, prompt=prompts[i][:n].copy(), max_new_tokens=2)
+               for i, n in enumerate((args.prompt, max(16, ecfg.max_prefill_tokens - args.prompt)))]
+    for d in dummies:
+        eng.add_request(d)
+    eng.step()
+    for d in dummies:
+        eng.abort(d)
+    eng.warm_decode_graphs(trace.n_decode[s0:s0 + args.warmup + args.steps].tolist())
+    eng.fill_kv_random(args.seed)
+
+    # 3. replay the scheduler to the window's start, then the warm-up steps
+    drv = ss.replay(eng.sched, reqs, cfg.vocab, s0, cost)
+    eng.clock = drv.clock
+    last_producers = []
 
     def one_step():
-        admit()
+        drv.admit(eng.add_request)
         if not eng.has_work():
             return None
-        return eng.step()
+        plan, done = eng.step()
+        drv.advance(plan)
+        return plan, done
 
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    parts = vis.split(",") if vis else []
+    phys = int(parts[local]) if len(parts) > local and parts[local].isdigit() else local
+    sampler = ClockSampler(gpu_index=phys, period_ms=20).start()  # running before the window starts
     for _ in range(args.warmup):
-        if one_step() is None:
+        r = one_step()
+        if r is None:
             break
-    # timed region
+        last_producers = [q.rid for q in ss.producers(r[0])]
+
+    # 4. timed region
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    phys = vis.split(",")[local] if vis and len(vis.split(",")) > local and vis.split(",")[local].isdigit() else local
-    sampler = ClockSampler(gpu_index=int(phys)).start()
-    first_step = len(eng.stats)
-    clock0 = eng.clock
-    tok0 = sum(s.n_decode for s in eng.stats)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    t_host0 = time.perf_counter()
-    ev0.record(stream)
-    steps = 0
+    first_stat = len(eng.stats)
+    launches0 = _ext.launches() + eng.graph_launches
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    produced = [last_producers]
+    decode_tokens = prefill_tokens = 0
     finished = []
-    decode_tokens = 0
-    for _ in range(args.steps):
+    d2h = 0
+    wall0 = time.time()
+    t_host0 = time.perf_counter()
+    steps = 0
+    for i in range(args.steps):
+        events[i].record(stream)
         r = one_step()
         if r is None:
             break
         plan, done = r
         decode_tokens += len(plan.decode)
+        prefill_tokens += sum(n for _, _, n in plan.prefill)
+        produced.append([q.rid for q in ss.producers(plan)])
+        d2h += 4 * len(produced[-1])
         finished.extend(done)
         steps += 1
-    ev1.record(stream)
+    events[steps].record(stream)
     torch.cuda.synchronize(dev)
     t_host1 = time.perf_counter()
+    wall1 = time.time()
+    launches = _ext.launches() + eng.graph_launches - launches0
     if world > 1:
         dist.barrier()
-    clocks = sampler.stop()
-    dev_s = ev0.elapsed_time(ev1) / 1e3
+    clocks = sampler.stop(window=(wall0, wall1))
+    per_step = [events[i].elapsed_time(events[i + 1]) / 1e3 for i in range(steps)]
+    dev_s = events[0].elapsed_time(events[steps]) / 1e3
     host_s = t_host1 - t_host0
     if world > 1:
-        t = torch.tensor([dev_s, host_s], device=dev)
+        t = torch.tensor([dev_s, host_s] + per_step, dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dev_s, host_s = float(t[0]), float(t[1])
-    tpots = sorted(x for x in (r.tpot() for r in finished) if x is not None)
-
-    def pct(v, p):
-        if not v:
-            return None
-        return float(v[min(len(v) - 1, int(math.ceil(p / 100.0 * len(v))) - 1)])
-
-    step_ms = [s.device_ms for s in eng.stats[first_step:]]
+        dev_s, host_s, per_step = float(t[0]), float(t[1]), t[2:].tolist()
+    w = window_tpot(produced, per_step)
+    fin_tpot = sorted(x for x in (q.tpot() for q in finished) if x is not None)
+    step_ms = [st.device_ms for st in eng.stats[first_stat:]]
     value = decode_tokens / dev_s if dev_s > 0 else 0.0
     e2e = decode_tokens / host_s if host_s > 0 else 0.0
-    bytes_in = eng.packed_len * 4
+    ms = lambda v: round(1e3 * v, 3) if v is not None else None  # noqa: E731
     out = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -193,7 +275,8 @@ def main():
         "scaling": "strong",
         "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
         "dtype": "bf16",
-        "data": "synthetic (random prompts, random-init weights)",
+        "data": "synthetic (random prompts, random-init weights; in-flight requests at the window start hold "
+                "random KV)",
         "config": {
             "model": cfg.name + "-arch", "global_batch": f"continuous (max {args.max_batch})",
             "seq_len": args.prompt + args.output, "prompt_tokens": args.prompt,
@@ -202,35 +285,36 @@ def main():
             "tp_collective": (tp.mode if tp is not None else "none"),
             "levers": "pi+timer(1/8)+policy armed; acquire=" + args.acquire,
             "step_tokens": args.step_tokens or None,
-            "l2": "inputs larger than L2 (weights stream every step)",
-            "workload_clock_s": round(eng.clock - clock0, 3),
+            "l2": "inputs larger than L2 (16 GB of weights / N stream every step)",
+            "window": dict(window, nominal_step_ms=round(step_s * 1e3, 3), nominal_prefill_us=round(tok_s * 1e6, 3),
+                           workload_clock_s=round(drv.clock - window["t0_s"], 4)),
+            "window_reproduced": (decode_tokens == window["window_decode_tokens"]
+                                  and prefill_tokens == window["window_prefill_tokens"]),
+            "mean_batch": round(decode_tokens / max(steps, 1), 3),
+            "prefill_token_share": round(prefill_tokens / max(decode_tokens + prefill_tokens, 1), 4),
         },
-        "p99_tpot_ms": round(1e3 * pct(tpots, 99), 3) if tpots else None,
-        "p50_tpot_ms": round(1e3 * pct(tpots, 50), 3) if tpots else None,
+        "p99_tpot_ms": ms(pct(w["tpot"], 99)),
+        "p50_tpot_ms": ms(pct(w["tpot"], 50)),
+        "p99_itl_ms": ms(pct(w["itl"], 99)),
+        "p50_itl_ms": ms(pct(w["itl"], 50)),
+        "tpot_requests": w["requests"],
         "finished_in_window": len(finished),
+        "finished_p99_tpot_ms": ms(pct(fin_tpot, 99)),
         "step_ms_p50": round(float(np.median(step_ms)), 3) if step_ms else None,
         "step_ms_p99": round(pct(sorted(step_ms), 99), 3) if step_ms else None,
-        # the engine is synchronous per step (it reads the sampled tokens back),
-        # so the device timeline spans the host's planning and copies too and
-        # e2e matches value; these two fields split that time: forward passes
-        # alone (sum of per-step device times) vs everything between them
+        # forward passes alone (per-step device times between the engine's
+        # own events) against the whole window: the rest is host work between
+        # forwards that the device waits for
         "forward_only_tok_s": (round(decode_tokens / (sum(step_ms) / 1e3), 2)
                                if step_ms and sum(step_ms) > 0 else None),
         "host_gap_share": (round(max(0.0, 1.0 - (sum(step_ms) / 1e3) / dev_s), 4)
                            if step_ms and dev_s > 0 else None),
-        "e2e": {"value": round(e2e, 2), "unit": "decode tokens/s", "h2d_bytes_per_step": bytes_in,
-                "d2h_bytes_per_step": 4 * 2 * args.max_batch},
-        "gpu_launches": None,
+        "e2e": {"value": round(e2e, 2), "unit": "decode tokens/s", "h2d_bytes_per_step": eng.packed_len * 4,
+                "d2h_bytes_per_step": round(d2h / max(steps, 1), 1)},
+        "gpu_launches": int(launches),
         "clocks": clocks,
         "impl": "ours",
     }
-    # launches of our kernels in the timed region: per decode step, per layer
-    # (norm, qkv gemm, rope/kv, attention (+merge), o gemm, norm, gate_up gemm,
-    # down gemm) plus embedding, final norm, lm_head gemm, argmax
-    per_layer = 8 + (1 if any(eng.splits_for(s.n_decode) > 1 for s in eng.stats[first_step:]) else 0)
-    if world > 1:
-        per_layer += 0  # fused collectives replace the o/down GEMMs one for one
-    out["gpu_launches"] = int(steps * (cfg.n_layers * per_layer + 4))
     if rank == 0:
         print(json.dumps(out))
     if world > 1:

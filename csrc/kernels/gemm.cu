@@ -1148,6 +1148,44 @@ extern "C" long long sched_gemm_ws_floats(int T, int N, int K, int grid) {
   return (long long)p.grid * 2 * tn * gemm::BM;
 }
 
+namespace gemm {
+
+// The schedule of a call: the stream-K plan for an explicit grid; for a
+// default-grid call (grid <= 0), cluster split-K where it fits the shape and
+// otherwise the stream-K plan. p.cs = 0 means stream-K.
+static void final_plan(const GemmArgs &a, Params &p, int &tn) {
+  plan(a, p, tn);
+  p.cs = 0;
+  if (a.grid > 0) return;
+  const int sms = a.num_sms > 0 ? a.num_sms : 148;
+  p.grid = std::max(1, sms);
+  p.units = (long long)p.tiles * p.kb;
+  if (a.epi == kEpiSwiGLU)
+    plan_cluster_for<kEpiSwiGLU>(tn, p, sms);
+  else if (a.epi == kEpiRopeKV)
+    plan_cluster_for<kEpiRopeKV>(tn, p, sms);
+  else if (a.epi == kEpiAllReduce)
+    plan_cluster_for<kEpiAllReduce>(tn, p, sms);
+  else if (a.epi == kEpiReduceScatter)
+    plan_cluster_for<kEpiReduceScatter>(tn, p, sms);
+  else
+    plan_cluster_for<kEpiStore>(tn, p, sms);
+  if (p.cs == 0) plan(a, p, tn);  // back to the stream-K grid
+}
+
+// Stream-K scratch a final plan needs: partial-slice floats and tile
+// counters (both 0 when no tile is split, e.g. under cluster split-K).
+static void scratch_need(const Params &p, int tn, long long &floats, int &counters) {
+  floats = 0;
+  counters = 0;
+  if (p.cs == 0 && splits_tiles(p)) {
+    floats = (long long)p.grid * 2 * tn * BM;
+    counters = p.tiles;
+  }
+}
+
+}  // namespace gemm
+
 // The schedule sched_gemm_run would use for a default-grid call of this
 // shape: writes the cluster size (0 = stream-K) and the grid.
 extern "C" void sched_gemm_plan(int T, int N, int K, int epi, int num_sms, int *cs, int *grid) {
@@ -1159,23 +1197,7 @@ extern "C" void sched_gemm_plan(int T, int N, int K, int epi, int num_sms, int *
   a.num_sms = num_sms;
   gemm::Params p;
   int tn;
-  gemm::plan(a, p, tn);
-  p.cs = 0;
-  {
-    p.grid = num_sms;
-    p.units = (long long)p.tiles * p.kb;
-    if (epi == kEpiSwiGLU)
-      gemm::plan_cluster_for<kEpiSwiGLU>(tn, p, num_sms);
-    else if (epi == kEpiRopeKV)
-      gemm::plan_cluster_for<kEpiRopeKV>(tn, p, num_sms);
-    else if (epi == kEpiAllReduce)
-      gemm::plan_cluster_for<kEpiAllReduce>(tn, p, num_sms);
-    else if (epi == kEpiReduceScatter)
-      gemm::plan_cluster_for<kEpiReduceScatter>(tn, p, num_sms);
-    else
-      gemm::plan_cluster_for<kEpiStore>(tn, p, num_sms);
-    if (p.cs == 0) gemm::plan(a, p, tn);
-  }
+  gemm::final_plan(a, p, tn);
   *cs = p.cs;
   *grid = p.grid;
 }
@@ -1187,30 +1209,13 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   gemm::Params p;
   int tn;
   p.a = a;
-  gemm::plan(a, p, tn);
-  p.cs = 0;
-  if (a.grid <= 0) {
-    // the default schedule: cluster split-K where it fits the shape
-    const int sms = a.num_sms > 0 ? a.num_sms : 148;
-    p.grid = std::max(1, sms);
-    p.units = (long long)p.tiles * p.kb;
-    if (a.epi == kEpiSwiGLU)
-      gemm::plan_cluster_for<kEpiSwiGLU>(tn, p, sms);
-    else if (a.epi == kEpiRopeKV)
-      gemm::plan_cluster_for<kEpiRopeKV>(tn, p, sms);
-    else if (a.epi == kEpiAllReduce)
-      gemm::plan_cluster_for<kEpiAllReduce>(tn, p, sms);
-    else if (a.epi == kEpiReduceScatter)
-      gemm::plan_cluster_for<kEpiReduceScatter>(tn, p, sms);
-    else
-      gemm::plan_cluster_for<kEpiStore>(tn, p, sms);
-    if (p.cs == 0) gemm::plan(a, p, tn);  // back to the stream-K grid
-  }
-
-  if (p.cs == 0 && gemm::splits_tiles(p)) {
+  gemm::final_plan(a, p, tn);
+  long long need_floats;
+  int need_counters;
+  gemm::scratch_need(p, tn, need_floats, need_counters);
+  if (need_counters > 0) {
     if (a.ws == nullptr || a.counters == nullptr) return -2;
-    const long long need = (long long)p.grid * 2 * tn * gemm::BM;
-    if (need > a.ws_floats || p.tiles > a.counter_count) return -5;
+    if (need_floats > a.ws_floats || need_counters > a.counter_count) return -5;
   }
   if (a.epi == kEpiRopeKV && (a.N / gemm::BM != a.Hq + 2 * a.Hkv || a.cos_sin == nullptr ||
                               a.pos == nullptr || a.slot == nullptr))
@@ -1285,13 +1290,15 @@ extern "C" int sched_gemm_run_fixed_scratch(const GemmArgs *args, cudaStream_t s
   GemmArgs a = *args;
   if (a.T <= 0) return 0;
   if (a.N % gemm::BM != 0 || a.K % gemm::BK != 0) return -1;
+  // the capacity check runs on the schedule sched_gemm_run will launch
+  // (cluster split-K for some default-grid calls, which needs no scratch)
   gemm::Params p;
   int tn;
-  gemm::plan(a, p, tn);
-  if (gemm::splits_tiles(p)) {
-    const long long need = (long long)p.grid * 2 * tn * gemm::BM;
-    if (need > kFixedScratchWsFloats || p.tiles > kFixedScratchCounters) return kFixedScratchTooLarge;
-  }
+  gemm::final_plan(a, p, tn);
+  long long need_floats;
+  int need_counters;
+  gemm::scratch_need(p, tn, need_floats, need_counters);
+  if (need_floats > kFixedScratchWsFloats || need_counters > kFixedScratchCounters) return kFixedScratchTooLarge;
   gemm::FixedScratch s;
   if (!gemm::fixed_scratch(s)) return kFixedScratchLookupFailed;
   a.ws = s.ws;
@@ -1299,4 +1306,11 @@ extern "C" int sched_gemm_run_fixed_scratch(const GemmArgs *args, cudaStream_t s
   a.counters = s.counters;
   a.counter_count = kFixedScratchCounters;
   return sched_gemm_run(&a, stream);
+}
+
+extern "C" int sched_gemm_fixed_scratch_reset(cudaStream_t stream) {
+  gemm::FixedScratch s;
+  if (!gemm::fixed_scratch(s)) return kFixedScratchLookupFailed;
+  // a memset node: no allocation, ordered on the caller's stream
+  return cudaMemsetAsync(s.counters, 0, sizeof(uint32_t) * kFixedScratchCounters, stream) == cudaSuccess ? 0 : -4;
 }

@@ -104,9 +104,13 @@ extern "C" long long sched_gemm_ws_floats(int T, int N, int K, int grid);
 //   * The per-tile counters must be zero when a call starts. They start zero
 //     (static storage) and each call that completes with a zero status word
 //     leaves them zero again: the last CTA on a split tile resets its
-//     counter. A call that reports a non-zero status may leave them dirty,
-//     after which results of this entry point on that device are unreliable.
-//     The partial slices need no initial value.
+//     counter. A call that reports a non-zero status (a bounded wait that
+//     gave up) may leave them dirty: call sched_gemm_fixed_scratch_reset on
+//     the stream before the next call on that device. The partial slices
+//     need no initial value.
+//   * The capacity check runs on the schedule the call will launch: a
+//     default-grid call (grid <= 0) that runs cluster split-K uses no
+//     scratch and is never refused for size.
 //   * The scratch is one per device and shared by all calls on it: calls
 //     that can overlap in time (different streams, or host threads on
 //     unsynchronised streams) race on it and corrupt each other. Calls in
@@ -127,3 +131,7 @@ enum FixedScratchError : int {
   kFixedScratchBadEpilogue = -10,  // kEpiAllReduce, kEpiReduceScatter or a null args pointer
 };
 extern "C" int sched_gemm_run_fixed_scratch(const GemmArgs *args, cudaStream_t stream);
+// Zeroes the fixed scratch's tile counters on the current device with one
+// cudaMemsetAsync on `stream` (no allocation). Returns 0, or
+// kFixedScratchLookupFailed / -4 (the memset was refused).
+extern "C" int sched_gemm_fixed_scratch_reset(cudaStream_t stream);

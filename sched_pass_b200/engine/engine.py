@@ -29,7 +29,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
-from .. import ops
+from .. import _ext, ops
 from ..models.config import ModelConfig
 from ..models.llama import ForwardBatch, KVCache, Llama, init_weights
 from ..runtime.controller import SchedControlPlane
@@ -86,6 +86,9 @@ class EngineConfig:
     host_kv_pages: int = 0          # tiered KV: pinned host pages the device pool spills to (0 = off)
     kv_staging_pages: int = 0       # staging slots (one layer of a host page each; 0 = host_kv_pages)
     host_kv_dtype: str = "bf16"     # host pool storage: "bf16" or "fp8" (e4m3 + per-head page scales)
+    clock_sync: bool = True         # tensor parallel: advance every rank's workload clock by the slowest
+                                    # rank's step time (one small collective per step); off when the
+                                    # caller admits requests on a clock of its own
 
 
 @dataclass
@@ -146,13 +149,7 @@ class Engine:
         else:
             self.model = Llama(cfg, weights, self.kv, self.device, tp=tp, max_tokens=T,
                                max_pos=e.max_context + 16)
-        capped = e.max_step_tokens > 0
-        self.sched = Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context, tier=self.tier,
-                               max_step_tokens=e.max_step_tokens,
-                               round_decode=(lambda nd: self._bucket(nd) or nd) if capped else None,
-                               max_prefill_segments=MIXED_SEGMENTS if capped else 0,
-                               prefix_cache=e.prefix_cache and self.tier is None,
-                               admission=e.admission if (e.admission != "lpm" or e.prefix_cache) else "fcfs")
+        self.sched = self.new_scheduler(tier=self.tier)
         self.hkv = cfg.n_kv_heads // tp_size
         self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.target_tasks = e.target_tasks or self.sms
@@ -163,7 +160,8 @@ class Engine:
         self.controller = SchedControlPlane(policy="lpt")
         self.R = self._resident_prefix()
         self.step_no = 0
-        self.graphs: dict[int, tuple] = {}
+        self.graphs: dict[int, tuple] = {}  # key -> (graph, splits, items, kernel launches it holds)
+        self.graph_launches = 0  # kernel launches replayed from graphs (the extension counts the rest)
         self._pool = None
         self.stats: list[StepStats] = []
         self.clock = 0.0  # workload clock in seconds (device time + idle gaps)
@@ -213,6 +211,18 @@ class Engine:
         self.part_lse = torch.zeros(B * S_max, self.part_o.shape[1], dtype=torch.float32, device=self.device)
         self.sample_idx64 = torch.zeros(2 * B, dtype=torch.int64, device=self.device)
         self.merge_cnt = torch.zeros(B * self.cfg.n_kv_heads, dtype=torch.int32, device=self.device)
+
+    def new_scheduler(self, tier=None) -> Scheduler:
+        """A scheduler with this engine's configuration (the engine's own, or
+        a fresh one that simulates the engine's decisions without a model)."""
+        e = self.ecfg
+        capped = e.max_step_tokens > 0
+        return Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context, tier=tier,
+                         max_step_tokens=e.max_step_tokens,
+                         round_decode=(lambda nd: self._bucket(nd) or nd) if capped else None,
+                         max_prefill_segments=MIXED_SEGMENTS if capped else 0,
+                         prefix_cache=e.prefix_cache and tier is None and self.tier is None,
+                         admission=e.admission if (e.admission != "lpm" or e.prefix_cache) else "fcfs")
 
     def _view(self, name, shape=None):
         o, n = self.layout[name]
@@ -430,10 +440,31 @@ class Engine:
         graph = torch.cuda.CUDAGraph()
         if self._pool is None:
             self._pool = torch.cuda.graph_pool_handle()
+        n0 = _ext.launches()
         with torch.cuda.graph(graph, pool=self._pool):
             self.model.forward(batch)
-        self.graphs[bucket] = (graph, info["S"], info["n_items"])
+        self.graphs[bucket] = (graph, info["S"], info["n_items"], _ext.launches() - n0)
         return self.graphs[bucket]
+
+    def warm_decode_graphs(self, sizes) -> list:
+        """Capture the decode-step CUDA graphs for the buckets that hold the
+        given decode batch sizes, before a timed or latency-sensitive run (a
+        capture costs far more than a step). The capture runs on padding rows
+        only: no cache writes, empty attention items. Every tensor-parallel
+        rank must pass the same sizes (the graphs hold collectives)."""
+        if not self.ecfg.cuda_graphs:
+            return []
+        done = []
+        for b in sorted({self._bucket(int(n)) for n in sizes if int(n) > 0} - {None}):
+            if b in self.graphs:
+                continue
+            info = self._fill(StepPlan(), b)
+            self.dev[: self.packed_len].copy_(self.host[: self.packed_len], non_blocking=True)
+            self.sample_idx64[: info["n_sample"]].copy_(self._view("sample_idx")[: info["n_sample"]])
+            self._graph_for(b, info, self.plane.slots() if self.ecfg.levers else None)
+            done.append(b)
+        torch.cuda.synchronize(self.device)
+        return done
 
     # ------------------------------------------------------------------ step
     def step(self) -> tuple[StepPlan, list]:
@@ -461,9 +492,10 @@ class Engine:
         ev0.record()
         used_graph = False
         if key is not None:
-            graph, S, n_items = self._graph_for(key, info, slots)
+            graph, S, n_items, n_launch = self._graph_for(key, info, slots)
             assert S == info["S"] and n_items == info["n_items"]
             graph.replay()
+            self.graph_launches += n_launch
             used_graph = True
         else:
             self.model.forward(self._batch(info, slots))
@@ -472,7 +504,7 @@ class Engine:
         self.out_host[:ns].copy_(self.out_ids[:ns], non_blocking=True)
         ev1.synchronize()
         ms = ev0.elapsed_time(ev1)
-        if self.tp is not None and self.tp.world > 1:
+        if self.tp is not None and self.tp.world > 1 and self.ecfg.clock_sync:
             # every tensor-parallel rank must make the same scheduling
             # decisions (admissions follow the workload clock): advance all
             # clocks by the slowest rank's step time

@@ -74,18 +74,23 @@ class EngineServer:
         if max_new_tokens < 1:
             raise ValueError("max_new_tokens must be >= 1")
         fut: cf.Future = cf.Future()
-        with self._lock:
-            rid = self._next_rid
-            self._next_rid += 1
-            if name is not None:
-                self._named[str(name)] = rid
-        req = Request(rid=rid, prompt=ids, max_new_tokens=int(max_new_tokens), urgency=float(urgency))
+        req = Request(rid=-1, prompt=ids, max_new_tokens=int(max_new_tokens), urgency=float(urgency))
         req._t_submit = time.perf_counter()  # host clock of the HTTP side
         req._name = None if name is None else str(name)
         req._stream = queue.Queue() if stream else None
         req._sent = 0
         fut.tokens = req._stream
-        self._inbox.put((req, fut))
+        with self._lock:
+            # under the lock that _die takes: a request is either refused here
+            # or queued before the engine thread drains the queue on its way out
+            if self.error is not None:
+                self._fail(req, fut, RuntimeError(f"the engine stopped on an error: {self.error!r}"))
+                return fut
+            req.rid = self._next_rid
+            self._next_rid += 1
+            if name is not None:
+                self._named[str(name)] = req.rid
+            self._inbox.put((req, fut))
         return fut
 
     def cancel(self, name) -> None:
@@ -108,6 +113,22 @@ class EngineServer:
         self._end_stream(req)
         if not fut.done():
             fut.set_exception(exc)
+
+    def _die(self, exc: BaseException) -> None:
+        """The engine thread ends on an error: every request it holds, admitted
+        or still queued, fails (its stream ends and its future raises), and
+        later submissions fail at once (``submit`` checks ``error``)."""
+        with self._lock:
+            self.error = exc
+            queued = []
+            while True:
+                try:
+                    queued.append(self._inbox.get_nowait())
+                except queue.Empty:
+                    break
+        for req, fut in list(self._pending.values()) + queued:
+            self._fail(req, fut, exc)
+        self._pending.clear()
 
     def _drain_aborts(self) -> list:
         rids = []
@@ -208,10 +229,7 @@ class EngineServer:
                     except queue.Empty:
                         pass
         except BaseException as e:  # noqa: BLE001 - report to every waiter
-            self.error = e
-            for req, fut in list(self._pending.values()):
-                self._fail(req, fut, e)
-            self._pending.clear()
+            self._die(e)
 
     def start(self) -> "EngineServer":
         if self._thread is None:
@@ -389,10 +407,7 @@ class TPEngineServer(EngineServer):
                     self._push_tokens(plan)
                     self._complete(done)
         except BaseException as e:  # noqa: BLE001 - report to every waiter
-            self.error = e
-            for req, fut in list(self._pending.values()):
-                self._fail(req, fut, e)
-            self._pending.clear()
+            self._die(e)
 
 
 def follow(engine, group=None, heartbeat=None, max_rounds: int | None = None) -> int:

@@ -292,3 +292,40 @@ def test_streaming_tokens_in_process_and_over_http():
         th.join(10)
     finally:
         srv.stop()
+
+
+def test_engine_error_fails_admitted_queued_and_later_requests():
+    """When a step raises, the running request, a request still in the
+    inbox and a request submitted afterwards all fail, and every stream
+    ends: no caller waits for ever."""
+    import concurrent.futures as cf
+
+    import pytest
+
+    gate = threading.Event()
+
+    class Broken(FakeEngine):
+        def step(self):
+            gate.wait(10)  # hold the first step until the second request is queued
+            raise RuntimeError("injected step failure")
+
+    srv = EngineServer(Broken()).start()
+    try:
+        a = srv.submit([1, 2, 3], 4, stream=True)
+        for _ in range(500):
+            if srv._pending:
+                break
+            time.sleep(0.01)
+        b = srv.submit([4, 5], 4, stream=True)  # queued behind the failing step
+        gate.set()
+        for f in (a, b):
+            with pytest.raises(RuntimeError, match="injected"):
+                f.result(timeout=10)
+            assert f.tokens.get(timeout=10) is None
+        c = srv.submit([6], 2, stream=True)
+        with pytest.raises(RuntimeError, match="engine stopped"):
+            c.result(timeout=10)
+        assert c.tokens.get(timeout=10) is None
+        assert isinstance(srv.error, RuntimeError)
+    finally:
+        srv.stop()
