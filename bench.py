@@ -28,7 +28,9 @@ Reported:
                p99 of all inter-token intervals
   e2e.value    the same tokens over the host clock of the same loop, which
                includes each step's pinned H2D input copy and the D2H read of
-               the sampled tokens through ``Engine.step`` (the public API)
+               the sampled tokens through ``Engine.step_async`` / ``drain``
+               (the public API; the host plans step k while the device runs
+               step k - 1)
   gpu_launches kernel launches of this framework's extension in the timed
                steps (counted at the launchers; a replayed graph adds the
                launches it captured)
@@ -201,7 +203,7 @@ def main(argv=None):
         drv.admit(eng.add_request)
         if not eng.has_work():
             return None
-        plan, done = eng.step()
+        plan, done = eng.step_async()  # the host plans step k while the device runs step k - 1
         drv.advance(plan)
         return plan, done
 
@@ -215,7 +217,8 @@ def main(argv=None):
             break
         last_producers = [q.rid for q in ss.producers(r[0])]
 
-    # 4. timed region
+    # 4. timed region (starts with nothing in flight)
+    eng.drain()
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         dist.barrier()
@@ -243,6 +246,7 @@ def main(argv=None):
         finished.extend(done)
         steps += 1
     events[steps].record(stream)
+    finished.extend(eng.drain())  # the last step's tokens, read back to the host
     torch.cuda.synchronize(dev)
     t_host1 = time.perf_counter()
     wall1 = time.time()

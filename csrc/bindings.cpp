@@ -34,8 +34,8 @@ int sched_add_rmsnorm(const void *x, void *res, const void *w, void *y, int T, i
 int sched_rope_kv_append(const void *qkv, const int32_t *pos, const int32_t *slot,
                          const float *cos_sin, void *q_out, void *k_cache, void *v_cache, int T,
                          int Hq, int Hkv, int D, int page_size, int num_pages, int *status, cudaStream_t st);
-int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int H, int vocab, int *status,
-                    cudaStream_t st);
+int sched_embedding(const int32_t *ids, const int32_t *prev, int n_prev, const void *table, void *out, int T, int H,
+                    int vocab, int *status, cudaStream_t st);
 int sched_argmax(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
                  int id_offset, cudaStream_t st);
 int sched_moe_router(const void *x, const void *wr, int T, int H, int E, int K, int32_t *ids,
@@ -399,11 +399,14 @@ void rope_kv_append(const at::Tensor &qkv, const at::Tensor &pos, const at::Tens
 }
 
 void embedding(const at::Tensor &ids, const at::Tensor &table, at::Tensor &out,
-               const c10::optional<at::Tensor> &status) {
+               const c10::optional<at::Tensor> &status, const c10::optional<at::Tensor> &prev) {
   check_i32(ids, "ids");
   check_bf16(table, "table");
+  const bool has_prev = prev.has_value() && prev->defined();
+  if (has_prev) check_i32(*prev, "prev");
   c10::cuda::CUDAGuard g(ids.device());
-  check_rc(sched_embedding(ids.data_ptr<int32_t>(), table.data_ptr(), out.data_ptr(), ids.numel(),
+  check_rc(sched_embedding(ids.data_ptr<int32_t>(), has_prev ? prev->data_ptr<int32_t>() : nullptr,
+                           has_prev ? (int)prev->numel() : 0, table.data_ptr(), out.data_ptr(), ids.numel(),
                            table.size(1), table.size(0), ptr_or_null<int>(status), cur_stream()),
            "embedding");
 }

@@ -146,13 +146,17 @@ __global__ void rope_kv_append_kernel(const __nv_bfloat16 *__restrict__ qkv,
   }
 }
 
-__global__ void embedding_kernel(const int32_t *__restrict__ ids,
-                                 const __nv_bfloat16 *__restrict__ table,
+// A negative id -(1 + j) with `prev` given names row j of `prev`: a token the
+// previous step sampled and that is still only on the device (the engine
+// plans step k + 1 before step k's tokens reach the host).
+__global__ void embedding_kernel(const int32_t *__restrict__ ids, const int32_t *__restrict__ prev,
+                                 int n_prev, const __nv_bfloat16 *__restrict__ table,
                                  __nv_bfloat16 *__restrict__ out, int H, int vocab, int *status) {
   const int t = blockIdx.x;
   ptx::pdl_launch_dependents();
   ptx::pdl_wait();
-  const int id = ids[t];
+  int id = ids[t];
+  if (id < 0 && prev != nullptr && -(id + 1) < n_prev) id = prev[-(id + 1)];
   if (id < 0 || id >= vocab) {  // reported; the row is zeroed instead of read out of bounds
     if (threadIdx.x == 0) report_bad_index(status, kSiteTokenId, id);
     for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
@@ -367,11 +371,11 @@ extern "C" int sched_rope_kv_append(const void *qkv, const int32_t *pos, const i
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
-extern "C" int sched_embedding(const int32_t *ids, const void *table, void *out, int T, int H, int vocab,
-                               int *status, cudaStream_t st) {
+extern "C" int sched_embedding(const int32_t *ids, const int32_t *prev, int n_prev, const void *table, void *out,
+                               int T, int H, int vocab, int *status, cudaStream_t st) {
   if (T <= 0) return 0;
-  launch_pdl(ew::embedding_kernel, T, 256, 0, st, ids, static_cast<const __nv_bfloat16 *>(table),
-             static_cast<__nv_bfloat16 *>(out), H, vocab, status);
+  launch_pdl(ew::embedding_kernel, T, 256, 0, st, ids, prev, prev != nullptr ? n_prev : 0,
+             static_cast<const __nv_bfloat16 *>(table), static_cast<__nv_bfloat16 *>(out), H, vocab, status);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

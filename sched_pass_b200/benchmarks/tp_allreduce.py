@@ -80,6 +80,43 @@ def graph_time(fn, iters=30, replays=5):
     return float(t)
 
 
+def trace_phases(fn, dev, max_ctas: int = 1024) -> dict:
+    """One eager call with the GEMM's per-CTA %globaltimer trace armed.
+    Stream-K kernel rows: [entry, fix-up count << 32 | epilogue done (low 32
+    bits), after the reduction phase, exit]; cluster kernel rows: [entry, -,
+    -, exit]. Returns the phases in us from the earliest CTA entry on this
+    rank: when the last CTA finished its own tiles (GEMM + pushes), the
+    median and max time CTAs spent in the owned-chunk reduction (flag waits +
+    sums), and the last exit."""
+    from .._ext import ext
+    buf = torch.zeros(max_ctas * 4, dtype=torch.int64, device=dev)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ext().set_gemm_trace(buf.data_ptr())
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        ext().set_gemm_trace(0)
+    rows = [[int(v) & ((1 << 64) - 1) for v in r] for r in buf.view(-1, 4).tolist() if r[0] != 0]
+    if not rows:
+        return {}
+    t0 = min(r[0] for r in rows)
+    out = {"ctas": len(rows), "exit_us": round((max(r[3] for r in rows) - t0) / 1e3, 2)}
+    if max(r[2] for r in rows) != 0:  # stream-K kernel: the epilogue and reduction marks exist
+        lo32 = (1 << 32) - 1
+        epi = []
+        for r in rows:
+            e = (r[0] & ~lo32) | (r[1] & lo32)
+            epi.append(e + (1 << 32) if e < r[0] else e)
+        red = sorted(r[2] - e for r, e in zip(rows, epi))
+        out.update({"own_tiles_done_us": round((max(epi) - t0) / 1e3, 2),
+                    "reduce_phase_us_p50": round(red[len(red) // 2] / 1e3, 2),
+                    "reduce_phase_us_max": round(red[-1] / 1e3, 2),
+                    "fixups": sum(r[1] >> 32 for r in rows)})
+    return out
+
+
 def sp_sublayer(args, shapes, world, rank, dev, peaks, fused, base):
     """Row-parallel projection + residual add + RMSNorm, three ways (graph
     replays, max over ranks)."""
@@ -127,6 +164,8 @@ def main():
     ap.add_argument("--tokens", default="1,16,64,256,2048")
     ap.add_argument("--sp", action="store_true", help="also time the sequence-parallel sub-layer")
     ap.add_argument("--sp-only", action="store_true")
+    ap.add_argument("--trace", action="store_true",
+                    help="also report the fused kernel's phases from its per-CTA %%globaltimer trace")
     args = ap.parse_args()
     rank, world, local = init_distributed("nccl")
     dev = torch.device("cuda", local)
@@ -147,6 +186,8 @@ def main():
             t_be = dev_time(lambda: base.linear_allreduce(x, w, y))
             t_f = graph_time(lambda: fused.linear_allreduce(x, w, y))
             t_b = graph_time(lambda: base.linear_allreduce(x, w, y))
+            t_g = graph_time(lambda: ops.linear(x, w, y))  # the GEMM alone (no collective)
+            phases = trace_phases(lambda: fused.linear_allreduce(x, w, y), dev) if args.trace else None
             wbytes = N * K * 2
             t_hbm = wbytes / (peaks["hbm_gbs"] * 1e9)
             t_flop = 2 * T * N * K / (peaks["bf16_tflops"] * 1e12)
@@ -154,11 +195,16 @@ def main():
             roof = max(t_hbm, t_flop, t_nvl)
             rec = {"op": name, "tp": world, "T": T, "N": N, "K_local": K,
                    "fused_us": round(t_f * 1e3, 2), "gemm_plus_nccl_us": round(t_b * 1e3, 2),
+                   "gemm_only_us": round(t_g * 1e3, 2), "collective_share_us": round((t_f - t_g) * 1e3, 2),
                    "eager_fused_us": round(t_fe * 1e3, 2), "eager_gemm_plus_nccl_us": round(t_be * 1e3, 2),
                    "speedup": round(t_b / t_f, 3), "roofline_us": round(roof * 1e6, 2),
                    "oneshot_push_bytes": (world - 1) * T * N * 2,
                    "bound": ["hbm", "tensor", "nvlink"][[t_hbm, t_flop, t_nvl].index(roof)],
                    "frac_of_roofline": round(roof * 1e3 / t_f, 3)}
+            if phases is not None:
+                ph = [None] * world
+                dist.all_gather_object(ph, phases)
+                rec["phases_by_rank"] = ph
             if rank == 0:
                 print(json.dumps(rec), flush=True)
     ops.check_status()

@@ -24,6 +24,7 @@ from __future__ import annotations
 import math
 import os
 import time
+from collections import deque
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -89,6 +90,22 @@ class EngineConfig:
     clock_sync: bool = True         # tensor parallel: advance every rank's workload clock by the slowest
                                     # rank's step time (one small collective per step); off when the
                                     # caller admits requests on a clock of its own
+
+
+PENDING = -1  # placeholder of a sampled token the host has not read back yet
+
+
+@dataclass
+class _InFlight:
+    plan: StepPlan
+    info: dict
+    ev0: object
+    ev1: object
+    done_ev: object
+    buf: int
+    pend: list       # (request, index in its output, row of the sampled ids)
+    graph: bool
+    finished: list   # requests whose last token this step produces
 
 
 @dataclass
@@ -162,6 +179,8 @@ class Engine:
         self.step_no = 0
         self.graphs: dict[int, tuple] = {}  # key -> (graph, splits, items, kernel launches it holds)
         self.graph_launches = 0  # kernel launches replayed from graphs (the extension counts the rest)
+        self._inflight: deque = deque()  # steps enqueued whose tokens the host has not read yet
+        self.sched.before_preempt = self._before_preempt
         self._pool = None
         self.stats: list[StepStats] = []
         self.clock = 0.0  # workload clock in seconds (device time + idle gaps)
@@ -201,11 +220,18 @@ class Engine:
         reserve("tiles", (e.max_prefill_tokens // Q_TILE + B) * 4)
         reserve("sample_idx", 2 * B)
         self.packed_len = off
-        self.host = torch.zeros(off, dtype=torch.int32, pin_memory=True)
+        # two pinned staging buffers (inputs) and two read-back buffers
+        # (sampled tokens) alternate between consecutive steps, so the host can
+        # plan step k + 1 while step k's copies are still queued
+        self._hosts = [torch.zeros(off, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._outs = [torch.zeros(2 * B, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._h2d_done = [None, None]  # event after the copy that last read each staging buffer
+        self._buf = 0
+        self.host, self.out_host = self._hosts[0], self._outs[0]
         self.dev = torch.zeros(off, dtype=torch.int32, device=self.device)
         self.host_np = self.host.numpy()
         self.out_ids = torch.zeros(2 * B, dtype=torch.int32, device=self.device)
-        self.out_host = torch.zeros(2 * B, dtype=torch.int32, pin_memory=True)
+        self._timer_snap = None  # pinned copies of the timer rows of probe steps (created on first use)
         self.part_o = torch.zeros(B * S_max, self.cfg.n_q_heads // (self.tp.world if self.tp else 1),
                                   self.cfg.head_dim, dtype=torch.float32, device=self.device)
         self.part_lse = torch.zeros(B * S_max, self.part_o.shape[1], dtype=torch.float32, device=self.device)
@@ -317,7 +343,10 @@ class Engine:
             self.tier.stage(dec)  # host-resident pages this step reads -> staging pages
         for i, r in enumerate(dec):
             p = r.total_len - 1
-            ids[i] = r.next_input_token()
+            tok = r.next_input_token()
+            # a token the previous step sampled and the host has not read:
+            # the embedding takes it from that step's output row on the device
+            ids[i] = tok if tok != PENDING else -(1 + r._pending_row)
             pos[i] = p
             slot[i] = r.pages[p // 16] * 16 + p % 16  # the last page is always on the device
             pages = self.tier.pages_for(r) if self.tier is not None else r.pages
@@ -382,7 +411,10 @@ class Engine:
             sidx[ns:ndp + MIXED_SEGMENTS] = 0  # dummy rows, results ignored
             ns = ndp + MIXED_SEGMENTS
         return dict(T=T, nd=ndp, n_items=n_items, S=S, n_tiles=len(tiles), n_sample=ns,
-                    sample_map=sample_map, n_real_decode=nd, pad=pad)
+                    sample_map=sample_map, n_real_decode=nd, pad=pad,
+                    # for hooks that run after the next step was planned into the other buffer
+                    items=self._host("items")[:n_items * 4].reshape(-1, 4).copy(),
+                    kv_lens=kvl[:nd].tolist())
 
     def _batch(self, info, slots) -> ForwardBatch:
         mp = self.max_pages_per_req
@@ -454,6 +486,7 @@ class Engine:
         rank must pass the same sizes (the graphs hold collectives)."""
         if not self.ecfg.cuda_graphs:
             return []
+        self.drain()
         done = []
         for b in sorted({self._bucket(int(n)) for n in sizes if int(n) > 0} - {None}):
             if b in self.graphs:
@@ -467,14 +500,32 @@ class Engine:
         return done
 
     # ------------------------------------------------------------------ step
-    def step(self) -> tuple[StepPlan, list]:
+    def _async_ok(self) -> bool:
+        """Whether the host may run a step ahead of the device. Not with the
+        tiered KV store (its page staging follows the host's plan) nor when
+        every step must agree on the slowest rank's time (``clock_sync``)."""
+        tp_sync = self.tp is not None and self.tp.world > 1 and self.ecfg.clock_sync
+        return self.tier is None and not tp_sync
+
+    def _use_buffers(self, k: int) -> None:
+        self._buf = k
+        self.host, self.out_host = self._hosts[k], self._outs[k]
+        self.host_np = self.host.numpy()
+        ev = self._h2d_done[k]
+        if ev is not None:
+            ev.synchronize()  # the copy that last read this staging buffer has run
+
+    def _dispatch(self):
+        """Plan and enqueue one step; its sampled tokens stay pending (-1 in
+        the requests' outputs) until ``_resolve``. None when there is no work."""
         plan = self.sched.schedule()
         if plan.empty:
-            return plan, []
+            return None
         nd = len(plan.decode)
         decode_only = not plan.prefill
         bucket = self._bucket(nd) if (decode_only and self.ecfg.cuda_graphs) else None
         mixed = None if decode_only else self._mixed_bucket(plan)
+        self._use_buffers(self._buf ^ 1)
         if mixed is not None:
             info = self._fill(plan, mixed, pad=self._mixed_pad(mixed))
             key = ("mixed", mixed) if self.ecfg.cuda_graphs else None
@@ -483,13 +534,17 @@ class Engine:
             key = bucket
         slots = self.plane.slots() if self.ecfg.levers else None
         self.hooks.begin(self, plan, info)
+        stream = torch.cuda.current_stream(self.device)
         # one H2D copy of every step input
         self.dev[: self.packed_len].copy_(self.host[: self.packed_len], non_blocking=True)
+        h2d = torch.cuda.Event()
+        h2d.record(stream)
+        self._h2d_done[self._buf] = h2d
         si = self._view("sample_idx")
         self.sample_idx64[: info["n_sample"]].copy_(si[: info["n_sample"]])
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
-        ev0.record()
+        ev0.record(stream)
         used_graph = False
         if key is not None:
             graph, S, n_items, n_launch = self._graph_for(key, info, slots)
@@ -499,26 +554,93 @@ class Engine:
             used_graph = True
         else:
             self.model.forward(self._batch(info, slots))
-        ev1.record()
+        ev1.record(stream)
+        if info.get("probe"):
+            # the timer rows of this step, before a later step clears them
+            n = info["n_items"] * self.hkv
+            if self._timer_snap is None:
+                self._timer_snap = [torch.zeros(self.plane.N, dtype=torch.int64, pin_memory=True) for _ in range(2)]
+            snap = self._timer_snap[self._buf][:n]
+            snap.copy_(self.plane.timer_t[:n], non_blocking=True)
+            info["timer"] = snap
         ns = info["n_sample"]
         self.out_host[:ns].copy_(self.out_ids[:ns], non_blocking=True)
-        ev1.synchronize()
-        ms = ev0.elapsed_time(ev1)
+        done_ev = torch.cuda.Event()
+        done_ev.record(stream)
+        # the step's tokens are pending: counts advance now (so the next step
+        # can be planned), values arrive in _resolve
+        by_rid = {r.rid: r for r in plan.decode}
+        by_rid.update({r.rid: r for r, _, _ in plan.prefill})
+        rows = [(by_rid[rid], row) for rid, row in info["sample_map"]]
+        finished = self.sched.commit(plan, {req.rid: PENDING for req, _ in rows}, float("nan"))
+        pend = []
+        for req, row in rows:
+            pend.append((req, len(req.output) - 1, row))
+            req._pending_row = row
+        self._inflight.append(_InFlight(plan, info, ev0, ev1, done_ev, self._buf, pend, used_graph, finished))
+        self.step_no += 1
+        return plan
+
+    def _resolve(self, f: "_InFlight") -> list:
+        """Wait for an enqueued step, write its tokens into the requests and
+        finish its bookkeeping. Returns the requests it finished."""
+        f.done_ev.synchronize()
+        ms = f.ev0.elapsed_time(f.ev1)
         if self.tp is not None and self.tp.world > 1 and self.ecfg.clock_sync:
             # every tensor-parallel rank must make the same scheduling
             # decisions (admissions follow the workload clock): advance all
             # clocks by the slowest rank's step time
             ms = self.tp.max_over_ranks(ms)
         self.clock += ms / 1e3
-        self.hooks.end(self, plan, info, ms)
-        out = self.out_host[:ns].numpy()
-        sampled = {rid: int(out[i]) for rid, i in info["sample_map"]}
-        done = self.sched.commit(plan, sampled, self.clock)
-        if done:
-            self.controller.forget([r.rid for r in done])
-        self.stats.append(StepStats(nd, plan.n_tokens - nd, ms, used_graph))
-        self.step_no += 1
-        return plan, done
+        out = self._outs[f.buf].numpy()
+        for req, idx, row in f.pend:
+            req.output[idx] = int(out[row])
+            req.token_times[idx] = self.clock
+            if idx == len(req.output) - 1:
+                req._pending_row = None
+        self.hooks.end(self, f.plan, f.info, ms)
+        if f.finished:
+            self.controller.forget([r.rid for r in f.finished])
+        self.stats.append(StepStats(len(f.plan.decode), f.plan.n_tokens - len(f.plan.decode), ms, f.graph))
+        return f.finished
+
+    def drain(self) -> list:
+        """Wait for every enqueued step and apply its tokens; returns the
+        requests they finished."""
+        done = []
+        while self._inflight:
+            done += self._resolve(self._inflight.popleft())
+        return done
+
+    def step(self) -> tuple[StepPlan, list]:
+        """One step, synchronously: plan it, run it, read its sampled tokens
+        back. Returns (plan, requests it finished)."""
+        done = self.drain()
+        plan = self._dispatch()
+        done += self.drain()
+        return (plan if plan is not None else StepPlan()), done
+
+    def step_async(self) -> tuple[StepPlan, list]:
+        """One step with the host a step ahead of the device: plan and
+        enqueue step k (decode inputs that step k - 1 samples are read on the
+        device), then wait for step k - 1 and apply its tokens, so the host's
+        planning of k overlaps the device's work on k - 1. Returns (plan of
+        step k, requests finished by the steps read back in this call);
+        ``drain()`` reads back the step still in flight. Falls back to
+        ``step()`` where the host may not run ahead (``_async_ok``)."""
+        if not self._async_ok():
+            return self.step()
+        plan = self._dispatch()
+        keep = 1 if plan is not None else 0
+        done = []
+        while len(self._inflight) > keep:
+            done += self._resolve(self._inflight.popleft())
+        return (plan if plan is not None else StepPlan()), done
+
+    def _before_preempt(self) -> None:
+        """A preempted request's generated tokens become part of its prompt,
+        so their values must be on the host: read back every step in flight."""
+        self.drain()
 
     # ------------------------------------------------------------------ convenience
     def generate(self, prompts, max_new_tokens: int = 16) -> list:
@@ -528,5 +650,6 @@ class Engine:
         for r in reqs:
             self.add_request(r)
         while self.has_work():
-            self.step()
+            self.step_async()
+        self.drain()
         return [r.output for r in reqs]

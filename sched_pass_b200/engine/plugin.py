@@ -188,6 +188,7 @@ class SchedPlugin:
         c = self.cfg
         nd, n_items = info["nd"], info["n_items"]
         self._probe = False
+        info["probe"] = False
         if c.hooks_noop or not engine.ecfg.levers or nd == 0:
             return
         st = self.stats
@@ -237,10 +238,11 @@ class SchedPlugin:
             plane.clear_timer()
         plane.push()
         self._probe = probe
+        info["probe"] = probe  # per step: the engine may begin step k + 1 before it ends step k
 
     def on_batch_end(self, engine, plan, info, ms: float) -> None:
         c = self.cfg
-        if self._probe and info["nd"] > 0:
+        if info.get("probe", self._probe) and info["nd"] > 0:
             self._fold_probe(engine, plan, info)
             self.stats.probes += 1
         self._probe = False
@@ -285,14 +287,25 @@ class SchedPlugin:
         engine.plane.set_rows(q=q, n=n_items * hkv)
 
     def _fold_probe(self, engine, plan, info) -> None:
+        """Per-request cycles of a probe step into the controller. The
+        engine snapshots the timer rows right after the step's forward
+        (``info["timer"]``, host memory) and keeps the step's work items and
+        KV lengths in ``info``, because the next step may already be
+        planned (and the timer cleared) when this runs."""
         hkv = engine.hkv
         n_items = info["n_items"]
-        cyc = engine.plane.timer_t[: n_items * hkv].view(n_items, hkv).sum(1).cpu().numpy()
-        items = engine._host("items")[: n_items * 4].reshape(-1, 4)
+        timer = info.get("timer")
+        if timer is None:
+            timer = engine.plane.timer_t[: n_items * hkv].cpu()
+        cyc = timer[: n_items * hkv].view(n_items, hkv).sum(1).numpy()
+        items = info.get("items")
+        if items is None:
+            items = engine._host("items")[: n_items * 4].reshape(-1, 4)
         per_req = np.zeros(info["nd"], dtype=np.float64)
-        np.add.at(per_req, items[:, 0], cyc)
+        np.add.at(per_req, items[:n_items, 0], cyc)
         dec = plan.decode
-        engine.controller.observe([r.rid for r in dec], [r.total_len for r in dec],
+        lens = info.get("kv_lens")
+        engine.controller.observe([r.rid for r in dec], lens if lens is not None else [r.total_len for r in dec],
                                   per_req[: len(dec)].tolist())
 
     def stats_line(self, engine) -> str:

@@ -64,6 +64,9 @@ class Scheduler:
         self.max_context = max_context
         self.waiting: deque[Request] = deque()
         self.running: list[Request] = []   # admitted (PREFILL or DECODE), admission order
+        # called before a preemption: an engine that runs ahead of the device
+        # reads back pending tokens (a preempted request's output joins its prompt)
+        self.before_preempt = None
 
     def add(self, req: Request) -> None:
         if req.prompt_len + req.max_new_tokens > self.max_context:
@@ -160,6 +163,8 @@ class Scheduler:
         return True
 
     def _preempt(self, victim: Request, plan: StepPlan) -> None:
+        if self.before_preempt is not None:
+            self.before_preempt()
         self.running.remove(victim)
         self.release(victim)
         # restart from scratch: generated tokens become part of the prompt

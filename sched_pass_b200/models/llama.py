@@ -287,7 +287,7 @@ class Llama:
         cfg, sp = self.cfg, self.sp
         T = b.n_tokens
         h = self.h[:T]
-        ops.embedding(b.ids[:T], self.w.embed, h)
+        ops.embedding(b.ids[:T], self.w.embed, h, prev=b.out_ids)
         if b.tier is not None:
             b.tier.begin_forward()
         layers = self.w.layers
@@ -315,7 +315,7 @@ class Llama:
         cfg = self.cfg
         T = b.n_tokens
         h, normed, delta = self.h[:T], self.normed[:T], self.delta[:T]
-        ops.embedding(b.ids[:T], self.w.embed, h)
+        ops.embedding(b.ids[:T], self.w.embed, h, prev=b.out_ids)
         if b.tier is not None:
             b.tier.begin_forward()
         for li, lw in enumerate(self.w.layers):

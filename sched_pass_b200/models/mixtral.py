@@ -24,7 +24,7 @@ class Mixtral(Llama):
         T = b.n_tokens
         h, normed, delta = self.h[:T], self.normed[:T], self.delta[:T]
         layers = self.w.layers
-        ops.embedding(b.ids[:T], self.w.embed, h)
+        ops.embedding(b.ids[:T], self.w.embed, h, prev=b.out_ids)
         ops.add_rmsnorm(h, None, layers[0].ln_in, cfg.rms_eps, normed)
         if b.tier is not None:
             b.tier.begin_forward()

@@ -176,10 +176,14 @@ def attention_prefill(q, out, k_cache, v_cache, block_table, kv_lens, tiles, num
     return out
 
 
-def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None,
+              prev: torch.Tensor | None = None) -> torch.Tensor:
+    """Rows of ``table`` for ``ids``. With ``prev`` (int32 on the device), an
+    id -(1 + j) stands for the token ``prev[j]``: a token sampled by the
+    previous step that the host has not read yet."""
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
-    ext().embedding(ids, table, out, status_buffer(ids.device))
+    ext().embedding(ids, table, out, status_buffer(ids.device), prev)
     return out
 
 

@@ -103,3 +103,42 @@ def test_prefill_tile_order_does_not_change_tokens():
         del eng
         torch.cuda.empty_cache()
     assert outs[0] == outs[1]
+
+
+def _generate_sync(eng, ps, n):
+    """The same requests as ``Engine.generate`` but one synchronous step at a time."""
+    from sched_pass_b200.engine.request import Request
+    reqs = [Request(rid=i, prompt=np.asarray(p, dtype=np.int32), max_new_tokens=n) for i, p in enumerate(ps)]
+    for r in reqs:
+        eng.add_request(r)
+    while eng.has_work():
+        eng.step()
+    return reqs
+
+
+def test_async_steps_match_synchronous_steps():
+    """The host planning step k + 1 while the device runs step k (decode
+    inputs taken from the previous step's sampled ids on the device) gives
+    the same tokens as reading every step back before planning the next;
+    every token time is filled in and the same number of steps ran. Also
+    under preemption (a KV pool too small for every request at once), where
+    pending tokens are read back before a request's output joins its prompt."""
+    ps = prompts(8, lo=20, hi=260, seed=11)
+    for kw in (dict(cuda_graphs=True, levers=True), dict(cuda_graphs=False, levers=True, acquire="clc"),
+               dict(cuda_graphs=True, levers=True, num_pages=48)):
+        a, _ = make_engine(**kw)
+        want = _generate_sync(a, ps, 7)
+        n_sync = len(a.stats)
+        a.graphs.clear()
+        del a
+        b, _ = make_engine(**kw)
+        got = b.generate(ps, max_new_tokens=7)
+        ops.check_status()
+        assert got == [r.output for r in want], kw
+        assert len(b.stats) == n_sync, kw
+        assert b.sched.alloc.free == b.sched.alloc.num_pages
+        b.graphs.clear()
+        del b
+        torch.cuda.empty_cache()
+    for r in want:
+        assert all(np.isfinite(r.token_times)) and r.token_times == sorted(r.token_times)

@@ -159,6 +159,18 @@ def test_embedding_and_argmax():
 
 
 # ------------------------------------------------------------------ decode attention
+
+def test_embedding_takes_negative_ids_from_the_previous_step():
+    """id -(1 + j) with ``prev`` reads token prev[j] (a token the previous
+    step sampled that only the device holds yet); other ids read directly."""
+    table = torch.randn(1000, 256, device="cuda").to(torch.bfloat16)
+    prev = torch.tensor([5, 7, 999], dtype=torch.int32, device="cuda")
+    ids = torch.tensor([3, -1, -3, 4, -2], dtype=torch.int32, device="cuda")
+    out = ops.embedding(ids, table, prev=prev)
+    torch.cuda.synchronize()
+    ops.check_status()
+    assert torch.equal(out, table[torch.tensor([3, 5, 999, 4, 7], device="cuda")])
+
 def make_paged(B, Hkv, lens, seed=0, pages_extra=7):
     D = 128
     total_pages = sum((int(n) + 15) // 16 for n in lens) + pages_extra
