@@ -21,6 +21,7 @@
 #include <map>
 #include <sstream>
 
+#include "cfg.h"
 #include "passes.h"
 
 namespace weave {
@@ -149,56 +150,13 @@ std::string find_softmax_score(const Function &f, const std::string &ld) {
   return "";
 }
 
-struct Loop {
-  int header = -1, latch = -1;  // block indices, latch >= header
-  std::string iv;               // canonical IV (phi result), "" if none
-  std::string iv_type;
-};
+// Loops come from the CFG analysis (cfg.h): natural loops over the
+// dominator tree, each with its structurally recognised canonical IV.
+using Loop = NaturalLoop;
 
-// Loops by back edges: block L branches to an earlier-or-same block H.
-std::vector<Loop> find_loops(const Function &f, const Defs &defs) {
-  std::vector<Loop> loops;
-  for (size_t b = 0; b < f.blocks.size(); ++b) {
-    const Block &blk = f.blocks[b];
-    if (blk.insts.empty()) continue;
-    const Inst &t = blk.insts.back();
-    if (t.opcode != "br") continue;
-    for (const std::string &lab : value_tokens(t.text)) {
-      int h = f.block_index(lab.substr(1));
-      if (h < 0 || h > (int)b) continue;
-      Loop L;
-      L.header = h;
-      L.latch = (int)b;
-      // canonical IV: phi iN [0, %pre], [%next, %latch], %next = add iN %iv, 1
-      for (const Inst &in : f.blocks[h].insts) {
-        if (in.opcode != "phi") break;
-        if (int_bits(in.type) == 0) continue;
-        std::string txt = in.text;
-        bool zero_init = txt.find("[ 0,") != std::string::npos || txt.find("[0,") != std::string::npos;
-        if (!zero_init) continue;
-        for (const std::string &op : in.operands) {
-          const Inst *d = defs.get(f, op);
-          if (!d || d->opcode != "add") continue;
-          if (!uses(*d, in.result)) continue;
-          std::string dt = d->text;
-          size_t c = dt.rfind(',');
-          std::string last = trim(dt.substr(c + 1));
-          std::string first_op = dt.substr(dt.find(in.type) + in.type.size());
-          first_op = trim(first_op.substr(0, first_op.find(',')));
-          if (last == "1" || first_op == "1") {
-            L.iv = in.result;
-            L.iv_type = in.type;
-          }
-        }
-        if (!L.iv.empty()) break;
-      }
-      loops.push_back(L);
-    }
-  }
-  return loops;
-}
+std::vector<Loop> find_loops(const Function &f) { return natural_loops(f, Cfg(f)); }
 
-bool in_loop(const Loop &L, int b) { return b >= L.header && b <= L.latch; }
+bool in_loop(const Loop &L, int b) { return L.contains(b); }
 
 // Does `v` depend (within a few steps of address arithmetic) on a load
 // inside the loop, or on the IV?
@@ -404,17 +362,26 @@ void insert_before(Block &b, int idx, const std::vector<Inst> &code) {
   b.insts.insert(b.insts.begin() + idx, code.begin(), code.end());
 }
 
-// Replace uses of `from` by `to` in: the rest of block `blk` after index
-// `after`, the later blocks of the loop, and header phis (back edge).
+// Replace uses of `from` by `to` wherever `to` (defined in block `blk` at
+// index `after`) dominates the use, within loop L: the rest of block `blk`,
+// the non-phi instructions of the loop blocks that `blk` dominates, and phi
+// incoming values on edges leaving a block that `blk` dominates (the back
+// edge into the header among them).
 void replace_dominated(Function &f, int blk, int after, const Loop &L, const std::string &from,
                        const std::string &to) {
-  for (size_t i = after + 1; i < f.blocks[blk].insts.size(); ++i) replace_uses(f.blocks[blk].insts[i], from, to);
-  for (int b = blk + 1; b <= L.latch && b < (int)f.blocks.size(); ++b)
-    for (Inst &in : f.blocks[b].insts)
-      if (in.opcode != "phi") replace_uses(in, from, to);
-  for (Inst &in : f.blocks[L.header].insts) {
-    if (in.opcode != "phi") break;
-    replace_uses(in, from, to);
+  const Cfg g(f);
+  for (size_t i = after + 1; i < f.blocks[blk].insts.size(); ++i)
+    if (f.blocks[blk].insts[i].opcode != "phi") replace_uses(f.blocks[blk].insts[i], from, to);
+  auto edge_ok = [&](const std::string &pred_label) { return g.dominates(blk, f.block_index(pred_label)); };
+  for (int b = 0; b < (int)f.blocks.size(); ++b) {
+    if (!L.contains(b)) continue;
+    const bool dom = b != blk && g.dominates(blk, b);
+    for (Inst &in : f.blocks[b].insts) {
+      if (in.opcode == "phi")
+        rewrite_phi_incoming(in, from, to, edge_ok);
+      else if (dom)
+        replace_uses(in, from, to);
+    }
   }
 }
 
@@ -426,15 +393,15 @@ class Weaver {
     const bool body = f.header.find(kTaskBody) != std::string::npos;
     Defs defs(f);
     // ---- phase 0: detection while the function is untouched
-    std::vector<Loop> loops = find_loops(f, defs);
+    std::vector<Loop> loops = find_loops(f);
     std::vector<Site> sites;
     async_sites.clear();
     if (c.policy || c.shed) {
       const std::set<std::string> written = written_roots(f, defs);
       for (size_t li = 0; li < loops.size(); ++li) {
         const Loop &L = loops[li];
-        for (int b = L.header; b <= L.latch; ++b)
-          for (size_t i = 0; i < f.blocks[b].insts.size(); ++i) {
+        for (int b = 0; b < (int)f.blocks.size(); ++b)
+          for (size_t i = 0; L.contains(b) && i < f.blocks[b].insts.size(); ++i) {
             const Inst &in = f.blocks[b].insts[i];
             if (in.opcode != "load" || in.operands.empty()) continue;
             Mu mu = L.iv.empty() ? Mu::None : address_kind(f, defs, L, in.operands.back());
@@ -454,8 +421,9 @@ class Weaver {
         for (size_t li = 0; li < loops.size(); ++li) {
           const Loop &L = loops[li];
           if (L.iv.empty()) continue;
-          for (int b = L.header; b <= L.latch; ++b)
+          for (int b = 0; b < (int)f.blocks.size(); ++b)
             for (const Inst &in : f.blocks[b].insts) {
+              if (!L.contains(b)) break;
               AsyncSite as;
               if (in.opcode != "call" || !parse_cp_async(in.text, as.src, as.src_type)) continue;
               if (address_kind(f, defs, L, as.src) == Mu::None) continue;
@@ -711,7 +679,7 @@ class Weaver {
         for (size_t k = 0; k < loops.size(); ++k) {
           const Loop &Lk = loops[k];
           if (Lk.iv.empty() || !in_loop(Lk, tb)) continue;
-          if (li < 0 || (Lk.latch - Lk.header) < (loops[li].latch - loops[li].header)) li = (int)k;
+          if (li < 0 || Lk.size < loops[li].size) li = (int)k;  // innermost loop around the site
         }
       }
       if (li < 0) {

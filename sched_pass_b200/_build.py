@@ -79,7 +79,7 @@ def build_extension(verbose: bool = False):
     )
 
 
-WEAVE_SOURCES = ["weave/ir.cpp", "weave/passes.cpp", "weave/weave_pass.cpp", "weave/workqueue_pass.cpp",
+WEAVE_SOURCES = ["weave/ir.cpp", "weave/cfg.cpp", "weave/passes.cpp", "weave/weave_pass.cpp", "weave/workqueue_pass.cpp",
                  "weave/main.cpp"]
 
 
