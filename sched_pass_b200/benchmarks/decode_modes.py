@@ -15,6 +15,10 @@ are stragglers and scheduling matters):
   ticket   persistent workers (R = occupancy x SMs), atomic ticket, LPT order
   clc      grid = tasks, cluster-launch-control stealing, region order
   split    KV split 4 ways + merge (for reference)
+  flashinfer  the installed FlashInfer library's BatchDecodeWithPagedKVCache
+           (the kernel the reference weaves into SGLang: jc-su/sched-pass
+           SGLANG.md, test/py/test_flashinfer_arm.py) on the same pages, HND
+           layout; run as a library only, its output checked against stock
 Each mode: median device time over iterations with an L2 flush between them,
 achieved KV bandwidth vs the measured HBM peak, and bit-exactness vs stock
 for the permutation-only modes.
@@ -54,11 +58,39 @@ def build(B=256, Hq=32, Hkv=8, seed=0, median=1024, sigma=1.0, lo=64, hi=32768):
     return lens, torch.from_numpy(bt).cuda(), kc, vc, q, urg
 
 
+def flashinfer_decode(lens, bt, kc, vc, q, Hq, Hkv, scale):
+    """A closure running FlashInfer's paged decode over this fixture's pages
+    (indptr / indices / last-page lengths from the block table), or None if
+    the library cannot plan it here."""
+    try:
+        import flashinfer
+    except ImportError:
+        return None
+    pages = (lens + 15) // 16
+    indptr = np.concatenate([[0], np.cumsum(pages)]).astype(np.int32)
+    btn = bt.cpu().numpy()
+    indices = np.concatenate([btn[b, :pages[b]] for b in range(len(lens))]).astype(np.int32)
+    last = (lens - (pages - 1) * 16).astype(np.int32)
+    ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(ws, kv_layout="HND")
+    try:
+        w.plan(torch.from_numpy(indptr).cuda(), torch.from_numpy(indices).cuda(), torch.from_numpy(last).cuda(),
+               Hq, Hkv, 128, 16, q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16, sm_scale=scale)
+    except Exception as e:  # noqa: BLE001 - report, do not fail the other modes
+        print(json.dumps({"mode": "flashinfer", "plan_error": repr(e)[:300]}))
+        return None
+    fo = torch.empty_like(q)
+
+    def run():
+        return w.run(q, (kc, vc), out=fo)
+    return run
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--requests", type=int, default=256)
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--modes", default="stock,woven,pi,policy,timer,shed,ticket,clc,split")
+    ap.add_argument("--modes", default="stock,woven,pi,policy,timer,shed,ticket,clc,split,flashinfer")
     args = ap.parse_args()
     Hq, Hkv = 32, 8
     lens, bt, kc, vc, q, urg = build(args.requests, Hq, Hkv)
@@ -91,6 +123,8 @@ def main():
                              slots=plane.slots() if (woven and slots) else None, woven=woven,
                              acquire=acquire, grid=grid)
 
+    from ..utils.clocks import ClockSampler
+    sampler = ClockSampler(gpu_index=torch.cuda.current_device()).start()
     results = {}
     stock_out = None
     for mode in args.modes.split(","):
@@ -142,6 +176,11 @@ def main():
                 ops.attention_decode(q, out, kc, vc, bt, it4_t, it4.shape[0], scale, part_o=po,
                                      part_lse=pl, woven=False)
                 ops.attention_merge(po, pl, mr, mb, B, out)
+        elif mode == "flashinfer":
+            fn = flashinfer_decode(lens, bt, kc, vc, q, Hq, Hkv, scale)
+            if fn is None:
+                print(json.dumps({"mode": mode, "unavailable": "flashinfer decode could not be planned"}))
+                continue
         else:
             raise ValueError(mode)
         ms = time_fn(fn, args.iters, flush=flush)
@@ -149,6 +188,11 @@ def main():
         torch.cuda.synchronize()
         rec = {"mode": mode, "us": round(ms * 1e3, 1), "kv_GBps": round(kv / ms / 1e6, 1),
                "frac_hbm_of_measured": round(kv / ms / 1e6 / peaks["hbm_gbs"], 3)}
+        if mode == "flashinfer" and stock_out is not None:
+            fo = fn()
+            torch.cuda.synchronize()
+            rec["rel_err_vs_stock"] = round(float((fo.float() - stock_out.float()).norm() /
+                                                  stock_out.float().norm()), 5)
         if mode == "stock":
             stock_out = out.clone()
         elif mode in ("woven", "pi", "timer", "ticket", "clc", "policy") and stock_out is not None:
@@ -159,6 +203,7 @@ def main():
         results[mode] = rec
         print(json.dumps(rec), flush=True)
     ops.check_status()
+    print(json.dumps({"clocks": sampler.stop()}))
     print(json.dumps({"requests": B, "tasks": n_tasks, "R": R, "occupancy": occ,
                       "kv_GB": round(kv_bytes / 1e9, 3), "len_p50": int(np.median(lens)),
                       "len_max": int(lens.max())}))

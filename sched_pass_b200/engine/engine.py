@@ -463,10 +463,15 @@ class Engine:
         if g is not None:
             return g
         batch = self._batch(info, slots)
+        # a forward reads the previous step's sampled ids (decode inputs the
+        # host has not seen) and overwrites them with its own: every warm-up
+        # run starts from the same ids, and the replay too
+        prev = self.out_ids.clone()
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             for _ in range(2):  # warm-up outside capture (lazy inits, attributes)
+                self.out_ids.copy_(prev)
                 self.model.forward(batch)
         torch.cuda.current_stream(self.device).wait_stream(s)
         graph = torch.cuda.CUDAGraph()
@@ -475,6 +480,7 @@ class Engine:
         n0 = _ext.launches()
         with torch.cuda.graph(graph, pool=self._pool):
             self.model.forward(batch)
+        self.out_ids.copy_(prev)
         self.graphs[bucket] = (graph, info["S"], info["n_items"], _ext.launches() - n0)
         return self.graphs[bucket]
 
