@@ -53,6 +53,9 @@ extern "C" int sched_probe_tasks(const uint32_t *cost, int n_tasks, int mode, in
                                  const void *data, size_t data_bytes, unsigned *hits, unsigned *per_cta,
                                  unsigned *ticket, unsigned *sink, int *status, cudaStream_t st);
 extern "C" int sched_probe_tasks_occupancy();
+extern "C" int sched_probe_clc(const uint32_t *work, int n_tasks, int mode, int grid, int max_rec, unsigned *hits,
+                               unsigned long long *rec, unsigned *n_rec, unsigned *smid, int *status,
+                               cudaStream_t st);
 extern "C" int sched_probe_mix(const void *R, size_t r_bytes, const void *S, size_t s_bytes, int mode, float frac,
                                unsigned *sink, int grid, cudaStream_t st);
 extern "C" int sched_probe_pdl_pairs(float *buf, float *out, int n, const float *table, int work, int prologue,
@@ -547,6 +550,27 @@ void probe_tasks(const at::Tensor &cost, int64_t mode, int64_t grid, int64_t mem
            "probe_tasks");
 }
 
+void probe_clc(const at::Tensor &work, int64_t mode, int64_t grid, at::Tensor &hits, at::Tensor &rec,
+               at::Tensor &n_rec, at::Tensor &smid, const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(work.is_cuda() && work.scalar_type() == at::kInt && work.is_contiguous(), "work int32 on the device");
+  TORCH_CHECK(mode >= 0 && mode <= 2, "mode is 0 (static), 1 (CLC late bound) or 2 (CLC claim-ahead)");
+  const int64_t n = work.numel();
+  const int64_t g = mode == 0 ? grid : n;
+  TORCH_CHECK(g > 0, "grid must be positive");
+  TORCH_CHECK(hits.numel() >= n && hits.element_size() == 4, "hits: int32 [n_tasks]");
+  TORCH_CHECK(rec.dim() == 2 && rec.size(0) >= g && rec.element_size() == 8 && rec.is_contiguous(),
+              "rec: int64 [grid, max_rec]");
+  TORCH_CHECK(n_rec.numel() >= g && smid.numel() >= g && n_rec.element_size() == 4 && smid.element_size() == 4,
+              "n_rec, smid: int32 [grid]");
+  c10::cuda::CUDAGuard gd(work.device());
+  check_rc(sched_probe_clc(reinterpret_cast<const uint32_t *>(work.data_ptr()), (int)n, (int)mode, (int)g,
+                           (int)rec.size(1), reinterpret_cast<unsigned *>(hits.data_ptr()),
+                           reinterpret_cast<unsigned long long *>(rec.data_ptr()),
+                           reinterpret_cast<unsigned *>(n_rec.data_ptr()), reinterpret_cast<unsigned *>(smid.data_ptr()),
+                           ptr_or_null<int>(status), cur_stream()),
+           "probe_clc");
+}
+
 void probe_mix(const at::Tensor &R, const at::Tensor &S, int64_t mode, double frac, at::Tensor &sink,
                int64_t grid) {
   TORCH_CHECK(R.is_cuda() && S.is_cuda() && R.is_contiguous() && S.is_contiguous(), "R, S on the device");
@@ -655,6 +679,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("probe_tasks", &probe_tasks);
   m.def("probe_tasks_occupancy", &sched_probe_tasks_occupancy);
   m.def("probe_mix", &probe_mix);
+  m.def("probe_clc", &probe_clc);
   m.def("kv_page_copy_fp8", &kv_page_copy_fp8);
   m.def("probe_pdl_pairs", &probe_pdl_pairs);
   m.def("probe_pdl_produce", &probe_pdl_produce);

@@ -23,6 +23,19 @@
 //    reference's test/cache_reuse.cu:1-45); sweeping f on an R larger than
 //    L2 asks whether residency is a continuous per-request budget (its
 //    test/cache_budget.cu:1-32).
+// 5. clc_probe: the behaviour of cluster launch control as CTA code sees
+//    it, one CTA per task (the grid is the task list). Every CTA runs its
+//    task (a %clock64 burn of work[task] cycles), then claims: late bound
+//    (try_cancel issued only once the body finished) or claim-ahead (the next
+//    try_cancel issued before the body, its answer collected after). Each
+//    claim is recorded with the cycles the CTA waited for the answer and the
+//    cancelled CTA's id (or a failure), so the host measures the claim
+//    latency, checks that every worker ends with exactly one failed claim
+//    and that every task ran once, and compares the makespan of the two
+//    placements with a static persistent grid (the reference's
+//    experiments/clc/FINDINGS.md:203-225 terminal-failure rule, :668-670
+//    claim latency, :1244-1256 claim-ahead vs late binding, re-measured on
+//    B200).
 // 4. pdl_producer / pdl_consumer: two dependent kernels on one stream. The
 //    producer releases its dependents at entry; the consumer runs an
 //    independent prologue, then griddepcontrol.wait, then reads what the
@@ -167,6 +180,108 @@ __global__ void __launch_bounds__(128) task_probe(const TaskArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- clc
+struct ClcArgs {
+  const uint32_t *work;       // per task: cycles of the body
+  int n_tasks;
+  int mode;                   // 0 static persistent grid, 1 CLC late bound, 2 CLC claim-ahead
+  int max_rec;                // claim records per CTA
+  unsigned *hits;             // [n_tasks] executions (must end at 1)
+  unsigned long long *rec;    // [grid][max_rec]: waited cycles << 32 | (cancelled CTA id, or ~0u on failure)
+  unsigned *n_rec;            // [grid] claims recorded per CTA
+  unsigned *smid;             // [grid] SM of each CTA
+  int *status;
+};
+
+__device__ __forceinline__ void clc_body(const ClcArgs &a, int task) {
+  if (threadIdx.x == 0) {
+    const long long t0 = clock64();
+    while (clock64() - t0 < (long long)a.work[task]) {
+    }
+    atomicAdd(a.hits + task, 1u);
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void clc_issue(uint4 *result, uint64_t *bar) {
+  const uint32_t res = static_cast<uint32_t>(__cvta_generic_to_shared(result));
+  const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  asm volatile(
+      "{\n.reg .b64 st;\n"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%1], 16;\n"
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];\n"
+      "}\n" ::"r"(res),
+      "r"(b)
+      : "memory");
+}
+
+// Waits (bounded) for the answer of the claim in flight; returns the
+// cancelled CTA's x id or ~0u (failure, or the wait gave up).
+__device__ __forceinline__ uint32_t clc_collect(uint4 *result, uint64_t *bar, uint32_t &phase, int *status) {
+  const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  const uint64_t t0 = ptx::globaltimer_ns();
+  uint32_t done = 0;
+  for (uint32_t polls = 0; !done; ++polls) {
+    asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(done)
+                 : "r"(b), "r"(phase)
+                 : "memory");
+    if (!done && (polls & 255u) == 255u && ptx::globaltimer_ns() - t0 > kWaitBudgetNs) {
+      report_status(status, kStatusClcTimeout);
+      return ~0u;
+    }
+  }
+  phase ^= 1u;
+  uint32_t x = ~0u;
+  const uint32_t res = static_cast<uint32_t>(__cvta_generic_to_shared(result));
+  asm volatile(
+      "{\n.reg .pred p;\n.reg .b128 h;\n"
+      "ld.shared.b128 h, [%1];\n"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, h;\n"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %0, h;\n"
+      "}\n"
+      : "+r"(x)
+      : "r"(res)
+      : "memory");
+  return x;
+}
+
+__global__ void __launch_bounds__(128) clc_probe(const ClcArgs a) {
+  __shared__ uint4 result;
+  __shared__ uint64_t bar;
+  __shared__ uint32_t next;
+  const int c = blockIdx.x;
+  if (threadIdx.x == 0) a.smid[c] = ptx::smid();
+  if (a.mode == 0) {
+    for (int t = c; t < a.n_tasks; t += gridDim.x) clc_body(a, t);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  uint32_t phase = 0, nrec = 0;
+  uint32_t t = c;
+  while (t < (uint32_t)a.n_tasks) {
+    if (a.mode == 2 && threadIdx.x == 0) clc_issue(&result, &bar);  // reserve the next task now
+    clc_body(a, (int)t);
+    if (threadIdx.x == 0) {
+      if (a.mode == 1) clc_issue(&result, &bar);  // late binding: claim only when free
+      const long long w0 = clock64();
+      const uint32_t x = clc_collect(&result, &bar, phase, a.status);
+      const unsigned long long waited = (unsigned long long)(clock64() - w0);
+      if (nrec < (uint32_t)a.max_rec) a.rec[(size_t)c * a.max_rec + nrec] = (waited << 32) | x;
+      ++nrec;
+      next = x;
+    }
+    __syncthreads();
+    t = next;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) a.n_rec[c] = nrec;
+}
+
 // ---------------------------------------------------------------- mix
 __device__ __forceinline__ uint4 ld_plain(const uint4 *a) {
   uint4 v;
@@ -254,6 +369,26 @@ extern "C" int sched_probe_tasks(const uint32_t *cost, int n_tasks, int mode, in
   const int g = mode == 2 ? n_tasks : grid;
   if (g <= 0) return -1;
   probe::task_probe<<<g, 128, 0, st>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int sched_probe_clc(const uint32_t *work, int n_tasks, int mode, int grid, int max_rec, unsigned *hits,
+                               unsigned long long *rec, unsigned *n_rec, unsigned *smid, int *status,
+                               cudaStream_t st) {
+  if (n_tasks <= 0 || mode < 0 || mode > 2 || max_rec <= 0) return -1;
+  probe::ClcArgs a{};
+  a.work = work;
+  a.n_tasks = n_tasks;
+  a.mode = mode;
+  a.max_rec = max_rec;
+  a.hits = hits;
+  a.rec = rec;
+  a.n_rec = n_rec;
+  a.smid = smid;
+  a.status = status;
+  const int g = mode == 0 ? grid : n_tasks;
+  if (g <= 0) return -1;
+  probe::clc_probe<<<g, 128, 0, st>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

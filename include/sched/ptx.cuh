@@ -73,6 +73,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)::"memory");
   return t;
 }
+__device__ __forceinline__ uint32_t smid() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
 // Bounded wait: true once the phase with `parity` has completed, false when
 // `budget_ns` of wall time (the %globaltimer clock) has passed without it.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,

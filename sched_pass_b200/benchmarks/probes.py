@@ -15,6 +15,13 @@
   0.125 to 1: is L2 residency a continuous per-request budget?
 * ``pdl``: producer -> consumer pairs with and without programmatic stream
   serialization, consumer prologue 0 / 256 FMAs; us per pair.
+* ``clc``: cluster launch control as the CTAs see it (one CTA per task):
+  cycles a CTA waits for a successful claim's answer (late bound: the claim
+  issued after the body), exactly one failed claim per worker and exactly-once
+  coverage, the number of workers against the resident prefix R, and the
+  makespan of static / CLC late-bound / CLC claim-ahead on uniform,
+  long-suffix, long-prefix and interleaved layouts (8192 tasks of 1024
+  cycles, a quarter 32x longer).
 
     python -m sched_pass_b200.benchmarks.probes [--only stream|tasks|reuse|budget|pdl]
 """
@@ -180,9 +187,105 @@ def pdl(n: int = 148 * 256 * 4, pairs: int = 200):
     return res
 
 
+CLC_MODES = ["static", "clc_late", "clc_ahead"]
+
+
+def clc_layout(n: int, base: int, name: str, long_frac: float = 0.25, factor: int = 32) -> np.ndarray:
+    """Per-task body cycles: uniform, or a quarter of the tasks ``factor``x
+    longer at the end (long-suffix), the start (long-prefix) or every
+    fourth task (interleaved)."""
+    w = np.full(n, base, dtype=np.int64)
+    k = int(n * long_frac)
+    if name == "long_suffix":
+        w[n - k:] *= factor
+    elif name == "long_prefix":
+        w[:k] *= factor
+    elif name == "interleaved":
+        w[::int(round(1 / long_frac))] *= factor
+    elif name != "uniform":
+        raise ValueError(name)
+    return w.astype(np.int32)
+
+
+def run_clc(work: np.ndarray, mode: int, R: int, max_rec: int = 16):
+    """One probe launch; returns (ms, hits, rec [grid, max_rec] int64, n_rec, smid)."""
+    n = work.size
+    grid = R if mode == 0 else n
+    w = torch.from_numpy(work).cuda()
+    hits = torch.zeros(n, dtype=torch.int32, device="cuda")
+    rec = torch.zeros(grid, max_rec, dtype=torch.int64, device="cuda")
+    n_rec = torch.zeros(grid, dtype=torch.int32, device="cuda")
+    smid = torch.full((grid,), -1, dtype=torch.int32, device="cuda")
+    st = ops.status_buffer()
+
+    def go():
+        hits.zero_()
+        n_rec.zero_()
+        ext().probe_clc(w, mode, grid, hits, rec, n_rec, smid, st)
+    ms = _time(go)
+    go()
+    torch.cuda.synchronize()
+    ops.check_status()
+    return ms, hits.cpu().numpy(), rec.cpu().numpy(), n_rec.cpu().numpy(), smid.cpu().numpy()
+
+
+def clc_claims(rec: np.ndarray, n_rec: np.ndarray):
+    """Per worker (a CTA that ran): its claims as (waited cycles, value)."""
+    out = {}
+    for c in np.flatnonzero(n_rec > 0):
+        k = min(int(n_rec[c]), rec.shape[1])
+        r = rec[c, :k].astype(np.uint64)
+        out[int(c)] = [(int(x >> np.uint64(32)), int(x & np.uint64(0xFFFFFFFF))) for x in r]
+    return out
+
+
+def clc(n: int = 8192, base: int = 1024):
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    occ = int(ext().probe_tasks_occupancy())
+    R = occ * sms
+    FAIL = 0xFFFFFFFF
+    # claim latency and the terminal-failure rule on uniform work
+    _, hits, rec, n_rec, smid = run_clc(clc_layout(n, base, "uniform"), 1, R)
+    claims = clc_claims(rec, n_rec)
+    ok_wait = sorted(w for cl in claims.values() for w, x in cl if x != FAIL)
+    terminal = [sum(1 for _, x in cl if x == FAIL) for cl in claims.values()]
+    last_is_fail = all(cl and cl[-1][1] == FAIL for cl in claims.values())
+    claimed = sorted(x for cl in claims.values() for _, x in cl if x != FAIL)
+    pct = lambda v, q: int(v[min(len(v) - 1, int(q * len(v)))]) if v else None  # noqa: E731
+    rec_out = {"probe": "clc_claims", "tasks": n, "R": R, "workers": len(claims),
+               "successes": len(claimed), "expected_successes": max(0, n - len(claims)),
+               "failures_per_worker_min": min(terminal), "failures_per_worker_max": max(terminal),
+               "failure_is_last_claim": last_is_fail,
+               "every_task_once": bool((hits == 1).all()), "claims_unique": len(set(claimed)) == len(claimed),
+               "claim_wait_cycles_p50": pct(ok_wait, 0.5), "claim_wait_cycles_p90": pct(ok_wait, 0.9),
+               "claim_wait_cycles_p99": pct(ok_wait, 0.99),
+               "distinct_sms": int(len(set(int(s) for s in smid[n_rec > 0])))}
+    print(json.dumps(rec_out), flush=True)
+    # placement: static vs late-bound vs claim-ahead
+    for layout in ("uniform", "long_suffix", "long_prefix", "interleaved"):
+        work = clc_layout(n, base, layout)
+        row = {"probe": "clc_placement", "layout": layout, "tasks": n, "body_cycles": base}
+        for mode, name in enumerate(CLC_MODES):
+            ms, hits, rec, n_rec, _ = run_clc(work, mode, R)
+            row[name + "_us"] = round(ms * 1e3, 2)
+            row[name + "_exactly_once"] = bool((hits == 1).all())
+            if mode == 2:
+                cl = clc_claims(rec, n_rec)
+                waits = sorted(w for c in cl.values() for w, x in c if x != FAIL)
+                row["clc_ahead_collect_wait_p50"] = pct(waits, 0.5)
+            if mode == 1:
+                cl = clc_claims(rec, n_rec)
+                waits = sorted(w for c in cl.values() for w, x in c if x != FAIL)
+                row["clc_late_claim_wait_p50"] = pct(waits, 0.5)
+        st = row["static_us"]
+        row["late_vs_static"] = round(row["clc_late_us"] / st - 1, 4)
+        row["ahead_vs_static"] = round(row["clc_ahead_us"] / st - 1, 4)
+        print(json.dumps(row), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", choices=["stream", "tasks", "reuse", "budget", "pdl"])
+    ap.add_argument("--only", choices=["stream", "tasks", "reuse", "budget", "pdl", "clc"])
     a = ap.parse_args(argv)
     if a.only in (None, "stream"):
         stream()
@@ -194,6 +297,8 @@ def main(argv=None):
         budget()
     if a.only in (None, "pdl"):
         pdl()
+    if a.only in (None, "clc"):
+        clc()
 
 
 if __name__ == "__main__":

@@ -76,3 +76,28 @@ def test_mix_probe_runs(mode):
     torch.cuda.synchronize()
     with pytest.raises(RuntimeError):
         ext().probe_mix(R, S, 1, 0.0, sink, sms * 4)  # fraction outside (0, 1]
+
+
+def test_clc_terminal_failure_rule_and_exactly_once():
+    """Cluster launch control, one CTA per task, late-bound claims: every
+    task runs exactly once, every worker (a CTA that launched) ends with
+    exactly one failed claim and no failure before it, claimed ids are
+    unique, and successes = tasks - workers (each worker ran its own task
+    first); the same holds with the claim issued ahead of the body."""
+    import numpy as np
+
+    from sched_pass_b200.benchmarks import probes
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    R = int(ext().probe_tasks_occupancy()) * sms
+    n = 4 * R
+    for mode in (1, 2):
+        _, hits, rec, n_rec, _ = probes.run_clc(probes.clc_layout(n, 1500, "interleaved"), mode, R, max_rec=64)
+        assert (hits == 1).all(), mode
+        claims = probes.clc_claims(rec, n_rec)
+        assert (n_rec <= 64).all()
+        fails = [[x for _, x in cl].count(0xFFFFFFFF) for cl in claims.values()]
+        assert set(fails) == {1}, (mode, set(fails))
+        assert all(cl[-1][1] == 0xFFFFFFFF for cl in claims.values())
+        got = [x for cl in claims.values() for _, x in cl if x != 0xFFFFFFFF]
+        assert len(got) == len(set(got)) == n - len(claims), (mode, len(got), len(claims))
+        assert len(claims) <= n and len(claims) >= min(n, R // 2)

@@ -78,7 +78,8 @@ def test_sp_sublayer_matches_the_allreduce_arithmetic(W):
     st = ops.status_buffer()
     lnw = (1 + 0.1 * torch.randn(H, device="cuda")).to(torch.bfloat16)
     w2 = (torch.randn(384, H, device="cuda") / math.sqrt(H)).to(torch.bfloat16)
-    for call, T in enumerate([37, 300, 5, 16, 300]):  # second use of each set; shrinking and growing T
+    # second use of each set; shrinking and growing T; fewer rows than ranks (T = 1, 2)
+    for call, T in enumerate([37, 300, 5, 1, 16, 2, 300]):
         g = call % 2
         xs = [torch.randn(T, K, device="cuda").to(torch.bfloat16) for _ in range(W)]
         wts = [(torch.randn(H, K, device="cuda") / math.sqrt(K * W)).to(torch.bfloat16) for _ in range(W)]
