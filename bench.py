@@ -233,9 +233,12 @@ def main(argv=None):
     wall0 = time.time()
     t_host0 = time.perf_counter()
     steps = 0
+    host_ms = []
     for i in range(args.steps):
         events[i].record(stream)
+        h0 = time.perf_counter()
         r = one_step()
+        host_ms.append(1e3 * (time.perf_counter() - h0))
         if r is None:
             break
         plan, done = r
@@ -262,6 +265,12 @@ def main(argv=None):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_s, host_s, per_step = float(t[0]), float(t[1]), t[2:].tolist()
     w = window_tpot(produced, per_step)
+    fwd = [st.device_ms for st in eng.stats[first_stat:first_stat + steps]]
+    # steps whose interval on the device exceeds their forward by over 1 ms:
+    # [index, interval ms, forward ms, host ms of step_async, decode rows, prefill tokens]
+    outliers = [[i, round(1e3 * per_step[i], 3), round(fwd[i], 3), round(host_ms[i], 3), eng.stats[first_stat + i].n_decode,
+                 eng.stats[first_stat + i].n_prefill_tokens]
+                for i in range(min(steps, len(fwd))) if 1e3 * per_step[i] - fwd[i] > 1.0]
     fin_tpot = sorted(x for x in (q.tpot() for q in finished) if x is not None)
     step_ms = [st.device_ms for st in eng.stats[first_stat:]]
     value = decode_tokens / dev_s if dev_s > 0 else 0.0
@@ -313,6 +322,7 @@ def main(argv=None):
                                if step_ms and sum(step_ms) > 0 else None),
         "host_gap_share": (round(max(0.0, 1.0 - (sum(step_ms) / 1e3) / dev_s), 4)
                            if step_ms and dev_s > 0 else None),
+        "gap_steps": outliers[:8],
         "e2e": {"value": round(e2e, 2), "unit": "decode tokens/s", "h2d_bytes_per_step": eng.packed_len * 4,
                 "d2h_bytes_per_step": round(d2h / max(steps, 1), 1)},
         "gpu_launches": int(launches),

@@ -183,18 +183,28 @@ void gemm_qkv_rope(const at::Tensor &x, const at::Tensor &w, const at::Tensor &p
 
 // Row-parallel projection with the all-reduce fused into the GEMM epilogue.
 // recv/flags: this process's addresses of every rank's slab and flag array.
+// ll_state (int32 [2] on this device) selects the low-latency exchange:
+// recv then holds every rank's line buffer (two sets of ll_set_lines
+// 16-byte lines) and flags is ignored.
 void gemm_allreduce(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int64_t rank,
                     int64_t world, const std::vector<int64_t> &recv,
                     const std::vector<int64_t> &flags, int64_t grid,
                     const c10::optional<at::Tensor> &ws,
                     const c10::optional<at::Tensor> &counters,
-                    const c10::optional<at::Tensor> &status) {
+                    const c10::optional<at::Tensor> &status,
+                    const c10::optional<at::Tensor> &ll_state, int64_t ll_set_lines) {
   GemmArgs a = base_args(x, w, grid, ws, counters, status);
   check_bf16(y, "y");
   TORCH_CHECK(y.dim() == 2 && y.stride(1) == 1 && y.size(1) >= a.N, "y [T, >= N]");
+  const bool ll = ll_state.has_value() && ll_state->defined();
   TORCH_CHECK(world >= 1 && world <= kMaxWorld && (int64_t)recv.size() == world &&
-                  (int64_t)flags.size() == world,
+                  (ll || (int64_t)flags.size() == world),
               "one slab and one flag array per rank");
+  if (ll) {
+    check_i32(*ll_state, "ll_state");
+    TORCH_CHECK(ll_state->numel() >= 2 && ll_state->device() == x.device(), "ll_state: int32 [2] on x's device");
+    TORCH_CHECK(ll_set_lines >= world * a.T * (a.N / 4), "line buffer too small for [world, T, N/4] lines");
+  }
   a.y = y.data_ptr();
   a.ldy = y.stride(0);
   a.epi = kEpiAllReduce;
@@ -202,7 +212,11 @@ void gemm_allreduce(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int
   a.world = world;
   for (int j = 0; j < world; ++j) {
     a.recv[j] = reinterpret_cast<__nv_bfloat16 *>(recv[j]);
-    a.flags[j] = reinterpret_cast<uint32_t *>(flags[j]);
+    a.flags[j] = ll ? nullptr : reinterpret_cast<uint32_t *>(flags[j]);
+  }
+  if (ll) {
+    a.ll_state = reinterpret_cast<uint32_t *>(ll_state->data_ptr<int32_t>());
+    a.ll_set_lines = ll_set_lines;
   }
   c10::cuda::CUDAGuard g(x.device());
   check_rc(sched_gemm_run(&a, cur_stream()), "gemm_allreduce");

@@ -244,7 +244,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int32_t *bt = p.block_table + (size_t)ti.req * p.bt_stride;
         const int first_page = ti.kv_begin / PS;  // kv_begin is block-aligned
         const int last_page = (ti.kv_end + PS - 1) / PS;
+        // The page ids of a block are loaded together (independent loads, so
+        // their latencies overlap) and one block ahead of its TMA issue, so
+        // the block-table reads hide behind the wait for a free stage
+        // instead of adding eight load latencies to every block.
+        int ids_next[PAGES_PER_BLK];
+        auto load_ids = [&](int b, int *ids) {
+          const int pg0 = first_page + b * PAGES_PER_BLK;
+          const int npg = min(PAGES_PER_BLK, last_page - pg0);
+#pragma unroll
+          for (int pi = 0; pi < PAGES_PER_BLK; ++pi) ids[pi] = pi < npg ? __ldg(bt + pg0 + pi) : -1;
+        };
+        if (ti.nblk > 0) load_ids(0, ids_next);
         for (int b = 0; b < ti.nblk; ++b, ++blk_counter) {
+          int ids[PAGES_PER_BLK];
+#pragma unroll
+          for (int pi = 0; pi < PAGES_PER_BLK; ++pi) ids[pi] = ids_next[pi];
+          if (b + 1 < ti.nblk) load_ids(b + 1, ids_next);
           const int s = blk_counter % STAGES;
           const uint32_t ph = (blk_counter / STAGES) & 1;
           if (!ptx::mbar_wait(&sh.kv_empty[s], ph ^ 1, kWaitBudgetNs)) {
@@ -258,10 +274,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int npg = min(PAGES_PER_BLK, last_page - pg0);
           ptx::mbar_arrive_expect_tx(&sh.k_full[s], KV_BLOCK_BYTES);
           ptx::mbar_arrive_expect_tx(&sh.v_full[s], KV_BLOCK_BYTES);
+#pragma unroll
           for (int pi = 0; pi < PAGES_PER_BLK; ++pi) {
             // pages past the request's end: an out-of-range box reads zeros;
             // ids from stage_split on live in the staging pool (tiered KV)
-            int page = pi < npg ? __ldg(bt + pg0 + pi) : -1;
+            int page = ids[pi];
             if (pi < npg && !page_ok(p, page)) {  // reported; read as an out-of-range (zero) box
               report_bad_index(p.status, kSiteDecodePage, page);
               page = -1;

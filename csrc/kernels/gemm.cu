@@ -129,9 +129,17 @@ __device__ __forceinline__ bool segment(const Params &p, int c, int k, Seg &s) {
 
 // Epilogue writer: token row v[0..127] (fp32, shared memory) of tile
 // (n_tile, token t); thread k of 8 writes its share.
+// A low-latency all-reduce line: 8 bytes of payload (two bf16x2 words) and
+// the call's epoch beside each, in one 16-byte store. Each 8-byte half lands
+// whole, so a reader that sees the epoch in a half has that half's payload.
+__device__ __forceinline__ void st_ll(uint4 *dst, uint32_t d0, uint32_t d1, uint32_t e) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(d0), "r"(e), "r"(d1), "r"(e)
+               : "memory");
+}
+
 template <int EPI>
 __device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, const float *v,
-                                          int k) {
+                                          int k, uint32_t ll_e = 0) {
   if (EPI == kEpiStore) {
     const int c = k * 16;
     uint4 o0, o1;
@@ -171,7 +179,17 @@ __device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, 
     o1.z = pack_bf16x2(v[c + 12], v[c + 13]);
     o1.w = pack_bf16x2(v[c + 14], v[c + 15]);
     const size_t off = ((size_t)a.rank * a.T + t) * a.N + (size_t)n_tile * BM + c;
-    if (EPI == kEpiAllReduce) {
+    if (EPI == kEpiAllReduce && a.ll_state != nullptr) {
+      // low-latency lines into every rank's buffer (set of this call's epoch)
+      const size_t line = (size_t)(ll_e & 1u) * a.ll_set_lines + off / 4;
+      for (int j = 0; j < a.world; ++j) {
+        uint4 *dst = reinterpret_cast<uint4 *>(a.recv[j]) + line;
+        st_ll(dst, o0.x, o0.y, ll_e);
+        st_ll(dst + 1, o0.z, o0.w, ll_e);
+        st_ll(dst + 2, o1.x, o1.y, ll_e);
+        st_ll(dst + 3, o1.z, o1.w, ll_e);
+      }
+    } else if (EPI == kEpiAllReduce) {
       for (int j = 0; j < a.world; ++j) {  // NVLink stores into every rank's slab
         uint4 *dst = reinterpret_cast<uint4 *>(a.recv[j] + off);
         dst[0] = o0;
@@ -423,6 +441,97 @@ __device__ void reduce_owned_chunks(const Params &p, int c, int et) {
   }
 }
 
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The epoch of this call (low-latency exchange): every CTA reads the same
+// value, since only the call's last CTA advances it (ll_finish).
+__device__ __forceinline__ uint32_t ll_epoch(const GemmArgs &a) {
+  return a.ll_state != nullptr ? ld_volatile_u32(a.ll_state) + 1u : 0u;
+}
+
+// Called by one thread of every CTA after its last read of the line buffer:
+// the last CTA of the launch resets the counter and advances the epoch
+// (skipping 0 on wrap-around, so a never-written line never matches).
+__device__ __forceinline__ void ll_finish(const GemmArgs &a) {
+  __threadfence();
+  if (atomicAdd(a.ll_state + 1, 1u) == gridDim.x - 1) {
+    a.ll_state[1] = 0u;
+    const uint32_t e = ld_volatile_u32(a.ll_state) + 1u;
+    __threadfence();
+    a.ll_state[0] = e == 0xFFFFFFFFu ? 1u : e;
+  }
+}
+
+// All-reduce, part 2 of the low-latency exchange: the same owned units and
+// rank-order sums as reduce_owned_chunks, but each thread polls its own four
+// lines per source until they carry the call's epoch (bounded), with no
+// flags, fences or block barriers.
+template <int TN>
+__device__ void reduce_owned_chunks_ll(const Params &p, int c, int et, uint32_t e) {
+  const GemmArgs &a = p.a;
+  constexpr int CH = TN / kSlab;
+  const uint4 *mine = reinterpret_cast<const uint4 *>(a.recv[a.rank]) + (size_t)(e & 1u) * a.ll_set_lines;
+  const int units = p.tiles * CH;
+  const int tl = et / 8, col = (et % 8) * 16;
+  for (int u = c; u < units; u += p.grid) {
+    const int tile = u / CH, ch = u % CH;
+    const int nt = tile / p.t_tiles, tt = tile % p.t_tiles;
+    const int t0 = tt * TN + ch * kSlab;
+    if (t0 >= a.T || tl >= min(kSlab, a.T - t0)) continue;
+    const int t = t0 + tl;
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+    for (int src = 0; src < a.world; ++src) {
+      const uint4 *q = mine + (((size_t)src * a.T + t) * a.N + (size_t)nt * BM + col) / 4;
+      uint4 l[4];
+      bool ok = false;
+      uint64_t start = 0;
+      for (uint32_t polls = 0; !ok; ++polls) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) l[i] = ld_volatile_v4(reinterpret_cast<const uint32_t *>(q + i));
+        ok = true;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ok = ok && l[i].y == e && l[i].w == e;
+        if (!ok && (polls & 63u) == 0u) {
+          const uint64_t now = ptx::globaltimer_ns();
+          if (start == 0) start = now;
+          else if (now - start > kWaitBudgetNs) {
+            report_status(a.status, kStatusPeerTimeout);
+            break;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat16 *lo = reinterpret_cast<const __nv_bfloat16 *>(&l[i].x);
+        const __nv_bfloat16 *hi = reinterpret_cast<const __nv_bfloat16 *>(&l[i].z);
+        acc[4 * i] += __bfloat162float(lo[0]);
+        acc[4 * i + 1] += __bfloat162float(lo[1]);
+        acc[4 * i + 2] += __bfloat162float(hi[0]);
+        acc[4 * i + 3] += __bfloat162float(hi[1]);
+      }
+    }
+    uint4 o0, o1;
+    o0.x = pack_bf16x2(acc[0], acc[1]);
+    o0.y = pack_bf16x2(acc[2], acc[3]);
+    o0.z = pack_bf16x2(acc[4], acc[5]);
+    o0.w = pack_bf16x2(acc[6], acc[7]);
+    o1.x = pack_bf16x2(acc[8], acc[9]);
+    o1.y = pack_bf16x2(acc[10], acc[11]);
+    o1.z = pack_bf16x2(acc[12], acc[13]);
+    o1.w = pack_bf16x2(acc[14], acc[15]);
+    uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(a.y) + (size_t)t * a.ldy +
+                                           (size_t)nt * BM + col);
+    dst[0] = o0;
+    dst[1] = o1;
+  }
+}
+
 template <int TN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
@@ -555,6 +664,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;         // accumulator row = weight row in the tile
     const int tj = et / 8, part = et % 8;  // slab token / writer share
     ptx::pdl_wait();
+    const uint32_t ll_e = EPI == kEpiAllReduce ? ll_epoch(a) : 0u;  // low-latency exchange: this call's epoch
+    const bool ll = EPI == kEpiAllReduce && a.ll_state != nullptr;
     Seg s;
     for (int k = 0; segment(p, c, k, s); ++k) {
       const int ab = k & 1;
@@ -581,7 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 16; ++j) slab[j * kSlabPitch + row] = __uint_as_float(r[j]);
           named_bar(1, kEpiThreads);
           const int t = t0 + ch * kSlab + tj;
-          if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part);
+          if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part, ll_e);
           named_bar(1, kEpiThreads);
         } else {
           // partial slice [TN tokens][128 rows]: a warp stores 32 consecutive rows
@@ -592,7 +703,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(&acc_empty[ab]);  // the MMA warp may refill this accumulator
-      if (EPI == kEpiAllReduce && direct) publish_tile<TN>(p, s.tile, et);
+      if (EPI == kEpiAllReduce && direct && !ll) publish_tile<TN>(p, s.tile, et);
       if (EPI == kEpiReduceScatter && direct) publish_rows_rs<TN>(p, s.tile, 0, min(TN, a.T - t0), et);
       if (!direct) {
         __threadfence();
@@ -644,11 +755,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) slab[tj * kSlabPitch + part * 16 + j] = acc[j];
             named_bar(1, kEpiThreads);
-            if (tl < tmax) write_row<EPI>(a, nt, t0 + tl, slab + tj * kSlabPitch, part);
+            if (tl < tmax) write_row<EPI>(a, nt, t0 + tl, slab + tj * kSlabPitch, part, ll_e);
             named_bar(1, kEpiThreads);
           }
           if (et == 0) a.counters[s.tile] = 0u;
-          if (EPI == kEpiAllReduce) publish_tile<TN>(p, s.tile, et);
+          if (EPI == kEpiAllReduce && !ll) publish_tile<TN>(p, s.tile, et);
           if (EPI == kEpiReduceScatter) publish_rows_rs<TN>(p, s.tile, 0, tmax, et);
         }
         named_bar(1, kEpiThreads);  // last_flag is rewritten by the next segment
@@ -659,7 +770,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       a.trace[c * 4 + 1] += te & 0xffffffffull;  // epilogue done (low 32 bits)
       *reinterpret_cast<volatile unsigned long long *>(slab) = te;
     }
-    if (EPI == kEpiAllReduce) reduce_owned_chunks<TN>(p, c, et);
+    if (EPI == kEpiAllReduce) {
+      if (ll)
+        reduce_owned_chunks_ll<TN>(p, c, et, ll_e);
+      else
+        reduce_owned_chunks<TN>(p, c, et);
+    }
   }
 
   // the producer and MMA warps ran their role on one elected lane: reconverge
@@ -674,6 +790,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (te > tp) a.trace[c * 4 + 0] = 0;  // marks a barrier that did not order the epilogue
   }
   if (warp == 0) ptx::tmem_dealloc(tmem, C::TMEM_COLS);
+  if (EPI == kEpiAllReduce && a.ll_state != nullptr && threadIdx.x == 0) ll_finish(a);
   if (a.trace && threadIdx.x == 0) a.trace[c * 4 + 3] = ptx::globaltimer_ns();
 }
 
@@ -820,6 +937,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const int tj = et / 8, part = et % 8;
     ptx::pdl_wait();
+    const uint32_t ll_e = EPI == kEpiAllReduce ? ll_epoch(a) : 0u;
+    const bool ll = EPI == kEpiAllReduce && a.ll_state != nullptr;
     const uint32_t red_addr = ptx::smem_u32(red);
     const uint32_t ready_addr = ptx::smem_u32(red_ready), free_addr = ptx::smem_u32(red_free);
     int j = 0;
@@ -841,12 +960,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int jj = 0; jj < 16; ++jj) slab[jj * kSlabPitch + row] = waited ? __uint_as_float(r[jj]) : 0.f;
           named_bar(1, kEpiThreads);
           const int t = t0 + ch * kSlab + tj;
-          if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part);
+          if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part, ll_e);
           named_bar(1, kEpiThreads);
         }
         ptx::tc_fence_before();
         ptx::mbar_arrive(&acc_empty[ab]);
-        if (EPI == kEpiAllReduce) publish_rows<TN>(p, tile, 0, tvalid, et);
+        if (EPI == kEpiAllReduce && !ll) publish_rows<TN>(p, tile, 0, tvalid, et);
         if (EPI == kEpiReduceScatter) publish_rows_rs<TN>(p, tile, 0, tvalid, et);
         continue;
       }
@@ -900,23 +1019,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) slab[tj * kSlabPitch + part * 16 + jj] = acc[jj];
         named_bar(1, kEpiThreads);
-        if (tl < hi) write_row<EPI>(a, nt, t0 + tl, slab + tj * kSlabPitch, part);
+        if (tl < hi) write_row<EPI>(a, nt, t0 + tl, slab + tj * kSlabPitch, part, ll_e);
         named_bar(1, kEpiThreads);
       }
       // every peer's partial has been read: release them
       named_bar(1, kEpiThreads);
       if (et == 0)
         for (int s2 = 0; s2 < CS; ++s2) ptx::mbar_arrive_cluster(ptx::mapa_shared(free_addr, s2));
-      if (EPI == kEpiAllReduce) publish_rows<TN>(p, tile, lo, hi, et);
+      if (EPI == kEpiAllReduce && !ll) publish_rows<TN>(p, tile, lo, hi, et);
       if (EPI == kEpiReduceScatter) publish_rows_rs<TN>(p, tile, lo, hi, et);
     }
-    if (EPI == kEpiAllReduce) reduce_owned_chunks<TN>(p, blockIdx.x, et);
+    if (EPI == kEpiAllReduce) {
+      if (ll)
+        reduce_owned_chunks_ll<TN>(p, blockIdx.x, et, ll_e);
+      else
+        reduce_owned_chunks<TN>(p, blockIdx.x, et);
+    }
   }
 
   __syncwarp();
   ptx::tc_fence_before();
   ptx::cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
   if (warp == 0) ptx::tmem_dealloc(tmem, C::TMEM_COLS);
+  if (EPI == kEpiAllReduce && a.ll_state != nullptr && threadIdx.x == 0) ll_finish(a);
   if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4 + 3] = ptx::globaltimer_ns();
 }
 
@@ -1223,8 +1348,13 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   if (a.x_ready != nullptr && (reinterpret_cast<uintptr_t>(a.x_ready) & 15) != 0) return -7;
   if (a.epi == kEpiAllReduce || a.epi == kEpiReduceScatter) {
     if (a.world < 1 || a.world > kMaxWorld || a.rank < 0 || a.rank >= a.world) return -7;
-    for (int j = 0; j < a.world; ++j)
-      if (a.recv[j] == nullptr || a.flags[j] == nullptr) return -7;
+    const bool ll = a.epi == kEpiAllReduce && a.ll_state != nullptr;
+    for (int j = 0; j < a.world; ++j) {
+      if (a.recv[j] == nullptr || (a.flags[j] == nullptr && !ll)) return -7;
+      if (ll && (reinterpret_cast<uintptr_t>(a.recv[j]) & 15) != 0) return -7;
+    }
+    // the low-latency line buffer holds [world][T][N / 4] lines per set
+    if (ll && a.ll_set_lines < (long long)a.world * a.T * (a.N / 4)) return -7;
   }
   try {
     CUtensorMap tw = tmap::make_2d(a.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.K,

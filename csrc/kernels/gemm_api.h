@@ -76,6 +76,15 @@ struct GemmArgs {
   // (sched_sp_reduce_norm's all-gather push). Must be 16-byte aligned and
   // readable up to T rounded up to a multiple of 4.
   const uint32_t *x_ready;
+  // kEpiAllReduce, low-latency exchange (ll_state != nullptr; decode sizes):
+  // recv[j] is rank j's line buffer of two sets, each [world][T][N / 4]
+  // 16-byte lines {bf16x2, epoch, bf16x2, epoch} (ll_set_lines lines per set),
+  // and `flags` is unused. ll_state is this rank's [epoch, done] pair (u32,
+  // zero before the first call): a call uses epoch + 1 and set (epoch + 1) & 1,
+  // the last CTA to finish advances the epoch. Readers poll the lines until
+  // both halves carry the call's epoch, so no fence, flag or reset is needed.
+  uint32_t *ll_state;
+  long long ll_set_lines;
 };
 
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream);

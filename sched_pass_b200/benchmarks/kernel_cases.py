@@ -10,6 +10,12 @@ a few hundred MB on the device at most).
                    (Llama-3-8B heads: 32 query / 8 KV, head_dim 128)
   --case sample    embedding gather (T tokens) and greedy argmax over the
                    128256-entry vocabulary
+  --case decode    the serving engine's decode attention launch for a small
+                   batch (``--batch`` requests of ``--context`` tokens, 32
+                   query / ``--kv-heads`` KV heads, pages scattered over a
+                   pool larger than L2): KV split the way the engine splits it
+                   (tasks up to one per SM), in-kernel merge, levers woven
+                   with neutral tables, cluster launch control grid
 
 Prints one JSON line per case with the median device time (CUDA events,
 after warm-up) and the algorithmic bytes / FLOPs per launch.
@@ -123,15 +129,56 @@ def case_sample(args, peaks):
                       "argmax_GBps": round(128 * V * 2 / (ms_a * 1e-3) / 1e9, 1)}))
 
 
+def case_decode(args, peaks):
+    import numpy as np
+
+    from ..engine import native
+    from ..runtime.sched_rt import SchedPlane
+    B, ctx, Hq, Hkv, D = args.batch, args.context, 32, args.kv_heads, 128
+    dev = "cuda"
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    S = int(min(8, max(1, sms // (B * Hkv))))  # the engine's split rule (Engine.splits_for)
+    pool = max(4096, 2 * B * (ctx + 15) // 16)  # pages: K + V pools of ~256 MB, above L2
+    kc = torch.randn(pool, Hkv, 16, D, device=dev).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    npg = (ctx + 15) // 16
+    bt = torch.randperm(pool, device=dev)[: B * npg].to(torch.int32).view(B, npg)
+    lens = np.full(B, ctx, dtype=np.int32)
+    items, _, _ = native.plan_decode(lens, S)
+    items_t = torch.from_numpy(items).to(dev)
+    q = torch.randn(B, Hq, D, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    part_o = torch.zeros(B * S, Hq, D, dtype=torch.float32, device=dev)
+    part_lse = torch.zeros(B * S, Hq, dtype=torch.float32, device=dev)
+    merge_cnt = torch.zeros(B * Hkv, dtype=torch.int32, device=dev)
+    plane = SchedPlane(max_tasks=max(64, items.shape[0] * Hkv), device=dev, mode="device")
+    plane.push()
+    n_items = items.shape[0]
+    fn = lambda: ops.attention_decode(q, out, kc, vc, bt, items_t, n_items, 1 / math.sqrt(D),  # noqa: E731
+                                      part_o=part_o if S > 1 else None, part_lse=part_lse if S > 1 else None,
+                                      merge_cnt=merge_cnt if S > 1 else None, splits=S, slots=plane.slots(),
+                                      woven=True, acquire=2, grid=n_items * Hkv)
+    ms = events_ms(fn, args.reps)
+    ops.check_status()
+    kv = B * ctx * Hkv * D * 2 * 2
+    print(json.dumps({"case": "decode", "batch": B, "context": ctx, "kv_heads": Hkv, "splits": S,
+                      "tasks": n_items * Hkv, "us": round(ms * 1e3, 2), "kv_MB": round(kv / 1e6, 1),
+                      "frac_hbm_of_measured": round(kv / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", default="sp_norm", choices=["sp_norm", "prefill", "sample"])
+    ap.add_argument("--case", default="sp_norm", choices=["sp_norm", "prefill", "sample", "decode"])
+    ap.add_argument("--batch", type=int, default=6)
+    ap.add_argument("--context", type=int, default=1536)
+    ap.add_argument("--kv-heads", type=int, default=8)
     ap.add_argument("--world", type=int, default=2)
     ap.add_argument("--tokens", type=int, default=256)
     ap.add_argument("--reps", type=int, default=5)
     args = ap.parse_args()
     peaks = measured_peaks()
-    {"sp_norm": case_sp_norm, "prefill": case_prefill, "sample": case_sample}[args.case](args, peaks)
+    {"sp_norm": case_sp_norm, "prefill": case_prefill, "sample": case_sample,
+     "decode": case_decode}[args.case](args, peaks)
 
 
 if __name__ == "__main__":

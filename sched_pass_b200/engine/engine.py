@@ -24,6 +24,7 @@ from __future__ import annotations
 import math
 import os
 import time
+import weakref
 from collections import deque
 from dataclasses import dataclass, field
 
@@ -93,6 +94,17 @@ class EngineConfig:
 
 
 PENDING = -1  # placeholder of a sampled token the host has not read back yet
+
+
+def _weak_call(obj, name: str):
+    """A callable that calls ``obj.name(...)`` without keeping ``obj`` alive
+    (None once ``obj`` is gone)."""
+    ref = weakref.ref(obj)
+
+    def call(*args):
+        o = ref()
+        return getattr(o, name)(*args) if o is not None else None
+    return call
 
 
 @dataclass
@@ -180,7 +192,9 @@ class Engine:
         self.graphs: dict[int, tuple] = {}  # key -> (graph, splits, items, kernel launches it holds)
         self.graph_launches = 0  # kernel launches replayed from graphs (the extension counts the rest)
         self._inflight: deque = deque()  # steps enqueued whose tokens the host has not read yet
-        self.sched.before_preempt = self._before_preempt
+        # through a weak reference: the scheduler must not keep the engine (and
+        # its CUDA graphs, which may hold collectives) alive after its owner drops it
+        self.sched.before_preempt = _weak_call(self, "_before_preempt")
         self._pool = None
         self.stats: list[StepStats] = []
         self.clock = 0.0  # workload clock in seconds (device time + idle gaps)
@@ -243,9 +257,10 @@ class Engine:
         a fresh one that simulates the engine's decisions without a model)."""
         e = self.ecfg
         capped = e.max_step_tokens > 0
+        bucket = _weak_call(self, "_bucket")
         return Scheduler(e.num_pages, 16, e.max_batch, e.max_prefill_tokens, e.max_context, tier=tier,
                          max_step_tokens=e.max_step_tokens,
-                         round_decode=(lambda nd: self._bucket(nd) or nd) if capped else None,
+                         round_decode=(lambda nd: bucket(nd) or nd) if capped else None,
                          max_prefill_segments=MIXED_SEGMENTS if capped else 0,
                          prefix_cache=e.prefix_cache and tier is None and self.tier is None,
                          admission=e.admission if (e.admission != "lpm" or e.prefix_cache) else "fcfs")

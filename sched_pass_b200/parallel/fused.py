@@ -10,12 +10,23 @@ causally after the slow rank finished with it: the fast rank needs the slow
 rank's pushes of the intervening call first).
 
 Under CUDA graphs the sets alternate in capture order, so a replay reuses
-the sequence it was captured with. Two calls in a row on the same set are
-only safe after a cross-rank synchronisation: the engine's step ends with
-one (every rank waits for its step, then all-reduces the step time), and a
-graph that is replayed back to back must capture an even number of calls.
+the sequence it was captured with, and a graph that is replayed back to back
+must capture an even number of calls.
+
+Decode-sized calls (T <= ``ll_max_tokens``, ``SCHED_TP_LL_MAX``, default 32)
+use the low-latency exchange instead: the partial goes out as 16-byte lines
+that carry 8 bytes of bf16 and the call's epoch in each half, and the owner
+of a chunk polls the lines themselves, so no system-scope fence, flag store
+or flag reset sits between the GEMM and the reduction. The epoch lives in
+device memory (this rank's call counter, advanced by the last CTA of each
+call) and also picks which of two line-buffer sets a call uses, so graphs
+replay it without host bookkeeping. The rank-order fp32 sum is the same as
+the flag path's, bit for bit. The lines double the bytes on NVLink, which is
+why larger calls keep the flag path.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 
@@ -40,23 +51,47 @@ class FusedAllReduce:
         self.sets = [(SymmetricBuffer(slab, group), SymmetricBuffer(flags, group)) for _ in range(2)]
         self.k = 0
         self.calls = 0
+        # low-latency exchange: two sets of [world][ll_max_tokens][max_n / 4] 16-byte lines
+        self.ll_max_tokens = int(os.environ.get("SCHED_TP_LL_MAX", "32"))
+        self.ll_calls = 0
+        self._ll_last = False
+        if self.ll_max_tokens > 0:
+            self.ll_set_lines = self.world * self.ll_max_tokens * max_n // 4
+            self.ll = SymmetricBuffer(2 * self.ll_set_lines * 16, group)
+            self.ll_state = torch.zeros(2, dtype=torch.int32, device=self.device)  # epoch, done
+        else:
+            self.ll = None
 
     def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         T, K = x.shape
         N = w.shape[0]
         if T > self.max_tokens or N > self.max_n:
             raise ValueError(f"fused all-reduce sized for T<={self.max_tokens}, N<={self.max_n}")
-        slab, flags = self.sets[self.k]
-        self.k ^= 1
         self.calls += 1
         ws = ops.kernels._ws_for(x, N, K, 0, None)
+        if self.ll is not None and T <= self.ll_max_tokens:
+            self.ll_calls += 1
+            self._ll_last = True
+            ext().gemm_allreduce(x, w, out, self.rank, self.world, self.ll.ptrs, [], 0, ws.ws, ws.counters,
+                                 ops.status_buffer(x.device), self.ll_state, self.ll_set_lines)
+            return out
+        self._ll_last = False
+        slab, flags = self.sets[self.k]
+        self.k ^= 1
         ext().gemm_allreduce(x, w, out, self.rank, self.world, slab.ptrs, flags.ptrs, 0, ws.ws,
-                             ws.counters, ops.status_buffer(x.device))
+                             ws.counters, ops.status_buffer(x.device), None, 0)
         return out
 
     def last_slab(self, T: int, N: int) -> torch.Tensor:
         """bf16 [world, T, N]: the partials every rank pushed into this rank's
         slab in the most recent call (the inputs of its reduction)."""
+        if self._ll_last:
+            # line buffer of the last call's set: lines {bf16x2, epoch, bf16x2, epoch}
+            e = int(self.ll_state[0].item())  # the last call's epoch
+            raw = ext().symm_view(self.ll.local, self.ll.nbytes, self.device.index).view(torch.int32)
+            lines = raw[(e & 1) * self.ll_set_lines * 4:][: self.world * T * N].view(-1, 4)
+            payload = lines[:, [0, 2]].contiguous().view(torch.bfloat16)
+            return payload.view(self.world, T, N)
         slab, _ = self.sets[self.k ^ 1]
         raw = ext().symm_view(slab.local, slab.nbytes, self.device.index)
         # the kernel packs the slab for the call's shape: [(src * T + t) * N + n]
@@ -66,3 +101,5 @@ class FusedAllReduce:
         for a, b in self.sets:
             a.close()
             b.close()
+        if self.ll is not None:
+            self.ll.close()

@@ -44,6 +44,7 @@ class GemmArgs(ctypes.Structure):
         ("recv", ctypes.c_void_p * 8), ("flags", ctypes.c_void_p * 8),
         ("trace", ctypes.c_void_p), ("kv_pages", ctypes.c_int),
         ("x_ready", ctypes.c_void_p),
+        ("ll_state", ctypes.c_void_p), ("ll_set_lines", ctypes.c_longlong),
     ]
 
 
