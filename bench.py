@@ -44,6 +44,7 @@ through its own public API; it cannot be installed or run here (see
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -217,8 +218,13 @@ def main(argv=None):
             break
         last_producers = [q.rid for q in ss.producers(r[0])]
 
-    # 4. timed region (starts with nothing in flight)
+    # 4. timed region (starts with nothing in flight). The set-up's objects
+    # (2000 requests, the simulation's trace) move to a permanent generation,
+    # so a cyclic garbage collection inside the window has little to walk: a
+    # full collection over them once stalled the host for ~20 ms mid-window.
     eng.drain()
+    gc.collect()
+    gc.freeze()
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         dist.barrier()

@@ -146,8 +146,12 @@ void gemm(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int64_t epi, 
   a.y = y.data_ptr();
   a.ldy = y.stride(0);
   a.epi = epi;
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(sched_gemm_run(&a, cur_stream()), "gemm");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(x.device());
+    rc_ = sched_gemm_run(&a, cur_stream());
+  }
+  check_rc(rc_, "gemm");
 }
 
 void gemm_qkv_rope(const at::Tensor &x, const at::Tensor &w, const at::Tensor &pos,
@@ -177,8 +181,12 @@ void gemm_qkv_rope(const at::Tensor &x, const at::Tensor &w, const at::Tensor &p
   a.Hkv = Hkv;
   a.page_size = k_cache.size(2);
   a.kv_pages = k_cache.size(0);
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(sched_gemm_run(&a, cur_stream()), "gemm_qkv_rope");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(x.device());
+    rc_ = sched_gemm_run(&a, cur_stream());
+  }
+  check_rc(rc_, "gemm_qkv_rope");
 }
 
 // Row-parallel projection with the all-reduce fused into the GEMM epilogue.
@@ -218,8 +226,12 @@ void gemm_allreduce(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int
     a.ll_state = reinterpret_cast<uint32_t *>(ll_state->data_ptr<int32_t>());
     a.ll_set_lines = ll_set_lines;
   }
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(sched_gemm_run(&a, cur_stream()), "gemm_allreduce");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(x.device());
+    rc_ = sched_gemm_run(&a, cur_stream());
+  }
+  check_rc(rc_, "gemm_allreduce");
 }
 
 // Row-parallel projection, sequence-parallel output: each finished row goes
@@ -241,8 +253,12 @@ void gemm_reduce_scatter(const at::Tensor &x, const at::Tensor &w, int64_t rank,
     a.recv[j] = reinterpret_cast<__nv_bfloat16 *>(recv[j]);
     a.flags[j] = reinterpret_cast<uint32_t *>(flags[j]);
   }
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(sched_gemm_run(&a, cur_stream()), "gemm_reduce_scatter");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(x.device());
+    rc_ = sched_gemm_run(&a, cur_stream());
+  }
+  check_rc(rc_, "gemm_reduce_scatter");
 }
 
 // Sequence-parallel reduce + residual + RMSNorm + all-gather push (sp_api.h).
@@ -280,16 +296,23 @@ void sp_reduce_norm(int64_t slab, int64_t row_flags, at::Tensor &res, const at::
   a.world = world;
   a.eps = (float)eps;
   a.status = ptr_or_null<int>(status);
-  c10::cuda::CUDAGuard g(res.device());
-  check_rc(sched_sp_reduce_norm(&a, cur_stream()), "sp_reduce_norm");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(res.device());
+    rc_ = sched_sp_reduce_norm(&a, cur_stream());
+  }
+  check_rc(rc_, "sp_reduce_norm");
 }
 
 void sp_wait_rows(int64_t ready, int64_t T, const at::Tensor &status) {
   check_cuda(status, "status");
-  c10::cuda::CUDAGuard g(status.device());
-  check_rc(sched_sp_wait_rows(reinterpret_cast<const uint32_t *>(ready), T,
-                              static_cast<int *>(status.data_ptr()), cur_stream()),
-           "sp_wait_rows");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(status.device());
+    rc_ = sched_sp_wait_rows(reinterpret_cast<const uint32_t *>(ready), T,
+                                static_cast<int *>(status.data_ptr()), cur_stream());
+  }
+  check_rc(rc_, "sp_wait_rows");
 }
 
 int64_t gemm_ws_floats(int64_t T, int64_t N, int64_t K, int64_t grid) {
@@ -338,18 +361,23 @@ void attn_decode(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache
               "cache [pages, Hkv, 16, 128]");
   TORCH_CHECK(items.numel() >= num_items * 4, "items [n, 4]");
   const int Hq = q.size(1), Hkv = k_cache.size(1);
-  c10::cuda::CUDAGuard g(q.device());
-  SchedSlots sl = make_slots(order, ctrl, timer, queue, max_tasks);
-  check_rc(sched_attn_decode(q.data_ptr(), out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                             k_cache.size(0), block_table.data_ptr<int32_t>(),
-                             block_table.stride(0), items.data_ptr(), num_items, Hq, Hkv,
-                             (float)sm_scale, ptr_or_null<float>(part_o),
-                             ptr_or_null<float>(part_lse), ptr_or_null<uint32_t>(merge_cnt),
-                             splits, sl, woven, acquire, grid, pf_blocks,
-                             (float)dT, (float)dR, (float)H, staged ? stage_k->data_ptr() : nullptr,
-                             staged ? stage_v->data_ptr() : nullptr, staged ? (int)stage_k->size(0) : 0,
-                             (int)stage_split, ptr_or_null<int>(status), cur_stream()),
-           "attn_decode");
+  TORCH_CHECK(Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv == 1 || Hq / Hkv == 2 || Hq / Hkv == 4 || Hq / Hkv == 8),
+              "query heads per KV head must be 1, 2, 4 or 8");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(q.device());
+    SchedSlots sl = make_slots(order, ctrl, timer, queue, max_tasks);
+    rc_ = sched_attn_decode(q.data_ptr(), out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                               k_cache.size(0), block_table.data_ptr<int32_t>(),
+                               block_table.stride(0), items.data_ptr(), num_items, Hq, Hkv,
+                               (float)sm_scale, ptr_or_null<float>(part_o),
+                               ptr_or_null<float>(part_lse), ptr_or_null<uint32_t>(merge_cnt),
+                               splits, sl, woven, acquire, grid, pf_blocks,
+                               (float)dT, (float)dR, (float)H, staged ? stage_k->data_ptr() : nullptr,
+                               staged ? stage_v->data_ptr() : nullptr, staged ? (int)stage_k->size(0) : 0,
+                               (int)stage_split, ptr_or_null<int>(status), cur_stream());
+  }
+  check_rc(rc_, "attn_decode");
 }
 
 void attn_merge(const at::Tensor &part_o, const at::Tensor &part_lse, const at::Tensor &merge_req,
@@ -357,11 +385,14 @@ void attn_merge(const at::Tensor &part_o, const at::Tensor &part_lse, const at::
   check_i32(merge_req, "merge_req");
   check_i32(merge_begin, "merge_begin");
   check_bf16(out, "out");
-  c10::cuda::CUDAGuard g(out.device());
-  check_rc(sched_attn_merge(part_o.data_ptr<float>(), part_lse.data_ptr<float>(),
-                            merge_req.data_ptr<int32_t>(), merge_begin.data_ptr<int32_t>(), rows,
-                            out.size(1), out.data_ptr(), cur_stream()),
-           "attn_merge");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(out.device());
+    rc_ = sched_attn_merge(part_o.data_ptr<float>(), part_lse.data_ptr<float>(),
+                              merge_req.data_ptr<int32_t>(), merge_begin.data_ptr<int32_t>(), rows,
+                              out.size(1), out.data_ptr(), cur_stream());
+  }
+  check_rc(rc_, "attn_merge");
 }
 
 void attn_prefill(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache,
@@ -374,12 +405,15 @@ void attn_prefill(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cach
   check_i32(kv_lens, "kv_lens");
   check_i32(tiles, "tiles");
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.is_contiguous(), "q [T, Hq, 128]");
-  c10::cuda::CUDAGuard g(q.device());
-  check_rc(sched_attn_prefill(q.data_ptr(), out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                              block_table.data_ptr<int32_t>(), block_table.stride(0),
-                              kv_lens.data_ptr<int32_t>(), tiles.data_ptr(), num_tiles, q.size(1),
-                              k_cache.size(1), k_cache.size(2), (float)sm_scale, cur_stream()),
-           "attn_prefill");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(q.device());
+    rc_ = sched_attn_prefill(q.data_ptr(), out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                block_table.data_ptr<int32_t>(), block_table.stride(0),
+                                kv_lens.data_ptr<int32_t>(), tiles.data_ptr(), num_tiles, q.size(1),
+                                k_cache.size(1), k_cache.size(2), (float)sm_scale, cur_stream());
+  }
+  check_rc(rc_, "attn_prefill");
 }
 
 int64_t attn_decode_occupancy(int64_t group) { return sched_attn_decode_occupancy(group); }
@@ -393,10 +427,13 @@ void add_rmsnorm(const at::Tensor &x, const c10::optional<at::Tensor> &res, cons
   check_bf16(y, "y");
   TORCH_CHECK(x.is_contiguous() && y.is_contiguous(), "contiguous rows");
   const int H = x.size(-1), T = x.numel() / H;
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(sched_add_rmsnorm(x.data_ptr(), res.has_value() ? res->data_ptr() : nullptr,
-                             w.data_ptr(), y.data_ptr(), T, H, (float)eps, cur_stream()),
-           "add_rmsnorm");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(x.device());
+    rc_ = sched_add_rmsnorm(x.data_ptr(), res.has_value() ? res->data_ptr() : nullptr,
+                               w.data_ptr(), y.data_ptr(), T, H, (float)eps, cur_stream());
+  }
+  check_rc(rc_, "add_rmsnorm");
 }
 
 void rope_kv_append(const at::Tensor &qkv, const at::Tensor &pos, const at::Tensor &slot,
@@ -407,12 +444,15 @@ void rope_kv_append(const at::Tensor &qkv, const at::Tensor &pos, const at::Tens
   check_i32(slot, "slot");
   TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin float32");
   const int T = qkv.size(0);
-  c10::cuda::CUDAGuard g(qkv.device());
-  check_rc(sched_rope_kv_append(qkv.data_ptr(), pos.data_ptr<int32_t>(), slot.data_ptr<int32_t>(),
-                                cos_sin.data_ptr<float>(), q_out.data_ptr(), k_cache.data_ptr(),
-                                v_cache.data_ptr(), T, Hq, Hkv, k_cache.size(3), k_cache.size(2),
-                                k_cache.size(0), ptr_or_null<int>(status), cur_stream()),
-           "rope_kv_append");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(qkv.device());
+    rc_ = sched_rope_kv_append(qkv.data_ptr(), pos.data_ptr<int32_t>(), slot.data_ptr<int32_t>(),
+                                  cos_sin.data_ptr<float>(), q_out.data_ptr(), k_cache.data_ptr(),
+                                  v_cache.data_ptr(), T, Hq, Hkv, k_cache.size(3), k_cache.size(2),
+                                  k_cache.size(0), ptr_or_null<int>(status), cur_stream());
+  }
+  check_rc(rc_, "rope_kv_append");
 }
 
 void embedding(const at::Tensor &ids, const at::Tensor &table, at::Tensor &out,
@@ -421,31 +461,40 @@ void embedding(const at::Tensor &ids, const at::Tensor &table, at::Tensor &out,
   check_bf16(table, "table");
   const bool has_prev = prev.has_value() && prev->defined();
   if (has_prev) check_i32(*prev, "prev");
-  c10::cuda::CUDAGuard g(ids.device());
-  check_rc(sched_embedding(ids.data_ptr<int32_t>(), has_prev ? prev->data_ptr<int32_t>() : nullptr,
-                           has_prev ? (int)prev->numel() : 0, table.data_ptr(), out.data_ptr(), ids.numel(),
-                           table.size(1), table.size(0), ptr_or_null<int>(status), cur_stream()),
-           "embedding");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(ids.device());
+    rc_ = sched_embedding(ids.data_ptr<int32_t>(), has_prev ? prev->data_ptr<int32_t>() : nullptr,
+                             has_prev ? (int)prev->numel() : 0, table.data_ptr(), out.data_ptr(), ids.numel(),
+                             table.size(1), table.size(0), ptr_or_null<int>(status), cur_stream());
+  }
+  check_rc(rc_, "embedding");
 }
 
 void argmax(const at::Tensor &logits, at::Tensor &ids, const c10::optional<at::Tensor> &maxv,
             int64_t id_offset) {
   check_bf16(logits, "logits");
   check_i32(ids, "ids");
-  c10::cuda::CUDAGuard g(logits.device());
-  check_rc(sched_argmax(logits.data_ptr(), logits.size(0), logits.size(1), logits.stride(0),
-                        ids.data_ptr<int32_t>(), ptr_or_null<float>(maxv), id_offset, cur_stream()),
-           "argmax");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(logits.device());
+    rc_ = sched_argmax(logits.data_ptr(), logits.size(0), logits.size(1), logits.stride(0),
+                          ids.data_ptr<int32_t>(), ptr_or_null<float>(maxv), id_offset, cur_stream());
+  }
+  check_rc(rc_, "argmax");
 }
 
 // ---------------------------------------------------------------- MoE
 void moe_router(const at::Tensor &x, const at::Tensor &wr, at::Tensor &ids, at::Tensor &wts, int64_t k) {
   check_bf16(x, "x");
   check_bf16(wr, "wr");
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(sched_moe_router(x.data_ptr(), wr.data_ptr(), x.size(0), x.size(1), wr.size(0), k,
-                            ids.data_ptr<int32_t>(), wts.data_ptr<float>(), cur_stream()),
-           "moe_router");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(x.device());
+    rc_ = sched_moe_router(x.data_ptr(), wr.data_ptr(), x.size(0), x.size(1), wr.size(0), k,
+                              ids.data_ptr<int32_t>(), wts.data_ptr<float>(), cur_stream());
+  }
+  check_rc(rc_, "moe_router");
 }
 
 // p: dict-like flat vector of int64 arguments (see sched_pass_b200/parallel/ep.py)
@@ -480,8 +529,12 @@ void moe_dispatch(const at::Tensor &x, const at::Tensor &ids, const at::Tensor &
   a.dropped_step = reinterpret_cast<uint32_t *>(dropped_step);
   a.dropped_total = reinterpret_cast<uint32_t *>(dropped_total);
   a.status = ptr_or_null<int>(status);
-  c10::cuda::CUDAGuard g(x.device());
-  check_rc(sched_moe_dispatch(&a, cur_stream()), "moe_dispatch");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(x.device());
+    rc_ = sched_moe_dispatch(&a, cur_stream());
+  }
+  check_rc(rc_, "moe_dispatch");
 }
 
 void moe_expert_gemm(int64_t epi, const at::Tensor &w, int64_t x_ptr, int64_t E_local, int64_t N, int64_t K,
@@ -516,9 +569,12 @@ void moe_expert_gemm(int64_t epi, const at::Tensor &w, int64_t x_ptr, int64_t E_
   a.grid = grid;
   a.trace = reinterpret_cast<unsigned long long *>(trace);
   a.status = ptr_or_null<int>(status);
-  c10::cuda::CUDAGuard g(w.device());
-  check_rc(sched_moe_expert_gemm(epi, w.data_ptr(), reinterpret_cast<const void *>(x_ptr), &a, cur_stream()),
-           "moe_expert_gemm");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(w.device());
+    rc_ = sched_moe_expert_gemm(epi, w.data_ptr(), reinterpret_cast<const void *>(x_ptr), &a, cur_stream());
+  }
+  check_rc(rc_, "moe_expert_gemm");
 }
 
 void moe_quantize(int64_t in, int64_t R, int64_t I, int64_t out, int64_t scale, int64_t rows_valid,
@@ -534,34 +590,43 @@ void moe_combine_norm(int64_t c, int64_t K, at::Tensor &h, const at::Tensor &w, 
                       const c10::optional<at::Tensor> &status) {
   check_bf16(h, "h");
   check_bf16(y, "y");
-  c10::cuda::CUDAGuard g(h.device());
-  check_rc(sched_moe_combine_norm(reinterpret_cast<const void *>(c), K, h.data_ptr(), w.data_ptr(), y.data_ptr(), T,
-                                  h.size(1), (float)eps, reinterpret_cast<uint32_t *>(cnt),
-                                  reinterpret_cast<uint32_t *>(dropped_step), reinterpret_cast<uint32_t *>(arrivals),
-                                  ptr_or_null<int>(status), cur_stream()),
-           "moe_combine_norm");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(h.device());
+    rc_ = sched_moe_combine_norm(reinterpret_cast<const void *>(c), K, h.data_ptr(), w.data_ptr(), y.data_ptr(), T,
+                                    h.size(1), (float)eps, reinterpret_cast<uint32_t *>(cnt),
+                                    reinterpret_cast<uint32_t *>(dropped_step), reinterpret_cast<uint32_t *>(arrivals),
+                                    ptr_or_null<int>(status), cur_stream());
+  }
+  check_rc(rc_, "moe_combine_norm");
 }
 
 void probe_stream(const at::Tensor &src, int64_t policy, at::Tensor &sink, int64_t grid) {
   TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "src on the device");
-  c10::cuda::CUDAGuard g(src.device());
-  check_rc(sched_probe_stream(src.data_ptr(), src.numel() * src.element_size(), policy,
-                              reinterpret_cast<unsigned *>(sink.data_ptr()), grid, cur_stream()),
-           "probe_stream");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(src.device());
+    rc_ = sched_probe_stream(src.data_ptr(), src.numel() * src.element_size(), policy,
+                                reinterpret_cast<unsigned *>(sink.data_ptr()), grid, cur_stream());
+  }
+  check_rc(rc_, "probe_stream");
 }
 
 void probe_tasks(const at::Tensor &cost, int64_t mode, int64_t grid, int64_t memory, const at::Tensor &data,
                  at::Tensor &hits, at::Tensor &per_cta, at::Tensor &ticket, at::Tensor &sink,
                  const c10::optional<at::Tensor> &status) {
   TORCH_CHECK(cost.is_cuda() && cost.scalar_type() == at::kInt, "cost int32 on the device");
-  c10::cuda::CUDAGuard g(cost.device());
-  check_rc(sched_probe_tasks(reinterpret_cast<const uint32_t *>(cost.data_ptr()), cost.numel(), mode, grid, memory,
-                             data.data_ptr(), data.numel() * data.element_size(),
-                             reinterpret_cast<unsigned *>(hits.data_ptr()),
-                             reinterpret_cast<unsigned *>(per_cta.data_ptr()),
-                             reinterpret_cast<unsigned *>(ticket.data_ptr()),
-                             reinterpret_cast<unsigned *>(sink.data_ptr()), ptr_or_null<int>(status), cur_stream()),
-           "probe_tasks");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(cost.device());
+    rc_ = sched_probe_tasks(reinterpret_cast<const uint32_t *>(cost.data_ptr()), cost.numel(), mode, grid, memory,
+                               data.data_ptr(), data.numel() * data.element_size(),
+                               reinterpret_cast<unsigned *>(hits.data_ptr()),
+                               reinterpret_cast<unsigned *>(per_cta.data_ptr()),
+                               reinterpret_cast<unsigned *>(ticket.data_ptr()),
+                               reinterpret_cast<unsigned *>(sink.data_ptr()), ptr_or_null<int>(status), cur_stream());
+  }
+  check_rc(rc_, "probe_tasks");
 }
 
 void probe_clc(const at::Tensor &work, int64_t mode, int64_t grid, at::Tensor &hits, at::Tensor &rec,
@@ -576,13 +641,16 @@ void probe_clc(const at::Tensor &work, int64_t mode, int64_t grid, at::Tensor &h
               "rec: int64 [grid, max_rec]");
   TORCH_CHECK(n_rec.numel() >= g && smid.numel() >= g && n_rec.element_size() == 4 && smid.element_size() == 4,
               "n_rec, smid: int32 [grid]");
-  c10::cuda::CUDAGuard gd(work.device());
-  check_rc(sched_probe_clc(reinterpret_cast<const uint32_t *>(work.data_ptr()), (int)n, (int)mode, (int)g,
-                           (int)rec.size(1), reinterpret_cast<unsigned *>(hits.data_ptr()),
-                           reinterpret_cast<unsigned long long *>(rec.data_ptr()),
-                           reinterpret_cast<unsigned *>(n_rec.data_ptr()), reinterpret_cast<unsigned *>(smid.data_ptr()),
-                           ptr_or_null<int>(status), cur_stream()),
-           "probe_clc");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard gd(work.device());
+    rc_ = sched_probe_clc(reinterpret_cast<const uint32_t *>(work.data_ptr()), (int)n, (int)mode, (int)g,
+                             (int)rec.size(1), reinterpret_cast<unsigned *>(hits.data_ptr()),
+                             reinterpret_cast<unsigned long long *>(rec.data_ptr()),
+                             reinterpret_cast<unsigned *>(n_rec.data_ptr()), reinterpret_cast<unsigned *>(smid.data_ptr()),
+                             ptr_or_null<int>(status), cur_stream());
+  }
+  check_rc(rc_, "probe_clc");
 }
 
 void probe_mix(const at::Tensor &R, const at::Tensor &S, int64_t mode, double frac, at::Tensor &sink,
@@ -591,10 +659,13 @@ void probe_mix(const at::Tensor &R, const at::Tensor &S, int64_t mode, double fr
   TORCH_CHECK(mode >= 0 && mode <= 2, "mode is 0 (plain), 1 or 2 (pinned fractions)");
   TORCH_CHECK(frac > 0.0 && frac <= 1.0, "the pinned fraction must be in (0, 1]");
   TORCH_CHECK(grid > 0 && sink.numel() >= grid, "sink holds one word per CTA");
-  c10::cuda::CUDAGuard g(R.device());
-  check_rc(sched_probe_mix(R.data_ptr(), R.numel() * R.element_size(), S.data_ptr(), S.numel() * S.element_size(),
-                           mode, (float)frac, reinterpret_cast<unsigned *>(sink.data_ptr()), grid, cur_stream()),
-           "probe_mix");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(R.device());
+    rc_ = sched_probe_mix(R.data_ptr(), R.numel() * R.element_size(), S.data_ptr(), S.numel() * S.element_size(),
+                             mode, (float)frac, reinterpret_cast<unsigned *>(sink.data_ptr()), grid, cur_stream());
+  }
+  check_rc(rc_, "probe_mix");
 }
 
 void probe_pdl_pairs(at::Tensor &buf, at::Tensor &out, const at::Tensor &table, int64_t work, int64_t prologue,
@@ -602,16 +673,23 @@ void probe_pdl_pairs(at::Tensor &buf, at::Tensor &out, const at::Tensor &table, 
   TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && out.sizes() == buf.sizes() &&
                   out.scalar_type() == at::kFloat && table.numel() >= 256 && table.scalar_type() == at::kFloat,
               "float32 buf/out of one shape and a float32 table of >= 256 entries");
-  c10::cuda::CUDAGuard g(buf.device());
-  check_rc(sched_probe_pdl_pairs(buf.data_ptr<float>(), out.data_ptr<float>(), buf.numel(), table.data_ptr<float>(),
-                                 work, prologue, pdl ? 1 : 0, pairs, cur_stream()),
-           "probe_pdl_pairs");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(buf.device());
+    rc_ = sched_probe_pdl_pairs(buf.data_ptr<float>(), out.data_ptr<float>(), buf.numel(), table.data_ptr<float>(),
+                                   work, prologue, pdl ? 1 : 0, pairs, cur_stream());
+  }
+  check_rc(rc_, "probe_pdl_pairs");
 }
 
 void probe_pdl_produce(at::Tensor &buf, int64_t work) {
   TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && buf.is_contiguous(), "float32 buf");
-  c10::cuda::CUDAGuard g(buf.device());
-  check_rc(sched_probe_pdl_produce(buf.data_ptr<float>(), buf.numel(), work, cur_stream()), "probe_pdl_produce");
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(buf.device());
+    rc_ = sched_probe_pdl_produce(buf.data_ptr<float>(), buf.numel(), work, cur_stream());
+  }
+  check_rc(rc_, "probe_pdl_produce");
 }
 
 // Page moves between KV pools (device <-> pinned host); pairs [n, 2] int32 on the device.

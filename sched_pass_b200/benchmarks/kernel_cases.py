@@ -11,8 +11,8 @@ a few hundred MB on the device at most).
   --case sample    embedding gather (T tokens) and greedy argmax over the
                    128256-entry vocabulary
   --case decode    the serving engine's decode attention launch for a small
-                   batch (``--batch`` requests of ``--context`` tokens, 32
-                   query / ``--kv-heads`` KV heads, pages scattered over a
+                   batch (``--batch`` requests of ``--context`` tokens, 4
+                   query heads per KV head, ``--kv-heads`` KV heads, pages scattered over a
                    pool larger than L2): KV split the way the engine splits it
                    (tasks up to one per SM), in-kernel merge, levers woven
                    with neutral tables, cluster launch control grid
@@ -134,7 +134,9 @@ def case_decode(args, peaks):
 
     from ..engine import native
     from ..runtime.sched_rt import SchedPlane
-    B, ctx, Hq, Hkv, D = args.batch, args.context, 32, args.kv_heads, 128
+    # Llama-3-8B's 4 query heads per KV head (a TP rank of 8 GPUs holds 1 KV head)
+    B, ctx, Hkv, D = args.batch, args.context, args.kv_heads, 128
+    Hq = 4 * Hkv
     dev = "cuda"
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     S = int(min(8, max(1, sms // (B * Hkv))))  # the engine's split rule (Engine.splits_for)

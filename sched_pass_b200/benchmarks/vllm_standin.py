@@ -16,6 +16,11 @@ arrivals up to the clock are admitted. Reported: decode tokens/s over the
 timed steps and p50/p99 TPOT of the requests that finished in the window.
 
     python -m sched_pass_b200.benchmarks.vllm_standin --tp 1
+
+``--steady-batch B`` instead times steady decode steps at a fixed batch: B
+requests of ``--prompt`` tokens are prefilled, then ``--steps`` decode steps
+are timed (host wall time per ``step()``, CUDA synchronised on both sides),
+the shape ``benchmarks/decode_step.py`` times for this framework.
 """
 from __future__ import annotations
 
@@ -50,6 +55,8 @@ def main():
     ap.add_argument("--max-batch", type=int, default=128)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--eager", action="store_true", help="no CUDA graphs / compilation")
+    ap.add_argument("--steady-batch", type=int, default=0,
+                    help="time decode steps of a fixed batch of this many requests instead")
     args = ap.parse_args()
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")  # step() in this process
 
@@ -65,6 +72,8 @@ def main():
         max_num_seqs=args.max_batch, enforce_eager=args.eager, seed=args.seed,
         gpu_memory_utilization=0.85, disable_log_stats=True))
 
+    if args.steady_batch:
+        return steady(eng, args, SamplingParams, TokensPrompt)
     rng = np.random.default_rng(args.seed)
     arrivals = np.cumsum(rng.exponential(1.0 / args.rate, size=args.requests))
     prompts = rng.integers(0, LLAMA3_8B["vocab_size"], size=(args.requests, args.prompt))
@@ -132,6 +141,40 @@ def main():
         "finished_in_window": len(finished), "cuda_graphs": not args.eager,
         "config": {"model": "llama-3-8b-arch (dummy weights)", "prompt_tokens": args.prompt,
                    "output_tokens": args.output, "arrival": f"poisson {args.rate} req/s"}}))
+
+
+def steady(eng, args, SamplingParams, TokensPrompt):
+    """Decode steps of a fixed batch (every request prefilled first)."""
+    import torch
+    rng = np.random.default_rng(args.seed)
+    B = args.steady_batch
+    sp = SamplingParams(max_tokens=args.steps + args.warmup + 64, temperature=0.0, ignore_eos=True,
+                        detokenize=False)
+    for i in range(B):
+        eng.add_request(str(i), TokensPrompt(prompt_token_ids=rng.integers(0, LLAMA3_8B["vocab_size"],
+                                                                           size=args.prompt).tolist()), sp)
+    started = set()
+    for _ in range(10 * B + 100):  # until every request has produced a token
+        for o in eng.step():
+            if o.outputs and len(o.outputs[0].token_ids) > 0:
+                started.add(o.request_id)
+        if len(started) == B:
+            break
+    for _ in range(args.warmup):
+        eng.step()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        eng.step()
+        torch.cuda.synchronize()
+        ts.append(time.perf_counter() - t0)
+    med = float(np.median(ts))
+    print(json.dumps({"impl": "vllm-standin", "mode": "steady-batch", "vllm_tp": args.tp, "batch": B,
+                      "context": args.prompt, "step_ms_p50": round(1e3 * med, 4),
+                      "step_ms_min": round(1e3 * min(ts), 4), "tok_s": round(B / med, 1), "steps": len(ts),
+                      "cuda_graphs": not args.eager}))
+    return 0
 
 
 if __name__ == "__main__":
