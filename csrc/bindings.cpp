@@ -107,6 +107,27 @@ int num_sms(const at::Tensor &t) {
 unsigned long long *g_gemm_trace = nullptr;
 void set_gemm_trace(int64_t ptr) { g_gemm_trace = reinterpret_cast<unsigned long long *>(ptr); }
 
+// Residual add + RMSNorm fused after the projection: res += y, out = rmsnorm(res) * nw
+// (all [T, N] bf16 except nw [N]); row_cnt int32 [>= T], zero between calls.
+void set_norm(GemmArgs &a, const c10::optional<at::Tensor> &res, const c10::optional<at::Tensor> &nw,
+              const c10::optional<at::Tensor> &out, const c10::optional<at::Tensor> &row_cnt, double eps) {
+  if (!(nw.has_value() && nw->defined())) return;
+  TORCH_CHECK(res.has_value() && out.has_value() && row_cnt.has_value(), "fused norm needs res, out and row_cnt");
+  check_bf16(*res, "norm res");
+  check_bf16(*nw, "norm weight");
+  check_bf16(*out, "norm out");
+  check_i32(*row_cnt, "row_cnt");
+  TORCH_CHECK(res->is_contiguous() && out->is_contiguous() && nw->is_contiguous(), "contiguous norm tensors");
+  TORCH_CHECK(res->dim() == 2 && res->size(0) >= a.T && res->size(1) == a.N && out->sizes() == res->sizes() &&
+                  nw->numel() == a.N && row_cnt->numel() >= a.T,
+              "norm tensors: res/out [>= T, N], weight [N], row_cnt [>= T]");
+  a.norm_res = reinterpret_cast<__nv_bfloat16 *>(res->data_ptr());
+  a.norm_w = reinterpret_cast<const __nv_bfloat16 *>(nw->data_ptr());
+  a.norm_out = reinterpret_cast<__nv_bfloat16 *>(out->data_ptr());
+  a.row_cnt = reinterpret_cast<uint32_t *>(row_cnt->data_ptr<int32_t>());
+  a.norm_eps = (float)eps;
+}
+
 GemmArgs base_args(const at::Tensor &x, const at::Tensor &w, int64_t grid,
                    const c10::optional<at::Tensor> &ws, const c10::optional<at::Tensor> &counters,
                    const c10::optional<at::Tensor> &status) {
@@ -136,7 +157,9 @@ GemmArgs base_args(const at::Tensor &x, const at::Tensor &w, int64_t grid,
 // x_ready: address of the gathered rows' ready flags (0: x is local and ready)
 void gemm(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int64_t epi, int64_t grid,
           const c10::optional<at::Tensor> &ws, const c10::optional<at::Tensor> &counters,
-          const c10::optional<at::Tensor> &status, int64_t x_ready) {
+          const c10::optional<at::Tensor> &status, int64_t x_ready, const c10::optional<at::Tensor> &norm_res,
+          const c10::optional<at::Tensor> &norm_w, const c10::optional<at::Tensor> &norm_out,
+          const c10::optional<at::Tensor> &row_cnt, double norm_eps) {
   GemmArgs a = base_args(x, w, grid, ws, counters, status);
   a.x_ready = reinterpret_cast<const uint32_t *>(x_ready);
   check_bf16(y, "y");
@@ -146,6 +169,8 @@ void gemm(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int64_t epi, 
   a.y = y.data_ptr();
   a.ldy = y.stride(0);
   a.epi = epi;
+  TORCH_CHECK(!(norm_w.has_value() && norm_w->defined()) || epi == kEpiStore, "the fused norm follows a plain store");
+  set_norm(a, norm_res, norm_w, norm_out, row_cnt, norm_eps);
   int rc_ = 0;
   {  // the guard is gone before check_rc may throw
     c10::cuda::CUDAGuard g(x.device());
@@ -200,7 +225,10 @@ void gemm_allreduce(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int
                     const c10::optional<at::Tensor> &ws,
                     const c10::optional<at::Tensor> &counters,
                     const c10::optional<at::Tensor> &status,
-                    const c10::optional<at::Tensor> &ll_state, int64_t ll_set_lines) {
+                    const c10::optional<at::Tensor> &ll_state, int64_t ll_set_lines,
+                    const c10::optional<at::Tensor> &norm_res, const c10::optional<at::Tensor> &norm_w,
+                    const c10::optional<at::Tensor> &norm_out, const c10::optional<at::Tensor> &row_cnt,
+                    double norm_eps) {
   GemmArgs a = base_args(x, w, grid, ws, counters, status);
   check_bf16(y, "y");
   TORCH_CHECK(y.dim() == 2 && y.stride(1) == 1 && y.size(1) >= a.N, "y [T, >= N]");
@@ -226,6 +254,7 @@ void gemm_allreduce(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int
     a.ll_state = reinterpret_cast<uint32_t *>(ll_state->data_ptr<int32_t>());
     a.ll_set_lines = ll_set_lines;
   }
+  set_norm(a, norm_res, norm_w, norm_out, row_cnt, norm_eps);
   int rc_ = 0;
   {  // the guard is gone before check_rc may throw
     c10::cuda::CUDAGuard g(x.device());

@@ -168,11 +168,70 @@ __global__ void embedding_kernel(const int32_t *__restrict__ ids, const int32_t 
         *reinterpret_cast<const uint4 *>(table + (size_t)id * H + c);
 }
 
+// Vocabulary-parallel greedy sampling across tensor-parallel ranks, inside
+// the argmax kernel: each row's (max, global id) goes to every rank as one
+// 16-byte line {max bits, epoch, id, epoch} (an 8-byte half lands whole), and
+// the row's block then polls the world's lines for that row in its own buffer
+// and keeps the largest value, the lowest id on ties. `state` = this rank's
+// [epoch, done]: a call uses epoch + 1 and the buffer set of its parity; the
+// last block advances the epoch (0 skipped on wrap-around). world == 0: off.
+struct ArgmaxExchange {
+  uint4 *lines[8];     // every rank's line buffer: 2 sets x [world][rows] lines
+  int world, rank;
+  uint32_t *state;     // this rank's [epoch, done] (device, zero at start)
+  long long set_lines;  // lines per set (>= world x rows)
+  int *status;
+};
+
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void exchange_row(const ArgmaxExchange &x, int t, int rows, float &best, int &gid) {
+  const uint32_t e = ld_volatile_u32(x.state) + 1u;
+  const size_t set = (size_t)(e & 1u) * x.set_lines;
+  const size_t mine = set + (size_t)x.rank * rows + t;
+  for (int j = 0; j < x.world; ++j)
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(x.lines[j] + mine),
+                 "r"(__float_as_uint(best)), "r"(e), "r"((uint32_t)gid), "r"(e)
+                 : "memory");
+  float b = -INFINITY;
+  int g = 0x7fffffff;
+  for (int src = 0; src < x.world; ++src) {
+    const uint4 *q = x.lines[x.rank] + set + (size_t)src * rows + t;
+    uint4 l = make_uint4(0, 0, 0, 0);
+    const uint64_t start = ptx::globaltimer_ns();
+    for (uint32_t polls = 0;; ++polls) {
+      asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(l.x), "=r"(l.y), "=r"(l.z), "=r"(l.w)
+                   : "l"(q)
+                   : "memory");
+      if (l.y == e && l.w == e) break;
+      if ((polls & 63u) == 63u && ptx::globaltimer_ns() - start > kWaitBudgetNs) {
+        report_status(x.status, kStatusPeerTimeout);
+        break;
+      }
+    }
+    const float v = __uint_as_float(l.x);
+    const int i = (int)l.z;
+    if (v > b || (v == b && i < g)) {
+      b = v;
+      g = i;
+    }
+  }
+  best = b;
+  gid = g;
+}
+
 // Row argmax; ties resolve to the lowest index. Also emits the row max so a
-// vocabulary-parallel caller can combine shards (value, index) pairs.
+// vocabulary-parallel caller can combine shards (value, index) pairs; with
+// an exchange (ArgmaxExchange::world > 0) the shards are combined here.
 __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16 *__restrict__ logits,
                                                       int V, int ld, int32_t *__restrict__ ids,
-                                                      float *__restrict__ maxv, int id_offset) {
+                                                      float *__restrict__ maxv, int id_offset,
+                                                      const ArgmaxExchange x) {
   __shared__ float sv[32];
   __shared__ int si[32];
   const int t = blockIdx.x;
@@ -229,8 +288,19 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16 *__res
       }
     }
     if (l == 0) {
-      ids[t] = bi + id_offset;
+      int gid = bi + id_offset;
+      if (x.world > 0) exchange_row(x, t, gridDim.x, best, gid);
+      ids[t] = gid;
       if (maxv != nullptr) maxv[t] = best;
+      if (x.world > 0) {
+        __threadfence();
+        if (atomicAdd(x.state + 1, 1u) == gridDim.x - 1) {  // the call's last block
+          x.state[1] = 0u;
+          const uint32_t e = ld_volatile_u32(x.state) + 1u;
+          __threadfence();
+          x.state[0] = e == 0xFFFFFFFFu ? 1u : e;
+        }
+      }
     }
   }
 }
@@ -382,8 +452,33 @@ extern "C" int sched_embedding(const int32_t *ids, const int32_t *prev, int n_pr
 extern "C" int sched_argmax(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
                             int id_offset, cudaStream_t st) {
   if (T <= 0) return 0;
+  ew::ArgmaxExchange none{};
   launch_pdl(ew::argmax_kernel, T, 1024, 0, st, static_cast<const __nv_bfloat16 *>(logits), V, ld,
-             ids, maxv, id_offset);
+             ids, maxv, id_offset, none);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+// Vocabulary-parallel argmax with the ranks' (max, id) exchange in the same
+// kernel: lines[j] is rank j's line buffer (two sets of set_lines 16-byte
+// lines, set_lines >= world * T), state this rank's [epoch, done] pair.
+extern "C" int sched_argmax_exchange(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
+                                     int id_offset, void *const *lines, int world, int rank, uint32_t *state,
+                                     long long set_lines, int *status, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || state == nullptr || set_lines < (long long)world * T)
+    return -1;
+  ew::ArgmaxExchange x{};
+  for (int j = 0; j < world; ++j) {
+    if (lines[j] == nullptr || (reinterpret_cast<uintptr_t>(lines[j]) & 15) != 0) return -1;
+    x.lines[j] = static_cast<uint4 *>(lines[j]);
+  }
+  x.world = world;
+  x.rank = rank;
+  x.state = state;
+  x.set_lines = set_lines;
+  x.status = status;
+  launch_pdl(ew::argmax_kernel, T, 1024, 0, st, static_cast<const __nv_bfloat16 *>(logits), V, ld,
+             ids, maxv, id_offset, x);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

@@ -96,6 +96,13 @@ struct Params {
   int cs;      // cluster split-K: CTAs per cluster (0: stream-K kernel)
 };
 
+// Residual add + RMSNorm of the output rows a CTA completes (defined below;
+// out of line, and only called when the launch fuses the norm).
+__device__ __noinline__ void finish_rows_impl(const Params &p, int r0, int nrows, int et, float *scratch);
+__device__ __forceinline__ void finish_rows(const Params &p, int r0, int nrows, int et, float *scratch) {
+  if (p.a.norm_w != nullptr && nrows > 0) finish_rows_impl(p, r0, nrows, et, scratch);
+}
+
 // One segment: the k-block range [kb0, kb1) of `tile` handled by one CTA.
 struct Seg {
   int tile, kb0, kb1;
@@ -377,7 +384,7 @@ __device__ __noinline__ void wait_rows_ready(const uint32_t *ready, int r0, int 
 // rank: bit-identical results), writes the bf16 output and clears its flags.
 // Pushes never wait, so no wait can form a cycle.
 template <int TN>
-__device__ void reduce_owned_chunks(const Params &p, int c, int et) {
+__device__ void reduce_owned_chunks(const Params &p, int c, int et, float *scratch) {
   const GemmArgs &a = p.a;
   constexpr int CH = TN / kSlab;
   const __nv_bfloat16 *mine = a.recv[a.rank];
@@ -438,7 +445,116 @@ __device__ void reduce_owned_chunks(const Params &p, int c, int et) {
     }
     named_bar(1, kEpiThreads);
     if (et < a.world) my_flags[((size_t)et * p.tiles + tile) * CH + ch] = 0u;
+    finish_rows(p, t0, tmax, et, scratch);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Residual add + RMSNorm fused after the projection (GemmArgs::norm_w).
+//
+// One output row, normalised by the 128 epilogue threads with the arithmetic
+// of sched_add_rmsnorm's NTV-thread kernel (elementwise.cu): NTV virtual
+// threads, virtual thread vt = et + 128 m owning the 8-element vectors
+// (vt + i NTV) * 8, i < 2; per-thread sums in the same order, the same xor
+// shuffle tree per virtual warp (virtual warp et / 32 + 4 m has the lanes of
+// real warp et / 32) and the virtual warps' sums added in index order, so
+// the results are bit-identical to the separate kernel.
+template <int NTV>
+__device__ __noinline__ void norm_row(const GemmArgs &a, int t, int et, float *red) {
+  constexpr int M = NTV / 128;
+  const int H = a.N, lane = et & 31, rw = et >> 5;
+  const __nv_bfloat16 *x = static_cast<const __nv_bfloat16 *>(a.y) + (size_t)t * a.ldy;
+  __nv_bfloat16 *res = a.norm_res + (size_t)t * H;
+  // pass 1: res += x (rounded to bf16 once) and the per-virtual-thread sums
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = (et + 128 * m + i * NTV) * 8;
+      if (c < H) {
+        const uint4 xv = __ldcg(reinterpret_cast<const uint4 *>(x + c));  // rows other CTAs wrote
+        const uint4 rv = *reinterpret_cast<const uint4 *>(res + c);
+        const __nv_bfloat16 *xe = reinterpret_cast<const __nv_bfloat16 *>(&xv);
+        const __nv_bfloat16 *re = reinterpret_cast<const __nv_bfloat16 *>(&rv);
+        uint4 ov;
+        __nv_bfloat16 *oe = reinterpret_cast<__nv_bfloat16 *>(&ov);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) oe[j] = __float2bfloat16(__bfloat162float(xe[j]) + __bfloat162float(re[j]));
+        *reinterpret_cast<uint4 *>(res + c) = ov;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float v = __bfloat162float(oe[j]);
+          ss += v * v;
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[rw + 4 * m] = ss;
+  }
+  named_bar(1, kEpiThreads);
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < NTV / 32; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / (float)H + a.norm_eps);
+  // pass 2: the values are the bf16 sums this thread just stored, read back
+#pragma unroll
+  for (int m = 0; m < M; ++m)
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = (et + 128 * m + i * NTV) * 8;
+      if (c < H) {
+        const uint4 rv = *reinterpret_cast<const uint4 *>(res + c);
+        const uint4 wv = *reinterpret_cast<const uint4 *>(a.norm_w + c);
+        const __nv_bfloat16 *re = reinterpret_cast<const __nv_bfloat16 *>(&rv);
+        const __nv_bfloat16 *we = reinterpret_cast<const __nv_bfloat16 *>(&wv);
+        float vv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vv[j] = __bfloat162float(re[j]);
+        uint4 ov;
+        ov.x = pack_bf16x2(vv[0] * inv * __bfloat162float(we[0]), vv[1] * inv * __bfloat162float(we[1]));
+        ov.y = pack_bf16x2(vv[2] * inv * __bfloat162float(we[2]), vv[3] * inv * __bfloat162float(we[3]));
+        ov.z = pack_bf16x2(vv[4] * inv * __bfloat162float(we[4]), vv[5] * inv * __bfloat162float(we[5]));
+        ov.w = pack_bf16x2(vv[6] * inv * __bfloat162float(we[6]), vv[7] * inv * __bfloat162float(we[7]));
+        *reinterpret_cast<uint4 *>(a.norm_out + (size_t)t * H + c) = ov;
+      }
+    }
+  named_bar(1, kEpiThreads);  // red is rewritten by the next row
+}
+
+// Called by all 128 epilogue threads after they wrote output rows
+// [r0, r0 + nrows) of n-tile nt: counts the n-tile against each row and
+// normalises the rows this CTA completed. `scratch` is shared memory of at
+// least (nrows + 4 + 32) words that no other role uses meanwhile.
+__device__ __noinline__ void finish_rows_impl(const Params &p, int r0, int nrows, int et, float *scratch) {
+  const GemmArgs &a = p.a;
+  int *fin = reinterpret_cast<int *>(scratch);
+  int *nfin = fin + nrows;
+  float *red = scratch + nrows + 4;
+  __threadfence();  // this thread's row stores are visible before its count
+  if (et == 0) *nfin = 0;
+  named_bar(1, kEpiThreads);
+  for (int r = et; r < nrows; r += kEpiThreads) {
+    const int t = r0 + r;
+    if (atomicAdd(a.row_cnt + t, 1u) == (uint32_t)(p.n_tiles - 1)) {
+      a.row_cnt[t] = 0u;  // zero for the next call
+      fin[atomicAdd(nfin, 1)] = t;
+    }
+  }
+  __threadfence();  // the other CTAs' stores of the rows we complete are visible to our reads
+  named_bar(1, kEpiThreads);
+  const int nf = *nfin;
+  for (int i = 0; i < nf; ++i) {
+    const int t = fin[i];
+    if (a.N <= 4096)
+      norm_row<256>(a, t, et, red);
+    else if (a.N <= 8192)
+      norm_row<512>(a, t, et, red);
+    else
+      norm_row<1024>(a, t, et, red);
+  }
+  named_bar(1, kEpiThreads);  // scratch reuse by the caller
 }
 
 __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t *p) {
@@ -466,12 +582,66 @@ __device__ __forceinline__ void ll_finish(const GemmArgs &a) {
   }
 }
 
+// One thread's share of a reduced row in the low-latency exchange: poll the
+// four lines of each source (rank order) until both halves carry the call's
+// epoch (bounded), sum in fp32, store 16 output columns.
+__device__ __forceinline__ void reduce_line_row(const GemmArgs &a, const uint4 *mine, int nt, int t, int col,
+                                                uint32_t e) {
+  float acc[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+  for (int src = 0; src < a.world; ++src) {
+    const uint4 *q = mine + (((size_t)src * a.T + t) * a.N + (size_t)nt * BM + col) / 4;
+    uint4 l[4];
+    bool ok = false;
+    uint64_t start = 0;
+    for (uint32_t polls = 0; !ok; ++polls) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) l[i] = ld_volatile_v4(reinterpret_cast<const uint32_t *>(q + i));
+      ok = true;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ok = ok && l[i].y == e && l[i].w == e;
+      if (!ok && (polls & 63u) == 0u) {
+        const uint64_t now = ptx::globaltimer_ns();
+        if (start == 0) {
+          start = now;
+        } else if (now - start > kWaitBudgetNs) {
+          report_status(a.status, kStatusPeerTimeout);
+          break;
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat16 *lo = reinterpret_cast<const __nv_bfloat16 *>(&l[i].x);
+      const __nv_bfloat16 *hi = reinterpret_cast<const __nv_bfloat16 *>(&l[i].z);
+      acc[4 * i] += __bfloat162float(lo[0]);
+      acc[4 * i + 1] += __bfloat162float(lo[1]);
+      acc[4 * i + 2] += __bfloat162float(hi[0]);
+      acc[4 * i + 3] += __bfloat162float(hi[1]);
+    }
+  }
+  uint4 o0, o1;
+  o0.x = pack_bf16x2(acc[0], acc[1]);
+  o0.y = pack_bf16x2(acc[2], acc[3]);
+  o0.z = pack_bf16x2(acc[4], acc[5]);
+  o0.w = pack_bf16x2(acc[6], acc[7]);
+  o1.x = pack_bf16x2(acc[8], acc[9]);
+  o1.y = pack_bf16x2(acc[10], acc[11]);
+  o1.z = pack_bf16x2(acc[12], acc[13]);
+  o1.w = pack_bf16x2(acc[14], acc[15]);
+  uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(a.y) + (size_t)t * a.ldy +
+                                         (size_t)nt * BM + col);
+  dst[0] = o0;
+  dst[1] = o1;
+}
+
 // All-reduce, part 2 of the low-latency exchange: the same owned units and
 // rank-order sums as reduce_owned_chunks, but each thread polls its own four
 // lines per source until they carry the call's epoch (bounded), with no
-// flags, fences or block barriers.
+// flags or fences; the rows of a unit are then counted for the fused norm.
 template <int TN>
-__device__ void reduce_owned_chunks_ll(const Params &p, int c, int et, uint32_t e) {
+__device__ void reduce_owned_chunks_ll(const Params &p, int c, int et, uint32_t e, float *scratch) {
   const GemmArgs &a = p.a;
   constexpr int CH = TN / kSlab;
   const uint4 *mine = reinterpret_cast<const uint4 *>(a.recv[a.rank]) + (size_t)(e & 1u) * a.ll_set_lines;
@@ -481,54 +651,10 @@ __device__ void reduce_owned_chunks_ll(const Params &p, int c, int et, uint32_t 
     const int tile = u / CH, ch = u % CH;
     const int nt = tile / p.t_tiles, tt = tile % p.t_tiles;
     const int t0 = tt * TN + ch * kSlab;
-    if (t0 >= a.T || tl >= min(kSlab, a.T - t0)) continue;
-    const int t = t0 + tl;
-    float acc[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-    for (int src = 0; src < a.world; ++src) {
-      const uint4 *q = mine + (((size_t)src * a.T + t) * a.N + (size_t)nt * BM + col) / 4;
-      uint4 l[4];
-      bool ok = false;
-      uint64_t start = 0;
-      for (uint32_t polls = 0; !ok; ++polls) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) l[i] = ld_volatile_v4(reinterpret_cast<const uint32_t *>(q + i));
-        ok = true;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) ok = ok && l[i].y == e && l[i].w == e;
-        if (!ok && (polls & 63u) == 0u) {
-          const uint64_t now = ptx::globaltimer_ns();
-          if (start == 0) start = now;
-          else if (now - start > kWaitBudgetNs) {
-            report_status(a.status, kStatusPeerTimeout);
-            break;
-          }
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __nv_bfloat16 *lo = reinterpret_cast<const __nv_bfloat16 *>(&l[i].x);
-        const __nv_bfloat16 *hi = reinterpret_cast<const __nv_bfloat16 *>(&l[i].z);
-        acc[4 * i] += __bfloat162float(lo[0]);
-        acc[4 * i + 1] += __bfloat162float(lo[1]);
-        acc[4 * i + 2] += __bfloat162float(hi[0]);
-        acc[4 * i + 3] += __bfloat162float(hi[1]);
-      }
-    }
-    uint4 o0, o1;
-    o0.x = pack_bf16x2(acc[0], acc[1]);
-    o0.y = pack_bf16x2(acc[2], acc[3]);
-    o0.z = pack_bf16x2(acc[4], acc[5]);
-    o0.w = pack_bf16x2(acc[6], acc[7]);
-    o1.x = pack_bf16x2(acc[8], acc[9]);
-    o1.y = pack_bf16x2(acc[10], acc[11]);
-    o1.z = pack_bf16x2(acc[12], acc[13]);
-    o1.w = pack_bf16x2(acc[14], acc[15]);
-    uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(a.y) + (size_t)t * a.ldy +
-                                           (size_t)nt * BM + col);
-    dst[0] = o0;
-    dst[1] = o1;
+    if (t0 >= a.T) continue;  // uniform across the CTA
+    const int tmax = min(kSlab, a.T - t0);
+    if (tl < tmax) reduce_line_row(a, mine, nt, t0 + tl, col, e);
+    finish_rows(p, t0, tmax, et, scratch);
   }
 }
 
@@ -705,6 +831,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_arrive(&acc_empty[ab]);  // the MMA warp may refill this accumulator
       if (EPI == kEpiAllReduce && direct && !ll) publish_tile<TN>(p, s.tile, et);
       if (EPI == kEpiReduceScatter && direct) publish_rows_rs<TN>(p, s.tile, 0, min(TN, a.T - t0), et);
+      if (EPI == kEpiStore && direct) finish_rows(p, t0, min(TN, a.T - t0), et, slab);
       if (!direct) {
         __threadfence();
         named_bar(1, kEpiThreads);
@@ -761,6 +888,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (et == 0) a.counters[s.tile] = 0u;
           if (EPI == kEpiAllReduce && !ll) publish_tile<TN>(p, s.tile, et);
           if (EPI == kEpiReduceScatter) publish_rows_rs<TN>(p, s.tile, 0, tmax, et);
+          if (EPI == kEpiStore) finish_rows(p, t0, tmax, et, slab);
         }
         named_bar(1, kEpiThreads);  // last_flag is rewritten by the next segment
       }
@@ -772,9 +900,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (EPI == kEpiAllReduce) {
       if (ll)
-        reduce_owned_chunks_ll<TN>(p, c, et, ll_e);
+        reduce_owned_chunks_ll<TN>(p, c, et, ll_e, slab);
       else
-        reduce_owned_chunks<TN>(p, c, et);
+        reduce_owned_chunks<TN>(p, c, et, slab);
     }
   }
 
@@ -967,6 +1095,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mbar_arrive(&acc_empty[ab]);
         if (EPI == kEpiAllReduce && !ll) publish_rows<TN>(p, tile, 0, tvalid, et);
         if (EPI == kEpiReduceScatter) publish_rows_rs<TN>(p, tile, 0, tvalid, et);
+        if (EPI == kEpiStore) finish_rows(p, t0, tvalid, et, slab);
         continue;
       }
       // our partial may overwrite `red` once every peer has read the previous one
@@ -1028,12 +1157,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s2 = 0; s2 < CS; ++s2) ptx::mbar_arrive_cluster(ptx::mapa_shared(free_addr, s2));
       if (EPI == kEpiAllReduce && !ll) publish_rows<TN>(p, tile, lo, hi, et);
       if (EPI == kEpiReduceScatter) publish_rows_rs<TN>(p, tile, lo, hi, et);
+      if (EPI == kEpiStore) finish_rows(p, t0 + lo, hi - lo, et, slab);
     }
     if (EPI == kEpiAllReduce) {
       if (ll)
-        reduce_owned_chunks_ll<TN>(p, blockIdx.x, et, ll_e);
+        reduce_owned_chunks_ll<TN>(p, blockIdx.x, et, ll_e, slab);
       else
-        reduce_owned_chunks<TN>(p, blockIdx.x, et);
+        reduce_owned_chunks<TN>(p, blockIdx.x, et, slab);
     }
   }
 
@@ -1346,6 +1476,10 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
                               a.pos == nullptr || a.slot == nullptr))
     return -6;
   if (a.x_ready != nullptr && (reinterpret_cast<uintptr_t>(a.x_ready) & 15) != 0) return -7;
+  if (a.norm_w != nullptr && (!(a.epi == kEpiStore || a.epi == kEpiAllReduce) || a.norm_res == nullptr ||
+                              a.norm_out == nullptr || a.row_cnt == nullptr || a.y == nullptr || a.N % 8 != 0 ||
+                              a.N > 16384 || a.ldy % 8 != 0))
+    return -11;
   if (a.epi == kEpiAllReduce || a.epi == kEpiReduceScatter) {
     if (a.world < 1 || a.world > kMaxWorld || a.rank < 0 || a.rank >= a.world) return -7;
     const bool ll = a.epi == kEpiAllReduce && a.ll_state != nullptr;

@@ -85,6 +85,18 @@ struct GemmArgs {
   // both halves carry the call's epoch, so no fence, flag or reset is needed.
   uint32_t *ll_state;
   long long ll_set_lines;
+  // Residual add + RMSNorm after the projection (kEpiStore, kEpiAllReduce;
+  // norm_w != nullptr): once every n-tile of output row t is written to y,
+  // the CTA that wrote the last one sets norm_res[t] += y[t] (bf16) and
+  // norm_out[t] = rmsnorm(norm_res[t]) * norm_w, with the arithmetic and
+  // reduction order of sched_add_rmsnorm (bit-identical results). row_cnt:
+  // u32 [>= T] counters, zero between calls (the finishing CTA resets them).
+  // Rows of norm_res / norm_out have N elements (contiguous); N <= 16384.
+  __nv_bfloat16 *norm_res;
+  const __nv_bfloat16 *norm_w;
+  __nv_bfloat16 *norm_out;
+  uint32_t *row_cnt;
+  float norm_eps;
 };
 
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream);

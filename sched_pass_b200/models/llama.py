@@ -14,6 +14,7 @@ the decode kernel (rows [0, n_decode)) and the prefill kernel (the rest).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -158,6 +159,10 @@ def shard_weights(cfg: ModelConfig, full: ModelWeights, rank: int, world: int, d
                         vocab_offset=rank * v_local)
 
 
+# residual add + RMSNorm inside the row-parallel projections (0: separate kernel)
+FUSED_NORM = os.environ.get("SCHED_FUSED_NORM", "1") != "0"
+
+
 @dataclass
 class ForwardBatch:
     """Device inputs of one forward (static buffers when graph-captured)."""
@@ -252,6 +257,20 @@ class Llama:
             return ops.linear(x, w, out)
         return self.tp.linear_allreduce(x, w, out)
 
+    def _row_linear_norm(self, x, w, out, res, nw, normed) -> None:
+        """out = row-parallel x @ w.T, then res += out and normed =
+        rmsnorm(res) * nw: in the projection kernel itself (the CTA that
+        finishes a token row normalises it; ``SCHED_FUSED_NORM=0`` runs the
+        separate add_rmsnorm kernel instead, with identical results)."""
+        eps = self.cfg.rms_eps
+        if not FUSED_NORM:
+            self._row_linear(x, w, out)
+            ops.add_rmsnorm(out, res, nw, eps, normed)
+        elif self.tp is None:
+            ops.linear_add_rmsnorm(x, w, out, res, nw, eps, normed)
+        else:
+            self.tp.linear_allreduce(x, w, out, norm=(res, nw, eps, normed))
+
     def _attention(self, li: int, b: ForwardBatch) -> None:
         kc, vc = self.kv.k[li], self.kv.v[li]
         nd = b.n_decode
@@ -318,22 +337,20 @@ class Llama:
         ops.embedding(b.ids[:T], self.w.embed, h, prev=b.out_ids)
         if b.tier is not None:
             b.tier.begin_forward()
-        for li, lw in enumerate(self.w.layers):
-            if li == 0:
-                ops.add_rmsnorm(h, None, lw.ln_in, cfg.rms_eps, normed)
-            else:
-                ops.add_rmsnorm(delta, h, lw.ln_in, cfg.rms_eps, normed)
+        layers = self.w.layers
+        ops.add_rmsnorm(h, None, layers[0].ln_in, cfg.rms_eps, normed)
+        for li, lw in enumerate(layers):
+            # normed holds this layer's input norm: from the embedding (layer 0)
+            # or from the previous layer's down_proj
             ops.linear_qkv_rope(normed, lw.qkv, b.pos[:T], b.slot[:T], self.cos_sin, self.q[:T],
                                 self.kv.k[li], self.kv.v[li], self.hq, self.hkv)
             self._attention(li, b)
-            self._row_linear(self.attn[:T].view(T, -1), lw.o, delta)
-            ops.add_rmsnorm(delta, h, lw.ln_post, cfg.rms_eps, normed)
-            d = self._mlp(li, normed, T)
-            if d is not delta:
-                delta.copy_(d)
+            self._row_linear_norm(self.attn[:T].view(T, -1), lw.o, delta, h, lw.ln_post, normed)
+            act = ops.linear(normed, lw.gate_up, self.act[:T], swiglu=True)
+            nxt = layers[li + 1].ln_in if li + 1 < len(layers) else self.w.ln_final
+            self._row_linear_norm(act, lw.down, delta, h, nxt, normed)
         if b.tier is not None:
             b.tier.end_forward()
-        ops.add_rmsnorm(delta, h, self.w.ln_final, cfg.rms_eps, normed)
         return self.sample(b)
 
     def sample(self, b: ForwardBatch) -> torch.Tensor:

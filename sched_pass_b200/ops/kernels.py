@@ -114,8 +114,46 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *,
         out = torch.empty(T, N // 2 if swiglu else N, dtype=torch.bfloat16, device=x.device)
     ws = _ws_for(x, N, K, grid, ws)
     ext().gemm(x, w, out, 1 if swiglu else 0, int(grid), ws.ws, ws.counters, status_buffer(x.device),
-               int(x_ready))
+               int(x_ready), None, None, None, None, 0.0)
     return out
+
+
+def linear_add_rmsnorm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, residual: torch.Tensor,
+                       norm_weight: torch.Tensor, eps: float, normed: torch.Tensor, *, grid: int = 0,
+                       ws: Workspace | None = None) -> torch.Tensor:
+    """out = x @ w.T, then residual += out and normed = rmsnorm(residual) *
+    norm_weight in the same kernel: the CTA that writes the last column tile
+    of a token row normalises that row, with the arithmetic of
+    ``add_rmsnorm`` (bit-identical). Returns normed."""
+    T, K = x.shape
+    N = w.shape[0]
+    ws = _ws_for(x, N, K, grid, ws)
+    ext().gemm(x, w, out, 0, int(grid), ws.ws, ws.counters, status_buffer(x.device), 0, residual,
+               norm_weight, normed, row_counters(x.device, T), float(eps))
+    return normed
+
+
+_row_cnt: dict[int, torch.Tensor] = {}
+
+
+def row_counters(device, n: int) -> torch.Tensor:
+    """Per-device int32 row counters of the fused norm (zero between calls:
+    the kernel that uses a counter resets it). One fixed buffer per device,
+    never replaced (CUDA graphs hold its address); calls on one device share
+    it, so they must be ordered on one stream."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    with _lock:
+        t = _row_cnt.get(idx)
+        if t is None:
+            t = torch.zeros(ROW_COUNTERS, dtype=torch.int32, device=f"cuda:{idx}")
+            _row_cnt[idx] = t
+    if n > t.numel():
+        raise ValueError(f"fused norm over {n} rows: at most {t.numel()} per call")
+    return t
+
+
+ROW_COUNTERS = 16384
 
 
 def linear_qkv_rope(x, w, pos, slot, cos_sin, q_out, k_cache, v_cache, n_q_heads, n_kv_heads, *,

@@ -62,24 +62,32 @@ class FusedAllReduce:
         else:
             self.ll = None
 
-    def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, norm=None) -> torch.Tensor:
+        """out = the all-reduced x @ w.T. ``norm = (residual, weight, eps,
+        normed)`` also applies residual += out and normed = rmsnorm(residual)
+        * weight inside the kernel (every rank, on its own copies)."""
         T, K = x.shape
         N = w.shape[0]
         if T > self.max_tokens or N > self.max_n:
             raise ValueError(f"fused all-reduce sized for T<={self.max_tokens}, N<={self.max_n}")
         self.calls += 1
         ws = ops.kernels._ws_for(x, N, K, 0, None)
+        if norm is not None:
+            res, nw, eps, normed = norm
+            nargs = (res, nw, normed, ops.kernels.row_counters(x.device, T), float(eps))
+        else:
+            nargs = (None, None, None, None, 0.0)
         if self.ll is not None and T <= self.ll_max_tokens:
             self.ll_calls += 1
             self._ll_last = True
             ext().gemm_allreduce(x, w, out, self.rank, self.world, self.ll.ptrs, [], 0, ws.ws, ws.counters,
-                                 ops.status_buffer(x.device), self.ll_state, self.ll_set_lines)
+                                 ops.status_buffer(x.device), self.ll_state, self.ll_set_lines, *nargs)
             return out
         self._ll_last = False
         slab, flags = self.sets[self.k]
         self.k ^= 1
         ext().gemm_allreduce(x, w, out, self.rank, self.world, slab.ptrs, flags.ptrs, 0, ws.ws,
-                             ws.counters, ops.status_buffer(x.device), None, 0)
+                             ws.counters, ops.status_buffer(x.device), None, 0, *nargs)
         return out
 
     def last_slab(self, T: int, N: int) -> torch.Tensor:

@@ -89,15 +89,25 @@ class TensorParallel:
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
         return float(t.item())
 
-    def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, norm=None) -> torch.Tensor:
+        """Row-parallel projection. ``norm = (residual, weight, eps, normed)``
+        also applies residual += out and normed = rmsnorm(residual) * weight:
+        inside the fused kernel, or as a separate add_rmsnorm after NCCL."""
         if self.world == 1:
+            if norm is not None:
+                res, nw, eps, normed = norm
+                ops.linear_add_rmsnorm(x, w, out, res, nw, eps, normed)
+                return out
             return ops.linear(x, w, out)
         if self._fused is not None and self.use_fused(x.shape[0], w.shape[0]):
             self.fused_calls += 1
-            return self._fused.linear_allreduce(x, w, out)
+            return self._fused.linear_allreduce(x, w, out, norm=norm)
         self.nccl_calls += 1
         ops.linear(x, w, out)
         dist.all_reduce(out, group=self.group)
+        if norm is not None:
+            res, nw, eps, normed = norm
+            ops.add_rmsnorm(out, res, nw, eps, normed)
         return out
 
     def sharded_argmax(self, rows: torch.Tensor, lm_head: torch.Tensor, vocab_offset: int, vocab: int,

@@ -371,3 +371,31 @@ def test_prefill_attention(qlens, prefix):
         r = ref.attention(q[row:row + ql], k, v, 1 / math.sqrt(D), causal_offset=pf)
         assert rel_err(out[row:row + ql], r) < 2e-2
         row += ql
+
+
+@pytest.mark.parametrize("T,N,K,grid", [
+    (1, 4096, 4096, 0), (6, 4096, 4096, 0), (16, 4096, 14336, 0), (6, 4096, 4096, 148),
+    (100, 4096, 4096, 0), (300, 4096, 14336, 0), (1541, 4096, 4096, 0), (6, 8192, 1024, 0), (5, 12288, 512, 0),
+])
+def test_linear_add_rmsnorm_fused_matches_separate_kernels(T, N, K, grid):
+    """The projection with the residual add + RMSNorm in its epilogue gives
+    the same bits as the GEMM followed by add_rmsnorm (cluster split-K and
+    stream-K schedules, hidden sizes using 256, 512 and 1024 virtual norm
+    threads), twice in a row (the row counters reset themselves)."""
+    g = torch.Generator(device="cuda").manual_seed(T + N + K)
+    x = torch.randn(T, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    res0 = torch.randn(T, N, device="cuda", generator=g).to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(N, device="cuda", generator=g)).to(torch.bfloat16)
+    y1 = ops.linear(x, w, grid=grid)
+    r1 = res0.clone()
+    n1 = ops.add_rmsnorm(y1, r1, nw, 1e-5)
+    for _ in range(2):
+        y2 = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+        r2 = res0.clone()
+        n2 = torch.empty_like(r2)
+        ops.linear_add_rmsnorm(x, w, y2, r2, nw, 1e-5, n2, grid=grid)
+        torch.cuda.synchronize()
+        ops.check_status()
+        assert torch.equal(y2, y1) and torch.equal(r2, r1) and torch.equal(n2, n1)
+    assert int(ops.kernels.row_counters(x.device, T)[:T].abs().sum()) == 0

@@ -36,6 +36,7 @@ def test_fused_allreduce_and_tp_engine():
         assert c["rel_err"] < 1e-2, c
         assert c["identical_on_ranks"], c
         assert c["matches_protocol_oracle"], c
+        assert c["fused_norm_exact"], c
     # bf16 partial sums across ranks round differently from one GPU's GEMM,
     # so greedy paths may diverge late; the first tokens must agree
     assert all(res["first_token_match"]), res

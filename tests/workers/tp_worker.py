@@ -40,8 +40,18 @@ def main():
         ys = [torch.empty_like(y) for _ in range(world)]
         dist.all_gather(ys, y)
         same = all(torch.equal(ys[0], z) for z in ys)
+        # residual add + RMSNorm inside the fused kernel == the separate kernel
+        res0 = torch.randn(T, N, generator=g).to(torch.bfloat16).to(dev)
+        nw = (1 + 0.1 * torch.randn(N, generator=g)).to(torch.bfloat16).to(dev)
+        r1 = res0.clone()
+        n1 = ops.add_rmsnorm(y, r1, nw, 1e-5)
+        y2, r2 = torch.empty_like(y), res0.clone()
+        n2 = torch.empty_like(r2)
+        tp.linear_allreduce(x, w, y2, norm=(r2, nw, 1e-5, n2))
+        torch.cuda.synchronize()
+        norm_ok = bool(torch.equal(y2, y) and torch.equal(r2, r1) and torch.equal(n2, n1))
         out["checks"].append({"T": T, "N": N, "K": K, "rel_err": err, "identical_on_ranks": same,
-                              "matches_protocol_oracle": oracle_ok})
+                              "matches_protocol_oracle": oracle_ok, "fused_norm_exact": norm_ok})
     ops.check_status()
     # engine: TP generation == single-GPU generation
     from sched_pass_b200.engine.engine import Engine, EngineConfig
