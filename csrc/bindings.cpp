@@ -53,6 +53,9 @@ extern "C" int sched_probe_tasks(const uint32_t *cost, int n_tasks, int mode, in
                                  const void *data, size_t data_bytes, unsigned *hits, unsigned *per_cta,
                                  unsigned *ticket, unsigned *sink, int *status, cudaStream_t st);
 extern "C" int sched_probe_tasks_occupancy();
+extern "C" int sched_argmax_exchange(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
+                                     int id_offset, void *const *lines, int world, int rank, uint32_t *state,
+                                     long long set_lines, int *status, cudaStream_t st);
 extern "C" int sched_probe_clc(const uint32_t *work, int n_tasks, int mode, int grid, int max_rec, unsigned *hits,
                                unsigned long long *rec, unsigned *n_rec, unsigned *smid, int *status,
                                cudaStream_t st);
@@ -500,6 +503,28 @@ void embedding(const at::Tensor &ids, const at::Tensor &table, at::Tensor &out,
   check_rc(rc_, "embedding");
 }
 
+void argmax_exchange(const at::Tensor &logits, at::Tensor &ids, int64_t id_offset,
+                     const std::vector<int64_t> &lines, int64_t rank, at::Tensor &state, int64_t set_lines,
+                     const c10::optional<at::Tensor> &status) {
+  check_bf16(logits, "logits");
+  check_i32(ids, "ids");
+  check_i32(state, "state");
+  const int64_t world = (int64_t)lines.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && rank >= 0 && rank < world, "one line buffer per rank (<= 8)");
+  TORCH_CHECK(state.numel() >= 2 && set_lines >= world * logits.size(0), "state [2]; set_lines >= world x rows");
+  std::vector<void *> ptrs(world);
+  for (int64_t j = 0; j < world; ++j) ptrs[j] = reinterpret_cast<void *>(lines[j]);
+  int rc_ = 0;
+  {  // the guard is gone before check_rc may throw
+    c10::cuda::CUDAGuard g(logits.device());
+    rc_ = sched_argmax_exchange(logits.data_ptr(), logits.size(0), logits.size(1), logits.stride(0),
+                                ids.data_ptr<int32_t>(), nullptr, id_offset, ptrs.data(), (int)world, (int)rank,
+                                reinterpret_cast<uint32_t *>(state.data_ptr<int32_t>()), set_lines,
+                                ptr_or_null<int>(status), cur_stream());
+  }
+  check_rc(rc_, "argmax_exchange");
+}
+
 void argmax(const at::Tensor &logits, at::Tensor &ids, const c10::optional<at::Tensor> &maxv,
             int64_t id_offset) {
   check_bf16(logits, "logits");
@@ -788,6 +813,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_kv_append", &rope_kv_append);
   m.def("embedding", &embedding);
   m.def("argmax", &argmax);
+  m.def("argmax_exchange", &argmax_exchange);
   m.def("set_gemm_trace", &set_gemm_trace);
   m.def("gemm_plan", [](int64_t T, int64_t N, int64_t K, int64_t epi, int64_t sms) {
     int cs = 0, grid = 0;

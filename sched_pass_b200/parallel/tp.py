@@ -57,6 +57,14 @@ class TensorParallel:
         if self.mode == "fused" and self.world > 1:
             from .fused import FusedAllReduce
             self._fused = FusedAllReduce(self.group, self.device)
+        # sampling exchange: two sets of [world][rows] 16-byte lines per rank
+        self._sample = None
+        self._sample_rows = 1024
+        if self.world > 1 and os.environ.get("SCHED_TP_SAMPLE", "exchange") != "nccl":
+            from .symm import SymmetricBuffer
+            self._sample_set_lines = self.world * self._sample_rows
+            self._sample = SymmetricBuffer(2 * self._sample_set_lines * 16, self.group)
+            self._sample_state = torch.zeros(2, dtype=torch.int32, device=self.device)
 
     def sequence_parallel(self, hidden: int, max_tokens: int):
         """The sequence-parallel buffers of this group (``mode == "sp"``) for
@@ -112,12 +120,19 @@ class TensorParallel:
 
     def sharded_argmax(self, rows: torch.Tensor, lm_head: torch.Tensor, vocab_offset: int, vocab: int,
                        out: torch.Tensor) -> torch.Tensor:
-        """Greedy token over a vocabulary split across ranks: local logits and
-        local (max, argmax), exchange the pairs, keep the best (lowest global
-        id on ties)."""
+        """Greedy token over a vocabulary split across ranks: local logits, then
+        one kernel that takes each row's local (max, argmax), exchanges the
+        pairs with every rank over NVLink and keeps the best (lowest global id
+        on ties); the same on every rank. ``SCHED_TP_SAMPLE=nccl`` (or more
+        rows than the exchange holds) keeps the all-gather of the pairs."""
         S = rows.shape[0]
         logits = ops.linear(rows, lm_head)
         v_local = min(lm_head.shape[0], max(0, vocab - vocab_offset))
+        if self._sample is not None and S <= self._sample_rows:
+            ext = ops.kernels.ext()
+            ext.argmax_exchange(logits[:, :v_local], out[:S], int(vocab_offset), self._sample.ptrs, self.rank,
+                                self._sample_state, self._sample_set_lines, ops.status_buffer(rows.device))
+            return out
         ids = torch.empty(S, dtype=torch.int32, device=rows.device)
         mx = torch.empty(S, dtype=torch.float32, device=rows.device)
         ops.argmax(logits[:, :v_local], ids, mx, vocab_offset)

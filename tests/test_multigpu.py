@@ -37,6 +37,9 @@ def test_fused_allreduce_and_tp_engine():
         assert c["identical_on_ranks"], c
         assert c["matches_protocol_oracle"], c
         assert c["fused_norm_exact"], c
+    for smp in res["sampling"]:
+        assert smp["exchange_equals_allgather"], smp
+        assert smp["agrees_with_fp32"] >= 0.9, smp
     # bf16 partial sums across ranks round differently from one GPU's GEMM,
     # so greedy paths may diverge late; the first tokens must agree
     assert all(res["first_token_match"]), res

@@ -53,6 +53,27 @@ def main():
         out["checks"].append({"T": T, "N": N, "K": K, "rel_err": err, "identical_on_ranks": same,
                               "matches_protocol_oracle": oracle_ok, "fused_norm_exact": norm_ok})
     ops.check_status()
+    # greedy sampling over a vocabulary split across ranks: the in-kernel
+    # exchange of (max, id) pairs == the all-gather of the pairs
+    H, V = 512, 1000 * world + 7
+    vloc = (V + world - 1) // world
+    lm = (torch.randn(vloc * world, H, generator=g) / H ** 0.5).to(torch.bfloat16)
+    lm_local = lm[rank * vloc:(rank + 1) * vloc].to(dev).contiguous()
+    samples = []
+    for S in (1, 6, 100):
+        rows = torch.randn(S, H, generator=g).to(torch.bfloat16).to(dev)
+        a = torch.empty(S, dtype=torch.int32, device=dev)
+        b = torch.empty(S, dtype=torch.int32, device=dev)
+        tp.sharded_argmax(rows, lm_local, rank * vloc, V, a)
+        saved, tp._sample = tp._sample, None
+        tp.sharded_argmax(rows, lm_local, rank * vloc, V, b)
+        tp._sample = saved
+        torch.cuda.synchronize()
+        want = (rows.float().cpu() @ lm[:V].float().t()).argmax(1)
+        samples.append({"S": S, "exchange_equals_allgather": bool(torch.equal(a, b)),
+                        "agrees_with_fp32": float((a.cpu().long() == want).float().mean())})
+    out["sampling"] = samples
+    ops.check_status()
     # engine: TP generation == single-GPU generation
     from sched_pass_b200.engine.engine import Engine, EngineConfig
     from sched_pass_b200.models.config import LLAMA_TINY, ModelConfig
