@@ -98,9 +98,17 @@ struct Params {
 
 // Residual add + RMSNorm of the output rows a CTA completes (defined below;
 // out of line, and only called when the launch fuses the norm).
-__device__ __noinline__ void finish_rows_impl(const Params &p, int r0, int nrows, int et, float *scratch);
+// Only scalars cross this call: taking the address of the kernel's Params
+// (a reference argument) would make the compiler copy them to local memory
+// for the whole kernel.
+__device__ __noinline__ void finish_rows_impl(const __nv_bfloat16 *y, int ldy, int N, __nv_bfloat16 *res,
+                                              const __nv_bfloat16 *w, __nv_bfloat16 *out, uint32_t *cnt, float eps,
+                                              int n_tiles, int r0, int nrows, int et, float *scratch);
 __device__ __forceinline__ void finish_rows(const Params &p, int r0, int nrows, int et, float *scratch) {
-  if (p.a.norm_w != nullptr && nrows > 0) finish_rows_impl(p, r0, nrows, et, scratch);
+  const GemmArgs &a = p.a;
+  if (a.norm_w != nullptr && nrows > 0)
+    finish_rows_impl(static_cast<const __nv_bfloat16 *>(a.y), a.ldy, a.N, a.norm_res, a.norm_w, a.norm_out,
+                     a.row_cnt, a.norm_eps, p.n_tiles, r0, nrows, et, scratch);
 }
 
 // One segment: the k-block range [kb0, kb1) of `tile` handled by one CTA.
@@ -460,11 +468,13 @@ __device__ void reduce_owned_chunks(const Params &p, int c, int et, float *scrat
 // real warp et / 32) and the virtual warps' sums added in index order, so
 // the results are bit-identical to the separate kernel.
 template <int NTV>
-__device__ __noinline__ void norm_row(const GemmArgs &a, int t, int et, float *red) {
+__device__ __forceinline__ void norm_row(const __nv_bfloat16 *y, int ldy, int H, __nv_bfloat16 *res_base,
+                                         const __nv_bfloat16 *nw, __nv_bfloat16 *out, float eps, int t, int et,
+                                         float *red) {
   constexpr int M = NTV / 128;
-  const int H = a.N, lane = et & 31, rw = et >> 5;
-  const __nv_bfloat16 *x = static_cast<const __nv_bfloat16 *>(a.y) + (size_t)t * a.ldy;
-  __nv_bfloat16 *res = a.norm_res + (size_t)t * H;
+  const int lane = et & 31, rw = et >> 5;
+  const __nv_bfloat16 *x = y + (size_t)t * ldy;
+  __nv_bfloat16 *res = res_base + (size_t)t * H;
   // pass 1: res += x (rounded to bf16 once) and the per-virtual-thread sums
 #pragma unroll
   for (int m = 0; m < M; ++m) {
@@ -497,7 +507,7 @@ __device__ __noinline__ void norm_row(const GemmArgs &a, int t, int et, float *r
   float tot = 0.f;
 #pragma unroll
   for (int i = 0; i < NTV / 32; ++i) tot += red[i];
-  const float inv = rsqrtf(tot / (float)H + a.norm_eps);
+  const float inv = rsqrtf(tot / (float)H + eps);
   // pass 2: the values are the bf16 sums this thread just stored, read back
 #pragma unroll
   for (int m = 0; m < M; ++m)
@@ -506,7 +516,7 @@ __device__ __noinline__ void norm_row(const GemmArgs &a, int t, int et, float *r
       const int c = (et + 128 * m + i * NTV) * 8;
       if (c < H) {
         const uint4 rv = *reinterpret_cast<const uint4 *>(res + c);
-        const uint4 wv = *reinterpret_cast<const uint4 *>(a.norm_w + c);
+        const uint4 wv = *reinterpret_cast<const uint4 *>(nw + c);
         const __nv_bfloat16 *re = reinterpret_cast<const __nv_bfloat16 *>(&rv);
         const __nv_bfloat16 *we = reinterpret_cast<const __nv_bfloat16 *>(&wv);
         float vv[8];
@@ -517,7 +527,7 @@ __device__ __noinline__ void norm_row(const GemmArgs &a, int t, int et, float *r
         ov.y = pack_bf16x2(vv[2] * inv * __bfloat162float(we[2]), vv[3] * inv * __bfloat162float(we[3]));
         ov.z = pack_bf16x2(vv[4] * inv * __bfloat162float(we[4]), vv[5] * inv * __bfloat162float(we[5]));
         ov.w = pack_bf16x2(vv[6] * inv * __bfloat162float(we[6]), vv[7] * inv * __bfloat162float(we[7]));
-        *reinterpret_cast<uint4 *>(a.norm_out + (size_t)t * H + c) = ov;
+        *reinterpret_cast<uint4 *>(out + (size_t)t * H + c) = ov;
       }
     }
   named_bar(1, kEpiThreads);  // red is rewritten by the next row
@@ -527,8 +537,9 @@ __device__ __noinline__ void norm_row(const GemmArgs &a, int t, int et, float *r
 // [r0, r0 + nrows) of n-tile nt: counts the n-tile against each row and
 // normalises the rows this CTA completed. `scratch` is shared memory of at
 // least (nrows + 4 + 32) words that no other role uses meanwhile.
-__device__ __noinline__ void finish_rows_impl(const Params &p, int r0, int nrows, int et, float *scratch) {
-  const GemmArgs &a = p.a;
+__device__ __noinline__ void finish_rows_impl(const __nv_bfloat16 *y, int ldy, int N, __nv_bfloat16 *res,
+                                              const __nv_bfloat16 *w, __nv_bfloat16 *out, uint32_t *cnt, float eps,
+                                              int n_tiles, int r0, int nrows, int et, float *scratch) {
   int *fin = reinterpret_cast<int *>(scratch);
   int *nfin = fin + nrows;
   float *red = scratch + nrows + 4;
@@ -537,8 +548,8 @@ __device__ __noinline__ void finish_rows_impl(const Params &p, int r0, int nrows
   named_bar(1, kEpiThreads);
   for (int r = et; r < nrows; r += kEpiThreads) {
     const int t = r0 + r;
-    if (atomicAdd(a.row_cnt + t, 1u) == (uint32_t)(p.n_tiles - 1)) {
-      a.row_cnt[t] = 0u;  // zero for the next call
+    if (atomicAdd(cnt + t, 1u) == (uint32_t)(n_tiles - 1)) {
+      cnt[t] = 0u;  // zero for the next call
       fin[atomicAdd(nfin, 1)] = t;
     }
   }
@@ -547,12 +558,12 @@ __device__ __noinline__ void finish_rows_impl(const Params &p, int r0, int nrows
   const int nf = *nfin;
   for (int i = 0; i < nf; ++i) {
     const int t = fin[i];
-    if (a.N <= 4096)
-      norm_row<256>(a, t, et, red);
-    else if (a.N <= 8192)
-      norm_row<512>(a, t, et, red);
+    if (N <= 4096)
+      norm_row<256>(y, ldy, N, res, w, out, eps, t, et, red);
+    else if (N <= 8192)
+      norm_row<512>(y, ldy, N, res, w, out, eps, t, et, red);
     else
-      norm_row<1024>(a, t, et, red);
+      norm_row<1024>(y, ldy, N, res, w, out, eps, t, et, red);
   }
   named_bar(1, kEpiThreads);  // scratch reuse by the caller
 }
