@@ -580,17 +580,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (sh.merge_last) {
             __threadfence();
             const int part0 = ti.req * p.splits;
+            constexpr int SMAX = 8;  // the engine splits a request at most 8 ways
 #pragma unroll
             for (int h = 0; h < G; ++h) {
-              float mx = -INFINITY;
-              for (int s2 = 0; s2 < p.splits; ++s2)
-                mx = fmaxf(mx, __ldcg(&p.part_lse[(size_t)(part0 + s2) * p.Hq + hq0 + h]));
-              float acc = 0.f, wsum = 0.f;
-              if (mx != -INFINITY) {
-                for (int s2 = 0; s2 < p.splits; ++s2) {  // fixed order: deterministic
-                  const float w = exp2f(__ldcg(&p.part_lse[(size_t)(part0 + s2) * p.Hq + hq0 + h]) - mx);
-                  acc += w * __ldcg(&p.part_o[((size_t)(part0 + s2) * p.Hq + hq0 + h) * D + t]);
-                  wsum += w;
+              float mx = -INFINITY, acc = 0.f, wsum = 0.f;
+              if (p.splits <= SMAX) {
+                // every split's LSE and partial row of this head in one round of
+                // independent loads (a loop over splits would wait for each)
+                float lse[SMAX], po[SMAX];
+#pragma unroll
+                for (int s2 = 0; s2 < SMAX; ++s2) {
+                  lse[s2] = s2 < p.splits ? __ldcg(&p.part_lse[(size_t)(part0 + s2) * p.Hq + hq0 + h]) : -INFINITY;
+                  po[s2] = s2 < p.splits ? __ldcg(&p.part_o[((size_t)(part0 + s2) * p.Hq + hq0 + h) * D + t]) : 0.f;
+                }
+#pragma unroll
+                for (int s2 = 0; s2 < SMAX; ++s2)
+                  if (s2 < p.splits) mx = fmaxf(mx, lse[s2]);
+                if (mx != -INFINITY) {
+#pragma unroll
+                  for (int s2 = 0; s2 < SMAX; ++s2) {  // fixed order: deterministic
+                    if (s2 < p.splits) {
+                      const float w = exp2f(lse[s2] - mx);
+                      acc += w * po[s2];
+                      wsum += w;
+                    }
+                  }
+                }
+              } else {
+                for (int s2 = 0; s2 < p.splits; ++s2)
+                  mx = fmaxf(mx, __ldcg(&p.part_lse[(size_t)(part0 + s2) * p.Hq + hq0 + h]));
+                if (mx != -INFINITY) {
+                  for (int s2 = 0; s2 < p.splits; ++s2) {  // fixed order: deterministic
+                    const float w = exp2f(__ldcg(&p.part_lse[(size_t)(part0 + s2) * p.Hq + hq0 + h]) - mx);
+                    acc += w * __ldcg(&p.part_o[((size_t)(part0 + s2) * p.Hq + hq0 + h) * D + t]);
+                    wsum += w;
+                  }
                 }
               }
               p.out[((size_t)ti.req * p.Hq + hq0 + h) * D + t] =
