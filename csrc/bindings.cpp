@@ -53,6 +53,7 @@ extern "C" int sched_probe_tasks(const uint32_t *cost, int n_tasks, int mode, in
                                  const void *data, size_t data_bytes, unsigned *hits, unsigned *per_cta,
                                  unsigned *ticket, unsigned *sink, int *status, cudaStream_t st);
 extern "C" int sched_probe_tasks_occupancy();
+extern "C" void sched_attn_decode_set_trace(unsigned long long *trace);
 extern "C" int sched_argmax_exchange(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
                                      int id_offset, void *const *lines, int world, int rank, uint32_t *state,
                                      long long set_lines, int *status, cudaStream_t st);
@@ -108,6 +109,7 @@ int num_sms(const at::Tensor &t) {
 
 // Diagnostic: when set, every GEMM launch records per-CTA timestamps here.
 unsigned long long *g_gemm_trace = nullptr;
+void set_attn_trace(int64_t ptr) { sched_attn_decode_set_trace(reinterpret_cast<unsigned long long *>(ptr)); }
 void set_gemm_trace(int64_t ptr) { g_gemm_trace = reinterpret_cast<unsigned long long *>(ptr); }
 
 // Residual add + RMSNorm fused after the projection: res += y, out = rmsnorm(res) * nw
@@ -815,6 +817,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax);
   m.def("argmax_exchange", &argmax_exchange);
   m.def("set_gemm_trace", &set_gemm_trace);
+  m.def("set_attn_trace", &set_attn_trace);
   m.def("gemm_plan", [](int64_t T, int64_t N, int64_t K, int64_t epi, int64_t sms) {
     int cs = 0, grid = 0;
     sched_gemm_plan(T, N, K, epi, sms, &cs, &grid);

@@ -96,6 +96,11 @@ struct Params {
   sched::PolicyConsts pc;
   int pf_blocks;  // urgent prefetch distance in KV blocks
   int *status;
+  // optional per-CTA %globaltimer trace [grid][8] (first task of a CTA):
+  // entry, past set-up and the dependency wait, task published, its first
+  // KV block's loads issued, first S tile seen by the softmax warps, last
+  // block done, output / merge written, exit (nullptr: off)
+  unsigned long long *trace;
 };
 
 struct TaskInfo {
@@ -147,6 +152,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const SchedSlots &sl = p.slots;
 
   // ------------------------------------------------------------------ setup
+  unsigned long long *tr = p.trace != nullptr ? p.trace + (size_t)blockIdx.x * 8 : nullptr;
+  if (tr != nullptr && threadIdx.x == 0) tr[0] = ptx::globaltimer_ns();
   if (warp == 0) {
     ptx::tmem_alloc(&sh.tmem_base, TMEM_COLS);
     ptx::tmem_relinquish();
@@ -195,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t ntasks = dynamic ? min(wq_tasks, (uint32_t)p.num_tasks) : (uint32_t)p.num_tasks;
 
   if (WOVEN) sched::pdl_wait();
+  if (tr != nullptr && threadIdx.x == 0) tr[1] = ptx::globaltimer_ns();
 
   if (warp == 4) {
     // ============================================================ producer
@@ -238,6 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         sh.tasks[slot] = ti;
         ptx::mbar_arrive(&sh.task_full[slot]);
         ++j;
+        if (tr != nullptr && j == 1) tr[2] = ptx::globaltimer_ns();
         if (ti.task < 0) break;
 
         // stream the task's KV blocks
@@ -303,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               ptx::tma_load_2d(vd + HALF, mv, &sh.v_full[s], 64, row);
             }
           }
+          if (tr != nullptr && j == 1 && b == 0) tr[3] = ptx::globaltimer_ns();
           // urgent: warm L2 with the pages pf_blocks ahead (pure hint)
           if (WOVEN && ti.prio == 1 && p.pf_blocks > 0) {
             const int pf0 = pg0 + p.pf_blocks * PAGES_PER_BLK;
@@ -462,6 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
+        if (tr != nullptr && j == 1 && b == 0 && t == 0) tr[4] = ptx::globaltimer_ns();
         uint32_t sr[16];
         ptx::tmem_ld16(tmem + lane_off + sb * 16, sr);
         ptx::tmem_ld_wait();
@@ -551,6 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       blk += ti.nblk;
+      if (tr != nullptr && j == 1 && t == 0) tr[5] = ptx::globaltimer_ns();
       // output: thread t owns head-dimension row d = t
       const int hq0 = ti.kvh * G;
       if (ti.part < 0) {
@@ -626,6 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (WOVEN && t == 0) sched::timer_commit(sl, timer_off, (uint32_t)ti.task, t0);
+      if (tr != nullptr && j == 1 && t == 0) tr[6] = ptx::globaltimer_ns();
       ptx::mbar_arrive(&sh.task_empty[slot]);
     }
   }
@@ -634,6 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_before();
   __syncthreads();
   if (warp == 0) ptx::tmem_dealloc(tmem, TMEM_COLS);
+  if (tr != nullptr && threadIdx.x == 0) tr[7] = ptx::globaltimer_ns();
   if (WOVEN) {
     // ticket queue: the last worker to leave resets the counters for the next launch
     if (ACQ == (int)sched::Acquire::Ticket && dynamic && sl.queue != nullptr && threadIdx.x == 0) {
@@ -712,6 +726,11 @@ static int dispatch_acq(bool woven, int acq, const CUtensorMap &tk, const CUtens
 extern "C" int sched_attn_decode_smem_bytes() { return attn::SMEM; }
 
 // Resident CTAs per SM of the woven static kernel (the CLC prefix R = this x SMs).
+// Diagnostic: when set, every decode-attention launch records its per-CTA
+// phase trace here ([grid][8] u64, see Params::trace).
+static unsigned long long *g_attn_trace = nullptr;
+extern "C" void sched_attn_decode_set_trace(unsigned long long *trace) { g_attn_trace = trace; }
+
 extern "C" int sched_attn_decode_occupancy(int group) {
   int blocks = 0;
   const void *k = nullptr;
@@ -770,6 +789,7 @@ extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
   p.pc.H = H;
   p.pf_blocks = pf_blocks;
   p.status = status;
+  p.trace = g_attn_trace;
   if (grid <= 0) grid = p.num_tasks;
   try {
     const uint64_t rows = (uint64_t)num_pages * Hkv * attn::PS;

@@ -162,10 +162,43 @@ def case_decode(args, peaks):
                                       woven=True, acquire=2, grid=n_items * Hkv)
     ms = events_ms(fn, args.reps)
     ops.check_status()
+    phases = decode_trace(fn, n_items * Hkv) if args.trace else None
     kv = B * ctx * Hkv * D * 2 * 2
     print(json.dumps({"case": "decode", "batch": B, "context": ctx, "kv_heads": Hkv, "splits": S,
                       "tasks": n_items * Hkv, "us": round(ms * 1e3, 2), "kv_MB": round(kv / 1e6, 1),
-                      "frac_hbm_of_measured": round(kv / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)}))
+                      "frac_hbm_of_measured": round(kv / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 3),
+                      "phases_us": phases}))
+
+
+DECODE_PHASES = ["setup_and_dep_wait", "task_published", "first_loads_issued", "first_s_tile", "blocks",
+                 "output_and_merge", "exit"]
+
+
+def decode_trace(fn, grid):
+    """One launch with the decode kernel's per-CTA %globaltimer trace armed:
+    median and max over CTAs of each phase (us), the spread of CTA entries
+    and the span from the first entry to the last exit."""
+    buf = torch.zeros(grid * 8, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    ext().set_attn_trace(buf.data_ptr())
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        ext().set_attn_trace(0)
+    rows = [[int(v) for v in r] for r in buf.view(-1, 8).tolist() if r[0] != 0 and r[7] != 0]
+    if not rows:
+        return None
+    out = {}
+    for k, name in enumerate(DECODE_PHASES):
+        d = sorted(r[k + 1] - r[k] for r in rows if r[k + 1] and r[k])
+        if d:
+            out[name] = {"p50": round(d[len(d) // 2] / 1e3, 2), "max": round(d[-1] / 1e3, 2)}
+    t0 = min(r[0] for r in rows)
+    out["entry_spread"] = round((max(r[0] for r in rows) - t0) / 1e3, 2)
+    out["span"] = round((max(r[7] for r in rows) - t0) / 1e3, 2)
+    out["ctas"] = len(rows)
+    return out
 
 
 def main():
@@ -174,6 +207,7 @@ def main():
     ap.add_argument("--batch", type=int, default=6)
     ap.add_argument("--context", type=int, default=1536)
     ap.add_argument("--kv-heads", type=int, default=8)
+    ap.add_argument("--trace", action="store_true", help="decode: per-CTA phase trace of one launch")
     ap.add_argument("--world", type=int, default=2)
     ap.add_argument("--tokens", type=int, default=256)
     ap.add_argument("--reps", type=int, default=5)
