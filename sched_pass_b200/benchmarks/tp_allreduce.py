@@ -139,7 +139,11 @@ def sp_sublayer(args, shapes, world, rank, dev, peaks, fused, base):
 
             def sp_path():
                 sp.linear_rs(x, w)
-                sp.reduce_norm(res, lnw, 1e-5, T)
+                _, ready = sp.reduce_norm(res, lnw, 1e-5, T)
+                # consume the gathered rows as the next GEMM would (it waits on
+                # their ready flags): without it a rank that owns no rows
+                # (T < W) is never held back by its peers
+                sp.wait_rows(ready, T)
 
             t_f = graph_time(lambda: ar_path(fused))
             t_b = graph_time(lambda: ar_path(base))

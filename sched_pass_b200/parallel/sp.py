@@ -29,7 +29,13 @@ instead of T.
 Buffer sets: two receive-slab sets and two gather sets alternate between
 consecutive calls, as in ``parallel/fused.py``. A set's next use is
 causally after every reader of its previous use (a peer needs this rank's
-contribution to the intervening call first). Row flags are reset by their
+contribution to the intervening call first) provided every rank consumes
+each gather (the next GEMM's ``x_ready`` wait, or ``wait_rows``) before its
+next ``linear_rs``: with fewer tokens than ranks a rank owns no rows, and
+that wait is the only thing that holds it back until its peers have read
+the slab set it is about to overwrite. The model's forward always consumes
+the gather; a caller that skips it can lose a row flag (the owner's wait then
+ends in a peer timeout). Row flags are reset by their
 reader (``reduce_norm``); the ready flags of one gather set are reset by the
 next ``reduce_norm`` (which follows, in stream order, every GEMM that read
 them). Per forward pass the model makes an even number of calls of each
