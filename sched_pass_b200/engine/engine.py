@@ -88,6 +88,8 @@ class EngineConfig:
     host_kv_pages: int = 0          # tiered KV: pinned host pages the device pool spills to (0 = off)
     kv_staging_pages: int = 0       # staging slots (one layer of a host page each; 0 = host_kv_pages)
     host_kv_dtype: str = "bf16"     # host pool storage: "bf16" or "fp8" (e4m3 + per-head page scales)
+    kv_stage_mode: str = "copy"     # tiered KV staging: "copy" (cudaMemcpyAsync runs on a side stream)
+                                    # or "kernel" (zero-copy page-copy kernel; always for the fp8 tier)
     clock_sync: bool = True         # tensor parallel: advance every rank's workload clock by the slowest
                                     # rank's step time (one small collective per step); off when the
                                     # caller admits requests on a clock of its own
@@ -168,7 +170,8 @@ class Engine:
         if e.host_kv_pages:
             from .tiered_kv import TieredKV
             self.tier = TieredKV(self.kv, e.num_pages, e.kv_staging_pages or e.host_kv_pages,
-                                 e.host_kv_pages, self.device, host_dtype=e.host_kv_dtype)
+                                 e.host_kv_pages, self.device, host_dtype=e.host_kv_dtype,
+                                 stage_mode=e.kv_stage_mode)
         if weights is None:
             weights = init_weights(cfg, self.device, tp_rank, tp_size, seed=e.seed,
                                    moe_builder=getattr(model_factory, "moe_builder", None))

@@ -25,8 +25,10 @@ table (``split`` = the device pool's page count; the decode kernel reads
 ids >= split from a second, staging pool). Slots are assigned in the order
 the decode kernel claims its tasks (most urgent request first). The staging
 pool holds ONE layer: two buffers alternate between even and odd layers, so
-layer l's pages are copied over PCIe (``csrc/kernels/kv_tier.cu``, zero-copy
-loads of the mapped pinned pool, on a side stream) while layer l-1 computes,
+layer l's pages are copied over PCIe on a side stream while layer l-1
+computes -- by the copy engines (one ``cudaMemcpyAsync`` per run of
+consecutive host pages; spills take host pages in ascending order, so runs
+are long) or by the zero-copy page-copy kernel (``csrc/kernels/kv_tier.cu``),
 and the copy for layer l+2 waits until layer l's attention has read the
 buffer. Staging costs 2 x slots x one layer's page of device memory, so the
 read set of a step may exceed HBM (the 70B / 131k-context configuration).
@@ -56,11 +58,34 @@ def is_host(page: int) -> bool:
     return page >= HOST_BASE
 
 
+def coalesce_runs(pairs) -> list:
+    """(host page, staging slot) pairs -> runs (first host page, first slot,
+    length) over which both advance by one: each run is one contiguous copy
+    per layer for K and one for V."""
+    runs = []
+    for h, s in pairs:
+        if runs and runs[-1][0] + runs[-1][2] == h and runs[-1][1] + runs[-1][2] == s:
+            runs[-1][2] += 1
+        else:
+            runs.append([h, s, 1])
+    return [tuple(r) for r in runs]
+
+
 class TieredKV:
-    def __init__(self, kv, n_device: int, n_staging: int, n_host: int, device, host_dtype: str = "bf16"):
+    def __init__(self, kv, n_device: int, n_staging: int, n_host: int, device, host_dtype: str = "bf16",
+                 stage_mode: str = "copy"):
         if host_dtype not in ("bf16", "fp8"):
             raise ValueError(f"host_dtype must be 'bf16' or 'fp8', not {host_dtype!r}")
+        if stage_mode not in ("copy", "kernel"):
+            raise ValueError(f"stage_mode must be 'copy' or 'kernel', not {stage_mode!r}")
         self.host_dtype = host_dtype
+        # "copy": the copy engines move each layer's staged pages with one
+        # cudaMemcpyAsync per run of consecutive host pages (K and V), on the
+        # side stream, leaving the SMs to the overlapped layer; "kernel": the
+        # zero-copy page-copy kernel (always used for the fp8 tier, which
+        # dequantizes on the way)
+        self.stage_mode = "kernel" if host_dtype == "fp8" else stage_mode
+        self._runs: list = []
         self.kv = kv
         self.n_device = int(n_device)
         self.n_staging = max(1, int(n_staging))
@@ -199,6 +224,7 @@ class TieredKV:
         n = len(pairs)
         self.last_stage = n
         self.staged_pages += n
+        self._runs = coalesce_runs(pairs)
         buf = self._pairs_pin.numpy()
         buf[0] = n
         if n:
@@ -217,6 +243,11 @@ class TieredKV:
     # ------------------------------------------------------------ per-layer streaming
     def _fetch(self, layer: int) -> None:
         b = layer & 1
+        if self.stage_mode == "copy":
+            for h0, s0, n in self._runs:  # pinned -> device: cudaMemcpyAsync on the current (side) stream
+                self.stage_k[b, s0:s0 + n].copy_(self.host_k[layer, h0:h0 + n], non_blocking=True)
+                self.stage_v[b, s0:s0 + n].copy_(self.host_v[layer, h0:h0 + n], non_blocking=True)
+            return
         if self.host_dtype == "fp8":
             ext().kv_page_copy_fp8(self.host_k[layer:layer + 1], self.host_v[layer:layer + 1],
                                    self.stage_k[b:b + 1], self.stage_v[b:b + 1],

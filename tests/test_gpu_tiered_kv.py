@@ -53,10 +53,14 @@ def test_engine_with_spilled_kv_matches_device_only_engine():
         return [r.output for r in reqs], eng, reqs
 
     ref, _, _ = run()
-    got, eng, reqs = run(num_pages=30, host_kv_pages=64, kv_staging_pages=40)
-    assert eng.tier.spilled_pages > 0 and eng.tier.staged_pages > 0
-    assert got == ref
-    assert all(r.preemptions == 0 for r in reqs)  # spilling replaced preemption
+    # the copy engines (cudaMemcpyAsync per run of host pages) and the
+    # zero-copy kernel stage the same bytes
+    for mode in ("copy", "kernel"):
+        got, eng, reqs = run(num_pages=30, host_kv_pages=64, kv_staging_pages=40, kv_stage_mode=mode)
+        assert eng.tier.stage_mode == mode
+        assert eng.tier.spilled_pages > 0 and eng.tier.staged_pages > 0
+        assert got == ref, mode
+        assert all(r.preemptions == 0 for r in reqs)  # spilling replaced preemption
 
 
 def _fp8_reference(x):

@@ -93,3 +93,10 @@ def test_staging_overflow_is_loud():
     admit(sched, 3, 16 * 10, urgency=0.7)
     with pytest.raises(RuntimeError, match="staging"):
         tier.stage([b])
+
+
+def test_staged_pages_coalesce_into_contiguous_runs():
+    from sched_pass_b200.engine.tiered_kv import coalesce_runs
+    pairs = [(5, 0), (6, 1), (7, 2), (2, 3), (9, 4), (10, 5), (12, 6)]
+    assert coalesce_runs(pairs) == [(5, 0, 3), (2, 3, 1), (9, 4, 2), (12, 6, 1)]
+    assert coalesce_runs([]) == []
