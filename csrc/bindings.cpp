@@ -26,9 +26,10 @@ int sched_attn_merge(const float *part_o, const float *part_lse, const int32_t *
 int sched_attn_decode_occupancy(int group);
 int sched_attn_decode_smem_bytes();
 int sched_attn_prefill(const void *q, void *out, const void *k_cache, const void *v_cache,
-                       const int32_t *block_table, int bt_stride, const int32_t *kv_lens,
-                       const void *tiles, int num_tiles, int Hq, int Hkv, int page_size,
-                       float sm_scale, cudaStream_t st);
+                       int num_pages, const int32_t *block_table, int bt_stride,
+                       const int32_t *kv_lens, const void *tiles, int num_tiles, int Hq, int Hkv,
+                       int page_size, float sm_scale, int *status, cudaStream_t st);
+int sched_attn_prefill_tile_rows();
 int sched_add_rmsnorm(const void *x, void *res, const void *w, void *y, int T, int H, float eps,
                       cudaStream_t st);
 int sched_rope_kv_append(const void *qkv, const int32_t *pos, const int32_t *slot,
@@ -432,20 +433,29 @@ void attn_merge(const at::Tensor &part_o, const at::Tensor &part_lse, const at::
 void attn_prefill(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache,
                   const at::Tensor &v_cache, const at::Tensor &block_table,
                   const at::Tensor &kv_lens, const at::Tensor &tiles, int64_t num_tiles,
-                  double sm_scale) {
+                  double sm_scale, const c10::optional<at::Tensor> &status) {
   check_bf16(q, "q");
   check_bf16(out, "out");
+  check_bf16(k_cache, "k_cache");
+  check_bf16(v_cache, "v_cache");
   check_i32(block_table, "block_table");
   check_i32(kv_lens, "kv_lens");
   check_i32(tiles, "tiles");
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.is_contiguous(), "q [T, Hq, 128]");
+  TORCH_CHECK(out.sizes() == q.sizes() && out.is_contiguous(), "out like q");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == 16 && k_cache.size(3) == 128 &&
+                  k_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes() && v_cache.is_contiguous(),
+              "cache [pages, Hkv, 16, 128]");
+  TORCH_CHECK(k_cache.size(1) > 0 && q.size(1) % k_cache.size(1) == 0, "query heads per KV head");
+  TORCH_CHECK(tiles.numel() >= num_tiles * 4 && tiles.is_contiguous(), "tiles [n, 4]");
   int rc_ = 0;
   {  // the guard is gone before check_rc may throw
     c10::cuda::CUDAGuard g(q.device());
     rc_ = sched_attn_prefill(q.data_ptr(), out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                                block_table.data_ptr<int32_t>(), block_table.stride(0),
-                                kv_lens.data_ptr<int32_t>(), tiles.data_ptr(), num_tiles, q.size(1),
-                                k_cache.size(1), k_cache.size(2), (float)sm_scale, cur_stream());
+                             k_cache.size(0), block_table.data_ptr<int32_t>(), block_table.stride(0),
+                             kv_lens.data_ptr<int32_t>(), tiles.data_ptr(), num_tiles, q.size(1),
+                             k_cache.size(1), k_cache.size(2), (float)sm_scale,
+                             ptr_or_null<int>(status), cur_stream());
   }
   check_rc(rc_, "attn_prefill");
 }
@@ -809,6 +819,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_decode", &attn_decode);
   m.def("attn_merge", &attn_merge);
   m.def("attn_prefill", &attn_prefill);
+  m.def("attn_prefill_tile_rows", &sched_attn_prefill_tile_rows);
   m.def("attn_decode_occupancy", &attn_decode_occupancy);
   m.def("attn_decode_smem_bytes", &attn_decode_smem_bytes);
   m.def("add_rmsnorm", &add_rmsnorm);

@@ -1,244 +1,453 @@
-// attention_prefill.cu -- causal attention of prefill chunks over the paged KV cache.
+// attention_prefill.cu -- causal attention of prefill chunks over the paged KV
+// cache on the sm_100a tensor cores (tcgen05, accumulators in TMEM, KV pages
+// fed by TMA).
 //
-// Each CTA owns 64 query rows of one request and one query head (4 warps x
-// 16 rows) and streams that request's KV pages in 64-token tiles through a
-// double-buffered cp.async ring. QK^T and PV use the warp-level bf16 MMA
-// (m16n8k16) with the online softmax kept in registers (the FlashAttention-2
-// schedule). The query rows are the newest tokens of the request: row i has
-// absolute position q_pos0 + i and sees KV tokens [0, q_pos0 + i], which
-// covers both a whole prompt and a chunk appended to a cached prefix.
+// Problem: a query tile is up to 128 consecutive query rows of one request
+// (row i at absolute position q_pos0 + i) and one query head; row i attends
+// to the request's KV tokens [0, q_pos0 + i]. This covers a whole prompt and
+// a chunk appended to a cached prefix alike. The cache layout is
+// [pages, Hkv, 16, 128] bf16: one TMA box (16 rows x 64 columns, 128-byte
+// swizzle) fetches half of one page of one KV head.
 //
-// Prefill attention is ~3% of a 1536-token prefill's FLOPs on Llama-3-8B (the
-// projections dominate and run on tcgen05, gemm.cu); this kernel is the
-// warp-MMA version of it.
+// Tensor-core mapping (one CTA per (tile, head)):
+//   S[128 q x 128 tok] = Q[128 q x 128 d] . K_blk^T          kind::f16, both K-major
+//   O[128 q x 128 d]  += P[128 q x 128 tok] . V_blk          P K-major, V MN-major
+// S and O live in TMEM with one query row per lane, so each of the 128
+// softmax threads owns one row: its max, exponentials and sum need no
+// shuffles or shared-memory reductions. S is double-buffered in TMEM
+// (columns [0,128) and [128,256)), O takes [256,384), and P is
+// double-buffered in shared memory, so the MMA warp computes S of block b+1
+// while the softmax warps turn S of block b into P.
+//
+// Online softmax with a lazy rescale: a row keeps the running maximum m it
+// used for its exponentials until a block raises the maximum by more than
+// 2^8 (8 in log2 units). Until then P <= 2^8 (exact enough in bf16, and the
+// fp32 O and l accumulate it without overflow); O/l is the same for any m, so
+// the result is exact softmax. Only a rescale touches O in TMEM (load,
+// scale, store), after the previous block's PV product has completed. For
+// the causal diagonal and for random data this happens in the first block
+// and almost never after.
+//
+// Warp roles (192 threads): warps 0-3 Q staging, softmax and output (TMEM lane
+// quarter = warp), warp 4 TMA producer, warp 5 MMA issuer. KV blocks of 128
+// tokens flow through a two-stage ring of 64 KB (K and V with separate
+// barriers, so S can start before V has landed).
+//
+// Reference: the woven FlashInfer prefill kernel (jc-su/sched-pass
+// test/py/test_flashinfer_prefill.py:1-146) is the hot path this replaces;
+// the tile order (pi over prefill tiles, longest first) is set by the host
+// (engine.order_prefill_tiles, after ROADMAP.md:450-451).
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <stdexcept>
 
 #include "common.cuh"
+#include "sched/ptx.cuh"
+#include "tmap.h"
 
 namespace pf {
 
 constexpr int D = 128;
-constexpr int BQ = 64;
-constexpr int BKV = 64;
-constexpr int PITCH = D + 8;  // padded smem row (elements): conflict-free ldmatrix
-constexpr int kThreads = 128;
+constexpr int PS = 16;                  // tokens per page
+constexpr int BQ = 128;                 // query rows per tile (MMA M)
+constexpr int BKV = 128;                // KV tokens per block
+constexpr int PAGES_PER_BLK = BKV / PS;
+constexpr int STAGES = 2;
+constexpr int kThreads = 192;
+constexpr int kSoftmaxThreads = 128;
+constexpr int HALF = 128 * 128;         // bytes of a 64-column half of a 128-row bf16 tile
+constexpr int TILE_BYTES = 2 * HALF;    // 128 rows x 128 bf16
+constexpr int STAGE_BYTES = 2 * TILE_BYTES;  // K + V
+constexpr int TMEM_COLS = 512;          // S0 [0,128), S1 [128,256), O [256,384)
+constexpr int O_COL = 256;
+constexpr float kRescaleLog2 = 8.f;     // lazy-rescale threshold (log2 units)
 
 struct QTile {
   int32_t req;     // request index (row of block table / kv_lens)
   int32_t q_row0;  // first row of this tile in the packed q / out tensors
-  int32_t nq;      // rows in this tile (<= 64)
+  int32_t nq;      // rows in this tile (<= 128; 0 = empty tile)
   int32_t q_pos0;  // absolute position of the first row
 };
 
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool pred) {
-  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-  const int n = pred ? 16 : 0;  // zero-fill when out of range
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+struct Params {
+  const __nv_bfloat16 *q;  // [T, Hq, D]
+  __nv_bfloat16 *out;      // [T, Hq, D]
+  const int32_t *block_table;
+  int bt_stride;
+  const int32_t *kv_lens;
+  const QTile *tiles;
+  int Hq, Hkv;
+  float scale_log2;  // softmax scale * log2(e)
+  int num_pages;     // pages of the cache: ids outside [0, num_pages) are reported and read as zeros
+  int total_rows;    // rows of the cache tensor maps (pages * Hkv * 16): an out-of-range box row
+  int *status;
+};
+
+struct Shared {
+  uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
+  uint64_t s_ready[2], s_free[2], p_ready[2], pv_done[2];
+  uint64_t q_ready;
+  uint32_t tmem_base;
+};
+
+constexpr int SMEM = 1024 + TILE_BYTES /*Q*/ + STAGES * STAGE_BYTES + 2 * TILE_BYTES /*P*/ +
+                     (int)sizeof(Shared);
+static_assert(SMEM <= 232448, "shared memory per CTA");
+
+__device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t byte_in_row) {
+  // 128-byte swizzle: the 16-byte chunk index is XORed with (row % 8).
+  return row * 128u + ((((byte_in_row >> 4) ^ (row & 7u)) << 4) | (byte_in_row & 15u));
 }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
-  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(a));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
-  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(a));
-}
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const Params p) {
+  const int task = blockIdx.x;
+  const QTile tile = p.tiles[task / p.Hq];
+  const int hq = task % p.Hq;
+  const int kvh = hq / (p.Hq / p.Hkv);
+  if (tile.nq <= 0) return;  // empty (padding) tile: uniform across the CTA
 
-__global__ void __launch_bounds__(kThreads) prefill_kernel(
-    const __nv_bfloat16 *__restrict__ q, __nv_bfloat16 *__restrict__ out,
-    const __nv_bfloat16 *__restrict__ k_cache, const __nv_bfloat16 *__restrict__ v_cache,
-    const int32_t *__restrict__ block_table, int bt_stride, const int32_t *__restrict__ kv_lens,
-    const QTile *__restrict__ tiles, int Hq, int Hkv, int page_size, float scale_log2) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  __nv_bfloat16 *sQ = reinterpret_cast<__nv_bfloat16 *>(smem);
-  __nv_bfloat16 *sK = sQ + BQ * PITCH;        // [2][BKV][PITCH]
-  __nv_bfloat16 *sV = sK + 2 * BKV * PITCH;   // [2][BKV][PITCH]
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *base = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *q_sm = base;
+  uint8_t *stages = q_sm + TILE_BYTES;
+  uint8_t *p_sm = stages + STAGES * STAGE_BYTES;  // two P buffers of TILE_BYTES
+  Shared &sh = *reinterpret_cast<Shared *>(p_sm + 2 * TILE_BYTES);
 
-  const QTile tile = tiles[blockIdx.x];
-  const int hq = blockIdx.y;
-  const int kvh = hq / (Hq / Hkv);
-  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int kv_len = kv_lens[tile.req];
-  const int32_t *bt = block_table + (size_t)tile.req * bt_stride;
-  const int kv_stop = min(kv_len, tile.q_pos0 + tile.nq);  // last row sees [0, q_pos0+nq-1]
-  const int ntiles = (kv_stop + BKV - 1) / BKV;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
 
-  // Q tile -> smem (rows beyond nq zero)
-  for (int i = tid; i < BQ * (D / 8); i += kThreads) {
-    const int r = i / (D / 8), c = (i % (D / 8)) * 8;
-    const bool ok = r < tile.nq;
-    const __nv_bfloat16 *src = q + ((size_t)(tile.q_row0 + (ok ? r : 0)) * Hq + hq) * D + c;
-    cp_async16(sQ + r * PITCH + c, src, ok);
+  // ------------------------------------------------------------------ setup
+  if (warp == 0) {
+    ptx::tmem_alloc(&sh.tmem_base, TMEM_COLS);
+    ptx::tmem_relinquish();
   }
-  auto load_kv = [&](int kt, int buf) {
-    for (int i = tid; i < BKV * (D / 8); i += kThreads) {
-      const int r = i / (D / 8), c = (i % (D / 8)) * 8;
-      const int tok = kt * BKV + r;
-      const bool ok = tok < kv_stop;
-      const int page = ok ? bt[tok / page_size] : 0;
-      const size_t off = (((size_t)page * Hkv + kvh) * page_size + (ok ? tok % page_size : 0)) * D + c;
-      cp_async16(sK + (buf * BKV + r) * PITCH + c, k_cache + off, ok);
-      cp_async16(sV + (buf * BKV + r) * PITCH + c, v_cache + off, ok);
+  if (threadIdx.x == 32 * 4) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&sh.k_full[s], 1);
+      ptx::mbar_init(&sh.v_full[s], 1);
+      ptx::mbar_init(&sh.kv_empty[s], 1);
     }
-  };
-  if (ntiles > 0) load_kv(0, 0);
-  cp_async_commit();
-
-  float o[D / 8][4];
-#pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  const int g = lane / 4, tq = lane % 4;
-  const int row0 = warp * 16 + g;  // this thread's rows: row0, row0 + 8
-  const int qp0 = tile.q_pos0 + row0, qp1 = qp0 + 8;
-  uint32_t qa[D / 16][4];
-
-  for (int kt = 0; kt < ntiles; ++kt) {
-    const int buf = kt & 1;
-    if (kt + 1 < ntiles) load_kv(kt + 1, buf ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    if (kt == 0) {
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
-        ldsm_x4(qa[kk], sQ + (warp * 16 + (lane % 16)) * PITCH + kk * 16 + (lane / 16) * 8);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&sh.s_ready[i], 1);
+      ptx::mbar_init(&sh.s_free[i], kSoftmaxThreads);
+      ptx::mbar_init(&sh.p_ready[i], kSoftmaxThreads);
+      ptx::mbar_init(&sh.pv_done[i], 1);
     }
-    const __nv_bfloat16 *kb = sK + buf * BKV * PITCH;
-    const __nv_bfloat16 *vb = sV + buf * BKV * PITCH;
-    float s[BKV / 8][4];
-#pragma unroll
-    for (int n = 0; n < BKV / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-#pragma unroll
-      for (int n2 = 0; n2 < BKV / 16; ++n2) {
-        uint32_t b[4];
-        ldsm_x4(b, kb + (n2 * 16 + (lane % 8) + (lane / 16) * 8) * PITCH + kk * 16 +
-                       ((lane / 8) % 2) * 8);
-        mma16816(s[2 * n2], qa[kk], b[0], b[1]);
-        mma16816(s[2 * n2 + 1], qa[kk], b[2], b[3]);
-      }
-    }
-    // mask + online softmax (rows row0 and row0 + 8)
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int n = 0; n < BKV / 8; ++n) {
-      const int c0 = kt * BKV + n * 8 + 2 * tq;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int col = c0 + (e & 1);
-        const int qp = (e < 2) ? qp0 : qp1;
-        const bool ok = col <= qp && col < kv_stop;
-        s[n][e] = ok ? s[n][e] * scale_log2 : -INFINITY;
-        mx[e >> 1] = fmaxf(mx[e >> 1], s[n][e]);
-      }
-    }
-    float alpha[2];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-      const float mn = fmaxf(m[r], mx[r]);
-      alpha[r] = (mn == -INFINITY) ? 1.f : exp2f(m[r] - mn);
-      m[r] = mn;
-    }
-    float rs[2] = {0.f, 0.f};
-    uint32_t pa[BKV / 16][4];
-#pragma unroll
-    for (int n = 0; n < BKV / 8; ++n) {
-      float pv[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float mr = m[e >> 1];
-        pv[e] = (mr == -INFINITY) ? 0.f : exp2f(s[n][e] - mr);
-        rs[e >> 1] += pv[e];
-      }
-      const int kk = n / 2, hi = n % 2;
-      pa[kk][hi * 2 + 0] = pack_bf16x2(pv[0], pv[1]);
-      pa[kk][hi * 2 + 1] = pack_bf16x2(pv[2], pv[3]);
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
-      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
-      l[r] = l[r] * alpha[r] + rs[r];
-    }
-#pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-      o[i][0] *= alpha[0];
-      o[i][1] *= alpha[0];
-      o[i][2] *= alpha[1];
-      o[i][3] *= alpha[1];
-    }
-    // P (A operand) x V: A fragment order is (row g k-lo, row g+8 k-lo, row g k-hi, row g+8 k-hi)
-#pragma unroll
-    for (int kk = 0; kk < BKV / 16; ++kk) {
-      uint32_t a[4] = {pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3]};
-#pragma unroll
-      for (int n2 = 0; n2 < D / 16; ++n2) {
-        uint32_t b[4];
-        ldsm_x4_t(b, vb + (kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8) * PITCH + n2 * 16 +
-                         (lane / 16) * 8);
-        mma16816(o[2 * n2], a, b[0], b[1]);
-        mma16816(o[2 * n2 + 1], a, b[2], b[3]);
-      }
-    }
-    __syncthreads();
+    ptx::mbar_init(&sh.q_ready, kSoftmaxThreads);
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tmK);
+    ptx::prefetch_tmap(&tmV);
   }
-  // write normalised rows
+  ptx::pdl_launch_dependents();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  ptx::pdl_wait();  // q and the cache are written by the kernels before this one
+
+  const int kv_len = p.kv_lens[tile.req];
+  const int kv_stop = min(kv_len, tile.q_pos0 + tile.nq);  // the last row sees [0, kv_stop)
+  const int nblk = kv_stop > 0 ? (kv_stop + BKV - 1) / BKV : 0;
+
+  if (warp == 4) {
+    // ============================================================ producer
+    if (lane == 0 && nblk > 0) {
+      const int32_t *bt = p.block_table + (size_t)tile.req * p.bt_stride;
+      const int last_page = (kv_stop + PS - 1) / PS;
+      // a block's page ids are loaded together and one block ahead of its
+      // TMA issue, so their latency hides behind the wait for a free stage
+      int ids_next[PAGES_PER_BLK];
+      auto load_ids = [&](int b, int *ids) {
+        const int pg0 = b * PAGES_PER_BLK;
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int row = row0 + r * 8;
-    if (row >= tile.nq) continue;
-    const float inv = l[r] > 0.f ? 1.f / l[r] : 0.f;
-    __nv_bfloat16 *dst = out + ((size_t)(tile.q_row0 + row) * Hq + hq) * D;
+        for (int pi = 0; pi < PAGES_PER_BLK; ++pi)
+          ids[pi] = pg0 + pi < last_page ? __ldg(bt + pg0 + pi) : -1;
+      };
+      load_ids(0, ids_next);
+      for (int b = 0; b < nblk; ++b) {
+        int ids[PAGES_PER_BLK];
 #pragma unroll
-    for (int n = 0; n < D / 8; ++n)
-      *reinterpret_cast<uint32_t *>(dst + n * 8 + 2 * tq) =
-          pack_bf16x2(o[n][2 * r] * inv, o[n][2 * r + 1] * inv);
+        for (int pi = 0; pi < PAGES_PER_BLK; ++pi) ids[pi] = ids_next[pi];
+        if (b + 1 < nblk) load_ids(b + 1, ids_next);
+        const int s = b % STAGES;
+        if (!ptx::mbar_wait(&sh.kv_empty[s], ((b / STAGES) & 1) ^ 1, kWaitBudgetNs)) {
+          report_status(p.status, kStatusMmaTimeout);
+          break;
+        }
+        uint8_t *kst = stages + s * STAGE_BYTES;
+        uint8_t *vst = kst + TILE_BYTES;
+        ptx::mbar_arrive_expect_tx(&sh.k_full[s], TILE_BYTES);
+        ptx::mbar_arrive_expect_tx(&sh.v_full[s], TILE_BYTES);
+#pragma unroll
+        for (int pi = 0; pi < PAGES_PER_BLK; ++pi) {
+          int page = ids[pi];
+          if (b * PAGES_PER_BLK + pi < last_page && (page < 0 || page >= p.num_pages)) {
+            report_bad_index(p.status, kSitePrefillPage, page);  // read as a zero box
+            page = -1;
+          }
+          // pages past the last one (and bad ids): an out-of-range box reads zeros
+          const int row = page < 0 ? p.total_rows : (page * p.Hkv + kvh) * PS;
+          ptx::tma_load_2d(kst + pi * PS * 128, &tmK, &sh.k_full[s], 0, row);
+          ptx::tma_load_2d(kst + HALF + pi * PS * 128, &tmK, &sh.k_full[s], 64, row);
+        }
+#pragma unroll
+        for (int pi = 0; pi < PAGES_PER_BLK; ++pi) {
+          int page = ids[pi];
+          if (page >= p.num_pages) page = -1;
+          const int row = page < 0 ? p.total_rows : (page * p.Hkv + kvh) * PS;
+          ptx::tma_load_2d(vst + pi * PS * 128, &tmV, &sh.v_full[s], 0, row);
+          ptx::tma_load_2d(vst + HALF + pi * PS * 128, &tmV, &sh.v_full[s], 64, row);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ============================================================ MMA issuer
+    if (lane == 0 && nblk > 0) {
+      constexpr uint32_t idS = ptx::idesc_f16(BQ, BKV, 1, false, false);  // Q, K both K-major
+      constexpr uint32_t idO = ptx::idesc_f16(BQ, D, 1, false, true);     // P K-major, V MN-major
+      bool ok = ptx::mbar_wait(&sh.q_ready, 0, kWaitBudgetNs);
+      auto issue_s = [&](int b) -> bool {
+        const int s = b % STAGES, sb = b & 1;
+        if (!ptx::mbar_wait(&sh.k_full[s], (b / STAGES) & 1, kWaitBudgetNs)) return false;
+        if (!ptx::mbar_wait(&sh.s_free[sb], ((b >> 1) & 1) ^ 1, kWaitBudgetNs)) return false;
+        ptx::tc_fence_after();
+        const uint8_t *kst = stages + s * STAGE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk / 4) * HALF + (kk % 4) * 32;
+          ptx::mma_f16_ss(tmem + sb * BKV, ptx::smem_desc(q_sm + off, 16, 1024, ptx::kLayoutSW128),
+                          ptx::smem_desc(kst + off, 16, 1024, ptx::kLayoutSW128), idS, kk > 0);
+        }
+        ptx::mma_commit(&sh.s_ready[sb]);
+        return true;
+      };
+      auto issue_o = [&](int b) -> bool {
+        const int s = b % STAGES, pb = b & 1;
+        if (!ptx::mbar_wait(&sh.v_full[s], (b / STAGES) & 1, kWaitBudgetNs)) return false;
+        if (!ptx::mbar_wait(&sh.p_ready[pb], (b >> 1) & 1, kWaitBudgetNs)) return false;
+        ptx::tc_fence_after();
+        const uint8_t *vst = stages + s * STAGE_BYTES + TILE_BYTES;
+        const uint8_t *pbuf = p_sm + pb * TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          // A = P (K-major: 64 tokens per 128-byte row, other token half at +HALF);
+          // B = V, MN-major: 64 d per 128-byte row, other d half at +HALF (LBO),
+          // 8-token groups at +1024 (SBO); 16 tokens per MMA = +2048 bytes.
+          const uint8_t *a = pbuf + (kk / 4) * HALF + (kk % 4) * 32;
+          const uint8_t *bv = vst + kk * 2048;
+          ptx::mma_f16_ss(tmem + O_COL, ptx::smem_desc(a, 16, 1024, ptx::kLayoutSW128),
+                          ptx::smem_desc(bv, HALF, 1024, ptx::kLayoutSW128), idO,
+                          (b > 0 || kk > 0) ? 1u : 0u);
+        }
+        ptx::mma_commit(&sh.pv_done[pb]);
+        ptx::mma_commit(&sh.kv_empty[s]);  // S(b) and PV(b) have read stage s
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int b = 0; ok && b < nblk; ++b) {
+        if (b + 1 < nblk && !issue_s(b + 1)) { ok = false; break; }
+        if (!issue_o(b)) { ok = false; break; }
+      }
+      if (!ok) report_status(p.status, kStatusTmaTimeout);
+    }
+  } else {
+    // ============================================================ softmax + output
+    const int t = threadIdx.x;  // query row of the tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // Q row t -> swizzled K-major tile (rows >= nq are zero)
+    {
+      const uint4 *src = reinterpret_cast<const uint4 *>(
+          p.q + ((size_t)(tile.q_row0 + (t < tile.nq ? t : 0)) * p.Hq + hq) * D);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = t < tile.nq ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4 *>(q_sm + (c / 8) * HALF + swz(t, (c % 8) * 16)) = v;
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(&sh.q_ready);
+    }
+    // this row sees tokens [0, qlim]
+    const int qlim = min(tile.q_pos0 + t, kv_stop - 1);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int b = 0; b < nblk; ++b) {
+      const int sb = b & 1;
+      if (!ptx::mbar_wait(&sh.s_ready[sb], (b >> 1) & 1, kWaitBudgetNs)) {
+        report_status(p.status, kStatusMmaTimeout);
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      uint32_t s[8][16];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ptx::tmem_ld16(tmem + lane_off + sb * BKV + i * 16, s[i]);
+      ptx::tmem_ld_wait();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&sh.s_free[sb]);
+      // causal / length mask (only the blocks that reach past qlim)
+      const int tok0 = b * BKV;
+      float mx = -INFINITY;
+      if (tok0 + BKV - 1 > qlim) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const float v = tok0 + i * 16 + k <= qlim ? __uint_as_float(s[i][k]) : -INFINITY;
+            s[i][k] = __float_as_uint(v);
+            mx = fmaxf(mx, v);
+          }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int k = 0; k < 16; ++k) mx = fmaxf(mx, __uint_as_float(s[i][k]));
+      }
+      const float m_cand = fmaxf(m_run, mx * p.scale_log2);
+      // lazy rescale: warp-uniform decision (the TMEM accesses are warp-collective)
+      if (__any_sync(0xffffffffu, m_cand > m_run + kRescaleLog2)) {
+        float f = 1.f;
+        if (m_cand > m_run) {
+          f = m_run == -INFINITY ? 0.f : exp2f(m_run - m_cand);
+          m_run = m_cand;
+        }
+        l_run *= f;
+        if (b > 0) {  // O holds blocks [0, b): wait for PV(b-1), then scale it in place
+          const int pb = (b - 1) & 1;
+          const bool got = ptx::mbar_wait(&sh.pv_done[pb], ((b - 1) >> 1) & 1, kWaitBudgetNs);
+          if (!__all_sync(0xffffffffu, got)) {
+            report_status(p.status, kStatusMmaTimeout);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            uint32_t o[16];
+            ptx::tmem_ld16(tmem + lane_off + O_COL + i * 16, o);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 16; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * f);
+            ptx::tmem_st16(tmem + lane_off + O_COL + i * 16, o);
+          }
+          ptx::tmem_st_wait();
+        }
+      }
+      // P = 2^(s * scale - m), row sum; an all-masked row so far has m = -inf
+      // and only -inf scores, which give 0 with an offset of 0
+      const float neg = m_run == -INFINITY ? 0.f : -m_run;
+      uint32_t pk[8][8];
+      float rs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float a = exp2f(fmaf(__uint_as_float(s[i][2 * k]), p.scale_log2, neg));
+          const float c = exp2f(fmaf(__uint_as_float(s[i][2 * k + 1]), p.scale_log2, neg));
+          rs += a + c;
+          pk[i][k] = pack_bf16x2(a, c);
+        }
+      l_run += rs;
+      // P buffer b&1 was last read by PV(b-2)
+      if (b >= 2 && !ptx::mbar_wait(&sh.pv_done[sb], ((b - 2) >> 1) & 1, kWaitBudgetNs)) {
+        report_status(p.status, kStatusMmaTimeout);
+        ok = false;
+        break;
+      }
+      uint8_t *pbuf = p_sm + sb * TILE_BYTES;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {  // 8 tokens (16 bytes) per chunk
+        const uint4 v = make_uint4(pk[c / 2][(c % 2) * 4 + 0], pk[c / 2][(c % 2) * 4 + 1],
+                                   pk[c / 2][(c % 2) * 4 + 2], pk[c / 2][(c % 2) * 4 + 3]);
+        *reinterpret_cast<uint4 *>(pbuf + (c / 8) * HALF + swz(t, (c % 8) * 16)) = v;
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&sh.p_ready[sb]);
+    }
+    // output: O / l for this row
+    if (ok && nblk > 0) {
+      const int pb = (nblk - 1) & 1;
+      const bool got = ptx::mbar_wait(&sh.pv_done[pb], ((nblk - 1) >> 1) & 1, kWaitBudgetNs);
+      if (__all_sync(0xffffffffu, got)) {
+        ptx::tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        uint4 *dst = reinterpret_cast<uint4 *>(p.out + ((size_t)(tile.q_row0 + t) * p.Hq + hq) * D);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t o[16];
+          ptx::tmem_ld16(tmem + lane_off + O_COL + i * 16, o);
+          ptx::tmem_ld_wait();
+          if (t < tile.nq) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              dst[i * 2 + h] = make_uint4(
+                  pack_bf16x2(__uint_as_float(o[8 * h + 0]) * inv, __uint_as_float(o[8 * h + 1]) * inv),
+                  pack_bf16x2(__uint_as_float(o[8 * h + 2]) * inv, __uint_as_float(o[8 * h + 3]) * inv),
+                  pack_bf16x2(__uint_as_float(o[8 * h + 4]) * inv, __uint_as_float(o[8 * h + 5]) * inv),
+                  pack_bf16x2(__uint_as_float(o[8 * h + 6]) * inv, __uint_as_float(o[8 * h + 7]) * inv));
+          }
+        }
+      } else {
+        report_status(p.status, kStatusMmaTimeout);
+      }
+    }
   }
+
+  __syncwarp();  // reconverge single-lane roles before the CTA barrier
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) ptx::tmem_dealloc(tmem, TMEM_COLS);
 }
 
 }  // namespace pf
 
+extern "C" int sched_attn_prefill_tile_rows() { return pf::BQ; }
+
+// q, out [T, Hq, 128] bf16; k_cache/v_cache [num_pages, Hkv, 16, 128] bf16;
+// tiles [num_tiles] (req, q_row0, nq <= 128, q_pos0), launched in the given
+// order (tile-major, heads minor). Returns 0 on success.
 extern "C" int sched_attn_prefill(const void *q, void *out, const void *k_cache,
-                                  const void *v_cache, const int32_t *block_table, int bt_stride,
-                                  const int32_t *kv_lens, const void *tiles, int num_tiles, int Hq,
-                                  int Hkv, int page_size, float sm_scale, cudaStream_t st) {
+                                  const void *v_cache, int num_pages, const int32_t *block_table,
+                                  int bt_stride, const int32_t *kv_lens, const void *tiles,
+                                  int num_tiles, int Hq, int Hkv, int page_size, float sm_scale,
+                                  int *status, cudaStream_t st) {
   if (num_tiles <= 0) return 0;
-  const int smem = (pf::BQ + 4 * pf::BKV) * pf::PITCH * 2;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(pf::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
+  if (page_size != pf::PS || Hkv <= 0 || Hq % Hkv != 0 || num_pages <= 0) return -1;
+  pf::Params p;
+  p.q = static_cast<const __nv_bfloat16 *>(q);
+  p.out = static_cast<__nv_bfloat16 *>(out);
+  p.block_table = block_table;
+  p.bt_stride = bt_stride;
+  p.kv_lens = kv_lens;
+  p.tiles = static_cast<const pf::QTile *>(tiles);
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.num_pages = num_pages;
+  p.total_rows = num_pages * Hkv * pf::PS;
+  p.status = status;
+  try {
+    const uint64_t rows = (uint64_t)num_pages * Hkv * pf::PS;
+    CUtensorMap tk = tmap::make_2d(k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, pf::D,
+                                   pf::D, pf::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap tv = tmap::make_2d(v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, pf::D,
+                                   pf::D, pf::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(pf::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
+      attr = true;
+    }
+    if (launch_pdl(pf::prefill_kernel, dim3(num_tiles * Hq), dim3(pf::kThreads), pf::SMEM, st, tk,
+                   tv, p) != cudaSuccess)
+      return -4;
+  } catch (const std::exception &) {
+    return -3;
   }
-  pf::prefill_kernel<<<dim3(num_tiles, Hq), pf::kThreads, smem, st>>>(
-      static_cast<const __nv_bfloat16 *>(q), static_cast<__nv_bfloat16 *>(out),
-      static_cast<const __nv_bfloat16 *>(k_cache), static_cast<const __nv_bfloat16 *>(v_cache),
-      block_table, bt_stride, kv_lens, static_cast<const pf::QTile *>(tiles), Hq, Hkv, page_size,
-      sm_scale * 1.4426950408889634f);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

@@ -29,6 +29,7 @@ enum IndexSite : int {
   kSiteKvSlot = 3,        // KV append: cache slot of a token
   kSiteTokenId = 4,       // embedding: token id
   kSiteDecodePage = 5,    // decode attention: block-table page id
+  kSitePrefillPage = 6,   // prefill attention: block-table page id
 };
 
 // A status buffer holds 4 int32 words: [0] the code, and for

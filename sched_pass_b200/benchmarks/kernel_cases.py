@@ -105,7 +105,9 @@ def case_prefill(args, peaks):
     vc = torch.randn_like(kc)
     bt = torch.randperm(pages, device=dev).to(torch.int32).view(1, pages)
     kvl = torch.tensor([T], dtype=torch.int32, device=dev)
-    tiles = torch.tensor([[0, t0, 64, t0] for t0 in range(0, T, 64)], dtype=torch.int32, device=dev)
+    R = ops.PREFILL_TILE_ROWS
+    tiles = torch.tensor([[0, t0, min(R, T - t0), t0] for t0 in range(T - (T - 1) % R - 1, -1, -R)],
+                         dtype=torch.int32, device=dev)  # longest first
     fn = lambda: ops.attention_prefill(q, out, kc, vc, bt, kvl, tiles, tiles.shape[0], 1 / math.sqrt(D))  # noqa: E731
     ms = events_ms(fn, args.reps)
     flops = 4 * (T * (T + 1) / 2) * Hq * D  # causal QK^T and PV

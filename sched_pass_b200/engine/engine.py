@@ -42,7 +42,7 @@ from .request import Request, State
 from .scheduler import Scheduler, StepPlan
 
 DECODE_BUCKETS = (1, 2, 4, 8, 12, 16, 24, 32, 40, 48, 56, 64, 80, 96, 112, 128, 160, 192, 224, 256)
-Q_TILE = 64
+Q_TILE = 128  # query rows per prefill-attention tile (ops.PREFILL_TILE_ROWS)
 MIXED_SEGMENTS = 4  # prefill requests per step of a fixed-shape (graph) mixed step
 
 

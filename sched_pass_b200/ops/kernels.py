@@ -30,7 +30,8 @@ def status_buffer(device=None) -> torch.Tensor:
 STATUS_NAMES = {0: "ok", 1: "tma-timeout", 2: "mma-timeout", 3: "epilogue-timeout",
                 4: "peer-timeout", 5: "clc-timeout", 6: "bad-argument", 7: "bad-index"}
 INDEX_SITES = {1: "kv page copy: source page", 2: "kv page copy: destination page", 3: "KV append: cache slot",
-               4: "embedding: token id", 5: "decode attention: block-table page"}
+               4: "embedding: token id", 5: "decode attention: block-table page",
+               6: "prefill attention: block-table page"}
 
 
 class KernelStatusError(RuntimeError):
@@ -208,9 +209,16 @@ def attention_merge(part_o, part_lse, merge_req, merge_begin, rows, out):
     return out
 
 
+PREFILL_TILE_ROWS = 128  # query rows per prefill-attention tile (the tcgen05 MMA's M)
+
+
 def attention_prefill(q, out, k_cache, v_cache, block_table, kv_lens, tiles, num_tiles, sm_scale):
+    """Causal attention of prefill rows over the paged cache. ``tiles`` [n, 4]
+    int32 rows (block-table row, first q row, rows <= PREFILL_TILE_ROWS,
+    position of the first row), launched in the given order; rows = 0 marks an
+    empty (padding) tile."""
     ext().attn_prefill(q, out, k_cache, v_cache, block_table, kv_lens, tiles, int(num_tiles),
-                       float(sm_scale))
+                       float(sm_scale), status_buffer(q.device))
     return out
 
 
