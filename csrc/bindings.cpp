@@ -25,7 +25,7 @@ int sched_attn_merge(const float *part_o, const float *part_lse, const int32_t *
                      const int32_t *merge_begin, int rows, int Hq, void *out, cudaStream_t st);
 int sched_attn_decode_occupancy(int group);
 int sched_attn_decode_smem_bytes();
-int sched_attn_prefill(const void *q, void *out, const void *k_cache, const void *v_cache,
+int sched_attn_prefill(const void *q, int q_rows, void *out, const void *k_cache, const void *v_cache,
                        int num_pages, const int32_t *block_table, int bt_stride,
                        const int32_t *kv_lens, const void *tiles, int num_tiles, int Hq, int Hkv,
                        int page_size, float sm_scale, int *status, cudaStream_t st);
@@ -451,8 +451,8 @@ void attn_prefill(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cach
   int rc_ = 0;
   {  // the guard is gone before check_rc may throw
     c10::cuda::CUDAGuard g(q.device());
-    rc_ = sched_attn_prefill(q.data_ptr(), out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                             k_cache.size(0), block_table.data_ptr<int32_t>(), block_table.stride(0),
+    rc_ = sched_attn_prefill(q.data_ptr(), q.size(0), out.data_ptr(), k_cache.data_ptr(),
+                             v_cache.data_ptr(), k_cache.size(0), block_table.data_ptr<int32_t>(), block_table.stride(0),
                              kv_lens.data_ptr<int32_t>(), tiles.data_ptr(), num_tiles, q.size(1),
                              k_cache.size(1), k_cache.size(2), (float)sm_scale,
                              ptr_or_null<int>(status), cur_stream());

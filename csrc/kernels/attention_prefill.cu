@@ -10,14 +10,15 @@
 // swizzle) fetches half of one page of one KV head.
 //
 // Tensor-core mapping (one CTA per (tile, head)):
-//   S[128 q x 128 tok] = Q[128 q x 128 d] . K_blk^T          kind::f16, both K-major
-//   O[128 q x 128 d]  += P[128 q x 128 tok] . V_blk          P K-major, V MN-major
-// S and O live in TMEM with one query row per lane, so each of the 128
+//   S[128 q x 128 tok] = Q[128 q x 128 d] . K_blk^T    kind::f16, Q and K from smem (K-major)
+//   O[128 q x 128 d]  += P[128 q x 128 tok] . V_blk    P from TMEM, V from smem (MN-major)
+// S, P and O live in TMEM with one query row per lane, so each of the 128
 // softmax threads owns one row: its max, exponentials and sum need no
-// shuffles or shared-memory reductions. S is double-buffered in TMEM
-// (columns [0,128) and [128,256)), O takes [256,384), and P is
-// double-buffered in shared memory, so the MMA warp computes S of block b+1
-// while the softmax warps turn S of block b into P.
+// shuffles or shared-memory reductions, and P goes back to the tensor core
+// through TMEM (tcgen05.st, bf16 pairs) without a trip through shared memory.
+// TMEM columns: S double-buffered at [0,128) and [128,256), O at [256,384),
+// P double-buffered at [384,448) and [448,512); so the MMA warp computes S of
+// block b+1 while the softmax warps turn S of block b into P.
 //
 // Online softmax with a lazy rescale: a row keeps the running maximum m it
 // used for its exponentials until a block raises the maximum by more than
@@ -30,7 +31,7 @@
 //
 // Warp roles (192 threads): warps 0-3 Q staging, softmax and output (TMEM lane
 // quarter = warp), warp 4 TMA producer, warp 5 MMA issuer. KV blocks of 128
-// tokens flow through a two-stage ring of 64 KB (K and V with separate
+// tokens flow through a three-stage ring of 64 KB (K and V with separate
 // barriers, so S can start before V has landed).
 //
 // Reference: the woven FlashInfer prefill kernel (jc-su/sched-pass
@@ -55,14 +56,15 @@ constexpr int PS = 16;                  // tokens per page
 constexpr int BQ = 128;                 // query rows per tile (MMA M)
 constexpr int BKV = 128;                // KV tokens per block
 constexpr int PAGES_PER_BLK = BKV / PS;
-constexpr int STAGES = 2;
+constexpr int STAGES = 3;
 constexpr int kThreads = 192;
 constexpr int kSoftmaxThreads = 128;
 constexpr int HALF = 128 * 128;         // bytes of a 64-column half of a 128-row bf16 tile
 constexpr int TILE_BYTES = 2 * HALF;    // 128 rows x 128 bf16
 constexpr int STAGE_BYTES = 2 * TILE_BYTES;  // K + V
-constexpr int TMEM_COLS = 512;          // S0 [0,128), S1 [128,256), O [256,384)
+constexpr int TMEM_COLS = 512;          // S0 [0,128), S1 [128,256), O [256,384), P0/P1 [384,512)
 constexpr int O_COL = 256;
+constexpr int P_COL = 384;              // 64 columns (128 bf16) per P buffer
 constexpr float kRescaleLog2 = 8.f;     // lazy-rescale threshold (log2 units)
 
 struct QTile {
@@ -89,12 +91,11 @@ struct Params {
 struct Shared {
   uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
   uint64_t s_ready[2], s_free[2], p_ready[2], pv_done[2];
-  uint64_t q_ready;
+  uint64_t q_full;
   uint32_t tmem_base;
 };
 
-constexpr int SMEM = 1024 + TILE_BYTES /*Q*/ + STAGES * STAGE_BYTES + 2 * TILE_BYTES /*P*/ +
-                     (int)sizeof(Shared);
+constexpr int SMEM = 1024 + TILE_BYTES /*Q*/ + STAGES * STAGE_BYTES + (int)sizeof(Shared);
 static_assert(SMEM <= 232448, "shared memory per CTA");
 
 __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t byte_in_row) {
@@ -103,8 +104,8 @@ __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t byte_in_row) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                   const Params p) {
+    prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const Params p) {
   const int task = blockIdx.x;
   const QTile tile = p.tiles[task / p.Hq];
   const int hq = task % p.Hq;
@@ -116,8 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *q_sm = base;
   uint8_t *stages = q_sm + TILE_BYTES;
-  uint8_t *p_sm = stages + STAGES * STAGE_BYTES;  // two P buffers of TILE_BYTES
-  Shared &sh = *reinterpret_cast<Shared *>(p_sm + 2 * TILE_BYTES);
+  Shared &sh = *reinterpret_cast<Shared *>(stages + STAGES * STAGE_BYTES);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -139,8 +139,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(&sh.p_ready[i], kSoftmaxThreads);
       ptx::mbar_init(&sh.pv_done[i], 1);
     }
-    ptx::mbar_init(&sh.q_ready, kSoftmaxThreads);
+    ptx::mbar_init(&sh.q_full, 1);
     ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tmQ);
     ptx::prefetch_tmap(&tmK);
     ptx::prefetch_tmap(&tmV);
   }
@@ -170,6 +171,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           ids[pi] = pg0 + pi < last_page ? __ldg(bt + pg0 + pi) : -1;
       };
       load_ids(0, ids_next);
+      // Q: 128 rows of this head from q_row0 (rows past nq are other tiles'
+      // rows or out-of-range zeros; they only feed rows that are never stored)
+      ptx::mbar_arrive_expect_tx(&sh.q_full, TILE_BYTES);
+      ptx::tma_load_3d(q_sm, &tmQ, &sh.q_full, 0, hq, tile.q_row0);
+      ptx::tma_load_3d(q_sm + HALF, &tmQ, &sh.q_full, 64, hq, tile.q_row0);
       for (int b = 0; b < nblk; ++b) {
         int ids[PAGES_PER_BLK];
 #pragma unroll
@@ -210,8 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ============================================================ MMA issuer
     if (lane == 0 && nblk > 0) {
       constexpr uint32_t idS = ptx::idesc_f16(BQ, BKV, 1, false, false);  // Q, K both K-major
-      constexpr uint32_t idO = ptx::idesc_f16(BQ, D, 1, false, true);     // P K-major, V MN-major
-      bool ok = ptx::mbar_wait(&sh.q_ready, 0, kWaitBudgetNs);
+      constexpr uint32_t idO = ptx::idesc_f16(BQ, D, 1, false, true);     // P (TMEM), V MN-major
+      bool ok = ptx::mbar_wait(&sh.q_full, 0, kWaitBudgetNs);
       auto issue_s = [&](int b) -> bool {
         const int s = b % STAGES, sb = b & 1;
         if (!ptx::mbar_wait(&sh.k_full[s], (b / STAGES) & 1, kWaitBudgetNs)) return false;
@@ -233,15 +239,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ptx::mbar_wait(&sh.p_ready[pb], (b >> 1) & 1, kWaitBudgetNs)) return false;
         ptx::tc_fence_after();
         const uint8_t *vst = stages + s * STAGE_BYTES + TILE_BYTES;
-        const uint8_t *pbuf = p_sm + pb * TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
-          // A = P (K-major: 64 tokens per 128-byte row, other token half at +HALF);
+          // A = P in TMEM: 16 tokens per MMA = 8 columns of bf16 pairs;
           // B = V, MN-major: 64 d per 128-byte row, other d half at +HALF (LBO),
           // 8-token groups at +1024 (SBO); 16 tokens per MMA = +2048 bytes.
-          const uint8_t *a = pbuf + (kk / 4) * HALF + (kk % 4) * 32;
           const uint8_t *bv = vst + kk * 2048;
-          ptx::mma_f16_ss(tmem + O_COL, ptx::smem_desc(a, 16, 1024, ptx::kLayoutSW128),
+          ptx::mma_f16_ts(tmem + O_COL, tmem + P_COL + pb * (BKV / 2) + kk * 8,
                           ptx::smem_desc(bv, HALF, 1024, ptx::kLayoutSW128), idO,
                           (b > 0 || kk > 0) ? 1u : 0u);
         }
@@ -260,18 +264,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ============================================================ softmax + output
     const int t = threadIdx.x;  // query row of the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    // Q row t -> swizzled K-major tile (rows >= nq are zero)
-    {
-      const uint4 *src = reinterpret_cast<const uint4 *>(
-          p.q + ((size_t)(tile.q_row0 + (t < tile.nq ? t : 0)) * p.Hq + hq) * D);
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint4 v = t < tile.nq ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4 *>(q_sm + (c / 8) * HALF + swz(t, (c % 8) * 16)) = v;
-      }
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive(&sh.q_ready);
-    }
     // this row sees tokens [0, qlim]
     const int qlim = min(tile.q_pos0 + t, kv_stop - 1);
     float m_run = -INFINITY, l_run = 0.f;
@@ -290,30 +282,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tmem_ld_wait();
       ptx::tc_fence_before();
       ptx::mbar_arrive(&sh.s_free[sb]);
-      // causal / length mask (only the blocks that reach past qlim)
+      // causal / length mask (only the blocks that reach past qlim); the row
+      // max is 4 independent chains of three-input maxima
       const int tok0 = b * BKV;
-      float mx = -INFINITY;
       if (tok0 + BKV - 1 > qlim) {
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float v = tok0 + i * 16 + k <= qlim ? __uint_as_float(s[i][k]) : -INFINITY;
-            s[i][k] = __float_as_uint(v);
-            mx = fmaxf(mx, v);
-          }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-          for (int k = 0; k < 16; ++k) mx = fmaxf(mx, __uint_as_float(s[i][k]));
+          for (int k = 0; k < 16; ++k)
+            if (tok0 + i * 16 + k > qlim) s[i][k] = __float_as_uint(-INFINITY);
       }
+      float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int k = 0; k < 16; k += 2)
+          mxp[(i * 8 + k / 2) & 3] =
+              fmax3(mxp[(i * 8 + k / 2) & 3], __uint_as_float(s[i][k]), __uint_as_float(s[i][k + 1]));
+      const float mx = fmax3(mxp[0], mxp[1], fmaxf(mxp[2], mxp[3]));
       const float m_cand = fmaxf(m_run, mx * p.scale_log2);
       // lazy rescale: warp-uniform decision (the TMEM accesses are warp-collective)
       if (__any_sync(0xffffffffu, m_cand > m_run + kRescaleLog2)) {
         float f = 1.f;
         if (m_cand > m_run) {
-          f = m_run == -INFINITY ? 0.f : exp2f(m_run - m_cand);
+          f = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m_cand);
           m_run = m_cand;
         }
         l_run *= f;
@@ -341,32 +333,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P = 2^(s * scale - m), row sum; an all-masked row so far has m = -inf
       // and only -inf scores, which give 0 with an offset of 0
       const float neg = m_run == -INFINITY ? 0.f : -m_run;
-      uint32_t pk[8][8];
-      float rs = 0.f;
+      const uint64_t sc2 = f32x2_splat(p.scale_log2), ng2 = f32x2_splat(neg);
+      uint32_t pk[4][16];  // P row as bf16 pairs: token 2c in the low half of column c
+      float rsp[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < 8; ++i) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const float a = exp2f(fmaf(__uint_as_float(s[i][2 * k]), p.scale_log2, neg));
-          const float c = exp2f(fmaf(__uint_as_float(s[i][2 * k + 1]), p.scale_log2, neg));
-          rs += a + c;
-          pk[i][k] = pack_bf16x2(a, c);
+          float x0, x1;
+          ffma2(x0, x1, __uint_as_float(s[i][2 * k]), __uint_as_float(s[i][2 * k + 1]), sc2, ng2);
+          const float a = ex2_approx(x0), c = ex2_approx(x1);
+          fadd2(rsp[k & 3][0], rsp[k & 3][1], a, c);
+          pk[i / 2][(i % 2) * 8 + k] = pack_bf16x2(a, c);
         }
-      l_run += rs;
+      }
+      l_run += ((rsp[0][0] + rsp[0][1]) + (rsp[1][0] + rsp[1][1])) +
+               ((rsp[2][0] + rsp[2][1]) + (rsp[3][0] + rsp[3][1]));
       // P buffer b&1 was last read by PV(b-2)
-      if (b >= 2 && !ptx::mbar_wait(&sh.pv_done[sb], ((b - 2) >> 1) & 1, kWaitBudgetNs)) {
+      const bool pfree = b < 2 || ptx::mbar_wait(&sh.pv_done[sb], ((b - 2) >> 1) & 1, kWaitBudgetNs);
+      if (!__all_sync(0xffffffffu, pfree)) {
         report_status(p.status, kStatusMmaTimeout);
         ok = false;
         break;
       }
-      uint8_t *pbuf = p_sm + sb * TILE_BYTES;
+      ptx::tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {  // 8 tokens (16 bytes) per chunk
-        const uint4 v = make_uint4(pk[c / 2][(c % 2) * 4 + 0], pk[c / 2][(c % 2) * 4 + 1],
-                                   pk[c / 2][(c % 2) * 4 + 2], pk[c / 2][(c % 2) * 4 + 3]);
-        *reinterpret_cast<uint4 *>(pbuf + (c / 8) * HALF + swz(t, (c % 8) * 16)) = v;
-      }
-      ptx::fence_proxy_async_smem();
+      for (int i = 0; i < 4; ++i) ptx::tmem_st16(tmem + lane_off + P_COL + sb * (BKV / 2) + i * 16, pk[i]);
+      ptx::tmem_st_wait();
       ptx::tc_fence_before();
       ptx::mbar_arrive(&sh.p_ready[sb]);
     }
@@ -378,20 +371,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         uint4 *dst = reinterpret_cast<uint4 *>(p.out + ((size_t)(tile.q_row0 + t) * p.Hq + hq) * D);
+        uint32_t o[8][16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint32_t o[16];
-          ptx::tmem_ld16(tmem + lane_off + O_COL + i * 16, o);
-          ptx::tmem_ld_wait();
-          if (t < tile.nq) {
+        for (int i = 0; i < 8; ++i) ptx::tmem_ld16(tmem + lane_off + O_COL + i * 16, o[i]);
+        ptx::tmem_ld_wait();
+        if (t < tile.nq) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
 #pragma unroll
             for (int h = 0; h < 2; ++h)
               dst[i * 2 + h] = make_uint4(
-                  pack_bf16x2(__uint_as_float(o[8 * h + 0]) * inv, __uint_as_float(o[8 * h + 1]) * inv),
-                  pack_bf16x2(__uint_as_float(o[8 * h + 2]) * inv, __uint_as_float(o[8 * h + 3]) * inv),
-                  pack_bf16x2(__uint_as_float(o[8 * h + 4]) * inv, __uint_as_float(o[8 * h + 5]) * inv),
-                  pack_bf16x2(__uint_as_float(o[8 * h + 6]) * inv, __uint_as_float(o[8 * h + 7]) * inv));
-          }
+                  pack_bf16x2(__uint_as_float(o[i][8 * h + 0]) * inv, __uint_as_float(o[i][8 * h + 1]) * inv),
+                  pack_bf16x2(__uint_as_float(o[i][8 * h + 2]) * inv, __uint_as_float(o[i][8 * h + 3]) * inv),
+                  pack_bf16x2(__uint_as_float(o[i][8 * h + 4]) * inv, __uint_as_float(o[i][8 * h + 5]) * inv),
+                  pack_bf16x2(__uint_as_float(o[i][8 * h + 6]) * inv, __uint_as_float(o[i][8 * h + 7]) * inv));
         }
       } else {
         report_status(p.status, kStatusMmaTimeout);
@@ -409,16 +402,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 extern "C" int sched_attn_prefill_tile_rows() { return pf::BQ; }
 
-// q, out [T, Hq, 128] bf16; k_cache/v_cache [num_pages, Hkv, 16, 128] bf16;
+// q, out [q_rows, Hq, 128] bf16; k_cache/v_cache [num_pages, Hkv, 16, 128] bf16;
 // tiles [num_tiles] (req, q_row0, nq <= 128, q_pos0), launched in the given
 // order (tile-major, heads minor). Returns 0 on success.
-extern "C" int sched_attn_prefill(const void *q, void *out, const void *k_cache,
+extern "C" int sched_attn_prefill(const void *q, int q_rows, void *out, const void *k_cache,
                                   const void *v_cache, int num_pages, const int32_t *block_table,
                                   int bt_stride, const int32_t *kv_lens, const void *tiles,
                                   int num_tiles, int Hq, int Hkv, int page_size, float sm_scale,
                                   int *status, cudaStream_t st) {
   if (num_tiles <= 0) return 0;
-  if (page_size != pf::PS || Hkv <= 0 || Hq % Hkv != 0 || num_pages <= 0) return -1;
+  if (page_size != pf::PS || Hkv <= 0 || Hq % Hkv != 0 || num_pages <= 0 || q_rows <= 0) return -1;
   pf::Params p;
   p.q = static_cast<const __nv_bfloat16 *>(q);
   p.out = static_cast<__nv_bfloat16 *>(out);
@@ -434,6 +427,10 @@ extern "C" int sched_attn_prefill(const void *q, void *out, const void *k_cache,
   p.status = status;
   try {
     const uint64_t rows = (uint64_t)num_pages * Hkv * pf::PS;
+    CUtensorMap tq = tmap::make_3d(q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                   {(uint64_t)pf::D, (uint64_t)Hq, (uint64_t)q_rows},
+                                   {(uint64_t)pf::D * 2, (uint64_t)Hq * pf::D * 2}, {64u, 1u, 128u},
+                                   CU_TENSOR_MAP_SWIZZLE_128B);
     CUtensorMap tk = tmap::make_2d(k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, pf::D,
                                    pf::D, pf::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     CUtensorMap tv = tmap::make_2d(v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, pf::D,
@@ -443,8 +440,8 @@ extern "C" int sched_attn_prefill(const void *q, void *out, const void *k_cache,
       cudaFuncSetAttribute(pf::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
       attr = true;
     }
-    if (launch_pdl(pf::prefill_kernel, dim3(num_tiles * Hq), dim3(pf::kThreads), pf::SMEM, st, tk,
-                   tv, p) != cudaSuccess)
+    if (launch_pdl(pf::prefill_kernel, dim3(num_tiles * Hq), dim3(pf::kThreads), pf::SMEM, st, tq,
+                   tk, tv, p) != cudaSuccess)
       return -4;
   } catch (const std::exception &) {
     return -3;

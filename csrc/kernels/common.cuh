@@ -57,6 +57,37 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// sm_100 scalar-pipe helpers for softmax-style row work: the hardware 2^x
+// (MUFU, flush-to-zero; 2^-inf = +0), a three-input max, and packed fp32
+// pairs (one instruction for two lanes' worth of FMA / add).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// (x0, x1) = (a0 * b0 + c0, a1 * b1 + c1) for b = (b0, b1) and c = (c0, c1) packed
+__device__ __forceinline__ void ffma2(float &x0, float &x1, float a0, float a1, uint64_t b, uint64_t c) {
+  asm("{\n.reg .b64 t;\nmov.b64 t, {%2, %3};\nfma.rn.f32x2 t, t, %4, %5;\nmov.b64 {%0, %1}, t;\n}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "l"(b), "l"(c));
+}
+// (acc0, acc1) += (a0, a1)
+__device__ __forceinline__ void fadd2(float &acc0, float &acc1, float a0, float a1) {
+  asm("{\n.reg .b64 t, u;\nmov.b64 t, {%0, %1};\nmov.b64 u, {%2, %3};\nadd.rn.f32x2 t, t, u;\n"
+      "mov.b64 {%0, %1}, t;\n}"
+      : "+f"(acc0), "+f"(acc1)
+      : "f"(a0), "f"(a1));
+}
+__device__ __forceinline__ uint64_t f32x2_splat(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return ((uint64_t)u << 32) | u;
+}
+
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 // Named barrier among `nthreads` threads (ids 1..15 are free for kernels).

@@ -50,4 +50,26 @@ inline CUtensorMap make_2d(const void *base, CUtensorMapDataType dtype, int elem
   return m;
 }
 
+// 3-D tensor, dims/box innermost first; strides (bytes) of dims 1 and 2.
+// Out-of-range boxes fill zeros.
+inline CUtensorMap make_3d(const void *base, CUtensorMapDataType dtype, const uint64_t (&dims)[3],
+                           const uint64_t (&stride_bytes)[2], const uint32_t (&box)[3],
+                           CUtensorMapSwizzle swz,
+                           CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_256B) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    throw std::runtime_error("TMA base address must be 16-byte aligned");
+  if (stride_bytes[0] % 16 != 0 || stride_bytes[1] % 16 != 0)
+    throw std::runtime_error("TMA strides must be multiples of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {stride_bytes[0], stride_bytes[1]};
+  cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encoder()(&m, dtype, 3, const_cast<void *>(base), d, st, bx, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
 }  // namespace tmap
