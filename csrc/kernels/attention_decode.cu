@@ -114,8 +114,11 @@ struct Shared {
   uint64_t q_ready, task_full[2], task_empty[2], clc_bar;
   alignas(16) uint4 clc_result;
   TaskInfo tasks[2];
-  float red_max[4][NPAD];
-  float red_sum[4][NPAD];
+  // per-warp partial max / sum of a block, double-buffered by block parity:
+  // block g+2 rewrites block g's row only after every thread has passed
+  // block g+1's first barrier, i.e. finished reading block g's values
+  float red_max[2][4][NPAD];
+  float red_sum[2][4][NPAD];
   uint32_t tmem_base;
   int merge_last;
 };
@@ -201,6 +204,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool dynamic = wq_tasks != 0u;
   const uint32_t ntasks = dynamic ? min(wq_tasks, (uint32_t)p.num_tasks) : (uint32_t)p.num_tasks;
 
+  // A task's table reads (order, item, budget, policy) and its page ids
+  // touch only tables the host wrote before the step, never the previous
+  // kernel's output (q and the newest KV rows), so the producer resolves its
+  // first task and that task's first page ids before waiting for the
+  // previous kernel: three dependent loads leave the critical path.
+  auto build_task = [&](uint32_t raw) -> TaskInfo {
+    TaskInfo ti;
+    ti.task = -1;
+    if (raw < ntasks) {
+      uint32_t task = WOVEN ? sched::remap(sl, raw, ntasks) : raw;
+      const int item = task / p.Hkv;
+      const Item it = p.items[item];
+      ti.task = (int32_t)task;
+      ti.req = it.req;
+      ti.kvh = task % p.Hkv;
+      ti.kv_begin = it.kv_begin;
+      int kv_end = it.kv_end;
+      ti.prio = 0;
+      if (WOVEN) {
+        const uint32_t tau = sched::budget(sl, task);
+        if (tau != 0xFFFFFFFFu) kv_end = min(kv_end, (int)tau);
+        const sched::PolicyFlags pf = sched::policy(sl, task, p.pc);
+        ti.prio = pf.urgent ? 1 : (pf.polite ? 2 : 0);
+      }
+      ti.kv_end = max(kv_end, it.kv_begin);
+      ti.part = it.part;
+      ti.nblk = (ti.kv_end - ti.kv_begin + BLK - 1) / BLK;
+    }
+    return ti;
+  };
+  TaskInfo first_ti;
+  first_ti.task = -1;
+  int first_ids[PAGES_PER_BLK];
+  if (warp == 4 && lane == 0) {
+    first_ti = build_task(blockIdx.x);
+    if (first_ti.task >= 0 && first_ti.nblk > 0) {
+      const int32_t *bt = p.block_table + (size_t)first_ti.req * p.bt_stride;
+      const int pg0 = first_ti.kv_begin / PS;
+      const int npg = min(PAGES_PER_BLK, (first_ti.kv_end + PS - 1) / PS - pg0);
+#pragma unroll
+      for (int pi = 0; pi < PAGES_PER_BLK; ++pi) first_ids[pi] = pi < npg ? __ldg(bt + pg0 + pi) : -1;
+    }
+  }
+
   if (WOVEN) sched::pdl_wait();
   if (tr != nullptr && threadIdx.x == 0) tr[1] = ptx::globaltimer_ns();
 
@@ -215,28 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_first = ptx::policy_evict_first();
       bool stop = false;
       while (!stop) {
-        TaskInfo ti;
-        ti.task = -1;
-        if (raw < ntasks) {
-          uint32_t task = WOVEN ? sched::remap(sl, raw, ntasks) : raw;
-          const int item = task / p.Hkv;
-          const Item it = p.items[item];
-          ti.task = (int32_t)task;
-          ti.req = it.req;
-          ti.kvh = task % p.Hkv;
-          ti.kv_begin = it.kv_begin;
-          int kv_end = it.kv_end;
-          ti.prio = 0;
-          if (WOVEN) {
-            const uint32_t tau = sched::budget(sl, task);
-            if (tau != 0xFFFFFFFFu) kv_end = min(kv_end, (int)tau);
-            const sched::PolicyFlags pf = sched::policy(sl, task, p.pc);
-            ti.prio = pf.urgent ? 1 : (pf.polite ? 2 : 0);
-          }
-          ti.kv_end = max(kv_end, it.kv_begin);
-          ti.part = it.part;
-          ti.nblk = (ti.kv_end - ti.kv_begin + BLK - 1) / BLK;
-        }
+        TaskInfo ti = j == 0 ? first_ti : build_task(raw);
         // publish the task to the MMA and softmax warps
         const int slot = j & 1;
         if (!ptx::mbar_wait(&sh.task_empty[slot], ((j >> 1) & 1) ^ 1, kWaitBudgetNs)) {
@@ -264,7 +290,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int pi = 0; pi < PAGES_PER_BLK; ++pi) ids[pi] = pi < npg ? __ldg(bt + pg0 + pi) : -1;
         };
-        if (ti.nblk > 0) load_ids(0, ids_next);
+        if (ti.nblk > 0) {
+          if (j == 1) {  // the first task's ids were loaded before the dependency wait
+#pragma unroll
+            for (int pi = 0; pi < PAGES_PER_BLK; ++pi) ids_next[pi] = first_ids[pi];
+          } else {
+            load_ids(0, ids_next);
+          }
+        }
         for (int b = 0; b < ti.nblk; ++b, ++blk_counter) {
           int ids[PAGES_PER_BLK];
 #pragma unroll
@@ -494,13 +527,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0)
 #pragma unroll
-          for (int h = 0; h < G; ++h) sh.red_max[q4][h] = mx[h];
+          for (int h = 0; h < G; ++h) sh.red_max[g & 1][q4][h] = mx[h];
         named_bar(1, kSoftmaxThreads);
         float alpha[G], pr[G], ps[G];
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          const float bm = fmaxf(fmaxf(sh.red_max[0][h], sh.red_max[1][h]),
-                                 fmaxf(sh.red_max[2][h], sh.red_max[3][h]));
+          const float(&rm)[4][NPAD] = sh.red_max[g & 1];
+          const float bm = fmaxf(fmaxf(rm[0][h], rm[1][h]), fmaxf(rm[2][h], rm[3][h]));
           const float m_new = fmaxf(m_run[h], bm);
           // m_new == -inf only when every token so far was masked
           alpha[h] = (m_new == -INFINITY) ? 1.f : exp2f(m_run[h] - m_new);
@@ -513,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0)
 #pragma unroll
-          for (int h = 0; h < G; ++h) sh.red_sum[q4][h] = ps[h];
+          for (int h = 0; h < G; ++h) sh.red_sum[g & 1][q4][h] = ps[h];
         // P^T -> shared (bf16, swizzled K-major, row = head, column = token)
         uint8_t *pb = p_sm + sb * P_BYTES + (t / 64) * (NPAD * 128);
 #pragma unroll
@@ -525,7 +558,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int h = 0; h < G; ++h)
           l_run[h] = l_run[h] * alpha[h] +
-                     (sh.red_sum[0][h] + sh.red_sum[1][h] + sh.red_sum[2][h] + sh.red_sum[3][h]);
+                     (sh.red_sum[g & 1][0][h] + sh.red_sum[g & 1][1][h] + sh.red_sum[g & 1][2][h] +
+                      sh.red_sum[g & 1][3][h]);
         // fold in the previous block's PV result (one-block delay)
         if (b > 0) {
           const int gp = g - 1, ob = gp & 1;
@@ -544,7 +578,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int h = 0; h < G; ++h) alpha_prev[h] = alpha[h];
-        named_bar(2, kSoftmaxThreads);  // red_* reuse guard for the next block
       }
       if (ti.nblk > 0) {
         const int gp = blk + ti.nblk - 1, ob = gp & 1;

@@ -245,3 +245,15 @@ def test_paged_linear_pdl_after_producer():
     ref = (kv.view(-1, 64)[bt.view(nreq, nb).long()] * w[None, :, None]).sum(1).flatten()
     assert (got - ref).abs().max().item() < 1e-3 and kv.abs().sum().item() > 0
     assert (t.timer[:nreq] > 0).all()
+
+
+def test_hetero_batch_closed_loop():
+    """The reference's heterogeneous batch (8 long + 56 short requests, 16
+    ticket workers): every arm is bit-exact with the stock launch, the woven
+    timer ranks the long requests costliest, and LPT from those cycles does
+    not lose to the identity order."""
+    from sched_pass_b200.benchmarks import hetero_batch
+    rec = hetero_batch.run(iters=5, emit=lambda s: None)
+    assert all(rec["bit_exact"].values()), rec
+    assert rec["timer_ranks_longs_first"], rec
+    assert rec["lpt_us"] <= 1.1 * rec["identity_us"], rec

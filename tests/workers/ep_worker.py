@@ -1,5 +1,6 @@
 """torchrun worker: one MoE layer with experts split across ranks (fused
 NVLink dispatch / expert GEMM / combine) vs an fp32 oracle over all experts."""
+import faulthandler
 import json
 import os
 import sys
@@ -27,6 +28,9 @@ def gather(t):
     ts = [torch.empty_like(t) for _ in range(dist.get_world_size())]
     dist.all_gather(ts, t)
     return torch.cat(ts)
+
+
+faulthandler.enable()  # a native crash prints the Python stack of every thread
 
 
 def main():

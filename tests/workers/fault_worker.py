@@ -6,6 +6,7 @@
   collective -- rank 1 skips one all_reduce; rank 0's must time out
 
 Prints one "FAULTJSON {...}" line per surviving rank."""
+import faulthandler
 import json
 import os
 import sys
@@ -19,6 +20,9 @@ import torch.distributed as dist  # noqa: E402
 
 from sched_pass_b200.parallel.health import (Heartbeat, RankFailure, guarded, publish_flag,  # noqa: E402
                                              wait_flag)
+
+
+faulthandler.enable()  # a native crash prints the Python stack of every thread
 
 
 def main():

@@ -1,6 +1,7 @@
 """One gloo rank of the fused all-reduce protocol emulation
 (sched_pass_b200/parallel/protocol.py). Scenario from argv[1]; prints one
 ``PROTOJSON {...}`` line."""
+import faulthandler
 import datetime
 import json
 import os
@@ -26,6 +27,9 @@ def expected(world, call, T, K, N):
                       (inputs(r, call, T, K, N) for r in range(world))])
     fp32 = sum(a.float() @ b.float().t() for a, b in (inputs(r, call, T, K, N) for r in range(world)))
     return parts, fp32
+
+
+faulthandler.enable()  # a native crash prints the Python stack of every thread
 
 
 def main():

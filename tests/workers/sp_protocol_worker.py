@@ -1,6 +1,7 @@
 """One gloo rank of the sequence-parallel protocol emulation
 (sched_pass_b200/parallel/sp_protocol.py). Scenario from argv[1]; prints one
 ``SPJSON {...}`` line."""
+import faulthandler
 import datetime
 import json
 import os
@@ -28,6 +29,9 @@ def inputs(rank, call, T):
 def norm_weight(call):
     g = torch.Generator().manual_seed(77 + call)
     return P.to_bf16_bits(1.0 + 0.1 * torch.randn(H, generator=g))
+
+
+faulthandler.enable()  # a native crash prints the Python stack of every thread
 
 
 def main():

@@ -2,6 +2,7 @@
 owner's reduce + residual + RMSNorm + all-gather, ready-gated GEMM) against
 the fused all-reduce path on the same inputs, and TP engine generation in
 mode "sp" against mode "fused"."""
+import faulthandler
 import json
 import math
 import os
@@ -19,6 +20,9 @@ from sched_pass_b200.parallel.tp import TensorParallel, init_distributed  # noqa
 
 def bits(t):
     return t.contiguous().cpu().view(torch.int16).numpy()
+
+
+faulthandler.enable()  # a native crash prints the Python stack of every thread
 
 
 def main():

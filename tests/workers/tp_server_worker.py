@@ -1,6 +1,7 @@
 """One gloo rank of the tensor-parallel server test: rank 0 runs
 TPEngineServer and submits requests, the other ranks follow; every rank has
 a fake engine behind the real scheduler. Prints one ``SRVJSON {...}`` line."""
+import faulthandler
 import datetime
 import json
 import os
@@ -81,6 +82,9 @@ def leave_scenario(rank, eng, out):
             out["follower"] = type(e).__name__
     print("SRVJSON " + json.dumps(out), flush=True)
     os._exit(0)  # skip the group teardown: a peer is gone
+
+
+faulthandler.enable()  # a native crash prints the Python stack of every thread
 
 
 def main():

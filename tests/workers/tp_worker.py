@@ -1,5 +1,6 @@
 """torchrun worker: fused GEMM + all-reduce vs an fp32 reference, and TP
 engine generation vs single-GPU generation on the same logical weights."""
+import faulthandler
 import json
 import math
 import os
@@ -13,6 +14,9 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspa
 
 from sched_pass_b200 import ops  # noqa: E402
 from sched_pass_b200.parallel.tp import TensorParallel, init_distributed  # noqa: E402
+
+
+faulthandler.enable()  # a native crash prints the Python stack of every thread
 
 
 def main():
