@@ -4,8 +4,9 @@
 // Problem: for each request b and KV head h, the G = Hq/Hkv query heads of h
 // attend (one query token each) to the request's KV tokens, stored in
 // 16-token pages addressed through a block table. The cache layout is
-// [pages, Hkv, 16, 128] (one page of one head = 4 KB contiguous), so one TMA
-// box (16 rows x 64 columns, 128-byte swizzle) fetches half a page-head.
+// [pages, Hkv, 16, 128] (one page of one head = 4 KB contiguous), so one 4-D
+// TMA box (128-byte swizzle) fetches a whole page-head: TMA issue, not bytes,
+// bounded the 2 KB half-page boxes used before (about 75 ns per box per SM).
 //
 // Tensor-core mapping ("transposed" decode): a decode query group is only G
 // rows, far below the 128-row MMA, so the KV tokens take the M dimension:
@@ -61,6 +62,13 @@ constexpr int kThreads = 192;
 constexpr int kSoftmaxThreads = 128;
 constexpr int HALF = BLK * 128;        // bytes of one 64-column half of a K or V block
 constexpr int KV_BLOCK_BYTES = 2 * HALF;
+// A K or V block in shared memory is 8 page-head boxes of 4 KB (one TMA box
+// each, tmap::make_kv_pages): [row group][column half][8 rows][128 bytes], so
+// an 8-row swizzle atom of one half is 1 KB, the other half's atom follows
+// it, and consecutive 8-token atoms of one half are 2 KB apart.
+constexpr int PAGE_BYTES = PS * 256;
+constexpr int ATOM = 1024;
+constexpr int ATOM_PAIR = 2048;
 constexpr int STAGE_BYTES = 2 * KV_BLOCK_BYTES;  // K + V
 constexpr int Q_BYTES = 2 * NPAD * 128;          // two 64-column halves of 16 rows
 constexpr int P_BYTES = 2 * NPAD * 128;          // two 64-token halves of 16 rows
@@ -326,23 +334,20 @@ __global__ void __launch_bounds__(kThreads, 1)
               page = -1;
             }
             const bool staged = page >= p.stage_split;
-            const int row = page < 0 ? p.total_rows
-                                     : ((staged ? page - p.stage_split : page) * p.Hkv + ti.kvh) * PS;
+            // one 4 KB box per page-head (row group = row / 8, two per page)
+            const int rg = page < 0 ? p.total_rows / 8
+                                    : ((staged ? page - p.stage_split : page) * p.Hkv + ti.kvh) * (PS / 8);
             const CUtensorMap *mk = staged ? &tmK2 : &tmK;
             const CUtensorMap *mv = staged ? &tmV2 : &tmV;
-            uint8_t *kd = kst + pi * PS * 128;
-            uint8_t *vd = vst + pi * PS * 128;
+            uint8_t *kd = kst + pi * PAGE_BYTES;
+            uint8_t *vd = vst + pi * PAGE_BYTES;
             if (WOVEN && ti.prio != 0) {
               const uint64_t pol = ti.prio == 1 ? pol_last : pol_first;
-              ptx::tma_load_2d_hint(kd, mk, &sh.k_full[s], 0, row, pol);
-              ptx::tma_load_2d_hint(kd + HALF, mk, &sh.k_full[s], 64, row, pol);
-              ptx::tma_load_2d_hint(vd, mv, &sh.v_full[s], 0, row, pol);
-              ptx::tma_load_2d_hint(vd + HALF, mv, &sh.v_full[s], 64, row, pol);
+              ptx::tma_load_4d_hint(kd, mk, &sh.k_full[s], 0, 0, 0, rg, pol);
+              ptx::tma_load_4d_hint(vd, mv, &sh.v_full[s], 0, 0, 0, rg, pol);
             } else {
-              ptx::tma_load_2d(kd, mk, &sh.k_full[s], 0, row);
-              ptx::tma_load_2d(kd + HALF, mk, &sh.k_full[s], 64, row);
-              ptx::tma_load_2d(vd, mv, &sh.v_full[s], 0, row);
-              ptx::tma_load_2d(vd + HALF, mv, &sh.v_full[s], 64, row);
+              ptx::tma_load_4d(kd, mk, &sh.k_full[s], 0, 0, 0, rg);
+              ptx::tma_load_4d(vd, mv, &sh.v_full[s], 0, 0, 0, rg);
             }
           }
           if (tr != nullptr && j == 1 && b == 0) tr[3] = ptx::globaltimer_ns();
@@ -354,13 +359,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int page = __ldg(bt + pf0 + pi);
               if (!page_ok(p, page)) continue;
               const bool staged = page >= p.stage_split;
-              const int row = ((staged ? page - p.stage_split : page) * p.Hkv + ti.kvh) * PS;
+              const int rg = ((staged ? page - p.stage_split : page) * p.Hkv + ti.kvh) * (PS / 8);
               const CUtensorMap *mk = staged ? &tmK2 : &tmK;
               const CUtensorMap *mv = staged ? &tmV2 : &tmV;
-              ptx::tma_prefetch_2d(mk, 0, row);
-              ptx::tma_prefetch_2d(mk, 64, row);
-              ptx::tma_prefetch_2d(mv, 0, row);
-              ptx::tma_prefetch_2d(mv, 64, row);
+              ptx::tma_prefetch_4d(mk, 0, 0, 0, rg);
+              ptx::tma_prefetch_4d(mv, 0, 0, 0, rg);
             }
           }
         }
@@ -419,9 +422,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint8_t *kst = stages + s * STAGE_BYTES;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
-            const uint8_t *a = kst + (kk / 4) * HALF + (kk % 4) * 32;
+            // K block: 8-token atoms of one column half 2048 bytes apart (SBO), the
+            // other half at +1024
+            const uint8_t *a = kst + (kk / 4) * ATOM + (kk % 4) * 32;
             const uint8_t *b = q_sm + (kk / 4) * (NPAD * 128) + (kk % 4) * 32;
-            ptx::mma_f16_ss(tmem + sb * 16, ptx::smem_desc(a, 16, 1024, ptx::kLayoutSW128),
+            ptx::mma_f16_ss(tmem + sb * 16, ptx::smem_desc(a, 16, ATOM_PAIR, ptx::kLayoutSW128),
                             ptx::smem_desc(b, 16, 1024, ptx::kLayoutSW128), idS, kk > 0);
           }
           ptx::mma_commit(&sh.s_ready[sb]);
@@ -438,11 +443,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint8_t *pb = p_sm + ob * P_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BLK / 16; ++kk) {
-            // A = V^T, MN-major: 64 d per 128-byte row, other d-half at +HALF (LBO),
-            // 8-token groups at +1024 (SBO); 16 tokens per MMA = +2048 bytes.
-            const uint8_t *a = vst + kk * 2048;
+            // A = V^T, MN-major: 64 d per 128-byte row, other d-half at +1024 (LBO),
+            // 8-token groups at +2048 (SBO); 16 tokens per MMA = +4096 bytes.
+            const uint8_t *a = vst + kk * 2 * ATOM_PAIR;
             const uint8_t *b = pb + (kk / 4) * (NPAD * 128) + (kk % 4) * 32;
-            ptx::mma_f16_ss(tmem + 32 + ob * 16, ptx::smem_desc(a, HALF, 1024, ptx::kLayoutSW128),
+            ptx::mma_f16_ss(tmem + 32 + ob * 16, ptx::smem_desc(a, ATOM, ATOM_PAIR, ptx::kLayoutSW128),
                             ptx::smem_desc(b, 16, 1024, ptx::kLayoutSW128), idO, kk > 0);
           }
           ptx::mma_commit(&sh.o_ready[ob]);
@@ -826,17 +831,13 @@ extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
   if (grid <= 0) grid = p.num_tasks;
   try {
     const uint64_t rows = (uint64_t)num_pages * Hkv * attn::PS;
-    CUtensorMap tk = tmap::make_2d(k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, attn::D,
-                                   attn::D, attn::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-    CUtensorMap tv = tmap::make_2d(v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, attn::D,
-                                   attn::D, attn::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap tk = tmap::make_kv_pages(k_cache, rows);
+    CUtensorMap tv = tmap::make_kv_pages(v_cache, rows);
     CUtensorMap tk2 = tk, tv2 = tv;
     if (stage_k != nullptr) {
       const uint64_t srows = (uint64_t)stage_pages * Hkv * attn::PS;
-      tk2 = tmap::make_2d(stage_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, srows, attn::D, attn::D, attn::PS, 64,
-                          CU_TENSOR_MAP_SWIZZLE_128B);
-      tv2 = tmap::make_2d(stage_v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, srows, attn::D, attn::D, attn::PS, 64,
-                          CU_TENSOR_MAP_SWIZZLE_128B);
+      tk2 = tmap::make_kv_pages(stage_k, srows);
+      tv2 = tmap::make_kv_pages(stage_v, srows);
     }
     switch (G) {
       case 1: attn::dispatch_acq<1>(woven, acquire, tk, tv, tk2, tv2, p, grid, st); break;

@@ -6,8 +6,8 @@
 // (row i at absolute position q_pos0 + i) and one query head; row i attends
 // to the request's KV tokens [0, q_pos0 + i]. This covers a whole prompt and
 // a chunk appended to a cached prefix alike. The cache layout is
-// [pages, Hkv, 16, 128] bf16: one TMA box (16 rows x 64 columns, 128-byte
-// swizzle) fetches half of one page of one KV head.
+// [pages, Hkv, 16, 128] bf16: one 4-D TMA box fetches one page of one KV
+// head (4 KB, 128-byte swizzle).
 //
 // Tensor-core mapping (one CTA per (tile, head)):
 //   S[128 q x 128 tok] = Q[128 q x 128 d] . K_blk^T    kind::f16, Q and K from smem (K-major)
@@ -61,6 +61,13 @@ constexpr int kThreads = 192;
 constexpr int kSoftmaxThreads = 128;
 constexpr int HALF = 128 * 128;         // bytes of a 64-column half of a 128-row bf16 tile
 constexpr int TILE_BYTES = 2 * HALF;    // 128 rows x 128 bf16
+// A K or V block is 8 page-head boxes of 4 KB (tmap::make_kv_pages):
+// [row group][column half][8 rows][128 bytes]; 8-row atoms of one column
+// half are 2 KB apart and the other half's atom is at +1 KB. (Q keeps the
+// plain layout: each half is a 16 KB plane with atoms 1 KB apart.)
+constexpr int PAGE_BYTES = PS * 256;
+constexpr int ATOM = 1024;
+constexpr int ATOM_PAIR = 2048;
 constexpr int STAGE_BYTES = 2 * TILE_BYTES;  // K + V
 constexpr int TMEM_COLS = 512;          // S0 [0,128), S1 [128,256), O [256,384), P0/P1 [384,512)
 constexpr int O_COL = 256;
@@ -198,17 +205,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             page = -1;
           }
           // pages past the last one (and bad ids): an out-of-range box reads zeros
-          const int row = page < 0 ? p.total_rows : (page * p.Hkv + kvh) * PS;
-          ptx::tma_load_2d(kst + pi * PS * 128, &tmK, &sh.k_full[s], 0, row);
-          ptx::tma_load_2d(kst + HALF + pi * PS * 128, &tmK, &sh.k_full[s], 64, row);
+          const int rg = page < 0 ? p.total_rows / 8 : (page * p.Hkv + kvh) * (PS / 8);
+          ptx::tma_load_4d(kst + pi * PAGE_BYTES, &tmK, &sh.k_full[s], 0, 0, 0, rg);
         }
 #pragma unroll
         for (int pi = 0; pi < PAGES_PER_BLK; ++pi) {
           int page = ids[pi];
           if (page >= p.num_pages) page = -1;
-          const int row = page < 0 ? p.total_rows : (page * p.Hkv + kvh) * PS;
-          ptx::tma_load_2d(vst + pi * PS * 128, &tmV, &sh.v_full[s], 0, row);
-          ptx::tma_load_2d(vst + HALF + pi * PS * 128, &tmV, &sh.v_full[s], 64, row);
+          const int rg = page < 0 ? p.total_rows / 8 : (page * p.Hkv + kvh) * (PS / 8);
+          ptx::tma_load_4d(vst + pi * PAGE_BYTES, &tmV, &sh.v_full[s], 0, 0, 0, rg);
         }
       }
     }
@@ -226,9 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t *kst = stages + s * STAGE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk / 4) * HALF + (kk % 4) * 32;
-          ptx::mma_f16_ss(tmem + sb * BKV, ptx::smem_desc(q_sm + off, 16, 1024, ptx::kLayoutSW128),
-                          ptx::smem_desc(kst + off, 16, 1024, ptx::kLayoutSW128), idS, kk > 0);
+          const uint32_t qoff = (kk / 4) * HALF + (kk % 4) * 32;
+          const uint32_t koff = (kk / 4) * ATOM + (kk % 4) * 32;
+          ptx::mma_f16_ss(tmem + sb * BKV, ptx::smem_desc(q_sm + qoff, 16, 1024, ptx::kLayoutSW128),
+                          ptx::smem_desc(kst + koff, 16, ATOM_PAIR, ptx::kLayoutSW128), idS, kk > 0);
         }
         ptx::mma_commit(&sh.s_ready[sb]);
         return true;
@@ -242,11 +248,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
           // A = P in TMEM: 16 tokens per MMA = 8 columns of bf16 pairs;
-          // B = V, MN-major: 64 d per 128-byte row, other d half at +HALF (LBO),
-          // 8-token groups at +1024 (SBO); 16 tokens per MMA = +2048 bytes.
-          const uint8_t *bv = vst + kk * 2048;
+          // B = V, MN-major: 64 d per 128-byte row, other d half at +1 KB (LBO),
+          // 8-token groups at +2 KB (SBO); 16 tokens per MMA = +4 KB.
+          const uint8_t *bv = vst + kk * 2 * ATOM_PAIR;
           ptx::mma_f16_ts(tmem + O_COL, tmem + P_COL + pb * (BKV / 2) + kk * 8,
-                          ptx::smem_desc(bv, HALF, 1024, ptx::kLayoutSW128), idO,
+                          ptx::smem_desc(bv, ATOM, ATOM_PAIR, ptx::kLayoutSW128), idO,
                           (b > 0 || kk > 0) ? 1u : 0u);
         }
         ptx::mma_commit(&sh.pv_done[pb]);
@@ -431,10 +437,8 @@ extern "C" int sched_attn_prefill(const void *q, int q_rows, void *out, const vo
                                    {(uint64_t)pf::D, (uint64_t)Hq, (uint64_t)q_rows},
                                    {(uint64_t)pf::D * 2, (uint64_t)Hq * pf::D * 2}, {64u, 1u, 128u},
                                    CU_TENSOR_MAP_SWIZZLE_128B);
-    CUtensorMap tk = tmap::make_2d(k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, pf::D,
-                                   pf::D, pf::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-    CUtensorMap tv = tmap::make_2d(v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, pf::D,
-                                   pf::D, pf::PS, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap tk = tmap::make_kv_pages(k_cache, rows);
+    CUtensorMap tv = tmap::make_kv_pages(v_cache, rows);
     static bool attr = false;
     if (!attr) {
       cudaFuncSetAttribute(pf::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
