@@ -307,10 +307,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               fmax3(mxp[(i * 8 + k / 2) & 3], __uint_as_float(s[i][k]), __uint_as_float(s[i][k + 1]));
       const float mx = fmax3(mxp[0], mxp[1], fmaxf(mxp[2], mxp[3]));
       const float m_cand = fmaxf(m_run, mx * p.scale_log2);
-      // lazy rescale: warp-uniform decision (the TMEM accesses are warp-collective)
-      if (__any_sync(0xffffffffu, m_cand > m_run + kRescaleLog2)) {
+      // lazy rescale. A row moves its reference max only when its own max
+      // grew past the threshold, so its arithmetic never depends on the other
+      // rows of its warp (or on how a prompt was cut into tiles and chunks);
+      // the TMEM accesses are warp-collective, so the warp runs them when any
+      // of its rows rescales, and the other rows scale by 1.
+      const bool grow = m_cand > m_run + kRescaleLog2;
+      if (__any_sync(0xffffffffu, grow)) {
         float f = 1.f;
-        if (m_cand > m_run) {
+        if (grow) {
           f = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m_cand);
           m_run = m_cand;
         }

@@ -556,6 +556,13 @@ class Engine:
         else:
             info = self._fill(plan, bucket)
             key = bucket
+        if key is not None and self.tier is not None and self.tier.stage_mode == "copy" and self.tier.last_stage:
+            # copy-mode staging issues one cudaMemcpyAsync per run of host
+            # pages, planned on the host for this step: a graph would replay
+            # the runs of the step it was captured in, so such steps run eagerly
+            # (the zero-copy kernel reads its page pairs from device memory and
+            # replays correctly)
+            key = None
         slots = self.plane.slots() if self.ecfg.levers else None
         self.hooks.begin(self, plan, info)
         stream = torch.cuda.current_stream(self.device)

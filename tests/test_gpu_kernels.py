@@ -383,6 +383,30 @@ def test_prefill_attention(qlens, prefix, Hkv, G):
         row += ql
 
 
+def test_prefill_attention_rows_do_not_depend_on_the_tiling():
+    """A prompt prefilled whole and the same prompt prefilled in two chunks
+    (different 128-row tiles) give every row the same bits: a row's online
+    softmax depends only on its own scores, so serving runs that chunk a
+    prompt differently produce identical KV caches and tokens."""
+    Hkv, G, D = 2, 4, 128
+    L, cut = 300, 100
+    kc, vc, bt = make_paged(1, Hkv, [L], seed=8)
+    q = torch.randn(L, Hkv * G, D, device=DEV).to(torch.bfloat16)
+
+    def run(chunks):
+        out = torch.zeros_like(q)
+        for q0, q1 in chunks:  # each chunk sees the cache up to its own end
+            tiles = [(0, t0, min(128, q1 - t0), t0) for t0 in range(q0, q1, 128)]
+            tt = torch.tensor(tiles, dtype=torch.int32, device=DEV)
+            ops.attention_prefill(q, out, kc, vc, bt, torch.tensor([q1], dtype=torch.int32, device=DEV), tt,
+                                  len(tiles), 1 / math.sqrt(D))
+        torch.cuda.synchronize()
+        return out
+    whole = run([(0, L)])
+    assert torch.equal(run([(0, cut), (cut, L)]), whole)
+    assert torch.equal(run([(0, 7), (7, 200), (200, L)]), whole)
+
+
 def test_prefill_attention_lazy_rescale():
     """Scores that grow by far more than 2^8 along the keys force the O
     rescale in TMEM on later blocks; the result is still exact softmax."""
