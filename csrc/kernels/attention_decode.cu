@@ -72,7 +72,8 @@ constexpr int ATOM_PAIR = 2048;
 constexpr int STAGE_BYTES = 2 * KV_BLOCK_BYTES;  // K + V
 constexpr int Q_BYTES = 2 * NPAD * 128;          // two 64-column halves of 16 rows
 constexpr int P_BYTES = 2 * NPAD * 128;          // two 64-token halves of 16 rows
-constexpr int TMEM_COLS = 64;  // S: cols [0,16) and [16,32); O: [32,48) and [48,64)
+constexpr int TMEM_COLS = 64;  // S: cols [0,16) and [16,32) by block parity; O: [32,48) and [48,64) by task parity
+constexpr float kRescaleLog2 = 8.f;  // a block moves a head's softmax reference only past 2^8
 constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + Q_BYTES + 2 * P_BYTES + 1024;
 
 struct Item {
@@ -118,15 +119,19 @@ struct TaskInfo {
 
 struct Shared {
   uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
-  uint64_t s_ready[2], s_free[2], p_ready[2], o_ready[2], o_free[2];
+  // pv_done[g & 1]: PV of global block g retired; o_free[task & 1]: the
+  // softmax warps have read that task's O (its TMEM buffer may be reused)
+  uint64_t s_ready[2], s_free[2], p_ready[2], pv_done[2], o_free[2];
   uint64_t q_ready, task_full[2], task_empty[2], clc_bar;
   alignas(16) uint4 clc_result;
   TaskInfo tasks[2];
-  // per-warp partial max / sum of a block, double-buffered by block parity:
-  // block g+2 rewrites block g's row only after every thread has passed
-  // block g+1's first barrier, i.e. finished reading block g's values
+  // per-warp partial max of a slow-path block and the flag that marks one
+  // (grow_blk[g & 1] == g), double-buffered by block parity: block g+2
+  // rewrites them only after every thread has passed block g+1's barrier,
+  // i.e. finished reading block g's; per-warp partial l of a task, by task parity
   float red_max[2][4][NPAD];
-  float red_sum[2][4][NPAD];
+  int grow_blk[2];
+  float red_l[2][4][NPAD];
   uint32_t tmem_base;
   int merge_last;
 };
@@ -179,7 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(&sh.s_ready[i], 1);
       ptx::mbar_init(&sh.s_free[i], kSoftmaxThreads);
       ptx::mbar_init(&sh.p_ready[i], kSoftmaxThreads);
-      ptx::mbar_init(&sh.o_ready[i], 1);
+      ptx::mbar_init(&sh.pv_done[i], 1);
+      sh.grow_blk[i] = -1;
       ptx::mbar_init(&sh.o_free[i], kSoftmaxThreads);
       ptx::mbar_init(&sh.task_full[i], 1);
       ptx::mbar_init(&sh.task_empty[i], 1 + kSoftmaxThreads);
@@ -274,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // publish the task to the MMA and softmax warps
         const int slot = j & 1;
         if (!ptx::mbar_wait(&sh.task_empty[slot], ((j >> 1) & 1) ^ 1, kWaitBudgetNs)) {
-          report_status(p.status, kStatusEpilogueTimeout);
+          report_timeout(p.status, kStatusEpilogueTimeout, kWaitProducerTaskEmpty);
           ti.task = -1;
         }
         sh.tasks[slot] = ti;
@@ -398,20 +404,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idO = ptx::idesc_f16(D, NPAD, 1, true, false);     // MN-major A (V^T)
       int blk = 0;  // global block counter
       int j = 0;
+      int o_use[2] = {0, 0};  // tasks with KV blocks that used each O buffer
+      int q_use = 0;          // tasks with KV blocks (q_ready phases)
       bool ok = true;
       while (ok) {
         const int slot = j & 1;
         if (!ptx::mbar_wait(&sh.task_full[slot], (j >> 1) & 1, kWaitBudgetNs)) {
-          report_status(p.status, kStatusEpilogueTimeout);
+          report_timeout(p.status, kStatusEpilogueTimeout, kWaitMmaTaskFull);
           break;
         }
         const TaskInfo ti = sh.tasks[slot];
         ++j;
         if (ti.task < 0) break;
-        // Q of this task is written by the softmax warps
-        if (!ptx::mbar_wait(&sh.q_ready, (j - 1) & 1, kWaitBudgetNs)) {
-          report_status(p.status, kStatusEpilogueTimeout);
-          break;
+        // Q of this task is written by the softmax warps (only for tasks with
+        // KV blocks, counted here the same way, so the barrier cannot run a
+        // phase ahead of this wait)
+        if (ti.nblk > 0) {
+          if (!ptx::mbar_wait(&sh.q_ready, q_use & 1, kWaitBudgetNs)) {
+            report_timeout(p.status, kStatusEpilogueTimeout, kWaitMmaQReady);
+            break;
+          }
+          ++q_use;
         }
         auto issue_s = [&](int g) -> bool {  // g: global block index
           const int s = g % STAGES;
@@ -432,12 +445,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::mma_commit(&sh.s_ready[sb]);
           return true;
         };
-        auto issue_o = [&](int g) -> bool {
+        // this task's O buffer (by task parity). Only tasks with KV blocks
+        // use it: the softmax warps release it after reading O, which they
+        // cannot do before this wait since they need this task's PV products.
+        // (A task without blocks is finished by the softmax warps without
+        // the MMA warp, so counting it would let the barrier run a phase ahead.)
+        const int ot = (j - 1) & 1;
+        if (ti.nblk > 0) {
+          if (!ptx::mbar_wait(&sh.o_free[ot], (o_use[ot] & 1) ^ 1, kWaitBudgetNs)) {
+            report_timeout(p.status, kStatusEpilogueTimeout, kWaitMmaOFree);
+            break;
+          }
+          ++o_use[ot];
+        }
+        auto issue_o = [&](int g, bool first) -> bool {
           const int s = g % STAGES;
           const int ob = g & 1;
           if (!ptx::mbar_wait(&sh.v_full[s], (g / STAGES) & 1, kWaitBudgetNs)) return false;
           if (!ptx::mbar_wait(&sh.p_ready[ob], (g >> 1) & 1, kWaitBudgetNs)) return false;
-          if (!ptx::mbar_wait(&sh.o_free[ob], ((g >> 1) & 1) ^ 1, kWaitBudgetNs)) return false;
           ptx::tc_fence_after();
           const uint8_t *vst = stages + s * STAGE_BYTES + KV_BLOCK_BYTES;
           const uint8_t *pb = p_sm + ob * P_BYTES;
@@ -447,10 +472,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // 8-token groups at +2048 (SBO); 16 tokens per MMA = +4096 bytes.
             const uint8_t *a = vst + kk * 2 * ATOM_PAIR;
             const uint8_t *b = pb + (kk / 4) * (NPAD * 128) + (kk % 4) * 32;
-            ptx::mma_f16_ss(tmem + 32 + ob * 16, ptx::smem_desc(a, ATOM, ATOM_PAIR, ptx::kLayoutSW128),
-                            ptx::smem_desc(b, 16, 1024, ptx::kLayoutSW128), idO, kk > 0);
+            ptx::mma_f16_ss(tmem + 32 + ot * 16, ptx::smem_desc(a, ATOM, ATOM_PAIR, ptx::kLayoutSW128),
+                            ptx::smem_desc(b, 16, 1024, ptx::kLayoutSW128), idO, (!first || kk > 0) ? 1u : 0u);
           }
-          ptx::mma_commit(&sh.o_ready[ob]);
+          ptx::mma_commit(&sh.pv_done[ob]);
           ptx::mma_commit(&sh.kv_empty[s]);
           return true;
         };
@@ -458,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ti.nblk > 0 && !issue_s(g0)) ok = false;
         for (int b = 0; ok && b < ti.nblk; ++b) {
           if (b + 1 < ti.nblk && !issue_s(g0 + b + 1)) { ok = false; break; }
-          if (!issue_o(g0 + b)) { ok = false; break; }
+          if (!issue_o(g0 + b, b == 0)) { ok = false; break; }
         }
         if (!ok) report_status(p.status, kStatusTmaTimeout);
         blk += ti.nblk;
@@ -475,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     while (true) {
       const int slot = j & 1;
       if (!ptx::mbar_wait(&sh.task_full[slot], (j >> 1) & 1, kWaitBudgetNs)) {
-        report_status(p.status, kStatusEpilogueTimeout);
+        report_timeout(p.status, kStatusEpilogueTimeout, kWaitSoftmaxTaskFull);
         break;
       }
       const TaskInfo ti = sh.tasks[slot];
@@ -484,29 +509,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       const unsigned long long t0 = sched::clock_now();
       const bool timer_off = WOVEN ? sched::timer_off_at_entry(sl) : true;
 
-      // Q rows of this task -> swizzled K-major tile (rows >= G stay zero).
-      if (t < G * 16) {
-        const int h = t / 16, c = t % 16;
-        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(
-            p.q + ((size_t)ti.req * p.Hq + ti.kvh * G + h) * D) + c);
-        *reinterpret_cast<uint4 *>(q_sm + (c / 8) * (NPAD * 128) + swz(h, (c % 8) * 16)) = v;
+      // Q rows of this task -> swizzled K-major tile (rows >= G stay zero);
+      // a task without KV blocks issues no MMA and needs none
+      if (ti.nblk > 0) {
+        if (t < G * 16) {
+          const int h = t / 16, c = t % 16;
+          const uint4 v = __ldg(reinterpret_cast<const uint4 *>(
+              p.q + ((size_t)ti.req * p.Hq + ti.kvh * G + h) * D) + c);
+          *reinterpret_cast<uint4 *>(q_sm + (c / 8) * (NPAD * 128) + swz(h, (c % 8) * 16)) = v;
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(&sh.q_ready);
       }
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive(&sh.q_ready);
 
-      float m_run[G], l_run[G], o_acc[G], alpha_prev[G];
+      // Online softmax with a fixed reference per head: every block whose
+      // scores stay within 2^8 of the reference m uses P = 2^(s - m), so the
+      // P of all blocks of a task share one m, O accumulates in TMEM across
+      // the task's blocks (no per-block fold), and each thread keeps the sum
+      // of its own token's P (one reduction per task). A block that raises a
+      // head's max by more than 2^8 (the first block always does) takes the
+      // CTA-uniform slow path: exact block max, new reference, O and the
+      // partial sums scaled. Normal blocks cost one barrier and no shuffles.
+      const int ot = (j - 1) & 1;  // this task's O buffer: TMEM columns 32 + 16 ot
+      const uint32_t o_col = 32 + ot * 16;
+      float m_ref[G], l_t[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        m_run[h] = -INFINITY;
-        l_run[h] = 0.f;
-        o_acc[h] = 0.f;
-        alpha_prev[h] = 1.f;
+        m_ref[h] = -INFINITY;
+        l_t[h] = 0.f;
       }
+      bool ok = true;
       for (int b = 0; b < ti.nblk; ++b) {
         const int g = blk + b;
         const int sb = g & 1;
         if (!ptx::mbar_wait(&sh.s_ready[sb], (g >> 1) & 1, kWaitBudgetNs)) {
           report_status(p.status, kStatusMmaTimeout);
+          ok = false;
           break;
         }
         ptx::tc_fence_after();
@@ -519,85 +557,99 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tok = ti.kv_begin + b * BLK + t;
         const bool valid = tok < ti.kv_end;
         float s[G];
-#pragma unroll
-        for (int h = 0; h < G; ++h) s[h] = valid ? __uint_as_float(sr[h]) * p.scale_log2 : -INFINITY;
-        // block max per head: warp, then across the 4 warps
-        float mx[G];
+        bool grow = false;
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          float v = s[h];
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-          mx[h] = v;
+          s[h] = valid ? __uint_as_float(sr[h]) * p.scale_log2 : -INFINITY;
+          grow |= s[h] > m_ref[h] + kRescaleLog2;
         }
-        if (lane == 0)
-#pragma unroll
-          for (int h = 0; h < G; ++h) sh.red_max[g & 1][q4][h] = mx[h];
+        if (__any_sync(0xffffffffu, grow) && lane == 0) sh.grow_blk[sb] = g;
         named_bar(1, kSoftmaxThreads);
-        float alpha[G], pr[G], ps[G];
+        if (sh.grow_blk[sb] == g) {  // CTA-uniform slow path
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float(&rm)[4][NPAD] = sh.red_max[g & 1];
-          const float bm = fmaxf(fmaxf(rm[0][h], rm[1][h]), fmaxf(rm[2][h], rm[3][h]));
-          const float m_new = fmaxf(m_run[h], bm);
-          // m_new == -inf only when every token so far was masked
-          alpha[h] = (m_new == -INFINITY) ? 1.f : exp2f(m_run[h] - m_new);
-          pr[h] = (m_new == -INFINITY) ? 0.f : exp2f(s[h] - m_new);
-          m_run[h] = m_new;
-          float v = pr[h];
+          for (int h = 0; h < G; ++h) {
+            float v = s[h];
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          ps[h] = v;
+            for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (lane == 0) sh.red_max[sb][q4][h] = v;
+          }
+          named_bar(1, kSoftmaxThreads);
+          float alpha[G];
+          bool scaled = false;  // the same in every thread: computed from shared values
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            const float(&rm)[4][NPAD] = sh.red_max[sb];
+            const float bm = fmaxf(fmaxf(rm[0][h], rm[1][h]), fmaxf(rm[2][h], rm[3][h]));
+            alpha[h] = 1.f;
+            if (bm > m_ref[h] + kRescaleLog2) {
+              alpha[h] = m_ref[h] == -INFINITY ? 0.f : ex2_approx(m_ref[h] - bm);
+              m_ref[h] = bm;
+              scaled = true;
+            }
+            l_t[h] *= alpha[h];
+          }
+          if (scaled && b > 0) {
+            // O holds blocks [0, b) of this task: scale each head's column
+            // once PV(g-1) has completed
+            const int gp = g - 1;
+            if (!ptx::mbar_wait(&sh.pv_done[gp & 1], (gp >> 1) & 1, kWaitBudgetNs)) {
+              report_status(p.status, kStatusMmaTimeout);
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
+            uint32_t o[16];
+            ptx::tmem_ld16(tmem + lane_off + o_col, o);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int h = 0; h < G; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
+            ptx::tmem_st16(tmem + lane_off + o_col, o);
+            ptx::tmem_st_wait();
+          }
         }
-        if (lane == 0)
-#pragma unroll
-          for (int h = 0; h < G; ++h) sh.red_sum[g & 1][q4][h] = ps[h];
         // P^T -> shared (bf16, swizzled K-major, row = head, column = token)
         uint8_t *pb = p_sm + sb * P_BYTES + (t / 64) * (NPAD * 128);
 #pragma unroll
-        for (int h = 0; h < G; ++h)
-          *reinterpret_cast<__nv_bfloat16 *>(pb + swz(h, (t % 64) * 2)) = __float2bfloat16(pr[h]);
-        ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(&sh.p_ready[sb]);
-        named_bar(1, kSoftmaxThreads);
-#pragma unroll
-        for (int h = 0; h < G; ++h)
-          l_run[h] = l_run[h] * alpha[h] +
-                     (sh.red_sum[g & 1][0][h] + sh.red_sum[g & 1][1][h] + sh.red_sum[g & 1][2][h] +
-                      sh.red_sum[g & 1][3][h]);
-        // fold in the previous block's PV result (one-block delay)
-        if (b > 0) {
-          const int gp = g - 1, ob = gp & 1;
-          if (!ptx::mbar_wait(&sh.o_ready[ob], (gp >> 1) & 1, kWaitBudgetNs)) {
-            report_status(p.status, kStatusMmaTimeout);
-            break;
-          }
-          ptx::tc_fence_after();
-          uint32_t orr[16];
-          ptx::tmem_ld16(tmem + lane_off + 32 + ob * 16, orr);
-          ptx::tmem_ld_wait();
-          ptx::tc_fence_before();
-          ptx::mbar_arrive(&sh.o_free[ob]);
-#pragma unroll
-          for (int h = 0; h < G; ++h) o_acc[h] = o_acc[h] * alpha_prev[h] + __uint_as_float(orr[h]);
+        for (int h = 0; h < G; ++h) {
+          const float pr = s[h] == -INFINITY ? 0.f : ex2_approx(s[h] - m_ref[h]);
+          l_t[h] += pr;
+          *reinterpret_cast<__nv_bfloat16 *>(pb + swz(h, (t % 64) * 2)) = __float2bfloat16(pr);
         }
-#pragma unroll
-        for (int h = 0; h < G; ++h) alpha_prev[h] = alpha[h];
+        ptx::fence_proxy_async_smem();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&sh.p_ready[sb]);
       }
-      if (ti.nblk > 0) {
-        const int gp = blk + ti.nblk - 1, ob = gp & 1;
-        if (ptx::mbar_wait(&sh.o_ready[ob], (gp >> 1) & 1, kWaitBudgetNs)) {
+      // l per head: the 128 threads' partial sums (warp, then the 4 warps)
+      float m_run[G], l_run[G], o_acc[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float v = l_t[h];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) sh.red_l[ot][q4][h] = v;
+        m_run[h] = m_ref[h];
+        o_acc[h] = 0.f;
+      }
+      named_bar(1, kSoftmaxThreads);
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        l_run[h] = (sh.red_l[ot][0][h] + sh.red_l[ot][1][h]) + (sh.red_l[ot][2][h] + sh.red_l[ot][3][h]);
+      if (ok && ti.nblk > 0) {
+        const int gl = blk + ti.nblk - 1;
+        if (ptx::mbar_wait(&sh.pv_done[gl & 1], (gl >> 1) & 1, kWaitBudgetNs)) {
           ptx::tc_fence_after();
           uint32_t orr[16];
-          ptx::tmem_ld16(tmem + lane_off + 32 + ob * 16, orr);
+          ptx::tmem_ld16(tmem + lane_off + o_col, orr);
           ptx::tmem_ld_wait();
-          ptx::tc_fence_before();
-          ptx::mbar_arrive(&sh.o_free[ob]);
 #pragma unroll
-          for (int h = 0; h < G; ++h) o_acc[h] = o_acc[h] * alpha_prev[h] + __uint_as_float(orr[h]);
+          for (int h = 0; h < G; ++h) o_acc[h] = __uint_as_float(orr[h]);
         } else {
           report_status(p.status, kStatusMmaTimeout);
         }
+      }
+      if (ti.nblk > 0) {  // the MMA warp counts only tasks with blocks
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&sh.o_free[ot]);
       }
       blk += ti.nblk;
       if (tr != nullptr && j == 1 && t == 0) tr[5] = ptx::globaltimer_ns();

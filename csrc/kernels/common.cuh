@@ -39,6 +39,20 @@ __device__ __forceinline__ void report_status(int *status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
 
+// A timeout with the wait that gave up (word [1]; sites kWait* below).
+__device__ __forceinline__ void report_timeout(int *status, int code, int wait_site) {
+  if (status == nullptr) return;
+  if (atomicCAS(status, 0, code) == 0) status[1] = wait_site;
+}
+// Decode attention's task-handoff waits (word [1] of a timeout status).
+enum WaitSite : int {
+  kWaitProducerTaskEmpty = 101,
+  kWaitMmaTaskFull = 102,
+  kWaitMmaQReady = 103,
+  kWaitMmaOFree = 104,
+  kWaitSoftmaxTaskFull = 105,
+};
+
 __device__ __forceinline__ void report_bad_index(int *status, int site, long long index) {
   if (status == nullptr) return;
   if (atomicCAS(status, 0, kStatusBadIndex) == 0) {

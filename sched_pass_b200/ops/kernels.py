@@ -32,6 +32,10 @@ STATUS_NAMES = {0: "ok", 1: "tma-timeout", 2: "mma-timeout", 3: "epilogue-timeou
 INDEX_SITES = {1: "kv page copy: source page", 2: "kv page copy: destination page", 3: "KV append: cache slot",
                4: "embedding: token id", 5: "decode attention: block-table page",
                6: "prefill attention: block-table page"}
+# the wait that gave up, for timeouts that record it
+WAIT_SITES = {101: "decode producer: task slot free", 102: "decode MMA: task published",
+              103: "decode MMA: query rows staged", 104: "decode MMA: task's O buffer free",
+              105: "decode softmax: task published"}
 
 
 class KernelStatusError(RuntimeError):
@@ -40,6 +44,8 @@ class KernelStatusError(RuntimeError):
         msg = f"kernel reported status {code} ({STATUS_NAMES.get(code, '?')})"
         if code == 7:
             msg += f": {INDEX_SITES.get(site, site)} {index} out of range (access skipped)"
+        elif site in WAIT_SITES:
+            msg += f" at {WAIT_SITES[site]}"
         super().__init__(msg)
 
 
