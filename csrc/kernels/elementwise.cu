@@ -240,7 +240,11 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16 *__res
   const __nv_bfloat16 *row = logits + (size_t)t * ld;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  const int nvec = V / 8;
+  // 16-byte vector loads only where the row starts on a 16-byte boundary
+  // (a row pitch that is not a multiple of 8 elements, e.g. a vocabulary
+  // shard of odd width, takes the scalar loop for the whole row)
+  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+  const int nvec = vec ? V / 8 : 0;
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
     uint4 u = *reinterpret_cast<const uint4 *>(row + i * 8);
     const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(&u);
@@ -444,6 +448,9 @@ extern "C" int sched_rope_kv_append(const void *qkv, const int32_t *pos, const i
 extern "C" int sched_embedding(const int32_t *ids, const int32_t *prev, int n_prev, const void *table, void *out,
                                int T, int H, int vocab, int *status, cudaStream_t st) {
   if (T <= 0) return 0;
+  // 16-byte row copies: rows of a multiple of 8 bf16 on 16-byte-aligned bases
+  if (H % 8 != 0 || (reinterpret_cast<uintptr_t>(table) & 15u) != 0 || (reinterpret_cast<uintptr_t>(out) & 15u) != 0)
+    return -1;
   launch_pdl(ew::embedding_kernel, T, 256, 0, st, ids, prev, prev != nullptr ? n_prev : 0,
              static_cast<const __nv_bfloat16 *>(table), static_cast<__nv_bfloat16 *>(out), H, vocab, status);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;

@@ -158,6 +158,26 @@ def test_embedding_and_argmax():
     assert got[2].item() == 77777
 
 
+def test_argmax_rows_of_any_pitch():
+    """Rows whose pitch is not a multiple of 8 elements (an odd vocabulary
+    shard, a column slice) are read without 16-byte vector loads; the plain
+    argmax and the in-kernel (max, id) exchange (one rank) agree with torch."""
+    from sched_pass_b200._ext import ext
+    for V, cols in ((1007, 1007), (1004, 1003), (2048, 2045)):
+        full = torch.randn(6, V, device=DEV).to(torch.bfloat16)
+        logits = full[:, :cols]
+        want = logits.float().argmax(-1)
+        assert torch.equal(ops.argmax(logits).long(), want)
+        set_lines = 1024
+        buf = torch.zeros(2 * set_lines * 4, dtype=torch.int32, device=DEV)
+        state = torch.zeros(2, dtype=torch.int32, device=DEV)
+        out = torch.empty(6, dtype=torch.int32, device=DEV)
+        for _ in range(3):  # epochs advance across calls
+            ext().argmax_exchange(logits, out, 0, [buf.data_ptr()], 0, state, set_lines, ops.status_buffer(DEV))
+            torch.cuda.synchronize()
+            assert torch.equal(out.long(), want)
+
+
 # ------------------------------------------------------------------ decode attention
 
 def test_embedding_takes_negative_ids_from_the_previous_step():
