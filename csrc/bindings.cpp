@@ -90,7 +90,28 @@ void check_i32(const at::Tensor &t, const char *name) {
   TORCH_CHECK(t.scalar_type() == at::kInt, name, " must be int32");
   TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
 }
-void check_rc(int rc, const char *op) { TORCH_CHECK(rc == 0, op, " launch failed (code ", rc, ")"); }
+// A launcher's non-zero return code is recorded here instead of thrown:
+// throwing a c10::Error out of a binding after its CUDA device guard has
+// run crashed the process (SIGSEGV) on the B200 boxes, while throws before
+// the guard (argument checks) are translated normally. The Python wrapper
+// of every launcher (_ext._Counted) calls take_error() after the call and
+// raises there.
+namespace {
+thread_local int g_last_rc = 0;
+thread_local const char *g_last_op = "";
+}  // namespace
+void check_rc(int rc, const char *op) {
+  if (rc != 0 && g_last_rc == 0) {
+    g_last_rc = rc;
+    g_last_op = op;
+  }
+}
+std::tuple<int64_t, std::string> take_error() {
+  std::tuple<int64_t, std::string> r{g_last_rc, std::string(g_last_op)};
+  g_last_rc = 0;
+  g_last_op = "";
+  return r;
+}
 
 template <typename T>
 T *ptr_or_null(const c10::optional<at::Tensor> &t) {
@@ -808,6 +829,7 @@ void register_symm(py::module &m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_symm(m);
+  m.def("take_error", &take_error);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("gemm_reduce_scatter", &gemm_reduce_scatter);
   m.def("sp_reduce_norm", &sp_reduce_norm);

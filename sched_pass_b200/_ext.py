@@ -44,9 +44,15 @@ class _Counted:
         if n is None or not callable(f):
             return f
 
+        take = self._mod.take_error
+
         def counted(*a, **k):
             self.launches += n
-            return f(*a, **k)
+            r = f(*a, **k)
+            rc, op = take()  # launch errors are recorded by the binding, raised here
+            if rc:
+                raise RuntimeError(f"{op} launch failed (code {rc})")
+            return r
 
         counted.__name__ = name
         self.__dict__[name] = counted  # later lookups skip __getattr__

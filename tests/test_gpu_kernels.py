@@ -178,6 +178,17 @@ def test_argmax_rows_of_any_pitch():
             assert torch.equal(out.long(), want)
 
 
+def test_launch_error_raises_and_the_process_survives():
+    """A launcher that refuses a call (here a GEMM whose N is not a multiple
+    of the 128-row tile) raises RuntimeError in Python; the next valid call
+    works (the binding records the code, the Python wrapper raises it)."""
+    x = torch.randn(3, 512, device=DEV).to(torch.bfloat16)
+    with pytest.raises(RuntimeError, match="gemm launch failed"):
+        ops.linear(x, torch.randn(1004, 512, device=DEV).to(torch.bfloat16))
+    w = torch.randn(1024, 512, device=DEV).to(torch.bfloat16)
+    assert rel_err(ops.linear(x, w), x.float() @ w.float().t()) < 1e-2
+
+
 # ------------------------------------------------------------------ decode attention
 
 def test_embedding_takes_negative_ids_from_the_previous_step():

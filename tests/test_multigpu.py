@@ -25,12 +25,20 @@ def run_torchrun(worker, n, timeout=600, env=None):
     return r
 
 
+def _why(r) -> str:
+    """A failed run's tail plus every Python frame a crashed rank's
+    faulthandler printed (the tails of interleaved rank streams cut them)."""
+    frames = [ln for ln in r.stderr.splitlines() if 'File "' in ln or "Fatal Python" in ln or "STAGE" in ln]
+    stages = [ln for ln in r.stdout.splitlines() if ln.startswith("STAGE")]
+    return "\n".join(stages[-10:] + frames[:60]) + "\n" + r.stdout[-2000:] + r.stderr[-2000:]
+
+
 @pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
 def test_fused_allreduce_and_tp_engine():
     n = 2 if _ngpus() < 4 else min(_ngpus(), 8)
     r = run_torchrun("tp_worker.py", n)
     line = [l for l in r.stdout.splitlines() if l.startswith("TPJSON ")]
-    assert r.returncode == 0 and line, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.returncode == 0 and line, _why(r)
     res = json.loads(line[0][len("TPJSON "):])
     for c in res["checks"]:
         assert c["rel_err"] < 1e-2, c
@@ -51,7 +59,7 @@ def test_expert_parallel_layer():
     n = 2 if _ngpus() < 4 else min(_ngpus(), 8)
     r = run_torchrun("ep_worker.py", n)
     line = [l for l in r.stdout.splitlines() if l.startswith("EPJSON ")]
-    assert r.returncode == 0 and line, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.returncode == 0 and line, _why(r)
     for res in json.loads(line[0][len("EPJSON "):]):
         assert res["dropped"] == 0, res
         for c in res["checks"]:
@@ -67,7 +75,7 @@ def test_sequence_parallel_matches_fused_allreduce():
     n = 2 if _ngpus() < 4 else min(_ngpus(), 8)
     r = run_torchrun("sp_worker.py", n)
     line = [l for l in r.stdout.splitlines() if l.startswith("SPJSON ")]
-    assert r.returncode == 0 and line, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.returncode == 0 and line, _why(r)
     res = json.loads(line[0][len("SPJSON "):])
     for c in res["checks"]:
         assert c["delta_bits"] and c["residual_bits"] and c["normed_bits"], c

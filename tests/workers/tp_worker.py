@@ -57,10 +57,11 @@ def main():
         out["checks"].append({"T": T, "N": N, "K": K, "rel_err": err, "identical_on_ranks": same,
                               "matches_protocol_oracle": oracle_ok, "fused_norm_exact": norm_ok})
     ops.check_status()
+    print(f"STAGE {rank} fused all-reduce checks done", flush=True)
     # greedy sampling over a vocabulary split across ranks: the in-kernel
     # exchange of (max, id) pairs == the all-gather of the pairs
     H, V = 512, 1000 * world + 7
-    vloc = (V + world - 1) // world
+    vloc = ((V + world - 1) // world + 127) // 128 * 128  # shard rows padded to GEMM row tiles, as the model does
     lm = (torch.randn(vloc * world, H, generator=g) / H ** 0.5).to(torch.bfloat16)
     lm_local = lm[rank * vloc:(rank + 1) * vloc].to(dev).contiguous()
     samples = []
@@ -78,6 +79,7 @@ def main():
                         "agrees_with_fp32": float((a.cpu().long() == want).float().mean())})
     out["sampling"] = samples
     ops.check_status()
+    print(f"STAGE {rank} sampling exchange done", flush=True)
     # engine: TP generation == single-GPU generation
     from sched_pass_b200.engine.engine import Engine, EngineConfig
     from sched_pass_b200.models.config import LLAMA_TINY, ModelConfig
@@ -92,6 +94,7 @@ def main():
     eng = Engine(cfg, EngineConfig(**ecfg), dev, tp=tp,
                  weights=shard_weights(cfg, full, rank, world, dev))
     tp_out = eng.generate(prompts, max_new_tokens=5)
+    print(f"STAGE {rank} TP engine generated", flush=True)
     del eng
     if rank == 0:
         single = Engine(cfg, EngineConfig(**ecfg), dev,
