@@ -683,8 +683,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             __threadfence();
             const int part0 = ti.req * p.splits;
             constexpr int SMAX = 8;  // the engine splits a request at most 8 ways
+            bool merged = false;
+            if constexpr (G * SMAX <= 32) {
+              if (p.splits <= SMAX) {
+                // every head's split LSEs and partial rows in ONE round of
+                // independent L2 loads, ahead of any output store (per head,
+                // the loads of head h+1 could not pass head h's store)
+                float lse[G][SMAX], po[G][SMAX];
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
+                for (int h = 0; h < G; ++h)
+#pragma unroll
+                  for (int s2 = 0; s2 < SMAX; ++s2) {
+                    const bool in = s2 < p.splits;
+                    lse[h][s2] = in ? __ldcg(&p.part_lse[(size_t)(part0 + s2) * p.Hq + hq0 + h]) : -INFINITY;
+                    po[h][s2] = in ? __ldcg(&p.part_o[((size_t)(part0 + s2) * p.Hq + hq0 + h) * D + t]) : 0.f;
+                  }
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                  float mx = -INFINITY, acc = 0.f, wsum = 0.f;
+#pragma unroll
+                  for (int s2 = 0; s2 < SMAX; ++s2)
+                    if (s2 < p.splits) mx = fmaxf(mx, lse[h][s2]);
+                  if (mx != -INFINITY) {
+#pragma unroll
+                    for (int s2 = 0; s2 < SMAX; ++s2) {  // fixed order: deterministic
+                      if (s2 < p.splits) {
+                        const float w = exp2f(lse[h][s2] - mx);
+                        acc += w * po[h][s2];
+                        wsum += w;
+                      }
+                    }
+                  }
+                  p.out[((size_t)ti.req * p.Hq + hq0 + h) * D + t] =
+                      __float2bfloat16(wsum > 0.f ? acc / wsum : 0.f);
+                }
+                merged = true;
+              }
+            }
+#pragma unroll
+            for (int h = 0; h < G && !merged; ++h) {
               float mx = -INFINITY, acc = 0.f, wsum = 0.f;
               if (p.splits <= SMAX) {
                 // every split's LSE and partial row of this head in one round of
