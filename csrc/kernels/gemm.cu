@@ -593,39 +593,60 @@ __device__ __forceinline__ void ll_finish(const GemmArgs &a) {
   }
 }
 
-// One thread's share of a reduced row in the low-latency exchange: poll the
-// four lines of each source (rank order) until both halves carry the call's
-// epoch (bounded), sum in fp32, store 16 output columns.
+// One thread's share of a reduced row in the low-latency exchange: load the
+// four lines of EVERY source in one round of independent loads, re-poll only
+// the sources whose halves do not yet carry the call's epoch (bounded), then
+// sum in rank order (fp32) and store 16 output columns. (Polling the sources
+// one after another put world dependent load round trips on every call.)
 __device__ __forceinline__ void reduce_line_row(const GemmArgs &a, const uint4 *mine, int nt, int t, int col,
                                                 uint32_t e) {
+  uint2 pl[kMaxWorld][4];  // payload words of each source's four lines, once they carry the epoch
+  const uint4 *base = mine + (((size_t)t * a.N + (size_t)nt * BM + col) / 4);
+  const size_t src_stride = (size_t)a.T * a.N / 4;  // lines between sources
+  uint32_t pending = a.world >= 32 ? 0xFFFFFFFFu : ((1u << a.world) - 1u);
+  uint64_t start = 0;
+  for (uint32_t polls = 0; pending != 0u; ++polls) {
+#pragma unroll
+    for (int src = 0; src < kMaxWorld; ++src) {
+      if (!(pending & (1u << src))) continue;
+      const uint4 *q = base + (size_t)src * src_stride;
+      uint4 l[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) l[i] = ld_volatile_v4(reinterpret_cast<const uint32_t *>(q + i));
+      bool ok = true;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ok = ok && l[i].y == e && l[i].w == e;
+      if (ok) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pl[src][i] = make_uint2(l[i].x, l[i].z);
+        pending &= ~(1u << src);
+      }
+    }
+    if (pending != 0u && (polls & 63u) == 0u) {
+      const uint64_t now = ptx::globaltimer_ns();
+      if (start == 0) {
+        start = now;
+      } else if (now - start > kWaitBudgetNs) {
+        report_status(a.status, kStatusPeerTimeout);
+#pragma unroll
+        for (int src = 0; src < kMaxWorld; ++src)
+          if (pending & (1u << src))
+#pragma unroll
+            for (int i = 0; i < 4; ++i) pl[src][i] = make_uint2(0u, 0u);
+        break;
+      }
+    }
+  }
   float acc[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-  for (int src = 0; src < a.world; ++src) {
-    const uint4 *q = mine + (((size_t)src * a.T + t) * a.N + (size_t)nt * BM + col) / 4;
-    uint4 l[4];
-    bool ok = false;
-    uint64_t start = 0;
-    for (uint32_t polls = 0; !ok; ++polls) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) l[i] = ld_volatile_v4(reinterpret_cast<const uint32_t *>(q + i));
-      ok = true;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) ok = ok && l[i].y == e && l[i].w == e;
-      if (!ok && (polls & 63u) == 0u) {
-        const uint64_t now = ptx::globaltimer_ns();
-        if (start == 0) {
-          start = now;
-        } else if (now - start > kWaitBudgetNs) {
-          report_status(a.status, kStatusPeerTimeout);
-          break;
-        }
-      }
-    }
+  for (int src = 0; src < kMaxWorld; ++src) {  // rank order: the same sums as the flag path
+    if (src >= a.world) break;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const __nv_bfloat16 *lo = reinterpret_cast<const __nv_bfloat16 *>(&l[i].x);
-      const __nv_bfloat16 *hi = reinterpret_cast<const __nv_bfloat16 *>(&l[i].z);
+      const __nv_bfloat16 *lo = reinterpret_cast<const __nv_bfloat16 *>(&pl[src][i].x);
+      const __nv_bfloat16 *hi = reinterpret_cast<const __nv_bfloat16 *>(&pl[src][i].y);
       acc[4 * i] += __bfloat162float(lo[0]);
       acc[4 * i + 1] += __bfloat162float(lo[1]);
       acc[4 * i + 2] += __bfloat162float(hi[0]);
