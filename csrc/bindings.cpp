@@ -58,6 +58,10 @@ extern "C" void sched_attn_decode_set_trace(unsigned long long *trace);
 extern "C" int sched_argmax_exchange(const void *logits, int T, int V, int ld, int32_t *ids, float *maxv,
                                      int id_offset, void *const *lines, int world, int rank, uint32_t *state,
                                      long long set_lines, int *status, cudaStream_t st);
+extern "C" int sched_probe_clc_shape(const uint32_t *work, int gx, int gy, int gz, int stride, int cx,
+                                     unsigned *hits, unsigned *claimed, unsigned *launched, unsigned *fails,
+                                     unsigned *w_nonzero, int *status, cudaStream_t st);
+extern "C" int sched_probe_clc_shape_capacity(int cx);
 extern "C" int sched_probe_clc(const uint32_t *work, int n_tasks, int mode, int grid, int max_rec, unsigned *hits,
                                unsigned long long *rec, unsigned *n_rec, unsigned *smid, int *status,
                                cudaStream_t st);
@@ -716,6 +720,29 @@ void probe_tasks(const at::Tensor &cost, int64_t mode, int64_t grid, int64_t mem
   check_rc(rc_, "probe_tasks");
 }
 
+// counters: int32 [4n + 1] on the device: hits, claimed, launched, fails
+// (n each) and the count of claim answers with a non-zero fourth word.
+void probe_clc_shape(const at::Tensor &work, int64_t gx, int64_t gy, int64_t gz, int64_t stride, int64_t cx,
+                     at::Tensor &counters, const c10::optional<at::Tensor> &status) {
+  TORCH_CHECK(work.is_cuda() && work.scalar_type() == at::kInt && work.is_contiguous(), "work int32 on the device");
+  TORCH_CHECK(gx > 0 && gy > 0 && gz > 0 && stride > 0 && cx >= 1 && cx <= 8 && gx % cx == 0,
+              "grid dims > 0, stride > 0, cluster 1..8 dividing gx");
+  const int64_t n = gx * gy * gz;
+  TORCH_CHECK(work.numel() >= n, "work: one entry per CTA");
+  TORCH_CHECK(counters.is_cuda() && counters.element_size() == 4 && counters.is_contiguous() &&
+                  counters.numel() >= 4 * n + 1,
+              "counters: int32 [4 n + 1]");
+  unsigned *c = reinterpret_cast<unsigned *>(counters.data_ptr());
+  int rc_ = 0;
+  {  // the guard is gone before the launch code is recorded
+    c10::cuda::CUDAGuard gd(work.device());
+    rc_ = sched_probe_clc_shape(reinterpret_cast<const uint32_t *>(work.data_ptr()), (int)gx, (int)gy, (int)gz,
+                                (int)stride, (int)cx, c, c + n, c + 2 * n, c + 3 * n, c + 4 * n,
+                                ptr_or_null<int>(status), cur_stream());
+  }
+  check_rc(rc_, "probe_clc_shape");
+}
+
 void probe_clc(const at::Tensor &work, int64_t mode, int64_t grid, at::Tensor &hits, at::Tensor &rec,
                at::Tensor &n_rec, at::Tensor &smid, const c10::optional<at::Tensor> &status) {
   TORCH_CHECK(work.is_cuda() && work.scalar_type() == at::kInt && work.is_contiguous(), "work int32 on the device");
@@ -863,6 +890,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("probe_tasks_occupancy", &sched_probe_tasks_occupancy);
   m.def("probe_mix", &probe_mix);
   m.def("probe_clc", &probe_clc);
+  m.def("probe_clc_shape", &probe_clc_shape);
+  m.def("probe_clc_shape_capacity", &sched_probe_clc_shape_capacity);
   m.def("kv_page_copy_fp8", &kv_page_copy_fp8);
   m.def("probe_pdl_pairs", &probe_pdl_pairs);
   m.def("probe_pdl_produce", &probe_pdl_produce);

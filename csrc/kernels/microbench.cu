@@ -282,6 +282,132 @@ __global__ void __launch_bounds__(128) clc_probe(const ClcArgs a) {
   if (threadIdx.x == 0) a.n_rec[c] = nrec;
 }
 
+// ---------------------------------------------------------------- clc shapes
+// The CLC contract under other launch shapes (after the reference's
+// experiments/clc/clc_2d_probe.cu, clc_tuple_probe.cu,
+// clc_participation_probe.cu, clc_cluster_probe.cu; FINDINGS.md:513-802):
+// 2-D / 3-D grids (a claim returns the cancelled CTA's (x, y, z); its linear
+// id is x + y gx + z gx gy), partial participation (only CTAs whose linear
+// id is a multiple of `stride` claim; the others run their own task and
+// leave), and clustered launches (cluster of `cx` CTAs along x: the cluster's
+// rank 0 claims once per round for the whole cluster and passes the answer to
+// its peers through distributed shared memory; a claim cancels a whole
+// cluster, whose CTA k then runs task base + k).
+struct ClcShapeArgs {
+  const uint32_t *work;  // [n] cycles of each task's body
+  int n;                 // tasks = CTAs of the launch
+  int gx, gy;            // grid x and y (linear id = x + y gx + z gx gy)
+  int stride;            // claim participation: linear id (cluster base) % stride == 0
+  int cx;                // cluster size along x (1: no cluster)
+  unsigned *hits;        // [n] executions (must end at 1)
+  unsigned *claimed;     // [n] times a task came back from a claim
+  unsigned *launched;    // [n] 1 when the task's CTA was started by the launcher
+  unsigned *fails;       // [n] failed claims of the worker that started as that CTA
+  unsigned *w_nonzero;   // fourth word of a claim answer seen non-zero
+  int *status;
+};
+
+__device__ __forceinline__ void clc_shape_body(const ClcShapeArgs &a, uint32_t task) {
+  if (threadIdx.x == 0) {
+    const long long t0 = clock64();
+    while (clock64() - t0 < (long long)a.work[task]) {
+    }
+    atomicAdd(a.hits + task, 1u);
+  }
+  __syncthreads();
+}
+
+// Waits (bounded) for the claim in flight; returns the cancelled CTA's
+// linear id, or ~0u on failure / give-up.
+__device__ __forceinline__ uint32_t clc_collect_linear(uint4 *result, uint64_t *bar, uint32_t &phase,
+                                                       const ClcShapeArgs &a) {
+  const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  const uint64_t t0 = ptx::globaltimer_ns();
+  uint32_t done = 0;
+  for (uint32_t polls = 0; !done; ++polls) {
+    asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(done)
+                 : "r"(b), "r"(phase)
+                 : "memory");
+    if (!done && (polls & 255u) == 255u && ptx::globaltimer_ns() - t0 > kWaitBudgetNs) {
+      report_status(a.status, kStatusClcTimeout);
+      return ~0u;
+    }
+  }
+  phase ^= 1u;
+  uint32_t ok = 0, x = 0, y = 0, z = 0, w = 0;
+  const uint32_t res = static_cast<uint32_t>(__cvta_generic_to_shared(result));
+  asm volatile(
+      "{\n.reg .pred p;\n.reg .b128 h;\n"
+      "ld.shared.b128 h, [%5];\n"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, h;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid.v4.b32.b128 {%1, %2, %3, %4}, h;\n"
+      "}\n"
+      : "=r"(ok), "+r"(x), "+r"(y), "+r"(z), "+r"(w)
+      : "r"(res)
+      : "memory");
+  if (!ok) return ~0u;
+  if (w != 0u) atomicAdd(a.w_nonzero, 1u);
+  return x + y * (uint32_t)a.gx + z * (uint32_t)a.gx * (uint32_t)a.gy;
+}
+
+__global__ void __launch_bounds__(128) clc_shape_probe(const ClcShapeArgs a) {
+  __shared__ uint4 result;
+  __shared__ uint64_t bar;
+  __shared__ uint32_t next;
+  const uint32_t me = blockIdx.x + blockIdx.y * (uint32_t)a.gx + blockIdx.z * (uint32_t)a.gx * (uint32_t)a.gy;
+  const uint32_t rank = a.cx > 1 ? ptx::cluster_ctarank() : 0u;
+  const uint32_t base = me - rank;  // the cluster's first CTA (clusters run along x)
+  if (threadIdx.x == 0) {
+    a.launched[me] = 1u;
+    ptx::mbar_init(&bar, 1);
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (a.cx > 1) ptx::cluster_sync_all();  // peers' shared memory is live before any DSMEM store
+  clc_shape_body(a, me);
+  const bool claims = (base % (uint32_t)a.stride) == 0u;
+  if (!claims) return;  // the whole cluster leaves together (same base)
+  uint32_t phase = 0, nfail = 0;
+  while (true) {
+    if (threadIdx.x == 0 && rank == 0u) {
+      const uint32_t r = static_cast<uint32_t>(__cvta_generic_to_shared(&result));
+      const uint32_t bb = static_cast<uint32_t>(__cvta_generic_to_shared(&bar));
+      asm volatile(
+          "{\n.reg .b64 st;\n"
+          "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%1], 16;\n"
+          "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];\n"
+          "}\n" ::"r"(r),
+          "r"(bb)
+          : "memory");
+      const uint32_t x = clc_collect_linear(&result, &bar, phase, a);
+      if (x == ~0u) ++nfail;
+      next = x;
+      // the cluster's other CTAs read the answer from rank 0's shared memory
+      // after the cluster barrier below
+    }
+    uint32_t t;
+    if (a.cx > 1) {
+      ptx::cluster_sync_all();  // rank 0's `next` is written
+      const uint32_t remote = ptx::mapa_shared(static_cast<uint32_t>(__cvta_generic_to_shared(&next)), 0);
+      uint32_t v;
+      asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(remote) : "memory");
+      t = v;
+      ptx::cluster_sync_all();  // everyone has read it before rank 0 overwrites it
+    } else {
+      __syncthreads();
+      t = next;
+      __syncthreads();
+    }
+    if (t == ~0u) break;
+    const uint32_t task = t + rank;
+    if (threadIdx.x == 0 && task < (uint32_t)a.n) atomicAdd(a.claimed + task, 1u);
+    if (task < (uint32_t)a.n) clc_shape_body(a, task);
+  }
+  if (threadIdx.x == 0 && rank == 0u) a.fails[me] = nfail;
+}
+
 // ---------------------------------------------------------------- mix
 __device__ __forceinline__ uint4 ld_plain(const uint4 *a) {
   uint4 v;
@@ -390,6 +516,69 @@ extern "C" int sched_probe_clc(const uint32_t *work, int n_tasks, int mode, int 
   if (g <= 0) return -1;
   probe::clc_probe<<<g, 128, 0, st>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+// grid (gx, gy, gz) of 128-thread CTAs, optional cluster of cx CTAs along x
+// (gx % cx == 0); every CTA runs its own task first; CTAs whose cluster base
+// is a multiple of `stride` then claim until a claim fails.
+extern "C" int sched_probe_clc_shape(const uint32_t *work, int gx, int gy, int gz, int stride, int cx,
+                                     unsigned *hits, unsigned *claimed, unsigned *launched, unsigned *fails,
+                                     unsigned *w_nonzero, int *status, cudaStream_t st) {
+  if (gx <= 0 || gy <= 0 || gz <= 0 || stride <= 0 || cx <= 0 || cx > 8 || gx % cx != 0) return -1;
+  probe::ClcShapeArgs a{};
+  a.work = work;
+  a.n = gx * gy * gz;
+  a.gx = gx;
+  a.gy = gy;
+  a.stride = stride;
+  a.cx = cx;
+  a.hits = hits;
+  a.claimed = claimed;
+  a.launched = launched;
+  a.fails = fails;
+  a.w_nonzero = w_nonzero;
+  a.status = status;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(gx, gy, gz);
+  cfg.blockDim = dim3(128);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cx;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = cx > 1 ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, probe::clc_shape_probe, a) != cudaSuccess) return -4;
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+// Resident clusters of cx CTAs of the shape probe (R_cta = this x cx), or
+// resident CTAs (x SMs) when cx = 1.
+extern "C" int sched_probe_clc_shape_capacity(int cx) {
+  if (cx <= 1) {
+    int n = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, probe::clc_shape_probe, 128, 0);
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    return n * sms;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cx * 1024);
+  cfg.blockDim = dim3(128);
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cx;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, probe::clc_shape_probe, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n * cx;
 }
 
 // CTAs of the task probe resident per SM (R = this x SMs).

@@ -23,7 +23,7 @@ LAUNCHERS = {
     "sp_wait_rows": 1, "attn_decode": 1, "attn_merge": 1, "attn_prefill": 1, "add_rmsnorm": 1,
     "rope_kv_append": 1, "embedding": 1, "argmax": 1, "argmax_exchange": 1, "moe_router": 1, "kv_page_copy": 1,
     "kv_page_copy_fp8": 1, "moe_dispatch": 1, "moe_expert_gemm": 1, "moe_quantize": 1,
-    "moe_combine_norm": 1, "probe_stream": 1, "probe_tasks": 1, "probe_mix": 1, "probe_clc": 1, "probe_pdl_pairs": 2,
+    "moe_combine_norm": 1, "probe_stream": 1, "probe_tasks": 1, "probe_mix": 1, "probe_clc": 1, "probe_clc_shape": 1, "probe_pdl_pairs": 2,
     "probe_pdl_produce": 1,
 }
 

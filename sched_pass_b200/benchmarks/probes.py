@@ -283,9 +283,81 @@ def clc(n: int = 8192, base: int = 1024):
         print(json.dumps(row), flush=True)
 
 
+def run_clc_shape(work: np.ndarray, gx: int, gy: int = 1, gz: int = 1, stride: int = 1, cx: int = 1,
+                  graph_replays: int = 0):
+    """One launch (or ``graph_replays`` replays of a CUDA graph holding the
+    counter reset and the launch) of the CLC shape probe; returns the
+    contract figures of the last run."""
+    n = gx * gy * gz
+    w = torch.from_numpy(work[:n]).cuda()
+    counters = torch.zeros(4 * n + 1, dtype=torch.int32, device="cuda")
+    st = ops.status_buffer()
+
+    def go():
+        counters.zero_()
+        ext().probe_clc_shape(w, gx, gy, gz, stride, cx, counters, st)
+    runs = []
+    if graph_replays:
+        go()  # warm-up outside the capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            go()
+        for _ in range(graph_replays):
+            g.replay()
+            torch.cuda.synchronize()
+            runs.append(counters.cpu().numpy().astype(np.int64))
+        del g
+    else:
+        go()
+        torch.cuda.synchronize()
+        runs.append(counters.cpu().numpy().astype(np.int64))
+    ops.check_status()
+    out = []
+    for c in runs:
+        hits, claimed, launched, fails = c[:n], c[n:2 * n], c[2 * n:3 * n], c[3 * n:4 * n]
+        cl = np.flatnonzero(claimed > 0)
+        workers = np.flatnonzero((launched > 0) & (np.arange(n) % (stride * cx) == 0))
+        holes = int(cl[-1] - cl[0] + 1 - cl.size) if cl.size else 0
+        out.append({
+            "tasks": n, "exactly_once": bool((hits == 1).all()), "duplicate_claims": int((claimed > 1).sum()),
+            "launched": int((launched > 0).sum()), "claimed": int(cl.size),
+            "claimed_min": int(cl[0]) if cl.size else None, "claimed_max": int(cl[-1]) if cl.size else None,
+            "claim_holes": holes, "claim_bases_aligned": bool((cl[cl % cx == 0].size * cx == cl.size)) if cx > 1 else True,
+            "claiming_workers": int(workers.size),
+            "failures_per_worker": sorted(set(int(f) for f in fails[workers])) if workers.size else [],
+            "w_nonzero": int(c[4 * n])})
+    return out
+
+
+def clc_shapes(base: int = 1024):
+    """The CLC contract under 2-D / 3-D grids, partial participation,
+    clustered launches and CUDA-graph replay (one JSON line per case)."""
+    R = int(ext().probe_clc_shape_capacity(1))
+    cases = [("1d", dict(gx=8192)), ("2d_64x128", dict(gx=64, gy=128)), ("3d_17x19x29", dict(gx=17, gy=19, gz=29)),
+             ("stride2", dict(gx=8192, stride=2)), ("stride4", dict(gx=8192, stride=4)),
+             ("cluster2", dict(gx=8192, cx=2)), ("cluster4", dict(gx=8192, cx=4)),
+             ("graph_replay", dict(gx=8192, graph_replays=5))]
+    rows = []
+    for name, kw in cases:
+        n = kw["gx"] * kw.get("gy", 1) * kw.get("gz", 1)
+        work = np.full(n, base, dtype=np.int32)
+        res = run_clc_shape(work, **kw)
+        cx = kw.get("cx", 1)
+        pred = int(ext().probe_clc_shape_capacity(cx)) if cx > 1 else R
+        row = {"probe": "clc_shape", "case": name, "predicted_R": pred, **res[-1]}
+        if len(res) > 1:
+            row["replays"] = len(res)
+            row["replays_identical_contract"] = all(
+                r["exactly_once"] and r["claimed_min"] == res[0]["claimed_min"] and r["claim_holes"] == 0 for r in res)
+        print(json.dumps(row), flush=True)
+        rows.append(row)
+    return rows
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", choices=["stream", "tasks", "reuse", "budget", "pdl", "clc"])
+    ap.add_argument("--only", choices=["stream", "tasks", "reuse", "budget", "pdl", "clc", "clc_shapes"])
     a = ap.parse_args(argv)
     if a.only in (None, "stream"):
         stream()
@@ -299,6 +371,8 @@ def main(argv=None):
         pdl()
     if a.only in (None, "clc"):
         clc()
+    if a.only in (None, "clc_shapes"):
+        clc_shapes()
 
 
 if __name__ == "__main__":

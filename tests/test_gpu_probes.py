@@ -101,3 +101,26 @@ def test_clc_terminal_failure_rule_and_exactly_once():
         got = [x for cl in claims.values() for _, x in cl if x != 0xFFFFFFFF]
         assert len(got) == len(set(got)) == n - len(claims), (mode, len(got), len(claims))
         assert len(claims) <= n and len(claims) >= min(n, R // 2)
+
+
+def test_clc_contract_under_shapes_participation_clusters_and_graphs():
+    """CLC on B200 under the launch shapes the reference probes
+    (experiments/clc/FINDINGS.md:441-802): in every case each task runs
+    exactly once; with full participation the claimed CTAs are exactly the
+    suffix [R, n) of the linear CTA order (2-D / 3-D ids map back linearly,
+    the answer's fourth word stays zero), every worker ends with one failed
+    claim, clustered launches claim whole aligned clusters, and CUDA-graph
+    replays keep the same contract; with partial participation no task is
+    lost or run twice."""
+    from sched_pass_b200.benchmarks import probes
+    rows = {r["case"]: r for r in probes.clc_shapes()}
+    for name, r in rows.items():
+        assert r["exactly_once"] and r["duplicate_claims"] == 0, r
+    for name in ("1d", "2d_64x128", "3d_17x19x29", "cluster2", "cluster4", "graph_replay"):
+        r = rows[name]
+        assert r["claim_holes"] == 0 and r["claimed_max"] == r["tasks"] - 1, r
+        assert r["claimed_min"] == r["launched"], r
+        assert r["failures_per_worker"] == [1], r
+        assert r["w_nonzero"] == 0, r
+    assert rows["cluster2"]["claim_bases_aligned"] and rows["cluster4"]["claim_bases_aligned"]
+    assert rows["graph_replay"]["replays_identical_contract"]
