@@ -1230,6 +1230,292 @@ static void launch_tn(const CUtensorMap &tw, const CUtensorMap &tx, const Params
   cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair GEMM for prefill-sized calls (tcgen05.mma.cta_group::2, M = 256).
+//
+// A cluster of two CTAs owns one 256 x 256 output tile (256 weight rows x 256
+// tokens): CTA r stages weight rows [128 r, 128 r + 128) and tokens
+// [128 r, 128 r + 128) of the tile in its shared memory, the even CTA issues
+// one M = 256, N = 256 MMA per 16-deep K step that reads both CTAs' stages,
+// and each CTA's TMEM receives its 128 weight rows x all 256 tokens. Per SM
+// that is 32 KB of operands per 2 x 128 x 256 x 64 multiply-adds, against
+// 48 KB for the single-CTA 128 x 256 tile: a third less L2-to-SM traffic,
+// which bounds the single-CTA kernel at prefill sizes. Two 256-column
+// accumulators per CTA (all of TMEM) let each epilogue drain one tile while
+// the MMA fills the next.
+//
+// Pipeline: both CTAs' producers load their halves with TMA (cta_group::2
+// form: completion counted on the even CTA's stage barrier, no multicast);
+// the even CTA's MMA thread releases each stage in both CTAs with one
+// tcgen05.commit per CTA, and signals each CTA's accumulator likewise; both
+// epilogues release an accumulator on the even CTA's barrier (256
+// arrivals). Tiles go to clusters round-robin (data-parallel, no split-K);
+// the host uses this kernel only where that fills the GPU's waves well.
+constexpr int kPairTN = 256;
+constexpr int kPairStages = 6;
+constexpr int kPairHalf = BM * BK * 2;  // 128 rows x 64 bf16: one CTA's W or X half of a stage
+constexpr int kPairStageBytes = 2 * kPairHalf;
+constexpr int kPairAccCols = 256;
+constexpr int kPairSmem = 1024 + kPairStages * kPairStageBytes + kSlab * kSlabPitch * 4 + 512;
+static_assert(kPairSmem <= 232448, "pair GEMM shared memory");
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                     const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *base = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *stage_mem = base;
+  float *slab = reinterpret_cast<float *>(base + kPairStages * kPairStageBytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + kPairStages * kPairStageBytes + kSlab * kSlabPitch * 4);
+  uint64_t *full = bars;                              // [stages] (the even CTA's count both halves)
+  uint64_t *empty = bars + kPairStages;               // [stages]
+  uint64_t *acc_full = bars + 2 * kPairStages;        // [2]
+  uint64_t *acc_empty = bars + 2 * kPairStages + 2;   // [2] (the even CTA's count both epilogues)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * kPairStages + 4);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+  const GemmArgs &a = p.a;
+  const int t_tiles = (a.T + kPairTN - 1) / kPairTN;
+  const int tiles = (a.N / (2 * BM)) * t_tiles;
+  const int kb = a.K / BK;
+  auto on_even = [](uint64_t *b) { return ptx::mapa_shared(ptx::smem_u32(b), 0); };
+  auto on_odd = [](uint64_t *b) { return ptx::mapa_shared(ptx::smem_u32(b), 1); };
+
+  ptx::pdl_launch_dependents();
+  if (warp == 0) {
+    ptx::tmem_alloc_pair(tmem_slot, 2 * kPairAccCols);
+    ptx::tmem_relinquish_pair();
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < kPairStages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(&acc_full[i], 1);
+      ptx::mbar_init(&acc_empty[i], 2 * kEpiThreads);
+    }
+    ptx::fence_mbar_init();
+  }
+  if (threadIdx.x == 64) {
+    ptx::prefetch_tmap(&tmW);
+    ptx::prefetch_tmap(&tmX);
+  }
+  ptx::tc_fence_before();
+  __syncwarp();
+  __syncthreads();
+  ptx::cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or TMA completion
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ============================================================ producer (both CTAs)
+    if (ptx::elect_one()) {
+      ptx::pdl_wait();
+      int i = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < tiles; tile += npairs) {
+        const int mt = tile / t_tiles, tt = tile % t_tiles;
+        for (int k = 0; k < kb; ++k, ++i) {
+          const int s = i % kPairStages;
+          if (!ptx::mbar_wait(&empty[s], ((i / kPairStages) & 1) ^ 1, kWaitBudgetNs)) {
+            report_status(a.status, kStatusMmaTimeout);
+            ok = false;
+            break;
+          }
+          if (rank == 0) ptx::mbar_arrive_expect_tx(&full[s], 2 * kPairStageBytes);
+          uint8_t *sm = stage_mem + s * kPairStageBytes;
+          const uint32_t fb = on_even(&full[s]);
+          ptx::tma_load_2d_pair(sm, &tmW, fb, k * BK, mt * 2 * BM + (int)rank * BM);
+          ptx::tma_load_2d_pair(sm + kPairHalf, &tmX, fb, k * BK, tt * kPairTN + (int)rank * BM);
+        }
+      }
+      // drain: every release the even CTA's MMA thread sends to this CTA's
+      // stages has landed before the CTA may exit
+      for (int j = i > kPairStages ? i - kPairStages : 0; ok && j < i; ++j)
+        if (!ptx::mbar_wait(&empty[j % kPairStages], (j / kPairStages) & 1, kWaitBudgetNs)) {
+          report_status(a.status, kStatusMmaTimeout);
+          break;
+        }
+    }
+  } else if (warp == 1) {
+    // ============================================================ MMA (the even CTA)
+    if (rank == 0 && ptx::elect_one()) {
+      constexpr uint32_t idesc = ptx::idesc_f16(2 * BM, kPairTN, /*bf16*/ 1, false, false);
+      int i = 0, n = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < tiles; tile += npairs, ++n) {
+        const int ab = n & 1;
+        if (!ptx::mbar_wait(&acc_empty[ab], ((n >> 1) & 1) ^ 1, kWaitBudgetNs)) {
+          report_status(a.status, kStatusEpilogueTimeout);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t acc = tmem + ab * kPairAccCols;
+        for (int k = 0; k < kb; ++k, ++i) {
+          const int s = i % kPairStages;
+          if (!ptx::mbar_wait(&full[s], (i / kPairStages) & 1, kWaitBudgetNs)) {
+            report_status(a.status, kStatusTmaTimeout);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          uint8_t *sm = stage_mem + s * kPairStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t da = ptx::smem_desc(sm + kk * 32, 16, 1024, ptx::kLayoutSW128);
+            const uint64_t db = ptx::smem_desc(sm + kPairHalf + kk * 32, 16, 1024, ptx::kLayoutSW128);
+            ptx::mma_f16_ss_pair(acc, da, db, idesc, (k > 0 || kk > 0) ? 1u : 0u);
+          }
+          ptx::mma_commit_pair(on_even(&empty[s]));  // both CTAs' stage s may refill
+          ptx::mma_commit_pair(on_odd(&empty[s]));
+        }
+        ptx::mma_commit_pair(on_even(&acc_full[ab]));  // both CTAs' accumulator ab is final
+        ptx::mma_commit_pair(on_odd(&acc_full[ab]));
+      }
+    }
+  } else {
+    // ============================================================ epilogue (both CTAs)
+    const int et = threadIdx.x - 64;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int tj = et / 8, part = et % 8;
+    ptx::pdl_wait();
+    int n = 0;
+    for (int tile = pair; tile < tiles; tile += npairs, ++n) {
+      const int ab = n & 1;
+      const bool waited = ptx::mbar_wait(&acc_full[ab], (n >> 1) & 1, kWaitBudgetNs);
+      if (!waited) report_status(a.status, kStatusEpilogueTimeout);
+      ptx::tc_fence_after();
+      const int mt = tile / t_tiles, tt = tile % t_tiles;
+      const int nt = mt * 2 + (int)rank;  // this CTA's 128-row weight tile
+      const int t0 = tt * kPairTN;
+      for (int ch = 0; ch < kPairTN / kSlab; ++ch) {
+        if (t0 + ch * kSlab >= a.T) break;  // uniform across the CTA
+        uint32_t r[16];
+        ptx::tmem_ld16(tmem + ab * kPairAccCols + ((uint32_t)(q * 32) << 16) + ch * kSlab, r);
+        ptx::tmem_ld_wait();
+        if (!waited) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) r[j] = 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) slab[j * kSlabPitch + row] = __uint_as_float(r[j]);
+        named_bar(1, kEpiThreads);
+        const int t = t0 + ch * kSlab + tj;
+        if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part);
+        named_bar(1, kEpiThreads);
+      }
+      ptx::tc_fence_before();
+      if (rank == 0)
+        ptx::mbar_arrive(&acc_empty[ab]);
+      else
+        ptx::mbar_arrive_cluster(on_even(&acc_empty[ab]));
+    }
+  }
+
+  __syncwarp();
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync_all();  // the pair's MMAs, reads of TMEM and remote arrivals are done
+  ptx::tc_fence_after();
+  if (warp == 0) ptx::tmem_dealloc_pair(tmem, 2 * kPairAccCols);
+}
+
+// Clusters of two pair-GEMM CTAs that fit on the GPU at once.
+template <int EPI>
+static int pair_capacity() {
+  static int cached = -1;
+  if (cached >= 0) return cached;
+  auto kern = gemm_pair_kernel<EPI>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 64);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmem;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cached = n;
+  return n;
+}
+
+// Clusters for a pair-GEMM launch of this call, or 0 for the single-CTA
+// schedules. Taken for default-grid store / SwiGLU / RoPE+KV calls with
+// N % 256 == 0 and T >= 256 whose 256 x 256 tiles keep at least 30 % of the
+// resident clusters busy over their waves (the kernel does not split K).
+// Measured on B200 (us, pair vs single-CTA stream-K): T = 1536: gate_up 232
+// vs 349, qkv 56 vs 91, o_proj 54 vs 73 and down_proj 151 vs 205 (65 % of
+// the clusters busy), lm_head 1007 vs 1441; T = 512: every shape faster
+// (o_proj 35 vs 44 with 43 % busy); T = 256: qkv 35 vs 49 (32 % busy),
+// gate_up 76 vs 102, but o_proj 33 vs 29 and down_proj 80 vs 62 (16 tiles,
+// 22 % busy) stay single-CTA. SCHED_GEMM_PAIR=0 turns it off; =1 takes it
+// for every eligible shape.
+template <int EPI>
+static int pair_plan_epi(const GemmArgs &a) {
+  const char *v = std::getenv("SCHED_GEMM_PAIR");
+  const int mode = v ? std::atoi(v) : -1;
+  if (mode == 0) return 0;
+  if (a.grid > 0 || a.norm_w != nullptr || a.x_ready != nullptr || a.N % (2 * BM) != 0 || a.K % BK != 0) return 0;
+  if (a.T < (mode == 1 ? 1 : 256)) return 0;
+  const long long tiles = (long long)(a.N / (2 * BM)) * ((a.T + kPairTN - 1) / kPairTN);
+  const int cap = pair_capacity<EPI>();
+  if (cap <= 0) return 0;
+  const int np = (int)std::min<long long>(cap, tiles);
+  const long long waves = (tiles + cap - 1) / cap;
+  const double busy = (double)tiles / (double)(waves * cap);  // resident clusters kept busy
+  return (mode == 1 || busy >= 0.3) ? np : 0;
+}
+
+static int pair_plan(const GemmArgs &a) {
+  switch (a.epi) {
+    case kEpiStore: return pair_plan_epi<kEpiStore>(a);
+    case kEpiSwiGLU: return pair_plan_epi<kEpiSwiGLU>(a);
+    case kEpiRopeKV: return pair_plan_epi<kEpiRopeKV>(a);
+    default: return 0;
+  }
+}
+
+template <int EPI>
+static void launch_pair(const CUtensorMap &tw, const CUtensorMap &tx, const Params &p, int npairs,
+                        cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * npairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
+}
+
 template <int TN, int EPI>
 static void launch_cluster_tn(const CUtensorMap &tw, const CUtensorMap &tx, const Params &p,
                               cudaStream_t stream) {
@@ -1531,6 +1817,18 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   try {
     CUtensorMap tw = tmap::make_2d(a.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.K,
                                    gemm::BM, gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (const int np = gemm::pair_plan(a); np > 0) {
+      // CTA pairs: each CTA stages 128 of a tile's 256 tokens
+      CUtensorMap tx2 = tmap::make_2d(a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.K, a.ldx, gemm::BM,
+                                      gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (a.epi == kEpiSwiGLU)
+        gemm::launch_pair<kEpiSwiGLU>(tw, tx2, p, np, stream);
+      else if (a.epi == kEpiRopeKV)
+        gemm::launch_pair<kEpiRopeKV>(tw, tx2, p, np, stream);
+      else
+        gemm::launch_pair<kEpiStore>(tw, tx2, p, np, stream);
+      return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+    }
     CUtensorMap tx = tmap::make_2d(a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.K, a.ldx, tn,
                                    gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
     if (a.epi == kEpiSwiGLU)

@@ -107,6 +107,57 @@ def test_gemm_qkv_rope_kv_append(T, grid):
         assert kc[slot[1:].long() // 16].abs().sum() > 0
 
 
+@pytest.mark.parametrize("T,N,K,swiglu", [
+    (600, 2048, 1024, False), (1030, 4096, 512, True), (256, 512, 256, False), (1536, 1024, 4096, False),
+    (1, 512, 512, False),
+])
+def test_gemm_cta_pair_matches_fp32(T, N, K, swiglu, monkeypatch):
+    """The CTA-pair GEMM (tcgen05.mma.cta_group::2, 256 x 256 tiles split over
+    a cluster of two CTAs), forced for every eligible shape, against fp32:
+    plain store and SwiGLU, token counts that do not fill the last tile."""
+    monkeypatch.setenv("SCHED_GEMM_PAIR", "1")
+    g = torch.Generator(device=DEV).manual_seed(T + N)
+    x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    got = ops.linear(x, w, swiglu=swiglu)
+    torch.cuda.synchronize()
+    want = ref.swiglu_linear(x, w) if swiglu else ref.linear(x, w)
+    assert rel_err(got, want) < 1e-2
+    monkeypatch.setenv("SCHED_GEMM_PAIR", "0")
+    assert rel_err(ops.linear(x, w, swiglu=swiglu), want) < 1e-2
+
+
+def test_gemm_cta_pair_qkv_rope(monkeypatch):
+    """The RoPE + KV-append epilogue on the CTA-pair schedule: rotated
+    queries against fp32, and queries, keys and values (written into their
+    cache pages) against the single-CTA schedule."""
+    from sched_pass_b200.models.config import LLAMA_TINY
+    from sched_pass_b200.models.llama import rope_table
+    cfg = LLAMA_TINY
+    Hq, Hkv, D, H = cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden
+    cs = rope_table(cfg, 4096, DEV)
+    T = 700
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn((Hq + 2 * Hkv) * D, H, device=DEV, generator=g) / math.sqrt(H)).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), device=DEV, dtype=torch.int32)
+    slot = torch.randperm(64 * 16, device=DEV)[:T].to(torch.int32)
+
+    def run(mode):
+        monkeypatch.setenv("SCHED_GEMM_PAIR", mode)
+        kc = torch.zeros(64, Hkv, 16, D, dtype=torch.bfloat16, device=DEV)
+        vc = torch.zeros_like(kc)
+        q = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=DEV)
+        ops.linear_qkv_rope(x, w, pos, slot, cs, q, kc, vc, Hq, Hkv)
+        torch.cuda.synchronize()
+        return q, kc, vc
+    qp, kp, vp = run("1")
+    q1, k1, v1 = run("0")
+    qkv = ref.linear(x, w).to(torch.bfloat16).view(T, Hq + 2 * Hkv, D)
+    assert rel_err(qp, ref.rope(qkv[:, :Hq], pos, cs)) < 1e-2
+    assert rel_err(qp, q1) < 1e-2 and rel_err(kp, k1) < 1e-2 and rel_err(vp, v1) < 1e-2
+
+
 # ------------------------------------------------------------------ elementwise
 def test_add_rmsnorm():
     T, H = 7, 4096
