@@ -518,11 +518,14 @@ def test_prefill_attention_lazy_rescale():
     (1, 4096, 4096, 0), (6, 4096, 4096, 0), (16, 4096, 14336, 0), (6, 4096, 4096, 148),
     (100, 4096, 4096, 0), (300, 4096, 14336, 0), (1541, 4096, 4096, 0), (6, 8192, 1024, 0), (5, 12288, 512, 0),
 ])
-def test_linear_add_rmsnorm_fused_matches_separate_kernels(T, N, K, grid):
+def test_linear_add_rmsnorm_fused_matches_separate_kernels(T, N, K, grid, monkeypatch):
     """The projection with the residual add + RMSNorm in its epilogue gives
     the same bits as the GEMM followed by add_rmsnorm (cluster split-K and
     stream-K schedules, hidden sizes using 256, 512 and 1024 virtual norm
-    threads), twice in a row (the row counters reset themselves)."""
+    threads), twice in a row (the row counters reset themselves). The plain
+    GEMM is held on the single-CTA schedules the fused one uses (the CTA-pair
+    schedule sums K in another order)."""
+    monkeypatch.setenv("SCHED_GEMM_PAIR", "0")
     g = torch.Generator(device="cuda").manual_seed(T + N + K)
     x = torch.randn(T, K, device="cuda", generator=g).to(torch.bfloat16)
     w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)

@@ -29,6 +29,14 @@ from sched_pass_b200.parallel.sp import owned_rows
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(autouse=True)
+def _single_cta_gemm_schedules(monkeypatch):
+    """The reference products use ops.linear, checked bit for bit against the
+    reduce-scatter and ready-gated GEMMs, which run the single-CTA schedules;
+    hold ops.linear on them too (the CTA-pair schedule sums K in another order)."""
+    monkeypatch.setenv("SCHED_GEMM_PAIR", "0")
+
 EPS = 1e-5
 
 
