@@ -20,7 +20,8 @@ int sched_attn_decode(const void *q, void *out, const void *k_cache, const void 
                       float *part_lse, uint32_t *merge_cnt, int splits, SchedSlots slots,
                       int woven, int acquire, int grid, int pf_blocks, float dT, float dR,
                       float H, const void *stage_k, const void *stage_v, int stage_pages,
-                      int stage_split, int *status, cudaStream_t st);
+                      int stage_split, const void *l2_prefetch, long long l2_prefetch_bytes, int *status,
+                      cudaStream_t st);
 int sched_attn_merge(const float *part_o, const float *part_lse, const int32_t *merge_req,
                      const int32_t *merge_begin, int rows, int Hq, void *out, cudaStream_t st);
 int sched_attn_decode_occupancy(int group);
@@ -402,7 +403,8 @@ void attn_decode(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache
                  int64_t max_tasks, int64_t woven, int64_t acquire, int64_t grid,
                  int64_t pf_blocks, double dT, double dR, double H,
                  const c10::optional<at::Tensor> &stage_k, const c10::optional<at::Tensor> &stage_v,
-                 int64_t stage_split, const c10::optional<at::Tensor> &status) {
+                 int64_t stage_split, const c10::optional<at::Tensor> &status, int64_t l2_prefetch,
+                 int64_t l2_prefetch_bytes) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   check_bf16(k_cache, "k_cache");
@@ -435,7 +437,8 @@ void attn_decode(const at::Tensor &q, at::Tensor &out, const at::Tensor &k_cache
                                splits, sl, woven, acquire, grid, pf_blocks,
                                (float)dT, (float)dR, (float)H, staged ? stage_k->data_ptr() : nullptr,
                                staged ? stage_v->data_ptr() : nullptr, staged ? (int)stage_k->size(0) : 0,
-                               (int)stage_split, ptr_or_null<int>(status), cur_stream());
+                               (int)stage_split, reinterpret_cast<const void *>(l2_prefetch),
+                               (long long)l2_prefetch_bytes, ptr_or_null<int>(status), cur_stream());
   }
   check_rc(rc_, "attn_decode");
 }

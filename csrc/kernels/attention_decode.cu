@@ -105,6 +105,11 @@ struct Params {
   sched::PolicyConsts pc;
   int pf_blocks;  // urgent prefetch distance in KV blocks
   int *status;
+  // L2 prefetch of the next kernel's operand (e.g. the output projection's
+  // weights) while this kernel leaves DRAM mostly idle: each CTA issues bulk
+  // prefetches for its 1/grid slice after its first task's loads (null: off)
+  const uint8_t *l2_prefetch;
+  long long l2_prefetch_bytes;
   // optional per-CTA %globaltimer trace [grid][8] (first task of a CTA):
   // entry, past set-up and the dependency wait, task published, its first
   // KV block's loads issued, first S tile seen by the softmax warps, last
@@ -357,6 +362,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (tr != nullptr && j == 1 && b == 0) tr[3] = ptx::globaltimer_ns();
+          if (j == 1 && b == 0 && p.l2_prefetch != nullptr) {
+            // this CTA's 16-byte-aligned slice of the next operand, in chunks
+            const long long per = ((p.l2_prefetch_bytes / gridDim.x) + 15) & ~15ll;
+            const long long lo = per * blockIdx.x;
+            const long long hi = min(p.l2_prefetch_bytes & ~15ll, lo + per);
+            for (long long o = lo; o < hi; o += 65536) {
+              const uint32_t n = (uint32_t)min(65536ll, hi - o);
+              asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.l2_prefetch + o), "r"(n)
+                           : "memory");
+            }
+          }
           // urgent: warm L2 with the pages pf_blocks ahead (pure hint)
           if (WOVEN && ti.prio == 1 && p.pf_blocks > 0) {
             const int pf0 = pg0 + p.pf_blocks * PAGES_PER_BLK;
@@ -886,7 +902,8 @@ extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
                                  uint32_t *merge_cnt, int splits, SchedSlots slots, int woven,
                                  int acquire, int grid, int pf_blocks, float dT, float dR, float H,
                                  const void *stage_k, const void *stage_v, int stage_pages,
-                                 int stage_split, int *status, cudaStream_t st) {
+                                 int stage_split, const void *l2_prefetch, long long l2_prefetch_bytes,
+                                 int *status, cudaStream_t st) {
   if (num_items <= 0) return 0;
   if (stage_k != nullptr && (stage_v == nullptr || stage_pages <= 0 || stage_split <= 0)) return -1;
   const int G = Hq / Hkv;
@@ -917,6 +934,11 @@ extern "C" int sched_attn_decode(const void *q, void *out, const void *k_cache,
   p.pf_blocks = pf_blocks;
   p.status = status;
   p.trace = g_attn_trace;
+  p.l2_prefetch = (l2_prefetch != nullptr && (reinterpret_cast<uintptr_t>(l2_prefetch) & 15u) == 0 &&
+                   l2_prefetch_bytes >= 16)
+                      ? static_cast<const uint8_t *>(l2_prefetch)
+                      : nullptr;
+  p.l2_prefetch_bytes = l2_prefetch_bytes;
   if (grid <= 0) grid = p.num_tasks;
   try {
     const uint64_t rows = (uint64_t)num_pages * Hkv * attn::PS;

@@ -163,6 +163,12 @@ def shard_weights(cfg: ModelConfig, full: ModelWeights, rank: int, world: int, d
 # separate add_rmsnorm kernel (0, the default: measured faster, see
 # _row_linear_norm)
 FUSED_NORM = os.environ.get("SCHED_FUSED_NORM", "0") == "1"
+# SCHED_L2_PREFETCH=1: decode attention prefetches the output projection's
+# weights into L2 while it streams the KV cache. Off by default: measured on
+# B200 (batch-6 Llama-3-8B steps) it made the decode step slower, 4.30-4.32 vs
+# 4.23 ms p50 (the prefetches compete with the KV stream and delay the
+# producer's first loads).
+L2_PREFETCH = os.environ.get("SCHED_L2_PREFETCH", "0") == "1"
 
 
 @dataclass
@@ -235,6 +241,7 @@ class Llama:
         self.hkv = cfg.n_kv_heads // self.tp_size
         self.cos_sin = rope_table(cfg, max_pos, self.device)
         self.sm_scale = 1.0 / math.sqrt(cfg.head_dim)
+        self.l2_prefetch = L2_PREFETCH
         self.max_tokens = max_tokens
         # sequence-parallel layer plumbing (tensor-parallel mode "sp"), else None
         self.sp = tp.sequence_parallel(cfg.hidden, max_tokens) if tp is not None else None
@@ -288,7 +295,8 @@ class Llama:
             ops.attention_decode(q, out, kc, vc, b.block_table, b.items, b.n_items, self.sm_scale,
                                  part_o=b.part_o, part_lse=b.part_lse, merge_cnt=b.merge_cnt,
                                  splits=b.splits, slots=b.slots, woven=b.slots is not None,
-                                 acquire=b.acquire, grid=b.grid, stage=stage)
+                                 acquire=b.acquire, grid=b.grid, stage=stage,
+                                 l2_prefetch=self.w.layers[li].o if self.l2_prefetch else None)
             if b.tier is not None:
                 b.tier.after_attention(li)
             if b.n_merge > 0 and b.merge_cnt is None:

@@ -194,19 +194,24 @@ def rope_kv_append(qkv: torch.Tensor, pos: torch.Tensor, slot: torch.Tensor, cos
 
 def attention_decode(q, out, k_cache, v_cache, block_table, items, num_items, sm_scale, *,
                      part_o=None, part_lse=None, merge_cnt=None, splits=1, slots=None, woven=True,
-                     acquire=0, grid=0, pf_blocks=2, dT=1.0, dR=1.0, H=0.25, stage=None):
+                     acquire=0, grid=0, pf_blocks=2, dT=1.0, dR=1.0, H=0.25, stage=None,
+                     l2_prefetch=None):
     """Paged decode attention. Items (req, kv_begin, kv_end, part) x KV heads
     are the tasks. With ``merge_cnt`` (int32 [requests * Hkv], zero), split
     requests (part = req * splits + s) are merged inside the kernel.
     ``stage=(k, v, split)``: block-table ids >= split index the staging pool
-    (k, v) [pages, Hkv, 16, 128] at id - split (tiered KV)."""
+    (k, v) [pages, Hkv, 16, 128] at id - split (tiered KV). ``l2_prefetch``:
+    a tensor (the next kernel's weights) whose bytes the CTAs prefetch into
+    L2 while they stream the KV cache (a hint: no result depends on it)."""
     s = slots or {}
+    pf_ptr = l2_prefetch.data_ptr() if l2_prefetch is not None else 0
+    pf_bytes = l2_prefetch.numel() * l2_prefetch.element_size() if l2_prefetch is not None else 0
     sk, sv, split = stage if stage is not None else (None, None, 0)
     ext().attn_decode(q, out, k_cache, v_cache, block_table, items, int(num_items), float(sm_scale),
                       part_o, part_lse, merge_cnt, int(splits), s.get("order"), s.get("ctrl"), s.get("timer"),
                       s.get("queue"), int(s.get("max_tasks", 0)), int(bool(woven)), int(acquire),
                       int(grid), int(pf_blocks), float(dT), float(dR), float(H), sk, sv, int(split),
-                      status_buffer(q.device))
+                      status_buffer(q.device), int(pf_ptr), int(pf_bytes))
     return out
 
 
