@@ -886,6 +886,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     sched_gemm_plan(T, N, K, epi, sms, &cs, &grid);
     return std::make_tuple(cs, grid);
   });
+  m.def("gemm_pair_plan", [](int64_t T, int64_t N, int64_t K, int64_t epi, int64_t ws_floats, int64_t counters) {
+    int np = 0, whole = 0, splits = 1;
+    sched_gemm_pair_plan(T, N, K, epi, ws_floats, counters, &np, &whole, &splits);
+    return std::make_tuple(np, whole, splits);
+  });
   m.def("moe_router", &moe_router);
   m.def("kv_page_copy", &kv_page_copy);
   m.def("probe_stream", &probe_stream);

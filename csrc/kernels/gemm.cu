@@ -94,6 +94,7 @@ struct Params {
   int grid;
   int stages;  // ring depth of this launch (<= Cfg<TN>::STAGES)
   int cs;      // cluster split-K: CTAs per cluster (0: stream-K kernel)
+  int pw = 0, ps = 1;  // pair kernel: tiles [0, pw) whole, the rest in ps k-ranges each (ps <= 1: none)
 };
 
 // Residual add + RMSNorm of the output rows a CTA completes (defined below;
@@ -1249,8 +1250,16 @@ static void launch_tn(const CUtensorMap &tw, const CUtensorMap &tx, const Params
 // the even CTA's MMA thread releases each stage in both CTAs with one
 // tcgen05.commit per CTA, and signals each CTA's accumulator likewise; both
 // epilogues release an accumulator on the even CTA's barrier (256
-// arrivals). Tiles go to clusters round-robin (data-parallel, no split-K);
-// the host uses this kernel only where that fills the GPU's waves well.
+// arrivals). Work units go to clusters round-robin: first the tiles of the
+// full waves whole, then each tile of the last, partly filled wave as ps
+// k-ranges, so that wave occupies ps times as many clusters. A k-range
+// unit writes its fp32 partial to the workspace, counts itself on the
+// tile's counter and waits (bounded) for the tile's other k-ranges: they
+// are the first units of their clusters and the grid never exceeds the
+// clusters that fit on the GPU, so all of them run at once. Each unit then
+// sums 1/ps of the tile's token slabs over the ps partials, in split order
+// (deterministic), and runs the epilogue on them: a CTA reads one tile's
+// worth of partials whatever ps is.
 constexpr int kPairTN = 256;
 constexpr int kPairStages = 6;
 constexpr int kPairHalf = BM * BK * 2;  // 128 rows x 64 bf16: one CTA's W or X half of a stage
@@ -1258,6 +1267,26 @@ constexpr int kPairStageBytes = 2 * kPairHalf;
 constexpr int kPairAccCols = 256;
 constexpr int kPairSmem = 1024 + kPairStages * kPairStageBytes + kSlab * kSlabPitch * 4 + 512;
 static_assert(kPairSmem <= 232448, "pair GEMM shared memory");
+constexpr int kPairMaxSplits = 8;    // k-ranges per tile of the last wave, at most
+constexpr int kPairMinSplitKb = 8;   // k-blocks per k-range, at least
+constexpr int kPairPartFloats = kPairTN * BM;  // one CTA's fp32 partial of a tile
+
+// Unit u of a pair launch: tile, k-block range, and its index among the
+// tile's k-ranges (-1: the whole tile). The k-range units come first (units
+// [0, (tiles - pw) * ps) over the tiles [pw, tiles)): each is the first unit
+// of its cluster, which makes the units of a tile co-resident, and their
+// sums overlap the MMA of the cluster's next, whole tile (units from
+// (tiles - pw) * ps on: tiles [0, pw)).
+struct PairUnit {
+  int tile, k0, k1, split;
+};
+__device__ __forceinline__ PairUnit pair_unit(const Params &p, int u, int kb, int tiles) {
+  if (p.ps <= 1) return {u, 0, kb, -1};
+  const int nsplit = (tiles - p.pw) * p.ps;
+  if (u >= nsplit) return {u - nsplit, 0, kb, -1};
+  const int s = u % p.ps;
+  return {p.pw + u / p.ps, s * kb / p.ps, (s + 1) * kb / p.ps, s};
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -1283,6 +1312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int t_tiles = (a.T + kPairTN - 1) / kPairTN;
   const int tiles = (a.N / (2 * BM)) * t_tiles;
   const int kb = a.K / BK;
+  const int units = p.ps > 1 ? p.pw + (tiles - p.pw) * p.ps : tiles;
+  // optional %globaltimer trace [grid][4]: entry, a k-range unit's tile
+  // complete (all k-ranges arrived), its slice summed, exit
+  if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4] = ptx::globaltimer_ns();
   auto on_even = [](uint64_t *b) { return ptx::mapa_shared(ptx::smem_u32(b), 0); };
   auto on_odd = [](uint64_t *b) { return ptx::mapa_shared(ptx::smem_u32(b), 1); };
 
@@ -1319,9 +1352,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::pdl_wait();
       int i = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < tiles; tile += npairs) {
-        const int mt = tile / t_tiles, tt = tile % t_tiles;
-        for (int k = 0; k < kb; ++k, ++i) {
+      for (int u = pair; ok && u < units; u += npairs) {
+        const PairUnit pu = pair_unit(p, u, kb, tiles);
+        const int mt = pu.tile / t_tiles, tt = pu.tile % t_tiles;
+        for (int k = pu.k0; k < pu.k1; ++k, ++i) {
           const int s = i % kPairStages;
           if (!ptx::mbar_wait(&empty[s], ((i / kPairStages) & 1) ^ 1, kWaitBudgetNs)) {
             report_status(a.status, kStatusMmaTimeout);
@@ -1349,7 +1383,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = ptx::idesc_f16(2 * BM, kPairTN, /*bf16*/ 1, false, false);
       int i = 0, n = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < tiles; tile += npairs, ++n) {
+      for (int u = pair; ok && u < units; u += npairs, ++n) {
+        const PairUnit pu = pair_unit(p, u, kb, tiles);
         const int ab = n & 1;
         if (!ptx::mbar_wait(&acc_empty[ab], ((n >> 1) & 1) ^ 1, kWaitBudgetNs)) {
           report_status(a.status, kStatusEpilogueTimeout);
@@ -1357,7 +1392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_after();
         const uint32_t acc = tmem + ab * kPairAccCols;
-        for (int k = 0; k < kb; ++k, ++i) {
+        for (int k = pu.k0; k < pu.k1; ++k, ++i) {
           const int s = i % kPairStages;
           if (!ptx::mbar_wait(&full[s], (i / kPairStages) & 1, kWaitBudgetNs)) {
             report_status(a.status, kStatusTmaTimeout);
@@ -1370,7 +1405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t da = ptx::smem_desc(sm + kk * 32, 16, 1024, ptx::kLayoutSW128);
             const uint64_t db = ptx::smem_desc(sm + kPairHalf + kk * 32, 16, 1024, ptx::kLayoutSW128);
-            ptx::mma_f16_ss_pair(acc, da, db, idesc, (k > 0 || kk > 0) ? 1u : 0u);
+            ptx::mma_f16_ss_pair(acc, da, db, idesc, (k > pu.k0 || kk > 0) ? 1u : 0u);
           }
           ptx::mma_commit_pair(on_even(&empty[s]));  // both CTAs' stage s may refill
           ptx::mma_commit_pair(on_odd(&empty[s]));
@@ -1387,35 +1422,132 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tj = et / 8, part = et % 8;
     ptx::pdl_wait();
     int n = 0;
-    for (int tile = pair; tile < tiles; tile += npairs, ++n) {
+    for (int u = pair; u < units; u += npairs, ++n) {
+      const PairUnit pu = pair_unit(p, u, kb, tiles);
       const int ab = n & 1;
       const bool waited = ptx::mbar_wait(&acc_full[ab], (n >> 1) & 1, kWaitBudgetNs);
       if (!waited) report_status(a.status, kStatusEpilogueTimeout);
       ptx::tc_fence_after();
-      const int mt = tile / t_tiles, tt = tile % t_tiles;
+      const int mt = pu.tile / t_tiles, tt = pu.tile % t_tiles;
       const int nt = mt * 2 + (int)rank;  // this CTA's 128-row weight tile
       const int t0 = tt * kPairTN;
-      for (int ch = 0; ch < kPairTN / kSlab; ++ch) {
-        if (t0 + ch * kSlab >= a.T) break;  // uniform across the CTA
-        uint32_t r[16];
-        ptx::tmem_ld16(tmem + ab * kPairAccCols + ((uint32_t)(q * 32) << 16) + ch * kSlab, r);
-        ptx::tmem_ld_wait();
-        if (!waited) {
+      const int nch = min(kPairTN, a.T - t0 + kSlab - 1) / kSlab;  // slabs holding tokens
+      const uint32_t acc_lane = tmem + ab * kPairAccCols + ((uint32_t)(q * 32) << 16);
+      if (pu.split < 0) {
+        for (int ch = 0; ch < nch; ++ch) {
+          uint32_t r[16];
+          ptx::tmem_ld16(acc_lane + ch * kSlab, r);
+          ptx::tmem_ld_wait();
+          if (!waited) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = 0u;
+            for (int j = 0; j < 16; ++j) r[j] = 0u;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) slab[j * kSlabPitch + row] = __uint_as_float(r[j]);
+          named_bar(1, kEpiThreads);
+          const int t = t0 + ch * kSlab + tj;
+          if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part);
+          named_bar(1, kEpiThreads);
         }
+        ptx::tc_fence_before();
+        if (rank == 0)
+          ptx::mbar_arrive(&acc_empty[ab]);
+        else
+          ptx::mbar_arrive_cluster(on_even(&acc_empty[ab]));
+      } else {
+        // k-range unit: this CTA's partial to its workspace slot as
+        // [slab][4][row] float4 (4 tokens of a row per vector; a warp's
+        // vectors are 512 contiguous bytes), then the accumulator is
+        // released at once
+        const int first = (pu.tile - p.pw) * p.ps;  // slot of the tile's k-range 0
+        float4 *mine = reinterpret_cast<float4 *>(a.ws + ((size_t)(first + pu.split) * 2 + rank) * kPairPartFloats);
+        for (int ch = 0; ch < nch; ++ch) {
+          uint32_t r[16];
+          ptx::tmem_ld16(acc_lane + ch * kSlab, r);
+          ptx::tmem_ld_wait();
+          if (!waited) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) slab[j * kSlabPitch + row] = __uint_as_float(r[j]);
+            for (int j = 0; j < 16; ++j) r[j] = 0u;
+          }
+#pragma unroll
+          for (int j4 = 0; j4 < 4; ++j4)
+            __stcg(mine + (ch * 4 + j4) * BM + row,
+                   make_float4(__uint_as_float(r[4 * j4]), __uint_as_float(r[4 * j4 + 1]),
+                               __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3])));
+        }
+        ptx::tc_fence_before();
+        if (rank == 0)
+          ptx::mbar_arrive(&acc_empty[ab]);
+        else
+          ptx::mbar_arrive_cluster(on_even(&acc_empty[ab]));
+        __threadfence();  // the partial is visible before the arrival is counted
         named_bar(1, kEpiThreads);
-        const int t = t0 + ch * kSlab + tj;
-        if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part);
+        // [arrivals, departures] of this CTA's half of the tile
+        uint32_t *cnt = a.counters + ((pu.tile - p.pw) * 2 + rank) * 2;
+        if (et == 0) {
+          // the tile's k-range units are the first units of their clusters
+          // and the grid fits the GPU, so they all run at once: wait (bounded)
+          // until every one has written its partial
+          ptx::red_add_release_gpu(cnt, 1u);
+          bool ok = ptx::ld_acquire_gpu(cnt) >= (uint32_t)p.ps;
+          if (!ok) {
+            const uint64_t start = ptx::globaltimer_ns();
+            while (!ok) {
+              for (int i = 0; i < 64 && !ok; ++i) ok = ptx::ld_acquire_gpu(cnt) >= (uint32_t)p.ps;
+              if (!ok && ptx::globaltimer_ns() - start > kWaitBudgetNs) break;
+            }
+            if (!ok) report_status(a.status, kStatusEpilogueTimeout);
+          }
+          if (a.trace) a.trace[blockIdx.x * 4 + 1] = ptx::globaltimer_ns();
+        }
         named_bar(1, kEpiThreads);
+        __threadfence();
+        // this unit sums slabs [c0, c1) of the tile over every k-range, in
+        // split order (the same sum whichever unit does it), and runs the
+        // epilogue on them
+        const float4 *slot0 = reinterpret_cast<const float4 *>(a.ws + ((size_t)first * 2 + rank) * kPairPartFloats);
+        constexpr size_t kSlotStride = 2 * (size_t)kPairPartFloats / 4;  // float4s from k-range s to s + 1
+        const int c0 = pu.split * nch / p.ps, c1 = (pu.split + 1) * nch / p.ps;
+        for (int ch = c0; ch < c1; ++ch) {
+          // every k-range's four vectors in one round of independent loads
+          float4 pv[kPairMaxSplits][4];
+#pragma unroll
+          for (int s2 = 0; s2 < kPairMaxSplits; ++s2)
+#pragma unroll
+            for (int j4 = 0; j4 < 4; ++j4)
+              pv[s2][j4] = s2 < p.ps ? __ldcg(slot0 + s2 * kSlotStride + (ch * 4 + j4) * BM + row)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int j4 = 0; j4 < 4; ++j4) {
+            float4 acc = pv[0][j4];
+#pragma unroll
+            for (int s2 = 1; s2 < kPairMaxSplits; ++s2) {
+              if (s2 < p.ps) {
+                acc.x += pv[s2][j4].x;
+                acc.y += pv[s2][j4].y;
+                acc.z += pv[s2][j4].z;
+                acc.w += pv[s2][j4].w;
+              }
+            }
+            slab[(4 * j4 + 0) * kSlabPitch + row] = acc.x;
+            slab[(4 * j4 + 1) * kSlabPitch + row] = acc.y;
+            slab[(4 * j4 + 2) * kSlabPitch + row] = acc.z;
+            slab[(4 * j4 + 3) * kSlabPitch + row] = acc.w;
+          }
+          named_bar(1, kEpiThreads);
+          const int t = t0 + ch * kSlab + tj;
+          if (t < a.T) write_row<EPI>(a, nt, t, slab + tj * kSlabPitch, part);
+          named_bar(1, kEpiThreads);
+        }
+        if (et == 0) {
+          // the last unit to finish its sum zeroes both counters for the next call
+          if (atomicAdd(cnt + 1, 1u) == (uint32_t)(p.ps - 1)) {
+            cnt[0] = 0u;
+            cnt[1] = 0u;
+          }
+          if (a.trace) a.trace[blockIdx.x * 4 + 2] = ptx::globaltimer_ns();
+        }
       }
-      ptx::tc_fence_before();
-      if (rank == 0)
-        ptx::mbar_arrive(&acc_empty[ab]);
-      else
-        ptx::mbar_arrive_cluster(on_even(&acc_empty[ab]));
     }
   }
 
@@ -1425,6 +1557,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::cluster_sync_all();  // the pair's MMAs, reads of TMEM and remote arrivals are done
   ptx::tc_fence_after();
   if (warp == 0) ptx::tmem_dealloc_pair(tmem, 2 * kPairAccCols);
+  if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 4 + 3] = ptx::globaltimer_ns();
 }
 
 // Clusters of two pair-GEMM CTAs that fit on the GPU at once.
@@ -1454,39 +1587,68 @@ static int pair_capacity() {
   return n;
 }
 
-// Clusters for a pair-GEMM launch of this call, or 0 for the single-CTA
-// schedules. Taken for default-grid store / SwiGLU / RoPE+KV calls with
-// N % 256 == 0 and T >= 256 whose 256 x 256 tiles keep at least 30 % of the
-// resident clusters busy over their waves (the kernel does not split K).
-// Measured on B200 (us, pair vs single-CTA stream-K): T = 1536: gate_up 232
-// vs 349, qkv 56 vs 91, o_proj 54 vs 73 and down_proj 151 vs 205 (65 % of
-// the clusters busy), lm_head 1007 vs 1441; T = 512: every shape faster
-// (o_proj 35 vs 44 with 43 % busy); T = 256: qkv 35 vs 49 (32 % busy),
-// gate_up 76 vs 102, but o_proj 33 vs 29 and down_proj 80 vs 62 (16 tiles,
-// 22 % busy) stay single-CTA. SCHED_GEMM_PAIR=0 turns it off; =1 takes it
-// for every eligible shape.
+// The pair-GEMM launch of a call: clusters, whole tiles and k-ranges per
+// tile of the last wave (np = 0: the single-CTA schedules). Taken for
+// default-grid store / SwiGLU / RoPE+KV calls with N % 256 == 0 and
+// T >= 256 whose 256 x 256 tiles keep at least 30 % of the resident clusters
+// busy. The tiles of a last, partly filled wave are split into k-ranges
+// (at most 8, each at least 8 k-blocks) so that the wave fills the
+// clusters, when the workspace and counters hold their partials.
+// Measured on B200 (us, L2 flushed; pair with k-ranges / pair with whole
+// tiles / single-CTA stream-K / cuBLAS): T = 1536: o_proj 45 / 54 / 73 / 41,
+// down_proj 121 / 151 / 205 / 117, gate_up 225 / 232 / 349 / 230;
+// T = 512: down_proj 63 / 82 / 101; T = 256: o_proj 27 / 33 / 29,
+// down_proj 47 / 80 / 62. SCHED_GEMM_PAIR=0 turns the kernel off, =1 takes
+// it for every eligible shape; SCHED_GEMM_PAIR_SPLIT=0 keeps every tile
+// whole.
+struct PairPlan {
+  int np = 0, whole = 0, splits = 1;
+};
+
 template <int EPI>
-static int pair_plan_epi(const GemmArgs &a) {
+static PairPlan pair_plan_epi(const GemmArgs &a) {
   const char *v = std::getenv("SCHED_GEMM_PAIR");
   const int mode = v ? std::atoi(v) : -1;
-  if (mode == 0) return 0;
-  if (a.grid > 0 || a.norm_w != nullptr || a.x_ready != nullptr || a.N % (2 * BM) != 0 || a.K % BK != 0) return 0;
-  if (a.T < (mode == 1 ? 1 : 256)) return 0;
+  const char *vs = std::getenv("SCHED_GEMM_PAIR_SPLIT");
+  const bool may_split = !(vs && std::atoi(vs) == 0);
+  PairPlan none;
+  if (mode == 0) return none;
+  if (a.grid > 0 || a.norm_w != nullptr || a.x_ready != nullptr || a.N % (2 * BM) != 0 || a.K % BK != 0) return none;
+  if (a.T < (mode == 1 ? 1 : 256)) return none;
   const long long tiles = (long long)(a.N / (2 * BM)) * ((a.T + kPairTN - 1) / kPairTN);
   const int cap = pair_capacity<EPI>();
-  if (cap <= 0) return 0;
-  const int np = (int)std::min<long long>(cap, tiles);
-  const long long waves = (tiles + cap - 1) / cap;
-  const double busy = (double)tiles / (double)(waves * cap);  // resident clusters kept busy
-  return (mode == 1 || busy >= 0.3) ? np : 0;
+  if (cap <= 0) return none;
+  const long long full = tiles / cap, rem = tiles % cap;
+  const int kb = a.K / BK;
+  int S = 1;
+  if (may_split && rem > 0) {
+    S = (int)std::min<long long>(std::min<long long>(cap / rem, kb / kPairMinSplitKb), kPairMaxSplits);
+    const long long need = rem * S * 2 * (long long)kPairPartFloats;
+    if (S < 2 || a.ws == nullptr || a.counters == nullptr || need > a.ws_floats || 4 * rem > a.counter_count)
+      S = 1;
+  }
+  PairPlan pl;
+  double waves;  // in whole-tile times
+  if (S > 1) {
+    pl.whole = (int)(full * cap);
+    pl.splits = S;
+    pl.np = full > 0 ? cap : (int)(rem * S);
+    waves = (double)full + 1.0 / S;
+  } else {
+    pl.whole = (int)tiles;
+    pl.np = (int)std::min<long long>(cap, tiles);
+    waves = (double)((tiles + cap - 1) / cap);
+  }
+  const double busy = (double)tiles / (waves * cap);  // resident clusters kept busy
+  return (mode == 1 || busy >= 0.3) ? pl : none;
 }
 
-static int pair_plan(const GemmArgs &a) {
+static PairPlan pair_plan(const GemmArgs &a) {
   switch (a.epi) {
     case kEpiStore: return pair_plan_epi<kEpiStore>(a);
     case kEpiSwiGLU: return pair_plan_epi<kEpiSwiGLU>(a);
     case kEpiRopeKV: return pair_plan_epi<kEpiRopeKV>(a);
-    default: return 0;
+    default: return PairPlan{};
   }
 }
 
@@ -1781,6 +1943,29 @@ extern "C" void sched_gemm_plan(int T, int N, int K, int epi, int num_sms, int *
   *grid = p.grid;
 }
 
+// The CTA-pair launch sched_gemm_run would make for a default-grid call of
+// this shape with a workspace of ws_floats floats and `counters` counters:
+// clusters (0: a single-CTA schedule), whole tiles and k-ranges per tile of
+// the last wave (1: none). Queries the device's cluster capacity.
+extern "C" void sched_gemm_pair_plan(int T, int N, int K, int epi, long long ws_floats, int counters, int *np,
+                                     int *whole, int *splits) {
+  GemmArgs a{};
+  a.T = T;
+  a.N = N;
+  a.K = K;
+  a.epi = epi;
+  static float dummy_ws;
+  static uint32_t dummy_cnt;
+  a.ws = ws_floats > 0 ? &dummy_ws : nullptr;
+  a.ws_floats = ws_floats;
+  a.counters = counters > 0 ? &dummy_cnt : nullptr;
+  a.counter_count = counters;
+  const gemm::PairPlan pl = gemm::pair_plan(a);
+  *np = pl.np;
+  *whole = pl.whole;
+  *splits = pl.splits;
+}
+
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   const GemmArgs &a = *args;
   if (a.T <= 0) return 0;
@@ -1817,10 +2002,13 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   try {
     CUtensorMap tw = tmap::make_2d(a.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.K,
                                    gemm::BM, gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (const int np = gemm::pair_plan(a); np > 0) {
+    if (const gemm::PairPlan pl = gemm::pair_plan(a); pl.np > 0) {
       // CTA pairs: each CTA stages 128 of a tile's 256 tokens
       CUtensorMap tx2 = tmap::make_2d(a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.K, a.ldx, gemm::BM,
                                       gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
+      p.pw = pl.whole;
+      p.ps = pl.splits;
+      const int np = pl.np;
       if (a.epi == kEpiSwiGLU)
         gemm::launch_pair<kEpiSwiGLU>(tw, tx2, p, np, stream);
       else if (a.epi == kEpiRopeKV)

@@ -102,6 +102,10 @@ struct GemmArgs {
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream);
 // Schedule of a default-grid call: cluster size (0 = stream-K) and grid.
 extern "C" void sched_gemm_plan(int T, int N, int K, int epi, int num_sms, int *cs, int *grid);
+// The CTA-pair launch of a default-grid call: clusters (0: none), whole
+// tiles, k-ranges per tile of the last wave.
+extern "C" void sched_gemm_pair_plan(int T, int N, int K, int epi, long long ws_floats, int counters, int *np,
+                                     int *whole, int *splits);
 extern "C" long long sched_gemm_ws_floats(int T, int N, int K, int grid);
 
 // ---------------------------------------------------------------------------

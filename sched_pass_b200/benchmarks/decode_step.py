@@ -32,12 +32,15 @@ def main():
     ap.add_argument("--levers", type=int, default=1)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=0)
+    ap.add_argument("--target-tasks", type=int, default=0,
+                    help="decode-attention tasks to aim for when splitting KV (0: one per SM)")
     args = ap.parse_args()
     cfg = get_config(args.model)
     new_tokens = args.steps + args.profile_steps + 8
     ecfg = EngineConfig(max_batch=max(args.batch, 8), max_prefill_tokens=4096,
                         max_context=(args.context + new_tokens + 127) // 128 * 128,
-                        cuda_graphs=not args.no_graphs, levers=bool(args.levers), acquire=args.acquire)
+                        cuda_graphs=not args.no_graphs, levers=bool(args.levers), acquire=args.acquire,
+                        target_tasks=args.target_tasks)
     eng = Engine(cfg, ecfg, "cuda")
     rng = np.random.default_rng(0)
     for i in range(args.batch):
@@ -66,7 +69,8 @@ def main():
     wbytes = sum(t.numel() * t.element_size() for t in
                  [eng.model.w.lm_head] + [x for lw in eng.model.w.layers for x in (lw.qkv, lw.o, lw.gate_up, lw.down)])
     kvbytes = args.batch * (args.context + 8) * cfg.kv_bytes_per_token()
-    print(json.dumps({"batch": args.batch, "context": args.context, "step_ms_p50": round(med, 4),
+    print(json.dumps({"batch": args.batch, "context": args.context, "splits": eng.splits_for(args.batch),
+                      "step_ms_p50": round(med, 4),
                       "step_ms_min": round(min(ms), 4), "tok_s": round(args.batch / med * 1e3, 1),
                       "weights_GB": round(wbytes / 1e9, 2), "kv_GB": round(kvbytes / 1e9, 3),
                       "effective_GBps": round((wbytes + kvbytes) / med / 1e6, 1),

@@ -127,6 +127,36 @@ def test_gemm_cta_pair_matches_fp32(T, N, K, swiglu, monkeypatch):
     assert rel_err(ops.linear(x, w, swiglu=swiglu), want) < 1e-2
 
 
+@pytest.mark.parametrize("T,N,K,swiglu", [
+    (1536, 4096, 4096, False), (256, 4096, 14336, False), (512, 4096, 4096, True),
+])
+def test_gemm_cta_pair_k_ranges(T, N, K, swiglu, monkeypatch):
+    """The CTA-pair GEMM with the tiles of its last, partly filled wave split
+    into k-ranges (fp32 partials in the workspace; once all have arrived,
+    each k-range unit sums a slice of the tile in split order), on the
+    automatic plan: against fp32, bit-identical over repeated calls (arrival
+    order does not matter), and close to the same kernel with every tile
+    whole."""
+    from sched_pass_b200._ext import ext
+    monkeypatch.delenv("SCHED_GEMM_PAIR", raising=False)
+    monkeypatch.delenv("SCHED_GEMM_PAIR_SPLIT", raising=False)
+    ws = ops.workspace(DEV)
+    np_, whole, splits = ext().gemm_pair_plan(T, N, K, 1 if swiglu else 0, ws.ws.numel(), ws.counters.numel())
+    assert np_ > 0 and splits > 1, (np_, whole, splits)
+    g = torch.Generator(device=DEV).manual_seed(T + K)
+    x = torch.randn(T, K, device=DEV, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    got = ops.linear(x, w, swiglu=swiglu)
+    again = ops.linear(x, w, swiglu=swiglu)
+    torch.cuda.synchronize()
+    want = ref.swiglu_linear(x, w) if swiglu else ref.linear(x, w)
+    assert rel_err(got, want) < 1e-2
+    assert torch.equal(got, again)
+    monkeypatch.setenv("SCHED_GEMM_PAIR_SPLIT", "0")
+    assert ext().gemm_pair_plan(T, N, K, 1 if swiglu else 0, ws.ws.numel(), ws.counters.numel())[2] == 1
+    assert rel_err(ops.linear(x, w, swiglu=swiglu), got) < 1e-2
+
+
 def test_gemm_cta_pair_qkv_rope(monkeypatch):
     """The RoPE + KV-append epilogue on the CTA-pair schedule: rotated
     queries against fp32, and queries, keys and values (written into their
