@@ -8,6 +8,8 @@ Modes (one task = one (request, KV head); no KV splitting, so long requests
 are stragglers and scheduling matters):
   stock    unwoven kernel, identity order
   woven    levers compiled in, tables neutral (bit-exact with stock)
+  unarmed  levers compiled in, no tables bound (what the woven code costs
+           without any table read)
   pi       LPT order (grouped, block 16)
   policy   urgency rows + hints (urgent tasks prefetch / evict_last)
   timer    per-task timer on
@@ -21,7 +23,8 @@ are stragglers and scheduling matters):
            layout; run as a library only, its output checked against stock
 Each mode: median device time over iterations with an L2 flush between them,
 achieved KV bandwidth vs the measured HBM peak, and bit-exactness vs stock
-for the permutation-only modes.
+for the permutation-only modes. ``--trace`` adds each mode's per-CTA phase
+trace of one launch (after an L2 flush).
 """
 from __future__ import annotations
 
@@ -91,6 +94,7 @@ def main():
     ap.add_argument("--requests", type=int, default=256)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--modes", default="stock,woven,pi,policy,timer,shed,ticket,clc,split,flashinfer")
+    ap.add_argument("--trace", action="store_true", help="per-CTA phase trace of one launch per mode")
     args = ap.parse_args()
     Hq, Hkv = 32, 8
     lens, bt, kc, vc, q, urg = build(args.requests, Hq, Hkv)
@@ -134,6 +138,8 @@ def main():
             fn = lambda: run(False)
         elif mode == "woven":
             fn = lambda: run(True)
+        elif mode == "unarmed":
+            fn = lambda: run(True, slots=False)
         elif mode == "pi":
             plane.install_order(torch.from_numpy(native.grouped_lpt(cost, 16)), n_tasks)
             plane.push()
@@ -195,8 +201,12 @@ def main():
                                                   stock_out.float().norm()), 5)
         if mode == "stock":
             stock_out = out.clone()
-        elif mode in ("woven", "pi", "timer", "ticket", "clc", "policy") and stock_out is not None:
+        elif mode in ("woven", "unarmed", "pi", "timer", "ticket", "clc", "policy") and stock_out is not None:
             rec["bit_exact_vs_stock"] = bool(torch.equal(out, stock_out))
+        if args.trace and mode not in ("split", "flashinfer"):
+            from .kernel_cases import decode_trace
+            flush()
+            rec["phases"] = decode_trace(fn, R if mode == "ticket" else n_tasks)
         if mode == "timer":
             cyc = plane.read_timer()[:n_tasks].double()
             rec["timer_rows_filled"] = int((cyc > 0).sum())
