@@ -260,7 +260,7 @@ void gemm_allreduce(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int
                     const c10::optional<at::Tensor> &ll_state, int64_t ll_set_lines,
                     const c10::optional<at::Tensor> &norm_res, const c10::optional<at::Tensor> &norm_w,
                     const c10::optional<at::Tensor> &norm_out, const c10::optional<at::Tensor> &row_cnt,
-                    double norm_eps) {
+                    double norm_eps, int64_t ll_mc) {
   GemmArgs a = base_args(x, w, grid, ws, counters, status);
   check_bf16(y, "y");
   TORCH_CHECK(y.dim() == 2 && y.stride(1) == 1 && y.size(1) >= a.N, "y [T, >= N]");
@@ -285,6 +285,7 @@ void gemm_allreduce(const at::Tensor &x, const at::Tensor &w, at::Tensor &y, int
   if (ll) {
     a.ll_state = reinterpret_cast<uint32_t *>(ll_state->data_ptr<int32_t>());
     a.ll_set_lines = ll_set_lines;
+    a.ll_mc = reinterpret_cast<void *>(ll_mc);
   }
   set_norm(a, norm_res, norm_w, norm_out, row_cnt, norm_eps);
   int rc_ = 0;

@@ -153,6 +153,15 @@ __device__ __forceinline__ void st_ll(uint4 *dst, uint32_t d0, uint32_t d1, uint
                : "memory");
 }
 
+// The same line through the multicast mapping: two 8-byte integer multimem
+// stores, one per half {payload, epoch}; the switch writes every rank's copy.
+__device__ __forceinline__ void st_ll_mc(uint4 *dst, uint32_t d0, uint32_t d1, uint32_t e) {
+  const uint64_t h0 = ((uint64_t)e << 32) | d0, h1 = ((uint64_t)e << 32) | d1;
+  asm volatile("multimem.st.relaxed.sys.global.b64 [%0], %1;" ::"l"(dst), "l"(h0) : "memory");
+  asm volatile("multimem.st.relaxed.sys.global.b64 [%0], %1;" ::"l"(reinterpret_cast<uint8_t *>(dst) + 8), "l"(h1)
+               : "memory");
+}
+
 template <int EPI>
 __device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, const float *v,
                                           int k, uint32_t ll_e = 0) {
@@ -198,12 +207,20 @@ __device__ __forceinline__ void write_row(const GemmArgs &a, int n_tile, int t, 
     if (EPI == kEpiAllReduce && a.ll_state != nullptr) {
       // low-latency lines into every rank's buffer (set of this call's epoch)
       const size_t line = (size_t)(ll_e & 1u) * a.ll_set_lines + off / 4;
-      for (int j = 0; j < a.world; ++j) {
-        uint4 *dst = reinterpret_cast<uint4 *>(a.recv[j]) + line;
-        st_ll(dst, o0.x, o0.y, ll_e);
-        st_ll(dst + 1, o0.z, o0.w, ll_e);
-        st_ll(dst + 2, o1.x, o1.y, ll_e);
-        st_ll(dst + 3, o1.z, o1.w, ll_e);
+      if (a.ll_mc != nullptr) {
+        uint4 *dst = reinterpret_cast<uint4 *>(a.ll_mc) + line;
+        st_ll_mc(dst, o0.x, o0.y, ll_e);
+        st_ll_mc(dst + 1, o0.z, o0.w, ll_e);
+        st_ll_mc(dst + 2, o1.x, o1.y, ll_e);
+        st_ll_mc(dst + 3, o1.z, o1.w, ll_e);
+      } else {
+        for (int j = 0; j < a.world; ++j) {
+          uint4 *dst = reinterpret_cast<uint4 *>(a.recv[j]) + line;
+          st_ll(dst, o0.x, o0.y, ll_e);
+          st_ll(dst + 1, o0.z, o0.w, ll_e);
+          st_ll(dst + 2, o1.x, o1.y, ll_e);
+          st_ll(dst + 3, o1.z, o1.w, ll_e);
+        }
       }
     } else if (EPI == kEpiAllReduce) {
       for (int j = 0; j < a.world; ++j) {  // NVLink stores into every rank's slab
@@ -1998,6 +2015,7 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
     }
     // the low-latency line buffer holds [world][T][N / 4] lines per set
     if (ll && a.ll_set_lines < (long long)a.world * a.T * (a.N / 4)) return -7;
+    if (a.ll_mc != nullptr && (!ll || (reinterpret_cast<uintptr_t>(a.ll_mc) & 15) != 0)) return -7;
   }
   try {
     CUtensorMap tw = tmap::make_2d(a.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.K,

@@ -97,6 +97,12 @@ struct GemmArgs {
   __nv_bfloat16 *norm_out;
   uint32_t *row_cnt;
   float norm_eps;
+  // Low-latency exchange through NVLink multicast (NVLS; nullptr: off): this
+  // rank's address of the multicast mapping of the line buffers, whose
+  // local copy is recv[rank]. A line is then written once, as two 8-byte
+  // multimem stores {bf16x2, epoch}, and the switch delivers it to every
+  // rank's copy, instead of one store per rank.
+  void *ll_mc;
 };
 
 extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream);

@@ -23,6 +23,12 @@ call) and also picks which of two line-buffer sets a call uses, so graphs
 replay it without host bookkeeping. The rank-order fp32 sum is the same as
 the flag path's, bit for bit. The lines double the bytes on NVLink, which is
 why larger calls keep the flag path.
+
+With ``SCHED_TP_NVLS=1`` the line buffers come from torch's symmetric memory
+with an NVLink multicast mapping: the epilogue writes each line once, as two
+8-byte ``multimem`` stores, and the switch delivers it to every rank, instead
+of one store per rank. Where the group has no multicast the IPC buffers are
+used as before.
 """
 from __future__ import annotations
 
@@ -32,7 +38,7 @@ import torch
 
 from .. import ops
 from .._ext import ext
-from .symm import SymmetricBuffer
+from .symm import MulticastBuffer, SymmetricBuffer
 
 FLAG_TILES = 1 << 15  # u32 flags per source rank (covers N/128 x token tiles)
 
@@ -55,9 +61,20 @@ class FusedAllReduce:
         self.ll_max_tokens = int(os.environ.get("SCHED_TP_LL_MAX", "32"))
         self.ll_calls = 0
         self._ll_last = False
+        self.ll_mc = 0
         if self.ll_max_tokens > 0:
             self.ll_set_lines = self.world * self.ll_max_tokens * max_n // 4
-            self.ll = SymmetricBuffer(2 * self.ll_set_lines * 16, group)
+            nbytes = 2 * self.ll_set_lines * 16
+            self.ll = None
+            if os.environ.get("SCHED_TP_NVLS", "0") == "1" and self.world > 1:
+                try:
+                    self.ll = MulticastBuffer(nbytes, group, self.device)
+                    self.ll_mc = self.ll.mc
+                except Exception as e:  # every rank takes the same branch: rendezvous is collective
+                    print(f"[sched] NVLS line buffers unavailable ({e}); using peer stores", flush=True)
+                    self.ll = None
+            if self.ll is None:
+                self.ll = SymmetricBuffer(nbytes, group)
             self.ll_state = torch.zeros(2, dtype=torch.int32, device=self.device)  # epoch, done
         else:
             self.ll = None
@@ -81,13 +98,13 @@ class FusedAllReduce:
             self.ll_calls += 1
             self._ll_last = True
             ext().gemm_allreduce(x, w, out, self.rank, self.world, self.ll.ptrs, [], 0, ws.ws, ws.counters,
-                                 ops.status_buffer(x.device), self.ll_state, self.ll_set_lines, *nargs)
+                                 ops.status_buffer(x.device), self.ll_state, self.ll_set_lines, *nargs, self.ll_mc)
             return out
         self._ll_last = False
         slab, flags = self.sets[self.k]
         self.k ^= 1
         ext().gemm_allreduce(x, w, out, self.rank, self.world, slab.ptrs, flags.ptrs, 0, ws.ws,
-                             ws.counters, ops.status_buffer(x.device), None, 0, *nargs)
+                             ws.counters, ops.status_buffer(x.device), None, 0, *nargs, 0)
         return out
 
     def last_slab(self, T: int, N: int) -> torch.Tensor:

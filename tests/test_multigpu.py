@@ -81,3 +81,21 @@ def test_sequence_parallel_matches_fused_allreduce():
         assert c["delta_bits"] and c["residual_bits"] and c["normed_bits"], c
         assert c["gated_gemm_bits"] and c["identical_on_ranks"], c
     assert res["engine_identical"], res
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+def test_nvls_line_exchange_matches_peer_stores():
+    """Decode-sized fused GEMM + all-reduce with NVLink multicast line
+    buffers (one multimem store per line) gives the same bits as the
+    per-peer-store exchange; records each one's per-call time."""
+    n = 2 if _ngpus() < 4 else min(_ngpus(), 8)
+    r = run_torchrun("nvls_worker.py", n)
+    line = [l for l in r.stdout.splitlines() if l.startswith("NVLSJSON ")]
+    assert r.returncode == 0 and line, _why(r)
+    res = json.loads(line[0][len("NVLSJSON "):])
+    assert not res["errors"], res
+    if not res["multicast"]:
+        pytest.skip("no NVLink multicast on these GPUs")
+    for c in res["checks"]:
+        assert c["bit_exact"], c
+        assert c["rel_err"] < 1e-2, c

@@ -45,6 +45,9 @@ class GemmArgs(ctypes.Structure):
         ("trace", ctypes.c_void_p), ("kv_pages", ctypes.c_int),
         ("x_ready", ctypes.c_void_p),
         ("ll_state", ctypes.c_void_p), ("ll_set_lines", ctypes.c_longlong),
+        ("norm_res", ctypes.c_void_p), ("norm_w", ctypes.c_void_p), ("norm_out", ctypes.c_void_p),
+        ("row_cnt", ctypes.c_void_p), ("norm_eps", ctypes.c_float),
+        ("ll_mc", ctypes.c_void_p),
     ]
 
 
