@@ -1991,10 +1991,13 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   int tn;
   p.a = a;
   gemm::final_plan(a, p, tn);
+  // the CTA-pair kernel sizes its k-ranges to the scratch it is given; the
+  // stream-K scratch check applies to the single-CTA schedules only
+  const gemm::PairPlan pl = gemm::pair_plan(a);
   long long need_floats;
   int need_counters;
   gemm::scratch_need(p, tn, need_floats, need_counters);
-  if (need_counters > 0) {
+  if (pl.np == 0 && need_counters > 0) {
     if (a.ws == nullptr || a.counters == nullptr) return -2;
     if (need_floats > a.ws_floats || need_counters > a.counter_count) return -5;
   }
@@ -2020,7 +2023,7 @@ extern "C" int sched_gemm_run(const GemmArgs *args, cudaStream_t stream) {
   try {
     CUtensorMap tw = tmap::make_2d(a.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.N, a.K, a.K,
                                    gemm::BM, gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (const gemm::PairPlan pl = gemm::pair_plan(a); pl.np > 0) {
+    if (pl.np > 0) {
       // CTA pairs: each CTA stages 128 of a tile's 256 tokens
       CUtensorMap tx2 = tmap::make_2d(a.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.T, a.K, a.ldx, gemm::BM,
                                       gemm::BK, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -2096,21 +2099,24 @@ extern "C" int sched_gemm_run_fixed_scratch(const GemmArgs *args, cudaStream_t s
   GemmArgs a = *args;
   if (a.T <= 0) return 0;
   if (a.N % gemm::BM != 0 || a.K % gemm::BK != 0) return -1;
-  // the capacity check runs on the schedule sched_gemm_run will launch
-  // (cluster split-K for some default-grid calls, which needs no scratch)
-  gemm::Params p;
-  int tn;
-  gemm::final_plan(a, p, tn);
-  long long need_floats;
-  int need_counters;
-  gemm::scratch_need(p, tn, need_floats, need_counters);
-  if (need_floats > kFixedScratchWsFloats || need_counters > kFixedScratchCounters) return kFixedScratchTooLarge;
   gemm::FixedScratch s;
   if (!gemm::fixed_scratch(s)) return kFixedScratchLookupFailed;
   a.ws = s.ws;
   a.ws_floats = kFixedScratchWsFloats;
   a.counters = s.counters;
   a.counter_count = kFixedScratchCounters;
+  // the capacity check runs on the schedule sched_gemm_run will launch: the
+  // CTA-pair kernel sizes its k-ranges to this scratch, cluster split-K
+  // needs none, stream-K needs its partial slices and tile counters
+  if (gemm::pair_plan(a).np == 0) {
+    gemm::Params p;
+    int tn;
+    gemm::final_plan(a, p, tn);
+    long long need_floats;
+    int need_counters;
+    gemm::scratch_need(p, tn, need_floats, need_counters);
+    if (need_floats > kFixedScratchWsFloats || need_counters > kFixedScratchCounters) return kFixedScratchTooLarge;
+  }
   return sched_gemm_run(&a, stream);
 }
 

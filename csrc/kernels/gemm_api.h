@@ -141,7 +141,10 @@ extern "C" long long sched_gemm_ws_floats(int T, int N, int K, int grid);
 //     need no initial value.
 //   * The capacity check runs on the schedule the call will launch: a
 //     default-grid call (grid <= 0) that runs cluster split-K uses no
-//     scratch and is never refused for size.
+//     scratch and is never refused for size, and one that runs the CTA-pair
+//     kernel (prefill sizes) splits its last wave into k-ranges only as far
+//     as their partials fit the fixed scratch (else it keeps tiles whole),
+//     so it is never refused for size either.
 //   * The scratch is one per device and shared by all calls on it: calls
 //     that can overlap in time (different streams, or host threads on
 //     unsynchronised streams) race on it and corrupt each other. Calls in

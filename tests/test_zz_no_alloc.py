@@ -144,3 +144,28 @@ def test_fixed_scratch_refuses_what_it_cannot_hold(lib):
     torch.cuda.synchronize()
     ops.check_status()
     assert torch.equal(ys, ops.linear(xs, ws, grid=148))
+
+
+def test_default_grid_pair_schedule_uses_the_fixed_scratch(lib, monkeypatch):
+    """A default-grid prefill-size call runs the CTA-pair kernel, whose last
+    wave's k-range partials fit the fixed scratch here (T=512: 32 tiles, 2
+    k-ranges each, exactly its capacity): not refused, and bit-identical to
+    the regular entry point, which plans the same schedule, on two calls in a
+    row (the second agrees only if the first left its counters at zero)."""
+    monkeypatch.delenv("SCHED_GEMM_PAIR", raising=False)
+    monkeypatch.delenv("SCHED_GEMM_PAIR_SPLIT", raising=False)
+    T, N, K = 512, 4096, 4096
+    np_, _, splits = ext().gemm_pair_plan(T, N, K, EPI_STORE, WS_CAP, 1 << 14)
+    if np_ == 0:
+        pytest.skip("the pair schedule is not planned for this shape on this GPU")
+    assert splits > 1
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(T, K, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    want = ops.linear(x, w)
+    for _ in range(2):
+        y = torch.full((T, N), float("nan"), dtype=torch.bfloat16, device="cuda")
+        assert call(lib, x, w, y, EPI_STORE, 0) == 0
+        torch.cuda.synchronize()
+        ops.check_status()
+        assert torch.equal(y, want)
