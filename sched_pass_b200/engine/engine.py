@@ -145,7 +145,9 @@ def summarize_steps(stats: list) -> dict:
             "device_ms_total": round(total, 3), "device_ms_mean": round(total / len(stats), 4),
             "decode_step_ms_p50": pct(dec, 0.5), "decode_step_ms_p99": pct(dec, 0.99),
             "decode_tokens": sum(s.n_decode for s in stats),
-            "prefill_tokens": sum(s.n_prefill_tokens for s in stats)}
+            "prefill_tokens": sum(s.n_prefill_tokens for s in stats),
+            # decode tokens per second of device time of these steps (this GPU, or the box under TP)
+            "decode_tok_s_device": round(sum(s.n_decode for s in stats) / (total / 1e3), 1) if total > 0 else None}
 
 
 class Engine:

@@ -29,13 +29,27 @@ steps while there is work, and completes finished requests. Endpoints:
 from __future__ import annotations
 
 import argparse
+import collections
 import concurrent.futures as cf
 import json
+import math
 import queue
 import threading
 import time
 
 import numpy as np
+
+
+def latency_summary(lat: list) -> dict:
+    """p50 / p99 of TPOT and TTFT (ms) over finished requests, given as
+    (tpot s or None, ttft s or None) pairs (nearest-rank percentiles)."""
+    def pct(v, q):
+        v = sorted(v)
+        return round(1e3 * v[min(len(v) - 1, max(0, math.ceil(q * len(v)) - 1))], 3) if v else None
+    tpot = [a for a, _ in lat if a is not None]
+    ttft = [b for _, b in lat if b is not None]
+    return {"finished": len(lat), "tpot_ms_p50": pct(tpot, 0.5), "tpot_ms_p99": pct(tpot, 0.99),
+            "ttft_ms_p50": pct(ttft, 0.5), "ttft_ms_p99": pct(ttft, 0.99)}
 
 
 class EngineServer:
@@ -54,6 +68,8 @@ class EngineServer:
         self.steps = 0
         self.decode_tokens = 0
         self.error: BaseException | None = None
+        # (tpot s or None, ttft s or None) of the most recently finished requests
+        self._latencies: collections.deque = collections.deque(maxlen=4096)
         try:
             from .metrics import ServerMetrics
             self.metrics = ServerMetrics(self)
@@ -196,6 +212,7 @@ class EngineServer:
                 with self._lock:
                     self._named.pop(r._name, None)
             tpot = r.tpot()
+            self._latencies.append((tpot, r.ttft()))
             if self.metrics is not None:
                 self.metrics.on_done(tpot, r.ttft(), now - r._t_submit)
             fut.set_result({
@@ -304,6 +321,7 @@ class EngineServer:
             if stats:
                 from .engine import summarize_steps
                 out["engine"] = summarize_steps(list(stats[-4096:]))
+            out["requests"] = latency_summary(list(self._latencies))
             cache = getattr(getattr(self.engine, "sched", None), "cache", None)
             if cache is not None:
                 out["prefix_cache"] = {"hit_tokens": cache.hits, "lookup_tokens": cache.lookups,

@@ -107,6 +107,8 @@ def test_server_futures_and_http_replay():
         import requests
         st = requests.get(f"http://127.0.0.1:{port}/stats", timeout=5).json()
         assert st["steps"] > 0 and st["decode_tokens"] > 0
+        rq = st["requests"]
+        assert rq["finished"] == 32 and rq["tpot_ms_p50"] is not None and rq["ttft_ms_p99"] >= rq["ttft_ms_p50"]
         assert requests.get(f"http://127.0.0.1:{port}/health", timeout=5).json()["ok"]
         m = requests.get(f"http://127.0.0.1:{port}/metrics", timeout=5)
         assert m.status_code == 200

@@ -72,3 +72,4 @@ def test_summarize_steps():
     assert s["steps"] == 3 and s["decode_only_steps"] == 2 and s["mixed_or_prefill_steps"] == 1
     assert s["graph_share"] == round(2 / 3, 4) and s["decode_step_ms_p50"] == 4.0
     assert s["decode_tokens"] == 12 and s["prefill_tokens"] == 1536 and summarize_steps([]) == {"steps": 0}
+    assert s["decode_tok_s_device"] == round(12 / 0.039, 1)  # 12 tokens over 39 ms of device time
