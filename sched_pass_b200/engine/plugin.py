@@ -309,11 +309,22 @@ class SchedPlugin:
                                   per_req[: len(dec)].tolist())
 
     def stats_line(self, engine) -> str:
+        """The periodic stats line: the reference's fields, then this rank,
+        the device time of its last step and its decode tokens per second of
+        device time over the last 64 steps (under TP every rank prints its
+        own line; the box's throughput is any rank's, since all decode the
+        same tokens)."""
         s = self.stats
+        recent = list(getattr(engine, "stats", None) or [])[-64:]
+        dev_ms = sum(st.device_ms for st in recent)
+        tok_s = sum(st.n_decode for st in recent) / (dev_ms / 1e3) if dev_ms > 0 else 0.0
+        tp = getattr(engine, "tp", None)
+        rank = tp.rank if tp is not None else 0
         return (f"[sched] step={engine.step_no} tasks={s.last_tasks} split={s.last_splits} R={engine.R} "
                 f"planned={s.planned} probes={s.probes} unc={s.last_unc:.3f} clc_armed={s.clc_armed} "
                 f"orders={s.orders} errors={engine.hooks.errors} "
-                f"mode={'enforce' if self.cfg.enforce else 'observe'}")
+                f"mode={'enforce' if self.cfg.enforce else 'observe'} "
+                f"rank={rank} step_ms={recent[-1].device_ms if recent else 0.0:.3f} tok_s={tok_s:.1f}")
 
     def as_dict(self) -> dict:
         return asdict(self.cfg)

@@ -162,3 +162,15 @@ def test_hook_errors_are_isolated_and_logged_once():
     text = out.getvalue()
     assert text.count("Bad.begin") == 1 and text.count("Bad.end") == 1
     assert good.stats.steps == 3  # the healthy hook kept running
+
+
+def test_stats_line_reports_rank_step_time_and_throughput():
+    from sched_pass_b200.engine.engine import StepStats
+    eng = FakeEngine([100, 200], R=64)
+    plug = SchedPlugin(SchedPluginConfig(), stream=io.StringIO())
+    eng.stats = [StepStats(6, 0, 4.0, True), StepStats(6, 0, 4.0, True)]
+    line = plug.stats_line(eng)
+    assert line.startswith("[sched] step=0 ") and "mode=enforce" in line
+    assert "rank=0 step_ms=4.000 tok_s=1500.0" in line  # 12 tokens in 8 ms of device time
+    eng.stats = []
+    assert "step_ms=0.000 tok_s=0.0" in plug.stats_line(eng)
