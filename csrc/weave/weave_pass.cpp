@@ -304,6 +304,19 @@ struct AsyncSite {
   int loop;
 };
 
+// A TMA tensor load (cp.async.bulk.tensor, tile mode, global -> shared) in a
+// loop: the stream the reference names as beyond its detectors (TMA-carried
+// mu). When a box coordinate advances with the canonical IV, the urgent tier
+// prefetches the box `dist` iterations ahead into L2 with
+// cp.async.bulk.prefetch.tensor on the advanced coordinates.
+struct TmaSite {
+  std::string text;
+  int dims = 0;
+  std::string tmap, tmap_type;      // the tensor-map operand
+  std::vector<std::string> coords;  // i32 box coordinates, innermost first
+  int loop = -1;
+};
+
 // Split "a, b(c, d), e" at top-level commas.
 std::vector<std::string> split_top(const std::string &s) {
   std::vector<std::string> out;
@@ -355,6 +368,82 @@ bool parse_cp_async(const std::string &text, std::string &src, std::string &src_
   return false;
 }
 
+// `call void asm sideeffect "<asm>", "<constraints>"(<args>)` whose asm holds
+// a tiled TMA load "cp.async.bulk.tensor.<N>d.shared...global... [dst],
+// [$m, {$c0, ...}], ...": the tensor map is argument m (a 64-bit "l"
+// operand), the coordinates the i32 arguments named inside the braces.
+// False for any other line, for stores and reductions (global before
+// shared), for im2col boxes and for prefetches.
+bool parse_tma_load(const std::string &text, TmaSite &s) {
+  const size_t a = text.find("asm ");
+  if (a == std::string::npos || text.find("cp.async.bulk.tensor.") == std::string::npos) return false;
+  const size_t q0 = text.find('"', a);
+  const size_t q1 = q0 == std::string::npos ? q0 : text.find('"', q0 + 1);
+  const size_t c0 = q1 == std::string::npos ? q1 : text.find('"', q1 + 1);
+  const size_t c1 = c0 == std::string::npos ? c0 : text.find('"', c0 + 1);
+  if (c1 == std::string::npos) return false;
+  const std::string asm_text = text.substr(q0 + 1, q1 - q0 - 1);
+  const size_t op = asm_text.find("cp.async.bulk.tensor.");
+  if (op == std::string::npos) return false;
+  const size_t op_end = asm_text.find_first_of(" \t[", op);
+  if (op_end == std::string::npos) return false;
+  const std::string opcode = asm_text.substr(op, op_end - op);
+  const size_t dpos = std::string("cp.async.bulk.tensor.").size();
+  if (opcode.size() < dpos + 2 || opcode[dpos + 1] != 'd') return false;
+  const int dims = opcode[dpos] - '0';
+  if (dims < 1 || dims > 5) return false;
+  const size_t sh = opcode.find(".shared"), gl = opcode.find(".global");
+  if (sh == std::string::npos || gl == std::string::npos || gl < sh) return false;  // loads only
+  if (opcode.find("im2col") != std::string::npos || opcode.find("prefetch") != std::string::npos) return false;
+  // the second bracketed operand: [$m, {$c0, ...}]
+  const size_t b1 = asm_text.find('[', op_end), e1 = b1 == std::string::npos ? b1 : asm_text.find(']', b1);
+  const size_t b2 = e1 == std::string::npos ? e1 : asm_text.find('[', e1);
+  const size_t e2 = b2 == std::string::npos ? b2 : asm_text.find(']', b2);
+  if (e2 == std::string::npos) return false;
+  const std::string inner = asm_text.substr(b2 + 1, e2 - b2 - 1);
+  const size_t lb = inner.find('{'), rb = inner.find('}');
+  if (lb == std::string::npos || rb == std::string::npos || rb < lb) return false;
+  auto operand_index = [](const std::string &tok) -> int {
+    const std::string t = trim(tok);
+    if (t.size() < 2 || t[0] != '$') return -1;
+    for (size_t i = 1; i < t.size(); ++i)
+      if (t[i] < '0' || t[i] > '9') return -1;
+    return std::atoi(t.c_str() + 1);
+  };
+  const int mi = operand_index(inner.substr(0, inner.find(',')));
+  std::vector<int> ci;
+  for (const std::string &tok : split_top(inner.substr(lb + 1, rb - lb - 1))) ci.push_back(operand_index(tok));
+  if (mi < 0 || (int)ci.size() != dims) return false;
+  std::vector<std::string> cons;
+  for (const std::string &k : split_top(text.substr(c0 + 1, c1 - c0 - 1))) {
+    if (starts_with(k, "=")) return false;  // an output would shift the operand numbers
+    if (!starts_with(k, "~{")) cons.push_back(k);
+  }
+  const size_t p0 = text.find('(', c1), p1 = text.rfind(')');
+  if (p0 == std::string::npos || p1 == std::string::npos || p1 <= p0) return false;
+  const std::vector<std::string> args = split_top(text.substr(p0 + 1, p1 - p0 - 1));
+  auto arg = [&](int k, std::string &ty, std::string &v) -> bool {
+    if (k < 0 || k >= (int)args.size() || k >= (int)cons.size()) return false;
+    const size_t sp = args[k].rfind(' ');
+    if (sp == std::string::npos) return false;
+    ty = trim(args[k].substr(0, sp));
+    v = trim(args[k].substr(sp + 1));
+    return !v.empty() && v[0] == '%';
+  };
+  TmaSite out;
+  out.dims = dims;
+  if (!arg(mi, out.tmap_type, out.tmap) || cons[mi] != "l") return false;
+  if (!(starts_with(out.tmap_type, "ptr") || out.tmap_type == "i64")) return false;
+  for (int k : ci) {
+    std::string ty, v;
+    if (!arg(k, ty, v) || ty != "i32" || cons[k] != "r") return false;
+    out.coords.push_back(v);
+  }
+  out.text = text;
+  s = out;
+  return true;
+}
+
 void insert_after(Block &b, int idx, const std::vector<Inst> &code) {
   b.insts.insert(b.insts.begin() + idx + 1, code.begin(), code.end());
 }
@@ -396,6 +485,7 @@ class Weaver {
     std::vector<Loop> loops = find_loops(f);
     std::vector<Site> sites;
     async_sites.clear();
+    tma_sites.clear();
     if (c.policy || c.shed) {
       const std::set<std::string> written = written_roots(f, defs);
       for (size_t li = 0; li < loops.size(); ++li) {
@@ -430,6 +520,19 @@ class Weaver {
               as.text = in.text;
               as.loop = (int)li;
               if (async_sites.size() < 4) async_sites.push_back(as);
+            }
+        }
+      if (c.policy)
+        for (size_t li = 0; li < loops.size(); ++li) {
+          const Loop &L = loops[li];
+          if (L.iv.empty()) continue;
+          for (int b = 0; b < (int)f.blocks.size(); ++b)
+            for (const Inst &in : f.blocks[b].insts) {
+              if (!L.contains(b)) break;
+              TmaSite ts;
+              if (in.opcode != "call" || !parse_tma_load(in.text, ts)) continue;
+              ts.loop = (int)li;
+              if (tma_sites.size() < 4) tma_sites.push_back(ts);
             }
         }
       for (const Loop &L : loops)
@@ -485,7 +588,7 @@ class Weaver {
     }
     // policy flags / shed budget from the task's row
     std::string urgent, polite, budget;
-    bool need_row = (!sites.empty() || !async_sites.empty()) && ctrl.available;
+    bool need_row = (!sites.empty() || !async_sites.empty() || !tma_sites.empty()) && ctrl.available;
     std::string row;
     if (need_row) {
       std::string inb = f.unique("%sched.row.inb"), use = f.unique("%sched.row.use"), idx = f.unique("%sched.row.idx");
@@ -583,6 +686,7 @@ class Weaver {
   const Config &c;
   Notes &n;
   std::vector<AsyncSite> async_sites;
+  std::vector<TmaSite> tma_sites;
 
   int sm() const {
     if (starts_with(m.target_cpu, "sm_")) return std::atoi(m.target_cpu.c_str() + 3);
@@ -778,6 +882,61 @@ class Weaver {
       n.add(f.name + ": L2 policy woven at a stream load");
     }
     for (const AsyncSite &as : async_sites) emit_async_warm(as, loops[as.loop], ui);
+    for (const TmaSite &ts : tma_sites) emit_tma_warm(ts, loops[ts.loop], ui);
+  }
+
+  // TMA stream warming: the same box `dist` iterations ahead, prefetched into
+  // L2 by the urgent tier (cp.async.bulk.prefetch.tensor, sm_90 and later)
+  // right before the load. Coordinates that do not move with the IV are
+  // kept; an advanced coordinate past the tensor's extent is a prefetch of
+  // nothing. The innermost coordinate moves by a multiple of its own
+  // per-iteration step, so its 16-byte alignment is the load's.
+  void emit_tma_warm(const TmaSite &ts, const Loop &L, const std::string &ui) {
+    if (sm() < 90) {
+      n.add(f.name + ": TMA stream warming needs sm_90 or later; declined");
+      return;
+    }
+    for (Block &b : f.blocks)
+      for (size_t i = 0; i < b.insts.size(); ++i) {
+        if (b.insts[i].text != ts.text) continue;
+        Defs defs(f);
+        std::vector<Inst> code;
+        std::vector<std::string> ahead = ts.coords;
+        bool moves = false;
+        for (size_t j = 0; j < ts.coords.size(); ++j) {
+          long long step = 0;
+          if (!iv_step(f, defs, L.iv, ts.coords[j], step)) {
+            n.add(f.name + ": TMA stream warming declined (a coordinate is not affine in the IV)");
+            return;
+          }
+          if (step == 0) continue;
+          moves = true;
+          ahead[j] = f.unique("%sched.tpf.c");
+          code.push_back(I("  " + ahead[j] + " = add i32 " + ts.coords[j] + ", " +
+                           std::to_string(step * (long long)c.prefetch_dist)));
+        }
+        if (!moves) {
+          n.add(f.name + ": TMA stream warming declined (no coordinate advances with the loop)");
+          return;
+        }
+        const int D = ts.dims;
+        std::string tmpl = "{ .reg .pred p; setp.ne.u32 p, $" + std::to_string(D + 1) +
+                           ", 0; @p cp.async.bulk.prefetch.tensor." + std::to_string(D) + "d.L2.global.tile [$0, {";
+        std::string cons = "l", args = ts.tmap_type + " " + ts.tmap;
+        for (int j = 0; j < D; ++j) {
+          tmpl += (j ? ", $" : "$") + std::to_string(j + 1);
+          cons += ",r";
+          args += ", i32 " + ahead[j];
+        }
+        tmpl += "}]; }";
+        cons += ",r,~{memory}";
+        args += ", i32 " + ui;
+        code.push_back(I("  call void asm sideeffect \"" + tmpl + "\", \"" + cons + "\"(" + args + ")"));
+        insert_before(b, (int)i, code);
+        n.add(f.name + ": TMA stream warming woven (urgent tensor prefetch ahead)");
+        return;
+      }
+    n.add(f.name + ": TMA load moved; warming skipped");
   }
 
   // cp.async source warming: prefetch the source `dist` iterations ahead,

@@ -264,6 +264,60 @@ def test_cp_async_source_warming():
     assert "%sched.apf" not in off
 
 
+def test_tma_stream_warming():
+    """A tiled TMA load (cp.async.bulk.tensor, global -> shared) whose box
+    coordinate is affine in the canonical IV is a TMA stream site: the urgent
+    tier prefetches the box 8 iterations ahead (innermost coordinate +64 per
+    iteration -> +512, the row coordinate unchanged) with
+    cp.async.bulk.prefetch.tensor right before the load, which itself stays
+    untouched; the policy knob removes it. The woven module assembles for
+    sm_100a (ptxas is given the generated PTX and only its status is used)."""
+    import shutil
+    import subprocess
+    import tempfile
+    src = fixture("tma_stream.ll")
+    out, notes = weave(src)
+    verify(out)
+    check_order(out, [
+        r"%sched\.urgent = or i1",
+        r"%sched\.tpf\.c = add i32 %x, 512",
+        r"@p cp\.async\.bulk\.prefetch\.tensor\.2d\.L2\.global\.tile \[\$0, \{\$1, \$2\}\]; \}\", \"l,r,r,r,~\{memory\}\"\(ptr %tmap, i32 %sched\.tpf\.c, i32 %y, i32 %sched\.urgent\.i32\)",
+        r"@p cp\.async\.bulk\.tensor\.2d\.shared::cluster\.global\.tile\.mbarrier::complete_tx::bytes \[\$0\], \[\$1, \{\$2, \$3\}\], \[\$4\]",
+        r"mbarrier\.try_wait\.parity",
+        r"%v = load i16, ptr addrspace\(3\) %sh",
+    ])
+    assert any("TMA stream warming woven" in n for n in notes)
+    assert "%sched.keep" not in out  # shared-memory data: no value mask
+    off, _ = weave(src, {"SCHED_NO_POLICY": "1"})
+    assert "%sched.tpf" not in off and "prefetch.tensor" not in off
+    ptxas = shutil.which("ptxas") or "/usr/local/cuda/bin/ptxas"
+    if not os.path.exists(ptxas):
+        pytest.skip("ptxas not installed")
+    from sched_pass_b200.compiler.nvptx import compile_ptx
+    with tempfile.TemporaryDirectory() as d:
+        ptx = os.path.join(d, "k.ptx")
+        with open(ptx, "wb") as fh:
+            fh.write(compile_ptx(out))
+        r = subprocess.run([ptxas, "-arch=sm_100a", ptx, "-o", os.path.join(d, "k.cubin")],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr[-2000:]
+
+
+def test_tma_parser_declines_stores_and_fixed_boxes():
+    """Stores (global before shared), im2col boxes and prefetches are not
+    stream loads; a load whose coordinates never move with the loop is
+    declined with a note."""
+    src = fixture("tma_stream.ll")
+    store = src.replace("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [$0], [$1, {$2, $3}], [$4]",
+                        "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [$1, {$2, $3}], [$0]")
+    out, notes = weave(store)
+    assert "%sched.tpf" not in out and not any("TMA stream" in n for n in notes)
+    fixed = src.replace("%x = mul i32 %k, 64", "%x = mul i32 %req, 64")
+    out, notes = weave(fixed)
+    assert "%sched.tpf" not in out
+    assert any("no coordinate advances with the loop" in n for n in notes)
+
+
 def test_manifest_markdown_lists_every_lever_in_order():
     from sched_pass_b200.runtime.manifest import manifest_markdown
     rows = manifest_markdown().splitlines()[2:]
