@@ -305,8 +305,11 @@ struct AsyncSite {
 };
 
 // A TMA tensor load (cp.async.bulk.tensor, tile mode, global -> shared) in a
-// loop: the stream the reference names as beyond its detectors (TMA-carried
-// mu). When a box coordinate advances with the canonical IV, the urgent tier
+// loop: the stream the reference lists as not visible to its IR detectors
+// (MODEL.md:100, "TMA descriptor ... not visible as plain loads at LLVM IR";
+// lib/SchedWeave.cpp:155-160 leaves it to other observation levels). Here
+// the load's inline asm names the descriptor and the box coordinates, so the
+// site is visible. When a box coordinate advances with the canonical IV, the urgent tier
 // prefetches the box `dist` iterations ahead into L2 with
 // cp.async.bulk.prefetch.tensor on the advanced coordinates.
 struct TmaSite {
