@@ -113,7 +113,12 @@ class TieredKV:
         cap = 2 * self.n_staging
         self.pairs_dev = torch.zeros(cap, dtype=torch.int32, device=self.device)  # (host page, slot)
         self.count_dev = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self._pairs_pin = torch.zeros(cap + 1, dtype=torch.int32, pin_memory=on_cuda)
+        # two pinned sources of the page-pair upload, alternating per step: a
+        # buffer is rewritten only after its copy of two steps ago has run
+        # (its event), so staging never waits for the step in flight
+        self._pairs_pin = [torch.zeros(cap + 1, dtype=torch.int32, pin_memory=on_cuda) for _ in range(2)]
+        self._pin_done = [None, None]
+        self._pin_k = 0
         self._spill_dev = torch.zeros(2, dtype=torch.int32, device=self.device)
         self._translation: dict = {}
         self._stream = torch.cuda.Stream(self.device) if on_cuda else None
@@ -225,17 +230,22 @@ class TieredKV:
         self.last_stage = n
         self.staged_pages += n
         self._runs = coalesce_runs(pairs)
-        buf = self._pairs_pin.numpy()
+        k = self._pin_k
+        self._pin_k ^= 1
+        pin = self._pairs_pin[k]
+        if self._pin_done[k] is not None:
+            self._pin_done[k].synchronize()  # this buffer's upload of two steps ago has run
+        buf = pin.numpy()
         buf[0] = n
         if n:
             buf[1:1 + 2 * n] = np.asarray(pairs, dtype=np.int32).reshape(-1)
-        self.count_dev.copy_(self._pairs_pin[:1], non_blocking=True)
+        self.count_dev.copy_(pin[:1], non_blocking=True)
         if n:
-            self.pairs_dev[: 2 * n].copy_(self._pairs_pin[1:1 + 2 * n], non_blocking=True)
-        # the pinned buffer is rewritten next step: let these copies finish
-        # (the engine synchronises once per step anyway)
+            self.pairs_dev[: 2 * n].copy_(pin[1:1 + 2 * n], non_blocking=True)
         if self.device.type == "cuda":
-            torch.cuda.current_stream(self.device).synchronize()
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self._pin_done[k] = ev
 
     def pages_for(self, req):
         return self._translation.get(id(req), req.pages)

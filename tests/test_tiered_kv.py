@@ -70,10 +70,11 @@ def test_stage_translates_read_pages_and_release_returns_host_pages():
     assert host_idx
     tier.stage([a, b])
     tr = tier.pages_for(b)
-    pairs = tier._pairs_pin.numpy()
-    n = int(pairs[0])
+    # what the page-copy kernels read: the count and the (host page, slot) pairs on the device
+    n = int(tier.count_dev[0])
+    pairs = tier.pairs_dev[: 2 * n].numpy()
     assert n == len(host_idx) and tier.last_stage == n
-    got = {int(pairs[2 + 2 * j]): int(pairs[1 + 2 * j]) for j in range(n)}  # slot -> host page
+    got = {int(pairs[1 + 2 * j]): int(pairs[2 * j]) for j in range(n)}  # slot -> host page
     for i in host_idx:
         slot = tr[i] - tier.split
         assert tier.split == 40 and 0 <= slot < 16
@@ -100,3 +101,25 @@ def test_staged_pages_coalesce_into_contiguous_runs():
     pairs = [(5, 0), (6, 1), (7, 2), (2, 3), (9, 4), (10, 5), (12, 6)]
     assert coalesce_runs(pairs) == [(5, 0, 3), (2, 3, 1), (9, 4, 2), (12, 6, 1)]
     assert coalesce_runs([]) == []
+
+
+def test_consecutive_steps_publish_each_steps_pairs():
+    """Staging alternates between two pinned upload buffers (a buffer is
+    reused only after its upload of two steps ago), and every step publishes
+    its own pairs: a step that reads fewer host pages after one that read
+    more leaves the device count and pairs of the smaller step."""
+    kv, tier, sched = make(n_device=40, n_staging=16)
+    a = admit(sched, 0, 16 * 12, urgency=0.9)
+    b = admit(sched, 1, 16 * 12, urgency=0.1)
+    admit(sched, 2, 16 * 12, urgency=0.5)
+    admit(sched, 3, 16 * 10, urgency=0.7)
+    host_b = [p - HOST_BASE for p in b.pages if is_host(p)]
+    assert len(host_b) >= 2
+    published = []
+    for step, reqs in enumerate([[a, b], [a], [a, b]]):
+        tier.stage(reqs)
+        n = int(tier.count_dev[0])
+        pairs = tier.pairs_dev[: 2 * n].numpy().reshape(-1, 2)
+        published.append(sorted(int(h) for h, _ in pairs))
+        assert tier._pin_k == (step + 1) % 2
+    assert published == [sorted(host_b), [], sorted(host_b)]
