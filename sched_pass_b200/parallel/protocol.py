@@ -226,3 +226,150 @@ class EmulatedAllReduce:
                 myflags[:, u] = 0
         y = torch.from_numpy(out.view(np.int16).copy()).view(torch.bfloat16)
         return y, status
+
+
+# ---------------------------------------------------------------------------
+# The decode-size line exchange (gemm.cu: write_row's line path,
+# reduce_line_row, ll_epoch / ll_finish).
+#
+# A call uses epoch e = state + 1 and line set e & 1. Every 4 output columns
+# of a rank's bf16 partial become one 16-byte line {c0|c1, e, c2|c3, e}
+# written into every rank's buffer at [set][source][token][column / 4]:
+# with per-peer stores one whole line per rank; through NVLink multicast as
+# two 8-byte halves, each reaching every rank's copy at once. A reader polls
+# its own buffer until both halves of every source's line carry e (bounded),
+# sums the sources in rank order in fp32 and rounds to bf16; no flag, fence
+# or reset is involved. After the call the epoch advances (0 is skipped on
+# wrap-around, so a never-written line never matches).
+
+LINE_WORDS = 4  # u32 words per 16-byte line
+
+
+class LineFabric:
+    """Shared mappings standing in for the symmetric line buffers: rank j's
+    buffer is ``lines(j)`` -> uint32 [2 sets, world, max_tokens, max_n / 4,
+    4], zero-filled at creation (epoch 0 matches no call)."""
+
+    def __init__(self, rank: int, world: int, max_tokens: int, max_n: int, directory: str, tag: str,
+                 group=None):
+        import torch.distributed as dist
+        if max_n % 4:
+            raise ValueError("max_n is a multiple of 4")
+        self.rank, self.world, self.max_tokens, self.max_n = rank, world, max_tokens, max_n
+        self.shape = (2, world, max_tokens, max_n // 4, LINE_WORDS)
+        self.nbytes = int(np.prod(self.shape)) * 4
+        self.paths = [os.path.join(directory, f"{tag}.lines{j}") for j in range(world)]
+        with open(self.paths[rank], "wb") as f:
+            f.truncate(self.nbytes)
+        dist.barrier(group=group)
+        self._files = [open(p, "r+b") for p in self.paths]
+        self._maps = [mmap.mmap(f.fileno(), self.nbytes) for f in self._files]
+        self.group = group
+
+    def lines(self, j: int) -> np.ndarray:
+        return np.frombuffer(self._maps[j], dtype=np.uint32).reshape(self.shape)
+
+    def close(self) -> None:
+        import torch.distributed as dist
+        dist.barrier(group=self.group)
+        for m in self._maps:
+            m.close()
+        for f in self._files:
+            f.close()
+        self._maps, self._files = [], []
+        dist.barrier(group=self.group)
+        try:
+            os.unlink(self.paths[self.rank])
+        except FileNotFoundError:
+            pass
+
+
+def state_after_call(e: int) -> int:
+    """ll_finish: the epoch state after a call that used epoch ``e`` (the
+    next call uses state + 1); 0xFFFFFFFF leaves 1, so no call ever uses
+    epoch 0, the value of a never-written line."""
+    return 1 if e == 0xFFFFFFFF else e
+
+
+class EmulatedLineAllReduce:
+    """y = all_reduce(x @ w.T) over the ranks by the line exchange.
+
+    ``multicast``: each line leaves as two 8-byte halves, each written into
+    every rank's copy before the next half (the NVLS path); otherwise each
+    rank's copy receives the whole line in turn (per-peer stores).
+    ``__call__`` options: ``seed`` shuffles the order lines are written;
+    ``torn`` writes every line's first halves before any second half (the
+    most a reader can see of 8-byte granularity); ``drop`` = token rows this
+    rank does not push (a lost message); ``stall_s`` sleeps before the push
+    (a slow rank). Returns (y, status) with the kernel's peer-timeout status
+    when a bounded wait gave up.
+    """
+
+    def __init__(self, fabric: LineFabric, multicast: bool = False, budget_s: float = 2.0):
+        self.f = fabric
+        self.multicast = multicast
+        self.budget_s = budget_s
+        self.state = 0  # ll_state[0]: the last call's epoch
+
+    def _push(self, e: int, set_: int, part: np.ndarray, rng, torn: bool, drop) -> None:
+        f = self.f
+        T, N = part.shape
+        pairs = part.reshape(T, N // 4, 2, 2).astype(np.uint32)
+        words = pairs[..., 0] | (pairs[..., 1] << 16)  # [T, N/4, 2]: c0|c1 and c2|c3
+        rows = [t for t in range(T) if t not in drop]
+        order = rng.permutation(len(rows))
+        dsts = [f.lines(j)[set_, f.rank] for j in range(f.world)]
+        halves = (0, 1)
+
+        def put(t, h, dst):
+            # payload word first, then its epoch word: a reader that sees
+            # the epoch of a half sees that half's payload (stores become
+            # visible in order)
+            dst[t, :N // 4, 2 * h] = words[t, :, h]
+            dst[t, :N // 4, 2 * h + 1] = e
+
+        if torn:
+            for h in halves:
+                for i in order:
+                    for dst in dsts:
+                        put(rows[i], h, dst)
+        elif self.multicast:
+            for i in order:
+                for h in halves:  # each 8-byte half reaches every copy before the next
+                    for dst in dsts:
+                        put(rows[i], h, dst)
+        else:
+            for dst in dsts:  # the whole line, one rank's copy after another
+                for i in order:
+                    for h in halves:
+                        put(rows[i], h, dst)
+
+    def __call__(self, x: torch.Tensor, w: torch.Tensor, seed: int = 0, torn: bool = False, drop=(),
+                 stall_s: float = 0.0):
+        f = self.f
+        T, N = x.shape[0], w.shape[0]
+        if T > f.max_tokens or N > f.max_n or N % 4:
+            raise ValueError("shape outside the line buffers")
+        e = self.state + 1  # ll_epoch
+        set_ = e & 1
+        rng = np.random.default_rng(seed)
+        part = to_bf16_bits(x.float() @ w.float().t())  # bf16 bits [T, N]
+        if stall_s:
+            time.sleep(stall_s)
+        self._push(e, set_, part, rng, torn, set(drop))
+        # reduce_line_row: poll this rank's own copy, every source, bounded
+        mine = f.lines(f.rank)[set_, :, :T, :N // 4]
+        status = STATUS_OK
+        deadline = time.monotonic() + self.budget_s
+        while not ((mine[..., 1] == e).all() and (mine[..., 3] == e).all()):
+            if time.monotonic() > deadline:
+                status = STATUS_PEER_TIMEOUT  # as the kernel: record, reduce what is there
+                break
+            time.sleep(1e-4)
+        got = mine.copy()
+        lo = np.stack([got[..., 0] & 0xFFFF, got[..., 0] >> 16, got[..., 2] & 0xFFFF, got[..., 2] >> 16], -1)
+        partials = lo.reshape(f.world, T, N).astype(np.uint16)
+        out = reduce_rank_order(partials)
+        self.state = state_after_call(e)  # ll_finish
+        y = torch.from_numpy(out.view(np.int16).copy()).view(torch.bfloat16)
+        return y, status

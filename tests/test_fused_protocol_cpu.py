@@ -3,7 +3,9 @@ CPU (sched_pass_b200/parallel/protocol.py): the flag counts of cluster
 split-K agree with the publishers, results are bit-identical to the
 kernel's rank-order reduction and close to the fp32 sum, a slow rank is
 tolerated because two buffer sets alternate (one set is not enough), and a
-lost push ends in a peer-timeout status instead of a hang."""
+lost push ends in a peer-timeout status instead of a hang. The same for the
+decode-size line exchange, with per-peer and with multicast writes, and
+with lines whose 8-byte halves land separately."""
 import json
 import os
 import shutil
@@ -106,3 +108,37 @@ def test_lost_push_times_out_with_status():
     outs = launch("drop", 2)
     for r in (0, 1):
         assert outs[r]["status"] == P.STATUS_PEER_TIMEOUT and outs[r]["elapsed"] < 10, outs[r]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("scen", ["ll_exact", "ll_torn"])
+def test_line_exchange_is_exact(world, scen):
+    """Epoch-tagged lines, written per peer or through multicast (each
+    8-byte half reaching every copy at once), and with every first half
+    landing before any second half: every rank's output is the kernel's
+    rank-order reduction, bit for bit, with no timeout."""
+    outs = launch(scen, world)
+    for r in range(world):
+        assert outs[r]["bad"] == [], outs[r]
+        assert set(outs[r]["statuses"]) == {P.STATUS_OK}
+        assert outs[r]["state"] == outs[r]["calls"]  # the epoch advanced once per call
+
+
+def test_line_exchange_tolerates_a_slow_rank():
+    """A rank that pushes late: the others poll their own copies until the
+    late lines carry the call's epoch, and never take the same set's lines
+    from two calls before (their epoch differs)."""
+    outs = launch("ll_skew", 2)
+    for r in (0, 1):
+        assert outs[r]["bad"] == [] and set(outs[r]["statuses"]) == {P.STATUS_OK}, outs[r]
+
+
+def test_line_exchange_lost_row_times_out_with_status():
+    outs = launch("ll_drop", 2)
+    for r in (0, 1):
+        assert outs[r]["status"] == P.STATUS_PEER_TIMEOUT and outs[r]["elapsed"] < 10, outs[r]
+
+
+def test_epoch_state_skips_zero():
+    assert P.state_after_call(7) == 7
+    assert P.state_after_call(0xFFFFFFFF) == 1  # next call uses epoch 2: never 0

@@ -32,16 +32,67 @@ def expected(world, call, T, K, N):
 faulthandler.enable()  # a native crash prints the Python stack of every thread
 
 
+def run_lines(scen, fab, rank, world, out):
+    """Scenarios of the decode-size line exchange. One emulator (one epoch
+    state) per process, as the kernel keeps one per rank."""
+    import time
+    lar = P.EmulatedLineAllReduce(fab, budget_s=1.5 if scen != "ll_drop" else 0.5)
+    bad, statuses, call = [], [], 0
+
+    def check(T, K, N, **kw):
+        nonlocal call
+        x, w = inputs(rank, call, T, K, N)
+        y, st = lar(x, w, seed=rank * 7919 + call, **kw)
+        parts, fp32 = expected(world, call, T, K, N)
+        yb = y.view(torch.int16).numpy().view(np.uint16)
+        if not np.array_equal(yb, P.reduce_rank_order(parts)):
+            bad.append([call, T, N, lar.multicast, "bits"])
+        err = (y.float() - fp32).abs().max().item() / max(1e-6, fp32.abs().max().item())
+        if err > 2e-2:
+            bad.append([call, T, N, f"err {err:.3g}"])
+        statuses.append(st)
+        call += 1
+
+    shapes = [(1, 64, 128), (5, 64, 256), (16, 128, 128), (33, 64, 256), (48, 32, 256), (2, 64, 64)]
+    if scen == "ll_exact":
+        for mc in (False, True):
+            lar.multicast = mc
+            for T, K, N in shapes:
+                check(T, K, N)
+    elif scen == "ll_torn":
+        for mc in (False, True):
+            lar.multicast = mc
+            for T, K, N in shapes:
+                check(T, K, N, torn=True)
+    elif scen == "ll_skew":
+        for mc in (False, True):
+            lar.multicast = mc
+            for i in range(3):
+                check(40, 64, 256, stall_s=0.3 if rank == world - 1 else 0.0)
+    elif scen == "ll_drop":
+        x, w = inputs(rank, 0, 40, 64, 128)
+        t0 = time.monotonic()
+        _, st = lar(x, w, drop={0} if rank == world - 1 else ())
+        out.update(status=st, elapsed=time.monotonic() - t0)
+        return
+    out.update(bad=bad, statuses=statuses, calls=call, state=lar.state)
+
+
 def main():
     scen = sys.argv[1]
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=30))
     out = {"rank": rank}
     sets = 1 if scen == "oneset" else 2
-    fab = P.PeerFabric(rank, world, max_tokens=96, max_n=384, tile_t=32, directory=os.environ["PROTO_DIR"],
-                       tag=f"{scen}", sets=sets)
+    if scen.startswith("ll_"):
+        fab = P.LineFabric(rank, world, max_tokens=48, max_n=256, directory=os.environ["PROTO_DIR"], tag=scen)
+    else:
+        fab = P.PeerFabric(rank, world, max_tokens=96, max_n=384, tile_t=32, directory=os.environ["PROTO_DIR"],
+                           tag=f"{scen}", sets=sets)
     try:
-        if scen == "exact":
+        if scen.startswith("ll_"):
+            run_lines(scen, fab, rank, world, out)
+        elif scen == "exact":
             bad, statuses = [], []
             shapes = [(1, 64, 128), (5, 64, 256), (16, 128, 128), (33, 64, 384), (96, 32, 256), (47, 64, 128)]
             call = 0
