@@ -113,11 +113,20 @@ class _LocalBuffer:
 
 
 class ExpertParallel:
-    """Receive slabs, counters and combine buffers of one MoE layer stack.
+    """Receive slabs, counters and combine buffers of one MoE layer stack, in
+    two sets that alternate between consecutive layer calls.
 
-    All layers share one set of buffers: layer l+1's dispatch from any rank
-    is causally after every owner finished layer l (its combine rows must
-    have arrived first), so single buffers are safe.
+    A source waits for the owners it routed rows to (their combine rows),
+    not for the others: a source that routed nothing to an owner can finish
+    layer l and dispatch layer l+1 while that owner is still in layer l,
+    whose consumer resets (row counters and done count, cleared at the end of
+    the gate/up GEMM) would clear the early arrivals with one set of
+    buffers. No source gets two calls ahead: its own gate/up GEMM of layer
+    l+1 waits for every source's layer-(l+1) dispatch, which each source
+    issues after finishing layer l. So two sets are enough
+    (``parallel/ep_protocol.py`` shows one set failing and two passing on
+    the CPU). Under CUDA graphs the sets alternate in capture order; every
+    step runs every layer, an even number of calls for the named models.
     """
 
     def __init__(self, cfg, device, group=None, max_tokens: int = 32, capacity: int | None = None):
@@ -154,9 +163,11 @@ class ExpertParallel:
             total += (n + 255) // 256 * 256
         if distributed and self.world > 1:
             from .symm import SymmetricBuffer
-            self.buf = SymmetricBuffer(total, group)
+            self.bufs = [SymmetricBuffer(total, group) for _ in range(2)]
         else:
-            self.buf = _LocalBuffer(total)
+            self.bufs = [_LocalBuffer(total) for _ in range(2)]
+        self.k = 0
+        self.buf = self.bufs[0]
         self.peer = lambda name: [p + self.off[name] for p in self.buf.ptrs]
         self.mine = lambda name: self.buf.ptrs[self.rank] + self.off[name]
         # local scratch
@@ -202,6 +213,8 @@ class ExpertParallel:
         T = x.shape[0]
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens > EP buffers sized for {self.max_tokens}")
+        self.buf = self.bufs[self.k]  # this call's buffer set (peer / mine read it)
+        self.k ^= 1
         st = ops.status_buffer(x.device)
         ids, wts = self.ids[:T], self.wts[:T]
         if T:
@@ -228,4 +241,5 @@ class ExpertParallel:
         return y
 
     def close(self):
-        self.buf.close()
+        for b in self.bufs:
+            b.close()
